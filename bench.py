@@ -1,0 +1,493 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 FP8 MoE hot path (one JSON line on rank 0).
+
+Headline workload: one packed-decode MoE layer at L=1,
+batch 1 -- FP32 router (288 experts, top-8) + fused gate/up/SwiGLU over the 8
+selected experts and the shared expert + down / weighted reduce / shared add,
+H=4096, I=1536, E4M3 weights with 128x128 FP32 scales, swiglu_limit 10.
+A step is one token through one layer.  Steps rotate over --layers distinct
+seeded layers (8 x 5.44 GB of experts, far above the 126 MB L2) and a pool of
+64 activation vectors, so every step streams its weights from HBM; no L2 flush
+is needed.  Steps are CUDA-graph captured; `value` = steps / device time.
+
+`e2e` runs the same steps through the public module API
+(`PackedFP8MoE(bank, config, Float32Gate, shared)(x)`), copying each token from
+pinned host memory and the result back inside the timed region.
+
+`--impl reference` times the CPU restatement of the reference kernels (the
+reference's MLX/Metal path cannot run off Apple hardware) on all host cores.
+
+Multi-GPU (torchrun, N>1): replicas only -- every rank runs its own layers,
+no collective on the data path; value = total tokens / max-over-ranks time.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+H, I, E, TOP_K, LIMIT = 4096, 1536, 288, 8, 10.0
+POOL = 64
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=256)
+    p.add_argument("--warmup", type=int, default=16)
+    p.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    p.add_argument("--layers", type=int, default=8, help="distinct layers rotated through (L2 defeat)")
+    p.add_argument("--no-prefill", action="store_true", help="skip the secondary T=2048 grouped measurement")
+    p.add_argument("--cpu-seconds", type=float, default=12.0, help="bounded CPU-baseline sample")
+    return p.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+
+
+def dist_setup(args):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.rows: list[list[str]] = []
+        self.proc = None
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            if self.thread is not None:
+                self.thread.join(timeout=2)
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+            except (ValueError, IndexError):
+                continue
+            for name, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------------------
+# workload
+# ---------------------------------------------------------------------------
+
+# algorithmic bytes of one decode step (config 2, I = 1536)
+ROUTER_BYTES = E * H * 4 + E * 4 + H * 2
+GATE_UP_BYTES = (TOP_K + 1) * 2 * I * H + TOP_K * 2 * (I // 128) * (H // 128) * 4 + 2 * (I // 128) * (H // 128) * 4 \
+    + H * 2 + (TOP_K * I + I) * 2 + TOP_K * 4
+DOWN_BYTES = (TOP_K + 1) * H * I + (TOP_K + 1) * (H // 128) * (I // 128) * 4 + (TOP_K * I + I) * 2 + H * 2 + TOP_K * 8
+STEP_BYTES = ROUTER_BYTES + GATE_UP_BYTES + DOWN_BYTES
+
+
+def build_layers(n_layers: int, seed0: int, device):
+    from glm53_flash_mlx_b200 import synthetic as S
+    from glm53_flash_mlx_b200.packed import shared_fp8_tensors
+
+    layers = []
+    for l in range(n_layers):
+        seed = seed0 + 17 * l
+        bank = S.make_bank(E, H, I, seed=seed, device=device)
+        shared_mod = S.make_shared(H, I, seed=seed + 1, limit=LIMIT, device=device)
+        w, b = S.make_router(E, H, seed=seed + 2, device=device)
+        layers.append({"bank": bank, "shared_mod": shared_mod, "shared": shared_fp8_tensors(shared_mod),
+                       "router_w": w, "router_b": b})
+    return layers
+
+
+def bench_b200(args, world, rank, local):
+    import torch
+
+    import glm53_flash_mlx_b200 as G
+    from glm53_flash_mlx_b200 import _native as N
+    from glm53_flash_mlx_b200 import synthetic as S
+    from glm53_flash_mlx_b200.router import Float32Gate
+
+    dev = torch.device("cuda", local)
+    N.lib()
+    layers = build_layers(args.layers, 1000 + 101 * rank, dev)
+    xs = S.random_bf16((POOL, H), seed=77 + rank, device=dev)
+    lib = N.lib()
+
+    # ---- one step = router + packed decode, captured per (layer, x) -------
+    ws = N.Workspace()
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    n_graphs = POOL
+    outs = [torch.empty(H, dtype=torch.bfloat16, device=dev) for _ in range(n_graphs)]
+    idxs = [torch.empty((1, TOP_K), dtype=torch.int32, device=dev) for _ in range(n_graphs)]
+    scs = [torch.empty((1, TOP_K), dtype=torch.float32, device=dev) for _ in range(n_graphs)]
+    rws = ws.get(dev, "router", lib.glm53_router_workspace_bytes(1, E))
+    dws = ws.get(dev, "decode", lib.glm53_packed_decode_workspace_bytes(TOP_K, I, I))
+
+    def step(i, stream):
+        L = layers[i % args.layers]
+        x = xs[i % POOL]
+        N.check(lib.glm53_router_topk(x.data_ptr(), 1, H, L["router_w"].data_ptr(), E, L["router_b"].data_ptr(), TOP_K,
+                                      1, 1, 1, 1.0, idxs[i].data_ptr(), scs[i].data_ptr(), None, rws.data_ptr(),
+                                      rws.numel(), stream), "router")
+        sh = L["shared"]
+        bank = L["bank"]
+        N.check(lib.glm53_packed_decode_moe(
+            x.data_ptr(), H, idxs[i].data_ptr(), scs[i].data_ptr(), TOP_K, bank.gate_up_weight.data_ptr(),
+            bank.gate_up_scale_inv.data_ptr(), bank.down_weight.data_ptr(), bank.down_scale_inv.data_ptr(), E, I,
+            sh[0].data_ptr(), sh[1].data_ptr(), sh[2].data_ptr(), sh[3].data_ptr(), sh[4].data_ptr(),
+            sh[5].data_ptr(), I, LIMIT, outs[i].data_ptr(), dws.data_ptr(), dws.numel(), status.data_ptr(),
+            stream), "decode")
+
+    s = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(s):
+        for i in range(n_graphs):  # eager warm-up (sets kernel attributes)
+            step(i, s.cuda_stream)
+    s.synchronize()
+    graphs = []
+    for i in range(n_graphs):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            step(i, torch.cuda.current_stream().cuda_stream)
+        graphs.append(g)
+    torch.cuda.synchronize()
+
+    for i in range(args.warmup):
+        graphs[i % n_graphs].replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        torch.cuda.synchronize()
+        barrier(world)
+        start.record()
+        for i in range(args.steps):
+            graphs[i % n_graphs].replay()
+        stop.record()
+        torch.cuda.synchronize()
+        barrier(world)
+    t_ms = max_over_ranks(start.elapsed_time(stop), world)
+    if int(status.item()) != 0:
+        raise RuntimeError(f"device status 0x{int(status.item()):x} during the timed region")
+    clk = clocks.summary()
+    tokens = args.steps * world
+    value = tokens / (t_ms / 1e3)
+
+    # ---- dominant kernel alone: fused gate/up/SwiGLU, CUDA events ---------
+    torch.cuda.synchronize()
+    k_start, k_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    cur = torch.cuda.current_stream().cuda_stream
+    reps = max(args.steps, 64)
+    k_start.record()
+    for i in range(reps):
+        L = layers[i % args.layers]
+        sh = L["shared"]
+        bank = L["bank"]
+        N.check(lib.glm53_packed_decode_gate_up(
+            xs[i % POOL].data_ptr(), H, idxs[i % n_graphs].data_ptr(), TOP_K, bank.gate_up_weight.data_ptr(),
+            bank.gate_up_scale_inv.data_ptr(), E, I, sh[0].data_ptr(), sh[1].data_ptr(), sh[2].data_ptr(),
+            sh[3].data_ptr(), I, LIMIT, dws.data_ptr(), dws.numel(), status.data_ptr(), cur), "gate_up")
+    k_stop.record()
+    torch.cuda.synchronize()
+    k_ms = k_start.elapsed_time(k_stop) / reps
+    peaks = measured_peaks()
+    achieved = GATE_UP_BYTES / (k_ms / 1e3) / 1e9
+    roofline = {"kernel": "decode_gate_up_kernel", "bound": "hbm", "achieved": round(achieved, 1),
+                "peak": peaks["hbm_gbs"], "peak_source": peaks["source"], "unit": "GB/s",
+                "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
+                "algorithmic_bytes_per_launch": GATE_UP_BYTES, "avg_launch_us": round(k_ms * 1e3, 2),
+                "step_bytes": STEP_BYTES,
+                "step_frac": round(STEP_BYTES / (t_ms / args.steps / 1e3) / 1e9 / peaks["hbm_gbs"], 4)}
+
+    # ---- e2e through the public module API -------------------------------
+    mods = []
+    for L in layers:
+        cfg = S.moe_config(H, I, E, TOP_K, LIMIT)
+        gate = Float32Gate(cfg, device=dev)
+        gate.weight.copy_(L["router_w"])
+        gate.e_score_correction_bias.copy_(L["router_b"])
+        mods.append(G.PackedFP8MoE(L["bank"], cfg, gate, L["shared_mod"]))
+    x_host = xs.cpu().reshape(POOL, 1, 1, H).pin_memory()
+    y_host = torch.empty((POOL, 1, 1, H), dtype=torch.bfloat16).pin_memory()
+    for i in range(args.warmup):
+        xd = x_host[i % POOL].to(dev, non_blocking=True)
+        y_host[i % POOL].copy_(mods[i % args.layers](xd), non_blocking=True)
+    torch.cuda.synchronize()
+    barrier(world)
+    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record()
+    for i in range(args.steps):
+        xd = x_host[i % POOL].to(dev, non_blocking=True)
+        y_host[i % POOL].copy_(mods[i % args.layers](xd), non_blocking=True)
+    e_stop.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    e_ms = max_over_ranks(e_start.elapsed_time(e_stop), world)
+    e2e = {"value": round(tokens / (e_ms / 1e3), 2), "unit": "tokens/s", "h2d_bytes_per_step": H * 2,
+           "d2h_bytes_per_step": H * 2, "api": "PackedFP8MoE.__call__ (Float32Gate router)"}
+
+    extra = {}
+    if not args.no_prefill:
+        extra["prefill_2048"] = bench_prefill(layers, dev, args)
+    return {"value": value, "t_ms": t_ms, "clocks": clk, "roofline": roofline, "e2e": e2e,
+            "gpu_launches": args.steps * 3, **extra}, layers, xs
+
+
+def bench_prefill(layers, dev, args):
+    """Secondary: config 3 grouped prefill, T=2048, Zipf-skewed router bias."""
+    import torch
+
+    import glm53_flash_mlx_b200 as G
+    from glm53_flash_mlx_b200 import _native as N
+    from glm53_flash_mlx_b200 import synthetic as S
+
+    T = 2048
+    x = S.random_bf16((T, H), seed=4242, device=dev)
+    w, b = S.make_router(E, H, seed=4243, device=dev, zipf_alpha=0.5)
+    ws = N.Workspace()
+    idx, sc = G.router_topk(x, w, b, top_k=TOP_K, workspace=ws)
+    touched = int(torch.unique(idx).numel())
+    for i in range(3):
+        L = layers[i % len(layers)]
+        G.router_topk(x, w, b, top_k=TOP_K, workspace=ws)
+        G.grouped_moe(x, idx, sc, L["bank"], L["shared"], limit=LIMIT, workspace=ws)
+    torch.cuda.synchronize()
+    reps = 8
+    st, sp = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st.record()
+    for i in range(reps):
+        L = layers[i % len(layers)]
+        G.router_topk(x, w, b, top_k=TOP_K, workspace=ws)
+        G.grouped_moe(x, idx, sc, L["bank"], L["shared"], limit=LIMIT, workspace=ws)
+    sp.record()
+    torch.cuda.synchronize()
+    ms = st.elapsed_time(sp) / reps
+    bytes_ = (touched + 1) * 3 * H * I + E * H * 4 + 2 * T * H * 2
+    flops = 2 * T * TOP_K * 3 * H * I + 2 * T * 3 * H * I + 2 * T * E * H
+    peaks = measured_peaks()
+    return {"tokens_per_s": round(T / (ms / 1e3), 1), "ms_per_layer": round(ms, 3), "touched_experts": touched,
+            "algorithmic_bytes": bytes_, "flops": flops,
+            "hbm_frac": round(bytes_ / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
+            "note": "router + route plan + grouped gate/up (SwiGLU epilogue) + grouped down + shared + combine"}
+
+
+# ---------------------------------------------------------------------------
+# CPU side (oracle port of the reference kernels)
+# ---------------------------------------------------------------------------
+
+
+def host_layer(layer):
+    """Host copies of one layer's weights for the CPU restatement."""
+    bank = layer["bank"]
+    return {
+        "bank": tuple(t.cpu().numpy() for t in (bank.gate_up_weight, bank.gate_up_scale_inv, bank.down_weight,
+                                                bank.down_scale_inv)),
+        "shared": tuple(t.cpu().numpy() for t in layer["shared"]),
+        "router_w": layer["router_w"].cpu().numpy(),
+        "router_b": layer["router_b"].cpu().numpy(),
+    }
+
+
+def cpu_token(O, hl, x_bits, threads):
+    idx, sc, _, _ = O.router(x_bits[None, :], hl["router_w"], hl["router_b"], top_k=TOP_K, threads=threads)
+    return O.packed_decode_moe(x_bits, idx[0], sc[0], hl["bank"], hl["shared"], LIMIT, threads=threads)
+
+
+def cpu_baseline(hl, xs_bits, seconds: float) -> dict:
+    import oracle as O
+
+    threads = O.default_threads()
+    cpu_token(O, hl, xs_bits[0], threads)  # warm
+    n, t0 = 0, time.perf_counter()
+    while True:
+        cpu_token(O, hl, xs_bits[n % len(xs_bits)], threads)
+        n += 1
+        el = time.perf_counter() - t0
+        if (el >= seconds and n >= 2) or n >= 2000:
+            break
+    return {"value": round(n / el, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{n} decode tokens through one config-2 layer (router + 8 experts + shared), "
+                      f"{el:.1f} s on {threads} host threads"}
+
+
+def bench_reference(args, world, rank, local):
+    """--impl reference: the CPU restatement of the reference kernels."""
+    import torch
+
+    import oracle as O
+    from glm53_flash_mlx_b200 import synthetic as S
+
+    dev = torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
+    layer = build_layers(1, 1000, dev)[0]
+    hl = host_layer(layer)
+    xs = S.random_bf16((POOL, H), seed=77, device=dev)
+    xs_bits = xs.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+    del layer
+    threads = O.default_threads()
+    for i in range(args.warmup):
+        cpu_token(O, hl, xs_bits[i % POOL], threads)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        cpu_token(O, hl, xs_bits[i % POOL], threads)
+    el = time.perf_counter() - t0
+    value = args.steps / el
+    return {
+        "metric": "FP8 MoE decode layer tokens/s (L=1, batch 1)", "value": round(value, 3), "unit": "tokens/s",
+        "impl": "reference", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(el / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "e4m3xbf16->f32", "data": "synthetic",
+        "config": config_block(args, 1),
+        "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} timed decode tokens (one config-2 layer each) after "
+                                   f"{args.warmup} warm-up tokens, {threads} host threads"},
+        "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def config_block(args, world):
+    return {"workload": "config2: packed decode MoE layer, L=1, batch 1 (router + top-8 of 288 + shared)",
+            "hidden": H, "moe_intermediate": I, "experts": E, "top_k": TOP_K, "swiglu_limit": LIMIT,
+            "weights": "E4M3 + FP32 128x128 block scales, seeded N(0,0.02) amax/448",
+            "global_batch": 1 * world, "seq_len": 1,
+            "l2": f"inputs larger than L2: {args.layers} distinct layers rotated "
+                  f"({args.layers * 5.44:.1f} GB of experts) and a {POOL}-vector activation pool; no flush",
+            "parallelism": f"replicas{world}" if world > 1 else "single"}
+
+
+def main():
+    args = parse_args()
+    world, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(bench_reference(args, world, rank, local)), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return
+    res, layers, xs = bench_b200(args, world, rank, local)
+    line = {
+        "metric": "FP8 MoE decode layer tokens/s (L=1, batch 1)",
+        "value": round(res["value"], 2),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(res["t_ms"] / args.steps, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "e4m3xbf16->f32",
+        "data": "synthetic (seeded random-init weights of the config-2 shapes)",
+        "config": config_block(args, world),
+        "clocks": res["clocks"],
+        "roofline": res["roofline"],
+        "e2e": res["e2e"],
+        "gpu_launches": res["gpu_launches"],
+    }
+    if "prefill_2048" in res:
+        line["prefill_2048"] = res["prefill_2048"]
+    if rank == 0 and world == 1:
+        import torch
+
+        hl = host_layer(layers[0])
+        xs_bits = xs.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+        line["cpu_baseline"] = cpu_baseline(hl, xs_bits, args.cpu_seconds)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,161 @@
+"""ctypes binding of the sm_100a C-ABI library (``include/glm53_b200.h``).
+
+The library is built in-tree by ``glm53_flash_mlx_b200.build`` into
+``_lib/libglm53_b200.so``.  There is no fallback: every operator raises
+``RuntimeError`` when the library is missing or no CUDA device is present,
+mirroring the reference's fail-closed ``RuntimeError`` when Metal is absent
+(glm53_flash_mlx/fp8.py:256-257).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libglm53_b200.so"
+
+GLM53_OK = 0
+GLM53_ERR_INVALID = 1
+GLM53_ERR_CUDA = 2
+GLM53_ERR_INDEX = 3
+
+STATUS_BAD_EXPERT = 1
+STATUS_WAIT_TIMEOUT = 2
+STATUS_BAD_GEOMETRY = 4
+
+_vp = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_int = ctypes.c_int
+_f = ctypes.c_float
+_sz = ctypes.c_size_t
+
+# name -> (restype, argtypes); mirrors include/glm53_b200.h
+SIGNATURES: dict[str, tuple] = {
+    "glm53_kernel_abi": (ctypes.c_char_p, []),
+    "glm53_last_error": (ctypes.c_char_p, []),
+    "glm53_fp8_linear": (_int, [_vp, _i64, _i64, _vp, _i64, _vp, _vp, _vp]),
+    "glm53_router_workspace_bytes": (_sz, [_i64, _i64]),
+    "glm53_router_topk": (
+        _int,
+        [_vp, _i64, _i64, _vp, _i64, _vp, _int, _int, _int, _int, _f, _vp, _vp, _vp, _vp, _sz, _vp],
+    ),
+    "glm53_packed_decode_workspace_bytes": (_sz, [_int, _i64, _i64]),
+    "glm53_packed_decode_moe": (
+        _int,
+        [_vp, _i64, _vp, _vp, _int, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _f,
+         _vp, _vp, _sz, _vp, _vp],
+    ),
+    "glm53_packed_decode_gate_up": (
+        _int,
+        [_vp, _i64, _vp, _int, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _f, _vp, _sz, _vp, _vp],
+    ),
+    "glm53_route_plan": (
+        _int,
+        [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
+    ),
+    "glm53_gather_rows": (_int, [_vp, _i64, _vp, _i64, _int, _vp, _vp]),
+    "glm53_grouped_fp8_linear": (
+        _int,
+        [_vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _vp, _vp, _vp],
+    ),
+    "glm53_activate_gate_up": (_int, [_vp, _i64, _i64, _f, _vp, _vp]),
+    "glm53_restore_and_reduce": (_int, [_vp, _vp, _vp, _i64, _int, _i64, _vp, _vp, _vp]),
+    "glm53_grouped_moe_workspace_bytes": (_sz, [_i64, _int, _i64, _i64, _i64, _i64]),
+    "glm53_grouped_moe": (
+        _int,
+        [_vp, _i64, _i64, _vp, _vp, _int, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp,
+         _i64, _f, _vp, _vp, _sz, _vp, _vp],
+    ),
+    "glm53_sigmoid_bf16": (_int, [_vp, _i64, _vp, _vp]),
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+def load_library(path: Path | None = None) -> ctypes.CDLL:
+    """Load the C-ABI library (no CUDA device needed to load it)."""
+    global _lib
+    with _lock:
+        if _lib is None or path is not None:
+            p = Path(path) if path is not None else LIB_PATH
+            if not p.exists():
+                raise RuntimeError(
+                    f"GLM-5.3 B200 CUDA extension not built ({p} missing); run "
+                    "`python -m glm53_flash_mlx_b200.build`"
+                )
+            lib = ctypes.CDLL(str(p))
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            if path is not None:
+                return lib
+            _lib = lib
+    return _lib
+
+
+def lib() -> ctypes.CDLL:
+    """The library, for a CUDA device: raises RuntimeError otherwise."""
+    if not torch.cuda.is_available():
+        raise RuntimeError("direct GLM-5.3 FP8 execution requires the CUDA (sm_100a) backend")
+    return load_library()
+
+
+def kernel_abi() -> str:
+    return load_library().glm53_kernel_abi().decode()
+
+
+def check(rc: int, what: str) -> None:
+    if rc == GLM53_OK:
+        return
+    msg = (load_library().glm53_last_error() or b"").decode() or what
+    if rc == GLM53_ERR_INVALID:
+        raise ValueError(msg)
+    if rc == GLM53_ERR_INDEX:
+        raise IndexError(msg)
+    raise RuntimeError(msg)
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def stream(device: torch.device | None = None) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def require_cuda(*tensors: torch.Tensor) -> torch.device:
+    lib()
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError("direct GLM-5.3 FP8 execution requires CUDA tensors")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError(f"tensors on different devices: {dev} vs {t.device}")
+    return dev
+
+
+class Workspace:
+    """Per-device, grow-only, zero-initialised scratch buffers owned by a plan.
+
+    Addresses are stable until a larger size is requested (the reference's
+    plan-owned scratch rule, glm53_flash_mlx/native_execution.py:141-165)."""
+
+    def __init__(self) -> None:
+        self._buffers: dict[tuple, torch.Tensor] = {}
+
+    def get(self, device: torch.device, key: str, nbytes: int) -> torch.Tensor:
+        k = (device, key)
+        buf = self._buffers.get(k)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.zeros(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+            self._buffers[k] = buf
+        return buf

@@ -1,0 +1,58 @@
+// Internal (non-ABI) declarations shared between the kernel translation units.
+#pragma once
+
+#include "common.cuh"
+
+namespace glm53 {
+
+// glm53_fp8_linear routes M <= kGemvMaxRows to the bandwidth GEMV and larger
+// M to the tensor-core GEMM.
+constexpr int64_t kGemvMaxRows = 16;
+
+int fp8_linear_small_m(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w, int64_t N,
+                       const float* s, uint16_t* y, cudaStream_t stream);
+
+// Tensor-core grouped GEMM (grouped.cu).
+//   A rows: x[a_index ? a_index[start+i] / a_div : start+i, :]  (BF16 [*, K])
+//   B: expert e rows of w_gate (and w_up for the fused SwiGLU mode).
+struct GroupedGemmArgs {
+  const uint16_t* x;          // activations, row stride K
+  const uint32_t* a_index;    // optional row indirection (sorted route order)
+  int a_div;                  // divisor applied to a_index (top_k)
+  int64_t R;                  // rows addressed by descriptors (routes)
+  int64_t K;
+  const uint32_t* tile_experts;
+  const uint32_t* tile_starts;
+  const uint32_t* tile_lengths;
+  int64_t capacity;           // descriptor slots (dense mode: ceil(R / 128))
+  bool dense;                 // descriptors implicit: (0, 128 d, min(128, R - 128 d))
+  const uint8_t* w_gate;      // [E, N_out, K] (plain) or gate rows (SwiGLU)
+  const uint8_t* w_up;        // up rows (SwiGLU) or nullptr
+  int64_t w_expert_stride;    // bytes between experts
+  const float* s_gate;
+  const float* s_up;
+  int64_t s_expert_stride;    // floats between experts
+  int64_t E;
+  int64_t N;                  // output columns (plain: N; SwiGLU: I)
+  bool swiglu;
+  float limit;
+  uint16_t* out;              // [R, N] BF16
+  uint32_t* status;
+};
+
+int grouped_gemm(const GroupedGemmArgs& a, cudaStream_t stream);
+
+bool dense_gemm_supported(int64_t K, int64_t N, const void* w);
+int dense_fp8_gemm(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w, int64_t N,
+                   const float* s, uint16_t* y, cudaStream_t stream);
+
+// Route plan (route_plan.cu), usable inside composite entry points.
+int route_plan(const uint32_t* ids, int64_t R, int64_t E, int64_t tile_rows, const float* scores,
+               uint32_t* order, uint32_t* inverse, uint32_t* sorted_experts, float* sorted_scores,
+               uint32_t* route_offsets, uint32_t* tile_experts, uint32_t* tile_starts,
+               uint32_t* tile_lengths, uint32_t* tile_offsets, uint32_t* descriptor_count,
+               uint32_t* invalid_count, cudaStream_t stream);
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+}  // namespace glm53

@@ -1,0 +1,314 @@
+// FP32 router (G0): logits, sigmoid, bias, optional group mask, top-k,
+// normalisation and scaling.
+//
+// Replaces Float32Gate.__call__ (glm53_flash_mlx/patch.py:131-142) and the
+// mlx-vlm group_expert_select it calls (mlx-vlm 0.6.17 @ e82d557, not vendored
+// in the reference; restated from its published algorithm):
+//   s = sigmoid(logits); choice = s + e_score_correction_bias;
+//   if n_group > 1: group score = sum of the top-2 choices in each group, the
+//     n_group - topk_group lowest groups have their choices set to 0.0;
+//   idx = top_k of choice; scores = s[idx]; if top_k > 1 and norm_topk_prob:
+//     scores /= sum(scores); scores *= routed_scaling_factor.
+// The reference's argpartition leaves slot order unspecified; here slots are
+// in descending choice, ties to the lower expert id.
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace glm53 {
+
+constexpr int kRouterSmallT = 8;   // tokens handled by the fused GEMV+top-k launch
+constexpr int kRouterMaxE = 1024;  // 32 lanes x 32 values per lane
+constexpr int kRouterMaxK = 32;
+
+struct TopkParams {
+  int E, top_k, n_group, topk_group, norm;
+  float scale;
+};
+
+// One warp selects the top-k of one token's logits (shared-memory scratch
+// `choice_smem` holds E floats for the group mask).
+template <int PER>
+__device__ void warp_topk(const float* logits, const float* __restrict__ bias, const TopkParams& p,
+                          uint32_t* idx_out, float* score_out, float* choice_smem) {
+  const int lane = threadIdx.x & 31;
+  float sig[PER], choice[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    int e = lane + 32 * i;
+    if (e < p.E) {
+      float l = __ldcg(logits + e);
+      float sg = 1.0f / (1.0f + expf(-l));
+      sig[i] = sg;
+      choice[i] = sg + bias[e];
+    } else {
+      sig[i] = 0.f;
+      choice[i] = -INFINITY;
+    }
+  }
+  if (p.n_group > 1) {
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      int e = lane + 32 * i;
+      if (e < p.E) choice_smem[e] = choice[i];
+    }
+    __syncwarp();
+    const int per_group = p.E / p.n_group;
+    // lane g computes the top-2 sum of group g (n_group <= 32)
+    float gscore = -INFINITY;
+    if (lane < p.n_group) {
+      float b1 = -INFINITY, b2 = -INFINITY;
+      for (int e = lane * per_group; e < (lane + 1) * per_group; ++e) {
+        float v = choice_smem[e];
+        if (v > b1) { b2 = b1; b1 = v; } else if (v > b2) { b2 = v; }
+      }
+      gscore = b1 + b2;
+    }
+    // drop the n_group - topk_group lowest groups (ties: the higher index first)
+    uint32_t dropped = 0;
+    for (int d = 0; d < p.n_group - p.topk_group; ++d) {
+      float v = (lane < p.n_group && !((dropped >> lane) & 1u)) ? gscore : INFINITY;
+      int g = lane;
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) {
+        float ov = __shfl_xor_sync(0xffffffffu, v, o);
+        int og = __shfl_xor_sync(0xffffffffu, g, o);
+        if (ov < v || (ov == v && og > g)) { v = ov; g = og; }
+      }
+      dropped |= 1u << g;
+    }
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      int e = lane + 32 * i;
+      if (e < p.E && ((dropped >> (e / per_group)) & 1u)) choice[i] = 0.0f;
+    }
+    __syncwarp();
+  }
+  uint32_t taken = 0;  // bit i: value i of this lane selected
+  float total = 0.f;
+  float picked_sig[kRouterMaxK];
+  uint32_t picked_idx[kRouterMaxK];
+  for (int j = 0; j < p.top_k; ++j) {
+    float v = -INFINITY;
+    int best = 0x7fffffff;
+    float bs = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      int e = lane + 32 * i;
+      if (e < p.E && !((taken >> i) & 1u)) {
+        if (choice[i] > v || (choice[i] == v && e < best)) { v = choice[i]; best = e; bs = sig[i]; }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+      float ov = __shfl_xor_sync(0xffffffffu, v, o);
+      int ob = __shfl_xor_sync(0xffffffffu, best, o);
+      float os = __shfl_xor_sync(0xffffffffu, bs, o);
+      if (ov > v || (ov == v && ob < best)) { v = ov; best = ob; bs = os; }
+    }
+    if ((best & 31) == lane) taken |= 1u << (best >> 5);
+    picked_idx[j] = (uint32_t)best;
+    picked_sig[j] = bs;
+  }
+  if (lane == 0) {
+    for (int j = 0; j < p.top_k; ++j) total = total + picked_sig[j];
+    for (int j = 0; j < p.top_k; ++j) {
+      float v = picked_sig[j];
+      if (p.top_k > 1 && p.norm) v = v / total;
+      idx_out[j] = picked_idx[j];
+      score_out[j] = v * p.scale;
+    }
+  }
+}
+
+// Split-K FP32 GEMV for T <= kRouterSmallT tokens: 4 warps per expert row,
+// 2 rows per 256-thread block.  The last block to finish runs the top-k.
+template <int T_MAX, int PER>
+__global__ void __launch_bounds__(256) router_small_kernel(
+    const uint16_t* __restrict__ x, int T, int H, const float* __restrict__ w,
+    const float* __restrict__ bias, TopkParams p, float* logits, uint32_t* counter,
+    uint32_t* __restrict__ idx, float* __restrict__ scores) {
+  __shared__ float part[8][T_MAX];
+  __shared__ bool is_last;
+  __shared__ float choice_smem[8][kRouterMaxE];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e = blockIdx.x * 2 + (warp >> 2);
+  const int q = warp & 3;
+  float acc[T_MAX];
+#pragma unroll
+  for (int t = 0; t < T_MAX; ++t) acc[t] = 0.f;
+  if (e < p.E) {
+    const float* wr = w + (size_t)e * H;
+    const int per = H / 4;  // H % 128 == 0 checked by the host
+    const int k0 = q * per;
+    for (int k = k0 + lane * 4; k < k0 + per; k += 128) {
+      float4 wv = __ldcs(reinterpret_cast<const float4*>(wr + k));
+#pragma unroll
+      for (int t = 0; t < T_MAX; ++t) {
+        if (t < T) {
+          uint2 raw = __ldg(reinterpret_cast<const uint2*>(x + (size_t)t * H + k));
+          acc[t] = fmaf(__uint_as_float(raw.x << 16), wv.x, acc[t]);
+          acc[t] = fmaf(__uint_as_float(raw.x & 0xFFFF0000u), wv.y, acc[t]);
+          acc[t] = fmaf(__uint_as_float(raw.y << 16), wv.z, acc[t]);
+          acc[t] = fmaf(__uint_as_float(raw.y & 0xFFFF0000u), wv.w, acc[t]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < T_MAX; ++t) {
+    float v = warp_sum(acc[t]);
+    if (lane == 0) part[warp][t] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x < 2 * T_MAX) {
+    int r = threadIdx.x / T_MAX, t = threadIdx.x % T_MAX;
+    int er = blockIdx.x * 2 + r;
+    if (er < p.E && t < T) {
+      float v = ((part[4 * r][t] + part[4 * r + 1][t]) + (part[4 * r + 2][t] + part[4 * r + 3][t]));
+      logits[(size_t)t * p.E + er] = v;
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned prev = atomicAdd(counter, 1u);
+    is_last = (prev == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  if (warp < T) {
+    warp_topk<PER>(logits + (size_t)warp * p.E, bias, p, idx + (size_t)warp * p.top_k,
+                   scores + (size_t)warp * p.top_k, choice_smem[warp]);
+  }
+  if (threadIdx.x == 0) *counter = 0u;  // leave the workspace reusable
+}
+
+// Tiled FP32 GEMM for larger T: logits[T,E] = x[T,H] @ w[E,H]^T.
+// 64x64 output tile per block, 256 threads, 4x4 outputs each.
+__global__ void __launch_bounds__(256) router_gemm_kernel(const uint16_t* __restrict__ x, int T, int H,
+                                                          const float* __restrict__ w, int E,
+                                                          float* __restrict__ logits) {
+  constexpr int BM = 64, BN = 64, BK = 16;
+  __shared__ float xs[BK][BM + 4];
+  __shared__ float ws[BK][BN + 4];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int t0 = blockIdx.x * BM, e0 = blockIdx.y * BN;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < H; k0 += BK) {
+    // 64 rows x 16 k = 1024 values per operand, 4 per thread
+    for (int i = threadIdx.x; i < BM * BK; i += 256) {
+      int r = i / BK, k = i % BK;
+      int t = t0 + r, e = e0 + r;
+      xs[k][r] = (t < T && k0 + k < H) ? bf16_bits_to_f32(x[(size_t)t * H + k0 + k]) : 0.f;
+      ws[k][r] = (e < E && k0 + k < H) ? w[(size_t)e * H + k0 + k] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < BK; ++k) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = xs[k][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = ws[k][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    int t = t0 + ty * 4 + i;
+    if (t >= T) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int e = e0 + tx * 4 + j;
+      if (e < E) logits[(size_t)t * E + e] = acc[i][j];
+    }
+  }
+}
+
+template <int PER>
+__global__ void __launch_bounds__(256) router_topk_kernel(const float* logits, int T,
+                                                          const float* __restrict__ bias, TopkParams p,
+                                                          uint32_t* __restrict__ idx,
+                                                          float* __restrict__ scores) {
+  __shared__ float choice_smem[8][kRouterMaxE];
+  const int warp = threadIdx.x >> 5;
+  const int t = blockIdx.x * 8 + warp;
+  if (t >= T) return;
+  warp_topk<PER>(logits + (size_t)t * p.E, bias, p, idx + (size_t)t * p.top_k,
+                 scores + (size_t)t * p.top_k, choice_smem[warp]);
+}
+
+template <int PER>
+static int launch_topk(const float* logits, int T, const float* bias, TopkParams p, uint32_t* idx,
+                       float* scores, cudaStream_t st) {
+  router_topk_kernel<PER><<<(T + 7) / 8, 256, 0, st>>>(logits, T, bias, p, idx, scores);
+  return check_launch("router_topk_kernel");
+}
+
+template <int PER>
+static int launch_small(const uint16_t* x, int T, int H, const float* w, const float* bias, TopkParams p,
+                        float* logits, uint32_t* counter, uint32_t* idx, float* scores, cudaStream_t st) {
+  int blocks = (p.E + 1) / 2;
+  if (T <= 1)
+    router_small_kernel<1, PER><<<blocks, 256, 0, st>>>(x, T, H, w, bias, p, logits, counter, idx, scores);
+  else
+    router_small_kernel<kRouterSmallT, PER><<<blocks, 256, 0, st>>>(x, T, H, w, bias, p, logits, counter, idx,
+                                                                    scores);
+  return check_launch("router_small_kernel");
+}
+
+}  // namespace glm53
+
+using namespace glm53;
+
+extern "C" size_t glm53_router_workspace_bytes(int64_t T, int64_t E) {
+  return align_up((size_t)std::max<int64_t>(T, 1) * (size_t)E * sizeof(float), 256) + 256;
+}
+
+extern "C" int glm53_router_topk(const void* x, int64_t T, int64_t H, const float* w, int64_t E,
+                                 const float* bias, int top_k, int n_group, int topk_group,
+                                 int norm_topk_prob, float routed_scaling_factor, uint32_t* indices,
+                                 float* scores, float* logits, void* workspace, size_t workspace_bytes,
+                                 void* stream) {
+  if (T < 0 || H <= 0 || E <= 0 || E > kRouterMaxE || top_k <= 0 || top_k > kRouterMaxK || top_k > E) {
+    set_last_error("glm53_router_topk: unsupported geometry T=%lld H=%lld E=%lld top_k=%d",
+                   (long long)T, (long long)H, (long long)E, top_k);
+    return GLM53_ERR_INVALID;
+  }
+  if (n_group > 1 && (n_group > 32 || E % n_group != 0 || topk_group < 1 || topk_group > n_group)) {
+    set_last_error("glm53_router_topk: invalid grouping n_group=%d topk_group=%d", n_group, topk_group);
+    return GLM53_ERR_INVALID;
+  }
+  if (T == 0) return GLM53_OK;
+  if (!x || !w || !bias || !indices || !scores || !workspace ||
+      workspace_bytes < glm53_router_workspace_bytes(T, E)) {
+    set_last_error("glm53_router_topk: missing pointer or workspace too small");
+    return GLM53_ERR_INVALID;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  char* ws = (char*)workspace;
+  float* lbuf = logits ? logits : (float*)ws;
+  uint32_t* counter = (uint32_t*)(ws + align_up((size_t)T * E * sizeof(float), 256));
+  TopkParams p{(int)E, top_k, n_group < 1 ? 1 : n_group, topk_group, norm_topk_prob, routed_scaling_factor};
+  const bool vec = (H % 128 == 0) && (((uintptr_t)w & 15) == 0) && (((uintptr_t)x & 7) == 0);
+  const int per = (int)((E + 31) / 32);
+  if (T <= kRouterSmallT && vec) {
+    if (per <= 4) return launch_small<4>((const uint16_t*)x, (int)T, (int)H, w, bias, p, lbuf, counter, indices, scores, st);
+    if (per <= 10) return launch_small<10>((const uint16_t*)x, (int)T, (int)H, w, bias, p, lbuf, counter, indices, scores, st);
+    return launch_small<32>((const uint16_t*)x, (int)T, (int)H, w, bias, p, lbuf, counter, indices, scores, st);
+  }
+  dim3 grid((unsigned)((T + 63) / 64), (unsigned)((E + 63) / 64));
+  router_gemm_kernel<<<grid, 256, 0, st>>>((const uint16_t*)x, (int)T, (int)H, w, (int)E, lbuf);
+  int rc = check_launch("router_gemm_kernel");
+  if (rc) return rc;
+  if (per <= 4) return launch_topk<4>(lbuf, (int)T, bias, p, indices, scores, st);
+  if (per <= 10) return launch_topk<10>(lbuf, (int)T, bias, p, indices, scores, st);
+  return launch_topk<32>(lbuf, (int)T, bias, p, indices, scores, st);
+}

@@ -1,0 +1,181 @@
+"""Direct E4M3 block-FP8 operators on B200 (sm_100a).
+
+Counterpart of glm53_flash_mlx/fp8.py: ``block_fp8_linear`` (fp8.py:254-299),
+``BlockFP8Linear`` (fp8.py:302-326), ``DirectFP8Expert`` (fp8.py:329-340) and
+``DirectFP8MoE`` (fp8.py:343-400) with the same argument meaning, the same
+fail-closed checks and the same exceptions.  Weights stay uint8 E4M3 codes with
+FP32 ``weight_scale_inv`` on the 128x128 grid; they are decoded only in
+registers or shared memory inside the CUDA kernels.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import nn
+
+from . import _native as N
+from .abi import KERNEL_ABI_VERSION  # noqa: F401  (re-exported like the reference)
+
+BLOCK_SIZE = 128
+THREADS = 256
+DECODE_TOP_K = 8
+PREFILL_TILE_ROWS = 8
+
+
+def _scale_shape(out_features: int, in_features: int) -> tuple[int, int]:
+    return ((out_features + BLOCK_SIZE - 1) // BLOCK_SIZE, (in_features + BLOCK_SIZE - 1) // BLOCK_SIZE)
+
+
+def block_fp8_linear(x: torch.Tensor, weight: torch.Tensor, scale_inv: torch.Tensor) -> torch.Tensor:
+    """Compute ``x @ dequant(weight, scale_inv).T`` without expanding weight.
+
+    x: BF16 [..., in] on a CUDA device; weight: uint8 E4M3 [out, in];
+    scale_inv: float32 [ceil(out/128), ceil(in/128)].  Returns BF16 [..., out].
+    """
+    if not (isinstance(x, torch.Tensor) and x.is_cuda):
+        raise RuntimeError("direct GLM-5.3 FP8 execution requires the CUDA backend")
+    N.lib()
+    if weight.dtype != torch.uint8 or weight.dim() != 2:
+        raise ValueError(f"expected 2-D uint8 E4M3 weight, got {tuple(weight.shape)} {weight.dtype}")
+    if scale_inv.dtype != torch.float32 or scale_inv.dim() != 2:
+        raise ValueError("weight_scale_inv must be a 2-D float32 block table")
+    out_features, in_features = weight.shape
+    if x.shape[-1] != in_features:
+        raise ValueError(f"input width {x.shape[-1]} != weight width {in_features}")
+    expected = _scale_shape(out_features, in_features)
+    if tuple(scale_inv.shape) != expected:
+        raise ValueError(f"scale shape {tuple(scale_inv.shape)} != block128 shape {expected}")
+    if x.dtype != torch.bfloat16:
+        raise ValueError(f"block_fp8_linear computes on BF16 activations, got {x.dtype}")
+    N.require_cuda(x, weight, scale_inv)
+    original_shape = x.shape
+    flat = x.reshape(-1, in_features).contiguous()
+    weight = weight.contiguous()
+    scale_inv = scale_inv.contiguous()
+    out = torch.empty((flat.shape[0], out_features), dtype=x.dtype, device=x.device)
+    if flat.shape[0]:
+        N.check(
+            N.lib().glm53_fp8_linear(
+                flat.data_ptr(), flat.shape[0], in_features, weight.data_ptr(), out_features,
+                scale_inv.data_ptr(), out.data_ptr(), N.stream(x.device),
+            ),
+            "glm53_fp8_linear",
+        )
+    return out.reshape(*original_shape[:-1], out_features)
+
+
+class BlockFP8Linear(nn.Module):
+    """``nn.Linear`` ABI backed by canonical block-128 E4M3 tensors."""
+
+    def __init__(self, in_features: int, out_features: int, bias: bool = False, device=None):
+        super().__init__()
+        self.in_features = in_features
+        self.out_features = out_features
+        self.register_buffer("weight", torch.zeros((out_features, in_features), dtype=torch.uint8, device=device))
+        self.register_buffer(
+            "weight_scale_inv",
+            torch.ones(_scale_shape(out_features, in_features), dtype=torch.float32, device=device),
+        )
+        if bias:
+            self.register_buffer("bias", torch.zeros((out_features,), dtype=torch.float32, device=device))
+        else:
+            self.bias = None
+
+    @classmethod
+    def from_linear(cls, linear: nn.Module) -> "BlockFP8Linear":
+        out_features, in_features = linear.weight.shape
+        return cls(in_features, out_features, bias=getattr(linear, "bias", None) is not None,
+                   device=linear.weight.device)
+
+    def forward(self, x):
+        y = block_fp8_linear(x, self.weight, self.weight_scale_inv)
+        return (y + self.bias).to(y.dtype) if self.bias is not None else y
+
+
+def swiglu_pair(gate: torch.Tensor, up: torch.Tensor, limit: float) -> torch.Tensor:
+    """silu(min(gate, L)) * clip(up, -L, L) on BF16 tensors with the reference's
+    per-op BF16 rounding (the MLX ops of glm53_flash_mlx/fp8.py:337-340)."""
+    inter = gate.shape[-1]
+    fused = torch.cat([gate.reshape(-1, inter), up.reshape(-1, inter)], dim=-1).contiguous()
+    hidden = torch.empty((fused.shape[0], inter), dtype=torch.bfloat16, device=gate.device)
+    if fused.shape[0]:
+        N.check(
+            N.lib().glm53_activate_gate_up(fused.data_ptr(), fused.shape[0], inter, float(limit),
+                                           hidden.data_ptr(), N.stream(gate.device)),
+            "glm53_activate_gate_up",
+        )
+    return hidden.reshape(gate.shape)
+
+
+class DirectFP8Expert(nn.Module):
+    def __init__(self, hidden_size: int, intermediate_size: int, limit: float, device=None):
+        super().__init__()
+        self.gate_proj = BlockFP8Linear(hidden_size, intermediate_size, device=device)
+        self.up_proj = BlockFP8Linear(hidden_size, intermediate_size, device=device)
+        self.down_proj = BlockFP8Linear(intermediate_size, hidden_size, device=device)
+        self.limit = float(limit)
+
+    def forward(self, x):
+        return self.down_proj(swiglu_pair(self.gate_proj(x), self.up_proj(x), self.limit))
+
+
+def _weighted_slot_sum(down: torch.Tensor, scores: torch.Tensor) -> torch.Tensor:
+    """FP32 weighted sum over the slot axis in slot order, then BF16
+    (glm53_flash_mlx/fp8.py:457, packed.py:168-179)."""
+    total = torch.zeros(down.shape[1:], dtype=torch.float32, device=down.device)
+    for j in range(down.shape[0]):
+        total = total + down[j].float() * scores[j].float()
+    return total.to(down.dtype)
+
+
+class DirectFP8MoE(nn.Module):
+    """Bucketed top-k MoE over separate canonical expert tensors
+    (glm53_flash_mlx/fp8.py:343-400): selected top-8 decode for one row,
+    ascending-expert BF16 scatter-add for more rows, plus the shared expert."""
+
+    def __init__(self, config, gate, shared_experts, device=None):
+        super().__init__()
+        self.config = config
+        self.gate = gate
+        self.shared_experts = shared_experts
+        self.experts = nn.ModuleList(
+            [
+                DirectFP8Expert(config.hidden_size, config.moe_intermediate_size, config.swiglu_limit, device=device)
+                for _ in range(config.n_routed_experts)
+            ]
+        )
+
+    def forward(self, x):
+        indices, scores = self.gate(x)
+        # Routing is a phase boundary: one readback gives the host the expert
+        # buckets (glm53_flash_mlx/fp8.py:366-369).
+        routes = indices.reshape(-1, self.config.num_experts_per_tok).to(torch.int64).cpu()
+        flat_x = x.reshape(-1, x.shape[-1])
+        flat_scores = scores.reshape(-1, self.config.num_experts_per_tok)
+        limit = self.config.swiglu_limit
+        if flat_x.shape[0] == 1 and routes.shape == (1, DECODE_TOP_K):
+            selected = [self._expert(int(e)) for e in routes[0].tolist()]
+            gate = torch.stack([m.gate_proj(flat_x[0]) for m in selected])
+            up = torch.stack([m.up_proj(flat_x[0]) for m in selected])
+            hidden = swiglu_pair(gate, up, limit)
+            down = torch.stack([m.down_proj(hidden[j]) for j, m in enumerate(selected)])
+            result = _weighted_slot_sum(down, flat_scores[0])[None, :].reshape(x.shape)
+            if self.shared_experts is not None:
+                result = result + self.shared_experts(x)
+            return result
+        result = torch.zeros_like(flat_x)
+        for expert_id in torch.unique(routes).tolist():
+            rows_cpu, slots_cpu = torch.nonzero(routes == expert_id, as_tuple=True)
+            rows = rows_cpu.to(flat_x.device)
+            slots = slots_cpu.to(flat_x.device)
+            expert_out = self._expert(int(expert_id))(flat_x[rows])
+            route_weight = flat_scores[rows, slots][..., None]
+            weighted = (expert_out.float() * route_weight.float()).to(flat_x.dtype)
+            result.index_add_(0, rows, weighted)
+        result = result.reshape(x.shape)
+        if self.shared_experts is not None:
+            result = result + self.shared_experts(x)
+        return result
+
+    def _expert(self, expert_id: int):
+        return self.experts[expert_id]

@@ -1,0 +1,287 @@
+"""Packed FP8 expert bank and exact packed decode MoE on B200.
+
+Counterpart of glm53_flash_mlx/packed.py: ``PackedFP8ExpertBank``
+(packed.py:747-876), the per-expert views used by Direct-semantics prefill
+(packed.py:658-744) and ``PackedFP8MoE`` (packed.py:879-923).  The one-token
+decode runs the router's top-8 through two CUDA launches (fused gate/up/SwiGLU
+over the 8 selected experts plus the shared expert, then down + slot-ordered
+FP32 weighted reduce + BF16 shared add) with the reference's rounding points.
+"""
+
+from __future__ import annotations
+
+import math
+import os
+
+import torch
+from torch import nn
+
+from . import _native as N
+from .abi import PACKED_EXPERT_BANK_ABI  # noqa: F401
+from .fp8 import BLOCK_SIZE, DECODE_TOP_K, DirectFP8MoE, block_fp8_linear, swiglu_pair
+from .ownership import (
+    ResidentTensor,
+    TensorLayout,
+    TensorLease,
+    borrowed_stable_tensor,
+    owned_tensor,
+    require_resident,
+    resident_concatenate,
+    storage_descriptor,
+)
+
+_SYNC_STATUS = os.environ.get("GLM53_SYNC_STATUS", "0") == "1"
+
+
+class _PackedLinearView:
+    """One projection of one expert, addressed inside the bank (no copy)."""
+
+    def __init__(self, weight, scale_inv, *, expert_id: int, row_offset: int, scale_row_offset: int,
+                 out_features: int):
+        self._bank_weight = weight
+        self._bank_scale_inv = scale_inv
+        self.expert_id = int(expert_id)
+        self.row_offset = int(row_offset)
+        self.scale_row_offset = int(scale_row_offset)
+        self.out_features = int(out_features)
+
+    @property
+    def weight(self):
+        start = self.row_offset
+        return self._bank_weight[self.expert_id, start : start + self.out_features]
+
+    @property
+    def weight_scale_inv(self):
+        rows = math.ceil(self.out_features / BLOCK_SIZE)
+        start = self.scale_row_offset
+        return self._bank_scale_inv[self.expert_id, start : start + rows]
+
+    def __call__(self, x):
+        return block_fp8_linear(x, self.weight, self.weight_scale_inv)
+
+
+class _PackedExpertView:
+    def __init__(self, bank: "PackedFP8ExpertBank", expert_id: int, limit: float):
+        inter = bank.intermediate_size
+        scale_rows = bank.intermediate_scale_rows
+        self.gate_proj = _PackedLinearView(bank.gate_up_weight, bank.gate_up_scale_inv, expert_id=expert_id,
+                                           row_offset=0, scale_row_offset=0, out_features=inter)
+        self.up_proj = _PackedLinearView(bank.gate_up_weight, bank.gate_up_scale_inv, expert_id=expert_id,
+                                         row_offset=inter, scale_row_offset=scale_rows, out_features=inter)
+        self.down_proj = _PackedLinearView(bank.down_weight, bank.down_scale_inv, expert_id=expert_id,
+                                           row_offset=0, scale_row_offset=0,
+                                           out_features=bank.down_weight.shape[1])
+        self.limit = float(limit)
+
+    def __call__(self, x):
+        return self.down_proj(swiglu_pair(self.gate_proj(x), self.up_proj(x), self.limit))
+
+
+class PackedFP8ExpertBank(nn.Module):
+    """Four contiguous canonical-FP8 buffers for one routed MoE layer:
+    gate_up_weight [E,2I,H] (gate rows then up rows), gate_up_scale_inv
+    [E,2*ceil(I/128),ceil(H/128)], down_weight [E,H,I], down_scale_inv
+    [E,ceil(H/128),ceil(I/128)]."""
+
+    def __init__(self, gate_up_weight: TensorLease | ResidentTensor, gate_up_scale_inv: TensorLease | ResidentTensor,
+                 down_weight: TensorLease | ResidentTensor, down_scale_inv: TensorLease | ResidentTensor, *,
+                 intermediate_size: int):
+        super().__init__()
+        resident = {
+            "gate_up_weight": require_resident(gate_up_weight),
+            "gate_up_scale_inv": require_resident(gate_up_scale_inv),
+            "down_weight": require_resident(down_weight),
+            "down_scale_inv": require_resident(down_scale_inv),
+        }
+        for name, value in resident.items():
+            self.register_buffer(name, value.value, persistent=False)
+        self.storage_contracts = {name: storage_descriptor(value) for name, value in resident.items()}
+        self._storage_owners = tuple(value.owner for value in resident.values() if value.owner is not None)
+        self.intermediate_size = int(intermediate_size)
+        self.intermediate_scale_rows = math.ceil(intermediate_size / BLOCK_SIZE)
+        E, two_i, H = self.gate_up_weight.shape
+        if self.gate_up_weight.dtype != torch.uint8 or self.down_weight.dtype != torch.uint8:
+            raise ValueError("packed expert weights must remain uint8 E4M3")
+        if self.gate_up_scale_inv.dtype != torch.float32 or self.down_scale_inv.dtype != torch.float32:
+            raise ValueError("packed expert scales must remain float32")
+        if two_i != 2 * self.intermediate_size or tuple(self.down_weight.shape) != (E, H, self.intermediate_size):
+            raise ValueError("packed expert bank shapes are inconsistent")
+
+    @classmethod
+    def pack(cls, experts) -> "PackedFP8ExpertBank":
+        experts = list(experts)
+        if not experts:
+            raise ValueError("cannot pack an empty expert list")
+        hidden_size = experts[0].gate_proj.weight.shape[1]
+        intermediate_size = experts[0].gate_proj.weight.shape[0]
+        expert_count = len(experts)
+        scale_rows = math.ceil(intermediate_size / BLOCK_SIZE)
+        hidden_scale_rows = math.ceil(hidden_size / BLOCK_SIZE)
+        for expert in experts:
+            expected = (
+                (tuple(expert.gate_proj.weight.shape), (intermediate_size, hidden_size)),
+                (tuple(expert.up_proj.weight.shape), (intermediate_size, hidden_size)),
+                (tuple(expert.down_proj.weight.shape), (hidden_size, intermediate_size)),
+            )
+            if any(actual != wanted for actual, wanted in expected):
+                raise ValueError("expert projection shapes are not uniform")
+            for projection in (expert.gate_proj, expert.up_proj, expert.down_proj):
+                if projection.weight.dtype != torch.uint8:
+                    raise ValueError("packed expert weights must remain uint8 E4M3")
+                if projection.weight_scale_inv.dtype != torch.float32:
+                    raise ValueError("packed expert scales must remain float32")
+
+        def stable(projection, name: str):
+            return borrowed_stable_tensor(getattr(projection, name), owner=projection,
+                                          layout=TensorLayout.ROW_MAJOR_CONTIGUOUS)
+
+        gate_up_weight = resident_concatenate(
+            [stable(p, "weight") for e in experts for p in (e.gate_proj, e.up_proj)], axis=0
+        ).value.reshape(expert_count, 2 * intermediate_size, hidden_size)
+        gate_up_scale_inv = resident_concatenate(
+            [stable(p, "weight_scale_inv") for e in experts for p in (e.gate_proj, e.up_proj)], axis=0
+        ).value.reshape(expert_count, 2 * scale_rows, hidden_scale_rows)
+        down_weight = resident_concatenate([stable(e.down_proj, "weight") for e in experts], axis=0
+                                           ).value.reshape(expert_count, hidden_size, intermediate_size)
+        down_scale_inv = resident_concatenate([stable(e.down_proj, "weight_scale_inv") for e in experts], axis=0
+                                              ).value.reshape(expert_count, hidden_scale_rows, scale_rows)
+        layout = TensorLayout.ROW_MAJOR_CONTIGUOUS
+        return cls(
+            owned_tensor(gate_up_weight, layout=layout),
+            owned_tensor(gate_up_scale_inv, layout=layout),
+            owned_tensor(down_weight, layout=layout),
+            owned_tensor(down_scale_inv, layout=layout),
+            intermediate_size=intermediate_size,
+        )
+
+    @property
+    def expert_count(self) -> int:
+        return self.gate_up_weight.shape[0]
+
+    @property
+    def hidden_size(self) -> int:
+        return self.gate_up_weight.shape[2]
+
+    @property
+    def nbytes(self) -> int:
+        return sum(
+            t.numel() * t.element_size()
+            for t in (self.gate_up_weight, self.gate_up_scale_inv, self.down_weight, self.down_scale_inv)
+        )
+
+    def expert(self, expert_id: int, *, limit: float) -> _PackedExpertView:
+        if not 0 <= expert_id < self.expert_count:
+            raise IndexError(expert_id)
+        return _PackedExpertView(self, expert_id, limit)
+
+
+def shared_fp8_tensors(shared) -> tuple | None:
+    """(gate_w, gate_s, up_w, up_s, down_w, down_s) of a shared expert made of
+    BlockFP8Linear projections, or None when it is some other module."""
+    if shared is None:
+        return None
+    try:
+        parts = []
+        for name in ("gate_proj", "up_proj", "down_proj"):
+            proj = getattr(shared, name)
+            if getattr(proj, "bias", None) is not None:
+                return None
+            if proj.weight.dtype != torch.uint8 or proj.weight_scale_inv.dtype != torch.float32:
+                return None
+            parts += [proj.weight.contiguous(), proj.weight_scale_inv.contiguous()]
+        return tuple(parts)
+    except AttributeError:
+        return None
+
+
+def packed_decode_moe(x: torch.Tensor, expert_ids: torch.Tensor, scores: torch.Tensor, bank: PackedFP8ExpertBank,
+                      shared: tuple | None, *, limit: float, workspace: N.Workspace | None = None,
+                      status: torch.Tensor | None = None) -> torch.Tensor:
+    """One-token routed MoE (+ shared expert) over the packed bank.
+
+    x: BF16 [H]; expert_ids: int32/uint32 [top_k]; scores: float32 [top_k].
+    Returns BF16 [H]."""
+    dev = N.require_cuda(x, expert_ids, scores, bank.gate_up_weight)
+    H = bank.hidden_size
+    I = bank.intermediate_size
+    top_k = expert_ids.numel()
+    if x.numel() != H:
+        raise ValueError(f"decode input width {x.numel()} != bank hidden {H}")
+    x = x.reshape(H).contiguous()
+    ids = expert_ids.reshape(-1).to(torch.int32).contiguous()
+    sc = scores.reshape(-1).to(torch.float32).contiguous()
+    if shared is not None:
+        sg_w, sg_s, su_w, su_s, sd_w, sd_s = shared
+        Is = sg_w.shape[0]
+    else:
+        sg_w = sg_s = su_w = su_s = sd_w = sd_s = None
+        Is = 0
+    ws_bytes = N.lib().glm53_packed_decode_workspace_bytes(top_k, I, Is)
+    wsp = workspace or N.Workspace()
+    ws = wsp.get(dev, "decode", ws_bytes)
+    if status is None:
+        status = wsp.get(dev, "status", 4)
+    out = torch.empty(H, dtype=torch.bfloat16, device=dev)
+    N.check(
+        N.lib().glm53_packed_decode_moe(
+            x.data_ptr(), H, ids.data_ptr(), sc.data_ptr(), top_k,
+            bank.gate_up_weight.data_ptr(), bank.gate_up_scale_inv.data_ptr(),
+            bank.down_weight.data_ptr(), bank.down_scale_inv.data_ptr(), bank.expert_count, I,
+            N.ptr(sg_w), N.ptr(sg_s), N.ptr(su_w), N.ptr(su_s), N.ptr(sd_w), N.ptr(sd_s), Is,
+            float(limit), out.data_ptr(), ws.data_ptr(), ws.numel(), status.data_ptr(), N.stream(dev),
+        ),
+        "glm53_packed_decode_moe",
+    )
+    if _SYNC_STATUS:
+        check_status(status)
+    return out
+
+
+def check_status(status: torch.Tensor) -> None:
+    """Raise for device-side fail-closed signals (one device->host read)."""
+    word = int(status.view(torch.int32)[0].item()) & 0xFFFFFFFF
+    if word & N.STATUS_BAD_EXPERT:
+        raise IndexError("expert id out of range in routed MoE")
+    if word & N.STATUS_WAIT_TIMEOUT:
+        raise RuntimeError("a bounded device wait gave up")
+    if word:
+        raise RuntimeError(f"device status 0x{word:x}")
+
+
+class PackedFP8MoE(DirectFP8MoE):
+    """Exact fused batch-1 decode and Direct semantics over a packed bank."""
+
+    def __init__(self, bank, config, gate, shared_experts):
+        nn.Module.__init__(self)
+        self.bank = bank
+        self.config = config
+        self.gate = gate
+        self.shared_experts = shared_experts
+        self._expert_views = tuple(
+            bank.expert(expert_id, limit=config.swiglu_limit) for expert_id in range(bank.expert_count)
+        )
+        self._workspace = N.Workspace()
+
+    def _expert(self, expert_id: int):
+        return self._expert_views[expert_id]
+
+    @property
+    def status(self) -> torch.Tensor:
+        return self._workspace.get(self.bank.gate_up_weight.device, "status", 4)
+
+    def forward(self, x):
+        flat_x = x.reshape(-1, x.shape[-1])
+        if flat_x.shape[0] != 1:
+            return super().forward(x)
+        indices, scores = self.gate(x)
+        if indices.shape[-1] != DECODE_TOP_K:
+            return super().forward(x)
+        limit = self.config.swiglu_limit
+        if float(limit) != int(limit):
+            raise ValueError("exact fused packed decode requires an integral clamp limit")
+        shared = shared_fp8_tensors(self.shared_experts)
+        result = packed_decode_moe(flat_x[0], indices.reshape(-1), scores.reshape(-1), self.bank, shared,
+                                   limit=limit, workspace=self._workspace).reshape(x.shape)
+        if shared is None and self.shared_experts is not None:
+            result = result + self.shared_experts(x)
+        return result

@@ -1,0 +1,193 @@
+/*
+ * glm53_b200.h -- C ABI of the B200 (sm_100a) FP8 block-scaled MoE hot path.
+ *
+ * Conventions
+ *   - Every entry point is `extern "C"`, takes plain device pointers, sizes
+ *     and a `cudaStream_t` passed as `void*` (NULL = legacy default stream),
+ *     and returns an int status: GLM53_OK or one of the GLM53_ERR_* codes.
+ *     glm53_last_error() returns a thread-local message for the last failure.
+ *   - BF16 tensors are passed as `void*` (16-bit storage), E4M3 weights as
+ *     `uint8_t*` codes, block scales (`weight_scale_inv`) as `float*` on the
+ *     128x128 grid, expert ids as `uint32_t*`, route weights as `float*`.
+ *   - All tensors are row-major contiguous.  No entry point allocates device
+ *     memory: callers pass workspace sized by the *_workspace_bytes queries.
+ *   - Status mapping used by the Python layer: GLM53_ERR_INVALID -> ValueError,
+ *     GLM53_ERR_INDEX -> IndexError, GLM53_ERR_CUDA -> RuntimeError.
+ *   - Device-side fail-closed signals (expert id >= expert count, a bounded
+ *     wait that gave up) are OR-ed into an optional `uint32_t* status` word in
+ *     device memory instead of trapping (bits GLM53_STATUS_*).
+ *
+ * Reference citations are paths inside kiojuvr/glm53-flash-mlx.
+ */
+#ifndef GLM53_B200_H_
+#define GLM53_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GLM53_OK 0
+#define GLM53_ERR_INVALID 1
+#define GLM53_ERR_CUDA 2
+#define GLM53_ERR_INDEX 3
+
+#define GLM53_STATUS_BAD_EXPERT 1u
+#define GLM53_STATUS_WAIT_TIMEOUT 2u
+#define GLM53_STATUS_BAD_GEOMETRY 4u
+
+/* Kernel ABI identity string (replaces glm53_flash_mlx/abi.py:3-15 for the
+ * CUDA kernels; part of any cache identity that depends on kernel numerics). */
+const char* glm53_kernel_abi(void);
+
+/* Message describing the last non-OK status returned on this thread. */
+const char* glm53_last_error(void);
+
+/* y[M,N] (BF16) = x[M,K] (BF16) @ dequant(w[N,K] E4M3, scale_inv[ceil(N/128),
+ * ceil(K/128)])^T with FP32 accumulation.
+ * Replaces block_fp8_linear, glm53_flash_mlx/fp8.py:254-299 (kernels K1/K2,
+ * fp8.py:41-116). */
+int glm53_fp8_linear(const void* x, int64_t M, int64_t K, const uint8_t* w,
+                     int64_t N, const float* scale_inv, void* y, void* stream);
+
+/* Workspace bytes needed by glm53_router_topk for T tokens and E experts. */
+size_t glm53_router_workspace_bytes(int64_t T, int64_t E);
+
+/* FP32 router: logits = f32(x[T,H]) @ w[E,H]^T; s = sigmoid(logits);
+ * choice = s + bias; optional group mask (n_group/topk_group); top_k of
+ * choice (slot order: descending choice, ties to the lower expert id);
+ * scores = s[idx], normalised over the top_k when norm_topk_prob, times
+ * routed_scaling_factor.  logits may be NULL.
+ * Replaces Float32Gate.__call__, glm53_flash_mlx/patch.py:131-142, and the
+ * mlx-vlm group_expert_select it calls. */
+int glm53_router_topk(const void* x, int64_t T, int64_t H, const float* w,
+                      int64_t E, const float* bias, int top_k, int n_group,
+                      int topk_group, int norm_topk_prob,
+                      float routed_scaling_factor, uint32_t* indices,
+                      float* scores, float* logits, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/* Workspace bytes needed by glm53_packed_decode_moe. */
+size_t glm53_packed_decode_workspace_bytes(int top_k, int64_t I, int64_t I_shared);
+
+/* One-token packed decode MoE over a packed expert bank:
+ *   bank: gate_up_w [E,2I,H] (gate rows [0,I), up rows [I,2I)),
+ *         gate_up_s [E, 2*ceil(I/128), ceil(H/128)],
+ *         down_w [E,H,I], down_s [E, ceil(H/128), ceil(I/128)];
+ *   shared expert (all six pointers NULL and I_shared 0 when absent):
+ *         gate/up [I_shared,H] + scales, down [H,I_shared] + scale.
+ * out[H] = BF16(sum_j f32(down_j) * scores[j]) (+ shared, BF16 add), with the
+ * exact BF16 SwiGLU rounding of the reference.
+ * Replaces PackedFP8MoE.__call__ decode, glm53_flash_mlx/packed.py:896-923
+ * (kernels K7/K6/K8/K9 at packed.py:66-235 and the shared down K1). */
+int glm53_packed_decode_moe(const void* x, int64_t H, const uint32_t* expert_ids,
+                            const float* scores, int top_k,
+                            const uint8_t* gate_up_w, const float* gate_up_s,
+                            const uint8_t* down_w, const float* down_s,
+                            int64_t E, int64_t I, const uint8_t* shared_gate_w,
+                            const float* shared_gate_s, const uint8_t* shared_up_w,
+                            const float* shared_up_s, const uint8_t* shared_down_w,
+                            const float* shared_down_s, int64_t I_shared,
+                            float limit, void* out, void* workspace,
+                            size_t workspace_bytes, uint32_t* status, void* stream);
+
+/* Diagnostic: only the first stage of glm53_packed_decode_moe (fused
+ * gate/up/SwiGLU of the selected experts and the shared expert); the BF16
+ * hidden rows [top_k*I + I_shared] are left at the start of `workspace`.
+ * Same arguments as glm53_packed_decode_moe minus `out`.  Counterpart of the
+ * reference's stage-dumping diagnostic kernel
+ * native_execution/native_indexer_plan.metal:231-321. */
+int glm53_packed_decode_gate_up(const void* x, int64_t H, const uint32_t* expert_ids,
+                                int top_k, const uint8_t* gate_up_w,
+                                const float* gate_up_s, int64_t E, int64_t I,
+                                const uint8_t* shared_gate_w, const float* shared_gate_s,
+                                const uint8_t* shared_up_w, const float* shared_up_s,
+                                int64_t I_shared, float limit, void* workspace,
+                                size_t workspace_bytes, uint32_t* status, void* stream);
+
+/* Stable expert-sorted route plan and tile descriptors on the device.
+ *   order[p] = route index at sorted position p; inverse[r] = its position;
+ *   sorted_experts / sorted_scores (scores may be NULL) follow the order;
+ *   route_offsets[E+1]; tile_offsets[E+1];
+ *   descriptors (capacity ceil(R/tile_rows)+E): (expert, start, length),
+ *   sentinel (0, R, 0) for unused slots; descriptor_count[0] = valid count;
+ *   invalid_count[0] = routes whose id >= E (placed after all valid routes).
+ * Replaces build_route_plan / build_grouped_tile_plan,
+ * glm53_flash_mlx/grouped_fp8.py:157-203, and the native route plan
+ * native_execution/native_prefill_moe_route_plan.h:16-82. */
+int glm53_route_plan(const uint32_t* expert_ids, int64_t R, int64_t E,
+                     int64_t tile_rows, const float* scores, uint32_t* order,
+                     uint32_t* inverse, uint32_t* sorted_experts,
+                     float* sorted_scores, uint32_t* route_offsets,
+                     uint32_t* tile_experts, uint32_t* tile_starts,
+                     uint32_t* tile_lengths, uint32_t* tile_offsets,
+                     uint32_t* descriptor_count, uint32_t* invalid_count,
+                     void* stream);
+
+/* sorted_x[p,:] = x[order[p] / top_k, :] (the gathered rows of build_route_plan,
+ * glm53_flash_mlx/grouped_fp8.py:164-166). */
+int glm53_gather_rows(const void* x, int64_t H, const uint32_t* order,
+                      int64_t R, int top_k, void* sorted_x, void* stream);
+
+/* Grouped projection of sorted route rows: for every descriptor d,
+ * out[start+i, :] = x[start+i, :] @ dequant(w[expert])^T (i < length).
+ * x [R,K] BF16, w [E,N,K] E4M3, scale_inv [E, ceil(N/128), ceil(K/128)],
+ * out [R,N] BF16; tile lengths must be <= 128.
+ * Replaces grouped_fp8_linear, glm53_flash_mlx/grouped_fp8.py:206-262
+ * (kernel K12, grouped_fp8.py:30-154). */
+int glm53_grouped_fp8_linear(const void* x, int64_t R, int64_t K,
+                             const uint32_t* tile_experts,
+                             const uint32_t* tile_starts,
+                             const uint32_t* tile_lengths,
+                             int64_t descriptor_capacity, const uint8_t* w,
+                             int64_t E, int64_t N, const float* scale_inv,
+                             void* out, void* stream);
+
+/* hidden[R,I] = silu(min(gate, L)) * clip(up, -L, L) with BF16 per-op
+ * rounding, gate_up [R,2I].
+ * Replaces activate_gate_up, glm53_flash_mlx/grouped_fp8.py:265-270. */
+int glm53_activate_gate_up(const void* gate_up, int64_t R, int64_t I,
+                           float limit, void* hidden, void* stream);
+
+/* out[T,H] = BF16(sum_j f32(sorted_out[inverse[t*k+j]]) *
+ * sorted_scores[inverse[t*k+j]]), then + shared[T,H] (BF16 add) if shared is
+ * not NULL.
+ * Replaces restore_and_reduce, glm53_flash_mlx/grouped_fp8.py:273-276, and the
+ * `result + shared` of grouped_fp8.py:319-320. */
+int glm53_restore_and_reduce(const void* sorted_out, const float* sorted_scores,
+                             const uint32_t* inverse, int64_t T, int top_k,
+                             int64_t H, const void* shared, void* out,
+                             void* stream);
+
+/* Workspace bytes needed by glm53_grouped_moe. */
+size_t glm53_grouped_moe_workspace_bytes(int64_t T, int top_k, int64_t E,
+                                         int64_t H, int64_t I, int64_t I_shared);
+
+/* Whole grouped prefill MoE layer given routes: route plan, grouped gate/up
+ * with fused SwiGLU, grouped down, slot-ordered FP32 combine, shared expert
+ * and BF16 add.  Bank and shared layouts as in glm53_packed_decode_moe.
+ * Replaces SortedGroupedFP8MoE.grouped_from_routes,
+ * glm53_flash_mlx/grouped_fp8.py:294-321. */
+int glm53_grouped_moe(const void* x, int64_t T, int64_t H,
+                      const uint32_t* indices, const float* scores, int top_k,
+                      const uint8_t* gate_up_w, const float* gate_up_s,
+                      const uint8_t* down_w, const float* down_s, int64_t E,
+                      int64_t I, const uint8_t* shared_gate_w,
+                      const float* shared_gate_s, const uint8_t* shared_up_w,
+                      const float* shared_up_s, const uint8_t* shared_down_w,
+                      const float* shared_down_s, int64_t I_shared, float limit,
+                      void* out, void* workspace, size_t workspace_bytes,
+                      uint32_t* status, void* stream);
+
+/* Diagnostic: the BF16 sigmoid stage of the SwiGLU epilogue over n BF16
+ * gate values (the reference's formula sweep,
+ * native_execution/native_indexer_plan.metal:323-366). */
+int glm53_sigmoid_bf16(const void* gate, int64_t n, void* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GLM53_B200_H_ */

@@ -1,0 +1,412 @@
+"""numpy/ctypes front end of the C oracle -- TEST INFRASTRUCTURE ONLY.
+
+BF16 tensors are numpy ``uint16`` bit patterns, E4M3 weights ``uint8`` codes,
+scales ``float32``.  Each function names the reference flow it restates; the
+scalar arithmetic is in ``oracle.c``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+import threading
+from pathlib import Path
+
+import numpy as np
+
+__all__ = [
+    "oracle_lib",
+    "e4m3_table",
+    "bf16_from_f32",
+    "f32_from_bf16",
+    "sigmoid_bf16",
+    "swiglu_bf16",
+    "block_fp8_linear",
+    "packed_decode_moe",
+    "router",
+    "scores_for_indices",
+    "route_plan",
+    "tile_plan",
+    "grouped_linear",
+    "activate_gate_up",
+    "restore_and_reduce",
+    "bf16_add",
+    "shared_expert",
+    "direct_moe",
+    "grouped_moe",
+    "default_threads",
+]
+
+_HERE = Path(__file__).resolve().parent
+_LIB_PATH = _HERE / "_build" / "liboracle.so"
+_lock = threading.Lock()
+_lib = None
+
+_u8 = ctypes.POINTER(ctypes.c_uint8)
+_u16 = ctypes.POINTER(ctypes.c_uint16)
+_u32 = ctypes.POINTER(ctypes.c_uint32)
+_f32 = ctypes.POINTER(ctypes.c_float)
+_f64 = ctypes.POINTER(ctypes.c_double)
+_i64 = ctypes.c_int64
+
+
+def default_threads() -> int:
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except AttributeError:  # pragma: no cover
+        return max(1, os.cpu_count() or 1)
+
+
+def build_oracle() -> Path:
+    subprocess.run(["make", "-s", "-C", str(_HERE)], check=True)
+    return _LIB_PATH
+
+
+def oracle_lib():
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not _LIB_PATH.exists():
+                build_oracle()
+            lib = ctypes.CDLL(str(_LIB_PATH))
+            sig = {
+                "orc_e4m3_table": (None, [_f32]),
+                "orc_sigmoid_bf16_vec": (None, [_u16, _i64, _u16]),
+                "orc_swiglu_bf16_vec": (None, [_u16, _u16, _i64, ctypes.c_float, _u16]),
+                "orc_block_fp8_linear": (ctypes.c_int, [_u16, _i64, _i64, _u8, _i64, _f32, _u16, ctypes.c_int]),
+                "orc_packed_decode_moe": (
+                    ctypes.c_int,
+                    [_u16, _i64, _u32, _f32, ctypes.c_int, _u8, _f32, _u8, _f32, _i64, _i64,
+                     _u8, _f32, _u8, _f32, _u8, _f32, _i64, ctypes.c_float, _u16, _u16, ctypes.c_int],
+                ),
+                "orc_router": (
+                    ctypes.c_int,
+                    [_u16, _i64, _i64, _f32, _i64, _f32, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                     ctypes.c_int, ctypes.c_float, _u32, _f32, _f64, _f32, _f32, ctypes.c_int],
+                ),
+                "orc_route_plan": (ctypes.c_int, [_u32, _i64, _i64, _f32, _u32, _u32, _u32, _f32, _u32, _u32]),
+                "orc_tile_plan": (ctypes.c_int, [_u32, _i64, _i64, _i64, _u32, _u32, _u32, _u32, _u32, _u32]),
+                "orc_grouped_linear": (ctypes.c_int, [_u16, _i64, _i64, _u32, _u8, _i64, _i64, _f32, _u16, ctypes.c_int]),
+                "orc_activate_gate_up": (None, [_u16, _i64, _i64, ctypes.c_float, _u16]),
+                "orc_restore_and_reduce": (None, [_u16, _f32, _u32, _i64, ctypes.c_int, _i64, _u16]),
+                "orc_bf16_add": (None, [_u16, _u16, _i64, _u16]),
+            }
+            for name, (res, args) in sig.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+def _p(a: np.ndarray | None, ptype):
+    if a is None:
+        return ctypes.cast(None, ptype)
+    assert a.flags["C_CONTIGUOUS"], "oracle inputs must be C-contiguous"
+    return a.ctypes.data_as(ptype)
+
+
+def _c(a, dtype) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=dtype))
+
+
+# ----------------------------------------------------------------------------
+# scalar helpers
+# ----------------------------------------------------------------------------
+
+
+def e4m3_table() -> np.ndarray:
+    out = np.empty(256, dtype=np.float32)
+    oracle_lib().orc_e4m3_table(_p(out, _f32))
+    return out
+
+
+def bf16_from_f32(a) -> np.ndarray:
+    """Round-to-nearest-even FP32 -> BF16 bit patterns."""
+    a = np.ascontiguousarray(np.asarray(a, dtype=np.float32))
+    b = a.view(np.uint32).astype(np.uint64)
+    out = ((b + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint16)
+    nan = np.isnan(a)
+    if nan.any():
+        out[nan] = ((a.view(np.uint32)[nan] >> 16) | 0x40).astype(np.uint16)
+    return out
+
+
+def f32_from_bf16(b) -> np.ndarray:
+    return (np.asarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def sigmoid_bf16(g_bits) -> np.ndarray:
+    g = _c(g_bits, np.uint16).reshape(-1)
+    out = np.empty_like(g)
+    oracle_lib().orc_sigmoid_bf16_vec(_p(g, _u16), g.size, _p(out, _u16))
+    return out
+
+
+def swiglu_bf16(gate_bits, up_bits, limit: float) -> np.ndarray:
+    g = _c(gate_bits, np.uint16)
+    u = _c(up_bits, np.uint16)
+    assert g.shape == u.shape
+    out = np.empty_like(g)
+    oracle_lib().orc_swiglu_bf16_vec(_p(g, _u16), _p(u, _u16), g.size, float(limit), _p(out, _u16))
+    return out
+
+
+def bf16_add(a, b) -> np.ndarray:
+    a = _c(a, np.uint16)
+    b = _c(b, np.uint16)
+    out = np.empty_like(a)
+    oracle_lib().orc_bf16_add(_p(a, _u16), _p(b, _u16), a.size, _p(out, _u16))
+    return out
+
+
+# ----------------------------------------------------------------------------
+# K1/K2 block linear, packed decode
+# ----------------------------------------------------------------------------
+
+
+def block_fp8_linear(x_bits, weight, scale_inv, *, threads: int | None = None) -> np.ndarray:
+    """glm53_flash_mlx/fp8.py:254-299 over [..., K] BF16 inputs."""
+    x = _c(x_bits, np.uint16)
+    w = _c(weight, np.uint8)
+    s = _c(scale_inv, np.float32)
+    n, k = w.shape
+    flat = x.reshape(-1, k)
+    out = np.empty((flat.shape[0], n), dtype=np.uint16)
+    if flat.shape[0]:
+        rc = oracle_lib().orc_block_fp8_linear(
+            _p(flat, _u16), flat.shape[0], k, _p(w, _u8), n, _p(s, _f32), _p(out, _u16),
+            threads or default_threads(),
+        )
+        assert rc == 0
+    return out.reshape(*x.shape[:-1], n)
+
+
+def packed_decode_moe(x_bits, ids, scores, bank, shared, limit: float, *,
+                      threads: int | None = None, return_hidden: bool = False):
+    """PackedFP8MoE.__call__ for one token (glm53_flash_mlx/packed.py:896-923).
+
+    ``bank`` = (gate_up_w [E,2I,H], gate_up_s, down_w [E,H,I], down_s);
+    ``shared`` = None or (gate_w, gate_s, up_w, up_s, down_w, down_s)."""
+    x = _c(x_bits, np.uint16).reshape(-1)
+    ids = _c(ids, np.uint32).reshape(-1)
+    scores = _c(scores, np.float32).reshape(-1)
+    gu_w, gu_s, d_w, d_s = (_c(bank[0], np.uint8), _c(bank[1], np.float32),
+                            _c(bank[2], np.uint8), _c(bank[3], np.float32))
+    E, two_i, H = gu_w.shape
+    I = two_i // 2
+    top_k = ids.size
+    if shared is not None:
+        sg_w, sg_s, su_w, su_s, sd_w, sd_s = (
+            _c(shared[0], np.uint8), _c(shared[1], np.float32), _c(shared[2], np.uint8),
+            _c(shared[3], np.float32), _c(shared[4], np.uint8), _c(shared[5], np.float32))
+        Is = sg_w.shape[0]
+    else:
+        sg_w = sg_s = su_w = su_s = sd_w = sd_s = None
+        Is = 0
+    out = np.empty(H, dtype=np.uint16)
+    hidden = np.empty(top_k * I + Is, dtype=np.uint16)
+    rc = oracle_lib().orc_packed_decode_moe(
+        _p(x, _u16), H, _p(ids, _u32), _p(scores, _f32), top_k,
+        _p(gu_w, _u8), _p(gu_s, _f32), _p(d_w, _u8), _p(d_s, _f32), E, I,
+        _p(sg_w, _u8), _p(sg_s, _f32), _p(su_w, _u8), _p(su_s, _f32), _p(sd_w, _u8), _p(sd_s, _f32), Is,
+        float(limit), _p(out, _u16), _p(hidden, _u16), threads or default_threads(),
+    )
+    if rc == 3:
+        raise IndexError("expert id out of range")
+    assert rc == 0
+    return (out, hidden) if return_hidden else out
+
+
+# ----------------------------------------------------------------------------
+# Router
+# ----------------------------------------------------------------------------
+
+
+def router(x_bits, weight, bias, *, top_k: int = 8, n_group: int = 1, topk_group: int = 1,
+           norm_topk_prob: bool = True, routed_scaling_factor: float = 1.0,
+           threads: int | None = None):
+    """Float32Gate + group_expert_select (glm53_flash_mlx/patch.py:131-142).
+
+    Returns (indices u32 [T,k], scores f32 [T,k], logits f64 [T,E],
+    margin f32 [T]) where margin = choice[k-th] - choice[(k+1)-th best]."""
+    x = _c(x_bits, np.uint16)
+    w = _c(weight, np.float32)
+    b = _c(bias, np.float32)
+    E, H = w.shape
+    flat = x.reshape(-1, H)
+    T = flat.shape[0]
+    idx = np.empty((T, top_k), dtype=np.uint32)
+    sc = np.empty((T, top_k), dtype=np.float32)
+    l64 = np.empty((T, E), dtype=np.float64)
+    margin = np.empty(T, dtype=np.float32)
+    rc = oracle_lib().orc_router(
+        _p(flat, _u16), T, H, _p(w, _f32), E, _p(b, _f32), int(top_k), int(n_group),
+        int(topk_group), int(bool(norm_topk_prob)), float(routed_scaling_factor),
+        _p(idx, _u32), _p(sc, _f32), _p(l64, _f64), None, _p(margin, _f32),
+        threads or default_threads(),
+    )
+    if rc != 0:
+        raise ValueError("invalid router geometry")
+    return idx, sc, l64, margin
+
+
+def scores_for_indices(logits, indices, *, norm_topk_prob: bool = True, routed_scaling_factor: float = 1.0):
+    """Route weights for given expert ids: sigmoid(logits) taken at the ids,
+    normalised over the slots, times the scaling factor (the indices-only gate
+    of scripts/localize_grouped_fp8_divergence.py, restated)."""
+    lg = np.asarray(logits, dtype=np.float64)
+    idx = np.asarray(indices, dtype=np.int64)
+    sc = np.take_along_axis(1.0 / (1.0 + np.exp(-lg)), idx, axis=-1)
+    if idx.shape[-1] > 1 and norm_topk_prob:
+        sc = sc / sc.sum(axis=-1, keepdims=True)
+    return (sc * routed_scaling_factor).astype(np.float32)
+
+
+# ----------------------------------------------------------------------------
+# Route plan / tile plan / grouped linear
+# ----------------------------------------------------------------------------
+
+
+def route_plan(ids, expert_count: int, scores=None):
+    """Stable expert sort (glm53_flash_mlx/grouped_fp8.py:157-170)."""
+    ids = _c(ids, np.uint32).reshape(-1)
+    R = ids.size
+    sc = None if scores is None else _c(scores, np.float32).reshape(-1)
+    order = np.empty(R, np.uint32)
+    inverse = np.empty(R, np.uint32)
+    sorted_experts = np.empty(R, np.uint32)
+    sorted_scores = np.empty(R, np.float32)
+    offsets = np.empty(expert_count + 1, np.uint32)
+    invalid = np.zeros(1, np.uint32)
+    oracle_lib().orc_route_plan(
+        _p(ids, _u32), R, expert_count, _p(sc, _f32), _p(order, _u32), _p(inverse, _u32),
+        _p(sorted_experts, _u32), _p(sorted_scores, _f32), _p(offsets, _u32), _p(invalid, _u32),
+    )
+    return {
+        "order": order,
+        "inverse": inverse,
+        "sorted_experts": sorted_experts,
+        "sorted_scores": sorted_scores if sc is not None else None,
+        "expert_offsets": offsets,
+        "invalid": int(invalid[0]),
+    }
+
+
+def tile_plan(sorted_experts, expert_count: int, tile_rows: int = 32):
+    """build_grouped_tile_plan (glm53_flash_mlx/grouped_fp8.py:173-203):
+    (tile_experts, tile_starts, tile_lengths, route_offsets, tile_offsets)."""
+    se = _c(sorted_experts, np.uint32).reshape(-1)
+    R = se.size
+    cap = (R + tile_rows - 1) // tile_rows + expert_count
+    te = np.empty(cap, np.uint32)
+    ts = np.empty(cap, np.uint32)
+    tl = np.empty(cap, np.uint32)
+    ro = np.empty(expert_count + 1, np.uint32)
+    to = np.empty(expert_count + 1, np.uint32)
+    cnt = np.zeros(1, np.uint32)
+    oracle_lib().orc_tile_plan(
+        _p(se, _u32), R, expert_count, tile_rows, _p(te, _u32), _p(ts, _u32), _p(tl, _u32),
+        _p(ro, _u32), _p(to, _u32), _p(cnt, _u32),
+    )
+    return te, ts, tl, ro, to
+
+
+def grouped_linear(x_sorted_bits, sorted_experts, weight, scale_inv, *,
+                   threads: int | None = None) -> np.ndarray:
+    """K12 semantics (glm53_flash_mlx/grouped_fp8.py:30-154, 206-262)."""
+    x = _c(x_sorted_bits, np.uint16)
+    se = _c(sorted_experts, np.uint32).reshape(-1)
+    w = _c(weight, np.uint8)
+    s = _c(scale_inv, np.float32)
+    E, N, K = w.shape
+    R = x.shape[0]
+    out = np.zeros((R, N), dtype=np.uint16)
+    oracle_lib().orc_grouped_linear(
+        _p(x, _u16), R, K, _p(se, _u32), _p(w, _u8), E, N, _p(s, _f32), _p(out, _u16),
+        threads or default_threads(),
+    )
+    return out
+
+
+def activate_gate_up(gate_up_bits, intermediate_size: int, limit: float) -> np.ndarray:
+    g = _c(gate_up_bits, np.uint16)
+    R = g.shape[0]
+    out = np.empty((R, intermediate_size), dtype=np.uint16)
+    oracle_lib().orc_activate_gate_up(_p(g, _u16), R, intermediate_size, float(limit), _p(out, _u16))
+    return out
+
+
+def restore_and_reduce(sorted_out_bits, sorted_scores, inverse, tokens: int, top_k: int) -> np.ndarray:
+    so = _c(sorted_out_bits, np.uint16)
+    ss = _c(sorted_scores, np.float32)
+    inv = _c(inverse, np.uint32)
+    H = so.shape[1]
+    out = np.empty((tokens, H), dtype=np.uint16)
+    oracle_lib().orc_restore_and_reduce(_p(so, _u16), _p(ss, _f32), _p(inv, _u32), tokens, top_k, H, _p(out, _u16))
+    return out
+
+
+# ----------------------------------------------------------------------------
+# Module-level flows
+# ----------------------------------------------------------------------------
+
+
+def shared_expert(x_bits, shared, limit: float, *, threads: int | None = None) -> np.ndarray:
+    """ClampedMLP / DirectFP8Expert over BlockFP8Linear projections
+    (glm53_flash_mlx/fp8.py:329-340): down(silu(min(gate, L)) * clip(up))."""
+    gate = block_fp8_linear(x_bits, shared[0], shared[1], threads=threads)
+    up = block_fp8_linear(x_bits, shared[2], shared[3], threads=threads)
+    hidden = swiglu_bf16(gate, up, limit)
+    return block_fp8_linear(hidden, shared[4], shared[5], threads=threads)
+
+
+def _bank_expert(bank, e: int):
+    gu_w, gu_s, d_w, d_s = bank
+    I = gu_w.shape[1] // 2
+    half = gu_s.shape[1] // 2
+    return (gu_w[e, :I], gu_s[e, :half], gu_w[e, I:], gu_s[e, half:], d_w[e], d_s[e])
+
+
+def direct_moe(x_bits, indices, scores, bank, shared, limit: float, *,
+               threads: int | None = None) -> np.ndarray:
+    """DirectFP8MoE prefill semantics (glm53_flash_mlx/fp8.py:384-397):
+    ascending expert id, BF16 scatter-add of expert_out * score, + shared."""
+    x = _c(x_bits, np.uint16)
+    H = x.shape[-1]
+    flat = x.reshape(-1, H)
+    routes = _c(indices, np.int64).reshape(flat.shape[0], -1)
+    sc = _c(scores, np.float32).reshape(flat.shape[0], -1)
+    result = np.zeros(flat.shape, dtype=np.uint16)
+    for e in np.unique(routes):
+        rows, slots = np.nonzero(routes == e)
+        expert = _bank_expert(bank, int(e))
+        out = shared_expert(flat[rows], expert, limit, threads=threads)
+        weighted = f32_from_bf16(out) * sc[rows, slots][:, None]
+        upd = bf16_from_f32(weighted)
+        result[rows] = bf16_add(result[rows], upd)
+    if shared is not None:
+        result = bf16_add(result, shared_expert(flat, shared, limit, threads=threads))
+    return result.reshape(x.shape)
+
+
+def grouped_moe(x_bits, indices, scores, bank, shared, limit: float, *,
+                threads: int | None = None) -> np.ndarray:
+    """SortedGroupedFP8MoE.grouped_from_routes (glm53_flash_mlx/grouped_fp8.py:294-321)."""
+    x = _c(x_bits, np.uint16)
+    H = x.shape[-1]
+    flat = x.reshape(-1, H)
+    T = flat.shape[0]
+    idx = _c(indices, np.uint32).reshape(T, -1)
+    top_k = idx.shape[1]
+    plan = route_plan(idx.reshape(-1), bank[0].shape[0], _c(scores, np.float32).reshape(-1))
+    sorted_x = flat[plan["order"] // top_k]
+    I = bank[0].shape[1] // 2
+    gate_up = grouped_linear(sorted_x, plan["sorted_experts"], bank[0], bank[1], threads=threads)
+    hidden = activate_gate_up(gate_up, I, limit)
+    down = grouped_linear(hidden, plan["sorted_experts"], bank[2], bank[3], threads=threads)
+    result = restore_and_reduce(down, plan["sorted_scores"], plan["inverse"], T, top_k)
+    if shared is not None:
+        result = bf16_add(result, shared_expert(flat, shared, limit, threads=threads))
+    return result.reshape(x.shape)

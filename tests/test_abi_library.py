@@ -1,0 +1,67 @@
+"""The C-ABI library loads and exports every entry point declared in
+include/*.h, and the Python binding covers exactly that set (CPU only: no
+compute call is made)."""
+
+import ctypes
+import re
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _declared() -> set[str]:
+    names = set()
+    for header in (ROOT / "include").glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", header.read_text(), flags=re.S)
+        names |= set(re.findall(r"\b(glm53_\w+)\s*\(", text))
+    return names
+
+
+def test_library_builds_and_exports_every_declared_symbol():
+    from glm53_flash_mlx_b200 import _native as N
+    from glm53_flash_mlx_b200.build import build
+
+    lib_path = build()
+    lib = ctypes.CDLL(str(lib_path))
+    declared = _declared()
+    assert declared, "no entry points found in include/*.h"
+    missing = [n for n in sorted(declared) if not hasattr(lib, n)]
+    assert not missing, missing
+    assert set(N.SIGNATURES) == declared
+    loaded = N.load_library()
+    assert loaded.glm53_kernel_abi().decode().startswith("glm53-b200-sm100a")
+    assert loaded.glm53_last_error() is not None
+
+
+def test_workspace_queries_are_pure_host_functions():
+    from glm53_flash_mlx_b200 import _native as N
+
+    lib = N.load_library()
+    assert lib.glm53_packed_decode_workspace_bytes(8, 1536, 1536) >= (8 * 1536 + 1536) * 2
+    assert lib.glm53_router_workspace_bytes(1, 288) >= 288 * 4
+    ws = lib.glm53_grouped_moe_workspace_bytes(2048, 8, 288, 4096, 1536, 1536)
+    assert ws >= 16384 * (4096 + 1536) * 2
+
+
+def test_operators_fail_closed_without_cuda():
+    import pytest
+    import torch
+
+    import glm53_flash_mlx_b200 as G
+
+    if torch.cuda.is_available():
+        pytest.skip("a CUDA device is present")
+    x = torch.zeros((1, 256), dtype=torch.bfloat16)
+    w = torch.zeros((128, 256), dtype=torch.uint8)
+    s = torch.ones((1, 2), dtype=torch.float32)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        G.block_fp8_linear(x, w, s)
+    with pytest.raises(RuntimeError):
+        G.router_topk(x, torch.zeros((8, 256)), torch.zeros(8), top_k=2)
+
+
+def test_oracle_library_is_separate_from_product():
+    """The product package never imports the oracle."""
+    for path in (ROOT / "glm53_flash_mlx_b200").rglob("*.py"):
+        text = path.read_text()
+        assert "import oracle" not in text and "from oracle" not in text, path

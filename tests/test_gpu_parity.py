@@ -1,0 +1,392 @@
+"""CUDA path vs the CPU oracle on seeded inputs (needs a B200: -m gpu)."""
+
+import ctypes
+import hashlib
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import MAX_ABS, assert_layer_close, bank_host, bits, f32, from_bits, shared_host
+
+pytestmark = pytest.mark.gpu
+KATS = json.loads((Path(__file__).resolve().parent / "golden" / "reference_kats.json").read_text())
+
+
+@pytest.fixture(scope="module")
+def G():
+    import glm53_flash_mlx_b200 as G
+
+    return G
+
+
+@pytest.fixture(scope="module")
+def N():
+    from glm53_flash_mlx_b200 import _native as N
+
+    N.lib()
+    return N
+
+
+@pytest.fixture(scope="module")
+def S():
+    from glm53_flash_mlx_b200 import synthetic as S
+
+    return S
+
+
+# ---------------------------------------------------------------------------
+# BF16 SwiGLU sigmoid: the reference's all-BF16 sweep, bit for bit
+# ---------------------------------------------------------------------------
+
+
+def test_sigmoid_sweep_bit_exact_on_gpu(N, oracle):
+    kat = KATS["sigmoid_sweep"]
+    allbits = np.arange(1 << 16, dtype=np.uint16)
+    vals = f32(allbits)
+    dom = allbits[np.isfinite(vals) & (np.abs(vals) <= np.float32(10.0))]
+    g = from_bits(dom)
+    out = torch.empty_like(g)
+    N.check(N.lib().glm53_sigmoid_bf16(g.data_ptr(), g.numel(), out.data_ptr(), N.stream()), "sigmoid")
+    torch.cuda.synchronize()
+    got = bits(out)
+    assert hashlib.sha256(got.tobytes()).hexdigest() == kat["reference_sigmoid_sha256"]
+    # and beyond the pinned domain (g < -10) GPU and oracle agree
+    neg = allbits[np.isfinite(vals) & (vals < -10.0)]
+    out2 = torch.empty(neg.size, dtype=torch.bfloat16, device="cuda")
+    N.check(N.lib().glm53_sigmoid_bf16(from_bits(neg).data_ptr(), neg.size, out2.data_ptr(), N.stream()), "sigmoid")
+    assert np.array_equal(bits(out2), oracle.sigmoid_bf16(neg))
+
+
+# ---------------------------------------------------------------------------
+# block_fp8_linear
+# ---------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize(
+    "M,N_,K",
+    [(1, 129, 257), (2, 129, 257), (1, 256, 4096), (3, 384, 1024), (8, 512, 2048), (16, 256, 256),
+     (17, 256, 512), (64, 256, 512), (200, 384, 1024), (1, 6144, 4096)],
+)
+def test_block_linear_matches_oracle(G, S, oracle, M, N_, K):
+    w, s = S.random_block_fp8(N_, K, seed=M * 1000 + N_, device="cuda")
+    x = S.random_bf16((M, K), seed=K, device="cuda")
+    y = G.block_fp8_linear(x, w, s)
+    torch.cuda.synchronize()
+    ref = oracle.block_fp8_linear(bits(x), w.cpu().numpy(), s.cpu().numpy())
+    stats = assert_layer_close(bits(y), ref, max_abs=0.03125)
+    if M <= 16:  # FP32 GEMV: only summation-order rounding flips
+        assert stats["bit_identical"] >= 0.97, stats
+
+
+def test_block_linear_reference_geometry_random_codes(G, oracle):
+    """tests/test_fp8_metal.py:23-39: random codes 0..246 (includes 0x7F = 480)."""
+    g = torch.Generator(device="cuda").manual_seed(5)
+    codes = torch.randint(0, 247, (129, 257), generator=g, device="cuda", dtype=torch.int32).to(torch.uint8)
+    scales = torch.rand((2, 3), generator=g, device="cuda") * 0.02
+    x = torch.randn((2, 257), generator=g, device="cuda").to(torch.bfloat16)
+    y = G.block_fp8_linear(x, codes, scales)
+    lut = oracle.e4m3_table()
+    dense = lut[codes.cpu().numpy()] * np.repeat(np.repeat(scales.cpu().numpy(), 128, 0), 128, 1)[:129, :257]
+    expected = oracle.bf16_from_f32(f32(bits(x)) @ dense.T)
+    assert np.abs(f32(bits(y)) - f32(expected)).max() <= 0.03125
+
+
+def test_block_linear_fail_closed_checks(G):
+    x = torch.zeros((1, 256), dtype=torch.bfloat16, device="cuda")
+    w = torch.zeros((128, 256), dtype=torch.uint8, device="cuda")
+    s = torch.ones((1, 2), dtype=torch.float32, device="cuda")
+    with pytest.raises(ValueError, match="uint8"):
+        G.block_fp8_linear(x, w.float(), s)
+    with pytest.raises(ValueError, match="float32"):
+        G.block_fp8_linear(x, w, s.double())
+    with pytest.raises(ValueError, match="input width"):
+        G.block_fp8_linear(x[:, :128], w, s)
+    with pytest.raises(ValueError, match="block128"):
+        G.block_fp8_linear(x, w, torch.ones((2, 2), device="cuda"))
+    with pytest.raises(RuntimeError):
+        G.block_fp8_linear(x.cpu(), w, s)
+    y = G.block_fp8_linear(x[:0], w, s)
+    assert y.shape == (0, 128)
+
+
+# ---------------------------------------------------------------------------
+# Router
+# ---------------------------------------------------------------------------
+
+
+def _logit_rel_err(gpu, ref64):
+    # |delta| / max(|logit|, 1% of the token's logit RMS): 1e-6 "relative"
+    # without dividing by logits that happen to sit at zero
+    floor = 0.01 * np.sqrt((ref64 ** 2).mean(axis=-1, keepdims=True))
+    return float((np.abs(gpu - ref64) / np.maximum(np.abs(ref64), floor)).max())
+
+
+@pytest.mark.parametrize("T", [1, 5, 8, 64, 300])
+def test_router_matches_oracle(G, S, oracle, T):
+    E, H = 288, 4096
+    w, b = S.make_router(E, H, seed=1, device="cuda", zipf_alpha=0.5 if T > 8 else 0.0)
+    x = S.random_bf16((T, H), seed=T, device="cuda")
+    idx, sc, logits = G.router_topk(x, w, b, top_k=8, return_logits=True)
+    torch.cuda.synchronize()
+    r_idx, r_sc, r_l64, margin = oracle.router(bits(x), w.cpu().numpy(), b.cpu().numpy(), top_k=8)
+    assert _logit_rel_err(logits.cpu().numpy(), r_l64) <= 1e-6
+    clear = margin > 1e-5
+    assert clear.mean() > 0.9
+    assert np.array_equal(idx.cpu().numpy()[clear].astype(np.uint32), r_idx[clear])
+    np.testing.assert_allclose(sc.cpu().numpy()[clear], r_sc[clear], rtol=1e-6, atol=1e-6)
+
+
+def test_router_group_selection_matches_oracle(G, S, oracle):
+    E, H, T = 64, 512, 16
+    w, b = S.make_router(E, H, seed=3, device="cuda")
+    x = S.random_bf16((T, H), seed=4, device="cuda")
+    idx, sc = G.router_topk(x, w, b, top_k=6, n_group=8, topk_group=3, routed_scaling_factor=2.5)
+    r_idx, r_sc, _, margin = oracle.router(bits(x), w.cpu().numpy(), b.cpu().numpy(), top_k=6, n_group=8,
+                                           topk_group=3, routed_scaling_factor=2.5)
+    clear = margin > 1e-5
+    assert np.array_equal(idx.cpu().numpy()[clear].astype(np.uint32), r_idx[clear])
+    np.testing.assert_allclose(sc.cpu().numpy()[clear], r_sc[clear], rtol=1e-6, atol=1e-6)
+
+
+# ---------------------------------------------------------------------------
+# Packed decode MoE
+# ---------------------------------------------------------------------------
+
+
+def _decode_case(S, E, H, I, seed, limit):
+    bank = S.make_bank(E, H, I, seed=seed, device="cuda")
+    shared = S.make_shared(H, I, seed=seed + 1, limit=limit, device="cuda")
+    return bank, shared
+
+
+@pytest.mark.parametrize("E,H,I,limit", [(8, 257, 129, 3.0), (8, 256, 128, 3.0), (16, 1024, 384, 10.0)])
+def test_packed_decode_matches_oracle_small(G, S, oracle, E, H, I, limit):
+    from glm53_flash_mlx_b200.packed import shared_fp8_tensors
+
+    bank, shared_mod = _decode_case(S, E, H, I, 11, limit)
+    shared = shared_fp8_tensors(shared_mod)
+    gen = np.random.default_rng(E + H)
+    for trial in range(3):
+        ids = gen.permutation(E)[:8].astype(np.int32)
+        sc = gen.uniform(0.05, 0.3, 8).astype(np.float32)
+        x = S.random_bf16((H,), seed=trial, device="cuda", std=2.0)
+        out = G.packed_decode_moe(x, torch.from_numpy(ids).cuda(), torch.from_numpy(sc).cuda(), bank, shared,
+                                  limit=limit)
+        torch.cuda.synchronize()
+        ref = oracle.packed_decode_moe(bits(x), ids, sc, bank_host(bank), shared_host(shared), limit)
+        stats = assert_layer_close(bits(out), ref)
+        assert stats["bit_identical"] >= 0.95, stats
+
+
+def test_packed_decode_config2_full_size(G, S, oracle):
+    """Config 2: H=4096, I=1536, 288 experts + shared, limit 10, routed by the
+    FP32 router; oracle on the 8 touched experts."""
+    from glm53_flash_mlx_b200.packed import shared_fp8_tensors
+
+    E, H, I = 288, 4096, 1536
+    bank = S.make_bank(E, H, I, seed=1, device="cuda")
+    shared = shared_fp8_tensors(S.make_shared(H, I, seed=2, device="cuda"))
+    w, b = S.make_router(E, H, seed=3, device="cuda")
+    for t in range(4):
+        x = S.random_bf16((1, H), seed=100 + t, device="cuda")
+        idx, sc = G.router_topk(x, w, b, top_k=8)
+        out = G.packed_decode_moe(x[0], idx[0], sc[0], bank, shared, limit=10.0)
+        torch.cuda.synchronize()
+        ids = idx[0].cpu().numpy()
+        sub = bank_host(bank, ids)
+        ref = oracle.packed_decode_moe(bits(x[0]), np.arange(8, dtype=np.uint32), sc[0].cpu().numpy(), sub,
+                                       shared_host(shared), 10.0)
+        stats = assert_layer_close(bits(out), ref)
+        assert stats["bit_identical"] >= 0.95, stats
+
+
+def test_packed_moe_module_matches_direct_module_bitwise(G, S):
+    """tests/test_fp8_metal.py:87-151: packed decode and 9-row prefill are
+    bit-equal to the Direct module over the same expert tensors."""
+    from types import SimpleNamespace
+
+    routes = torch.tensor([[7, 1, 5, 0, 3, 6, 2, 4]], dtype=torch.int32, device="cuda")
+    scores = torch.tensor([[0.24, 0.18, 0.15, 0.13, 0.11, 0.08, 0.06, 0.05]], device="cuda")
+
+    class FixedGate(torch.nn.Module):
+        def forward(self, x):
+            shape = (*x.shape[:-1], 8)
+            return routes.expand(shape), scores.expand(shape)
+
+    config = SimpleNamespace(hidden_size=257, moe_intermediate_size=129, swiglu_limit=3.0, n_routed_experts=8,
+                             num_experts_per_tok=8)
+    direct = G.DirectFP8MoE(config, FixedGate(), None, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(7)
+    for e in direct.experts:
+        for p in (e.gate_proj, e.up_proj, e.down_proj):
+            p.weight = torch.randint(0, 247, p.weight.shape, generator=g, device="cuda", dtype=torch.int32).to(
+                torch.uint8)
+            p.weight_scale_inv = torch.rand(p.weight_scale_inv.shape, generator=g, device="cuda") * 0.002
+    bank = G.PackedFP8ExpertBank.pack(direct.experts)
+    packed = G.PackedFP8MoE(bank, config, direct.gate, None)
+    x = (torch.randn((1, 1, 257), generator=g, device="cuda") * 2).to(torch.bfloat16)
+    assert torch.equal(packed(x), direct(x))
+    xp = (torch.randn((1, 9, 257), generator=g, device="cuda") * 2).to(torch.bfloat16)
+    assert torch.equal(packed(xp), direct(xp))
+
+
+def test_packed_decode_flags_bad_expert_without_trapping(G, S):
+    from glm53_flash_mlx_b200.packed import check_status
+
+    bank, _ = _decode_case(S, 8, 256, 128, 5, 3.0)
+    x = S.random_bf16((256,), seed=1, device="cuda")
+    ids = torch.tensor([0, 1, 2, 3, 4, 5, 6, 99], dtype=torch.int32, device="cuda")
+    sc = torch.full((8,), 0.125, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = G.packed_decode_moe(x, ids, sc, bank, None, limit=3.0, status=status)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
+    with pytest.raises(IndexError):
+        check_status(status)
+    with pytest.raises(ValueError):
+        G.packed_decode_moe(x[:128], ids, sc, bank, None, limit=3.0)
+
+
+# ---------------------------------------------------------------------------
+# Route plan and grouped prefill
+# ---------------------------------------------------------------------------
+
+
+def _plan_gpu(ids, E, tile_rows, scores=None):
+    from glm53_flash_mlx_b200.grouped_fp8 import _route_plan
+
+    t = torch.from_numpy(ids.astype(np.int32)).cuda()
+    s = None if scores is None else torch.from_numpy(scores).cuda()
+    p = _route_plan(t, E, s, tile_rows)
+    torch.cuda.synchronize()
+    return {k: (v.cpu().numpy() if v is not None else None) for k, v in p.items()}
+
+
+def test_route_plan_tile_descriptor_known_answer_on_gpu(G):
+    kat = KATS["tile_descriptors"]
+    se = torch.tensor([0] * 31 + [1] * 32 + [287] * 33, dtype=torch.int32, device="cuda")
+    te, ts, tl, ro, to = (t.cpu().numpy() for t in G.build_grouped_tile_plan(se, 288))
+    valid = ts < 96
+    assert [list(map(int, t)) for t in zip(te[valid], ts[valid], tl[valid])] == kat["valid"]
+    assert te.size == 3 + 288 and (te[~valid] == 0).all() and (ts[~valid] == 96).all() and (tl[~valid] == 0).all()
+
+
+@pytest.mark.parametrize("R,E,tile_rows", [(96, 8, 32), (16384, 288, 32), (16384, 288, 128), (65536, 288, 128),
+                                           (1000, 1024, 8), (1, 288, 128)])
+def test_route_plan_bit_exact(oracle, R, E, tile_rows):
+    rng = np.random.default_rng(R + E)
+    ids = rng.integers(0, E, R).astype(np.uint32)
+    if R > 10:
+        ids[::37] = E + 5  # invalid ids, counted and placed last
+    scores = rng.uniform(size=R).astype(np.float32)
+    got = _plan_gpu(ids, E, tile_rows, scores)
+    ref = oracle.route_plan(ids, E, scores)
+    for k in ("order", "inverse", "sorted_experts", "sorted_scores"):
+        assert np.array_equal(got[k].view(np.uint32), ref[k].view(np.uint32)), k
+    assert np.array_equal(got["route_offsets"].view(np.uint32), ref["expert_offsets"])
+    assert int(got["invalid_count"][0]) == ref["invalid"]
+    te, ts, tl, ro, to = oracle.tile_plan(ref["sorted_experts"], E, tile_rows)
+    assert np.array_equal(got["tile_experts"].view(np.uint32), te)
+    assert np.array_equal(got["tile_starts"].view(np.uint32), ts)
+    assert np.array_equal(got["tile_lengths"].view(np.uint32), tl)
+    assert np.array_equal(got["tile_offsets"].view(np.uint32), to)
+    assert int(got["descriptor_count"][0]) == int(to[-1])
+
+
+def test_grouped_linear_and_pieces_match_oracle(G, S, oracle):
+    E, H, I, T, k = 8, 256, 128, 32, 8
+    bank = S.make_bank(E, H, I, seed=21, device="cuda")
+    x = S.random_bf16((T, H), seed=22, device="cuda")
+    gen = np.random.default_rng(3)
+    idx = np.stack([gen.permutation(E)[:k] for _ in range(T)]).astype(np.int32)
+    sc = gen.uniform(0.05, 0.3, (T, k)).astype(np.float32)
+    it, st = torch.from_numpy(idx).cuda(), torch.from_numpy(sc).cuda()
+    sorted_x, sorted_experts, sorted_scores, inverse = G.build_route_plan(x, it, st)
+    plan = G.build_grouped_tile_plan(sorted_experts, E)
+    gate_up = G.grouped_fp8_linear(sorted_x, plan, bank.gate_up_weight, bank.gate_up_scale_inv)
+    hidden = G.activate_gate_up(gate_up, I, 3.0)
+    down = G.grouped_fp8_linear(hidden, plan, bank.down_weight, bank.down_scale_inv)
+    out = G.restore_and_reduce(down, sorted_scores, inverse, (T, H), k)
+    torch.cuda.synchronize()
+    rp = oracle.route_plan(idx.reshape(-1), E, sc.reshape(-1))
+    assert np.array_equal(bits(sorted_x), bits(x)[rp["order"] // k])
+    hb = bank_host(bank)
+    r_gu = oracle.grouped_linear(bits(sorted_x), rp["sorted_experts"], hb[0], hb[1])
+    assert_layer_close(bits(gate_up), r_gu, max_abs=0.05)
+    r_hidden = oracle.activate_gate_up(bits(gate_up), I, 3.0)
+    assert np.array_equal(bits(hidden), r_hidden)  # same inputs -> bit-exact elementwise
+    r_down = oracle.grouped_linear(bits(hidden), rp["sorted_experts"], hb[2], hb[3])
+    assert_layer_close(bits(down), r_down)
+    r_out = oracle.restore_and_reduce(bits(down), rp["sorted_scores"], rp["inverse"], T, k)
+    assert np.array_equal(bits(out), r_out)  # same inputs -> bit-exact combine
+
+
+@pytest.mark.parametrize("T,E,H,I,Is", [(32, 8, 256, 128, 128), (200, 64, 1024, 384, 256)])
+def test_grouped_moe_matches_oracle(G, S, oracle, T, E, H, I, Is):
+    from glm53_flash_mlx_b200.packed import shared_fp8_tensors
+
+    bank = S.make_bank(E, H, I, seed=T, device="cuda")
+    shared = shared_fp8_tensors(S.make_shared(H, Is, seed=T + 1, device="cuda"))
+    w, b = S.make_router(E, H, seed=T + 2, device="cuda", zipf_alpha=0.5)
+    x = S.random_bf16((T, H), seed=T + 3, device="cuda")
+    idx, sc = G.router_topk(x, w, b, top_k=8)
+    out = G.grouped_moe(x, idx, sc, bank, shared, limit=10.0)
+    torch.cuda.synchronize()
+    ref = oracle.grouped_moe(bits(x), idx.cpu().numpy(), sc.cpu().numpy(), bank_host(bank), shared_host(shared), 10.0)
+    assert_layer_close(bits(out), ref)
+
+
+def test_grouped_moe_config3_full_size_token_subset(G, S, oracle):
+    """Config 3 at T=2048 (16,384 routes, Zipf-skewed bias): the whole layer
+    on the GPU, checked against the oracle on a 24-token subset (a token's
+    output depends only on its own routes)."""
+    from glm53_flash_mlx_b200.packed import shared_fp8_tensors
+
+    E, H, I, T = 288, 4096, 1536, 2048
+    bank = S.make_bank(E, H, I, seed=2, device="cuda")
+    shared = shared_fp8_tensors(S.make_shared(H, I, seed=3, device="cuda"))
+    w, b = S.make_router(E, H, seed=4, device="cuda", zipf_alpha=0.5)
+    x = S.random_bf16((T, H), seed=5, device="cuda")
+    idx, sc = G.router_topk(x, w, b, top_k=8)
+    out = G.grouped_moe(x, idx, sc, bank, shared, limit=10.0)
+    torch.cuda.synchronize()
+    sel = np.linspace(0, T - 1, 24).astype(np.int64)
+    idx_np = idx.cpu().numpy()[sel]
+    touched = np.unique(idx_np)
+    remap = np.searchsorted(touched, idx_np).astype(np.uint32)
+    ref = oracle.grouped_moe(bits(x)[sel], remap, sc.cpu().numpy()[sel], bank_host(bank, touched),
+                             shared_host(shared), 10.0)
+    assert_layer_close(bits(out)[sel], ref)
+
+
+def test_sorted_grouped_module_vs_direct_and_decode_fallback(G, S):
+    """tests/test_fp8_metal.py:154-198: 32-token grouped prefill within
+    0.02/0.02 of Direct; decode falls back and is bit-equal; min_routes 256."""
+    from types import SimpleNamespace
+
+    class DeterministicGate(torch.nn.Module):
+        def forward(self, x):
+            rows = x.reshape(-1, x.shape[-1]).shape[0]
+            routes = torch.arange(rows * 8, dtype=torch.int32, device=x.device).reshape(rows, 8)
+            indices = ((routes * 5 + 3) % 8).reshape(*x.shape[:-1], 8)
+            return indices, torch.full(indices.shape, 0.125, dtype=torch.float32, device=x.device)
+
+    config = SimpleNamespace(hidden_size=256, moe_intermediate_size=128, swiglu_limit=3.0, n_routed_experts=8,
+                             num_experts_per_tok=8)
+    direct = G.DirectFP8MoE(config, DeterministicGate(), None, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(9)
+    for e in direct.experts:
+        for p in (e.gate_proj, e.up_proj, e.down_proj):
+            p.weight = torch.randint(0, 247, p.weight.shape, generator=g, device="cuda", dtype=torch.int32).to(
+                torch.uint8)
+            p.weight_scale_inv = torch.rand(p.weight_scale_inv.shape, generator=g, device="cuda") * 0.002
+    bank = G.PackedFP8ExpertBank.pack(direct.experts)
+    grouped = G.SortedGroupedFP8MoE(bank, config, direct.gate, None)
+    assert grouped.min_routes == 256
+    xp = torch.randn((1, 32, 256), generator=g, device="cuda").to(torch.bfloat16)
+    assert torch.allclose(grouped(xp).float(), direct(xp).float(), rtol=0.02, atol=0.02)
+    xd = torch.randn((1, 1, 256), generator=g, device="cuda").to(torch.bfloat16)
+    assert torch.equal(grouped(xd), direct(xd))
