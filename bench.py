@@ -45,12 +45,15 @@ POOL = 64
 def parse_args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=256)
-    p.add_argument("--warmup", type=int, default=16)
+    p.add_argument("--steps", type=int, default=20000)
+    p.add_argument("--warmup", type=int, default=2000)
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
     p.add_argument("--layers", type=int, default=8, help="distinct layers rotated through (L2 defeat)")
     p.add_argument("--no-prefill", action="store_true", help="skip the secondary T=2048 grouped measurement")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="bounded CPU-baseline sample")
+    p.add_argument("--experts", type=int, default=E, help="routed experts per layer (profiling uses fewer)")
+    p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    p.add_argument("--no-e2e", action="store_true", help="skip the module-API end-to-end pass")
     return p.parse_args()
 
 
@@ -125,7 +128,7 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.rows.append([c.strip() for c in line.split(",")])
+            self.rows.append([time.monotonic()] + [c.strip() for c in line.split(",")])
 
     def __exit__(self, *exc):
         if self.proc is not None:
@@ -137,10 +140,14 @@ class ClockSampler:
             if self.thread is not None:
                 self.thread.join(timeout=2)
 
-    def summary(self) -> dict:
+    def summary(self, t0: float | None = None, t1: float | None = None) -> dict:
+        """Clocks sampled between host times t0 and t1 (the timed region)."""
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for r in self.rows:
+            if (t0 is not None and r[0] < t0) or (t1 is not None and r[0] > t1):
+                continue
+            r = r[1:]
             try:
                 sm.append(float(r[1]))
                 mx.append(float(r[2]))
@@ -173,16 +180,16 @@ DOWN_BYTES = (TOP_K + 1) * H * I + (TOP_K + 1) * (H // 128) * (I // 128) * 4 + (
 STEP_BYTES = ROUTER_BYTES + GATE_UP_BYTES + DOWN_BYTES
 
 
-def build_layers(n_layers: int, seed0: int, device):
+def build_layers(n_layers: int, seed0: int, device, experts: int = E):
     from glm53_flash_mlx_b200 import synthetic as S
     from glm53_flash_mlx_b200.packed import shared_fp8_tensors
 
     layers = []
     for l in range(n_layers):
         seed = seed0 + 17 * l
-        bank = S.make_bank(E, H, I, seed=seed, device=device)
+        bank = S.make_bank(experts, H, I, seed=seed, device=device)
         shared_mod = S.make_shared(H, I, seed=seed + 1, limit=LIMIT, device=device)
-        w, b = S.make_router(E, H, seed=seed + 2, device=device)
+        w, b = S.make_router(experts, H, seed=seed + 2, device=device)
         layers.append({"bank": bank, "shared_mod": shared_mod, "shared": shared_fp8_tensors(shared_mod),
                        "router_w": w, "router_b": b})
     return layers
@@ -197,10 +204,10 @@ def bench_b200(args, world, rank, local):
     from glm53_flash_mlx_b200.router import Float32Gate
 
     dev = torch.device("cuda", local)
-    N.lib()
-    layers = build_layers(args.layers, 1000 + 101 * rank, dev)
-    xs = S.random_bf16((POOL, H), seed=77 + rank, device=dev)
     lib = N.lib()
+    n_exp = args.experts
+    layers = build_layers(args.layers, 1000 + 101 * rank, dev, n_exp)
+    xs = S.random_bf16((POOL, H), seed=77 + rank, device=dev)
 
     # ---- one step = router + packed decode, captured per (layer, x) -------
     ws = N.Workspace()
@@ -209,21 +216,21 @@ def bench_b200(args, world, rank, local):
     outs = [torch.empty(H, dtype=torch.bfloat16, device=dev) for _ in range(n_graphs)]
     idxs = [torch.empty((1, TOP_K), dtype=torch.int32, device=dev) for _ in range(n_graphs)]
     scs = [torch.empty((1, TOP_K), dtype=torch.float32, device=dev) for _ in range(n_graphs)]
-    rws = ws.get(dev, "router", lib.glm53_router_workspace_bytes(1, E))
+    rws = ws.get(dev, "router", lib.glm53_router_workspace_bytes(1, n_exp))
     dws = ws.get(dev, "decode", lib.glm53_packed_decode_workspace_bytes(TOP_K, I, I))
 
     def step(i, stream):
         L = layers[i % args.layers]
         x = xs[i % POOL]
-        N.check(lib.glm53_router_topk(x.data_ptr(), 1, H, L["router_w"].data_ptr(), E, L["router_b"].data_ptr(), TOP_K,
-                                      1, 1, 1, 1.0, idxs[i].data_ptr(), scs[i].data_ptr(), None, rws.data_ptr(),
-                                      rws.numel(), stream), "router")
+        N.check(lib.glm53_router_topk(x.data_ptr(), 1, H, L["router_w"].data_ptr(), n_exp, L["router_b"].data_ptr(),
+                                      TOP_K, 1, 1, 1, 1.0, idxs[i].data_ptr(), scs[i].data_ptr(), None,
+                                      rws.data_ptr(), rws.numel(), stream), "router")
         sh = L["shared"]
         bank = L["bank"]
         N.check(lib.glm53_packed_decode_moe(
             x.data_ptr(), H, idxs[i].data_ptr(), scs[i].data_ptr(), TOP_K, bank.gate_up_weight.data_ptr(),
-            bank.gate_up_scale_inv.data_ptr(), bank.down_weight.data_ptr(), bank.down_scale_inv.data_ptr(), E, I,
-            sh[0].data_ptr(), sh[1].data_ptr(), sh[2].data_ptr(), sh[3].data_ptr(), sh[4].data_ptr(),
+            bank.gate_up_scale_inv.data_ptr(), bank.down_weight.data_ptr(), bank.down_scale_inv.data_ptr(), n_exp,
+            I, sh[0].data_ptr(), sh[1].data_ptr(), sh[2].data_ptr(), sh[3].data_ptr(), sh[4].data_ptr(),
             sh[5].data_ptr(), I, LIMIT, outs[i].data_ptr(), dws.data_ptr(), dws.numel(), status.data_ptr(),
             stream), "decode")
 
@@ -240,24 +247,24 @@ def bench_b200(args, world, rank, local):
         graphs.append(g)
     torch.cuda.synchronize()
 
-    for i in range(args.warmup):
-        graphs[i % n_graphs].replay()
-    torch.cuda.synchronize()
-    barrier(world)
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(torch.cuda.current_device()) as clocks:
+        for i in range(args.warmup):
+            graphs[i % n_graphs].replay()
         torch.cuda.synchronize()
         barrier(world)
+        h0 = time.monotonic()
         start.record()
         for i in range(args.steps):
             graphs[i % n_graphs].replay()
         stop.record()
         torch.cuda.synchronize()
+        h1 = time.monotonic()
         barrier(world)
     t_ms = max_over_ranks(start.elapsed_time(stop), world)
     if int(status.item()) != 0:
         raise RuntimeError(f"device status 0x{int(status.item()):x} during the timed region")
-    clk = clocks.summary()
+    clk = clocks.summary(h0, h1)
     tokens = args.steps * world
     value = tokens / (t_ms / 1e3)
 
@@ -265,7 +272,7 @@ def bench_b200(args, world, rank, local):
     torch.cuda.synchronize()
     k_start, k_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     cur = torch.cuda.current_stream().cuda_stream
-    reps = max(args.steps, 64)
+    reps = min(max(args.steps, 64), 4000)
     k_start.record()
     for i in range(reps):
         L = layers[i % args.layers]
@@ -273,7 +280,7 @@ def bench_b200(args, world, rank, local):
         bank = L["bank"]
         N.check(lib.glm53_packed_decode_gate_up(
             xs[i % POOL].data_ptr(), H, idxs[i % n_graphs].data_ptr(), TOP_K, bank.gate_up_weight.data_ptr(),
-            bank.gate_up_scale_inv.data_ptr(), E, I, sh[0].data_ptr(), sh[1].data_ptr(), sh[2].data_ptr(),
+            bank.gate_up_scale_inv.data_ptr(), n_exp, I, sh[0].data_ptr(), sh[1].data_ptr(), sh[2].data_ptr(),
             sh[3].data_ptr(), I, LIMIT, dws.data_ptr(), dws.numel(), status.data_ptr(), cur), "gate_up")
     k_stop.record()
     torch.cuda.synchronize()
@@ -284,35 +291,37 @@ def bench_b200(args, world, rank, local):
                 "peak": peaks["hbm_gbs"], "peak_source": peaks["source"], "unit": "GB/s",
                 "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
                 "algorithmic_bytes_per_launch": GATE_UP_BYTES, "avg_launch_us": round(k_ms * 1e3, 2),
-                "step_bytes": STEP_BYTES,
+                "launches_timed": reps, "step_bytes": STEP_BYTES,
                 "step_frac": round(STEP_BYTES / (t_ms / args.steps / 1e3) / 1e9 / peaks["hbm_gbs"], 4)}
 
     # ---- e2e through the public module API -------------------------------
-    mods = []
-    for L in layers:
-        cfg = S.moe_config(H, I, E, TOP_K, LIMIT)
-        gate = Float32Gate(cfg, device=dev)
-        gate.weight.copy_(L["router_w"])
-        gate.e_score_correction_bias.copy_(L["router_b"])
-        mods.append(G.PackedFP8MoE(L["bank"], cfg, gate, L["shared_mod"]))
-    x_host = xs.cpu().reshape(POOL, 1, 1, H).pin_memory()
-    y_host = torch.empty((POOL, 1, 1, H), dtype=torch.bfloat16).pin_memory()
-    for i in range(args.warmup):
-        xd = x_host[i % POOL].to(dev, non_blocking=True)
-        y_host[i % POOL].copy_(mods[i % args.layers](xd), non_blocking=True)
-    torch.cuda.synchronize()
-    barrier(world)
-    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e_start.record()
-    for i in range(args.steps):
-        xd = x_host[i % POOL].to(dev, non_blocking=True)
-        y_host[i % POOL].copy_(mods[i % args.layers](xd), non_blocking=True)
-    e_stop.record()
-    torch.cuda.synchronize()
-    barrier(world)
-    e_ms = max_over_ranks(e_start.elapsed_time(e_stop), world)
-    e2e = {"value": round(tokens / (e_ms / 1e3), 2), "unit": "tokens/s", "h2d_bytes_per_step": H * 2,
-           "d2h_bytes_per_step": H * 2, "api": "PackedFP8MoE.__call__ (Float32Gate router)"}
+    e2e = None
+    if not args.no_e2e:
+        mods = []
+        for L in layers:
+            cfg = S.moe_config(H, I, n_exp, TOP_K, LIMIT)
+            gate = Float32Gate(cfg, device=dev)
+            gate.weight.copy_(L["router_w"])
+            gate.e_score_correction_bias.copy_(L["router_b"])
+            mods.append(G.PackedFP8MoE(L["bank"], cfg, gate, L["shared_mod"]))
+        x_host = xs.cpu().reshape(POOL, 1, 1, H).pin_memory()
+        y_host = torch.empty((POOL, 1, 1, H), dtype=torch.bfloat16).pin_memory()
+        for i in range(min(args.warmup, 500)):
+            xd = x_host[i % POOL].to(dev, non_blocking=True)
+            y_host[i % POOL].copy_(mods[i % args.layers](xd), non_blocking=True)
+        torch.cuda.synchronize()
+        barrier(world)
+        e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e_start.record()
+        for i in range(args.steps):
+            xd = x_host[i % POOL].to(dev, non_blocking=True)
+            y_host[i % POOL].copy_(mods[i % args.layers](xd), non_blocking=True)
+        e_stop.record()
+        torch.cuda.synchronize()
+        barrier(world)
+        e_ms = max_over_ranks(e_start.elapsed_time(e_stop), world)
+        e2e = {"value": round(tokens / (e_ms / 1e3), 2), "unit": "tokens/s", "h2d_bytes_per_step": H * 2,
+               "d2h_bytes_per_step": H * 2, "api": "PackedFP8MoE.__call__ (Float32Gate router)"}
 
     extra = {}
     if not args.no_prefill:
@@ -331,7 +340,8 @@ def bench_prefill(layers, dev, args):
 
     T = 2048
     x = S.random_bf16((T, H), seed=4242, device=dev)
-    w, b = S.make_router(E, H, seed=4243, device=dev, zipf_alpha=0.5)
+    n_exp = layers[0]["bank"].expert_count
+    w, b = S.make_router(n_exp, H, seed=4243, device=dev, zipf_alpha=0.5)
     ws = N.Workspace()
     idx, sc = G.router_topk(x, w, b, top_k=TOP_K, workspace=ws)
     touched = int(torch.unique(idx).numel())
@@ -350,8 +360,8 @@ def bench_prefill(layers, dev, args):
     sp.record()
     torch.cuda.synchronize()
     ms = st.elapsed_time(sp) / reps
-    bytes_ = (touched + 1) * 3 * H * I + E * H * 4 + 2 * T * H * 2
-    flops = 2 * T * TOP_K * 3 * H * I + 2 * T * 3 * H * I + 2 * T * E * H
+    bytes_ = (touched + 1) * 3 * H * I + n_exp * H * 4 + 2 * T * H * 2
+    flops = 2 * T * TOP_K * 3 * H * I + 2 * T * 3 * H * I + 2 * T * n_exp * H
     peaks = measured_peaks()
     return {"tokens_per_s": round(T / (ms / 1e3), 1), "ms_per_layer": round(ms, 3), "touched_experts": touched,
             "algorithmic_bytes": bytes_, "flops": flops,
@@ -475,7 +485,7 @@ def main():
     }
     if "prefill_2048" in res:
         line["prefill_2048"] = res["prefill_2048"]
-    if rank == 0 and world == 1:
+    if rank == 0 and world == 1 and not args.no_cpu:
         import torch
 
         hl = host_layer(layers[0])

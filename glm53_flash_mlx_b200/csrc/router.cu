@@ -186,8 +186,10 @@ __global__ void __launch_bounds__(256) router_small_kernel(
   if (threadIdx.x == 0) *counter = 0u;  // leave the workspace reusable
 }
 
-// Tiled FP32 GEMM for larger T: logits[T,E] = x[T,H] @ w[E,H]^T.
-// 64x64 output tile per block, 256 threads, 4x4 outputs each.
+// Tiled GEMM for larger T: logits[T,E] = x[T,H] @ w[E,H]^T.  64x64 output
+// tile per block, 256 threads, 4x4 outputs each.  Each 16-wide K slice is
+// summed in FP32 and the slice sums are accumulated in FP64, so the error
+// stays near that of a 16-term FP32 sum however long H is.
 __global__ void __launch_bounds__(256) router_gemm_kernel(const uint16_t* __restrict__ x, int T, int H,
                                                           const float* __restrict__ w, int E,
                                                           float* __restrict__ logits) {
@@ -196,9 +198,8 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(const uint16_t* __rest
   __shared__ float ws[BK][BN + 4];
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
   const int t0 = blockIdx.x * BM, e0 = blockIdx.y * BN;
-  float acc[4][4] = {};
+  double acc[4][4] = {};
   for (int k0 = 0; k0 < H; k0 += BK) {
-    // 64 rows x 16 k = 1024 values per operand, 4 per thread
     for (int i = threadIdx.x; i < BM * BK; i += 256) {
       int r = i / BK, k = i % BK;
       int t = t0 + r, e = e0 + r;
@@ -206,6 +207,7 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(const uint16_t* __rest
       ws[k][r] = (e < E && k0 + k < H) ? w[(size_t)e * H + k0 + k] : 0.f;
     }
     __syncthreads();
+    float part[4][4] = {};
 #pragma unroll
     for (int k = 0; k < BK; ++k) {
       float a[4], b[4];
@@ -216,8 +218,12 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(const uint16_t* __rest
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        for (int j = 0; j < 4; ++j) part[i][j] = fmaf(a[i], b[j], part[i][j]);
     }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] += (double)part[i][j];
     __syncthreads();
   }
 #pragma unroll
@@ -227,7 +233,7 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(const uint16_t* __rest
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       int e = e0 + tx * 4 + j;
-      if (e < E) logits[(size_t)t * E + e] = acc[i][j];
+      if (e < E) logits[(size_t)t * E + e] = (float)acc[i][j];
     }
   }
 }

@@ -32,16 +32,31 @@ def cosine(a: np.ndarray, b: np.ndarray) -> float:
     return float(a @ b / (na * nb))
 
 
+def bf16_ulp(v: np.ndarray) -> np.ndarray:
+    """Spacing of BF16 values at |v| (2^(e-7) for |v| in [2^e, 2^(e+1)))."""
+    a = np.abs(np.asarray(v, dtype=np.float32))
+    e = np.floor(np.log2(np.maximum(a, np.float32(2.0 ** -126))))
+    return np.exp2(e - 7).astype(np.float32)
+
+
 def assert_layer_close(gpu_bits: np.ndarray, ref_bits: np.ndarray, *, max_abs: float = MAX_ABS,
                        min_cos: float = MIN_COSINE) -> dict:
+    """BF16 layer tolerance: every element within max(max_abs, one BF16 ulp of
+    the reference value) -- above |y| = 4 one ulp is 0.03125, so a single
+    rounding flip of a non-bit-identical FP32 sum exceeds 2e-2 -- and
+    cosine >= min_cos over the tensor."""
     g, r = f32(gpu_bits), f32(ref_bits)
     assert np.isfinite(g).all(), "non-finite GPU output"
-    err = float(np.abs(g - r).max()) if g.size else 0.0
+    diff = np.abs(g - r)
+    err = float(diff.max()) if g.size else 0.0
+    bound = np.maximum(np.float32(max_abs), bf16_ulp(r))
+    worst = float((diff / bound).max()) if g.size else 0.0
     cos = cosine(g, r)
     same = float((np.asarray(gpu_bits) == np.asarray(ref_bits)).mean()) if g.size else 1.0
-    assert err <= max_abs, f"max-abs {err} > {max_abs}"
+    over = int((diff > max_abs).sum())
+    assert worst <= 1.0, f"max-abs {err} exceeds max({max_abs}, 1 BF16 ulp) (worst ratio {worst:.3f})"
     assert cos >= min_cos, f"cosine {cos} < {min_cos}"
-    return {"max_abs": err, "cosine": cos, "bit_identical": same}
+    return {"max_abs": err, "cosine": cos, "bit_identical": same, "over_max_abs_within_ulp": over}
 
 
 def bank_host(bank, ids=None):
