@@ -217,7 +217,9 @@ def bench_b200(args, world, rank, local):
     idxs = [torch.empty((1, TOP_K), dtype=torch.int32, device=dev) for _ in range(n_graphs)]
     scs = [torch.empty((1, TOP_K), dtype=torch.float32, device=dev) for _ in range(n_graphs)]
     rws = ws.get(dev, "router", lib.glm53_router_workspace_bytes(1, n_exp))
-    dws = ws.get(dev, "decode", lib.glm53_packed_decode_workspace_bytes(TOP_K, I, I))
+    flags = [N.decode_flags(L["bank"].gate_up_weight, L["bank"].down_weight, L["shared"][0], L["shared"][2],
+                            L["shared"][4]) for L in layers]
+    dws = ws.get(dev, "decode", lib.glm53_packed_decode_workspace_bytes(TOP_K, H, I, I))
 
     def step(i, stream):
         L = layers[i % args.layers]
@@ -232,7 +234,7 @@ def bench_b200(args, world, rank, local):
             bank.gate_up_scale_inv.data_ptr(), bank.down_weight.data_ptr(), bank.down_scale_inv.data_ptr(), n_exp,
             I, sh[0].data_ptr(), sh[1].data_ptr(), sh[2].data_ptr(), sh[3].data_ptr(), sh[4].data_ptr(),
             sh[5].data_ptr(), I, LIMIT, outs[i].data_ptr(), dws.data_ptr(), dws.numel(), status.data_ptr(),
-            stream), "decode")
+            flags[i % args.layers], stream), "decode")
 
     s = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(s):
@@ -281,13 +283,14 @@ def bench_b200(args, world, rank, local):
         N.check(lib.glm53_packed_decode_gate_up(
             xs[i % POOL].data_ptr(), H, idxs[i % n_graphs].data_ptr(), TOP_K, bank.gate_up_weight.data_ptr(),
             bank.gate_up_scale_inv.data_ptr(), n_exp, I, sh[0].data_ptr(), sh[1].data_ptr(), sh[2].data_ptr(),
-            sh[3].data_ptr(), I, LIMIT, dws.data_ptr(), dws.numel(), status.data_ptr(), cur), "gate_up")
+            sh[3].data_ptr(), I, LIMIT, dws.data_ptr(), dws.numel(), status.data_ptr(), flags[i % args.layers],
+            cur), "gate_up")
     k_stop.record()
     torch.cuda.synchronize()
     k_ms = k_start.elapsed_time(k_stop) / reps
     peaks = measured_peaks()
     achieved = GATE_UP_BYTES / (k_ms / 1e3) / 1e9
-    roofline = {"kernel": "decode_gate_up_kernel", "bound": "hbm", "achieved": round(achieved, 1),
+    roofline = {"kernel": "decode_gate_up_v4", "bound": "hbm", "achieved": round(achieved, 1),
                 "peak": peaks["hbm_gbs"], "peak_source": peaks["source"], "unit": "GB/s",
                 "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
                 "algorithmic_bytes_per_launch": GATE_UP_BYTES, "avg_launch_us": round(k_ms * 1e3, 2),

@@ -22,6 +22,8 @@ GLM53_ERR_INVALID = 1
 GLM53_ERR_CUDA = 2
 GLM53_ERR_INDEX = 3
 
+FLAG_E4M3_FINITE = 1
+
 STATUS_BAD_EXPERT = 1
 STATUS_WAIT_TIMEOUT = 2
 STATUS_BAD_GEOMETRY = 4
@@ -31,26 +33,33 @@ _i64 = ctypes.c_int64
 _int = ctypes.c_int
 _f = ctypes.c_float
 _sz = ctypes.c_size_t
+_u32 = ctypes.c_uint32
 
 # name -> (restype, argtypes); mirrors include/glm53_b200.h
 SIGNATURES: dict[str, tuple] = {
     "glm53_kernel_abi": (ctypes.c_char_p, []),
     "glm53_last_error": (ctypes.c_char_p, []),
-    "glm53_fp8_linear": (_int, [_vp, _i64, _i64, _vp, _i64, _vp, _vp, _vp]),
+    "glm53_fp8_linear": (_int, [_vp, _i64, _i64, _vp, _i64, _vp, _vp, _u32, _vp]),
+    "glm53_e4m3_scan": (_int, [_vp, _i64, _vp, _vp]),
     "glm53_router_workspace_bytes": (_sz, [_i64, _i64]),
     "glm53_router_topk": (
         _int,
         [_vp, _i64, _i64, _vp, _i64, _vp, _int, _int, _int, _int, _f, _vp, _vp, _vp, _vp, _sz, _vp],
     ),
-    "glm53_packed_decode_workspace_bytes": (_sz, [_int, _i64, _i64]),
+    "glm53_packed_decode_workspace_bytes": (_sz, [_int, _i64, _i64, _i64]),
     "glm53_packed_decode_moe": (
         _int,
         [_vp, _i64, _vp, _vp, _int, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _f,
-         _vp, _vp, _sz, _vp, _vp],
+         _vp, _vp, _sz, _vp, _u32, _vp],
+    ),
+    "glm53_selected_decode_moe": (
+        _int,
+        [_vp, _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _f,
+         _vp, _vp, _sz, _vp, _u32, _vp],
     ),
     "glm53_packed_decode_gate_up": (
         _int,
-        [_vp, _i64, _vp, _int, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _f, _vp, _sz, _vp, _vp],
+        [_vp, _i64, _vp, _int, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _f, _vp, _sz, _vp, _u32, _vp],
     ),
     "glm53_route_plan": (
         _int,
@@ -59,7 +68,7 @@ SIGNATURES: dict[str, tuple] = {
     "glm53_gather_rows": (_int, [_vp, _i64, _vp, _i64, _int, _vp, _vp]),
     "glm53_grouped_fp8_linear": (
         _int,
-        [_vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _vp, _vp, _vp],
+        [_vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _vp, _vp, _u32, _vp],
     ),
     "glm53_activate_gate_up": (_int, [_vp, _i64, _i64, _f, _vp, _vp]),
     "glm53_restore_and_reduce": (_int, [_vp, _vp, _vp, _i64, _int, _i64, _vp, _vp, _vp]),
@@ -67,7 +76,7 @@ SIGNATURES: dict[str, tuple] = {
     "glm53_grouped_moe": (
         _int,
         [_vp, _i64, _i64, _vp, _vp, _int, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp,
-         _i64, _f, _vp, _vp, _sz, _vp, _vp],
+         _i64, _f, _vp, _vp, _sz, _vp, _u32, _vp],
     ),
     "glm53_sigmoid_bf16": (_int, [_vp, _i64, _vp, _vp]),
 }
@@ -141,6 +150,36 @@ def require_cuda(*tensors: torch.Tensor) -> torch.device:
         elif t.device != dev:
             raise ValueError(f"tensors on different devices: {dev} vs {t.device}")
     return dev
+
+
+_finite_cache: dict[tuple, bool] = {}
+
+
+def e4m3_finite(*weights: torch.Tensor) -> bool:
+    """True when none of the E4M3 weight tensors holds code 0x7F or 0xFF:
+    GLM53_FLAG_E4M3_FINITE may be used.  One device pass per tensor at first
+    use; the answer is cached per (storage, shape, version), so an in-place
+    write to a weight triggers a new scan."""
+    dev = require_cuda(*weights)
+    ok = True
+    for w in weights:
+        key = (w.data_ptr(), tuple(w.shape), w._version, w.device.index)
+        hit = _finite_cache.get(key)
+        if hit is None:
+            wc = w.contiguous()
+            count = torch.zeros(1, dtype=torch.int32, device=dev)
+            check(lib().glm53_e4m3_scan(wc.data_ptr(), wc.numel(), count.data_ptr(), stream(dev)),
+                  "glm53_e4m3_scan")
+            hit = int(count.item()) == 0
+            if len(_finite_cache) > 4096:
+                _finite_cache.clear()
+            _finite_cache[key] = hit
+        ok = ok and hit
+    return ok
+
+
+def decode_flags(*weights: torch.Tensor) -> int:
+    return FLAG_E4M3_FINITE if e4m3_finite(*weights) else 0
 
 
 class Workspace:

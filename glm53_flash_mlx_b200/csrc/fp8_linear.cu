@@ -2,102 +2,99 @@
 //
 // Replaces block_fp8_linear (glm53_flash_mlx/fp8.py:254-299) and its Metal
 // kernels K1/K2 (fp8.py:41-116).  Small M is HBM-bound: every weight byte is
-// read once with 16-byte streaming loads, decoded in registers and multiplied
-// against FP32 activations held in shared memory.  Large M goes to the
-// tensor-core grouped GEMM with a single expert (grouped.cu).
+// read once with 16-byte streaming loads and decoded in registers into
+// tensor-core fragments (gemv_tile.cuh).  Large M goes to the grouped GEMM
+// with a single expert (grouped.cu).
 #include <algorithm>
 
 #include "common.cuh"
+#include "gemv_tile.cuh"
 #include "kernels.cuh"
 
 namespace glm53 {
 
-// Activations are stored in shared memory as FP32 with the float4 index of
-// (chunk c, quarter q) at 4c + (q ^ ((c >> 1) & 3)): the 8 lanes of one
-// LDS.128 phase read chunks c..c+7 and land in 8 distinct bank groups.
-__device__ __forceinline__ int xs_swizzle(int c, int q) { return 4 * c + (q ^ ((c >> 1) & 3)); }
+// Tensor-core GEMV: persistent blocks over 16-row tiles for one chunk of up
+// to 8 activation rows (blockIdx.y); K split across ksplit_for(K) warps, each
+// streaming its K range through a cp.async ring; ordered cross-warp sum.
+// Requires K % 128 == 0 and 16-byte aligned x / w rows.
+constexpr int kGemvRing = 8;
 
-// Dot product of the 16 codes of chunk c with the swizzled activations.
-__device__ __forceinline__ float dot16_swz(uint4 w, const float4* xs4, int c) {
-  float f[4];
-  float acc = 0.f;
-  uint32_t words[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    e4m3x4_to_f32(words[q], f);
-    float4 xv = xs4[xs_swizzle(c, q)];
-    acc = fmaf(xv.x, f[0], acc);
-    acc = fmaf(xv.y, f[1], acc);
-    acc = fmaf(xv.z, f[2], acc);
-    acc = fmaf(xv.w, f[3], acc);
-  }
-  return acc;
-}
-
-__device__ __forceinline__ void load_x_swizzled(float* xs, const uint16_t* x, int K, int tid, int nthreads) {
-  const int nchunks = K >> 4;
-  for (int i = tid; i < (K >> 2); i += nthreads) {
-    int c = i >> 2, q = i & 3;
-    const uint2 raw = *reinterpret_cast<const uint2*>(x + 4 * i);
-    float4 v;
-    v.x = __uint_as_float(raw.x << 16);
-    v.y = __uint_as_float(raw.x & 0xFFFF0000u);
-    v.z = __uint_as_float(raw.y << 16);
-    v.w = __uint_as_float(raw.y & 0xFFFF0000u);
-    reinterpret_cast<float4*>(xs)[xs_swizzle(c, q)] = v;
-  }
-  (void)nchunks;
-}
-
-// One warp per output row; MR activation rows share each weight load.
-// Requires K % 16 == 0 and 16-byte aligned rows.
-template <int MR, int U>
-__global__ void __launch_bounds__(256) fp8_gemv_kernel(const uint16_t* __restrict__ x, int M, int K,
-                                                       const uint8_t* __restrict__ w, int N,
-                                                       const float* __restrict__ s,
-                                                       uint16_t* __restrict__ y) {
-  extern __shared__ float4 smem_x4[];
-  float* xs = reinterpret_cast<float*>(smem_x4);
-  const int m0 = blockIdx.y * MR;
-  const int mr = min(MR, M - m0);
-  for (int m = 0; m < mr; ++m)
-    load_x_swizzled(xs + (size_t)m * K, x + (size_t)(m0 + m) * K, K, threadIdx.x, blockDim.x);
-  __syncthreads();
-  const int lane = threadIdx.x & 31;
-  const int warps = blockDim.x >> 5;
-  const int nchunks = K >> 4;
-  const int scale_cols = (K + kBlock - 1) / kBlock;
-  for (int n = blockIdx.x * warps + (threadIdx.x >> 5); n < N; n += gridDim.x * warps) {
-    const uint4* wr = reinterpret_cast<const uint4*>(w + (size_t)n * K);
-    const float* srow = s + (size_t)(n / kBlock) * scale_cols;
-    float acc[MR];
-#pragma unroll
-    for (int m = 0; m < MR; ++m) acc[m] = 0.f;
-    for (int c0 = 0; c0 < nchunks; c0 += 32 * U) {
-      uint4 wv[U];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        int c = c0 + u * 32 + lane;
-        if (c < nchunks) wv[u] = ldg_stream(wr + c);
-      }
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        int c = c0 + u * 32 + lane;
-        if (c < nchunks) {
-          float sc = __ldg(srow + (c >> 3)) * 256.0f;
-#pragma unroll
-          for (int m = 0; m < MR; ++m) {
-            if (m < mr) acc[m] = fmaf(sc, dot16_swz(wv[u], smem_x4 + (size_t)m * (K >> 2), c), acc[m]);
-          }
-        }
+template <int KS, bool FINITE>
+__global__ void __launch_bounds__(32 * KS) gemv_stream_kernel(const uint16_t* __restrict__ x, int M, int K,
+                                                              const uint8_t* __restrict__ w, int N,
+                                                              const float* __restrict__ s, uint16_t* __restrict__ y,
+                                                              int chunk) {
+  constexpr int P = kGemvRing;
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+  const int m0 = blockIdx.y * chunk;
+  const int ncols = min(chunk, M - m0);
+  const int stride = (xs_stride(K) + 7) & ~7;
+  uint4* ring = reinterpret_cast<uint4*>(smem) + (size_t)warp * P * 64;
+  __half* xs = reinterpret_cast<__half*>(reinterpret_cast<uint4*>(smem) + (size_t)KS * P * 64);
+  float* red = reinterpret_cast<float*>(xs + (size_t)chunk * stride);  // [2][KS][128]
+  float* scratch = red + 2 * KS * 128;
+  const int ntiles = (N + 15) >> 4;
+  const int my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int kper = K / KS;
+  const int nslice = kper >> 6;
+  const int kw = warp * kper + 16 * q;
+  const int scols = K >> 7;
+  // issue cursor (tile, slice) runs P - 1 slices ahead of the consume cursor
+  int i_it = 0, i_sl = 0;
+  auto issue = [&]() {
+    if (i_it < my_tiles) {
+      const int row0 = (blockIdx.x + i_it * gridDim.x) << 4;
+      const int k = kw + 64 * i_sl;
+      uint4* dst = ring + ((i_it * nslice + i_sl) % P) * 64 + lane;
+      const bool v0 = row0 + g < N, v8 = row0 + g + 8 < N;
+      cp_async_16(dst, v0 ? (const void*)(w + (size_t)(row0 + g) * K + k) : (const void*)w, v0);
+      cp_async_16(dst + 32, v8 ? (const void*)(w + (size_t)(row0 + g + 8) * K + k) : (const void*)w, v8);
+      if (++i_sl == nslice) {
+        i_sl = 0;
+        ++i_it;
       }
     }
+    cp_async_commit_group();
+  };
+#pragma unroll 1
+  for (int p = 0; p < P - 1; ++p) issue();
+  const float smul = decode_unscale<FINITE>() * stage_f16(xs, stride, x + (size_t)m0 * K, K, ncols, K, scratch);
+  float part[4] = {0.f, 0.f, 0.f, 0.f}, tot[4] = {0.f, 0.f, 0.f, 0.f};
+  int u = 0;
+  for (int it = 0; it < my_tiles; ++it) {
+    const int row0 = (blockIdx.x + it * gridDim.x) << 4;
+    const float* srow = s + (size_t)(row0 >> 7) * scols + ((warp * kper) >> 7);
+    for (int sl = 0; sl < nslice; ++sl, ++u) {
+      issue();
+      cp_async_wait_group<P - 1>();
+      const uint4* src = ring + (u % P) * 64 + lane;
+      const uint4 f0 = src[0], f1 = src[32];
+      uint32_t xw[8];
+      load_x_frag(xw, xs + (g < ncols ? g : 0) * stride + kw + 64 * sl, g < ncols);
+      mma_slice<FINITE>(part, f0, f1, xw);
+      if (sl & 1) promote(tot, part, __ldg(srow + (sl >> 1)) * smul);
+    }
+    float* r = red + (it & 1) * KS * 128 + warp * 128;
+    r[g * 8 + 2 * q] = tot[0];
+    r[g * 8 + 2 * q + 1] = tot[1];
+    r[(g + 8) * 8 + 2 * q] = tot[2];
+    r[(g + 8) * 8 + 2 * q + 1] = tot[3];
 #pragma unroll
-    for (int m = 0; m < MR; ++m) {
-      float v = warp_sum(acc[m]);
-      if (lane == 0 && m < mr) y[(size_t)(m0 + m) * N + n] = f32_to_bf16_bits(v);
+    for (int c = 0; c < 4; ++c) tot[c] = 0.f;
+    __syncthreads();
+    const float* rb = red + (it & 1) * KS * 128;
+    for (int i = threadIdx.x; i < 128; i += blockDim.x) {
+      const int rr = i >> 3, c = i & 7;
+      if (c < ncols && row0 + rr < N) {
+        float v = 0.f;
+#pragma unroll
+        for (int ww = 0; ww < KS; ++ww) v = v + rb[ww * 128 + i];
+        y[(size_t)(m0 + c) * N + row0 + rr] = f32_to_bf16_bits(v);
+      }
     }
   }
+  cp_async_wait_group<0>();
 }
 
 // Generic path for any K / alignment: one warp per (row m, output n).
@@ -120,38 +117,53 @@ __global__ void __launch_bounds__(256) fp8_linear_scalar_kernel(const uint16_t* 
   if (lane == 0) y[m * N + n] = f32_to_bf16_bits(acc);
 }
 
-template <int MR>
-static int launch_gemv(const uint16_t* x, int M, int K, const uint8_t* w, int N, const float* s,
-                       uint16_t* y, cudaStream_t stream) {
-  constexpr int U = 4;
-  const size_t smem = (size_t)MR * K * sizeof(float);
-  if (smem > 48 * 1024) {
-    int rc_attr = ensure_max_smem((const void*)fp8_gemv_kernel<MR, U>, smem);
-    if (rc_attr) return rc_attr;
+static size_t gemv_smem(int KS, int chunk, int64_t K) {
+  return (size_t)KS * kGemvRing * 64 * 16 + (size_t)chunk * ((xs_stride(K) + 7) & ~7) * 2 +
+         (size_t)(2 * KS * 128 + 32) * sizeof(float);
+}
+
+template <int KS, bool FINITE>
+static int launch_gemv_stream(const uint16_t* x, int M, int K, const uint8_t* w, int N, const float* s,
+                              uint16_t* y, cudaStream_t stream) {
+  int chunk = std::min(8, M);
+  while (chunk > 1 && gemv_smem(KS, chunk, K) > 200 * 1024) chunk = (chunk + 1) / 2;
+  const size_t smem = gemv_smem(KS, chunk, K);
+  int rc_attr = ensure_max_smem((const void*)gemv_stream_kernel<KS, FINITE>, smem);
+  if (rc_attr) return rc_attr;
+  const int ntiles = (N + 15) / 16;
+  const int chunks = (M + chunk - 1) / chunk;
+  const int per_sm = std::max(1, std::min(2, (int)((220 * 1024) / smem)));
+  const int bx = std::max(1, std::min(ntiles, (sm_count() * per_sm + chunks - 1) / chunks));
+  dim3 grid((unsigned)bx, (unsigned)chunks);
+  gemv_stream_kernel<KS, FINITE><<<grid, 32 * KS, smem, stream>>>(x, M, K, w, N, s, y, chunk);
+  return check_launch("gemv_stream_kernel");
+}
+
+template <bool FINITE>
+static int dispatch_gemv(const uint16_t* x, int M, int K, const uint8_t* w, int N, const float* s, uint16_t* y,
+                         cudaStream_t stream) {
+  switch (ksplit_for(K)) {
+    case 8: return launch_gemv_stream<8, FINITE>(x, M, K, w, N, s, y, stream);
+    case 6: return launch_gemv_stream<6, FINITE>(x, M, K, w, N, s, y, stream);
+    case 4: return launch_gemv_stream<4, FINITE>(x, M, K, w, N, s, y, stream);
+    case 3: return launch_gemv_stream<3, FINITE>(x, M, K, w, N, s, y, stream);
+    case 2: return launch_gemv_stream<2, FINITE>(x, M, K, w, N, s, y, stream);
+    default: return launch_gemv_stream<1, FINITE>(x, M, K, w, N, s, y, stream);
   }
-  const int warps = 8;
-  int sms = sm_count();
-  int per_sm = std::max(1, std::min(8, (int)((200 * 1024) / std::max<size_t>(smem, 1))));
-  int blocks = std::min((N + warps - 1) / warps, sms * per_sm);
-  dim3 grid(blocks, (M + MR - 1) / MR);
-  fp8_gemv_kernel<MR, U><<<grid, warps * 32, smem, stream>>>(x, M, K, w, N, s, y);
-  return check_launch("fp8_gemv_kernel");
 }
 
 int fp8_linear_small_m(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w, int64_t N,
-                       const float* s, uint16_t* y, cudaStream_t stream) {
-  const bool vec = (K % 16 == 0) && (((uintptr_t)w & 15) == 0) && (((uintptr_t)x & 7) == 0) &&
-                   K <= 24576;
-  if (!vec) {
+                       const float* s, uint16_t* y, uint32_t flags, cudaStream_t stream) {
+  const bool tc = (K % 128 == 0) && (((uintptr_t)w & 15) == 0) && (((uintptr_t)x & 15) == 0) &&
+                  gemv_smem(ksplit_for(K), 1, K) <= 200 * 1024 && N <= INT32_MAX - 16;
+  if (!tc) {
     int64_t warps = M * N;
     int64_t blocks = (warps + 7) / 8;
     fp8_linear_scalar_kernel<<<(unsigned)blocks, 256, 0, stream>>>(x, M, K, w, N, s, y);
     return check_launch("fp8_linear_scalar_kernel");
   }
-  const size_t per_row = (size_t)K * sizeof(float);
-  if (M >= 4 && 4 * per_row <= 96 * 1024) return launch_gemv<4>(x, (int)M, (int)K, w, (int)N, s, y, stream);
-  if (M >= 2 && 2 * per_row <= 96 * 1024) return launch_gemv<2>(x, (int)M, (int)K, w, (int)N, s, y, stream);
-  return launch_gemv<1>(x, (int)M, (int)K, w, (int)N, s, y, stream);
+  if (flags & GLM53_FLAG_E4M3_FINITE) return dispatch_gemv<true>(x, (int)M, (int)K, w, (int)N, s, y, stream);
+  return dispatch_gemv<false>(x, (int)M, (int)K, w, (int)N, s, y, stream);
 }
 
 }  // namespace glm53
@@ -159,7 +171,7 @@ int fp8_linear_small_m(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w
 using namespace glm53;
 
 extern "C" int glm53_fp8_linear(const void* x, int64_t M, int64_t K, const uint8_t* w, int64_t N,
-                                const float* scale_inv, void* y, void* stream) {
+                                const float* scale_inv, void* y, uint32_t flags, void* stream) {
   if (M < 0 || K <= 0 || N <= 0 || (M > 0 && (!x || !w || !scale_inv || !y))) {
     set_last_error("glm53_fp8_linear: invalid arguments M=%lld K=%lld N=%lld", (long long)M,
                    (long long)K, (long long)N);
@@ -169,5 +181,5 @@ extern "C" int glm53_fp8_linear(const void* x, int64_t M, int64_t K, const uint8
   cudaStream_t st = (cudaStream_t)stream;
   if (M > kGemvMaxRows && dense_gemm_supported(K, N, w))
     return dense_fp8_gemm((const uint16_t*)x, M, K, w, N, scale_inv, (uint16_t*)y, st);
-  return fp8_linear_small_m((const uint16_t*)x, M, K, w, N, scale_inv, (uint16_t*)y, st);
+  return fp8_linear_small_m((const uint16_t*)x, M, K, w, N, scale_inv, (uint16_t*)y, flags, st);
 }

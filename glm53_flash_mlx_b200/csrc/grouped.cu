@@ -436,7 +436,8 @@ extern "C" int glm53_gather_rows(const void* x, int64_t H, const uint32_t* order
 extern "C" int glm53_grouped_fp8_linear(const void* x, int64_t R, int64_t K, const uint32_t* tile_experts,
                                         const uint32_t* tile_starts, const uint32_t* tile_lengths,
                                         int64_t descriptor_capacity, const uint8_t* w, int64_t E, int64_t N,
-                                        const float* scale_inv, void* out, void* stream) {
+                                        const float* scale_inv, void* out, uint32_t flags, void* stream) {
+  (void)flags;  // the BF16 tile path decodes exactly for every code
   if (R < 0 || K <= 0 || N <= 0 || E <= 0 || descriptor_capacity < 0 ||
       (R > 0 && (!x || !tile_experts || !tile_starts || !tile_lengths || !w || !scale_inv || !out))) {
     set_last_error("glm53_grouped_fp8_linear: invalid arguments");
@@ -547,7 +548,8 @@ extern "C" int glm53_grouped_moe(const void* x, int64_t T, int64_t H, const uint
                                  const float* shared_gate_s, const uint8_t* shared_up_w, const float* shared_up_s,
                                  const uint8_t* shared_down_w, const float* shared_down_s, int64_t I_shared,
                                  float limit, void* out, void* workspace, size_t workspace_bytes, uint32_t* status,
-                                 void* stream) {
+                                 uint32_t flags, void* stream) {
+  (void)flags;
   if (T < 0 || H <= 0 || I <= 0 || E <= 0 || top_k <= 0 || I_shared < 0) {
     set_last_error("glm53_grouped_moe: invalid geometry");
     return GLM53_ERR_INVALID;

@@ -10,7 +10,7 @@ namespace glm53 {
 constexpr int64_t kGemvMaxRows = 16;
 
 int fp8_linear_small_m(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w, int64_t N,
-                       const float* s, uint16_t* y, cudaStream_t stream);
+                       const float* s, uint16_t* y, uint32_t flags, cudaStream_t stream);
 
 // Tensor-core grouped GEMM (grouped.cu).
 //   A rows: x[a_index ? a_index[start+i] / a_div : start+i, :]  (BF16 [*, K])

@@ -1,4 +1,4 @@
-// Packed L=1 decode MoE (G3 + G4).
+// One-token decode MoE (G3 + G4) on tensor-core GEMV tiles.
 //
 // Replaces PackedFP8MoE.__call__ decode (glm53_flash_mlx/packed.py:896-923):
 //   K7  fused gate/up/SwiGLU over the selected experts  (packed.py:100-166)
@@ -6,60 +6,49 @@
 //   K6  selected down projections                        (packed.py:66-98)
 //   K8  FP32 slot-ordered weighted reduction             (packed.py:168-179)
 //   shared down (K1) and the BF16 `result + shared` add  (packed.py:915-922)
+// and the Direct module's selected-expert decode over separately allocated
+// experts (glm53_flash_mlx/fp8.py:372-383, kernels K3/K4 at fp8.py:142-251),
 // in two launches:
-//   decode_gate_up_kernel: one warp per (slot, row) pair; the shared expert is
-//     one more slot.  Each lane streams 16-byte chunks of the gate and up rows
-//     and multiplies them against FP32 activations in shared memory.
-//   decode_down_kernel: one warp per slot, a block owns RB output rows; the
-//     per-slot dot products meet in shared memory and are reduced in slot
-//     order with the reference's rounding points.
+//   decode_gate_up_v4: one warp per (slot, 8 hidden rows).  Its m16 MMA tile
+//     is the 8 gate rows (tile rows 0-7) and the 8 up rows (rows 8-15) of
+//     those hidden rows, over the whole K; lane 4g ends up holding gate and
+//     up of hidden row g and applies the BF16 SwiGLU itself.
+//   decode_down_v4: one warp per (slot, 16 output rows) over the whole K;
+//     per-slot dot products go to workspace and the last warp of each 16-row
+//     block (completion counter) reduces them in slot order with the
+//     reference's rounding points and adds the shared expert.
+// Weight fragments stream through per-warp cp.async rings (gemv_tile.cuh);
+// weight copies are issued before the activations are staged.
+// Shapes the tiles do not cover take a scalar path, one warp per dot product.
 #include <algorithm>
 
 #include "common.cuh"
+#include "gemv_tile.cuh"
 #include "kernels.cuh"
 
 namespace glm53 {
 
-__device__ __forceinline__ int xsw(int c, int q) { return 4 * c + (q ^ ((c >> 1) & 3)); }
-
-__device__ __forceinline__ float dot16_x(uint4 w, const float4* xs4, int c) {
-  float f[4];
-  float acc = 0.f;
-  uint32_t words[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    e4m3x4_to_f32(words[q], f);
-    float4 xv = xs4[xsw(c, q)];
-    acc = fmaf(xv.x, f[0], acc);
-    acc = fmaf(xv.y, f[1], acc);
-    acc = fmaf(xv.z, f[2], acc);
-    acc = fmaf(xv.w, f[3], acc);
-  }
-  return acc;
-}
-
-// BF16 [n] -> swizzled FP32 in shared memory (n % 16 == 0).
-__device__ __forceinline__ void stage_bf16_swizzled(float4* xs4, const uint16_t* src, int n) {
-  for (int i = threadIdx.x; i < (n >> 2); i += blockDim.x) {
-    const uint2 raw = *reinterpret_cast<const uint2*>(src + 4 * i);
-    float4 v;
-    v.x = __uint_as_float(raw.x << 16);
-    v.y = __uint_as_float(raw.x & 0xFFFF0000u);
-    v.z = __uint_as_float(raw.y << 16);
-    v.w = __uint_as_float(raw.y & 0xFFFF0000u);
-    xs4[xsw(i >> 2, i & 3)] = v;
-  }
-}
+constexpr int kMaxSlots = 16;
 
 struct DecodeArgs {
   const uint16_t* x;
   int H, I, Is, E, top_k;
-  const uint32_t* ids;
+  const uint32_t* ids;  // bank mode: device expert ids
   const float* scores;
+  // bank mode (PackedFP8ExpertBank layout)
   const uint8_t* gu_w;
   const float* gu_s;
   const uint8_t* d_w;
   const float* d_s;
+  // table mode: per routed slot, the expert's own tensors (Direct experts)
+  bool table;
+  const uint8_t* tg_w[kMaxSlots];
+  const float* tg_s[kMaxSlots];
+  const uint8_t* tu_w[kMaxSlots];
+  const float* tu_s[kMaxSlots];
+  const uint8_t* td_w[kMaxSlots];
+  const float* td_s[kMaxSlots];
+  // shared expert (Is == 0 when absent)
   const uint8_t* sg_w;
   const float* sg_s;
   const uint8_t* su_w;
@@ -67,196 +56,233 @@ struct DecodeArgs {
   const uint8_t* sd_w;
   const float* sd_s;
   float limit;
-  uint16_t* hidden;  // [top_k*I + Is]
-  uint16_t* out;     // [H]
+  uint16_t* hidden;    // [top_k*I + Is]
+  float* partial;      // [(top_k + 1) * H] per-slot down dot products
+  uint32_t* counters;  // [H / 16] completion counters (zero between calls)
+  uint16_t* out;       // [H]
   uint32_t* status;
 };
 
+__host__ __device__ __forceinline__ int align16i(int v) { return (v + 15) & ~15; }
+
+constexpr int kWarpsPerBlock = 4;
+constexpr int kRing = 8;  // 64-wide K slices in flight per warp (1 KB each)
+
 // ---------------------------------------------------------------------------
-// Gate/up/SwiGLU.  Vector path: H % 16 == 0, 16-byte aligned weights.
+// Gate / up / SwiGLU
 // ---------------------------------------------------------------------------
-template <int CPL>  // 16-byte chunks per lane per row: ceil(H / 16 / 32)
-__global__ void __launch_bounds__(256) decode_gate_up_kernel(DecodeArgs a) {
-  extern __shared__ float4 xs4[];
-  stage_bf16_swizzled(xs4, a.x, a.H);
-  __syncthreads();
-  const int lane = threadIdx.x & 31;
-  const int nwarps = gridDim.x * (blockDim.x >> 5);
-  const int nchunks = a.H >> 4;
-  const int cols = (a.H + kBlock - 1) / kBlock;
-  const int half = (a.I + kBlock - 1) / kBlock;
-  const int routed = a.top_k * a.I;
-  const int items = routed + a.Is;
-  for (int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); item < items; item += nwarps) {
-    const uint8_t* gw;
-    const uint8_t* uw;
-    const float* gs;
-    const float* us;
-    if (item < routed) {
-      const int slot = item / a.I, row = item - slot * a.I;
-      const uint32_t e = a.ids[slot];
-      if (e >= (uint32_t)a.E) {
-        if (lane == 0) {
-          atomicOr(a.status, kStatusBadExpert);
-          a.hidden[item] = 0;
-        }
-        continue;
-      }
-      gw = a.gu_w + ((size_t)e * 2 * a.I + row) * a.H;
-      uw = gw + (size_t)a.I * a.H;
-      gs = a.gu_s + ((size_t)e * 2 * half + row / kBlock) * cols;
-      us = gs + (size_t)half * cols;
+
+struct GateUpRows {
+  const uint8_t* g;  // gate row r0
+  const uint8_t* u;  // up row r0
+  const float* sg;   // block-scale row of the gate rows
+  const float* su;
+  int hoff;          // hidden index of row r0
+  bool valid;
+};
+
+__device__ __forceinline__ GateUpRows gate_up_rows(const DecodeArgs& a, int unit) {
+  GateUpRows r;
+  const int per = a.I >> 3;
+  const int routed = a.top_k * per;
+  const int cols = a.H >> 7;
+  if (unit < routed) {
+    const int slot = unit / per, r0 = (unit - slot * per) << 3;
+    r.hoff = slot * a.I + r0;
+    if (a.table) {
+      r.valid = true;
+      r.g = a.tg_w[slot] + (size_t)r0 * a.H;
+      r.u = a.tu_w[slot] + (size_t)r0 * a.H;
+      r.sg = a.tg_s[slot] + (size_t)(r0 >> 7) * cols;
+      r.su = a.tu_s[slot] + (size_t)(r0 >> 7) * cols;
     } else {
-      const int row = item - routed;
-      gw = a.sg_w + (size_t)row * a.H;
-      uw = a.su_w + (size_t)row * a.H;
-      gs = a.sg_s + (size_t)(row / kBlock) * cols;
-      us = a.su_s + (size_t)(row / kBlock) * cols;
+      const int half = a.I >> 7;
+      const uint32_t e = a.ids[slot];
+      r.valid = e < (uint32_t)a.E;
+      const uint32_t es = r.valid ? e : 0u;
+      r.g = a.gu_w + ((size_t)es * 2 * a.I + r0) * a.H;
+      r.u = r.g + (size_t)a.I * a.H;
+      r.sg = a.gu_s + ((size_t)es * 2 * half + (r0 >> 7)) * cols;
+      r.su = r.sg + (size_t)half * cols;
     }
-    const uint4* g4 = reinterpret_cast<const uint4*>(gw);
-    const uint4* u4 = reinterpret_cast<const uint4*>(uw);
-    uint4 gv[CPL], uv[CPL];
-#pragma unroll
-    for (int j = 0; j < CPL; ++j) {
-      const int c = lane + 32 * j;
-      if (c < nchunks) {
-        gv[j] = ldg_stream(g4 + c);
-        uv[j] = ldg_stream(u4 + c);
-      }
-    }
-    float gacc = 0.f, uacc = 0.f;
-#pragma unroll
-    for (int j = 0; j < CPL; ++j) {
-      const int c = lane + 32 * j;
-      if (c < nchunks) {
-        const float gsc = __ldg(gs + (c >> 3)) * 256.0f;
-        const float usc = __ldg(us + (c >> 3)) * 256.0f;
-        gacc = fmaf(gsc, dot16_x(gv[j], xs4, c), gacc);
-        uacc = fmaf(usc, dot16_x(uv[j], xs4, c), uacc);
-      }
-    }
-    gacc = warp_sum(gacc);
-    uacc = warp_sum(uacc);
-    if (lane == 0) a.hidden[item] = swiglu_bf16(gacc, uacc, a.limit);
+  } else {
+    const int r0 = (unit - routed) << 3;
+    r.valid = true;
+    r.hoff = a.top_k * a.I + r0;
+    r.g = a.sg_w + (size_t)r0 * a.H;
+    r.u = a.su_w + (size_t)r0 * a.H;
+    r.sg = a.sg_s + (size_t)(r0 >> 7) * cols;
+    r.su = a.su_s + (size_t)(r0 >> 7) * cols;
   }
+  return r;
+}
+
+template <bool FINITE>
+__global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_gate_up_v4(DecodeArgs a) {
+  constexpr int P = kRing;
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+  uint4* ring = reinterpret_cast<uint4*>(smem) + (size_t)warp * P * 64;
+  __half* xs = reinterpret_cast<__half*>(reinterpret_cast<uint4*>(smem) + (size_t)kWarpsPerBlock * P * 64);
+  float* scratch = reinterpret_cast<float*>(xs + align16i(a.H + 8));
+  const int nunits = a.top_k * (a.I >> 3) + (a.Is >> 3);
+  const int unit = blockIdx.x * kWarpsPerBlock + warp;
+  const bool active = unit < nunits;
+  GateUpRows rw{};
+  if (active) rw = gate_up_rows(a, unit);
+  const bool ld = active && rw.valid;
+  const uint8_t* pg = ld ? rw.g + (size_t)g * a.H + 16 * q : nullptr;
+  const uint8_t* pu = ld ? rw.u + (size_t)g * a.H + 16 * q : nullptr;
+  const int nslice = a.H >> 6;
+  auto issue = [&](int sl) {
+    uint4* d = ring + (sl % P) * 64 + lane;
+    cp_async_16(d, ld ? (const void*)(pg + 64 * sl) : (const void*)a.x, ld);
+    cp_async_16(d + 32, ld ? (const void*)(pu + 64 * sl) : (const void*)a.x, ld);
+  };
+#pragma unroll
+  for (int s = 0; s < P - 1; ++s) {
+    if (s < nslice) issue(s);
+    cp_async_commit_group();
+  }
+  const float smul = decode_unscale<FINITE>() * stage_f16(xs, a.H + 8, a.x, 0, 1, a.H, scratch);
+  float part[4] = {0.f, 0.f, 0.f, 0.f}, tot[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int sl = 0; sl < nslice; ++sl) {
+    if (sl + P - 1 < nslice) issue(sl + P - 1);
+    cp_async_commit_group();
+    cp_async_wait_group<P - 1>();
+    const uint4* src = ring + (sl % P) * 64 + lane;
+    const uint4 fg = src[0], fu = src[32];
+    uint32_t xw[8];
+    load_x_frag(xw, xs + 64 * sl + 16 * q, g == 0);
+    mma_slice<FINITE>(part, fg, fu, xw);
+    if ((sl & 1) && ld) promote2(tot, part, __ldg(rw.sg + (sl >> 1)) * smul, __ldg(rw.su + (sl >> 1)) * smul);
+  }
+  cp_async_wait_group<0>();
+  if (active && q == 0) a.hidden[rw.hoff + g] = rw.valid ? swiglu_bf16(tot[0], tot[2], a.limit) : (uint16_t)0;
+  if (active && !rw.valid && lane == 0) atomicOr(a.status, kStatusBadExpert);
 }
 
 // ---------------------------------------------------------------------------
-// Down + weighted reduction + shared add.  Block = NS warps (one per slot,
-// the shared expert last), RB output rows per block iteration.
+// Down + slot-ordered reduce + shared add
 // ---------------------------------------------------------------------------
-constexpr int kDownRB = 4;
-constexpr int kDownMaxSlots = 9;  // 8 routed + shared on the vector path
 
-template <int CPL>  // chunks per lane per row: ceil(I / 16 / 32)
-__global__ void __launch_bounds__(32 * kDownMaxSlots) decode_down_kernel(DecodeArgs a) {
-  extern __shared__ float4 smem4[];
+template <bool FINITE>
+__global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_down_v4(DecodeArgs a) {
+  constexpr int P = kRing;
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
   const int ns = a.top_k + (a.Is > 0 ? 1 : 0);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // per-slot activations: routed slots stride I, the shared slot stride Is
-  float4* xs4 = smem4 + (size_t)warp * (max(a.I, a.Is) >> 2);
-  float* dots = reinterpret_cast<float*>(smem4 + (size_t)ns * (max(a.I, a.Is) >> 2));  // [RB][ns]
-  const bool shared_slot = (warp == a.top_k);
-  const int kin = shared_slot ? a.Is : a.I;
-  if (warp < ns) {
-    const uint16_t* src = a.hidden + (shared_slot ? (size_t)a.top_k * a.I : (size_t)warp * a.I);
-    for (int i = lane; i < (kin >> 2); i += 32) {
-      const uint2 raw = *reinterpret_cast<const uint2*>(src + 4 * i);
-      float4 v;
-      v.x = __uint_as_float(raw.x << 16);
-      v.y = __uint_as_float(raw.x & 0xFFFF0000u);
-      v.z = __uint_as_float(raw.y << 16);
-      v.w = __uint_as_float(raw.y & 0xFFFF0000u);
-      xs4[xsw(i >> 2, i & 3)] = v;
+  const int K = a.I;  // I_shared == I on this path
+  uint4* ring = reinterpret_cast<uint4*>(smem) + (size_t)warp * P * 64;
+  __half* xs = reinterpret_cast<__half*>(reinterpret_cast<uint4*>(smem) + (size_t)kWarpsPerBlock * P * 64);
+  float* scratch = reinterpret_cast<float*>(xs + align16i(K + 8));
+  const int rtiles = a.H >> 4;
+  const int nunits = ns * rtiles;
+  const int unit = blockIdx.x * kWarpsPerBlock + warp;
+  const bool active = unit < nunits;
+  const int j = active ? unit / rtiles : 0;
+  const int tile = unit - j * rtiles;
+  const int row0 = tile << 4;
+  const int cols = K >> 7;
+  bool valid = active;
+  const uint8_t* w0 = nullptr;
+  const float* srow = nullptr;
+  if (active) {
+    if (j == a.top_k) {
+      w0 = a.sd_w + (size_t)row0 * K;
+      srow = a.sd_s + (size_t)(row0 >> 7) * cols;
+    } else if (a.table) {
+      w0 = a.td_w[j] + (size_t)row0 * K;
+      srow = a.td_s[j] + (size_t)(row0 >> 7) * cols;
+    } else {
+      const uint32_t e = a.ids[j];
+      valid = e < (uint32_t)a.E;
+      const uint32_t es = valid ? e : 0u;
+      w0 = a.d_w + ((size_t)es * a.H + row0) * K;
+      srow = a.d_s + ((size_t)es * (a.H >> 7) + (row0 >> 7)) * cols;
     }
   }
-  __syncthreads();
-  uint32_t e = 0;
-  bool valid = warp < ns;
-  if (valid && !shared_slot) {
-    e = a.ids[warp];
-    if (e >= (uint32_t)a.E) {
-      valid = false;
-      if (lane == 0 && blockIdx.x == 0) atomicOr(a.status, kStatusBadExpert);
-    }
+  const bool ld = active && valid;
+  const uint8_t* p0 = ld ? w0 + (size_t)g * K + 16 * q : nullptr;
+  const uint8_t* p8 = ld ? w0 + (size_t)(g + 8) * K + 16 * q : nullptr;
+  const int nslice = K >> 6;
+  auto issue = [&](int sl) {
+    uint4* d = ring + (sl % P) * 64 + lane;
+    cp_async_16(d, ld ? (const void*)(p0 + 64 * sl) : (const void*)a.x, ld);
+    cp_async_16(d + 32, ld ? (const void*)(p8 + 64 * sl) : (const void*)a.x, ld);
+  };
+#pragma unroll
+  for (int s = 0; s < P - 1; ++s) {
+    if (s < nslice) issue(s);
+    cp_async_commit_group();
   }
-  const int nchunks = kin >> 4;
-  const int cols = (kin + kBlock - 1) / kBlock;
-  const int hrows = (a.H + kBlock - 1) / kBlock;
-  const uint8_t* wbase = shared_slot ? a.sd_w : a.d_w + (size_t)e * a.H * a.I;
-  const float* sbase = shared_slot ? a.sd_s : a.d_s + (size_t)e * hrows * cols;
-  for (int h0 = blockIdx.x * kDownRB; h0 < a.H; h0 += gridDim.x * kDownRB) {
-    if (warp < ns) {
-      float acc[kDownRB];
-      if (valid) {
-        uint4 wv[kDownRB][CPL];
-#pragma unroll
-        for (int r = 0; r < kDownRB; ++r) {
-          const uint4* w4 = reinterpret_cast<const uint4*>(wbase + (size_t)(h0 + r) * kin);
-#pragma unroll
-          for (int j = 0; j < CPL; ++j) {
-            const int c = lane + 32 * j;
-            if (c < nchunks && h0 + r < a.H) wv[r][j] = ldg_stream(w4 + c);
-          }
-        }
-#pragma unroll
-        for (int r = 0; r < kDownRB; ++r) {
-          const float* srow = sbase + (size_t)((h0 + r) / kBlock) * cols;
-          float v = 0.f;
-#pragma unroll
-          for (int j = 0; j < CPL; ++j) {
-            const int c = lane + 32 * j;
-            if (c < nchunks && h0 + r < a.H)
-              v = fmaf(__ldg(srow + (c >> 3)) * 256.0f, dot16_x(wv[r][j], xs4, c), v);
-          }
-          acc[r] = warp_sum(v);
-        }
-      } else {
-#pragma unroll
-        for (int r = 0; r < kDownRB; ++r) acc[r] = 0.f;
-      }
-      if (lane == 0) {
-#pragma unroll
-        for (int r = 0; r < kDownRB; ++r) dots[r * ns + warp] = acc[r];
-      }
-    }
-    __syncthreads();
-    if (threadIdx.x < kDownRB && h0 + (int)threadIdx.x < a.H) {
-      const int r = threadIdx.x;
-      float total = 0.f;
-      for (int j = 0; j < a.top_k; ++j) {
-        // K6 stores BF16, K8 multiplies f32(down) by the FP32 route weight
-        const float d = bf16_round(dots[r * ns + j]);
-        total = total + __fmul_rn(d, a.scores[j]);
-      }
-      float res = bf16_round(total);
-      if (a.Is > 0) res = res + bf16_round(dots[r * ns + a.top_k]);
-      a.out[h0 + r] = f32_to_bf16_bits(res);
-    }
-    __syncthreads();
+  // every unit of a block has the same slot (H/16 is a multiple of 4 here)
+  const int jb = min((int)(blockIdx.x * kWarpsPerBlock) / rtiles, ns - 1);
+  const float smul =
+      decode_unscale<FINITE>() * stage_f16(xs, K + 8, a.hidden + (size_t)jb * a.I, 0, 1, K, scratch);
+  float part[4] = {0.f, 0.f, 0.f, 0.f}, tot[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int sl = 0; sl < nslice; ++sl) {
+    if (sl + P - 1 < nslice) issue(sl + P - 1);
+    cp_async_commit_group();
+    cp_async_wait_group<P - 1>();
+    const uint4* src = ring + (sl % P) * 64 + lane;
+    const uint4 f0 = src[0], f8 = src[32];
+    uint32_t xw[8];
+    load_x_frag(xw, xs + 64 * sl + 16 * q, g == 0);
+    mma_slice<FINITE>(part, f0, f8, xw);
+    if ((sl & 1) && ld) promote(tot, part, __ldg(srow + (sl >> 1)) * smul);
   }
+  cp_async_wait_group<0>();
+  if (!active) return;
+  if (q == 0) {
+    a.partial[(size_t)j * a.H + row0 + g] = valid ? tot[0] : 0.f;
+    a.partial[(size_t)j * a.H + row0 + g + 8] = valid ? tot[2] : 0.f;
+  }
+  if (!valid && lane == 0) atomicOr(a.status, kStatusBadExpert);
+  __syncwarp();
+  __threadfence();
+  unsigned last = 0;
+  if (lane == 0) last = atomicAdd(&a.counters[tile], 1u) == (unsigned)(ns - 1);
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (!last) return;
+  __threadfence();
+  if (lane < 16) {
+    const int h = row0 + lane;
+    float total = 0.f;
+    for (int s2 = 0; s2 < a.top_k; ++s2) {
+      // K6 stores each slot's dot product as BF16; K8 weights it in FP32
+      const float d = bf16_round(__ldcg(a.partial + (size_t)s2 * a.H + h));
+      total = total + __fmul_rn(d, a.scores[s2]);
+    }
+    float res = bf16_round(total);
+    if (a.Is > 0) res = res + bf16_round(__ldcg(a.partial + (size_t)a.top_k * a.H + h));
+    a.out[h] = f32_to_bf16_bits(res);
+  }
+  if (lane == 0) a.counters[tile] = 0u;  // leave the workspace reusable
 }
 
 // ---------------------------------------------------------------------------
 // Generic (unaligned) path: one warp per dot product, scalar loads.
 // ---------------------------------------------------------------------------
-__global__ void decode_gate_up_scalar_kernel(DecodeArgs a) {
-  const int lane = threadIdx.x & 31;
-  const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+
+__device__ __forceinline__ void scalar_rows(const DecodeArgs& a, int item, const uint8_t*& gw, const uint8_t*& uw,
+                                            const float*& gs, const float*& us, bool& valid) {
   const int routed = a.top_k * a.I;
-  if (item >= routed + a.Is) return;
   const int cols = (a.H + kBlock - 1) / kBlock;
   const int half = (a.I + kBlock - 1) / kBlock;
-  const uint8_t *gw, *uw;
-  const float *gs, *us;
+  valid = true;
   if (item < routed) {
     const int slot = item / a.I, row = item % a.I;
+    if (a.table) {
+      gw = a.tg_w[slot] + (size_t)row * a.H;
+      uw = a.tu_w[slot] + (size_t)row * a.H;
+      gs = a.tg_s[slot] + (size_t)(row / kBlock) * cols;
+      us = a.tu_s[slot] + (size_t)(row / kBlock) * cols;
+      return;
+    }
     const uint32_t e = a.ids[slot];
     if (e >= (uint32_t)a.E) {
-      if (lane == 0) {
-        atomicOr(a.status, kStatusBadExpert);
-        a.hidden[item] = 0;
-      }
+      valid = false;
       return;
     }
     gw = a.gu_w + ((size_t)e * 2 * a.I + row) * a.H;
@@ -269,6 +295,23 @@ __global__ void decode_gate_up_scalar_kernel(DecodeArgs a) {
     uw = a.su_w + (size_t)row * a.H;
     gs = a.sg_s + (size_t)(row / kBlock) * cols;
     us = a.su_s + (size_t)(row / kBlock) * cols;
+  }
+}
+
+__global__ void decode_gate_up_scalar_kernel(DecodeArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (item >= a.top_k * a.I + a.Is) return;
+  const uint8_t *gw = nullptr, *uw = nullptr;
+  const float *gs = nullptr, *us = nullptr;
+  bool valid;
+  scalar_rows(a, item, gw, uw, gs, us, valid);
+  if (!valid) {
+    if (lane == 0) {
+      atomicOr(a.status, kStatusBadExpert);
+      a.hidden[item] = 0;
+    }
+    return;
   }
   float g = 0.f, u = 0.f;
   for (int k = lane; k < a.H; k += 32) {
@@ -285,27 +328,36 @@ __global__ void decode_down_scalar_kernel(DecodeArgs a) {
   const int lane = threadIdx.x & 31;
   const int h = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (h >= a.H) return;
+  const int cols = (a.I + kBlock - 1) / kBlock;
+  const int hrows = (a.H + kBlock - 1) / kBlock;
   float total = 0.f;
   for (int j = 0; j < a.top_k; ++j) {
-    const uint32_t e = a.ids[j];
-    float v = 0.f;
-    if (e < (uint32_t)a.E) {
-      const int cols = (a.I + kBlock - 1) / kBlock;
-      const int hrows = (a.H + kBlock - 1) / kBlock;
-      const uint8_t* wr = a.d_w + ((size_t)e * a.H + h) * a.I;
-      const float* sr = a.d_s + ((size_t)e * hrows + h / kBlock) * cols;
-      const uint16_t* xr = a.hidden + (size_t)j * a.I;
-      for (int k = lane; k < a.I; k += 32)
-        v = fmaf(bf16_bits_to_f32(xr[k]) * e4m3_to_f32_scaled(wr[k]), sr[k / kBlock] * 256.0f, v);
-      v = warp_sum(v);
+    const uint8_t* wr;
+    const float* sr;
+    if (a.table) {
+      wr = a.td_w[j] + (size_t)h * a.I;
+      sr = a.td_s[j] + (size_t)(h / kBlock) * cols;
+    } else {
+      const uint32_t e = a.ids[j];
+      if (e >= (uint32_t)a.E) {
+        if (lane == 0) atomicOr(a.status, kStatusBadExpert);
+        continue;
+      }
+      wr = a.d_w + ((size_t)e * a.H + h) * a.I;
+      sr = a.d_s + ((size_t)e * hrows + h / kBlock) * cols;
     }
+    const uint16_t* xr = a.hidden + (size_t)j * a.I;
+    float v = 0.f;
+    for (int k = lane; k < a.I; k += 32)
+      v = fmaf(bf16_bits_to_f32(xr[k]) * e4m3_to_f32_scaled(wr[k]), sr[k / kBlock] * 256.0f, v);
+    v = warp_sum(v);
     total = total + __fmul_rn(bf16_round(v), a.scores[j]);
   }
   float res = bf16_round(total);
   if (a.Is > 0) {
-    const int cols = (a.Is + kBlock - 1) / kBlock;
+    const int scols = (a.Is + kBlock - 1) / kBlock;
     const uint8_t* wr = a.sd_w + (size_t)h * a.Is;
-    const float* sr = a.sd_s + (size_t)(h / kBlock) * cols;
+    const float* sr = a.sd_s + (size_t)(h / kBlock) * scols;
     const uint16_t* xr = a.hidden + (size_t)a.top_k * a.I;
     float v = 0.f;
     for (int k = lane; k < a.Is; k += 32)
@@ -316,42 +368,52 @@ __global__ void decode_down_scalar_kernel(DecodeArgs a) {
   if (lane == 0) a.out[h] = f32_to_bf16_bits(res);
 }
 
-template <int CPL>
-static int launch_gate_up(const DecodeArgs& a, cudaStream_t st) {
-  const size_t smem = (size_t)a.H * sizeof(float);
-  if (smem > 48 * 1024) {
-    int rc_attr = ensure_max_smem((const void*)decode_gate_up_kernel<CPL>, smem);
-    if (rc_attr) return rc_attr;
-  }
-  const int items = a.top_k * a.I + a.Is;
-  const int blocks = std::min((items + 7) / 8, sm_count() * 4);
-  decode_gate_up_kernel<CPL><<<blocks, 256, smem, st>>>(a);
-  return check_launch("decode_gate_up_kernel");
-}
+// ---------------------------------------------------------------------------
+// Launch
+// ---------------------------------------------------------------------------
 
-template <int CPL>
-static int launch_down(const DecodeArgs& a, cudaStream_t st) {
-  const int ns = a.top_k + (a.Is > 0 ? 1 : 0);
-  const size_t smem = (size_t)ns * std::max(a.I, a.Is) * sizeof(float) + (size_t)kDownRB * ns * sizeof(float);
-  if (smem > 48 * 1024) {
-    int rc_attr = ensure_max_smem((const void*)decode_down_kernel<CPL>, smem);
-    if (rc_attr) return rc_attr;
-  }
-  const int row_blocks = (a.H + kDownRB - 1) / kDownRB;
-  const int per_sm = std::max(1, std::min(4, (int)(200 * 1024 / smem)));
-  const int blocks = std::min(row_blocks, sm_count() * per_sm);
-  decode_down_kernel<CPL><<<blocks, 32 * ns, smem, st>>>(a);
-  return check_launch("decode_down_kernel");
-}
-
-int packed_decode(const DecodeArgs& a, cudaStream_t st, bool gate_up_only) {
+static bool tensor_core_shape(const DecodeArgs& a) {
   const bool has_shared = a.Is > 0;
-  const bool aligned =
-      a.H % 16 == 0 && a.I % 16 == 0 && (!has_shared || a.Is % 16 == 0) &&
-      ((uintptr_t)a.gu_w & 15) == 0 && ((uintptr_t)a.d_w & 15) == 0 && ((uintptr_t)a.x & 7) == 0 &&
-      (!has_shared || ((((uintptr_t)a.sg_w | (uintptr_t)a.su_w | (uintptr_t)a.sd_w) & 15) == 0)) &&
-      a.H <= 8192 && std::max(a.I, a.Is) <= 2048 && a.top_k + (has_shared ? 1 : 0) <= kDownMaxSlots;
-  if (!aligned) {
+  bool aligned = (((uintptr_t)a.x | (uintptr_t)a.hidden) & 15) == 0;
+  if (a.table) {
+    for (int j = 0; j < a.top_k; ++j)
+      aligned = aligned && ((((uintptr_t)a.tg_w[j] | (uintptr_t)a.tu_w[j] | (uintptr_t)a.td_w[j]) & 15) == 0);
+  } else {
+    aligned = aligned && ((((uintptr_t)a.gu_w | (uintptr_t)a.d_w) & 15) == 0);
+  }
+  if (has_shared) aligned = aligned && ((((uintptr_t)a.sg_w | (uintptr_t)a.su_w | (uintptr_t)a.sd_w) & 15) == 0);
+  // H % 64 keeps every 4-warp block of the down kernel inside one slot
+  return aligned && a.H % 128 == 0 && a.I % 128 == 0 && (!has_shared || a.Is == a.I) && a.H <= 32768 &&
+         a.I <= 32768;
+}
+
+template <bool FINITE>
+static int launch_v4(const DecodeArgs& a, cudaStream_t st, bool gate_up_only) {
+  const size_t ring = (size_t)kWarpsPerBlock * kRing * 64 * 16;
+  {
+    const size_t smem = ring + (size_t)align16i(a.H + 8) * 2 + 32 * sizeof(float);
+    if (smem > 48 * 1024) {
+      int rc = ensure_max_smem((const void*)decode_gate_up_v4<FINITE>, smem);
+      if (rc) return rc;
+    }
+    const int units = a.top_k * (a.I >> 3) + (a.Is >> 3);
+    decode_gate_up_v4<FINITE><<<(units + kWarpsPerBlock - 1) / kWarpsPerBlock, 32 * kWarpsPerBlock, smem, st>>>(a);
+    int rc = check_launch("decode_gate_up_v4");
+    if (rc || gate_up_only) return rc;
+  }
+  const size_t smem = ring + (size_t)align16i(a.I + 8) * 2 + 32 * sizeof(float);
+  if (smem > 48 * 1024) {
+    int rc = ensure_max_smem((const void*)decode_down_v4<FINITE>, smem);
+    if (rc) return rc;
+  }
+  const int ns = a.top_k + (a.Is > 0 ? 1 : 0);
+  const int units = ns * (a.H >> 4);
+  decode_down_v4<FINITE><<<(units + kWarpsPerBlock - 1) / kWarpsPerBlock, 32 * kWarpsPerBlock, smem, st>>>(a);
+  return check_launch("decode_down_v4");
+}
+
+int packed_decode(const DecodeArgs& a, cudaStream_t st, bool gate_up_only, uint32_t flags) {
+  if (!tensor_core_shape(a)) {
     const int items = a.top_k * a.I + a.Is;
     decode_gate_up_scalar_kernel<<<(items + 7) / 8, 256, 0, st>>>(a);
     int rc = check_launch("decode_gate_up_scalar_kernel");
@@ -359,74 +421,134 @@ int packed_decode(const DecodeArgs& a, cudaStream_t st, bool gate_up_only) {
     decode_down_scalar_kernel<<<(a.H + 7) / 8, 256, 0, st>>>(a);
     return check_launch("decode_down_scalar_kernel");
   }
-  const int cpl_h = (a.H / 16 + 31) / 32;
-  int rc;
-  if (cpl_h <= 4) rc = launch_gate_up<4>(a, st);
-  else if (cpl_h <= 8) rc = launch_gate_up<8>(a, st);
-  else rc = launch_gate_up<16>(a, st);
-  if (rc || gate_up_only) return rc;
-  const int cpl_i = (std::max(a.I, a.Is) / 16 + 31) / 32;
-  if (cpl_i <= 1) return launch_down<1>(a, st);
-  if (cpl_i <= 2) return launch_down<2>(a, st);
-  if (cpl_i <= 3) return launch_down<3>(a, st);
-  return launch_down<4>(a, st);
+  if (flags & GLM53_FLAG_E4M3_FINITE) return launch_v4<true>(a, st, gate_up_only);
+  return launch_v4<false>(a, st, gate_up_only);
+}
+
+// Workspace: BF16 hidden rows | FP32 per-slot down dot products | counters.
+struct DecodeWorkspace {
+  size_t hidden, partial, counters, bytes;
+};
+
+static DecodeWorkspace decode_workspace(int top_k, int64_t H, int64_t I, int64_t I_shared) {
+  DecodeWorkspace w;
+  w.hidden = 0;
+  w.partial = align_up(((size_t)top_k * I + (size_t)I_shared) * sizeof(uint16_t), 256);
+  w.counters = w.partial + align_up((size_t)(top_k + 1) * H * sizeof(float), 256);
+  w.bytes = w.counters + align_up((size_t)((H + 15) / 16) * sizeof(uint32_t), 256);
+  return w;
+}
+
+static int check_geometry(const char* fn, int64_t H, int64_t I, int top_k, int64_t I_shared) {
+  if (H <= 0 || I <= 0 || top_k <= 0 || top_k > kMaxSlots || I_shared < 0 || H > INT32_MAX / 2 ||
+      I > INT32_MAX / 64 || I_shared > INT32_MAX / 64) {
+    set_last_error("%s: invalid geometry H=%lld I=%lld top_k=%d I_shared=%lld", fn, (long long)H, (long long)I,
+                   top_k, (long long)I_shared);
+    return GLM53_ERR_INVALID;
+  }
+  return GLM53_OK;
+}
+
+static void fill_common(DecodeArgs& a, const void* x, int64_t H, const float* scores, int top_k, int64_t I,
+                        const uint8_t* sg_w, const float* sg_s, const uint8_t* su_w, const float* su_s,
+                        const uint8_t* sd_w, const float* sd_s, int64_t Is, float limit, void* out, void* workspace,
+                        uint32_t* status) {
+  a.x = (const uint16_t*)x;
+  a.H = (int)H;
+  a.I = (int)I;
+  a.Is = (int)Is;
+  a.top_k = top_k;
+  a.scores = scores;
+  a.sg_w = sg_w;
+  a.sg_s = sg_s;
+  a.su_w = su_w;
+  a.su_s = su_s;
+  a.sd_w = sd_w;
+  a.sd_s = sd_s;
+  a.limit = limit;
+  const DecodeWorkspace wl = decode_workspace(top_k, H, I, Is);
+  a.hidden = (uint16_t*)((char*)workspace + wl.hidden);
+  a.partial = (float*)((char*)workspace + wl.partial);
+  a.counters = (uint32_t*)((char*)workspace + wl.counters);
+  a.out = (uint16_t*)out;
+  a.status = status;
 }
 
 }  // namespace glm53
 
 using namespace glm53;
 
-extern "C" size_t glm53_packed_decode_workspace_bytes(int top_k, int64_t I, int64_t I_shared) {
-  return align_up(((size_t)top_k * I + (size_t)I_shared) * sizeof(uint16_t), 256);
+extern "C" size_t glm53_packed_decode_workspace_bytes(int top_k, int64_t H, int64_t I, int64_t I_shared) {
+  return decode_workspace(top_k, H, I, I_shared).bytes;
 }
 
-extern "C" int glm53_packed_decode_moe(const void* x, int64_t H, const uint32_t* expert_ids,
-                                       const float* scores, int top_k, const uint8_t* gate_up_w,
-                                       const float* gate_up_s, const uint8_t* down_w, const float* down_s,
-                                       int64_t E, int64_t I, const uint8_t* shared_gate_w,
-                                       const float* shared_gate_s, const uint8_t* shared_up_w,
-                                       const float* shared_up_s, const uint8_t* shared_down_w,
-                                       const float* shared_down_s, int64_t I_shared, float limit, void* out,
-                                       void* workspace, size_t workspace_bytes, uint32_t* status,
-                                       void* stream) {
-  if (H <= 0 || I <= 0 || E <= 0 || top_k <= 0 || top_k > 16 || I_shared < 0 || H > INT32_MAX / 2 ||
-      I > INT32_MAX / 64) {
-    set_last_error("glm53_packed_decode_moe: invalid geometry H=%lld I=%lld E=%lld top_k=%d", (long long)H,
-                   (long long)I, (long long)E, top_k);
-    return GLM53_ERR_INVALID;
-  }
+extern "C" int glm53_packed_decode_moe(const void* x, int64_t H, const uint32_t* expert_ids, const float* scores,
+                                       int top_k, const uint8_t* gate_up_w, const float* gate_up_s,
+                                       const uint8_t* down_w, const float* down_s, int64_t E, int64_t I,
+                                       const uint8_t* shared_gate_w, const float* shared_gate_s,
+                                       const uint8_t* shared_up_w, const float* shared_up_s,
+                                       const uint8_t* shared_down_w, const float* shared_down_s, int64_t I_shared,
+                                       float limit, void* out, void* workspace, size_t workspace_bytes,
+                                       uint32_t* status, uint32_t flags, void* stream) {
+  int rc = check_geometry("glm53_packed_decode_moe", H, I, top_k, I_shared);
+  if (rc) return rc;
   const bool has_shared = I_shared > 0;
-  if (!x || !expert_ids || !scores || !gate_up_w || !gate_up_s || !down_w || !down_s || !out || !status ||
-      !workspace || workspace_bytes < glm53_packed_decode_workspace_bytes(top_k, I, I_shared) ||
+  if (E <= 0 || !x || !expert_ids || !scores || !gate_up_w || !gate_up_s || !down_w || !down_s || !out || !status ||
+      !workspace || workspace_bytes < glm53_packed_decode_workspace_bytes(top_k, H, I, I_shared) ||
       (has_shared && (!shared_gate_w || !shared_gate_s || !shared_up_w || !shared_up_s || !shared_down_w ||
                       !shared_down_s))) {
-    set_last_error("glm53_packed_decode_moe: missing pointer or workspace too small");
+    set_last_error("glm53_packed_decode_moe: missing pointer, E <= 0 or workspace too small");
     return GLM53_ERR_INVALID;
   }
-  DecodeArgs a;
-  a.x = (const uint16_t*)x;
-  a.H = (int)H;
-  a.I = (int)I;
-  a.Is = (int)I_shared;
+  DecodeArgs a{};
+  fill_common(a, x, H, scores, top_k, I, shared_gate_w, shared_gate_s, shared_up_w, shared_up_s, shared_down_w,
+              shared_down_s, I_shared, limit, out, workspace, status);
   a.E = (int)std::min<int64_t>(E, INT32_MAX);
-  a.top_k = top_k;
   a.ids = expert_ids;
-  a.scores = scores;
   a.gu_w = gate_up_w;
   a.gu_s = gate_up_s;
   a.d_w = down_w;
   a.d_s = down_s;
-  a.sg_w = shared_gate_w;
-  a.sg_s = shared_gate_s;
-  a.su_w = shared_up_w;
-  a.su_s = shared_up_s;
-  a.sd_w = shared_down_w;
-  a.sd_s = shared_down_s;
-  a.limit = limit;
-  a.hidden = (uint16_t*)workspace;
-  a.out = (uint16_t*)out;
-  a.status = status;
-  return packed_decode(a, (cudaStream_t)stream, false);
+  return packed_decode(a, (cudaStream_t)stream, false, flags);
+}
+
+extern "C" int glm53_selected_decode_moe(const void* x, int64_t H, const float* scores, int top_k,
+                                         const uint8_t* const* gate_w, const float* const* gate_s,
+                                         const uint8_t* const* up_w, const float* const* up_s,
+                                         const uint8_t* const* down_w, const float* const* down_s, int64_t I,
+                                         const uint8_t* shared_gate_w, const float* shared_gate_s,
+                                         const uint8_t* shared_up_w, const float* shared_up_s,
+                                         const uint8_t* shared_down_w, const float* shared_down_s,
+                                         int64_t I_shared, float limit, void* out, void* workspace,
+                                         size_t workspace_bytes, uint32_t* status, uint32_t flags, void* stream) {
+  int rc = check_geometry("glm53_selected_decode_moe", H, I, top_k, I_shared);
+  if (rc) return rc;
+  const bool has_shared = I_shared > 0;
+  if (!x || !scores || !gate_w || !gate_s || !up_w || !up_s || !down_w || !down_s || !out || !status ||
+      !workspace || workspace_bytes < glm53_packed_decode_workspace_bytes(top_k, H, I, I_shared) ||
+      (has_shared && (!shared_gate_w || !shared_gate_s || !shared_up_w || !shared_up_s || !shared_down_w ||
+                      !shared_down_s))) {
+    set_last_error("glm53_selected_decode_moe: missing pointer or workspace too small");
+    return GLM53_ERR_INVALID;
+  }
+  DecodeArgs a{};
+  fill_common(a, x, H, scores, top_k, I, shared_gate_w, shared_gate_s, shared_up_w, shared_up_s, shared_down_w,
+              shared_down_s, I_shared, limit, out, workspace, status);
+  a.E = top_k;
+  a.table = true;
+  for (int j = 0; j < top_k; ++j) {
+    if (!gate_w[j] || !gate_s[j] || !up_w[j] || !up_s[j] || !down_w[j] || !down_s[j]) {
+      set_last_error("glm53_selected_decode_moe: missing expert pointer for slot %d", j);
+      return GLM53_ERR_INVALID;
+    }
+    a.tg_w[j] = gate_w[j];
+    a.tg_s[j] = gate_s[j];
+    a.tu_w[j] = up_w[j];
+    a.tu_s[j] = up_s[j];
+    a.td_w[j] = down_w[j];
+    a.td_s[j] = down_s[j];
+  }
+  return packed_decode(a, (cudaStream_t)stream, false, flags);
 }
 
 extern "C" int glm53_packed_decode_gate_up(const void* x, int64_t H, const uint32_t* expert_ids, int top_k,
@@ -434,39 +556,63 @@ extern "C" int glm53_packed_decode_gate_up(const void* x, int64_t H, const uint3
                                            const uint8_t* shared_gate_w, const float* shared_gate_s,
                                            const uint8_t* shared_up_w, const float* shared_up_s, int64_t I_shared,
                                            float limit, void* workspace, size_t workspace_bytes, uint32_t* status,
-                                           void* stream) {
-  if (H <= 0 || I <= 0 || E <= 0 || top_k <= 0 || top_k > 16 || I_shared < 0 || H > INT32_MAX / 2 ||
-      I > INT32_MAX / 64) {
-    set_last_error("glm53_packed_decode_gate_up: invalid geometry");
-    return GLM53_ERR_INVALID;
-  }
+                                           uint32_t flags, void* stream) {
+  int rc = check_geometry("glm53_packed_decode_gate_up", H, I, top_k, I_shared);
+  if (rc) return rc;
   const bool has_shared = I_shared > 0;
-  if (!x || !expert_ids || !gate_up_w || !gate_up_s || !status || !workspace ||
-      workspace_bytes < glm53_packed_decode_workspace_bytes(top_k, I, I_shared) ||
+  if (E <= 0 || !x || !expert_ids || !gate_up_w || !gate_up_s || !status || !workspace ||
+      workspace_bytes < glm53_packed_decode_workspace_bytes(top_k, H, I, I_shared) ||
       (has_shared && (!shared_gate_w || !shared_gate_s || !shared_up_w || !shared_up_s))) {
-    set_last_error("glm53_packed_decode_gate_up: missing pointer or workspace too small");
+    set_last_error("glm53_packed_decode_gate_up: missing pointer, E <= 0 or workspace too small");
     return GLM53_ERR_INVALID;
   }
   DecodeArgs a{};
-  a.x = (const uint16_t*)x;
-  a.H = (int)H;
-  a.I = (int)I;
-  a.Is = (int)I_shared;
+  // the down stage's pointers are unused by this stage; the shape check sees
+  // the gate/up pointers in their place
+  fill_common(a, x, H, nullptr, top_k, I, shared_gate_w, shared_gate_s, shared_up_w, shared_up_s,
+              has_shared ? shared_gate_w : nullptr, shared_gate_s, I_shared, limit, nullptr, workspace, status);
   a.E = (int)std::min<int64_t>(E, INT32_MAX);
-  a.top_k = top_k;
   a.ids = expert_ids;
   a.gu_w = gate_up_w;
   a.gu_s = gate_up_s;
-  a.sg_w = shared_gate_w;
-  a.sg_s = shared_gate_s;
-  a.su_w = shared_up_w;
-  a.su_s = shared_up_s;
-  a.limit = limit;
-  a.hidden = (uint16_t*)workspace;
-  a.status = status;
-  // the down-stage pointers are not used by this stage; keep the alignment
-  // test of packed_decode() satisfied with the gate/up bank pointer
   a.d_w = gate_up_w;
-  a.sd_w = has_shared ? shared_gate_w : nullptr;
-  return packed_decode(a, (cudaStream_t)stream, true);
+  return packed_decode(a, (cudaStream_t)stream, true, flags);
+}
+
+// ---------------------------------------------------------------------------
+// Bind-time E4M3 scan
+// ---------------------------------------------------------------------------
+
+namespace glm53 {
+__global__ void e4m3_nan_scan_kernel(const uint8_t* __restrict__ w, int64_t n, uint32_t* __restrict__ count) {
+  uint32_t c = 0;
+  const int64_t n16 = n >> 4;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += stride) {
+    const uint4 v = reinterpret_cast<const uint4*>(w)[i];
+    const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      // a code whose low 7 bits are all ones becomes 0xFF after | 0x80, i.e. a
+      // zero byte of z; the classic zero-byte test then flags it
+      const uint32_t z = ~(words[t] | 0x80808080u);
+      c += ((z - 0x01010101u) & ~z & 0x80808080u) ? 1u : 0u;
+    }
+  }
+  for (int64_t i = (n16 << 4) + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+    c += ((w[i] & 0x7Fu) == 0x7Fu) ? 1u : 0u;
+  c = __reduce_add_sync(0xffffffffu, c);
+  if ((threadIdx.x & 31) == 0 && c) atomicAdd(count, c);
+}
+}  // namespace glm53
+
+extern "C" int glm53_e4m3_scan(const uint8_t* w, int64_t n, uint32_t* nan_count, void* stream) {
+  if (n < 0 || (n > 0 && (!w || !nan_count)) || (((uintptr_t)w) & 15) != 0) {
+    set_last_error("glm53_e4m3_scan: invalid arguments (16-byte aligned weights required)");
+    return GLM53_ERR_INVALID;
+  }
+  if (n == 0) return GLM53_OK;
+  const int blocks = std::max(1, std::min(sm_count() * 8, (int)((n / 16 + 255) / 256)));
+  e4m3_nan_scan_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(w, n, nan_count);
+  return check_launch("e4m3_nan_scan_kernel");
 }

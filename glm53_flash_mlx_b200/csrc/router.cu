@@ -122,8 +122,9 @@ __device__ void warp_topk(const float* logits, const float* __restrict__ bias, c
   }
 }
 
-// Split-K FP32 GEMV for T <= kRouterSmallT tokens: 4 warps per expert row,
-// 2 rows per 256-thread block.  The last block to finish runs the top-k.
+// FP32 GEMV for T <= kRouterSmallT tokens: one block per expert row, each
+// thread sums float4 slices k = 4*tid + 1024*i in K order, then an ordered
+// warp / block reduction.  The last block to finish runs the top-k.
 template <int T_MAX, int PER>
 __global__ void __launch_bounds__(256) router_small_kernel(
     const uint16_t* __restrict__ x, int T, int H, const float* __restrict__ w,
@@ -133,42 +134,36 @@ __global__ void __launch_bounds__(256) router_small_kernel(
   __shared__ bool is_last;
   __shared__ float choice_smem[8][kRouterMaxE];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int e = blockIdx.x * 2 + (warp >> 2);
-  const int q = warp & 3;
+  const int e = blockIdx.x;
+  const float* wr = w + (size_t)e * H;
   float acc[T_MAX];
 #pragma unroll
   for (int t = 0; t < T_MAX; ++t) acc[t] = 0.f;
-  if (e < p.E) {
-    const float* wr = w + (size_t)e * H;
-    const int per = H / 4;  // H % 128 == 0 checked by the host
-    const int k0 = q * per;
-    for (int k = k0 + lane * 4; k < k0 + per; k += 128) {
-      float4 wv = __ldcs(reinterpret_cast<const float4*>(wr + k));
+#pragma unroll 4
+  for (int k = 4 * threadIdx.x; k < H; k += 1024) {
+    const float4 wv = __ldcs(reinterpret_cast<const float4*>(wr + k));
 #pragma unroll
-      for (int t = 0; t < T_MAX; ++t) {
-        if (t < T) {
-          uint2 raw = __ldg(reinterpret_cast<const uint2*>(x + (size_t)t * H + k));
-          acc[t] = fmaf(__uint_as_float(raw.x << 16), wv.x, acc[t]);
-          acc[t] = fmaf(__uint_as_float(raw.x & 0xFFFF0000u), wv.y, acc[t]);
-          acc[t] = fmaf(__uint_as_float(raw.y << 16), wv.z, acc[t]);
-          acc[t] = fmaf(__uint_as_float(raw.y & 0xFFFF0000u), wv.w, acc[t]);
-        }
+    for (int t = 0; t < T_MAX; ++t) {
+      if (t < T) {
+        const uint2 raw = __ldg(reinterpret_cast<const uint2*>(x + (size_t)t * H + k));
+        acc[t] = fmaf(__uint_as_float(raw.x << 16), wv.x, acc[t]);
+        acc[t] = fmaf(__uint_as_float(raw.x & 0xFFFF0000u), wv.y, acc[t]);
+        acc[t] = fmaf(__uint_as_float(raw.y << 16), wv.z, acc[t]);
+        acc[t] = fmaf(__uint_as_float(raw.y & 0xFFFF0000u), wv.w, acc[t]);
       }
     }
   }
 #pragma unroll
   for (int t = 0; t < T_MAX; ++t) {
-    float v = warp_sum(acc[t]);
+    const float v = warp_sum(acc[t]);
     if (lane == 0) part[warp][t] = v;
   }
   __syncthreads();
-  if (threadIdx.x < 2 * T_MAX) {
-    int r = threadIdx.x / T_MAX, t = threadIdx.x % T_MAX;
-    int er = blockIdx.x * 2 + r;
-    if (er < p.E && t < T) {
-      float v = ((part[4 * r][t] + part[4 * r + 1][t]) + (part[4 * r + 2][t] + part[4 * r + 3][t]));
-      logits[(size_t)t * p.E + er] = v;
-    }
+  if (threadIdx.x < T_MAX && threadIdx.x < T) {
+    float v = 0.f;
+#pragma unroll
+    for (int ww = 0; ww < 8; ++ww) v = v + part[ww][threadIdx.x];
+    logits[(size_t)threadIdx.x * p.E + e] = v;
   }
   __threadfence();
   __syncthreads();
@@ -261,7 +256,7 @@ static int launch_topk(const float* logits, int T, const float* bias, TopkParams
 template <int PER>
 static int launch_small(const uint16_t* x, int T, int H, const float* w, const float* bias, TopkParams p,
                         float* logits, uint32_t* counter, uint32_t* idx, float* scores, cudaStream_t st) {
-  int blocks = (p.E + 1) / 2;
+  int blocks = p.E;
   if (T <= 1)
     router_small_kernel<1, PER><<<blocks, 256, 0, st>>>(x, T, H, w, bias, p, logits, counter, idx, scores);
   else
@@ -303,7 +298,7 @@ extern "C" int glm53_router_topk(const void* x, int64_t T, int64_t H, const floa
   float* lbuf = logits ? logits : (float*)ws;
   uint32_t* counter = (uint32_t*)(ws + align_up((size_t)T * E * sizeof(float), 256));
   TopkParams p{(int)E, top_k, n_group < 1 ? 1 : n_group, topk_group, norm_topk_prob, routed_scaling_factor};
-  const bool vec = (H % 128 == 0) && (((uintptr_t)w & 15) == 0) && (((uintptr_t)x & 7) == 0);
+  const bool vec = (H % 4 == 0) && (((uintptr_t)w & 15) == 0) && (((uintptr_t)x & 7) == 0);
   const int per = (int)((E + 31) / 32);
   if (T <= kRouterSmallT && vec) {
     if (per <= 4) return launch_small<4>((const uint16_t*)x, (int)T, (int)H, w, bias, p, lbuf, counter, indices, scores, st);

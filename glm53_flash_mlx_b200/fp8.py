@@ -26,11 +26,14 @@ def _scale_shape(out_features: int, in_features: int) -> tuple[int, int]:
     return ((out_features + BLOCK_SIZE - 1) // BLOCK_SIZE, (in_features + BLOCK_SIZE - 1) // BLOCK_SIZE)
 
 
-def block_fp8_linear(x: torch.Tensor, weight: torch.Tensor, scale_inv: torch.Tensor) -> torch.Tensor:
+def block_fp8_linear(x: torch.Tensor, weight: torch.Tensor, scale_inv: torch.Tensor, *,
+                     e4m3_finite: bool = False) -> torch.Tensor:
     """Compute ``x @ dequant(weight, scale_inv).T`` without expanding weight.
 
     x: BF16 [..., in] on a CUDA device; weight: uint8 E4M3 [out, in];
     scale_inv: float32 [ceil(out/128), ceil(in/128)].  Returns BF16 [..., out].
+    ``e4m3_finite=True`` certifies that ``weight`` holds no code 0x7F/0xFF
+    (see ``_native.e4m3_finite``) and enables the hardware E4M3 decode.
     """
     if not (isinstance(x, torch.Tensor) and x.is_cuda):
         raise RuntimeError("direct GLM-5.3 FP8 execution requires the CUDA backend")
@@ -57,7 +60,8 @@ def block_fp8_linear(x: torch.Tensor, weight: torch.Tensor, scale_inv: torch.Ten
         N.check(
             N.lib().glm53_fp8_linear(
                 flat.data_ptr(), flat.shape[0], in_features, weight.data_ptr(), out_features,
-                scale_inv.data_ptr(), out.data_ptr(), N.stream(x.device),
+                scale_inv.data_ptr(), out.data_ptr(), N.FLAG_E4M3_FINITE if e4m3_finite else 0,
+                N.stream(x.device),
             ),
             "glm53_fp8_linear",
         )
@@ -88,7 +92,8 @@ class BlockFP8Linear(nn.Module):
                    device=linear.weight.device)
 
     def forward(self, x):
-        y = block_fp8_linear(x, self.weight, self.weight_scale_inv)
+        finite = self.weight.is_cuda and N.e4m3_finite(self.weight)
+        y = block_fp8_linear(x, self.weight, self.weight_scale_inv, e4m3_finite=finite)
         return (y + self.bias).to(y.dtype) if self.bias is not None else y
 
 
@@ -119,15 +124,6 @@ class DirectFP8Expert(nn.Module):
         return self.down_proj(swiglu_pair(self.gate_proj(x), self.up_proj(x), self.limit))
 
 
-def _weighted_slot_sum(down: torch.Tensor, scores: torch.Tensor) -> torch.Tensor:
-    """FP32 weighted sum over the slot axis in slot order, then BF16
-    (glm53_flash_mlx/fp8.py:457, packed.py:168-179)."""
-    total = torch.zeros(down.shape[1:], dtype=torch.float32, device=down.device)
-    for j in range(down.shape[0]):
-        total = total + down[j].float() * scores[j].float()
-    return total.to(down.dtype)
-
-
 class DirectFP8MoE(nn.Module):
     """Bucketed top-k MoE over separate canonical expert tensors
     (glm53_flash_mlx/fp8.py:343-400): selected top-8 decode for one row,
@@ -155,14 +151,8 @@ class DirectFP8MoE(nn.Module):
         limit = self.config.swiglu_limit
         if flat_x.shape[0] == 1 and routes.shape == (1, DECODE_TOP_K):
             selected = [self._expert(int(e)) for e in routes[0].tolist()]
-            gate = torch.stack([m.gate_proj(flat_x[0]) for m in selected])
-            up = torch.stack([m.up_proj(flat_x[0]) for m in selected])
-            hidden = swiglu_pair(gate, up, limit)
-            down = torch.stack([m.down_proj(hidden[j]) for j, m in enumerate(selected)])
-            result = _weighted_slot_sum(down, flat_scores[0])[None, :].reshape(x.shape)
-            if self.shared_experts is not None:
-                result = result + self.shared_experts(x)
-            return result
+            return selected_decode_moe(flat_x[0], flat_scores[0], selected, self.shared_experts,
+                                       limit=limit, workspace=self._decode_workspace()).reshape(x.shape)
         result = torch.zeros_like(flat_x)
         for expert_id in torch.unique(routes).tolist():
             rows_cpu, slots_cpu = torch.nonzero(routes == expert_id, as_tuple=True)
@@ -179,3 +169,59 @@ class DirectFP8MoE(nn.Module):
 
     def _expert(self, expert_id: int):
         return self.experts[expert_id]
+
+    def _decode_workspace(self):
+        ws = self.__dict__.get("_ws")
+        if ws is None:
+            ws = self.__dict__["_ws"] = N.Workspace()
+        return ws
+
+
+def _shared_parts(shared):
+    from .packed import shared_fp8_tensors
+
+    return shared_fp8_tensors(shared)
+
+
+def selected_decode_moe(x: torch.Tensor, scores: torch.Tensor, experts, shared, *, limit: float,
+                        workspace: N.Workspace | None = None) -> torch.Tensor:
+    """Top-k decode over separately allocated experts (the Direct module's
+    selected top-8 path, glm53_flash_mlx/fp8.py:372-383) with the packed
+    decode kernels: bit-identical to PackedFP8MoE over the same tensors."""
+    import ctypes
+
+    dev = N.require_cuda(x, scores)
+    H = x.numel()
+    top_k = len(experts)
+    I = experts[0].gate_proj.weight.shape[0]
+    x = x.reshape(H).contiguous()
+    sc = scores.reshape(-1).to(torch.float32).contiguous()
+    tensors = []
+    tables = {name: (ctypes.c_void_p * top_k)() for name in ("gw", "gs", "uw", "us", "dw", "ds")}
+    for j, e in enumerate(experts):
+        parts = (e.gate_proj.weight, e.gate_proj.weight_scale_inv, e.up_proj.weight, e.up_proj.weight_scale_inv,
+                 e.down_proj.weight, e.down_proj.weight_scale_inv)
+        parts = tuple(t.contiguous() for t in parts)
+        tensors.append(parts)
+        for name, t in zip(("gw", "gs", "uw", "us", "dw", "ds"), parts):
+            tables[name][j] = t.data_ptr()
+    sh = _shared_parts(shared)
+    Is = sh[0].shape[0] if sh is not None else 0
+    weights = [t for p in tensors for t in (p[0], p[2], p[4])] + ([sh[0], sh[2], sh[4]] if sh else [])
+    flags = N.decode_flags(*weights)
+    wsp = workspace or N.Workspace()
+    ws = wsp.get(dev, "decode", N.lib().glm53_packed_decode_workspace_bytes(top_k, H, I, Is))
+    status = wsp.get(dev, "status", 4)
+    out = torch.empty(H, dtype=torch.bfloat16, device=dev)
+    p = (lambda i: None if sh is None else sh[i].data_ptr())
+    N.check(
+        N.lib().glm53_selected_decode_moe(
+            x.data_ptr(), H, sc.data_ptr(), top_k, tables["gw"], tables["gs"], tables["uw"], tables["us"],
+            tables["dw"], tables["ds"], I, p(0), p(1), p(2), p(3), p(4), p(5), Is, float(limit), out.data_ptr(),
+            ws.data_ptr(), ws.numel(), status.data_ptr(), flags, N.stream(dev),
+        ),
+        "glm53_selected_decode_moe",
+    )
+    if sh is None and shared is not None:
+        out = (out.reshape(1, H) + shared(x.reshape(1, H))).reshape(H)
+    return out

@@ -130,7 +130,7 @@ def grouped_fp8_linear(x, tile_plan, weight, scale_inv):
             N.lib().glm53_grouped_fp8_linear(
                 x.data_ptr(), routes, in_features, tile_experts.data_ptr(), tile_starts.data_ptr(),
                 tile_lengths.data_ptr(), tile_experts.numel(), weight.contiguous().data_ptr(), experts,
-                out_features, scale_inv.contiguous().data_ptr(), out.data_ptr(), N.stream(dev),
+                out_features, scale_inv.contiguous().data_ptr(), out.data_ptr(), 0, N.stream(dev),
             ),
             "glm53_grouped_fp8_linear",
         )
@@ -202,7 +202,7 @@ def grouped_moe(x, indices, scores, bank, shared, *, limit: float, workspace: N.
                 bank.gate_up_weight.data_ptr(), bank.gate_up_scale_inv.data_ptr(), bank.down_weight.data_ptr(),
                 bank.down_scale_inv.data_ptr(), bank.expert_count, I, N.ptr(sg_w), N.ptr(sg_s), N.ptr(su_w),
                 N.ptr(su_s), N.ptr(sd_w), N.ptr(sd_s), Is, float(limit), out.data_ptr(), ws.data_ptr(),
-                ws.numel(), status.data_ptr(), N.stream(dev),
+                ws.numel(), status.data_ptr(), 0, N.stream(dev),
             ),
             "glm53_grouped_moe",
         )

@@ -216,7 +216,8 @@ def packed_decode_moe(x: torch.Tensor, expert_ids: torch.Tensor, scores: torch.T
     else:
         sg_w = sg_s = su_w = su_s = sd_w = sd_s = None
         Is = 0
-    ws_bytes = N.lib().glm53_packed_decode_workspace_bytes(top_k, I, Is)
+    flags = N.decode_flags(bank.gate_up_weight, bank.down_weight, *(() if shared is None else (sg_w, su_w, sd_w)))
+    ws_bytes = N.lib().glm53_packed_decode_workspace_bytes(top_k, H, I, Is)
     wsp = workspace or N.Workspace()
     ws = wsp.get(dev, "decode", ws_bytes)
     if status is None:
@@ -228,7 +229,7 @@ def packed_decode_moe(x: torch.Tensor, expert_ids: torch.Tensor, scores: torch.T
             bank.gate_up_weight.data_ptr(), bank.gate_up_scale_inv.data_ptr(),
             bank.down_weight.data_ptr(), bank.down_scale_inv.data_ptr(), bank.expert_count, I,
             N.ptr(sg_w), N.ptr(sg_s), N.ptr(su_w), N.ptr(su_s), N.ptr(sd_w), N.ptr(sd_s), Is,
-            float(limit), out.data_ptr(), ws.data_ptr(), ws.numel(), status.data_ptr(), N.stream(dev),
+            float(limit), out.data_ptr(), ws.data_ptr(), ws.numel(), status.data_ptr(), flags, N.stream(dev),
         ),
         "glm53_packed_decode_moe",
     )
@@ -237,9 +238,12 @@ def packed_decode_moe(x: torch.Tensor, expert_ids: torch.Tensor, scores: torch.T
     return out
 
 
-def check_status(status: torch.Tensor) -> None:
-    """Raise for device-side fail-closed signals (one device->host read)."""
+def check_status(status: torch.Tensor, *, clear: bool = True) -> None:
+    """Raise for device-side fail-closed signals (one device->host read);
+    the word is cleared first so the next call starts clean."""
     word = int(status.view(torch.int32)[0].item()) & 0xFFFFFFFF
+    if clear and word:
+        status.view(torch.int32)[:1].zero_()
     if word & N.STATUS_BAD_EXPERT:
         raise IndexError("expert id out of range in routed MoE")
     if word & N.STATUS_WAIT_TIMEOUT:

@@ -38,6 +38,13 @@ extern "C" {
 #define GLM53_STATUS_WAIT_TIMEOUT 2u
 #define GLM53_STATUS_BAD_GEOMETRY 4u
 
+/* `flags` bit: the caller guarantees that the E4M3 weights contain no code
+ * 0x7F or 0xFF (true of every E4M3FN checkpoint, where those codes are NaN;
+ * checked once at bind time with glm53_e4m3_scan).  The kernels then decode
+ * with the hardware conversion.  Without it they decode with an exact bit
+ * re-bias that also maps 0x7F/0xFF to +-480 as the reference table does. */
+#define GLM53_FLAG_E4M3_FINITE 1u
+
 /* Kernel ABI identity string (replaces glm53_flash_mlx/abi.py:3-15 for the
  * CUDA kernels; part of any cache identity that depends on kernel numerics). */
 const char* glm53_kernel_abi(void);
@@ -50,7 +57,15 @@ const char* glm53_last_error(void);
  * Replaces block_fp8_linear, glm53_flash_mlx/fp8.py:254-299 (kernels K1/K2,
  * fp8.py:41-116). */
 int glm53_fp8_linear(const void* x, int64_t M, int64_t K, const uint8_t* w,
-                     int64_t N, const float* scale_inv, void* y, void* stream);
+                     int64_t N, const float* scale_inv, void* y, uint32_t flags,
+                     void* stream);
+
+/* Count (into *nan_count, device memory, accumulated) the 4-byte words of
+ * w[n] that hold an E4M3 code 0x7F or 0xFF; zero means GLM53_FLAG_E4M3_FINITE
+ * may be passed for these weights.  w must be 16-byte aligned.
+ * Counterpart of the bind-time fail-closed scan the reference's table
+ * (glm53_flash_mlx/fp8.py:22-39, 0x7F/0xFF = +-480) calls for. */
+int glm53_e4m3_scan(const uint8_t* w, int64_t n, uint32_t* nan_count, void* stream);
 
 /* Workspace bytes needed by glm53_router_topk for T tokens and E experts. */
 size_t glm53_router_workspace_bytes(int64_t T, int64_t E);
@@ -69,8 +84,10 @@ int glm53_router_topk(const void* x, int64_t T, int64_t H, const float* w,
                       float* scores, float* logits, void* workspace,
                       size_t workspace_bytes, void* stream);
 
-/* Workspace bytes needed by glm53_packed_decode_moe. */
-size_t glm53_packed_decode_workspace_bytes(int top_k, int64_t I, int64_t I_shared);
+/* Workspace bytes needed by glm53_packed_decode_moe (and its gate/up stage).
+ * The workspace must be zero-filled before its first use; every call leaves
+ * its completion counters at zero again. */
+size_t glm53_packed_decode_workspace_bytes(int top_k, int64_t H, int64_t I, int64_t I_shared);
 
 /* One-token packed decode MoE over a packed expert bank:
  *   bank: gate_up_w [E,2I,H] (gate rows [0,I), up rows [I,2I)),
@@ -91,7 +108,25 @@ int glm53_packed_decode_moe(const void* x, int64_t H, const uint32_t* expert_ids
                             const float* shared_up_s, const uint8_t* shared_down_w,
                             const float* shared_down_s, int64_t I_shared,
                             float limit, void* out, void* workspace,
-                            size_t workspace_bytes, uint32_t* status, void* stream);
+                            size_t workspace_bytes, uint32_t* status,
+                            uint32_t flags, void* stream);
+
+/* The same decode over separately allocated experts: gate_w[j], gate_s[j],
+ * up_w[j], up_s[j] ([I,H] + [ceil(I/128), ceil(H/128)]) and down_w[j],
+ * down_s[j] ([H,I] + scales) are host arrays of top_k device pointers, one
+ * per routed slot, in slot order; no expert-id indirection on the device.
+ * Replaces DirectFP8MoE's selected top-8 decode, glm53_flash_mlx/fp8.py:
+ * 372-383 (kernels K3/K4, fp8.py:142-251). */
+int glm53_selected_decode_moe(const void* x, int64_t H, const float* scores, int top_k,
+                              const uint8_t* const* gate_w, const float* const* gate_s,
+                              const uint8_t* const* up_w, const float* const* up_s,
+                              const uint8_t* const* down_w, const float* const* down_s,
+                              int64_t I, const uint8_t* shared_gate_w,
+                              const float* shared_gate_s, const uint8_t* shared_up_w,
+                              const float* shared_up_s, const uint8_t* shared_down_w,
+                              const float* shared_down_s, int64_t I_shared, float limit,
+                              void* out, void* workspace, size_t workspace_bytes,
+                              uint32_t* status, uint32_t flags, void* stream);
 
 /* Diagnostic: only the first stage of glm53_packed_decode_moe (fused
  * gate/up/SwiGLU of the selected experts and the shared expert); the BF16
@@ -105,7 +140,8 @@ int glm53_packed_decode_gate_up(const void* x, int64_t H, const uint32_t* expert
                                 const uint8_t* shared_gate_w, const float* shared_gate_s,
                                 const uint8_t* shared_up_w, const float* shared_up_s,
                                 int64_t I_shared, float limit, void* workspace,
-                                size_t workspace_bytes, uint32_t* status, void* stream);
+                                size_t workspace_bytes, uint32_t* status, uint32_t flags,
+                                void* stream);
 
 /* Stable expert-sorted route plan and tile descriptors on the device.
  *   order[p] = route index at sorted position p; inverse[r] = its position;
@@ -143,7 +179,7 @@ int glm53_grouped_fp8_linear(const void* x, int64_t R, int64_t K,
                              const uint32_t* tile_lengths,
                              int64_t descriptor_capacity, const uint8_t* w,
                              int64_t E, int64_t N, const float* scale_inv,
-                             void* out, void* stream);
+                             void* out, uint32_t flags, void* stream);
 
 /* hidden[R,I] = silu(min(gate, L)) * clip(up, -L, L) with BF16 per-op
  * rounding, gate_up [R,2I].
@@ -179,7 +215,7 @@ int glm53_grouped_moe(const void* x, int64_t T, int64_t H,
                       const float* shared_up_s, const uint8_t* shared_down_w,
                       const float* shared_down_s, int64_t I_shared, float limit,
                       void* out, void* workspace, size_t workspace_bytes,
-                      uint32_t* status, void* stream);
+                      uint32_t* status, uint32_t flags, void* stream);
 
 /* Diagnostic: the BF16 sigmoid stage of the SwiGLU epilogue over n BF16
  * gate values (the reference's formula sweep,

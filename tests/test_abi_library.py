@@ -37,7 +37,7 @@ def test_workspace_queries_are_pure_host_functions():
     from glm53_flash_mlx_b200 import _native as N
 
     lib = N.load_library()
-    assert lib.glm53_packed_decode_workspace_bytes(8, 1536, 1536) >= (8 * 1536 + 1536) * 2
+    assert lib.glm53_packed_decode_workspace_bytes(8, 4096, 1536, 1536) >= (8 * 1536 + 1536) * 2 + 9 * 4096 * 4
     assert lib.glm53_router_workspace_bytes(1, 288) >= 288 * 4
     ws = lib.glm53_grouped_moe_workspace_bytes(2048, 8, 288, 4096, 1536, 1536)
     assert ws >= 16384 * (4096 + 1536) * 2

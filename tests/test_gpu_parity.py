@@ -391,3 +391,45 @@ def test_sorted_grouped_module_vs_direct_and_decode_fallback(G, S):
     assert torch.allclose(grouped(xp).float(), direct(xp).float(), rtol=0.02, atol=0.02)
     xd = torch.randn((1, 1, 256), generator=g, device="cuda").to(torch.bfloat16)
     assert torch.equal(grouped(xd), direct(xd))
+
+
+# ---------------------------------------------------------------------------
+# E4M3 decode modes
+# ---------------------------------------------------------------------------
+
+
+def test_e4m3_scan_detects_nan_codes(S):
+    from glm53_flash_mlx_b200 import _native as N
+
+    w, _ = S.random_block_fp8(256, 4096, seed=3, device="cuda")
+    assert N.e4m3_finite(w)
+    w2 = w.clone()
+    w2[100, 1234] = 0x7F
+    assert not N.e4m3_finite(w2)
+    w3 = w.clone()
+    w3[-1, -1] = 0xFF
+    assert not N.e4m3_finite(w3)
+
+
+@pytest.mark.parametrize("M,N_,K", [(1, 6144, 4096), (8, 512, 2048), (3, 384, 1536)])
+def test_finite_decode_matches_exact_decode_bitwise(G, S, M, N_, K):
+    """The hardware E4M3 decode (codes scaled by 1) and the exact bit decode
+    (codes scaled by 1/256, scale x 256) give identical FP32 sums."""
+    w, s = S.random_block_fp8(N_, K, seed=7, device="cuda")
+    x = S.random_bf16((M, K), seed=8, device="cuda")
+    a = G.block_fp8_linear(x, w, s, e4m3_finite=False)
+    b = G.block_fp8_linear(x, w, s, e4m3_finite=True)
+    assert torch.equal(a, b)
+
+
+def test_exact_decode_handles_0x7f_as_480(G, oracle):
+    """Codes 0x7F/0xFF decode to +-480 (the reference table) on the exact path."""
+    codes = torch.full((16, 256), 0x38, dtype=torch.uint8, device="cuda")  # 1.0
+    codes[:, 0] = 0x7F
+    codes[:, 1] = 0xFF
+    s = torch.ones((1, 2), dtype=torch.float32, device="cuda")
+    x = torch.zeros((1, 256), dtype=torch.bfloat16, device="cuda")
+    x[0, 0] = 1.0
+    x[0, 1] = 0.5
+    y = G.block_fp8_linear(x, codes, s)
+    assert torch.all(y.float() == 480.0 - 240.0)
