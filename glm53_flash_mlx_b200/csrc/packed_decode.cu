@@ -21,6 +21,7 @@
 // weight copies are issued before the activations are staged.
 // Shapes the tiles do not cover take a scalar path, one warp per dot product.
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 #include "gemv_tile.cuh"
@@ -577,6 +578,96 @@ extern "C" int glm53_packed_decode_gate_up(const void* x, int64_t H, const uint3
   a.gu_s = gate_up_s;
   a.d_w = gate_up_w;
   return packed_decode(a, (cudaStream_t)stream, true, flags);
+}
+
+// ---------------------------------------------------------------------------
+// Packed decode with a fixed, statically allocated scratch area.
+//
+// For callers that must not allocate device memory at call time: an engine
+// whose own pool already owns all of HBM, or a latency-critical loop where an
+// allocation (which may synchronise the device) is not acceptable.  The
+// scratch lives in one file-scope device array per device; its address is
+// looked up once per device and then reused, so a call allocates nothing.
+// Every call on a device shares the array: calls whose GPU work overlaps
+// (different streams, or other host threads) race on it.
+// ---------------------------------------------------------------------------
+
+namespace glm53 {
+constexpr size_t kStaticScratchBytes = GLM53_STATIC_SCRATCH_BYTES;
+static __device__ __align__(256) unsigned char g_decode_scratch[kStaticScratchBytes];
+
+constexpr int kMaxScratchDevices = 64;
+static std::mutex g_scratch_mutex;
+static void* g_scratch_ptr[kMaxScratchDevices];
+
+// Address of this device's scratch array; the caller's device is current.
+static int static_scratch(int device, void** out) {
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (!g_scratch_ptr[device]) {
+    void* p = nullptr;
+    const cudaError_t err = cudaGetSymbolAddress(&p, g_decode_scratch);
+    if (err != cudaSuccess || !p) {
+      set_last_error("glm53_packed_decode_moe_static_scratch: cudaGetSymbolAddress failed on device %d: %s",
+                     device, cudaGetErrorString(err));
+      return GLM53_ERR_CUDA;
+    }
+    g_scratch_ptr[device] = p;
+  }
+  *out = g_scratch_ptr[device];
+  return GLM53_OK;
+}
+}  // namespace glm53
+
+extern "C" int glm53_packed_decode_moe_static_scratch(
+    const void* x, int64_t H, const uint32_t* expert_ids, const float* scores, int top_k, const uint8_t* gate_up_w,
+    const float* gate_up_s, const uint8_t* down_w, const float* down_s, int64_t E, int64_t I,
+    const uint8_t* shared_gate_w, const float* shared_gate_s, const uint8_t* shared_up_w, const float* shared_up_s,
+    const uint8_t* shared_down_w, const float* shared_down_s, int64_t I_shared, float limit, void* out,
+    uint32_t* status, uint32_t flags, void* stream) {
+  const char* fn = "glm53_packed_decode_moe_static_scratch";
+  int rc = check_geometry(fn, H, I, top_k, I_shared);
+  if (rc) return rc;
+  const bool has_shared = I_shared > 0;
+  if (E <= 0 || !x || !expert_ids || !scores || !gate_up_w || !gate_up_s || !down_w || !down_s || !out || !status ||
+      (has_shared && (!shared_gate_w || !shared_gate_s || !shared_up_w || !shared_up_s || !shared_down_w ||
+                      !shared_down_s))) {
+    set_last_error("%s: missing pointer or E <= 0", fn);
+    return GLM53_ERR_INVALID;
+  }
+  const DecodeWorkspace wl = decode_workspace(top_k, H, I, I_shared);
+  if (wl.bytes > kStaticScratchBytes) {
+    set_last_error("%s: needs %zu scratch bytes for top_k=%d H=%lld I=%lld I_shared=%lld, above the fixed maximum "
+                   "of %zu; use glm53_packed_decode_moe with a caller-provided workspace",
+                   fn, wl.bytes, top_k, (long long)H, (long long)I, (long long)I_shared, kStaticScratchBytes);
+    return GLM53_ERR_INVALID;
+  }
+  int device = -1;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err != cudaSuccess || device < 0 || device >= kMaxScratchDevices) {
+    set_last_error("%s: no usable current device (%d): %s", fn, device, cudaGetErrorString(err));
+    return GLM53_ERR_CUDA;
+  }
+  void* scratch = nullptr;
+  rc = static_scratch(device, &scratch);
+  if (rc) return rc;
+  // The completion counters must start at zero; a call that ended early
+  // (invalid expert id, launch error) may have left them set.  Everything
+  // else in the scratch area is written before it is read.
+  err = cudaMemsetAsync((char*)scratch + wl.counters, 0, wl.bytes - wl.counters, (cudaStream_t)stream);
+  if (err != cudaSuccess) {
+    set_last_error("%s: clearing the completion counters failed: %s", fn, cudaGetErrorString(err));
+    return GLM53_ERR_CUDA;
+  }
+  DecodeArgs a{};
+  fill_common(a, x, H, scores, top_k, I, shared_gate_w, shared_gate_s, shared_up_w, shared_up_s, shared_down_w,
+              shared_down_s, I_shared, limit, out, scratch, status);
+  a.E = (int)std::min<int64_t>(E, INT32_MAX);
+  a.ids = expert_ids;
+  a.gu_w = gate_up_w;
+  a.gu_s = gate_up_s;
+  a.d_w = down_w;
+  a.d_s = down_s;
+  return packed_decode(a, (cudaStream_t)stream, false, flags);
 }
 
 // ---------------------------------------------------------------------------

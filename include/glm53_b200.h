@@ -128,6 +128,35 @@ int glm53_selected_decode_moe(const void* x, int64_t H, const float* scores, int
                               void* out, void* workspace, size_t workspace_bytes,
                               uint32_t* status, uint32_t flags, void* stream);
 
+/* Size of the fixed scratch area of glm53_packed_decode_moe_static_scratch:
+ * 1 MiB of device memory per device, reserved when the library is loaded. */
+#define GLM53_STATIC_SCRATCH_BYTES (1u << 20)
+
+/* glm53_packed_decode_moe without a workspace argument: it allocates no device
+ * memory.  No counterpart in the reference; it exists for callers that cannot
+ * allocate at call time (an engine whose own pool already holds all of device
+ * memory, or a decode loop where an allocation's possible device
+ * synchronisation is not acceptable).  Same arguments, layouts and results as
+ * glm53_packed_decode_moe.  Its scratch is one fixed array per device of
+ * GLM53_STATIC_SCRATCH_BYTES: a call whose glm53_packed_decode_workspace_bytes
+ * (top_k, H, I, I_shared) exceeds that returns GLM53_ERR_INVALID (config 2,
+ * top_k 8, H 4096, I = I_shared = 1536, needs 176 KiB).  The calling thread's
+ * current device must own `stream` and the pointers; the first call on each
+ * device looks up the array's address.  Each call clears the array's
+ * completion counters on `stream` before its kernels run.  All calls on one
+ * device share the array, so calls whose GPU work overlaps (other streams,
+ * other host threads) race and must be serialised by the caller. */
+int glm53_packed_decode_moe_static_scratch(const void* x, int64_t H, const uint32_t* expert_ids,
+                                           const float* scores, int top_k,
+                                           const uint8_t* gate_up_w, const float* gate_up_s,
+                                           const uint8_t* down_w, const float* down_s,
+                                           int64_t E, int64_t I, const uint8_t* shared_gate_w,
+                                           const float* shared_gate_s, const uint8_t* shared_up_w,
+                                           const float* shared_up_s, const uint8_t* shared_down_w,
+                                           const float* shared_down_s, int64_t I_shared,
+                                           float limit, void* out, uint32_t* status,
+                                           uint32_t flags, void* stream);
+
 /* Diagnostic: only the first stage of glm53_packed_decode_moe (fused
  * gate/up/SwiGLU of the selected experts and the shared expert); the BF16
  * hidden rows [top_k*I + I_shared] are left at the start of `workspace`.
