@@ -40,6 +40,7 @@ sys.path.insert(0, str(ROOT))
 
 H, I, E, TOP_K, LIMIT = 4096, 1536, 288, 8, 10.0
 POOL = 64
+GRAPH_STEPS = 64  # decode steps chained in one CUDA graph
 
 
 def parse_args():
@@ -195,6 +196,34 @@ def build_layers(n_layers: int, seed0: int, device, experts: int = E):
     return layers
 
 
+def time_stage_graph(fn, n, reps, stream, dev):
+    """Average device time (ms) of one fn(i, stream) call: n calls are
+    captured into one CUDA graph (after an eager pass that sets kernel
+    attributes), replayed `reps` times between CUDA events."""
+    import torch
+
+    with torch.cuda.stream(stream):
+        for i in range(n):
+            fn(i, stream.cuda_stream)
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for i in range(n):
+            fn(i, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    g.replay()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(reps):
+        g.replay()
+    stop.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(stop) / (reps * n)
+    del g
+    return ms
+
+
 def bench_b200(args, world, rank, local):
     import torch
 
@@ -236,29 +265,41 @@ def bench_b200(args, world, rank, local):
             sh[5].data_ptr(), I, LIMIT, outs[i].data_ptr(), dws.data_ptr(), dws.numel(), status.data_ptr(),
             flags[i % args.layers], stream), "decode")
 
+    # A model's decode graph chains its layers back to back; here one CUDA
+    # graph chains GRAPH_STEPS steps (rotating layers and inputs), and a
+    # second graph holds the remainder so that exactly K steps are timed.
     s = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(s):
         for i in range(n_graphs):  # eager warm-up (sets kernel attributes)
             step(i, s.cuda_stream)
     s.synchronize()
-    graphs = []
-    for i in range(n_graphs):
+
+    def capture(n):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=s):
-            step(i, torch.cuda.current_stream().cuda_stream)
-        graphs.append(g)
+            for i in range(n):
+                step(i, torch.cuda.current_stream().cuda_stream)
+        return g
+
+    full = capture(GRAPH_STEPS)
+    rem_w, rem_t = args.warmup % GRAPH_STEPS, args.steps % GRAPH_STEPS
+    rem = {n: capture(n) for n in {rem_w, rem_t} if n}
     torch.cuda.synchronize()
+
+    def run(k):
+        for _ in range(k // GRAPH_STEPS):
+            full.replay()
+        if k % GRAPH_STEPS:
+            rem[k % GRAPH_STEPS].replay()
 
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(torch.cuda.current_device()) as clocks:
-        for i in range(args.warmup):
-            graphs[i % n_graphs].replay()
+        run(args.warmup)
         torch.cuda.synchronize()
         barrier(world)
         h0 = time.monotonic()
         start.record()
-        for i in range(args.steps):
-            graphs[i % n_graphs].replay()
+        run(args.steps)
         stop.record()
         torch.cuda.synchronize()
         h1 = time.monotonic()
@@ -270,13 +311,15 @@ def bench_b200(args, world, rank, local):
     tokens = args.steps * world
     value = tokens / (t_ms / 1e3)
 
-    # ---- dominant kernel alone: fused gate/up/SwiGLU, CUDA events ---------
-    torch.cuda.synchronize()
-    k_start, k_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    cur = torch.cuda.current_stream().cuda_stream
-    reps = min(max(args.steps, 64), 4000)
-    k_start.record()
-    for i in range(reps):
+    # ---- single stages, each captured 64 times into one graph -------------
+    def router_only(i, stream):
+        L = layers[i % args.layers]
+        N.check(lib.glm53_router_topk(xs[i % POOL].data_ptr(), 1, H, L["router_w"].data_ptr(), n_exp,
+                                      L["router_b"].data_ptr(), TOP_K, 1, 1, 1, 1.0, idxs[i % n_graphs].data_ptr(),
+                                      scs[i % n_graphs].data_ptr(), None, rws.data_ptr(), rws.numel(), stream),
+                "router")
+
+    def gate_up_only(i, stream):
         L = layers[i % args.layers]
         sh = L["shared"]
         bank = L["bank"]
@@ -284,17 +327,18 @@ def bench_b200(args, world, rank, local):
             xs[i % POOL].data_ptr(), H, idxs[i % n_graphs].data_ptr(), TOP_K, bank.gate_up_weight.data_ptr(),
             bank.gate_up_scale_inv.data_ptr(), n_exp, I, sh[0].data_ptr(), sh[1].data_ptr(), sh[2].data_ptr(),
             sh[3].data_ptr(), I, LIMIT, dws.data_ptr(), dws.numel(), status.data_ptr(), flags[i % args.layers],
-            cur), "gate_up")
-    k_stop.record()
-    torch.cuda.synchronize()
-    k_ms = k_start.elapsed_time(k_stop) / reps
+            stream), "gate_up")
+
+    reps = max(4, min(args.steps // 64, 64))
+    router_ms = time_stage_graph(router_only, 64, reps, s, dev)
+    k_ms = time_stage_graph(gate_up_only, 64, reps, s, dev)
     peaks = measured_peaks()
     achieved = GATE_UP_BYTES / (k_ms / 1e3) / 1e9
     roofline = {"kernel": "decode_gate_up_v4", "bound": "hbm", "achieved": round(achieved, 1),
                 "peak": peaks["hbm_gbs"], "peak_source": peaks["source"], "unit": "GB/s",
                 "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
                 "algorithmic_bytes_per_launch": GATE_UP_BYTES, "avg_launch_us": round(k_ms * 1e3, 2),
-                "launches_timed": reps, "step_bytes": STEP_BYTES,
+                "launches_timed": reps * 64, "step_bytes": STEP_BYTES,
                 "step_frac": round(STEP_BYTES / (t_ms / args.steps / 1e3) / 1e9 / peaks["hbm_gbs"], 4)}
 
     # ---- e2e through the public module API -------------------------------
@@ -326,7 +370,10 @@ def bench_b200(args, world, rank, local):
         e2e = {"value": round(tokens / (e_ms / 1e3), 2), "unit": "tokens/s", "h2d_bytes_per_step": H * 2,
                "d2h_bytes_per_step": H * 2, "api": "PackedFP8MoE.__call__ (Float32Gate router)"}
 
-    extra = {}
+    step_us = t_ms / args.steps * 1e3
+    extra = {"stages_us": {"router": round(router_ms * 1e3, 2), "gate_up": round(k_ms * 1e3, 2),
+                           "down_and_boundaries": round(step_us - (router_ms + k_ms) * 1e3, 2),
+                           "note": "router and gate/up each timed alone (64 calls per CUDA graph)"}}
     if not args.no_prefill:
         extra["prefill_2048"] = bench_prefill(layers, dev, args)
     return {"value": value, "t_ms": t_ms, "clocks": clk, "roofline": roofline, "e2e": e2e,
@@ -452,6 +499,7 @@ def config_block(args, world):
             "global_batch": 1 * world, "seq_len": 1,
             "l2": f"inputs larger than L2: {args.layers} distinct layers rotated "
                   f"({args.layers * 5.44:.1f} GB of experts) and a {POOL}-vector activation pool; no flush",
+            "graph": f"{GRAPH_STEPS} decode steps (router + decode each, stream-ordered) per CUDA graph",
             "parallelism": f"replicas{world}" if world > 1 else "single"}
 
 
@@ -486,6 +534,8 @@ def main():
         "e2e": res["e2e"],
         "gpu_launches": res["gpu_launches"],
     }
+    if "stages_us" in res:
+        line["stages_us"] = res["stages_us"]
     if "prefill_2048" in res:
         line["prefill_2048"] = res["prefill_2048"]
     if rank == 0 and world == 1 and not args.no_cpu:

@@ -61,10 +61,17 @@ __global__ void __launch_bounds__(32 * KS) gemv_stream_kernel(const uint16_t* __
   for (int p = 0; p < P - 1; ++p) issue();
   const float smul = decode_unscale<FINITE>() * stage_f16(xs, stride, x + (size_t)m0 * K, K, ncols, K, scratch);
   float part[4] = {0.f, 0.f, 0.f, 0.f}, tot[4] = {0.f, 0.f, 0.f, 0.f};
+  // this warp's block scales of the current tile, the next tile's prefetched
+  const int nb = kper >> 7;
+  auto srow_of = [&](int it) {
+    return s + (size_t)(((blockIdx.x + it * gridDim.x) << 4) >> 7) * scols + ((warp * kper) >> 7);
+  };
+  WarpScales cur, nxt;
+  cur.load(srow_of(0), nb, my_tiles > 0);
   int u = 0;
   for (int it = 0; it < my_tiles; ++it) {
     const int row0 = (blockIdx.x + it * gridDim.x) << 4;
-    const float* srow = s + (size_t)(row0 >> 7) * scols + ((warp * kper) >> 7);
+    nxt.load(srow_of(it + 1), nb, it + 1 < my_tiles);
     for (int sl = 0; sl < nslice; ++sl, ++u) {
       issue();
       cp_async_wait_group<P - 1>();
@@ -73,8 +80,9 @@ __global__ void __launch_bounds__(32 * KS) gemv_stream_kernel(const uint16_t* __
       uint32_t xw[8];
       load_x_frag(xw, xs + (g < ncols ? g : 0) * stride + kw + 64 * sl, g < ncols);
       mma_slice<FINITE>(part, f0, f1, xw);
-      if (sl & 1) promote(tot, part, __ldg(srow + (sl >> 1)) * smul);
+      if (sl & 1) promote(tot, part, cur.at(sl >> 1) * smul);
     }
+    cur = nxt;
     float* r = red + (it & 1) * KS * 128 + warp * 128;
     r[g * 8 + 2 * q] = tot[0];
     r[g * 8 + 2 * q + 1] = tot[1];

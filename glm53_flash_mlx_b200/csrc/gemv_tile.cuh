@@ -176,6 +176,35 @@ __device__ __forceinline__ void load_x_frag(uint32_t (&xw)[8], const __half* xp,
   xw[7] = xb.w;
 }
 
+// Programmatic dependent launch.  pdl_wait: block until the grids this
+// kernel depends on have completed and their writes are visible (returns at
+// once when the kernel was launched without programmatic serialisation).
+// pdl_trigger: let the next kernel, if launched with programmatic
+// serialisation, start once every block of this grid has triggered or exited.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// One row of block scales spread over the warp (entry b in lane b % 32,
+// register b / 32), loaded once up front so that a promotion never waits on
+// memory.  Rows longer than 64 entries fall back to a load per promotion.
+struct WarpScales {
+  float r0, r1;
+  const float* row;
+  int n;
+  __device__ __forceinline__ void load(const float* p, int count, bool ok) {
+    const int lane = threadIdx.x & 31;
+    row = p;
+    n = count;
+    r0 = (ok && lane < count) ? __ldg(p + lane) : 0.f;
+    r1 = (ok && lane + 32 < count) ? __ldg(p + lane + 32) : 0.f;
+  }
+  // b is warp-uniform and every lane of the warp calls this.
+  __device__ __forceinline__ float at(int b) const {
+    if (n <= 64) return __shfl_sync(0xffffffffu, b < 32 ? r0 : r1, b & 31);
+    return __ldg(row + b);
+  }
+};
+
 // Promotion at the end of a 128-K block with one scale for rows g and g+8
 // (tot[0..1]) and another for the other half of the tile (tot[2..3]).
 __device__ __forceinline__ void promote2(float (&tot)[4], float (&part)[4], float s_lo, float s_hi) {

@@ -129,6 +129,8 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_gate_up_v4(DecodeA
   const int nunits = a.top_k * (a.I >> 3) + (a.Is >> 3);
   const int unit = blockIdx.x * kWarpsPerBlock + warp;
   const bool active = unit < nunits;
+  // the down stage may launch now: its prologue only streams weights
+  pdl_trigger();
   GateUpRows rw{};
   if (active) rw = gate_up_rows(a, unit);
   const bool ld = active && rw.valid;
@@ -145,6 +147,9 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_gate_up_v4(DecodeA
     if (s < nslice) issue(s);
     cp_async_commit_group();
   }
+  WarpScales ssg, ssu;
+  ssg.load(rw.sg, a.H >> 7, ld);
+  ssu.load(rw.su, a.H >> 7, ld);
   const float smul = decode_unscale<FINITE>() * stage_f16(xs, a.H + 8, a.x, 0, 1, a.H, scratch);
   float part[4] = {0.f, 0.f, 0.f, 0.f}, tot[4] = {0.f, 0.f, 0.f, 0.f};
   for (int sl = 0; sl < nslice; ++sl) {
@@ -156,7 +161,7 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_gate_up_v4(DecodeA
     uint32_t xw[8];
     load_x_frag(xw, xs + 64 * sl + 16 * q, g == 0);
     mma_slice<FINITE>(part, fg, fu, xw);
-    if ((sl & 1) && ld) promote2(tot, part, __ldg(rw.sg + (sl >> 1)) * smul, __ldg(rw.su + (sl >> 1)) * smul);
+    if ((sl & 1) && ld) promote2(tot, part, ssg.at(sl >> 1) * smul, ssu.at(sl >> 1) * smul);
   }
   cp_async_wait_group<0>();
   if (active && q == 0) a.hidden[rw.hoff + g] = rw.valid ? swiglu_bf16(tot[0], tot[2], a.limit) : (uint16_t)0;
@@ -217,6 +222,10 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_down_v4(DecodeArgs
     if (s < nslice) issue(s);
     cp_async_commit_group();
   }
+  WarpScales sd;
+  sd.load(srow, cols, ld);
+  // weights are streaming; the hidden rows come from the gate/up stage
+  pdl_wait();
   // every unit of a block has the same slot (H/16 is a multiple of 4 here)
   const int jb = min((int)(blockIdx.x * kWarpsPerBlock) / rtiles, ns - 1);
   const float smul =
@@ -231,7 +240,7 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_down_v4(DecodeArgs
     uint32_t xw[8];
     load_x_frag(xw, xs + 64 * sl + 16 * q, g == 0);
     mma_slice<FINITE>(part, f0, f8, xw);
-    if ((sl & 1) && ld) promote(tot, part, __ldg(srow + (sl >> 1)) * smul);
+    if ((sl & 1) && ld) promote(tot, part, sd.at(sl >> 1) * smul);
   }
   cp_async_wait_group<0>();
   if (!active) return;
@@ -388,6 +397,24 @@ static bool tensor_core_shape(const DecodeArgs& a) {
          a.I <= 32768;
 }
 
+// Launch with or without programmatic stream serialisation (the kernel may
+// start before the previous kernel on the stream has finished; it orders
+// itself with pdl_wait).
+static cudaError_t launch_decode(void (*kernel)(DecodeArgs), int blocks, size_t smem, cudaStream_t st, bool pdl,
+                                 const DecodeArgs& a) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)blocks);
+  cfg.blockDim = dim3(32 * kWarpsPerBlock);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, a);
+}
+
 template <bool FINITE>
 static int launch_v4(const DecodeArgs& a, cudaStream_t st, bool gate_up_only) {
   const size_t ring = (size_t)kWarpsPerBlock * kRing * 64 * 16;
@@ -398,7 +425,7 @@ static int launch_v4(const DecodeArgs& a, cudaStream_t st, bool gate_up_only) {
       if (rc) return rc;
     }
     const int units = a.top_k * (a.I >> 3) + (a.Is >> 3);
-    decode_gate_up_v4<FINITE><<<(units + kWarpsPerBlock - 1) / kWarpsPerBlock, 32 * kWarpsPerBlock, smem, st>>>(a);
+    launch_decode(decode_gate_up_v4<FINITE>, (units + kWarpsPerBlock - 1) / kWarpsPerBlock, smem, st, false, a);
     int rc = check_launch("decode_gate_up_v4");
     if (rc || gate_up_only) return rc;
   }
@@ -409,7 +436,8 @@ static int launch_v4(const DecodeArgs& a, cudaStream_t st, bool gate_up_only) {
   }
   const int ns = a.top_k + (a.Is > 0 ? 1 : 0);
   const int units = ns * (a.H >> 4);
-  decode_down_v4<FINITE><<<(units + kWarpsPerBlock - 1) / kWarpsPerBlock, 32 * kWarpsPerBlock, smem, st>>>(a);
+  // the previous kernel is always this call's gate/up stage
+  launch_decode(decode_down_v4<FINITE>, (units + kWarpsPerBlock - 1) / kWarpsPerBlock, smem, st, true, a);
   return check_launch("decode_down_v4");
 }
 

@@ -27,31 +27,37 @@ struct TopkParams {
   float scale;
 };
 
-// One warp selects the top-k of one token's logits (shared-memory scratch
-// `choice_smem` holds E floats for the group mask).
+// Order-preserving map of a float onto uint32 (larger float -> larger key);
+// key 0 is below every non-NaN value and marks an empty position.
+__device__ __forceinline__ uint32_t order_key(float v) {
+  const uint32_t b = __float_as_uint(v);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+// Inverse of order_key.
+__device__ __forceinline__ float key_value(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+// sigmoid(logit) and its selection key sigmoid + bias (the reference's
+// `choice`), shared by both router paths.
+__device__ __forceinline__ void route_key(float logit, float bias, float& sig, uint32_t& key) {
+  sig = 1.0f / (1.0f + expf(-logit));
+  key = order_key(sig + bias);
+}
+
+// One warp selects the top-k of one token from its keys and sigmoids
+// (value i of lane l is expert e = l + 32 i; key 0 marks e >= E).  Shared
+// scratch `choice_smem` holds E floats for the group mask.
 template <int PER>
-__device__ void warp_topk(const float* logits, const float* __restrict__ bias, const TopkParams& p,
-                          uint32_t* idx_out, float* score_out, float* choice_smem) {
+__device__ void warp_topk_core(uint32_t (&key)[PER], const float (&sig)[PER], const TopkParams& p,
+                               uint32_t* idx_out, float* score_out, float* choice_smem) {
   const int lane = threadIdx.x & 31;
-  float sig[PER], choice[PER];
-#pragma unroll
-  for (int i = 0; i < PER; ++i) {
-    int e = lane + 32 * i;
-    if (e < p.E) {
-      float l = __ldcg(logits + e);
-      float sg = 1.0f / (1.0f + expf(-l));
-      sig[i] = sg;
-      choice[i] = sg + bias[e];
-    } else {
-      sig[i] = 0.f;
-      choice[i] = -INFINITY;
-    }
-  }
   if (p.n_group > 1) {
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
       int e = lane + 32 * i;
-      if (e < p.E) choice_smem[e] = choice[i];
+      if (e < p.E) choice_smem[e] = key_value(key[i]);
     }
     __syncwarp();
     const int per_group = p.E / p.n_group;
@@ -81,45 +87,81 @@ __device__ void warp_topk(const float* logits, const float* __restrict__ bias, c
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
       int e = lane + 32 * i;
-      if (e < p.E && ((dropped >> (e / per_group)) & 1u)) choice[i] = 0.0f;
+      if (e < p.E && ((dropped >> (e / per_group)) & 1u)) key[i] = order_key(0.0f);
     }
     __syncwarp();
   }
+  // k rounds of a warp arg-max on the keys: the largest choice wins, ties go
+  // to the lower expert id (the lowest i of a lane, then the lowest lane).
+  // Slot j's pick stays in lane j.
   uint32_t taken = 0;  // bit i: value i of this lane selected
-  float total = 0.f;
-  float picked_sig[kRouterMaxK];
-  uint32_t picked_idx[kRouterMaxK];
+  uint32_t my_idx = 0;
+  float my_sig = 0.f;
   for (int j = 0; j < p.top_k; ++j) {
-    float v = -INFINITY;
-    int best = 0x7fffffff;
+    uint32_t bk = 0u;
+    int bi = -1;
     float bs = 0.f;
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
-      int e = lane + 32 * i;
-      if (e < p.E && !((taken >> i) & 1u)) {
-        if (choice[i] > v || (choice[i] == v && e < best)) { v = choice[i]; best = e; bs = sig[i]; }
+      if (!((taken >> i) & 1u) && key[i] > bk) {
+        bk = key[i];
+        bi = i;
+        bs = sig[i];
       }
     }
+    const uint32_t wmax = __reduce_max_sync(0xffffffffu, bk);
+    const uint32_t cand = (bi >= 0 && bk == wmax) ? (uint32_t)(32 * bi + lane) : 0xffffffffu;
+    const uint32_t best = __reduce_min_sync(0xffffffffu, cand);
+    const float ps = __shfl_sync(0xffffffffu, bs, best & 31);
+    if ((best & 31) == (uint32_t)lane) taken |= 1u << (best >> 5);
+    if (lane == j) {
+      my_idx = best;
+      my_sig = ps;
+    }
+  }
+  // normaliser summed in slot order
+  float total = 0.f;
+  for (int j = 0; j < p.top_k; ++j) total = total + __shfl_sync(0xffffffffu, my_sig, j);
+  if (lane < p.top_k) {
+    float v = my_sig;
+    if (p.top_k > 1 && p.norm) v = v / total;
+    idx_out[lane] = my_idx;
+    score_out[lane] = v * p.scale;
+  }
+}
+
+// Top-k from logits (the tiled path's separate top-k kernel).
+template <int PER>
+__device__ void warp_topk(const float* logits, const float* __restrict__ bias, const TopkParams& p,
+                          uint32_t* idx_out, float* score_out, float* choice_smem) {
+  const int lane = threadIdx.x & 31;
+  uint32_t key[PER];
+  float sig[PER];
 #pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) {
-      float ov = __shfl_xor_sync(0xffffffffu, v, o);
-      int ob = __shfl_xor_sync(0xffffffffu, best, o);
-      float os = __shfl_xor_sync(0xffffffffu, bs, o);
-      if (ov > v || (ov == v && ob < best)) { v = ov; best = ob; bs = os; }
-    }
-    if ((best & 31) == lane) taken |= 1u << (best >> 5);
-    picked_idx[j] = (uint32_t)best;
-    picked_sig[j] = bs;
+  for (int i = 0; i < PER; ++i) {
+    const int e = lane + 32 * i;
+    key[i] = 0u;
+    sig[i] = 0.f;
+    if (e < p.E) route_key(__ldcg(logits + e), bias[e], sig[i], key[i]);
   }
-  if (lane == 0) {
-    for (int j = 0; j < p.top_k; ++j) total = total + picked_sig[j];
-    for (int j = 0; j < p.top_k; ++j) {
-      float v = picked_sig[j];
-      if (p.top_k > 1 && p.norm) v = v / total;
-      idx_out[j] = picked_idx[j];
-      score_out[j] = v * p.scale;
-    }
+  warp_topk_core<PER>(key, sig, p, idx_out, score_out, choice_smem);
+}
+
+// Top-k from keys and sigmoids already computed per expert (the fused path:
+// every block computed its own expert's, so the last block only loads them).
+template <int PER>
+__device__ void warp_topk_keys(const uint32_t* keys, const float* sigs, const TopkParams& p, uint32_t* idx_out,
+                               float* score_out, float* choice_smem) {
+  const int lane = threadIdx.x & 31;
+  uint32_t key[PER];
+  float sig[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int e = lane + 32 * i;
+    key[i] = e < p.E ? __ldcg(keys + e) : 0u;
+    sig[i] = e < p.E ? __ldcg(sigs + e) : 0.f;
   }
+  warp_topk_core<PER>(key, sig, p, idx_out, score_out, choice_smem);
 }
 
 // FP32 GEMV for T <= kRouterSmallT tokens: one block per expert row, each
@@ -128,14 +170,15 @@ __device__ void warp_topk(const float* logits, const float* __restrict__ bias, c
 template <int T_MAX, int PER>
 __global__ void __launch_bounds__(256) router_small_kernel(
     const uint16_t* __restrict__ x, int T, int H, const float* __restrict__ w,
-    const float* __restrict__ bias, TopkParams p, float* logits, uint32_t* counter,
-    uint32_t* __restrict__ idx, float* __restrict__ scores) {
+    const float* __restrict__ bias, TopkParams p, float* logits, float* sig_buf, uint32_t* key_buf,
+    uint32_t* counter, uint32_t* __restrict__ idx, float* __restrict__ scores) {
   __shared__ float part[8][T_MAX];
   __shared__ bool is_last;
   __shared__ float choice_smem[8][kRouterMaxE];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e = blockIdx.x;
   const float* wr = w + (size_t)e * H;
+  const float be = threadIdx.x < T ? __ldg(bias + e) : 0.f;
   float acc[T_MAX];
 #pragma unroll
   for (int t = 0; t < T_MAX; ++t) acc[t] = 0.f;
@@ -163,9 +206,11 @@ __global__ void __launch_bounds__(256) router_small_kernel(
     float v = 0.f;
 #pragma unroll
     for (int ww = 0; ww < 8; ++ww) v = v + part[ww][threadIdx.x];
-    logits[(size_t)threadIdx.x * p.E + e] = v;
+    const size_t o = (size_t)threadIdx.x * p.E + e;
+    logits[o] = v;
+    route_key(v, be, sig_buf[o], key_buf[o]);
+    __threadfence();  // the writers publish before the block signals completion
   }
-  __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
     unsigned prev = atomicAdd(counter, 1u);
@@ -175,8 +220,8 @@ __global__ void __launch_bounds__(256) router_small_kernel(
   if (!is_last) return;
   __threadfence();
   if (warp < T) {
-    warp_topk<PER>(logits + (size_t)warp * p.E, bias, p, idx + (size_t)warp * p.top_k,
-                   scores + (size_t)warp * p.top_k, choice_smem[warp]);
+    warp_topk_keys<PER>(key_buf + (size_t)warp * p.E, sig_buf + (size_t)warp * p.E, p,
+                        idx + (size_t)warp * p.top_k, scores + (size_t)warp * p.top_k, choice_smem[warp]);
   }
   if (threadIdx.x == 0) *counter = 0u;  // leave the workspace reusable
 }
@@ -253,15 +298,23 @@ static int launch_topk(const float* logits, int T, const float* bias, TopkParams
   return check_launch("router_topk_kernel");
 }
 
+struct RouterScratch {
+  float* logits;
+  float* sig;
+  uint32_t* key;
+  uint32_t* counter;
+};
+
 template <int PER>
 static int launch_small(const uint16_t* x, int T, int H, const float* w, const float* bias, TopkParams p,
-                        float* logits, uint32_t* counter, uint32_t* idx, float* scores, cudaStream_t st) {
+                        const RouterScratch& r, uint32_t* idx, float* scores, cudaStream_t st) {
   int blocks = p.E;
   if (T <= 1)
-    router_small_kernel<1, PER><<<blocks, 256, 0, st>>>(x, T, H, w, bias, p, logits, counter, idx, scores);
+    router_small_kernel<1, PER><<<blocks, 256, 0, st>>>(x, T, H, w, bias, p, r.logits, r.sig, r.key, r.counter,
+                                                        idx, scores);
   else
-    router_small_kernel<kRouterSmallT, PER><<<blocks, 256, 0, st>>>(x, T, H, w, bias, p, logits, counter, idx,
-                                                                    scores);
+    router_small_kernel<kRouterSmallT, PER><<<blocks, 256, 0, st>>>(x, T, H, w, bias, p, r.logits, r.sig, r.key,
+                                                                    r.counter, idx, scores);
   return check_launch("router_small_kernel");
 }
 
@@ -269,8 +322,9 @@ static int launch_small(const uint16_t* x, int T, int H, const float* w, const f
 
 using namespace glm53;
 
+// Workspace: logits | sigmoids | keys (T x E each) | completion counter.
 extern "C" size_t glm53_router_workspace_bytes(int64_t T, int64_t E) {
-  return align_up((size_t)std::max<int64_t>(T, 1) * (size_t)E * sizeof(float), 256) + 256;
+  return 3 * align_up((size_t)std::max<int64_t>(T, 1) * (size_t)E * sizeof(float), 256) + 256;
 }
 
 extern "C" int glm53_router_topk(const void* x, int64_t T, int64_t H, const float* w, int64_t E,
@@ -295,15 +349,16 @@ extern "C" int glm53_router_topk(const void* x, int64_t T, int64_t H, const floa
   }
   cudaStream_t st = (cudaStream_t)stream;
   char* ws = (char*)workspace;
+  const size_t plane = align_up((size_t)T * E * sizeof(float), 256);
   float* lbuf = logits ? logits : (float*)ws;
-  uint32_t* counter = (uint32_t*)(ws + align_up((size_t)T * E * sizeof(float), 256));
+  const RouterScratch rs{lbuf, (float*)(ws + plane), (uint32_t*)(ws + 2 * plane), (uint32_t*)(ws + 3 * plane)};
   TopkParams p{(int)E, top_k, n_group < 1 ? 1 : n_group, topk_group, norm_topk_prob, routed_scaling_factor};
   const bool vec = (H % 4 == 0) && (((uintptr_t)w & 15) == 0) && (((uintptr_t)x & 7) == 0);
   const int per = (int)((E + 31) / 32);
   if (T <= kRouterSmallT && vec) {
-    if (per <= 4) return launch_small<4>((const uint16_t*)x, (int)T, (int)H, w, bias, p, lbuf, counter, indices, scores, st);
-    if (per <= 10) return launch_small<10>((const uint16_t*)x, (int)T, (int)H, w, bias, p, lbuf, counter, indices, scores, st);
-    return launch_small<32>((const uint16_t*)x, (int)T, (int)H, w, bias, p, lbuf, counter, indices, scores, st);
+    if (per <= 4) return launch_small<4>((const uint16_t*)x, (int)T, (int)H, w, bias, p, rs, indices, scores, st);
+    if (per <= 10) return launch_small<10>((const uint16_t*)x, (int)T, (int)H, w, bias, p, rs, indices, scores, st);
+    return launch_small<32>((const uint16_t*)x, (int)T, (int)H, w, bias, p, rs, indices, scores, st);
   }
   dim3 grid((unsigned)((T + 63) / 64), (unsigned)((E + 63) / 64));
   router_gemm_kernel<<<grid, 256, 0, st>>>((const uint16_t*)x, (int)T, (int)H, w, (int)E, lbuf);

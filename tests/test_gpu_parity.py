@@ -191,10 +191,13 @@ def test_packed_decode_config2_full_size(G, S, oracle):
     bank = S.make_bank(E, H, I, seed=1, device="cuda")
     shared = shared_fp8_tensors(S.make_shared(H, I, seed=2, device="cuda"))
     w, b = S.make_router(E, H, seed=3, device="cuda")
+    from glm53_flash_mlx_b200 import _native as N
+
+    ws = N.Workspace()
     for t in range(4):
         x = S.random_bf16((1, H), seed=100 + t, device="cuda")
         idx, sc = G.router_topk(x, w, b, top_k=8)
-        out = G.packed_decode_moe(x[0], idx[0], sc[0], bank, shared, limit=10.0)
+        out = G.packed_decode_moe(x[0], idx[0], sc[0], bank, shared, limit=10.0, workspace=ws)
         torch.cuda.synchronize()
         ids = idx[0].cpu().numpy()
         sub = bank_host(bank, ids)
