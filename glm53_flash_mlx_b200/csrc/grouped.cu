@@ -498,11 +498,16 @@ extern "C" int glm53_restore_and_reduce(const void* sorted_out, const float* sor
 // ---------------------------------------------------------------------------
 
 namespace {
+// Routes per descriptor of the tensor-core (tcgen05) path; the fallback path
+// uses BM-route descriptors, and the capacity covers both.
+constexpr int kTcTileRows = 64;
+
 struct MoeWorkspace {
   uint32_t *order, *inverse, *sorted_experts, *route_offsets, *tile_offsets, *tile_experts, *tile_starts,
       *tile_lengths, *counts;
-  float* sorted_scores;
+  float *sorted_scores, *xscale, *shared_xscale;
   uint16_t *hidden, *down, *shared_hidden, *shared_out;
+  __half *x16, *shared_x16;
   int64_t capacity;
   size_t bytes;
 };
@@ -510,7 +515,7 @@ struct MoeWorkspace {
 MoeWorkspace carve(void* base, int64_t T, int top_k, int64_t E, int64_t H, int64_t I, int64_t Is) {
   MoeWorkspace w{};
   const int64_t R = T * top_k;
-  w.capacity = (R + BM - 1) / BM + E;
+  w.capacity = (R + kTcTileRows - 1) / kTcTileRows + E;
   size_t off = 0;
   char* b = (char*)base;
   auto take = [&](size_t n) {
@@ -532,10 +537,126 @@ MoeWorkspace carve(void* base, int64_t T, int top_k, int64_t E, int64_t H, int64
   w.down = (uint16_t*)take((size_t)R * H * 2);
   w.shared_hidden = (uint16_t*)take((size_t)T * (Is > 0 ? Is : 1) * 2);
   w.shared_out = (uint16_t*)take((size_t)T * H * 2);
+  w.x16 = (__half*)take((size_t)R * H * 2);
+  w.xscale = (float*)take((size_t)R * 4);
+  w.shared_x16 = (__half*)take((size_t)T * H * 2);
+  w.shared_xscale = (float*)take((size_t)T * 4);
   w.bytes = off;
   return w;
 }
 }  // namespace
+
+// Tensor-core composition: route plan (64-route descriptors), sorted FP16
+// activations, tcgen05 gate/up with the SwiGLU epilogue (FP16 hidden rows),
+// tcgen05 down, the dense shared expert on the same kernels, combine.
+static int grouped_moe_tc(const MoeWorkspace& w, const void* x, int64_t T, int64_t H, const uint32_t* indices,
+                          const float* scores, int top_k, const uint8_t* gate_up_w, const float* gate_up_s,
+                          const uint8_t* down_w, const float* down_s, int64_t E, int64_t I,
+                          const uint8_t* shared_gate_w, const float* shared_gate_s, const uint8_t* shared_up_w,
+                          const float* shared_up_s, const uint8_t* shared_down_w, const float* shared_down_s,
+                          int64_t Is, float limit, uint16_t* out, uint32_t* status, bool finite, cudaStream_t st) {
+  const int64_t R = T * top_k;
+  int rc = route_plan(indices, R, E, kTcTileRows, scores, w.order, w.inverse, w.sorted_experts, w.sorted_scores,
+                      w.route_offsets, w.tile_experts, w.tile_starts, w.tile_lengths, w.tile_offsets, w.counts,
+                      w.counts + 1, st);
+  if (rc) return rc;
+  rc = rows_to_f16((const uint16_t*)x, H, w.order, top_k, R, w.x16, w.xscale, st);
+  if (rc) return rc;
+  const int64_t hcols = H / 128, icols = I / 128;
+  TcGemm gu{};
+  gu.x16 = w.x16;
+  gu.xscale = w.xscale;
+  gu.R = R;
+  gu.K = H;
+  gu.tile_experts = w.tile_experts;
+  gu.tile_starts = w.tile_starts;
+  gu.tile_lengths = w.tile_lengths;
+  gu.capacity = (R + kTcTileRows - 1) / kTcTileRows + E;
+  gu.max_rows = kTcTileRows;
+  gu.w = gate_up_w;
+  gu.w_up = gate_up_w;
+  gu.w_rows = 2 * I;
+  gu.u_rows = 2 * I;
+  gu.u_off = I;
+  gu.s_gate = gate_up_s;
+  gu.s_up = gate_up_s + icols * hcols;
+  gu.s_expert = 2 * icols * hcols;
+  gu.E = E;
+  gu.I = I;
+  gu.swiglu = true;
+  gu.limit = limit;
+  gu.finite = finite;
+  gu.out = w.hidden;
+  gu.status = status;
+  rc = grouped_tc(gu, st);
+  if (rc) return rc;
+  TcGemm dn = gu;
+  dn.x16 = reinterpret_cast<const __half*>(w.hidden);
+  dn.xscale = nullptr;
+  dn.K = I;
+  dn.w = down_w;
+  dn.w_up = nullptr;
+  dn.w_rows = H;
+  dn.u_rows = 0;
+  dn.u_off = 0;
+  dn.s_gate = down_s;
+  dn.s_up = nullptr;
+  dn.s_expert = hcols * icols;
+  dn.N = H;
+  dn.I = 0;
+  dn.swiglu = false;
+  dn.out = w.down;
+  rc = grouped_tc(dn, st);
+  if (rc) return rc;
+  const uint16_t* shared_ptr = nullptr;
+  if (Is > 0) {
+    rc = rows_to_f16((const uint16_t*)x, H, nullptr, 1, T, w.shared_x16, w.shared_xscale, st);
+    if (rc) return rc;
+    TcGemm sg{};
+    sg.x16 = w.shared_x16;
+    sg.xscale = w.shared_xscale;
+    sg.R = T;
+    sg.K = H;
+    sg.capacity = (T + kTcTileRows - 1) / kTcTileRows;
+    sg.max_rows = kTcTileRows;
+    sg.dense = true;
+    sg.w = shared_gate_w;
+    sg.w_up = shared_up_w;
+    sg.w_rows = Is;
+    sg.u_rows = Is;
+    sg.u_off = 0;
+    sg.s_gate = shared_gate_s;
+    sg.s_up = shared_up_s;
+    sg.s_expert = 0;
+    sg.E = 1;
+    sg.I = Is;
+    sg.swiglu = true;
+    sg.limit = limit;
+    sg.finite = finite;
+    sg.out = w.shared_hidden;
+    sg.status = status;
+    rc = grouped_tc(sg, st);
+    if (rc) return rc;
+    TcGemm sd = sg;
+    sd.x16 = reinterpret_cast<const __half*>(w.shared_hidden);
+    sd.xscale = nullptr;
+    sd.K = Is;
+    sd.w = shared_down_w;
+    sd.w_up = nullptr;
+    sd.w_rows = H;
+    sd.u_rows = 0;
+    sd.s_gate = shared_down_s;
+    sd.s_up = nullptr;
+    sd.N = H;
+    sd.I = 0;
+    sd.swiglu = false;
+    sd.out = w.shared_out;
+    rc = grouped_tc(sd, st);
+    if (rc) return rc;
+    shared_ptr = w.shared_out;
+  }
+  return combine(w.down, w.sorted_scores, w.inverse, w.sorted_experts, E, T, top_k, H, shared_ptr, out, status, st);
+}
 
 extern "C" size_t glm53_grouped_moe_workspace_bytes(int64_t T, int top_k, int64_t E, int64_t H, int64_t I,
                                                     int64_t I_shared) {
@@ -549,7 +670,6 @@ extern "C" int glm53_grouped_moe(const void* x, int64_t T, int64_t H, const uint
                                  const uint8_t* shared_down_w, const float* shared_down_s, int64_t I_shared,
                                  float limit, void* out, void* workspace, size_t workspace_bytes, uint32_t* status,
                                  uint32_t flags, void* stream) {
-  (void)flags;
   if (T < 0 || H <= 0 || I <= 0 || E <= 0 || top_k <= 0 || I_shared < 0) {
     set_last_error("glm53_grouped_moe: invalid geometry");
     return GLM53_ERR_INVALID;
@@ -571,6 +691,13 @@ extern "C" int glm53_grouped_moe(const void* x, int64_t T, int64_t H, const uint
   cudaStream_t st = (cudaStream_t)stream;
   MoeWorkspace w = carve(workspace, T, top_k, E, H, I, I_shared);
   const int64_t R = T * top_k;
+  if (grouped_tc_supported(H, I, limit, true) && grouped_tc_supported(I, H, limit, false) &&
+      (!has_shared || (I_shared % 128 == 0 && grouped_tc_supported(I_shared, H, limit, false))) &&
+      ((((uintptr_t)x | (uintptr_t)gate_up_w | (uintptr_t)down_w) & 15) == 0) &&
+      (!has_shared || ((((uintptr_t)shared_gate_w | (uintptr_t)shared_up_w | (uintptr_t)shared_down_w) & 15) == 0)))
+    return grouped_moe_tc(w, x, T, H, indices, scores, top_k, gate_up_w, gate_up_s, down_w, down_s, E, I,
+                          shared_gate_w, shared_gate_s, shared_up_w, shared_up_s, shared_down_w, shared_down_s,
+                          I_shared, limit, (uint16_t*)out, status, (flags & GLM53_FLAG_E4M3_FINITE) != 0, st);
   int rc = route_plan(indices, R, E, BM, scores, w.order, w.inverse, w.sorted_experts, w.sorted_scores,
                       w.route_offsets, w.tile_experts, w.tile_starts, w.tile_lengths, w.tile_offsets, w.counts,
                       w.counts + 1, st);

@@ -1,0 +1,634 @@
+// Grouped block-FP8 GEMM on the 5th-generation tensor cores (tcgen05, TMEM,
+// TMA) for expert-sorted routes: the prefill projections of the grouped MoE
+// (glm53_flash_mlx/grouped_fp8.py:206-321, Metal kernel K12 at
+// grouped_fp8.py:30-154) and the dense shared expert.
+//
+// One CTA computes a tile of 128 weight rows x 64 routes (D = W . X^T, the
+// weights as the M operand) over the whole K, for one route descriptor
+// (expert, first route, routes <= 64) and one 128-row weight tile:
+//   warp 0      TMA producer: raw E4M3 weight tiles [128 rows x 128 K] and
+//               activation tiles [64 routes x 128 K] (FP16, 128-byte swizzle)
+//               into a 4-stage shared-memory ring;
+//   warp 1      allocates TMEM and issues tcgen05.mma (kind::f16, A from TMEM,
+//               B from shared memory, FP32 accumulation in TMEM);
+//   warps 2-5   decode each weight row exactly to FP16 (lut(c), or lut(c)/256
+//               on the bit-exact path for banks holding 0x7F/0xFF) and store
+//               it into TMEM as the A operand (one TMEM lane per weight row);
+//   warps 6-9   epilogue: after every 128-K block, read the block's partial
+//               product from TMEM and promote it in FP32 with the 128x128
+//               block scale (tot += s_kb * P_kb), then apply the route's
+//               activation range scale and either store BF16 rows or apply
+//               the reference's BF16 SwiGLU to a gate tile and its up tile.
+// Products of FP16 weights (4 significant bits) and FP16 activations are
+// exact in FP32, so each 128-K block sum differs from the reference's FP32
+// sum only in summation order.  Activations are the BF16 inputs converted to
+// FP16 after multiplication by a power of two 2^-e per route (e chosen so the
+// row's largest magnitude stays below 2^15); the epilogue multiplies by 2^e.
+//
+// Every wait on an mbarrier is bounded (a deadline on the global timer); a
+// CTA that gives up sets GLM53_STATUS_WAIT_TIMEOUT, lets its copies and MMAs
+// drain, frees its TMEM and exits.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "gemv_tile.cuh"
+#include "kernels.cuh"
+
+namespace glm53 {
+namespace tc {
+
+constexpr int kM = 128;        // weight rows per tile (MMA M)
+constexpr int kN = 64;         // routes per tile (MMA N)
+constexpr int kKB = 128;       // K per block-scale block
+constexpr int kStages = 4;     // raw weight / activation ring depth
+constexpr int kThreads = 320;  // 10 warps
+constexpr int kRawBytes = kM * kKB;        // 16 KB of E4M3 per matrix and stage
+constexpr int kActBytes = kN * kKB * 2;    // 16 KB of FP16 per stage (two 64-K boxes)
+constexpr int kTmemCols = 512;
+// TMEM columns: accumulators [2 buffers][2 matrices][kN] at 0, A [2 stages][2 matrices][64] at 256
+constexpr int kAccCol = 0;
+constexpr int kACol = 256;
+constexpr uint64_t kWaitNs = 200ull * 1000 * 1000;  // per-CTA deadline
+
+struct TcArgs {
+  const uint32_t* tile_experts;
+  const uint32_t* tile_starts;
+  const uint32_t* tile_lengths;
+  int dense;             // descriptors implicit: (0, 64 d, min(64, R - 64 d))
+  int R;                 // activation rows
+  int K;                 // reduction length
+  int E;
+  int w_rows;            // gate (or plain) weight-map rows per expert
+  int u_rows;            // up weight-map rows per expert
+  int u_off;             // row offset of the up projection inside an expert
+  const float* s_gate;   // block-scale rows of the gate (or plain) tile
+  const float* s_up;     // block-scale rows of the up tile
+  int64_t s_expert;      // floats between experts in both scale tables
+  const float* xscale;   // per activation row multiplier 2^e
+  float limit;
+  int out_cols;          // columns of out (SwiGLU: I, plain: N)
+  uint16_t* out;         // SwiGLU: FP16 hidden rows; plain: BF16 rows
+  uint32_t* status;
+};
+
+// ---------------------------------------------------------------------------
+// PTX wrappers
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("{ .reg .b64 st; mbarrier.arrive.shared::cta.b64 st, [%0]; }" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("{ .reg .b64 st; mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1; }" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.b32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: false when the CTA has aborted or the deadline passed (which
+// aborts the CTA).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          uint64_t deadline) {
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_try(bar, parity)) return true;
+    if ((it & 63u) == 63u) {
+      if (*abort_flag) return false;
+      if (global_ns() > deadline) {
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tmem_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// D[tmem] (+)= A[tmem] . B[smem]^T, kind::f16, cta_group::1.
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// Instruction descriptor: FP32 accumulate, FP16 A and B, both K-major,
+// N >> 3 at bit 17, M >> 4 at bit 24.
+__host__ __device__ constexpr uint32_t make_idesc(int M, int N) {
+  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// Shared-memory matrix descriptor of a K-major tile with 128-byte swizzle:
+// rows of 128 bytes, 8-row groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t make_sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1u << 16;            // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024u >> 4) << 32;  // stride byte offset
+  d |= (uint64_t)1u << 46;            // descriptor version
+  d |= (uint64_t)2u << 61;            // SWIZZLE_128B
+  return d;
+}
+
+// ---------------------------------------------------------------------------
+// Kernel
+// ---------------------------------------------------------------------------
+
+struct __align__(8) Bars {
+  uint64_t raw_full[kStages], raw_empty[kStages], act_full[kStages], act_empty[kStages];
+  uint64_t a_full[2], a_empty[2], acc_full[2], acc_empty[2], drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+template <bool SWIGLU>
+constexpr size_t smem_bytes() {
+  return 1024 /* alignment slack */ + (size_t)kStages * (SWIGLU ? 2 : 1) * kRawBytes + (size_t)kStages * kActBytes +
+         sizeof(Bars);
+}
+
+template <bool SWIGLU, bool FINITE>
+__global__ void __launch_bounds__(kThreads, 1)
+    grouped_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap umap,
+                      const __grid_constant__ CUtensorMap xmap, TcArgs a) {
+  constexpr int NMAT = SWIGLU ? 2 : 1;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint8_t* raw = smem;                                          // [stage][mat][128][128] E4M3, swizzled
+  uint8_t* act = raw + (size_t)kStages * NMAT * kRawBytes;      // [stage][box 2][64][128 B] FP16, swizzled
+  Bars* bars = reinterpret_cast<Bars*>(act + (size_t)kStages * kActBytes);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int d = blockIdx.x, mt = blockIdx.y;
+  uint32_t e, start, len;
+  if (a.dense) {
+    e = 0;
+    start = (uint32_t)d * kN;
+    len = start < (uint32_t)a.R ? min((uint32_t)kN, (uint32_t)a.R - start) : 0u;
+  } else {
+    // descriptors of up to gridDim.z * 64 routes: this CTA takes sub-chunk z
+    e = a.tile_experts[d];
+    const uint32_t dstart = a.tile_starts[d], dlen = a.tile_lengths[d];
+    const uint32_t off = blockIdx.z * (uint32_t)kN;
+    start = dstart + off;
+    len = dlen > off ? min((uint32_t)kN, dlen - off) : 0u;
+  }
+  if (len == 0) return;  // unused descriptor slot
+  if (e >= (uint32_t)a.E) {
+    if (threadIdx.x == 0) atomicOr(a.status, kStatusBadExpert);
+    return;
+  }
+  const int nkb = a.K / kKB;
+
+  auto bar = [&](uint64_t* p) { return smem_addr(p); };
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(bar(&bars->raw_full[s]), 1);
+      mbar_init(bar(&bars->raw_empty[s]), 4);
+      mbar_init(bar(&bars->act_full[s]), 1);
+      mbar_init(bar(&bars->act_empty[s]), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar(&bars->a_full[s]), 4);
+      mbar_init(bar(&bars->a_empty[s]), 1);
+      mbar_init(bar(&bars->acc_full[s]), 1);
+      mbar_init(bar(&bars->acc_empty[s]), 4);
+    }
+    mbar_init(bar(&bars->drain), 1);
+    bars->abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&wmap)) : "memory");
+    if (SWIGLU) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&umap)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_addr(&bars->tmem_base)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tmem_fence_before();
+  __syncthreads();
+  tmem_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  volatile int* abort_flag = &bars->abort_flag;
+  const uint64_t deadline = global_ns() + kWaitNs;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      const int wrow = (int)e * a.w_rows + mt * kM;
+      const int urow = (int)e * a.u_rows + a.u_off + mt * kM;
+      int issued = 0;
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % kStages;
+        const uint32_t ph = (uint32_t)(kb / kStages) & 1u;
+        if (!mbar_wait(bar(&bars->raw_empty[s]), ph ^ 1u, abort_flag, deadline)) break;
+        if (!mbar_wait(bar(&bars->act_empty[s]), ph ^ 1u, abort_flag, deadline)) break;
+        const uint32_t rf = bar(&bars->raw_full[s]);
+        mbar_expect_tx(rf, NMAT * kRawBytes);
+        uint8_t* rs = raw + (size_t)s * NMAT * kRawBytes;
+        tma_load_2d(smem_addr(rs), &wmap, kb * kKB, wrow, rf);
+        if (SWIGLU) tma_load_2d(smem_addr(rs + kRawBytes), &umap, kb * kKB, urow, rf);
+        const uint32_t af = bar(&bars->act_full[s]);
+        mbar_expect_tx(af, kActBytes);
+        uint8_t* as = act + (size_t)s * kActBytes;
+        tma_load_2d(smem_addr(as), &xmap, kb * kKB, (int)start, af);
+        tma_load_2d(smem_addr(as + kActBytes / 2), &xmap, kb * kKB + 64, (int)start, af);
+        ++issued;
+      }
+      // let every issued copy land before the CTA can exit
+      for (int kb = max(0, issued - kStages); kb < issued; ++kb) {
+        const int s = kb % kStages;
+        const uint32_t ph = (uint32_t)(kb / kStages) & 1u;
+        int zero = 0;
+        const uint64_t dl = global_ns() + kWaitNs;
+        mbar_wait(bar(&bars->raw_full[s]), ph, &zero, dl);
+        mbar_wait(bar(&bars->act_full[s]), ph, &zero, dl);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc(kM, kN);
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % kStages;
+        const uint32_t ph = (uint32_t)(kb / kStages) & 1u;
+        const int ab = kb & 1;
+        const uint32_t aph = (uint32_t)(kb >> 1) & 1u;
+        if (!mbar_wait(bar(&bars->a_full[ab]), aph, abort_flag, deadline)) break;
+        if (!mbar_wait(bar(&bars->act_full[s]), ph, abort_flag, deadline)) break;
+        if (!mbar_wait(bar(&bars->acc_empty[ab]), aph ^ 1u, abort_flag, deadline)) break;
+        tmem_fence_after();
+        const uint32_t act_s = smem_addr(act + (size_t)s * kActBytes);
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m) {
+          const uint32_t d_t = tmem + kAccCol + (ab * 2 + m) * kN;
+#pragma unroll
+          for (int k16 = 0; k16 < kKB / 16; ++k16) {
+            const uint32_t a_t = tmem + kACol + (ab * 2 + m) * 64 + k16 * 8;
+            const uint64_t b_desc =
+                make_sw128_desc(act_s + (k16 >> 2) * (kActBytes / 2) + (k16 & 3) * 32);
+            mma_f16_ts(d_t, a_t, b_desc, idesc, k16 > 0 ? 1u : 0u);
+          }
+        }
+        mma_commit(bar(&bars->a_empty[ab]));
+        mma_commit(bar(&bars->act_empty[s]));
+        mma_commit(bar(&bars->acc_full[ab]));
+      }
+      // every MMA issued so far has completed once this commit arrives
+      int zero = 0;
+      mma_commit(bar(&bars->drain));
+      mbar_wait(bar(&bars->drain), 0, &zero, global_ns() + kWaitNs);
+    }
+    __syncwarp();
+  } else if (warp < 6) {
+    // ---------------- weight decode into TMEM (A operand) ----------------
+    const int q = warp & 3;
+    const int r = q * 32 + lane;  // weight row of this thread = TMEM lane
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    for (int kb = 0; kb < nkb; ++kb) {
+      const int s = kb % kStages;
+      const uint32_t ph = (uint32_t)(kb / kStages) & 1u;
+      const int ab = kb & 1;
+      const uint32_t aph = (uint32_t)(kb >> 1) & 1u;
+      // the whole warp waits and leaves together (tcgen05.st is warp-wide)
+      bool ok = mbar_wait(bar(&bars->raw_full[s]), ph, abort_flag, deadline);
+      ok = __all_sync(0xffffffffu, ok) && __all_sync(0xffffffffu, mbar_wait(bar(&bars->a_empty[ab]), aph ^ 1u,
+                                                                              abort_flag, deadline));
+      if (!ok) break;
+      tmem_fence_after();
+#pragma unroll
+      for (int m = 0; m < NMAT; ++m) {
+        const uint8_t* line = raw + (size_t)s * NMAT * kRawBytes + (size_t)m * kRawBytes + r * 128;
+#pragma unroll
+        for (int half = 0; half < 4; ++half) {  // 32 K codes -> 16 TMEM columns
+          uint32_t v[16];
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc) {
+            const int c = half * 2 + cc;  // 16-byte chunk (16 codes) of the 128-byte row
+            const uint4 w = *reinterpret_cast<const uint4*>(line + 16 * (c ^ (r & 7)));
+            e4m3x4_frag<FINITE>(w.x, v[cc * 8 + 0], v[cc * 8 + 1]);
+            e4m3x4_frag<FINITE>(w.y, v[cc * 8 + 2], v[cc * 8 + 3]);
+            e4m3x4_frag<FINITE>(w.z, v[cc * 8 + 4], v[cc * 8 + 5]);
+            e4m3x4_frag<FINITE>(w.w, v[cc * 8 + 6], v[cc * 8 + 7]);
+          }
+          tmem_st16(tmem + lane_base + kACol + (ab * 2 + m) * 64 + half * 16, v);
+        }
+      }
+      tmem_wait_st();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(&bars->raw_empty[s]));
+      tmem_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(&bars->a_full[ab]));
+    }
+  } else {
+    // ---------------- epilogue: per-block promotion, then output ----------------
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    const int scols = nkb;
+    const float* sg_row = a.s_gate + (size_t)e * a.s_expert + (size_t)mt * scols;
+    const float* su_row = a.s_up + (size_t)e * a.s_expert + (size_t)mt * scols;
+    WarpScales sgs, sus;
+    sgs.load(sg_row, scols, true);
+    sus.load(su_row, scols, SWIGLU);
+    float tg[kN], tu[SWIGLU ? kN : 1];
+#pragma unroll
+    for (int n = 0; n < kN; ++n) tg[n] = 0.f;
+#pragma unroll
+    for (int n = 0; n < (SWIGLU ? kN : 1); ++n) tu[n] = 0.f;
+    bool ok = true;
+    for (int kb = 0; kb < nkb; ++kb) {
+      const int ab = kb & 1;
+      const uint32_t aph = (uint32_t)(kb >> 1) & 1u;
+      if (!__all_sync(0xffffffffu, mbar_wait(bar(&bars->acc_full[ab]), aph, abort_flag, deadline))) {
+        ok = false;
+        break;
+      }
+      tmem_fence_after();
+      const float s_g = sgs.at(kb) * decode_unscale<FINITE>();
+#pragma unroll
+      for (int c = 0; c < kN / 16; ++c) {
+        uint32_t v[16];
+        tmem_ld16(tmem + lane_base + kAccCol + (ab * 2) * kN + c * 16, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) tg[c * 16 + i] = fmaf(s_g, __uint_as_float(v[i]), tg[c * 16 + i]);
+      }
+      if (SWIGLU) {
+        const float s_u = sus.at(kb) * decode_unscale<FINITE>();
+#pragma unroll
+        for (int c = 0; c < kN / 16; ++c) {
+          uint32_t v[16];
+          tmem_ld16(tmem + lane_base + kAccCol + (ab * 2 + 1) * kN + c * 16, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) tu[c * 16 + i] = fmaf(s_u, __uint_as_float(v[i]), tu[c * 16 + i]);
+        }
+      }
+      tmem_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(&bars->acc_empty[ab]));
+    }
+    if (ok) {
+      // Every load has landed and every MMA has completed (the last block's
+      // partial was read), so the raw weight ring is free: park the totals
+      // there, one column per thread (conflict-free), and loop over routes.
+      float* tbuf = reinterpret_cast<float*>(raw);
+#pragma unroll
+      for (int n = 0; n < kN; ++n) {
+        tbuf[n * kM + r] = tg[n];
+        if (SWIGLU) tbuf[(kN + n) * kM + r] = tu[n];
+      }
+      const int col = mt * kM + r;
+      for (uint32_t n = 0; n < len; ++n) {
+        const uint32_t row = start + n;
+        const float xs = a.xscale ? __ldg(a.xscale + row) : 1.0f;
+        uint16_t outv;
+        if (SWIGLU) {
+          const uint16_t h = swiglu_bf16(tbuf[n * kM + r] * xs, tbuf[(kN + n) * kM + r] * xs, a.limit);
+          const __half hh = __float2half_rn(bf16_bits_to_f32(h));
+          outv = *reinterpret_cast<const uint16_t*>(&hh);
+        } else {
+          outv = f32_to_bf16_bits(tbuf[n * kM + r] * xs);
+        }
+        a.out[(size_t)row * a.out_cols + col] = outv;
+      }
+    }
+  }
+
+  __syncthreads();
+  if (threadIdx.x == 0 && bars->abort_flag) atomicOr(a.status, kStatusWaitTimeout);
+  if (warp == 1) {
+    tmem_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host: tensor maps and launch
+// ---------------------------------------------------------------------------
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D map over a row-major [rows, cols] tensor, box [box_rows, box_cols],
+// 128-byte swizzle, zero fill outside.
+static int make_map(CUtensorMap* map, const void* base, CUtensorMapDataType type, int elem_bytes, uint64_t cols,
+                    uint64_t rows, uint32_t box_cols, uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) {
+    set_last_error("grouped_tc: cuTensorMapEncodeTiled is unavailable");
+    return GLM53_ERR_CUDA;
+  }
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * (uint64_t)elem_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, type, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_last_error("grouped_tc: cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return GLM53_ERR_CUDA;
+  }
+  return GLM53_OK;
+}
+
+}  // namespace tc
+
+bool grouped_tc_supported(int64_t K, int64_t N, float limit, bool swiglu) {
+  if (K % tc::kKB != 0 || N % tc::kM != 0 || K <= 0) return false;
+  // FP16 hidden rows: |SwiGLU| <= limit^2 must stay inside FP16 range
+  if (swiglu && !(limit > 0.0f && limit <= 128.0f)) return false;
+  return true;
+}
+
+int grouped_tc(const TcGemm& g, cudaStream_t st) {
+  using namespace tc;
+  const int64_t cols = g.swiglu ? g.I : g.N;
+  if (!grouped_tc_supported(g.K, cols, g.limit, g.swiglu) || g.R <= 0 || g.max_rows <= 0 ||
+      (((uintptr_t)g.x16 | (uintptr_t)g.w | (uintptr_t)(g.swiglu ? g.w_up : g.w)) & 15) != 0) {
+    set_last_error("grouped_tc: unsupported geometry");
+    return GLM53_ERR_INVALID;
+  }
+  if (g.capacity == 0) return GLM53_OK;
+  CUtensorMap wmap, umap, xmap;
+  int rc = make_map(&wmap, g.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)g.K, (uint64_t)(g.E * g.w_rows), kKB,
+                    kM);
+  if (rc) return rc;
+  if (g.swiglu) {
+    rc = make_map(&umap, g.w_up, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)g.K, (uint64_t)(g.E * g.u_rows), kKB,
+                  kM);
+    if (rc) return rc;
+  } else {
+    umap = wmap;
+  }
+  rc = make_map(&xmap, g.x16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)g.K, (uint64_t)g.R, 64, kN);
+  if (rc) return rc;
+  TcArgs a{};
+  a.tile_experts = g.tile_experts;
+  a.tile_starts = g.tile_starts;
+  a.tile_lengths = g.tile_lengths;
+  a.dense = g.dense ? 1 : 0;
+  a.R = (int)g.R;
+  a.K = (int)g.K;
+  a.E = (int)g.E;
+  a.w_rows = (int)g.w_rows;
+  a.u_rows = (int)g.u_rows;
+  a.u_off = (int)g.u_off;
+  a.s_gate = g.s_gate;
+  a.s_up = g.s_up ? g.s_up : g.s_gate;
+  a.s_expert = g.s_expert;
+  a.xscale = g.xscale;
+  a.limit = g.limit;
+  a.out_cols = (int)cols;
+  a.out = g.out;
+  a.status = g.status;
+  dim3 grid((unsigned)g.capacity, (unsigned)(cols / kM), (unsigned)(g.dense ? 1 : (g.max_rows + kN - 1) / kN));
+  void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, TcArgs);
+  size_t smem;
+  if (g.swiglu) {
+    kern = g.finite ? grouped_tc_kernel<true, true> : grouped_tc_kernel<true, false>;
+    smem = smem_bytes<true>();
+  } else {
+    kern = g.finite ? grouped_tc_kernel<false, true> : grouped_tc_kernel<false, false>;
+    smem = smem_bytes<false>();
+  }
+  rc = ensure_max_smem((const void*)kern, smem);
+  if (rc) return rc;
+  kern<<<grid, kThreads, smem, st>>>(wmap, umap, xmap, a);
+  return check_launch("grouped_tc_kernel");
+}
+
+// ---------------------------------------------------------------------------
+// Activations: BF16 rows (optionally gathered through the route order) ->
+// FP16 * 2^-e with 2^e per row.
+// ---------------------------------------------------------------------------
+
+__global__ void to_f16_rows_kernel(const uint16_t* __restrict__ x, int64_t H, const uint32_t* __restrict__ order,
+                                   int div, int64_t rows, __half* __restrict__ y, float* __restrict__ scale) {
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int64_t src = order ? (int64_t)(order[row] / (uint32_t)div) : row;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + src * H);
+  const int n8 = (int)(H >> 3);
+  float m = 0.f;
+  for (int i = lane; i < n8; i += 32) {
+    const uint4 v = xr[i];
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      m = fmaxf(m, fabsf(__uint_as_float(w[t] << 16)));
+      m = fmaxf(m, fabsf(__uint_as_float(w[t] & 0xFFFF0000u)));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  int e = 0;
+  if (m >= 16384.0f) {  // keep |x| * 2^-e < 2^15
+    int ex;
+    frexpf(m, &ex);
+    e = ex - 14;
+  }
+  const float down = ldexpf(1.0f, -e);
+  uint4* yr = reinterpret_cast<uint4*>(y + row * H);
+  for (int i = lane; i < n8; i += 32) {
+    const uint4 v = xr[i];
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      __half2 h = __floats2half2_rn(__uint_as_float(w[t] << 16) * down, __uint_as_float(w[t] & 0xFFFF0000u) * down);
+      o[t] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    yr[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  if (lane == 0) scale[row] = ldexpf(1.0f, e);
+}
+
+int rows_to_f16(const uint16_t* x, int64_t H, const uint32_t* order, int div, int64_t rows, __half* y, float* scale,
+                cudaStream_t st) {
+  if (rows <= 0) return GLM53_OK;
+  if (H % 8 != 0 || (((uintptr_t)x | (uintptr_t)y) & 15) != 0) {
+    set_last_error("rows_to_f16: 16-byte aligned rows required");
+    return GLM53_ERR_INVALID;
+  }
+  to_f16_rows_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(x, H, order, div, rows, y, scale);
+  return check_launch("to_f16_rows_kernel");
+}
+
+}  // namespace glm53

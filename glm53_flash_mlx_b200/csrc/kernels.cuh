@@ -53,6 +53,43 @@ int route_plan(const uint32_t* ids, int64_t R, int64_t E, int64_t tile_rows, con
                uint32_t* tile_lengths, uint32_t* tile_offsets, uint32_t* descriptor_count,
                uint32_t* invalid_count, cudaStream_t stream);
 
+// tcgen05 grouped GEMM (grouped_tc.cu).  Rows of x16 (FP16, row multiplier
+// xscale) are routes; descriptors as for GroupedGemmArgs, each at most
+// max_rows routes.  Plain: out [R, N] BF16 = x . W^T.  SwiGLU: out [R, I] FP16
+// = the reference's BF16 SwiGLU of the gate tile (w rows [u_off.. of w_up for
+// the up tile), stored as FP16.
+struct TcGemm {
+  const __half* x16;
+  const float* xscale;
+  int64_t R, K;
+  const uint32_t* tile_experts;
+  const uint32_t* tile_starts;
+  const uint32_t* tile_lengths;
+  int64_t capacity;
+  int64_t max_rows;       // longest descriptor (ignored when dense)
+  bool dense;             // descriptors implicit: (0, 64 d, min(64, R - 64 d))
+  const uint8_t* w;       // gate (or plain) weights, w_rows rows per expert
+  const uint8_t* w_up;    // up weights (SwiGLU), u_rows rows per expert
+  int64_t w_rows, u_rows, u_off;
+  const float* s_gate;    // scale table of w: [E][w_rows/128][K/128] (row offset included)
+  const float* s_up;
+  int64_t s_expert;       // floats between experts in the scale tables
+  int64_t E;
+  int64_t N;              // plain output columns
+  int64_t I;              // SwiGLU hidden columns
+  bool swiglu;
+  float limit;
+  bool finite;            // no 0x7F/0xFF codes: hardware E4M3 conversion
+  uint16_t* out;
+  uint32_t* status;
+};
+
+bool grouped_tc_supported(int64_t K, int64_t N, float limit, bool swiglu);
+int grouped_tc(const TcGemm& g, cudaStream_t stream);
+// y[r] = FP16(x[order ? order[r] / div : r] * 2^-e_r), scale[r] = 2^e_r.
+int rows_to_f16(const uint16_t* x, int64_t H, const uint32_t* order, int div, int64_t rows, __half* y, float* scale,
+                cudaStream_t stream);
+
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 }  // namespace glm53
