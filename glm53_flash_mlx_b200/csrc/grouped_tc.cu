@@ -14,7 +14,8 @@
 //   warps 2-5   decode each weight row exactly to FP16 (lut(c), or lut(c)/256
 //               on the bit-exact path for banks holding 0x7F/0xFF) and store
 //               it into TMEM as the A operand (one TMEM lane per weight row);
-//   warps 6-9   epilogue: after every 128-K block, read the block's partial
+//   warps 6-13  epilogue (two warps per TMEM lane quarter, 32 routes each):
+//               after every 128-K block, read the block's partial
 //               product from TMEM and promote it in FP32 with the 128x128
 //               block scale (tot += s_kb * P_kb), then apply the route's
 //               activation range scale and either store BF16 rows or apply
@@ -31,6 +32,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -44,14 +46,15 @@ constexpr int kM = 128;        // weight rows per tile (MMA M)
 constexpr int kN = 64;         // routes per tile (MMA N)
 constexpr int kKB = 128;       // K per block-scale block
 constexpr int kStages = 4;     // raw weight / activation ring depth
-constexpr int kThreads = 320;  // 10 warps
+constexpr int kThreads = 448;  // 14 warps
+constexpr int kEpiWarps = 8;   // two per TMEM lane quarter, 32 routes each
 constexpr int kRawBytes = kM * kKB;        // 16 KB of E4M3 per matrix and stage
 constexpr int kActBytes = kN * kKB * 2;    // 16 KB of FP16 per stage (two 64-K boxes)
 constexpr int kTmemCols = 512;
 // TMEM columns: accumulators [2 buffers][2 matrices][kN] at 0, A [2 stages][2 matrices][64] at 256
 constexpr int kAccCol = 0;
 constexpr int kACol = 256;
-constexpr uint64_t kWaitNs = 200ull * 1000 * 1000;  // per-CTA deadline
+constexpr uint64_t kWaitNs = 200ull * 1000 * 1000;  // longest single wait
 
 struct TcArgs {
   const uint32_t* tile_experts;
@@ -107,15 +110,18 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: false when the CTA has aborted or the deadline passed (which
-// aborts the CTA).
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                          uint64_t deadline) {
+// Bounded wait: false when the CTA has aborted, or when this wait has run
+// for longer than kWaitNs (which aborts the CTA).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  uint64_t t0 = 0;
   for (uint32_t it = 0;; ++it) {
     if (mbar_try(bar, parity)) return true;
     if ((it & 63u) == 63u) {
       if (*abort_flag) return false;
-      if (global_ns() > deadline) {
+      const uint64_t now = global_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > kWaitNs) {
         *abort_flag = 1;
         return false;
       }
@@ -140,6 +146,18 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16
       "%15, %16};" ::"r"(taddr),
       "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
       "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr)
       : "memory");
 }
 
@@ -200,43 +218,58 @@ struct __align__(8) Bars {
   int abort_flag;
 };
 
+// Output staging of one tile: BF16 gate (and up) totals, [matrix][route][row].
+constexpr int kOutBytes = 2 * kN * kM * 2;
+
 template <bool SWIGLU>
 constexpr size_t smem_bytes() {
   return 1024 /* alignment slack */ + (size_t)kStages * (SWIGLU ? 2 : 1) * kRawBytes + (size_t)kStages * kActBytes +
-         sizeof(Bars);
+         (SWIGLU ? kOutBytes : 0) + sizeof(Bars);
+}
+
+// Tile t of the persistent schedule: descriptor d = t / (mtiles * zsub), then
+// the weight tile, then the route sub-chunk (weight tiles innermost, so the
+// CTAs in flight share activation rows and an expert's chunks share weights
+// through L2).  len == 0 marks an unused slot.
+struct Tile {
+  uint32_t e, start, len;
+  int mt;
+};
+
+__device__ __forceinline__ Tile tile_at(const TcArgs& a, int t, int mtiles, int zsub) {
+  Tile tl;
+  const int d = t / (mtiles * zsub);
+  const int rem = t - d * mtiles * zsub;
+  tl.mt = rem / zsub;
+  const int z = rem - tl.mt * zsub;
+  if (a.dense) {
+    tl.e = 0;
+    tl.start = (uint32_t)d * kN;
+    tl.len = tl.start < (uint32_t)a.R ? min((uint32_t)kN, (uint32_t)a.R - tl.start) : 0u;
+  } else {
+    tl.e = __ldg(a.tile_experts + d);
+    const uint32_t dstart = __ldg(a.tile_starts + d), dlen = __ldg(a.tile_lengths + d);
+    const uint32_t off = (uint32_t)z * kN;
+    tl.start = dstart + off;
+    tl.len = dlen > off ? min((uint32_t)kN, dlen - off) : 0u;
+    if (tl.len && tl.e >= (uint32_t)a.E) tl.len = 0;  // flagged once by the producer
+  }
+  return tl;
 }
 
 template <bool SWIGLU, bool FINITE>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap umap,
-                      const __grid_constant__ CUtensorMap xmap, TcArgs a) {
+                      const __grid_constant__ CUtensorMap xmap, TcArgs a, int ntiles, int mtiles, int zsub) {
   constexpr int NMAT = SWIGLU ? 2 : 1;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint8_t* raw = smem;                                          // [stage][mat][128][128] E4M3, swizzled
   uint8_t* act = raw + (size_t)kStages * NMAT * kRawBytes;      // [stage][box 2][64][128 B] FP16, swizzled
-  Bars* bars = reinterpret_cast<Bars*>(act + (size_t)kStages * kActBytes);
+  uint16_t* obuf = reinterpret_cast<uint16_t*>(act + (size_t)kStages * kActBytes);
+  Bars* bars = reinterpret_cast<Bars*>(reinterpret_cast<uint8_t*>(obuf) + (SWIGLU ? kOutBytes : 0));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int d = blockIdx.x, mt = blockIdx.y;
-  uint32_t e, start, len;
-  if (a.dense) {
-    e = 0;
-    start = (uint32_t)d * kN;
-    len = start < (uint32_t)a.R ? min((uint32_t)kN, (uint32_t)a.R - start) : 0u;
-  } else {
-    // descriptors of up to gridDim.z * 64 routes: this CTA takes sub-chunk z
-    e = a.tile_experts[d];
-    const uint32_t dstart = a.tile_starts[d], dlen = a.tile_lengths[d];
-    const uint32_t off = blockIdx.z * (uint32_t)kN;
-    start = dstart + off;
-    len = dlen > off ? min((uint32_t)kN, dlen - off) : 0u;
-  }
-  if (len == 0) return;  // unused descriptor slot
-  if (e >= (uint32_t)a.E) {
-    if (threadIdx.x == 0) atomicOr(a.status, kStatusBadExpert);
-    return;
-  }
   const int nkb = a.K / kKB;
 
   auto bar = [&](uint64_t* p) { return smem_addr(p); };
@@ -251,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(&bars->a_full[s]), 4);
       mbar_init(bar(&bars->a_empty[s]), 1);
       mbar_init(bar(&bars->acc_full[s]), 1);
-      mbar_init(bar(&bars->acc_empty[s]), 4);
+      mbar_init(bar(&bars->acc_empty[s]), kEpiWarps);
     }
     mbar_init(bar(&bars->drain), 1);
     bars->abort_flag = 0;
@@ -272,74 +305,129 @@ __global__ void __launch_bounds__(kThreads, 1)
   tmem_fence_after();
   const uint32_t tmem = bars->tmem_base;
   volatile int* abort_flag = &bars->abort_flag;
-  const uint64_t deadline = global_ns() + kWaitNs;
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
+    // Two independent cursors over the same (tile, k-block) sequence: the
+    // weight ring refills as soon as a stage is decoded, the activation ring
+    // as soon as its MMAs completed.
     if (lane == 0) {
-      const int wrow = (int)e * a.w_rows + mt * kM;
-      const int urow = (int)e * a.u_rows + a.u_off + mt * kM;
-      int issued = 0;
-      for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % kStages;
-        const uint32_t ph = (uint32_t)(kb / kStages) & 1u;
-        if (!mbar_wait(bar(&bars->raw_empty[s]), ph ^ 1u, abort_flag, deadline)) break;
-        if (!mbar_wait(bar(&bars->act_empty[s]), ph ^ 1u, abort_flag, deadline)) break;
-        const uint32_t rf = bar(&bars->raw_full[s]);
-        mbar_expect_tx(rf, NMAT * kRawBytes);
-        uint8_t* rs = raw + (size_t)s * NMAT * kRawBytes;
-        tma_load_2d(smem_addr(rs), &wmap, kb * kKB, wrow, rf);
-        if (SWIGLU) tma_load_2d(smem_addr(rs + kRawBytes), &umap, kb * kKB, urow, rf);
-        const uint32_t af = bar(&bars->act_full[s]);
-        mbar_expect_tx(af, kActBytes);
-        uint8_t* as = act + (size_t)s * kActBytes;
-        tma_load_2d(smem_addr(as), &xmap, kb * kKB, (int)start, af);
-        tma_load_2d(smem_addr(as + kActBytes / 2), &xmap, kb * kKB + 64, (int)start, af);
-        ++issued;
+      struct Cursor {
+        int t, kb;
+        uint32_t g;  // k-blocks issued
+        Tile tl;
+      };
+      auto first = [&](Cursor& c, int t) {
+        for (c.t = t; c.t < ntiles; c.t += gridDim.x) {
+          c.tl = tile_at(a, c.t, mtiles, zsub);
+          if (c.tl.len) return;
+        }
+      };
+      auto advance = [&](Cursor& c) {
+        ++c.g;
+        if (++c.kb == nkb) {
+          c.kb = 0;
+          first(c, c.t + gridDim.x);
+        }
+      };
+      // flag used descriptors whose expert is out of range (skipped as empty)
+      if (!a.dense) {
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+          const int d = t / (mtiles * zsub);
+          if ((t % (mtiles * zsub)) == 0 && __ldg(a.tile_lengths + d) && __ldg(a.tile_experts + d) >= (uint32_t)a.E)
+            atomicOr(a.status, kStatusBadExpert);
+        }
+      }
+      Cursor cr{0, 0, 0u, Tile{}}, ca{0, 0, 0u, Tile{}};
+      first(cr, blockIdx.x);
+      first(ca, blockIdx.x);
+      uint64_t t_idle = 0;
+      while ((cr.t < ntiles || ca.t < ntiles) && !*abort_flag) {
+        bool progress = false;
+        if (cr.t < ntiles) {
+          const int s = cr.g % kStages;
+          if (mbar_try(bar(&bars->raw_empty[s]), ((cr.g / kStages) & 1u) ^ 1u)) {
+            const uint32_t rf = bar(&bars->raw_full[s]);
+            mbar_expect_tx(rf, NMAT * kRawBytes);
+            uint8_t* rs = raw + (size_t)s * NMAT * kRawBytes;
+            tma_load_2d(smem_addr(rs), &wmap, cr.kb * kKB, (int)cr.tl.e * a.w_rows + cr.tl.mt * kM, rf);
+            if (SWIGLU)
+              tma_load_2d(smem_addr(rs + kRawBytes), &umap, cr.kb * kKB,
+                          (int)cr.tl.e * a.u_rows + a.u_off + cr.tl.mt * kM, rf);
+            advance(cr);
+            progress = true;
+          }
+        }
+        if (ca.t < ntiles) {
+          const int s = ca.g % kStages;
+          if (mbar_try(bar(&bars->act_empty[s]), ((ca.g / kStages) & 1u) ^ 1u)) {
+            const uint32_t af = bar(&bars->act_full[s]);
+            mbar_expect_tx(af, kActBytes);
+            uint8_t* as = act + (size_t)s * kActBytes;
+            tma_load_2d(smem_addr(as), &xmap, ca.kb * kKB, (int)ca.tl.start, af);
+            tma_load_2d(smem_addr(as + kActBytes / 2), &xmap, ca.kb * kKB + 64, (int)ca.tl.start, af);
+            advance(ca);
+            progress = true;
+          }
+        }
+        if (progress) {
+          t_idle = 0;
+        } else {
+          const uint64_t now = global_ns();
+          if (t_idle == 0) {
+            t_idle = now;
+          } else if (now - t_idle > kWaitNs) {
+            *abort_flag = 1;
+          }
+        }
       }
       // let every issued copy land before the CTA can exit
-      for (int kb = max(0, issued - kStages); kb < issued; ++kb) {
-        const int s = kb % kStages;
-        const uint32_t ph = (uint32_t)(kb / kStages) & 1u;
-        int zero = 0;
-        const uint64_t dl = global_ns() + kWaitNs;
-        mbar_wait(bar(&bars->raw_full[s]), ph, &zero, dl);
-        mbar_wait(bar(&bars->act_full[s]), ph, &zero, dl);
-      }
+      int zero = 0;
+      for (uint32_t k = cr.g > (uint32_t)kStages ? cr.g - kStages : 0u; k < cr.g; ++k)
+        mbar_wait(bar(&bars->raw_full[k % kStages]), (k / kStages) & 1u, &zero);
+      for (uint32_t k = ca.g > (uint32_t)kStages ? ca.g - kStages : 0u; k < ca.g; ++k)
+        mbar_wait(bar(&bars->act_full[k % kStages]), (k / kStages) & 1u, &zero);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc(kM, kN);
-      for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % kStages;
-        const uint32_t ph = (uint32_t)(kb / kStages) & 1u;
-        const int ab = kb & 1;
-        const uint32_t aph = (uint32_t)(kb >> 1) & 1u;
-        if (!mbar_wait(bar(&bars->a_full[ab]), aph, abort_flag, deadline)) break;
-        if (!mbar_wait(bar(&bars->act_full[s]), ph, abort_flag, deadline)) break;
-        if (!mbar_wait(bar(&bars->acc_empty[ab]), aph ^ 1u, abort_flag, deadline)) break;
-        tmem_fence_after();
-        const uint32_t act_s = smem_addr(act + (size_t)s * kActBytes);
-#pragma unroll
-        for (int m = 0; m < NMAT; ++m) {
-          const uint32_t d_t = tmem + kAccCol + (ab * 2 + m) * kN;
-#pragma unroll
-          for (int k16 = 0; k16 < kKB / 16; ++k16) {
-            const uint32_t a_t = tmem + kACol + (ab * 2 + m) * 64 + k16 * 8;
-            const uint64_t b_desc =
-                make_sw128_desc(act_s + (k16 >> 2) * (kActBytes / 2) + (k16 & 3) * 32);
-            mma_f16_ts(d_t, a_t, b_desc, idesc, k16 > 0 ? 1u : 0u);
+      uint32_t g = 0;
+      bool stop = false;
+      for (int t = blockIdx.x; t < ntiles && !stop; t += gridDim.x) {
+        if (tile_at(a, t, mtiles, zsub).len == 0) continue;
+        for (int kb = 0; kb < nkb; ++kb, ++g) {
+          const int s = g % kStages;
+          const uint32_t ph = (g / kStages) & 1u;
+          const int ab = g & 1;
+          const uint32_t aph = (g >> 1) & 1u;
+          if (!mbar_wait(bar(&bars->a_full[ab]), aph, abort_flag) ||
+              !mbar_wait(bar(&bars->act_full[s]), ph, abort_flag) ||
+              !mbar_wait(bar(&bars->acc_empty[ab]), aph ^ 1u, abort_flag)) {
+            stop = true;
+            break;
           }
+          tmem_fence_after();
+          const uint32_t act_s = smem_addr(act + (size_t)s * kActBytes);
+#pragma unroll
+          for (int m = 0; m < NMAT; ++m) {
+            const uint32_t d_t = tmem + kAccCol + (ab * 2 + m) * kN;
+#pragma unroll
+            for (int k16 = 0; k16 < kKB / 16; ++k16) {
+              const uint32_t a_t = tmem + kACol + (ab * 2 + m) * 64 + k16 * 8;
+              const uint64_t b_desc = make_sw128_desc(act_s + (k16 >> 2) * (kActBytes / 2) + (k16 & 3) * 32);
+              mma_f16_ts(d_t, a_t, b_desc, idesc, k16 > 0 ? 1u : 0u);
+            }
+          }
+          mma_commit(bar(&bars->a_empty[ab]));
+          mma_commit(bar(&bars->act_empty[s]));
+          mma_commit(bar(&bars->acc_full[ab]));
         }
-        mma_commit(bar(&bars->a_empty[ab]));
-        mma_commit(bar(&bars->act_empty[s]));
-        mma_commit(bar(&bars->acc_full[ab]));
       }
       // every MMA issued so far has completed once this commit arrives
       int zero = 0;
       mma_commit(bar(&bars->drain));
-      mbar_wait(bar(&bars->drain), 0, &zero, global_ns() + kWaitNs);
+      mbar_wait(bar(&bars->drain), 0, &zero);
     }
     __syncwarp();
   } else if (warp < 6) {
@@ -347,114 +435,126 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;
     const int r = q * 32 + lane;  // weight row of this thread = TMEM lane
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-    for (int kb = 0; kb < nkb; ++kb) {
-      const int s = kb % kStages;
-      const uint32_t ph = (uint32_t)(kb / kStages) & 1u;
-      const int ab = kb & 1;
-      const uint32_t aph = (uint32_t)(kb >> 1) & 1u;
-      // the whole warp waits and leaves together (tcgen05.st is warp-wide)
-      bool ok = mbar_wait(bar(&bars->raw_full[s]), ph, abort_flag, deadline);
-      ok = __all_sync(0xffffffffu, ok) && __all_sync(0xffffffffu, mbar_wait(bar(&bars->a_empty[ab]), aph ^ 1u,
-                                                                              abort_flag, deadline));
-      if (!ok) break;
-      tmem_fence_after();
-#pragma unroll
-      for (int m = 0; m < NMAT; ++m) {
-        const uint8_t* line = raw + (size_t)s * NMAT * kRawBytes + (size_t)m * kRawBytes + r * 128;
-#pragma unroll
-        for (int half = 0; half < 4; ++half) {  // 32 K codes -> 16 TMEM columns
-          uint32_t v[16];
-#pragma unroll
-          for (int cc = 0; cc < 2; ++cc) {
-            const int c = half * 2 + cc;  // 16-byte chunk (16 codes) of the 128-byte row
-            const uint4 w = *reinterpret_cast<const uint4*>(line + 16 * (c ^ (r & 7)));
-            e4m3x4_frag<FINITE>(w.x, v[cc * 8 + 0], v[cc * 8 + 1]);
-            e4m3x4_frag<FINITE>(w.y, v[cc * 8 + 2], v[cc * 8 + 3]);
-            e4m3x4_frag<FINITE>(w.z, v[cc * 8 + 4], v[cc * 8 + 5]);
-            e4m3x4_frag<FINITE>(w.w, v[cc * 8 + 6], v[cc * 8 + 7]);
-          }
-          tmem_st16(tmem + lane_base + kACol + (ab * 2 + m) * 64 + half * 16, v);
+    uint32_t g = 0;
+    bool stop = false;
+    for (int t = blockIdx.x; t < ntiles && !stop; t += gridDim.x) {
+      if (tile_at(a, t, mtiles, zsub).len == 0) continue;
+      for (int kb = 0; kb < nkb; ++kb, ++g) {
+        const int s = g % kStages;
+        const uint32_t ph = (g / kStages) & 1u;
+        const int ab = g & 1;
+        const uint32_t aph = (g >> 1) & 1u;
+        // the whole warp waits and leaves together (tcgen05.st is warp-wide)
+        bool ok = __all_sync(0xffffffffu, mbar_wait(bar(&bars->raw_full[s]), ph, abort_flag));
+        ok = ok && __all_sync(0xffffffffu, mbar_wait(bar(&bars->a_empty[ab]), aph ^ 1u, abort_flag));
+        if (!ok) {
+          stop = true;
+          break;
         }
+        tmem_fence_after();
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m) {
+          const uint8_t* line = raw + (size_t)s * NMAT * kRawBytes + (size_t)m * kRawBytes + r * 128;
+#pragma unroll
+          for (int half = 0; half < 4; ++half) {  // 32 K codes -> 16 TMEM columns
+            uint32_t v[16];
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) {
+              const int c = half * 2 + cc;  // 16-byte chunk (16 codes) of the 128-byte row
+              const uint4 w = *reinterpret_cast<const uint4*>(line + 16 * (c ^ (r & 7)));
+              e4m3x4_frag<FINITE>(w.x, v[cc * 8 + 0], v[cc * 8 + 1]);
+              e4m3x4_frag<FINITE>(w.y, v[cc * 8 + 2], v[cc * 8 + 3]);
+              e4m3x4_frag<FINITE>(w.z, v[cc * 8 + 4], v[cc * 8 + 5]);
+              e4m3x4_frag<FINITE>(w.w, v[cc * 8 + 6], v[cc * 8 + 7]);
+            }
+            tmem_st16(tmem + lane_base + kACol + (ab * 2 + m) * 64 + half * 16, v);
+          }
+        }
+        tmem_wait_st();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(&bars->raw_empty[s]));
+        tmem_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(&bars->a_full[ab]));
       }
-      tmem_wait_st();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(&bars->raw_empty[s]));
-      tmem_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(&bars->a_full[ab]));
     }
   } else {
     // ---------------- epilogue: per-block promotion, then output ----------------
+    // warp pair (w, w + 4) shares a TMEM lane quarter; half h takes routes
+    // [32 h, 32 h + 32) of the tile
     const int q = warp & 3;
+    const int h = (warp - 6) >> 2;
     const int r = q * 32 + lane;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     const int scols = nkb;
-    const float* sg_row = a.s_gate + (size_t)e * a.s_expert + (size_t)mt * scols;
-    const float* su_row = a.s_up + (size_t)e * a.s_expert + (size_t)mt * scols;
-    WarpScales sgs, sus;
-    sgs.load(sg_row, scols, true);
-    sus.load(su_row, scols, SWIGLU);
-    float tg[kN], tu[SWIGLU ? kN : 1];
+    uint32_t g = 0;
+    bool stop = false;
+    for (int t = blockIdx.x; t < ntiles && !stop; t += gridDim.x) {
+      const Tile tl = tile_at(a, t, mtiles, zsub);
+      if (tl.len == 0) continue;
+      const float* sg_row = a.s_gate + (size_t)tl.e * a.s_expert + (size_t)tl.mt * scols;
+      const float* su_row = a.s_up + (size_t)tl.e * a.s_expert + (size_t)tl.mt * scols;
+      WarpScales sgs, sus;
+      sgs.load(sg_row, scols, true);
+      sus.load(su_row, scols, SWIGLU);
+      const uint32_t n0 = (uint32_t)h * 32;
+      // this half's route range multipliers, one per lane
+      const float xs = (a.xscale && n0 + lane < tl.len) ? __ldg(a.xscale + tl.start + n0 + lane) : 1.0f;
+      float tg[32], tu[SWIGLU ? 32 : 1];
 #pragma unroll
-    for (int n = 0; n < kN; ++n) tg[n] = 0.f;
+      for (int n = 0; n < 32; ++n) tg[n] = 0.f;
 #pragma unroll
-    for (int n = 0; n < (SWIGLU ? kN : 1); ++n) tu[n] = 0.f;
-    bool ok = true;
-    for (int kb = 0; kb < nkb; ++kb) {
-      const int ab = kb & 1;
-      const uint32_t aph = (uint32_t)(kb >> 1) & 1u;
-      if (!__all_sync(0xffffffffu, mbar_wait(bar(&bars->acc_full[ab]), aph, abort_flag, deadline))) {
-        ok = false;
-        break;
-      }
-      tmem_fence_after();
-      const float s_g = sgs.at(kb) * decode_unscale<FINITE>();
-#pragma unroll
-      for (int c = 0; c < kN / 16; ++c) {
-        uint32_t v[16];
-        tmem_ld16(tmem + lane_base + kAccCol + (ab * 2) * kN + c * 16, v);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 16; ++i) tg[c * 16 + i] = fmaf(s_g, __uint_as_float(v[i]), tg[c * 16 + i]);
-      }
-      if (SWIGLU) {
-        const float s_u = sus.at(kb) * decode_unscale<FINITE>();
-#pragma unroll
-        for (int c = 0; c < kN / 16; ++c) {
-          uint32_t v[16];
-          tmem_ld16(tmem + lane_base + kAccCol + (ab * 2 + 1) * kN + c * 16, v);
+      for (int n = 0; n < (SWIGLU ? 32 : 1); ++n) tu[n] = 0.f;
+      for (int kb = 0; kb < nkb; ++kb, ++g) {
+        const int ab = g & 1;
+        const uint32_t aph = (g >> 1) & 1u;
+        if (!__all_sync(0xffffffffu, mbar_wait(bar(&bars->acc_full[ab]), aph, abort_flag))) {
+          stop = true;
+          break;
+        }
+        tmem_fence_after();
+        const float s_g = sgs.at(kb) * decode_unscale<FINITE>();
+        const float s_u = SWIGLU ? sus.at(kb) * decode_unscale<FINITE>() : 0.f;
+        uint32_t vg[32];
+        tmem_ld32(tmem + lane_base + kAccCol + (ab * 2) * kN + n0, vg);
+        if (SWIGLU) {
+          uint32_t vu[32];
+          tmem_ld32(tmem + lane_base + kAccCol + (ab * 2 + 1) * kN + n0, vu);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 16; ++i) tu[c * 16 + i] = fmaf(s_u, __uint_as_float(v[i]), tu[c * 16 + i]);
-        }
-      }
-      tmem_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(&bars->acc_empty[ab]));
-    }
-    if (ok) {
-      // Every load has landed and every MMA has completed (the last block's
-      // partial was read), so the raw weight ring is free: park the totals
-      // there, one column per thread (conflict-free), and loop over routes.
-      float* tbuf = reinterpret_cast<float*>(raw);
-#pragma unroll
-      for (int n = 0; n < kN; ++n) {
-        tbuf[n * kM + r] = tg[n];
-        if (SWIGLU) tbuf[(kN + n) * kM + r] = tu[n];
-      }
-      const int col = mt * kM + r;
-      for (uint32_t n = 0; n < len; ++n) {
-        const uint32_t row = start + n;
-        const float xs = a.xscale ? __ldg(a.xscale + row) : 1.0f;
-        uint16_t outv;
-        if (SWIGLU) {
-          const uint16_t h = swiglu_bf16(tbuf[n * kM + r] * xs, tbuf[(kN + n) * kM + r] * xs, a.limit);
-          const __half hh = __float2half_rn(bf16_bits_to_f32(h));
-          outv = *reinterpret_cast<const uint16_t*>(&hh);
+          for (int i = 0; i < 32; ++i) tu[i] = fmaf(s_u, __uint_as_float(vu[i]), tu[i]);
         } else {
-          outv = f32_to_bf16_bits(tbuf[n * kM + r] * xs);
+          tmem_wait_ld();
         }
-        a.out[(size_t)row * a.out_cols + col] = outv;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) tg[i] = fmaf(s_g, __uint_as_float(vg[i]), tg[i]);
+        tmem_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(&bars->acc_empty[ab]));
+      }
+      if (stop) break;
+      const int col = tl.mt * kM + r;
+      if (SWIGLU) {
+        // BF16 gate/up (the reference's gate_up output rounding) parked one
+        // column per thread, then the SwiGLU over this half's routes
+#pragma unroll
+        for (int n = 0; n < 32; ++n) {
+          const float x = __shfl_sync(0xffffffffu, xs, n);
+          obuf[(n0 + n) * kM + r] = f32_to_bf16_bits(tg[n] * x);
+          obuf[(kN + n0 + n) * kM + r] = f32_to_bf16_bits(tu[n] * x);
+        }
+        for (uint32_t n = n0; n < min(n0 + 32u, tl.len); ++n) {
+          const uint16_t hv = swiglu_bf16(bf16_bits_to_f32(obuf[n * kM + r]), bf16_bits_to_f32(obuf[(kN + n) * kM + r]),
+                                          a.limit);
+          const __half hh = __float2half_rn(bf16_bits_to_f32(hv));
+          a.out[(size_t)(tl.start + n) * a.out_cols + col] = *reinterpret_cast<const uint16_t*>(&hh);
+        }
+      } else {
+#pragma unroll
+        for (int n = 0; n < 32; ++n) {
+          const float x = __shfl_sync(0xffffffffu, xs, n);
+          if (n0 + n < tl.len) a.out[(size_t)(tl.start + n0 + n) * a.out_cols + col] = f32_to_bf16_bits(tg[n] * x);
+        }
       }
     }
   }
@@ -557,8 +657,15 @@ int grouped_tc(const TcGemm& g, cudaStream_t st) {
   a.out_cols = (int)cols;
   a.out = g.out;
   a.status = g.status;
-  dim3 grid((unsigned)g.capacity, (unsigned)(cols / kM), (unsigned)(g.dense ? 1 : (g.max_rows + kN - 1) / kN));
-  void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, TcArgs);
+  const int mtiles = (int)(cols / kM);
+  const int zsub = g.dense ? 1 : (int)((g.max_rows + kN - 1) / kN);
+  const int64_t ntiles = g.capacity * mtiles * zsub;
+  if (ntiles > INT32_MAX) {
+    set_last_error("grouped_tc: too many tiles");
+    return GLM53_ERR_INVALID;
+  }
+  const int grid = (int)std::min<int64_t>(ntiles, sm_count());
+  void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, TcArgs, int, int, int);
   size_t smem;
   if (g.swiglu) {
     kern = g.finite ? grouped_tc_kernel<true, true> : grouped_tc_kernel<true, false>;
@@ -569,7 +676,7 @@ int grouped_tc(const TcGemm& g, cudaStream_t st) {
   }
   rc = ensure_max_smem((const void*)kern, smem);
   if (rc) return rc;
-  kern<<<grid, kThreads, smem, st>>>(wmap, umap, xmap, a);
+  kern<<<grid, kThreads, smem, st>>>(wmap, umap, xmap, a, (int)ntiles, mtiles, zsub);
   return check_launch("grouped_tc_kernel");
 }
 

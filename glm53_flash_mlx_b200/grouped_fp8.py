@@ -189,6 +189,7 @@ def grouped_moe(x, indices, scores, bank, shared, *, limit: float, workspace: N.
     else:
         sg_w = sg_s = su_w = su_s = sd_w = sd_s = None
         Is = 0
+    flags = N.decode_flags(bank.gate_up_weight, bank.down_weight, *(() if shared is None else (sg_w, su_w, sd_w)))
     wsp = workspace or N.Workspace()
     nbytes = N.lib().glm53_grouped_moe_workspace_bytes(T, top_k, bank.expert_count, H, I, Is)
     ws = wsp.get(dev, "grouped", nbytes)
@@ -202,7 +203,7 @@ def grouped_moe(x, indices, scores, bank, shared, *, limit: float, workspace: N.
                 bank.gate_up_weight.data_ptr(), bank.gate_up_scale_inv.data_ptr(), bank.down_weight.data_ptr(),
                 bank.down_scale_inv.data_ptr(), bank.expert_count, I, N.ptr(sg_w), N.ptr(sg_s), N.ptr(su_w),
                 N.ptr(su_s), N.ptr(sd_w), N.ptr(sd_s), Is, float(limit), out.data_ptr(), ws.data_ptr(),
-                ws.numel(), status.data_ptr(), 0, N.stream(dev),
+                ws.numel(), status.data_ptr(), flags, N.stream(dev),
             ),
             "glm53_grouped_moe",
         )
