@@ -55,6 +55,9 @@ def parse_args():
     p.add_argument("--experts", type=int, default=E, help="routed experts per layer (profiling uses fewer)")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     p.add_argument("--no-e2e", action="store_true", help="skip the module-API end-to-end pass")
+    p.add_argument("--prefill-only", action="store_true",
+                   help="profiling aid: only the T=2048 grouped prefill measurement (prints its JSON and exits)")
+    p.add_argument("--prefill-reps", type=int, default=8, help="timed grouped prefill layers")
     return p.parse_args()
 
 
@@ -400,7 +403,7 @@ def bench_prefill(layers, dev, args):
         G.router_topk(x, w, b, top_k=TOP_K, workspace=ws)
         G.grouped_moe(x, idx, sc, L["bank"], L["shared"], limit=LIMIT, workspace=ws)
     torch.cuda.synchronize()
-    reps = 8
+    reps = args.prefill_reps
     st, sp = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     st.record()
     for i in range(reps):
@@ -513,6 +516,14 @@ def main():
             import torch.distributed as dist
 
             dist.destroy_process_group()
+        return
+    if args.prefill_only:
+        import torch
+
+        dev = torch.device("cuda", local)
+        layers = build_layers(args.layers, 1000 + 101 * rank, dev, args.experts)
+        if rank == 0:
+            print(json.dumps({"prefill_2048": bench_prefill(layers, dev, args)}), flush=True)
         return
     res, layers, xs = bench_b200(args, world, rank, local)
     line = {
