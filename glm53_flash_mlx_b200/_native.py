@@ -62,6 +62,16 @@ SIGNATURES: dict[str, tuple] = {
         [_vp, _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _f,
          _vp, _vp, _sz, _vp, _u32, _vp],
     ),
+    "glm53_routes_decode_workspace_bytes": (_sz, [_i64, _i64, _i64]),
+    "glm53_routes_decode": (
+        _int,
+        [_vp, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f, _vp, _vp, _sz, _vp, _u32, _vp],
+    ),
+    "glm53_ep_dispatch_pack": (
+        _int,
+        [_vp, _i64, _i64, _vp, _vp, _int, _i64, _int, _i64, _vp, _vp, _vp, _vp, _vp, _vp],
+    ),
+    "glm53_ep_combine": (_int, [_vp, _vp, _vp, _i64, _int, _i64, _vp, _vp, _vp]),
     "glm53_packed_decode_gate_up": (
         _int,
         [_vp, _i64, _vp, _int, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _f, _vp, _sz, _vp, _u32, _vp],

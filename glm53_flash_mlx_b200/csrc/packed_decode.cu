@@ -62,7 +62,14 @@ struct DecodeArgs {
   uint32_t* counters;  // [H / 16] completion counters (zero between calls)
   uint16_t* out;       // [H]
   uint32_t* status;
+  // per-route mode (expert-parallel owners): slot j reads x + j * x_stride and
+  // writes its BF16 down row to route_out[j]; no reduction, no shared expert;
+  // slots whose expert id is kEmptySlot are skipped
+  int64_t x_stride;
+  uint16_t* route_out;
 };
+
+constexpr uint32_t kEmptySlot = 0xFFFFFFFFu;
 
 __host__ __device__ __forceinline__ int align16i(int v) { return (v + 15) & ~15; }
 
@@ -131,6 +138,9 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_gate_up_v4(DecodeA
   const bool active = unit < nunits;
   // the down stage may launch now: its prologue only streams weights
   pdl_trigger();
+  // every unit of a block belongs to one slot (I/8 is a multiple of 4 here)
+  const int jb = (int)(blockIdx.x * kWarpsPerBlock) / (a.I >> 3);
+  if (a.route_out && jb < a.top_k && a.ids[jb] == kEmptySlot) return;
   GateUpRows rw{};
   if (active) rw = gate_up_rows(a, unit);
   const bool ld = active && rw.valid;
@@ -150,7 +160,8 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_gate_up_v4(DecodeA
   WarpScales ssg, ssu;
   ssg.load(rw.sg, a.H >> 7, ld);
   ssu.load(rw.su, a.H >> 7, ld);
-  const float smul = decode_unscale<FINITE>() * stage_f16(xs, a.H + 8, a.x, 0, 1, a.H, scratch);
+  const uint16_t* xb = a.x + (jb < a.top_k ? (size_t)jb * a.x_stride : 0);
+  const float smul = decode_unscale<FINITE>() * stage_f16(xs, a.H + 8, xb, 0, 1, a.H, scratch);
   float part[4] = {0.f, 0.f, 0.f, 0.f}, tot[4] = {0.f, 0.f, 0.f, 0.f};
   for (int sl = 0; sl < nslice; ++sl) {
     if (sl + P - 1 < nslice) issue(sl + P - 1);
@@ -190,6 +201,9 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_down_v4(DecodeArgs
   const int tile = unit - j * rtiles;
   const int row0 = tile << 4;
   const int cols = K >> 7;
+  // every unit of a block belongs to one slot (H/16 is a multiple of 4 here)
+  const int jb = min((int)(blockIdx.x * kWarpsPerBlock) / rtiles, ns - 1);
+  if (a.route_out && a.ids[jb] == kEmptySlot) return;
   bool valid = active;
   const uint8_t* w0 = nullptr;
   const float* srow = nullptr;
@@ -226,8 +240,6 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_down_v4(DecodeArgs
   sd.load(srow, cols, ld);
   // weights are streaming; the hidden rows come from the gate/up stage
   pdl_wait();
-  // every unit of a block has the same slot (H/16 is a multiple of 4 here)
-  const int jb = min((int)(blockIdx.x * kWarpsPerBlock) / rtiles, ns - 1);
   const float smul =
       decode_unscale<FINITE>() * stage_f16(xs, K + 8, a.hidden + (size_t)jb * a.I, 0, 1, K, scratch);
   float part[4] = {0.f, 0.f, 0.f, 0.f}, tot[4] = {0.f, 0.f, 0.f, 0.f};
@@ -244,6 +256,14 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_down_v4(DecodeArgs
   }
   cp_async_wait_group<0>();
   if (!active) return;
+  if (a.route_out) {  // per-route mode: this slot's BF16 down rows, as K6 stores them
+    if (q == 0) {
+      a.route_out[(size_t)j * a.H + row0 + g] = valid ? f32_to_bf16_bits(tot[0]) : (uint16_t)0;
+      a.route_out[(size_t)j * a.H + row0 + g + 8] = valid ? f32_to_bf16_bits(tot[2]) : (uint16_t)0;
+    }
+    if (!valid && lane == 0) atomicOr(a.status, kStatusBadExpert);
+    return;
+  }
   if (q == 0) {
     a.partial[(size_t)j * a.H + row0 + g] = valid ? tot[0] : 0.f;
     a.partial[(size_t)j * a.H + row0 + g + 8] = valid ? tot[2] : 0.f;
@@ -606,6 +626,55 @@ extern "C" int glm53_packed_decode_gate_up(const void* x, int64_t H, const uint3
   a.gu_s = gate_up_s;
   a.d_w = gate_up_w;
   return packed_decode(a, (cudaStream_t)stream, true, flags);
+}
+
+// ---------------------------------------------------------------------------
+// Per-route decode (expert-parallel owners)
+// ---------------------------------------------------------------------------
+
+extern "C" size_t glm53_routes_decode_workspace_bytes(int64_t R, int64_t H, int64_t I) {
+  return align_up((size_t)std::max<int64_t>(R, 1) * (size_t)I * sizeof(uint16_t), 256);
+}
+
+extern "C" int glm53_routes_decode(const void* x_rows, int64_t R, int64_t H, const uint32_t* expert_ids,
+                                   const uint8_t* gate_up_w, const float* gate_up_s, const uint8_t* down_w,
+                                   const float* down_s, int64_t E, int64_t I, float limit, void* out_rows,
+                                   void* workspace, size_t workspace_bytes, uint32_t* status, uint32_t flags,
+                                   void* stream) {
+  const char* fn = "glm53_routes_decode";
+  if (R < 0 || H <= 0 || I <= 0 || E <= 0 || H > INT32_MAX / 2 || I > INT32_MAX / 64 || R > INT32_MAX / I) {
+    set_last_error("%s: invalid geometry R=%lld H=%lld I=%lld E=%lld", fn, (long long)R, (long long)H, (long long)I,
+                   (long long)E);
+    return GLM53_ERR_INVALID;
+  }
+  if (R == 0) return GLM53_OK;
+  if (!x_rows || !expert_ids || !gate_up_w || !gate_up_s || !down_w || !down_s || !out_rows || !status ||
+      !workspace || workspace_bytes < glm53_routes_decode_workspace_bytes(R, H, I)) {
+    set_last_error("%s: missing pointer or workspace too small", fn);
+    return GLM53_ERR_INVALID;
+  }
+  DecodeArgs a{};
+  a.x = (const uint16_t*)x_rows;
+  a.H = (int)H;
+  a.I = (int)I;
+  a.Is = 0;
+  a.top_k = (int)R;
+  a.E = (int)std::min<int64_t>(E, INT32_MAX);
+  a.ids = expert_ids;
+  a.gu_w = gate_up_w;
+  a.gu_s = gate_up_s;
+  a.d_w = down_w;
+  a.d_s = down_s;
+  a.limit = limit;
+  a.hidden = (uint16_t*)workspace;
+  a.status = status;
+  a.x_stride = H;
+  a.route_out = (uint16_t*)out_rows;
+  if (!tensor_core_shape(a) || (((uintptr_t)out_rows) & 15) != 0) {
+    set_last_error("%s: H and I must be multiples of 128 with 16-byte aligned tensors", fn);
+    return GLM53_ERR_INVALID;
+  }
+  return packed_decode(a, (cudaStream_t)stream, false, flags);
 }
 
 // ---------------------------------------------------------------------------

@@ -1,0 +1,208 @@
+"""Expert-parallel decode MoE across the GPUs of one node.
+
+One process per GPU.  Rank ``r`` of ``world`` holds the contiguous expert range
+``expert_range(r, world, E)`` of every layer's bank (E / world experts), and a
+full copy of the router and the shared expert; tokens stay on their home rank.
+Per layer and decode step:
+
+1. the home rank routes its tokens (``glm53_router_topk``);
+2. ``glm53_ep_dispatch_pack`` places every route into ``capacity`` slots per
+   destination rank (slots in route order) and an all-to-all of equal chunks
+   delivers token rows and local expert ids to the owners;
+3. each owner runs ``glm53_routes_decode`` on the slots it received (gate/up,
+   SwiGLU, down: one BF16 row per route, the K7 + K6 arithmetic of the packed
+   decode);
+4. a second all-to-all returns the rows to their home slots;
+5. ``glm53_ep_combine`` reduces them in slot order and adds the shared expert
+   (computed at home with the same kernels).
+
+Because every route's row is computed by the same kernels as the one-GPU
+packed decode and reduced in the same order, the result is bit-identical for
+every world size.  The reference runs this layer on one device only
+(glm53_flash_mlx/packed.py:879-923); the partition, the fixed capacity and the
+slot order are this package's design.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from . import _native as N
+
+EMPTY_SLOT = 0xFFFFFFFF
+
+
+def expert_range(rank: int, world: int, experts: int) -> tuple[int, int]:
+    """Experts [start, stop) owned by ``rank``: E / world contiguous ids."""
+    if world < 1 or experts % world:
+        raise ValueError(f"{experts} experts do not split evenly over {world} ranks")
+    per = experts // world
+    return rank * per, (rank + 1) * per
+
+
+def owner_of(expert: int, world: int, experts: int) -> int:
+    return int(expert) // (experts // world)
+
+
+def plan_slots(indices: np.ndarray, experts: int, world: int, capacity: int):
+    """Host statement of the dispatch layout that ``glm53_ep_dispatch_pack``
+    builds on the device: returns ``(send_expert [world*capacity] uint32,
+    route_pos [T*top_k] uint32)``.  Route r = t*top_k + j goes to the next free
+    slot of its owner, in route order; a full destination drops the route
+    (position ``EMPTY_SLOT``)."""
+    ids = np.asarray(indices, dtype=np.uint32).reshape(-1)
+    per = experts // world
+    send = np.full(world * capacity, EMPTY_SLOT, dtype=np.uint32)
+    pos = np.full(ids.size, EMPTY_SLOT, dtype=np.uint32)
+    fill = [0] * world
+    for r, e in enumerate(ids.tolist()):
+        if e >= experts:
+            continue
+        d = e // per
+        if fill[d] < capacity:
+            p = d * capacity + fill[d]
+            send[p] = e - d * per
+            pos[r] = p
+            fill[d] += 1
+    return send, pos
+
+
+def local_bank(bank, rank: int, world: int):
+    """This rank's experts of a full bank, as a bank of borrowed-stable views
+    (the full bank stays their owner)."""
+    from .ownership import TensorLayout, borrowed_stable_tensor
+    from .packed import PackedFP8ExpertBank
+
+    lo, hi = expert_range(rank, world, bank.expert_count)
+    lay = TensorLayout.ROW_MAJOR_CONTIGUOUS
+
+    def view(t):
+        return borrowed_stable_tensor(t[lo:hi], owner=bank, layout=lay)
+
+    return PackedFP8ExpertBank(view(bank.gate_up_weight), view(bank.gate_up_scale_inv), view(bank.down_weight),
+                               view(bank.down_scale_inv), intermediate_size=bank.intermediate_size)
+
+
+def pack_shared_bank(shared) -> tuple[torch.Tensor, ...] | None:
+    """The shared expert's six tensors as a one-expert bank (gate rows then up
+    rows), so the per-route kernels run it like any routed expert."""
+    if shared is None:
+        return None
+    sg_w, sg_s, su_w, su_s, sd_w, sd_s = shared
+    gu_w = torch.cat([sg_w, su_w], dim=0).unsqueeze(0).contiguous()
+    gu_s = torch.cat([sg_s, su_s], dim=0).unsqueeze(0).contiguous()
+    return gu_w, gu_s, sd_w.unsqueeze(0).contiguous(), sd_s.unsqueeze(0).contiguous()
+
+
+def routes_decode(x_rows: torch.Tensor, expert_ids: torch.Tensor, bank: tuple, *, limit: float,
+                  out: torch.Tensor | None = None, workspace: N.Workspace | None = None,
+                  status: torch.Tensor | None = None, flags: int | None = None) -> torch.Tensor:
+    """One BF16 down row per route slot (``glm53_routes_decode``).  ``bank`` is
+    ``(gate_up_w [E,2I,H], gate_up_s, down_w [E,H,I], down_s)``."""
+    gu_w, gu_s, d_w, d_s = bank
+    dev = N.require_cuda(x_rows, expert_ids, gu_w)
+    R, H = x_rows.shape
+    E, I2, _ = gu_w.shape
+    I = I2 // 2
+    if out is None:
+        out = torch.empty((R, H), dtype=torch.bfloat16, device=dev)
+    wsp = workspace or N.Workspace()
+    ws = wsp.get(dev, "routes", N.lib().glm53_routes_decode_workspace_bytes(R, H, I))
+    if status is None:
+        status = wsp.get(dev, "status", 4)
+    if flags is None:
+        flags = N.decode_flags(gu_w, d_w)
+    N.check(
+        N.lib().glm53_routes_decode(
+            x_rows.data_ptr(), R, H, expert_ids.data_ptr(), gu_w.data_ptr(), gu_s.data_ptr(), d_w.data_ptr(),
+            d_s.data_ptr(), E, I, float(limit), out.data_ptr(), ws.data_ptr(), ws.numel(), status.data_ptr(), flags,
+            N.stream(dev),
+        ),
+        "glm53_routes_decode",
+    )
+    return out
+
+
+class ExpertParallelDecode:
+    """Plan-owned buffers and the five steps above for one layer.
+
+    ``bank`` holds this rank's experts ``expert_range(rank, world, experts)``;
+    ``shared`` the shared expert's six tensors (or None).  ``max_tokens`` sizes
+    the fixed capacity (``max_tokens * top_k`` slots per destination, which
+    never drops a route).  ``group`` is the ``torch.distributed`` process group
+    (NCCL for CUDA tensors); ``world == 1`` needs none."""
+
+    def __init__(self, bank, *, experts: int, rank: int, world: int, shared, limit: float,
+                 group=None, max_tokens: int = 1, top_k: int = 8):
+        self.bank = (bank.gate_up_weight, bank.gate_up_scale_inv, bank.down_weight, bank.down_scale_inv)
+        self.experts, self.rank, self.world, self.group = int(experts), int(rank), int(world), group
+        lo, hi = expert_range(rank, world, experts)
+        if bank.expert_count != hi - lo:
+            raise ValueError(f"rank {rank} bank holds {bank.expert_count} experts, expected {hi - lo}")
+        self.limit = float(limit)
+        self.top_k = int(top_k)
+        self.max_tokens = int(max_tokens)
+        self.capacity = self.max_tokens * self.top_k
+        self.H = bank.hidden_size
+        self.shared_bank = pack_shared_bank(shared)
+        dev = bank.gate_up_weight.device
+        self.device = dev
+        slots = world * self.capacity
+        self.send_x = torch.zeros((slots, self.H), dtype=torch.bfloat16, device=dev)
+        self.recv_x = torch.zeros_like(self.send_x)
+        self.send_e = torch.full((slots,), -1, dtype=torch.int32, device=dev)
+        self.recv_e = torch.full_like(self.send_e, -1)
+        self.rows = torch.zeros_like(self.send_x)
+        self.back = torch.zeros_like(self.send_x)
+        self.slot_scores = torch.zeros(slots, dtype=torch.float32, device=dev)
+        self.route_pos = torch.zeros(self.max_tokens * self.top_k, dtype=torch.int32, device=dev)
+        self.zero_ids = torch.zeros(self.max_tokens, dtype=torch.int32, device=dev)
+        self.shared_rows = torch.zeros((self.max_tokens, self.H), dtype=torch.bfloat16, device=dev)
+        self.workspace = N.Workspace()
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.flags = N.decode_flags(self.bank[0], self.bank[2])
+        self.shared_flags = N.decode_flags(self.shared_bank[0], self.shared_bank[2]) if self.shared_bank else 0
+
+    def _exchange(self, recv: torch.Tensor, send: torch.Tensor) -> None:
+        if self.world == 1:
+            recv.copy_(send)
+            return
+        import torch.distributed as dist
+
+        dist.all_to_all_single(recv, send, group=self.group)
+
+    def __call__(self, x: torch.Tensor, indices: torch.Tensor, scores: torch.Tensor,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+        flat = x.reshape(-1, self.H)
+        T = flat.shape[0]
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens exceed the plan's max_tokens={self.max_tokens}")
+        if indices.shape[-1] != self.top_k:
+            raise ValueError(f"expected top-{self.top_k} routes, got {indices.shape[-1]}")
+        lib = N.lib()
+        st = N.stream(self.device)
+        ids = indices.reshape(-1).to(torch.int32).contiguous()
+        sc = scores.reshape(-1).to(torch.float32).contiguous()
+        flat = flat.contiguous()
+        if out is None:
+            out = torch.empty((T, self.H), dtype=torch.bfloat16, device=self.device)
+        N.check(lib.glm53_ep_dispatch_pack(flat.data_ptr(), T, self.H, ids.data_ptr(), sc.data_ptr(), self.top_k,
+                                           self.experts, self.world, self.capacity, self.send_x.data_ptr(),
+                                           self.send_e.data_ptr(), self.slot_scores.data_ptr(),
+                                           self.route_pos.data_ptr(), self.status.data_ptr(), st),
+                "glm53_ep_dispatch_pack")
+        self._exchange(self.recv_x, self.send_x)
+        self._exchange(self.recv_e, self.send_e)
+        routes_decode(self.recv_x, self.recv_e, self.bank, limit=self.limit, out=self.rows,
+                      workspace=self.workspace, status=self.status, flags=self.flags)
+        shared_ptr = None
+        if self.shared_bank is not None:
+            routes_decode(flat, self.zero_ids[:T], self.shared_bank, limit=self.limit, out=self.shared_rows[:T],
+                          workspace=self.workspace, status=self.status, flags=self.shared_flags)
+            shared_ptr = self.shared_rows.data_ptr()
+        self._exchange(self.back, self.rows)
+        N.check(lib.glm53_ep_combine(self.back.data_ptr(), self.route_pos.data_ptr(), self.slot_scores.data_ptr(), T,
+                                     self.top_k, self.H, shared_ptr, out.data_ptr(), st),
+                "glm53_ep_combine")
+        return out.reshape(x.shape)

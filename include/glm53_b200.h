@@ -157,6 +157,52 @@ int glm53_packed_decode_moe_static_scratch(const void* x, int64_t H, const uint3
                                            float limit, void* out, uint32_t* status,
                                            uint32_t flags, void* stream);
 
+/* Workspace bytes needed by glm53_routes_decode for R route slots. */
+size_t glm53_routes_decode_workspace_bytes(int64_t R, int64_t H, int64_t I);
+
+/* Per-route decode, the expert owner's half of expert-parallel decode: for
+ * every slot r, out_rows[r] = BF16 of expert expert_ids[r]'s
+ * down(SwiGLU(gate . x_r, up . x_r)) (the K7 + K6 arithmetic of
+ * glm53_packed_decode_moe for one slot, bit-identical to its per-slot value),
+ * with x_r = x_rows[r] (BF16 [R,H]).  Slots whose id is 0xFFFFFFFF are empty
+ * and skipped (their rows are left untouched); other ids >= E raise
+ * GLM53_STATUS_BAD_EXPERT.  Bank layout as glm53_packed_decode_moe; H and I
+ * multiples of 128.  Replaces the owner-side expert loop of the expert-
+ * parallel layout the reference's Direct/packed modules run on one device
+ * (glm53_flash_mlx/packed.py:896-923, per slot). */
+int glm53_routes_decode(const void* x_rows, int64_t R, int64_t H, const uint32_t* expert_ids,
+                        const uint8_t* gate_up_w, const float* gate_up_s,
+                        const uint8_t* down_w, const float* down_s, int64_t E, int64_t I,
+                        float limit, void* out_rows, void* workspace, size_t workspace_bytes,
+                        uint32_t* status, uint32_t flags, void* stream);
+
+/* Expert-parallel dispatch packing on the tokens' home rank.  Experts are
+ * split into `world` contiguous ranges of E / world; route (t, j) with expert
+ * e goes to rank d = e / (E / world), into the next free of `capacity` slots
+ * of destination d (slots in route order t * top_k + j):
+ *   send_x [world * capacity, H] BF16 = the token's row,
+ *   send_expert [world * capacity] = e - d * (E / world) or 0xFFFFFFFF (empty),
+ *   slot_scores [world * capacity] = the route's score (kept home),
+ *   route_pos [T * top_k] = d * capacity + slot (0xFFFFFFFF when dropped).
+ * capacity >= T * top_k never drops; a drop raises GLM53_STATUS_BAD_GEOMETRY.
+ * The exchange is an all-to-all of equal `capacity`-slot chunks (NCCL on the
+ * host).  No counterpart in the reference (single device); it implements the
+ * expert-parallel dispatch its MoE layer is to run with across GPUs. */
+int glm53_ep_dispatch_pack(const void* x, int64_t T, int64_t H, const uint32_t* expert_ids,
+                           const float* scores, int top_k, int64_t E, int world,
+                           int64_t capacity, void* send_x, uint32_t* send_expert,
+                           float* slot_scores, uint32_t* route_pos, uint32_t* status,
+                           void* stream);
+
+/* Expert-parallel combine on the home rank: out[t] = BF16(sum_j
+ * f32(rows[route_pos[t,j]]) * slot_scores[route_pos[t,j]]) in slot order,
+ * then + shared[t] (BF16 add) when shared is not NULL — the reduce of
+ * glm53_flash_mlx/packed.py:168-179 and the shared add of packed.py:915-922,
+ * applied to rows returned by their owners. */
+int glm53_ep_combine(const void* rows, const uint32_t* route_pos, const float* slot_scores,
+                     int64_t T, int top_k, int64_t H, const void* shared, void* out,
+                     void* stream);
+
 /* Diagnostic: only the first stage of glm53_packed_decode_moe (fused
  * gate/up/SwiGLU of the selected experts and the shared expert); the BF16
  * hidden rows [top_k*I + I_shared] are left at the start of `workspace`.
