@@ -58,6 +58,8 @@ def parse_args():
     p.add_argument("--prefill-only", action="store_true",
                    help="profiling aid: only the T=2048 grouped prefill measurement (prints its JSON and exits)")
     p.add_argument("--prefill-reps", type=int, default=8, help="timed grouped prefill layers")
+    p.add_argument("--ep-transport", choices=["p2p", "nccl"], default="p2p",
+                   help="N > 1: expert-parallel dispatch/combine through peer memory or NCCL all-to-alls")
     return p.parse_args()
 
 
@@ -383,6 +385,164 @@ def bench_b200(args, world, rank, local):
             "gpu_launches": args.steps * 3, **extra}, layers, xs
 
 
+def build_ep_layers(n_layers: int, rank: int, world: int, device, experts: int = E):
+    """Per-rank expert slices (E / world experts of each layer) plus the
+    replicated router and shared expert (same seeds on every rank)."""
+    from glm53_flash_mlx_b200 import synthetic as S
+    from glm53_flash_mlx_b200.packed import shared_fp8_tensors
+
+    layers = []
+    for l in range(n_layers):
+        seed = 1000 + 17 * l
+        bank = S.make_bank(experts // world, H, I, seed=seed + 7919 * (rank + 1), device=device)
+        shared_mod = S.make_shared(H, I, seed=seed + 1, limit=LIMIT, device=device)
+        w, b = S.make_router(experts, H, seed=seed + 2, device=device)
+        layers.append({"bank": bank, "shared_mod": shared_mod, "shared": shared_fp8_tensors(shared_mod),
+                       "router_w": w, "router_b": b})
+    return layers
+
+
+def bench_ep(args, world, rank, local):
+    """N > 1: expert-parallel decode (config 4 at batch 1 per rank): each rank
+    routes its own token, the routes travel to their experts' ranks and back
+    through peer memory (``--ep-transport nccl``: NCCL all-to-alls), 64 steps
+    per CUDA graph."""
+    import torch
+
+    from glm53_flash_mlx_b200 import _native as N
+    from glm53_flash_mlx_b200 import ep
+    from glm53_flash_mlx_b200 import synthetic as S
+
+    dev = torch.device("cuda", local)
+    lib = N.lib()
+    n_exp = args.experts
+    layers = build_ep_layers(args.layers, rank, world, dev, n_exp)
+    xs = S.random_bf16((POOL, H), seed=77 + rank, device=dev)
+    plans = [ep.ExpertParallelDecode(L["bank"], experts=n_exp, rank=rank, world=world, shared=L["shared"],
+                                     limit=LIMIT, max_tokens=1, transport=args.ep_transport) for L in layers]
+    ws = N.Workspace()
+    rws = ws.get(dev, "router", lib.glm53_router_workspace_bytes(1, n_exp))
+    idxs = [torch.empty((1, TOP_K), dtype=torch.int32, device=dev) for _ in range(GRAPH_STEPS)]
+    scs = [torch.empty((1, TOP_K), dtype=torch.float32, device=dev) for _ in range(GRAPH_STEPS)]
+    outs = [torch.empty((1, H), dtype=torch.bfloat16, device=dev) for _ in range(GRAPH_STEPS)]
+
+    def step(i, stream):
+        L = layers[i % args.layers]
+        x = xs[i % POOL].reshape(1, H)
+        N.check(lib.glm53_router_topk(x.data_ptr(), 1, H, L["router_w"].data_ptr(), n_exp, L["router_b"].data_ptr(),
+                                      TOP_K, 1, 1, 1, 1.0, idxs[i].data_ptr(), scs[i].data_ptr(), None,
+                                      rws.data_ptr(), rws.numel(), stream), "router")
+        plans[i % args.layers](x, idxs[i], scs[i], out=outs[i])
+
+    s = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(s):
+        for i in range(GRAPH_STEPS):
+            step(i, s.cuda_stream)
+    s.synchronize()
+    barrier(world)
+    graph_mode = "64 EP decode steps per CUDA graph (NCCL all-to-alls captured)"
+    try:
+        full = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(full, stream=s):
+            for i in range(GRAPH_STEPS):
+                step(i, torch.cuda.current_stream().cuda_stream)
+        rem_w, rem_t = args.warmup % GRAPH_STEPS, args.steps % GRAPH_STEPS
+        rem = {}
+        for n in sorted({rem_w, rem_t} - {0}):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                for i in range(n):
+                    step(i, torch.cuda.current_stream().cuda_stream)
+            rem[n] = g
+
+        def run(k):
+            for _ in range(k // GRAPH_STEPS):
+                full.replay()
+            if k % GRAPH_STEPS:
+                rem[k % GRAPH_STEPS].replay()
+    except Exception:  # capture unsupported: eager steps on the side stream
+        full, rem = None, {}
+        graph_mode = "eager EP decode steps (graph capture unavailable)"
+
+        def run(k):
+            with torch.cuda.stream(s):
+                for i in range(k):
+                    step(i % GRAPH_STEPS, s.cuda_stream)
+
+    torch.cuda.synchronize()
+    barrier(world)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        run(args.warmup)
+        torch.cuda.synchronize()
+        barrier(world)
+        h0 = time.monotonic()
+        start.record()
+        run(args.steps)
+        stop.record()
+        torch.cuda.synchronize()
+        h1 = time.monotonic()
+        barrier(world)
+    t_ms = max_over_ranks(start.elapsed_time(stop), world)
+    bad = max_over_ranks(float(max(int(p.status.item()) for p in plans)), world)
+    if bad:
+        raise RuntimeError(f"device status 0x{int(bad):x} during the timed region")
+    clk = clocks.summary(h0, h1)
+    tokens = args.steps * world
+    value = tokens / (t_ms / 1e3)
+    peaks = measured_peaks()
+    step_s = t_ms / args.steps / 1e3
+    roofline = {"kernel": "EP decode step (per rank: ~8 received routes + shared + router)", "bound": "hbm",
+                "achieved": round(STEP_BYTES / step_s / 1e9, 1), "peak": peaks["hbm_gbs"],
+                "peak_source": peaks["source"], "unit": "GB/s",
+                "frac": round(STEP_BYTES / step_s / 1e9 / peaks["hbm_gbs"], 4), "traffic": None,
+                "algorithmic_bytes_per_launch": STEP_BYTES,
+                "note": "per-rank bytes of an average step: world tokens x 8 routes spread over world ranks"}
+    # release the graphs (they hold NCCL work) before any later teardown
+    rem.clear()
+    del full, run
+    torch.cuda.synchronize()
+    # e2e: the module API with host copies, every rank one token per step
+    e2e = None
+    if not args.no_e2e:
+        from types import SimpleNamespace
+
+        from glm53_flash_mlx_b200.router import Float32Gate
+
+        cfg = SimpleNamespace(hidden_size=H, moe_intermediate_size=I, swiglu_limit=LIMIT, n_routed_experts=n_exp,
+                              num_experts_per_tok=TOP_K)
+        mods = []
+        for L in layers:
+            gate = Float32Gate(cfg, device=dev)
+            gate.weight.copy_(L["router_w"])
+            gate.e_score_correction_bias.copy_(L["router_b"])
+            mods.append(ep.ExpertParallelMoE(L["bank"], cfg, gate, L["shared_mod"], rank=rank, world=world,
+                                             transport=args.ep_transport))
+        hx = xs.cpu().pin_memory()
+        hout = torch.empty((1, H), dtype=torch.bfloat16).pin_memory()
+        n_e2e = min(args.steps, 2000)
+        for i in range(min(args.warmup, 50)):
+            mods[i % len(mods)](hx[i % POOL].reshape(1, H).to(dev, non_blocking=True))
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(n_e2e):
+            y = mods[i % len(mods)](hx[i % POOL].reshape(1, H).to(dev, non_blocking=True))
+            hout.copy_(y, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+        e2e = {"value": round(n_e2e * world / (e_ms / 1e3), 2), "unit": "tokens/s", "h2d_bytes_per_step": H * 2,
+               "d2h_bytes_per_step": H * 2, "api": "ExpertParallelMoE.__call__ (Float32Gate router)",
+               "steps": n_e2e}
+    for p in plans + ([m.plan for m in mods] if not args.no_e2e else []):
+        p.close()
+    launches = 5 if args.ep_transport == "p2p" else 8
+    return {"value": value, "t_ms": t_ms, "clocks": clk, "roofline": roofline, "e2e": e2e,
+            "gpu_launches": args.steps * launches, "graph": graph_mode + f"; transport {args.ep_transport}"}
+
+
 def bench_prefill(layers, dev, args):
     """Secondary: config 3 grouped prefill, T=2048, Zipf-skewed router bias."""
     import torch
@@ -495,15 +655,20 @@ def bench_reference(args, world, rank, local):
     }
 
 
-def config_block(args, world):
-    return {"workload": "config2: packed decode MoE layer, L=1, batch 1 (router + top-8 of 288 + shared)",
+def config_block(args, world, graph=None):
+    workload = ("config2: packed decode MoE layer, L=1, batch 1 (router + top-8 of 288 + shared)" if world == 1 else
+                f"config2 layer expert-parallel over {world} GPUs (config 4 at batch 1 per rank): {E // world} "
+                "experts per GPU, router and shared expert replicated; dispatch and combine as NVLink peer-memory "
+                "stores with arrival counters (CUDA IPC buffers)")
+    return {"workload": workload,
             "hidden": H, "moe_intermediate": I, "experts": E, "top_k": TOP_K, "swiglu_limit": LIMIT,
             "weights": "E4M3 + FP32 128x128 block scales, seeded N(0,0.02) amax/448",
             "global_batch": 1 * world, "seq_len": 1,
             "l2": f"inputs larger than L2: {args.layers} distinct layers rotated "
-                  f"({args.layers * 5.44:.1f} GB of experts) and a {POOL}-vector activation pool; no flush",
-            "graph": f"{GRAPH_STEPS} decode steps (router + decode each, stream-ordered) per CUDA graph",
-            "parallelism": f"replicas{world}" if world > 1 else "single"}
+                  f"({args.layers * 5.44 / world:.1f} GB of experts per GPU) and a {POOL}-vector activation pool; "
+                  "no flush",
+            "graph": graph or f"{GRAPH_STEPS} decode steps (router + decode each, stream-ordered) per CUDA graph",
+            "parallelism": f"ep{world}" if world > 1 else "single"}
 
 
 def main():
@@ -525,7 +690,11 @@ def main():
         if rank == 0:
             print(json.dumps({"prefill_2048": bench_prefill(layers, dev, args)}), flush=True)
         return
-    res, layers, xs = bench_b200(args, world, rank, local)
+    if world > 1:
+        res = bench_ep(args, world, rank, local)
+        layers = xs = None
+    else:
+        res, layers, xs = bench_b200(args, world, rank, local)
     line = {
         "metric": "FP8 MoE decode layer tokens/s (L=1, batch 1)",
         "value": round(res["value"], 2),
@@ -539,7 +708,7 @@ def main():
         "vs_baseline": None,
         "dtype": "e4m3xbf16->f32",
         "data": "synthetic (seeded random-init weights of the config-2 shapes)",
-        "config": config_block(args, world),
+        "config": config_block(args, world, res.get("graph")),
         "clocks": res["clocks"],
         "roofline": res["roofline"],
         "e2e": res["e2e"],

@@ -72,6 +72,21 @@ SIGNATURES: dict[str, tuple] = {
         [_vp, _i64, _i64, _vp, _vp, _int, _i64, _int, _i64, _vp, _vp, _vp, _vp, _vp, _vp],
     ),
     "glm53_ep_combine": (_int, [_vp, _vp, _vp, _i64, _int, _i64, _vp, _vp, _vp]),
+    "glm53_ep_shared_bytes": (_sz, [_int, _i64, _i64]),
+    "glm53_ep_buffer_alloc": (_int, [_sz, _vp, _vp]),
+    "glm53_ep_buffer_free": (_int, [_vp]),
+    "glm53_ep_ipc_open": (_int, [_vp, _vp]),
+    "glm53_ep_ipc_close": (_int, [_vp]),
+    "glm53_ep_dispatch_p2p": (
+        _int,
+        [_vp, _i64, _i64, _vp, _vp, _int, _i64, _int, _int, _i64, _vp, _vp, _vp, _vp, _vp, _vp],
+    ),
+    "glm53_ep_owner_decode_p2p": (
+        _int,
+        [_vp, _i64, _int, _i64, _int, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp,
+         _i64, _vp, _f, _vp, _vp, _sz, _vp, _u32, _vp],
+    ),
+    "glm53_ep_combine_p2p": (_int, [_vp, _vp, _vp, _i64, _int, _i64, _int, _i64, _vp, _vp, _vp, _vp]),
     "glm53_packed_decode_gate_up": (
         _int,
         [_vp, _i64, _vp, _int, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _f, _vp, _sz, _vp, _u32, _vp],

@@ -92,4 +92,48 @@ int rows_to_f16(const uint16_t* x, int64_t H, const uint32_t* order, int div, in
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// Peer-memory expert parallelism: every rank allocates one buffer of this
+// layout and maps every peer's (CUDA IPC).  Slot (src, s) of recv_x/recv_e is
+// written by rank src; slot (owner, s) of back by rank owner; the counters
+// only grow (one per arriving CTA), the epoch counts this rank's steps.
+struct EpLayout {
+  size_t recv_x, recv_e, back, cnt_dispatch, cnt_back, epoch, done, bytes;
+};
+
+inline EpLayout ep_layout(int world, int cap, int64_t H) {
+  EpLayout l;
+  const size_t slots = (size_t)world * cap;
+  l.recv_x = 0;
+  l.recv_e = align_up(slots * H * 2, 256);
+  l.back = l.recv_e + align_up(slots * 4, 256);
+  l.cnt_dispatch = l.back + align_up(slots * H * 2, 256);
+  l.cnt_back = l.cnt_dispatch + 256;
+  l.epoch = l.cnt_back + 256;
+  l.done = l.epoch + 256;
+  l.bytes = l.done + 256;
+  return l;
+}
+
+// Bounded wait of one thread until *counter >= target (system-scope acquire);
+// false (and GLM53_STATUS_WAIT_TIMEOUT) after about two seconds.
+__device__ __forceinline__ bool wait_counter_geq(const unsigned long long* counter, unsigned long long target,
+                                                 uint32_t* status) {
+  unsigned long long t0 = 0;
+  for (uint32_t it = 0;; ++it) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(counter) : "memory");
+    if (v >= target) return true;
+    if ((it & 255u) == 255u) {
+      unsigned long long now;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > 2000000000ull) {
+        atomicOr(status, kStatusWaitTimeout);
+        return false;
+      }
+    }
+  }
+}
+
 }  // namespace glm53

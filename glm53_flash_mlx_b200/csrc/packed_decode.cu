@@ -67,9 +67,30 @@ struct DecodeArgs {
   // slots whose expert id is kEmptySlot are skipped
   int64_t x_stride;
   uint16_t* route_out;
+  // peer-memory expert parallelism (per-route mode): the slots arrive from
+  // other GPUs; gate/up waits until *arrivals >= (*epoch + 1) * arrivals_per_step
+  // before reading them, and down writes slot j = (home, s) to the home rank's
+  // back buffer at slot (rank, s), then counts one arrival there per CTA
+  const unsigned long long* arrivals;
+  const unsigned long long* epoch;
+  unsigned long long arrivals_per_step;
+  const unsigned long long* peer_base;  // [world] buffer bases (device pointers)
+  int64_t back_off, back_cnt_off;
+  int rank, cap;
+  // per-route mode: n_shared shared-expert slots after the routed ones, slot
+  // top_k + t reading shared_x + t * H and writing shared_out + t * H
+  int n_shared;
+  const uint16_t* shared_x;
+  uint16_t* shared_out;
 };
 
 constexpr uint32_t kEmptySlot = 0xFFFFFFFFu;
+
+// Shared-expert slots: one (sharing x) in the packed decode, n_shared in the
+// per-route modes.
+__host__ __device__ __forceinline__ int shared_slots(const DecodeArgs& a) {
+  return a.Is > 0 ? (a.n_shared > 0 ? a.n_shared : 1) : 0;
+}
 
 __host__ __device__ __forceinline__ int align16i(int v) { return (v + 15) & ~15; }
 
@@ -114,9 +135,11 @@ __device__ __forceinline__ GateUpRows gate_up_rows(const DecodeArgs& a, int unit
       r.su = r.sg + (size_t)half * cols;
     }
   } else {
-    const int r0 = (unit - routed) << 3;
+    const int per_s = a.Is >> 3;
+    const int u2 = unit - routed, t = u2 / per_s;
+    const int r0 = (u2 - t * per_s) << 3;
     r.valid = true;
-    r.hoff = a.top_k * a.I + r0;
+    r.hoff = a.top_k * a.I + t * a.Is + r0;
     r.g = a.sg_w + (size_t)r0 * a.H;
     r.u = a.su_w + (size_t)r0 * a.H;
     r.sg = a.sg_s + (size_t)(r0 >> 7) * cols;
@@ -133,13 +156,20 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_gate_up_v4(DecodeA
   uint4* ring = reinterpret_cast<uint4*>(smem) + (size_t)warp * P * 64;
   __half* xs = reinterpret_cast<__half*>(reinterpret_cast<uint4*>(smem) + (size_t)kWarpsPerBlock * P * 64);
   float* scratch = reinterpret_cast<float*>(xs + align16i(a.H + 8));
-  const int nunits = a.top_k * (a.I >> 3) + (a.Is >> 3);
+  const int routed_units = a.top_k * (a.I >> 3);
+  const int nunits = routed_units + shared_slots(a) * (a.Is >> 3);
   const int unit = blockIdx.x * kWarpsPerBlock + warp;
   const bool active = unit < nunits;
+  // every unit of a block belongs to one slot (I/8 and I_shared/8 are
+  // multiples of 4 here)
+  const int unit0 = blockIdx.x * kWarpsPerBlock;
+  const int jb = unit0 < routed_units ? unit0 / (a.I >> 3) : a.top_k + (unit0 - routed_units) / (a.Is >> 3);
+  if (a.arrivals && jb < a.top_k) {  // peer-memory dispatch: wait for every rank's slots
+    if (threadIdx.x == 0) wait_counter_geq(a.arrivals, (*a.epoch + 1ull) * a.arrivals_per_step, a.status);
+    __syncthreads();
+  }
   // the down stage may launch now: its prologue only streams weights
   pdl_trigger();
-  // every unit of a block belongs to one slot (I/8 is a multiple of 4 here)
-  const int jb = (int)(blockIdx.x * kWarpsPerBlock) / (a.I >> 3);
   if (a.route_out && jb < a.top_k && a.ids[jb] == kEmptySlot) return;
   GateUpRows rw{};
   if (active) rw = gate_up_rows(a, unit);
@@ -160,7 +190,8 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_gate_up_v4(DecodeA
   WarpScales ssg, ssu;
   ssg.load(rw.sg, a.H >> 7, ld);
   ssu.load(rw.su, a.H >> 7, ld);
-  const uint16_t* xb = a.x + (jb < a.top_k ? (size_t)jb * a.x_stride : 0);
+  const uint16_t* xb = jb < a.top_k ? a.x + (size_t)jb * a.x_stride
+                                    : (a.shared_x ? a.shared_x + (size_t)(jb - a.top_k) * a.H : a.x);
   const float smul = decode_unscale<FINITE>() * stage_f16(xs, a.H + 8, xb, 0, 1, a.H, scratch);
   float part[4] = {0.f, 0.f, 0.f, 0.f}, tot[4] = {0.f, 0.f, 0.f, 0.f};
   for (int sl = 0; sl < nslice; ++sl) {
@@ -183,12 +214,93 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_gate_up_v4(DecodeA
 // Down + slot-ordered reduce + shared add
 // ---------------------------------------------------------------------------
 
+// Down stage of one CTA in peer-memory mode (all four warps on slot jb).  A
+// routed slot arrived from rank jb / cap: its expert id is read after an
+// acquire of the arrival counter (which gate/up already saw complete), the
+// weights start streaming, and only then does the CTA wait for the gate/up
+// grid; the BF16 rows go straight into the home rank's back buffer and one
+// arrival per CTA is counted there (empty slots count too).  Shared-expert
+// slots (jb >= top_k) write their rows locally and count nothing.
+template <bool FINITE>
+__device__ __forceinline__ void decode_down_peer(const DecodeArgs& a, int jb) {
+  constexpr int P = kRing;
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+  const int K = a.I;
+  uint4* ring = reinterpret_cast<uint4*>(smem) + (size_t)warp * P * 64;
+  __half* xs = reinterpret_cast<__half*>(reinterpret_cast<uint4*>(smem) + (size_t)kWarpsPerBlock * P * 64);
+  float* scratch = reinterpret_cast<float*>(xs + align16i(K + 8));
+  const int rtiles = a.H >> 4;
+  const int tile = blockIdx.x * kWarpsPerBlock + warp - jb * rtiles;
+  const int row0 = tile << 4;
+  const int cols = K >> 7;
+  const bool routed = jb < a.top_k;
+  const int home = routed ? jb / a.cap : 0, s = routed ? jb - home * a.cap : 0;
+  char* hb = reinterpret_cast<char*>(routed ? a.peer_base[home] : 0ull);
+  uint32_t e = 0;
+  if (routed) {
+    if (threadIdx.x == 0) wait_counter_geq(a.arrivals, (*a.epoch + 1ull) * a.arrivals_per_step, a.status);
+    __syncthreads();
+    e = a.ids[jb];
+  }
+  if (e != kEmptySlot) {  // uniform over the CTA
+    const bool valid = !routed || e < (uint32_t)a.E;
+    const uint32_t es = valid ? e : 0u;
+    const uint8_t* w0 = routed ? a.d_w + ((size_t)es * a.H + row0) * K : a.sd_w + (size_t)row0 * K;
+    const float* srow = routed ? a.d_s + ((size_t)es * (a.H >> 7) + (row0 >> 7)) * cols
+                               : a.sd_s + (size_t)(row0 >> 7) * cols;
+    const uint8_t* p0 = w0 + (size_t)g * K + 16 * q;
+    const uint8_t* p8 = w0 + (size_t)(g + 8) * K + 16 * q;
+    const int nslice = K >> 6;
+    auto issue = [&](int sl) {
+      uint4* d = ring + (sl % P) * 64 + lane;
+      cp_async_16(d, valid ? (const void*)(p0 + 64 * sl) : (const void*)a.x, valid);
+      cp_async_16(d + 32, valid ? (const void*)(p8 + 64 * sl) : (const void*)a.x, valid);
+    };
+#pragma unroll
+    for (int k = 0; k < P - 1; ++k) {
+      if (k < nslice) issue(k);
+      cp_async_commit_group();
+    }
+    WarpScales sd;
+    sd.load(srow, cols, valid);
+    pdl_wait();  // the hidden rows come from the gate/up grid
+    const float smul =
+        decode_unscale<FINITE>() * stage_f16(xs, K + 8, a.hidden + (size_t)jb * a.I, 0, 1, K, scratch);
+    float part[4] = {0.f, 0.f, 0.f, 0.f}, tot[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int sl = 0; sl < nslice; ++sl) {
+      if (sl + P - 1 < nslice) issue(sl + P - 1);
+      cp_async_commit_group();
+      cp_async_wait_group<P - 1>();
+      const uint4* src = ring + (sl % P) * 64 + lane;
+      const uint4 f0 = src[0], f8 = src[32];
+      uint32_t xw[8];
+      load_x_frag(xw, xs + 64 * sl + 16 * q, g == 0);
+      mma_slice<FINITE>(part, f0, f8, xw);
+      if ((sl & 1) && valid) promote(tot, part, sd.at(sl >> 1) * smul);
+    }
+    cp_async_wait_group<0>();
+    if (q == 0) {
+      uint16_t* dst = routed ? reinterpret_cast<uint16_t*>(hb + a.back_off) + ((size_t)a.rank * a.cap + s) * a.H
+                             : a.shared_out + (size_t)(jb - a.top_k) * a.H;
+      dst[row0 + g] = valid ? f32_to_bf16_bits(tot[0]) : (uint16_t)0;
+      dst[row0 + g + 8] = valid ? f32_to_bf16_bits(tot[2]) : (uint16_t)0;
+    }
+    if (!valid && lane == 0) atomicOr(a.status, kStatusBadExpert);
+  }
+  if (routed) {
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) atomicAdd(reinterpret_cast<unsigned long long*>(hb + a.back_cnt_off), 1ull);
+  }
+}
+
 template <bool FINITE>
 __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_down_v4(DecodeArgs a) {
   constexpr int P = kRing;
   extern __shared__ __align__(16) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
-  const int ns = a.top_k + (a.Is > 0 ? 1 : 0);
+  const int ns = a.top_k + shared_slots(a);
   const int K = a.I;  // I_shared == I on this path
   uint4* ring = reinterpret_cast<uint4*>(smem) + (size_t)warp * P * 64;
   __half* xs = reinterpret_cast<__half*>(reinterpret_cast<uint4*>(smem) + (size_t)kWarpsPerBlock * P * 64);
@@ -203,12 +315,16 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_down_v4(DecodeArgs
   const int cols = K >> 7;
   // every unit of a block belongs to one slot (H/16 is a multiple of 4 here)
   const int jb = min((int)(blockIdx.x * kWarpsPerBlock) / rtiles, ns - 1);
-  if (a.route_out && a.ids[jb] == kEmptySlot) return;
+  if (a.peer_base) {
+    decode_down_peer<FINITE>(a, jb);
+    return;
+  }
+  if (a.route_out && jb < a.top_k && a.ids[jb] == kEmptySlot) return;
   bool valid = active;
   const uint8_t* w0 = nullptr;
   const float* srow = nullptr;
   if (active) {
-    if (j == a.top_k) {
+    if (j >= a.top_k) {
       w0 = a.sd_w + (size_t)row0 * K;
       srow = a.sd_s + (size_t)(row0 >> 7) * cols;
     } else if (a.table) {
@@ -257,9 +373,10 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_down_v4(DecodeArgs
   cp_async_wait_group<0>();
   if (!active) return;
   if (a.route_out) {  // per-route mode: this slot's BF16 down rows, as K6 stores them
+    uint16_t* dst = j < a.top_k ? a.route_out + (size_t)j * a.H : a.shared_out + (size_t)(j - a.top_k) * a.H;
     if (q == 0) {
-      a.route_out[(size_t)j * a.H + row0 + g] = valid ? f32_to_bf16_bits(tot[0]) : (uint16_t)0;
-      a.route_out[(size_t)j * a.H + row0 + g + 8] = valid ? f32_to_bf16_bits(tot[2]) : (uint16_t)0;
+      dst[row0 + g] = valid ? f32_to_bf16_bits(tot[0]) : (uint16_t)0;
+      dst[row0 + g + 8] = valid ? f32_to_bf16_bits(tot[2]) : (uint16_t)0;
     }
     if (!valid && lane == 0) atomicOr(a.status, kStatusBadExpert);
     return;
@@ -444,7 +561,7 @@ static int launch_v4(const DecodeArgs& a, cudaStream_t st, bool gate_up_only) {
       int rc = ensure_max_smem((const void*)decode_gate_up_v4<FINITE>, smem);
       if (rc) return rc;
     }
-    const int units = a.top_k * (a.I >> 3) + (a.Is >> 3);
+    const int units = a.top_k * (a.I >> 3) + shared_slots(a) * (a.Is >> 3);
     launch_decode(decode_gate_up_v4<FINITE>, (units + kWarpsPerBlock - 1) / kWarpsPerBlock, smem, st, false, a);
     int rc = check_launch("decode_gate_up_v4");
     if (rc || gate_up_only) return rc;
@@ -454,7 +571,7 @@ static int launch_v4(const DecodeArgs& a, cudaStream_t st, bool gate_up_only) {
     int rc = ensure_max_smem((const void*)decode_down_v4<FINITE>, smem);
     if (rc) return rc;
   }
-  const int ns = a.top_k + (a.Is > 0 ? 1 : 0);
+  const int ns = a.top_k + shared_slots(a);
   const int units = ns * (a.H >> 4);
   // the previous kernel is always this call's gate/up stage
   launch_decode(decode_down_v4<FINITE>, (units + kWarpsPerBlock - 1) / kWarpsPerBlock, smem, st, true, a);
@@ -671,6 +788,77 @@ extern "C" int glm53_routes_decode(const void* x_rows, int64_t R, int64_t H, con
   a.x_stride = H;
   a.route_out = (uint16_t*)out_rows;
   if (!tensor_core_shape(a) || (((uintptr_t)out_rows) & 15) != 0) {
+    set_last_error("%s: H and I must be multiples of 128 with 16-byte aligned tensors", fn);
+    return GLM53_ERR_INVALID;
+  }
+  return packed_decode(a, (cudaStream_t)stream, false, flags);
+}
+
+extern "C" int glm53_ep_owner_decode_p2p(void* buffer, int64_t H, int world, int64_t capacity, int rank,
+                                         const uint8_t* gate_up_w, const float* gate_up_s, const uint8_t* down_w,
+                                         const float* down_s, int64_t E, int64_t I, const void* shared_x,
+                                         int64_t T_shared, const uint8_t* shared_gate_w, const float* shared_gate_s,
+                                         const uint8_t* shared_up_w, const float* shared_up_s,
+                                         const uint8_t* shared_down_w, const float* shared_down_s, int64_t I_shared,
+                                         void* shared_out, float limit, const unsigned long long* peer_base,
+                                         void* workspace, size_t workspace_bytes, uint32_t* status, uint32_t flags,
+                                         void* stream) {
+  const char* fn = "glm53_ep_owner_decode_p2p";
+  const bool has_shared = I_shared > 0 && T_shared > 0;
+  if (world < 1 || world > 32 || rank < 0 || rank >= world || capacity <= 0 || H <= 0 || H % 64 != 0 || I <= 0 ||
+      E <= 0 || (int64_t)world * capacity > (1 << 20) || H > INT32_MAX / 2 || I > INT32_MAX / 64 || T_shared < 0 ||
+      T_shared > (1 << 16) || (has_shared && I_shared != I)) {
+    set_last_error("%s: invalid geometry", fn);
+    return GLM53_ERR_INVALID;
+  }
+  const int64_t R = (int64_t)world * capacity;
+  if (!buffer || !gate_up_w || !gate_up_s || !down_w || !down_s || !peer_base || !status || !workspace ||
+      workspace_bytes < glm53_routes_decode_workspace_bytes(R + (has_shared ? T_shared : 0), H, I) ||
+      (has_shared && (!shared_x || !shared_gate_w || !shared_gate_s || !shared_up_w || !shared_up_s ||
+                      !shared_down_w || !shared_down_s || !shared_out))) {
+    set_last_error("%s: missing pointer or workspace too small", fn);
+    return GLM53_ERR_INVALID;
+  }
+  const EpLayout lay = ep_layout(world, (int)capacity, H);
+  char* b = (char*)buffer;
+  DecodeArgs a{};
+  a.x = (const uint16_t*)(b + lay.recv_x);
+  a.H = (int)H;
+  a.I = (int)I;
+  a.Is = 0;
+  a.top_k = (int)R;
+  a.E = (int)std::min<int64_t>(E, INT32_MAX);
+  a.ids = (const uint32_t*)(b + lay.recv_e);
+  a.gu_w = gate_up_w;
+  a.gu_s = gate_up_s;
+  a.d_w = down_w;
+  a.d_s = down_s;
+  a.limit = limit;
+  a.hidden = (uint16_t*)workspace;
+  a.status = status;
+  a.x_stride = H;
+  a.route_out = (uint16_t*)(b + lay.back);  // marks per-route mode; rows go to the homes
+  a.arrivals = (const unsigned long long*)(b + lay.cnt_dispatch);
+  a.epoch = (const unsigned long long*)(b + lay.epoch);
+  a.arrivals_per_step = (unsigned long long)R;
+  a.peer_base = peer_base;
+  a.back_off = (int64_t)lay.back;
+  a.back_cnt_off = (int64_t)lay.cnt_back;
+  a.rank = rank;
+  a.cap = (int)capacity;
+  if (has_shared) {  // the home tokens' shared expert rides in the same launches
+    a.Is = (int)I_shared;
+    a.n_shared = (int)T_shared;
+    a.shared_x = (const uint16_t*)shared_x;
+    a.shared_out = (uint16_t*)shared_out;
+    a.sg_w = shared_gate_w;
+    a.sg_s = shared_gate_s;
+    a.su_w = shared_up_w;
+    a.su_s = shared_up_s;
+    a.sd_w = shared_down_w;
+    a.sd_s = shared_down_s;
+  }
+  if (!tensor_core_shape(a) || (has_shared && (((uintptr_t)shared_x | (uintptr_t)shared_out) & 15) != 0)) {
     set_last_error("%s: H and I must be multiples of 128 with 16-byte aligned tensors", fn);
     return GLM53_ERR_INVALID;
   }

@@ -134,7 +134,7 @@ class ExpertParallelDecode:
     (NCCL for CUDA tensors); ``world == 1`` needs none."""
 
     def __init__(self, bank, *, experts: int, rank: int, world: int, shared, limit: float,
-                 group=None, max_tokens: int = 1, top_k: int = 8):
+                 group=None, max_tokens: int = 1, top_k: int = 8, transport: str = "p2p"):
         self.bank = (bank.gate_up_weight, bank.gate_up_scale_inv, bank.down_weight, bank.down_scale_inv)
         self.experts, self.rank, self.world, self.group = int(experts), int(rank), int(world), group
         lo, hi = expert_range(rank, world, experts)
@@ -145,6 +145,7 @@ class ExpertParallelDecode:
         self.max_tokens = int(max_tokens)
         self.capacity = self.max_tokens * self.top_k
         self.H = bank.hidden_size
+        self.shared = None if shared is None else tuple(t.contiguous() for t in shared)
         self.shared_bank = pack_shared_bank(shared)
         dev = bank.gate_up_weight.device
         self.device = dev
@@ -163,6 +164,60 @@ class ExpertParallelDecode:
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         self.flags = N.decode_flags(self.bank[0], self.bank[2])
         self.shared_flags = N.decode_flags(self.shared_bank[0], self.shared_bank[2]) if self.shared_bank else 0
+        if transport not in ("p2p", "nccl"):
+            raise ValueError(f"unknown transport {transport!r}")
+        self.transport = transport if world > 1 else "nccl"
+        self._buffer = None
+        self._opened: list[int] = []
+        if self.transport == "p2p":
+            self._setup_p2p()
+
+    def _setup_p2p(self) -> None:
+        """One buffer per rank, every peer's mapped through CUDA IPC."""
+        import ctypes
+
+        import torch.distributed as dist
+
+        lib = N.lib()
+        nbytes = lib.glm53_ep_shared_bytes(self.world, self.capacity, self.H)
+        if nbytes == 0:
+            raise ValueError("geometry unsupported by the peer-memory transport")
+        ptr = ctypes.c_void_p()
+        handle = (ctypes.c_char * 64)()
+        with torch.cuda.device(self.device):
+            N.check(lib.glm53_ep_buffer_alloc(nbytes, ctypes.byref(ptr), handle), "glm53_ep_buffer_alloc")
+            self._buffer = ptr.value
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=self.group)
+            bases = []
+            for d in range(self.world):
+                if d == self.rank:
+                    bases.append(self._buffer)
+                    continue
+                peer = ctypes.c_void_p()
+                N.check(lib.glm53_ep_ipc_open(ctypes.create_string_buffer(handles[d], 64), ctypes.byref(peer)),
+                        "glm53_ep_ipc_open")
+                self._opened.append(peer.value)
+                bases.append(peer.value)
+        self.peer_base = torch.tensor(np.array(bases, dtype=np.uint64).view(np.int64), device=self.device)
+        self.slot_route = torch.zeros(self.world * self.capacity, dtype=torch.int32, device=self.device)
+        dist.barrier(group=self.group)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (collective: every
+        rank calls it once, after its last step)."""
+        if self._buffer is None:
+            return
+        import torch.distributed as dist
+
+        lib = N.lib()
+        torch.cuda.synchronize(self.device)
+        for p in self._opened:
+            lib.glm53_ep_ipc_close(p)
+        self._opened = []
+        dist.barrier(group=self.group)
+        lib.glm53_ep_buffer_free(self._buffer)
+        self._buffer = None
 
     def _exchange(self, recv: torch.Tensor, send: torch.Tensor) -> None:
         if self.world == 1:
@@ -187,6 +242,8 @@ class ExpertParallelDecode:
         flat = flat.contiguous()
         if out is None:
             out = torch.empty((T, self.H), dtype=torch.bfloat16, device=self.device)
+        if self.transport == "p2p":
+            return self._call_p2p(lib, st, flat, T, ids, sc, out).reshape(x.shape)
         N.check(lib.glm53_ep_dispatch_pack(flat.data_ptr(), T, self.H, ids.data_ptr(), sc.data_ptr(), self.top_k,
                                            self.experts, self.world, self.capacity, self.send_x.data_ptr(),
                                            self.send_e.data_ptr(), self.slot_scores.data_ptr(),
@@ -206,3 +263,62 @@ class ExpertParallelDecode:
                                      self.top_k, self.H, shared_ptr, out.data_ptr(), st),
                 "glm53_ep_combine")
         return out.reshape(x.shape)
+
+
+    def _shared_rows(self, flat, T):
+        if self.shared_bank is None:
+            return None
+        routes_decode(flat, self.zero_ids[:T], self.shared_bank, limit=self.limit, out=self.shared_rows[:T],
+                      workspace=self.workspace, status=self.status, flags=self.shared_flags)
+        return self.shared_rows.data_ptr()
+
+    def _call_p2p(self, lib, st, flat, T, ids, sc, out):
+        gu_w, gu_s, d_w, d_s = self.bank
+        R = self.world * self.capacity
+        sh = self.shared
+        Ts = T if sh is not None else 0
+        ws = self.workspace.get(self.device, "routes",
+                                lib.glm53_routes_decode_workspace_bytes(R + Ts, self.H, gu_w.shape[1] // 2))
+        N.check(lib.glm53_ep_dispatch_p2p(flat.data_ptr(), T, self.H, ids.data_ptr(), sc.data_ptr(), self.top_k,
+                                          self.experts, self.world, self.rank, self.capacity,
+                                          self.peer_base.data_ptr(), self.slot_route.data_ptr(),
+                                          self.slot_scores.data_ptr(), self.route_pos.data_ptr(),
+                                          self.status.data_ptr(), st), "glm53_ep_dispatch_p2p")
+        sp = [N.ptr(t) for t in sh] if sh is not None else [None] * 6
+        Is = sh[0].shape[0] if sh is not None else 0
+        N.check(lib.glm53_ep_owner_decode_p2p(self._buffer, self.H, self.world, self.capacity, self.rank,
+                                              gu_w.data_ptr(), gu_s.data_ptr(), d_w.data_ptr(), d_s.data_ptr(),
+                                              gu_w.shape[0], gu_w.shape[1] // 2, flat.data_ptr(), Ts, *sp, Is,
+                                              self.shared_rows.data_ptr(), self.limit, self.peer_base.data_ptr(),
+                                              ws.data_ptr(), ws.numel(), self.status.data_ptr(),
+                                              self.flags & self.shared_flags if sh is not None else self.flags, st),
+                "glm53_ep_owner_decode_p2p")
+        shared_ptr = self.shared_rows.data_ptr() if sh is not None else None
+        N.check(lib.glm53_ep_combine_p2p(self._buffer, self.route_pos.data_ptr(), self.slot_scores.data_ptr(), T,
+                                         self.top_k, self.H, self.world, self.capacity, shared_ptr, out.data_ptr(),
+                                         self.status.data_ptr(), st), "glm53_ep_combine_p2p")
+        return out
+
+
+class ExpertParallelMoE(torch.nn.Module):
+    """Decode MoE layer run expert-parallel: this rank's ``gate`` (the full
+    router, replicated), its expert slice and the replicated shared expert.
+    ``forward(x)`` takes this rank's tokens ``[..., H]`` (at most
+    ``max_tokens``) and returns their layer outputs; every rank of the group
+    must call it the same number of times (the all-to-alls are collective)."""
+
+    def __init__(self, bank, config, gate, shared, *, rank: int, world: int, group=None, max_tokens: int = 1,
+                 transport: str = "p2p"):
+        super().__init__()
+        from .packed import shared_fp8_tensors
+
+        self.gate = gate
+        self.config = config
+        self.plan = ExpertParallelDecode(bank, experts=config.n_routed_experts, rank=rank, world=world,
+                                         shared=shared_fp8_tensors(shared), limit=config.swiglu_limit, group=group,
+                                         max_tokens=max_tokens, top_k=config.num_experts_per_tok,
+                                         transport=transport)
+
+    def forward(self, x):
+        indices, scores = self.gate(x)
+        return self.plan(x, indices, scores)

@@ -203,6 +203,49 @@ int glm53_ep_combine(const void* rows, const uint32_t* route_pos, const float* s
                      int64_t T, int top_k, int64_t H, const void* shared, void* out,
                      void* stream);
 
+/* Expert-parallel decode over peer memory (NVLink) — the transport that
+ * replaces the two all-to-alls.  No counterpart in the reference (single
+ * device).  Every rank allocates one buffer of glm53_ep_shared_bytes(world,
+ * capacity, H) bytes (glm53_ep_buffer_alloc, once per layer plan: zeroed,
+ * with its CUDA IPC handle, 64 bytes) and maps every peer's
+ * (glm53_ep_ipc_open); `peer_base` is a device array of the world buffer
+ * addresses as seen by this rank (its own at index rank).  Per step, on one
+ * stream: glm53_ep_dispatch_p2p (stores each route's token row and local
+ * expert id into its owner's buffer and counts the arrival there),
+ * glm53_ep_owner_decode_p2p (waits for every rank's slots of this step,
+ * decodes them, stores each BF16 row into its home rank's buffer; the home
+ * tokens' shared expert, shared_x [T_shared, H] -> shared_out BF16 rows, runs
+ * in the same launches and streams while the slots are in flight),
+ * glm53_ep_combine_p2p (waits for the rows, slot-ordered reduce + shared add,
+ * advances the step counter).  Every rank must run the same steps; each wait
+ * gives up after about two seconds with GLM53_STATUS_WAIT_TIMEOUT.
+ * slot_route [world * capacity] is scratch; slot_scores and route_pos are as
+ * in glm53_ep_dispatch_pack. */
+size_t glm53_ep_shared_bytes(int world, int64_t capacity, int64_t H);
+int glm53_ep_buffer_alloc(size_t bytes, void** ptr, void* ipc_handle);
+int glm53_ep_buffer_free(void* ptr);
+int glm53_ep_ipc_open(const void* ipc_handle, void** ptr);
+int glm53_ep_ipc_close(void* ptr);
+int glm53_ep_dispatch_p2p(const void* x, int64_t T, int64_t H, const uint32_t* expert_ids,
+                          const float* scores, int top_k, int64_t E, int world, int rank,
+                          int64_t capacity, const unsigned long long* peer_base,
+                          uint32_t* slot_route, float* slot_scores, uint32_t* route_pos,
+                          uint32_t* status, void* stream);
+int glm53_ep_owner_decode_p2p(void* buffer, int64_t H, int world, int64_t capacity, int rank,
+                              const uint8_t* gate_up_w, const float* gate_up_s,
+                              const uint8_t* down_w, const float* down_s, int64_t E, int64_t I,
+                              const void* shared_x, int64_t T_shared,
+                              const uint8_t* shared_gate_w, const float* shared_gate_s,
+                              const uint8_t* shared_up_w, const float* shared_up_s,
+                              const uint8_t* shared_down_w, const float* shared_down_s,
+                              int64_t I_shared, void* shared_out, float limit,
+                              const unsigned long long* peer_base, void* workspace,
+                              size_t workspace_bytes, uint32_t* status, uint32_t flags,
+                              void* stream);
+int glm53_ep_combine_p2p(void* buffer, const uint32_t* route_pos, const float* slot_scores,
+                         int64_t T, int top_k, int64_t H, int world, int64_t capacity,
+                         const void* shared, void* out, uint32_t* status, void* stream);
+
 /* Diagnostic: only the first stage of glm53_packed_decode_moe (fused
  * gate/up/SwiGLU of the selected experts and the shared expert); the BF16
  * hidden rows [top_k*I + I_shared] are left at the start of `workspace`.

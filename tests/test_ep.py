@@ -179,7 +179,7 @@ def test_expert_parallel_decode_virtual_ranks_bitwise(world, E, H, I):
     ids = torch.stack([torch.randperm(E, generator=gen)[:8] for _ in range(world * T)]).to(torch.int32).to(dev)
     sc = (torch.rand((world * T, 8), generator=gen) * 0.25 + 0.05).to(dev)
     plans = [ep.ExpertParallelDecode(ep.local_bank(bank, r, world), experts=E, rank=r, world=world, shared=shared,
-                                     limit=10.0, max_tokens=T) for r in range(world)]
+                                     limit=10.0, max_tokens=T, transport="nccl") for r in range(world)]
     outs = []
     # step by step across virtual ranks (each all-to-all = chunk transpose)
     from glm53_flash_mlx_b200 import _native as N
@@ -232,7 +232,7 @@ def test_expert_parallel_decode_world1_module_bitwise():
         assert torch.equal(out, _single_device(bank, shared, x, ids, sc, 10.0))
 
 
-def _nccl_rank(rank, world, port, result_dir):
+def _nccl_rank(rank, world, port, result_dir, transport):
     import torch.distributed as dist
 
     from glm53_flash_mlx_b200 import synthetic as S
@@ -252,12 +252,18 @@ def _nccl_rank(rank, world, port, result_dir):
         ids = torch.stack([torch.randperm(E, generator=gen)[:8] for _ in range(world * T)]).to(torch.int32).to(dev)
         sc = (torch.rand((world * T, 8), generator=gen) * 0.25 + 0.05).to(dev)
         plan = ep.ExpertParallelDecode(ep.local_bank(bank, rank, world), experts=E, rank=rank, world=world,
-                                       shared=shared, limit=10.0, max_tokens=T)
-        out = plan(x[rank * T:(rank + 1) * T], ids[rank * T:(rank + 1) * T], sc[rank * T:(rank + 1) * T])
-        want = torch.stack([packed_decode_moe(x[t], ids[t], sc[t], bank, shared, limit=10.0)
-                            for t in range(rank * T, (rank + 1) * T)])
-        torch.cuda.synchronize()
-        ok = bool(torch.equal(out, want)) and int(plan.status.item()) == 0
+                                       shared=shared, limit=10.0, max_tokens=T, transport=transport)
+        ok = True
+        for step in range(3):  # consecutive steps reuse the buffers and counters
+            sl = slice(rank * T, (rank + 1) * T)
+            xs = (x[sl] * (step + 1)).to(torch.bfloat16)
+            out = plan(xs, ids[sl], sc[sl])
+            want = torch.stack([packed_decode_moe(xs[t], ids[sl][t], sc[sl][t], bank, shared, limit=10.0)
+                                for t in range(T)])
+            torch.cuda.synchronize()
+            ok = ok and bool(torch.equal(out, want))
+        ok = ok and int(plan.status.item()) == 0
+        plan.close()
         with open(os.path.join(result_dir, f"ok{rank}"), "w") as f:
             f.write("1" if ok else "0")
     finally:
@@ -265,10 +271,12 @@ def _nccl_rank(rank, world, port, result_dir):
 
 
 @pytest.mark.gpu
-def test_expert_parallel_decode_over_nccl_two_gpus(tmp_path):
+@pytest.mark.parametrize("transport", ["nccl", "p2p"])
+def test_expert_parallel_decode_two_gpus(tmp_path, transport):
     import torch.multiprocessing as mp
 
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
-    mp.start_processes(_nccl_rank, args=(2, _free_port(), str(tmp_path)), nprocs=2, start_method="spawn")
+    mp.start_processes(_nccl_rank, args=(2, _free_port(), str(tmp_path), transport), nprocs=2,
+                       start_method="spawn")
     assert [(tmp_path / f"ok{r}").read_text() for r in range(2)] == ["1", "1"]
