@@ -23,6 +23,8 @@ GLM53_ERR_CUDA = 2
 GLM53_ERR_INDEX = 3
 
 FLAG_E4M3_FINITE = 1
+FLAG_SHARED_ONLY = 2
+FLAG_SKIP_SHARED = 4
 
 STATUS_BAD_EXPERT = 1
 STATUS_WAIT_TIMEOUT = 2

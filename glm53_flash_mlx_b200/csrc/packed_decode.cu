@@ -82,6 +82,11 @@ struct DecodeArgs {
   int n_shared;
   const uint16_t* shared_x;
   uint16_t* shared_out;
+  // split execution (GLM53_FLAG_SHARED_ONLY / GLM53_FLAG_SKIP_SHARED): the
+  // unit ranges each launch covers (end 0 = all), and the number of slot
+  // partials the last-arriver reduce waits for (0 = every slot)
+  int gu_begin, gu_end, dn_begin, dn_end, dn_expect;
+  bool dn_no_reduce;
 };
 
 constexpr uint32_t kEmptySlot = 0xFFFFFFFFu;
@@ -95,7 +100,8 @@ __host__ __device__ __forceinline__ int shared_slots(const DecodeArgs& a) {
 __host__ __device__ __forceinline__ int align16i(int v) { return (v + 15) & ~15; }
 
 constexpr int kWarpsPerBlock = 4;
-constexpr int kRing = 8;  // 64-wide K slices in flight per warp (1 KB each)
+constexpr int kRing = 8;       // gate/up: 64-wide K slices in flight per warp (1 KB each)
+constexpr int kRingDown = 12;  // down: its per-warp streams are short (I/64 slices), so deeper
 
 // ---------------------------------------------------------------------------
 // Gate / up / SwiGLU
@@ -157,12 +163,12 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_gate_up_v4(DecodeA
   __half* xs = reinterpret_cast<__half*>(reinterpret_cast<uint4*>(smem) + (size_t)kWarpsPerBlock * P * 64);
   float* scratch = reinterpret_cast<float*>(xs + align16i(a.H + 8));
   const int routed_units = a.top_k * (a.I >> 3);
-  const int nunits = routed_units + shared_slots(a) * (a.Is >> 3);
-  const int unit = blockIdx.x * kWarpsPerBlock + warp;
+  const int nunits = a.gu_end ? a.gu_end : routed_units + shared_slots(a) * (a.Is >> 3);
+  const int unit = a.gu_begin + blockIdx.x * kWarpsPerBlock + warp;
   const bool active = unit < nunits;
   // every unit of a block belongs to one slot (I/8 and I_shared/8 are
   // multiples of 4 here)
-  const int unit0 = blockIdx.x * kWarpsPerBlock;
+  const int unit0 = a.gu_begin + blockIdx.x * kWarpsPerBlock;
   const int jb = unit0 < routed_units ? unit0 / (a.I >> 3) : a.top_k + (unit0 - routed_units) / (a.Is >> 3);
   if (a.arrivals && jb < a.top_k) {  // peer-memory dispatch: wait for every rank's slots
     if (threadIdx.x == 0) wait_counter_geq(a.arrivals, (*a.epoch + 1ull) * a.arrivals_per_step, a.status);
@@ -223,7 +229,7 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_gate_up_v4(DecodeA
 // slots (jb >= top_k) write their rows locally and count nothing.
 template <bool FINITE>
 __device__ __forceinline__ void decode_down_peer(const DecodeArgs& a, int jb) {
-  constexpr int P = kRing;
+  constexpr int P = kRingDown;
   extern __shared__ __align__(16) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
   const int K = a.I;
@@ -297,7 +303,7 @@ __device__ __forceinline__ void decode_down_peer(const DecodeArgs& a, int jb) {
 
 template <bool FINITE>
 __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_down_v4(DecodeArgs a) {
-  constexpr int P = kRing;
+  constexpr int P = kRingDown;
   extern __shared__ __align__(16) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
   const int ns = a.top_k + shared_slots(a);
@@ -306,15 +312,15 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_down_v4(DecodeArgs
   __half* xs = reinterpret_cast<__half*>(reinterpret_cast<uint4*>(smem) + (size_t)kWarpsPerBlock * P * 64);
   float* scratch = reinterpret_cast<float*>(xs + align16i(K + 8));
   const int rtiles = a.H >> 4;
-  const int nunits = ns * rtiles;
-  const int unit = blockIdx.x * kWarpsPerBlock + warp;
+  const int nunits = a.dn_end ? a.dn_end : ns * rtiles;
+  const int unit = a.dn_begin + blockIdx.x * kWarpsPerBlock + warp;
   const bool active = unit < nunits;
   const int j = active ? unit / rtiles : 0;
   const int tile = unit - j * rtiles;
   const int row0 = tile << 4;
   const int cols = K >> 7;
   // every unit of a block belongs to one slot (H/16 is a multiple of 4 here)
-  const int jb = min((int)(blockIdx.x * kWarpsPerBlock) / rtiles, ns - 1);
+  const int jb = min((int)(a.dn_begin + blockIdx.x * kWarpsPerBlock) / rtiles, ns - 1);
   if (a.peer_base) {
     decode_down_peer<FINITE>(a, jb);
     return;
@@ -386,10 +392,12 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_down_v4(DecodeArgs
     a.partial[(size_t)j * a.H + row0 + g + 8] = valid ? tot[2] : 0.f;
   }
   if (!valid && lane == 0) atomicOr(a.status, kStatusBadExpert);
+  if (a.dn_no_reduce) return;  // shared-only pass: the partial waits in the workspace
   __syncwarp();
   __threadfence();
   unsigned last = 0;
-  if (lane == 0) last = atomicAdd(&a.counters[tile], 1u) == (unsigned)(ns - 1);
+  const int expect = a.dn_expect ? a.dn_expect : ns;
+  if (lane == 0) last = atomicAdd(&a.counters[tile], 1u) == (unsigned)(expect - 1);
   last = __shfl_sync(0xffffffffu, last, 0);
   if (!last) return;
   __threadfence();
@@ -561,24 +569,44 @@ static int launch_v4(const DecodeArgs& a, cudaStream_t st, bool gate_up_only) {
       int rc = ensure_max_smem((const void*)decode_gate_up_v4<FINITE>, smem);
       if (rc) return rc;
     }
-    const int units = a.top_k * (a.I >> 3) + shared_slots(a) * (a.Is >> 3);
+    const int units = (a.gu_end ? a.gu_end : a.top_k * (a.I >> 3) + shared_slots(a) * (a.Is >> 3)) - a.gu_begin;
     launch_decode(decode_gate_up_v4<FINITE>, (units + kWarpsPerBlock - 1) / kWarpsPerBlock, smem, st, false, a);
     int rc = check_launch("decode_gate_up_v4");
     if (rc || gate_up_only) return rc;
   }
-  const size_t smem = ring + (size_t)align16i(a.I + 8) * 2 + 32 * sizeof(float);
+  const size_t smem = (size_t)kWarpsPerBlock * kRingDown * 64 * 16 + (size_t)align16i(a.I + 8) * 2 + 32 * sizeof(float);
   if (smem > 48 * 1024) {
     int rc = ensure_max_smem((const void*)decode_down_v4<FINITE>, smem);
     if (rc) return rc;
   }
   const int ns = a.top_k + shared_slots(a);
-  const int units = ns * (a.H >> 4);
+  const int units = (a.dn_end ? a.dn_end : ns * (a.H >> 4)) - a.dn_begin;
   // the previous kernel is always this call's gate/up stage
   launch_decode(decode_down_v4<FINITE>, (units + kWarpsPerBlock - 1) / kWarpsPerBlock, smem, st, true, a);
   return check_launch("decode_down_v4");
 }
 
-int packed_decode(const DecodeArgs& a, cudaStream_t st, bool gate_up_only, uint32_t flags) {
+int packed_decode(const DecodeArgs& a_in, cudaStream_t st, bool gate_up_only, uint32_t flags) {
+  DecodeArgs a = a_in;
+  const bool shared_only = (flags & GLM53_FLAG_SHARED_ONLY) != 0, skip_shared = (flags & GLM53_FLAG_SKIP_SHARED) != 0;
+  if (shared_only || skip_shared) {
+    if ((shared_only && skip_shared) || a.Is <= 0 || a.route_out || a.table || !tensor_core_shape(a)) {
+      set_last_error("split decode: needs a shared expert, the tensor-core shapes, and one of the two flags");
+      return GLM53_ERR_INVALID;
+    }
+    const int routed_units = a.top_k * (a.I >> 3), rtiles = a.H >> 4;
+    if (shared_only) {  // the shared expert's gate/up and its down partial
+      a.gu_begin = routed_units;
+      a.gu_end = routed_units + (a.Is >> 3);
+      a.dn_begin = a.top_k * rtiles;
+      a.dn_end = (a.top_k + 1) * rtiles;
+      a.dn_no_reduce = true;
+    } else {  // the routed slots; the reduce adds the shared partial already in the workspace
+      a.gu_end = routed_units;
+      a.dn_end = a.top_k * rtiles;
+      a.dn_expect = a.top_k;
+    }
+  }
   if (!tensor_core_shape(a)) {
     const int items = a.top_k * a.I + a.Is;
     decode_gate_up_scalar_kernel<<<(items + 7) / 8, 256, 0, st>>>(a);

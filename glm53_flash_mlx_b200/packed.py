@@ -196,11 +196,14 @@ def shared_fp8_tensors(shared) -> tuple | None:
 
 def packed_decode_moe(x: torch.Tensor, expert_ids: torch.Tensor, scores: torch.Tensor, bank: PackedFP8ExpertBank,
                       shared: tuple | None, *, limit: float, workspace: N.Workspace | None = None,
-                      status: torch.Tensor | None = None) -> torch.Tensor:
+                      status: torch.Tensor | None = None, split: str | None = None) -> torch.Tensor | None:
     """One-token routed MoE (+ shared expert) over the packed bank.
 
     x: BF16 [H]; expert_ids: int32/uint32 [top_k]; scores: float32 [top_k].
-    Returns BF16 [H]."""
+    Returns BF16 [H].  ``split="shared"`` computes only the shared expert into
+    ``workspace`` (ids and scores unread, returns None); a later
+    ``split="routed"`` call on the same workspace, ordered after it, finishes
+    the layer (GLM53_FLAG_SHARED_ONLY / GLM53_FLAG_SKIP_SHARED)."""
     dev = N.require_cuda(x, expert_ids, scores, bank.gate_up_weight)
     H = bank.hidden_size
     I = bank.intermediate_size
@@ -217,6 +220,10 @@ def packed_decode_moe(x: torch.Tensor, expert_ids: torch.Tensor, scores: torch.T
         sg_w = sg_s = su_w = su_s = sd_w = sd_s = None
         Is = 0
     flags = N.decode_flags(bank.gate_up_weight, bank.down_weight, *(() if shared is None else (sg_w, su_w, sd_w)))
+    if split is not None:
+        if shared is None or split not in ("shared", "routed"):
+            raise ValueError("split decode needs a shared expert and split='shared' or 'routed'")
+        flags |= N.FLAG_SHARED_ONLY if split == "shared" else N.FLAG_SKIP_SHARED
     ws_bytes = N.lib().glm53_packed_decode_workspace_bytes(top_k, H, I, Is)
     wsp = workspace or N.Workspace()
     ws = wsp.get(dev, "decode", ws_bytes)
@@ -235,7 +242,7 @@ def packed_decode_moe(x: torch.Tensor, expert_ids: torch.Tensor, scores: torch.T
     )
     if _SYNC_STATUS:
         check_status(status)
-    return out
+    return None if split == "shared" else out
 
 
 def check_status(status: torch.Tensor, *, clear: bool = True) -> None:

@@ -45,6 +45,20 @@ extern "C" {
  * re-bias that also maps 0x7F/0xFF to +-480 as the reference table does. */
 #define GLM53_FLAG_E4M3_FINITE 1u
 
+/* `flags` bits of glm53_packed_decode_moe that split one decode into two
+ * calls on the same workspace, so that the shared expert (which needs no
+ * routing) can run on a second stream while the router runs:
+ * GLM53_FLAG_SHARED_ONLY computes only the shared expert (expert_ids and
+ * scores are not read) and leaves its down partial in the workspace;
+ * GLM53_FLAG_SKIP_SHARED then computes the routed slots and the final reduce,
+ * adding that partial.  The second call's down stage must be ordered after
+ * the first call (e.g. an event join).  Together they give the same bits as
+ * one call.  (Measured on B200 inside one CUDA graph with the router between
+ * them, the fork/join edges cost more than the overlap gains; the split is for
+ * callers that overlap the shared expert with longer work of their own.) */
+#define GLM53_FLAG_SHARED_ONLY 2u
+#define GLM53_FLAG_SKIP_SHARED 4u
+
 /* Kernel ABI identity string (replaces glm53_flash_mlx/abi.py:3-15 for the
  * CUDA kernels; part of any cache identity that depends on kernel numerics). */
 const char* glm53_kernel_abi(void);

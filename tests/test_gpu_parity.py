@@ -207,6 +207,32 @@ def test_packed_decode_config2_full_size(G, S, oracle):
         assert stats["bit_identical"] >= 0.95, stats
 
 
+def test_split_decode_matches_single_call_bitwise(G, S):
+    """GLM53_FLAG_SHARED_ONLY on a side stream + GLM53_FLAG_SKIP_SHARED after
+    the join give the bits of one glm53_packed_decode_moe call."""
+    from glm53_flash_mlx_b200 import _native as N
+    from glm53_flash_mlx_b200.packed import packed_decode_moe, shared_fp8_tensors
+
+    E, H, I = 16, 4096, 1536
+    bank = S.make_bank(E, H, I, seed=71, device="cuda")
+    shared = shared_fp8_tensors(S.make_shared(H, I, seed=72, device="cuda"))
+    gen = torch.Generator().manual_seed(73)
+    ws_full, ws_split = N.Workspace(), N.Workspace()
+    side = torch.cuda.Stream()
+    for t in range(3):
+        x = S.random_bf16((H,), seed=74 + t, device="cuda")
+        ids = torch.randperm(E, generator=gen)[:8].to(torch.int32).cuda()
+        sc = (torch.rand(8, generator=gen) * 0.25 + 0.05).cuda()
+        full = packed_decode_moe(x, ids, sc, bank, shared, limit=10.0, workspace=ws_full)
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            packed_decode_moe(x, ids, sc, bank, shared, limit=10.0, workspace=ws_split, split="shared")
+        torch.cuda.current_stream().wait_stream(side)
+        part = packed_decode_moe(x, ids, sc, bank, shared, limit=10.0, workspace=ws_split, split="routed")
+        torch.cuda.synchronize()
+        assert torch.equal(full, part), t
+
+
 def test_packed_moe_module_matches_direct_module_bitwise(G, S):
     """tests/test_fp8_metal.py:87-151: packed decode and 9-row prefill are
     bit-equal to the Direct module over the same expert tensors."""
