@@ -322,3 +322,10 @@ class ExpertParallelMoE(torch.nn.Module):
     def forward(self, x):
         indices, scores = self.gate(x)
         return self.plan(x, indices, scores)
+
+    def capture_decode(self):
+        """One-token expert-parallel decode as a replayable CUDA graph (every
+        rank captures and replays in the same order)."""
+        from .packed import CapturedDecode
+
+        return CapturedDecode(self, self.plan.H, self.plan.device)

@@ -259,6 +259,39 @@ def check_status(status: torch.Tensor, *, clear: bool = True) -> None:
         raise RuntimeError(f"device status 0x{word:x}")
 
 
+class CapturedDecode:
+    """One decode token through a MoE module (its gate, the decode kernels and
+    the shared expert) captured into a CUDA graph with static buffers.
+
+    ``step(x, out=None)`` copies ``x`` (host or device, ``hidden`` values) into
+    the static input, replays the graph on the current stream and returns the
+    static output (or copies it into ``out``, e.g. pinned host memory); the
+    static output is overwritten by the next call.  Every operation stays
+    stream-ordered, so host buffers may be pinned and the copies asynchronous.
+    """
+
+    def __init__(self, module: nn.Module, hidden: int, device):
+        device = torch.device(device)
+        self.x = torch.zeros((1, 1, hidden), dtype=torch.bfloat16, device=device)
+        side = torch.cuda.Stream(device=device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(side):  # buffers, scans and kernel attributes outside the capture
+            for _ in range(2):
+                module(self.x)
+        torch.cuda.current_stream(device).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=side):
+            self.out = module(self.x)
+
+    def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        self.x.copy_(x.reshape(self.x.shape), non_blocking=True)
+        self.graph.replay()
+        if out is None:
+            return self.out
+        out.copy_(self.out.reshape(out.shape), non_blocking=True)
+        return out
+
+
 class PackedFP8MoE(DirectFP8MoE):
     """Exact fused batch-1 decode and Direct semantics over a packed bank."""
 
@@ -279,6 +312,10 @@ class PackedFP8MoE(DirectFP8MoE):
     @property
     def status(self) -> torch.Tensor:
         return self._workspace.get(self.bank.gate_up_weight.device, "status", 4)
+
+    def capture_decode(self) -> CapturedDecode:
+        """This layer's one-token decode as a replayable CUDA graph."""
+        return CapturedDecode(self, self.bank.hidden_size, self.bank.gate_up_weight.device)
 
     def forward(self, x):
         flat_x = x.reshape(-1, x.shape[-1])

@@ -462,3 +462,25 @@ def test_exact_decode_handles_0x7f_as_480(G, oracle):
     x[0, 1] = 0.5
     y = G.block_fp8_linear(x, codes, s)
     assert torch.all(y.float() == 480.0 - 240.0)
+
+
+def test_captured_decode_matches_module_call(G, S):
+    """PackedFP8MoE.capture_decode() replays give the module's own bits."""
+    from glm53_flash_mlx_b200.router import Float32Gate
+
+    E, H, I = 16, 1024, 256
+    cfg = S.moe_config(H, I, E, 8, 10.0)
+    bank = S.make_bank(E, H, I, seed=81, device="cuda")
+    shared = S.make_shared(H, I, seed=82, device="cuda")
+    gate = Float32Gate(cfg, device="cuda")
+    w, b = S.make_router(E, H, seed=83, device="cuda")
+    gate.weight.copy_(w)
+    gate.e_score_correction_bias.copy_(b)
+    mod = G.PackedFP8MoE(bank, cfg, gate, shared)
+    cap = mod.capture_decode()
+    for t in range(3):
+        x = S.random_bf16((1, 1, H), seed=84 + t, device="cuda")
+        want = mod(x).clone()
+        got = cap(x.cpu().pin_memory()).clone()
+        torch.cuda.synchronize()
+        assert torch.equal(got, want), t
