@@ -278,6 +278,107 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(const uint16_t* __rest
   }
 }
 
+// Tensor-core FP32 router logits for T > 8 tokens.  x is BF16, hence exact
+// as a BF16 MMA operand; every FP32 weight splits exactly into three BF16
+// numbers w = hi + mid + lo (8 + 8 + 8 significant bits).  For each 16-wide
+// K slice three m16n8k16 BF16 MMAs with a zero accumulator give the slice's
+// exact products summed in FP32, and their sum is added into FP64
+// accumulators: the slice-then-FP64 scheme of router_gemm_kernel on the
+// tensor cores.  Block tile 64 tokens x 64 experts, 4 warps of 32 x 32.
+constexpr int kRmBT = 64, kRmBE = 64, kRmBK = 32;
+
+__device__ __forceinline__ void mma_16816_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Two FP32 values -> their exact three-part BF16 split, packed in pairs.
+__device__ __forceinline__ void split3_bf16x2(float a, float b, uint32_t& hi, uint32_t& mid, uint32_t& lo) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  const float ra = a - __low2float(h), rb = b - __high2float(h);
+  const __nv_bfloat162 m = __floats2bfloat162_rn(ra, rb);
+  const __nv_bfloat162 l = __floats2bfloat162_rn(ra - __low2float(m), rb - __high2float(m));
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  mid = *reinterpret_cast<const uint32_t*>(&m);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+__global__ void __launch_bounds__(128) router_mma_kernel(const uint16_t* __restrict__ x, int T, int H,
+                                                         const float* __restrict__ w, int E,
+                                                         float* __restrict__ logits) {
+  __shared__ __align__(16) uint16_t xs[kRmBT][kRmBK + 8];
+  __shared__ __align__(16) float ws[kRmBE][kRmBK + 4];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+  const int t0 = blockIdx.x * kRmBT, e0 = blockIdx.y * kRmBE;
+  const int wt = (warp >> 1) * 32, we = (warp & 1) * 32;
+  double acc[2][4][4];
+#pragma unroll
+  for (int m = 0; m < 2; ++m)
+#pragma unroll
+    for (int n = 0; n < 4; ++n)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[m][n][c] = 0.0;
+  for (int k0 = 0; k0 < H; k0 += kRmBK) {
+    for (int i = threadIdx.x; i < kRmBT * (kRmBK / 8); i += blockDim.x) {
+      const int r = i / (kRmBK / 8), c = i - r * (kRmBK / 8);
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (t0 + r < T) v = *reinterpret_cast<const uint4*>(x + (size_t)(t0 + r) * H + k0 + 8 * c);
+      *reinterpret_cast<uint4*>(&xs[r][8 * c]) = v;
+    }
+    for (int i = threadIdx.x; i < kRmBE * (kRmBK / 4); i += blockDim.x) {
+      const int r = i / (kRmBK / 4), c = i - r * (kRmBK / 4);
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (e0 + r < E) v = *reinterpret_cast<const float4*>(w + (size_t)(e0 + r) * H + k0 + 4 * c);
+      *reinterpret_cast<float4*>(&ws[r][4 * c]) = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < kRmBK; kk += 16) {
+      uint32_t a[2][4];
+#pragma unroll
+      for (int m = 0; m < 2; ++m) {
+        const int row = wt + 16 * m + g;
+        a[m][0] = *reinterpret_cast<const uint32_t*>(&xs[row][kk + 2 * q]);
+        a[m][1] = *reinterpret_cast<const uint32_t*>(&xs[row + 8][kk + 2 * q]);
+        a[m][2] = *reinterpret_cast<const uint32_t*>(&xs[row][kk + 2 * q + 8]);
+        a[m][3] = *reinterpret_cast<const uint32_t*>(&xs[row + 8][kk + 2 * q + 8]);
+      }
+#pragma unroll
+      for (int n = 0; n < 4; ++n) {
+        const float* wr = &ws[we + 8 * n + g][kk];
+        const float2 w0 = *reinterpret_cast<const float2*>(wr + 2 * q);
+        const float2 w1 = *reinterpret_cast<const float2*>(wr + 2 * q + 8);
+        uint32_t bh0, bm0, bl0, bh1, bm1, bl1;
+        split3_bf16x2(w0.x, w0.y, bh0, bm0, bl0);
+        split3_bf16x2(w1.x, w1.y, bh1, bm1, bl1);
+#pragma unroll
+        for (int m = 0; m < 2; ++m) {
+          float dh[4] = {0.f, 0.f, 0.f, 0.f}, dm[4] = {0.f, 0.f, 0.f, 0.f}, dl[4] = {0.f, 0.f, 0.f, 0.f};
+          mma_16816_bf16(dh, a[m], bh0, bh1);
+          mma_16816_bf16(dm, a[m], bm0, bm1);
+          mma_16816_bf16(dl, a[m], bl0, bl1);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) acc[m][n][c] += (double)(dh[c] + (dm[c] + dl[c]));
+        }
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int m = 0; m < 2; ++m)
+#pragma unroll
+    for (int n = 0; n < 4; ++n)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int t = t0 + wt + 16 * m + g + (c >= 2 ? 8 : 0);
+        const int e = e0 + we + 8 * n + 2 * q + (c & 1);
+        if (t < T && e < E) logits[(size_t)t * E + e] = (float)acc[m][n][c];
+      }
+}
+
 template <int PER>
 __global__ void __launch_bounds__(256) router_topk_kernel(const float* logits, int T,
                                                           const float* __restrict__ bias, TopkParams p,
@@ -361,8 +462,14 @@ extern "C" int glm53_router_topk(const void* x, int64_t T, int64_t H, const floa
     return launch_small<32>((const uint16_t*)x, (int)T, (int)H, w, bias, p, rs, indices, scores, st);
   }
   dim3 grid((unsigned)((T + 63) / 64), (unsigned)((E + 63) / 64));
-  router_gemm_kernel<<<grid, 256, 0, st>>>((const uint16_t*)x, (int)T, (int)H, w, (int)E, lbuf);
-  int rc = check_launch("router_gemm_kernel");
+  int rc;
+  if (H % kRmBK == 0 && (((uintptr_t)x | (uintptr_t)w) & 15) == 0) {
+    router_mma_kernel<<<grid, 128, 0, st>>>((const uint16_t*)x, (int)T, (int)H, w, (int)E, lbuf);
+    rc = check_launch("router_mma_kernel");
+  } else {
+    router_gemm_kernel<<<grid, 256, 0, st>>>((const uint16_t*)x, (int)T, (int)H, w, (int)E, lbuf);
+    rc = check_launch("router_gemm_kernel");
+  }
   if (rc) return rc;
   if (per <= 4) return launch_topk<4>(lbuf, (int)T, bias, p, indices, scores, st);
   if (per <= 10) return launch_topk<10>(lbuf, (int)T, bias, p, indices, scores, st);
