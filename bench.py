@@ -383,8 +383,49 @@ def bench_b200(args, world, rank, local):
                            "note": "router and gate/up each timed alone (64 calls per CUDA graph)"}}
     if not args.no_prefill:
         extra["prefill_2048"] = bench_prefill(layers, dev, args)
+        extra["linear_config1"] = bench_linear(dev, args)
     return {"value": value, "t_ms": t_ms, "clocks": clk, "roofline": roofline, "e2e": e2e,
             "gpu_launches": args.steps * 3, **extra}, layers, xs
+
+
+def bench_linear(dev, args):
+    """Secondary: config 1 (block-FP8 GEMV y = x . W^T, W E4M3 [6144, 4096] +
+    128x128 scales, x BF16 [1, 4096]) and the same weights at larger M
+    (config 5 shapes).  8 weight copies rotate (201 MB > L2); 64 calls per CUDA
+    graph, CUDA events."""
+    import torch
+
+    from glm53_flash_mlx_b200 import _native as N
+    from glm53_flash_mlx_b200 import synthetic as S
+
+    lib = N.lib()
+    Nn, K, copies = 6144, 4096, 8
+    ws = []
+    for c in range(copies):
+        w, sc = S.random_block_fp8(Nn, K, seed=c, tensor=0, std=0.02, device=dev)
+        ws.append((w, sc))
+    fl = N.decode_flags(*[w for w, _ in ws])
+    peaks = measured_peaks()
+    res = {}
+    s = torch.cuda.Stream(device=dev)
+    for M in (1, 8, 64, 512):
+        x = S.random_bf16((M, K), seed=M, device=dev)
+        y = torch.empty((M, Nn), dtype=torch.bfloat16, device=dev)
+
+        def call(i, stream):
+            w, sc = ws[i % copies]
+            N.check(lib.glm53_fp8_linear(x.data_ptr(), M, K, w.data_ptr(), Nn, sc.data_ptr(), y.data_ptr(), fl,
+                                         stream), "linear")
+
+        ms = time_stage_graph(call, 64, 8, s, dev)
+        bytes_ = Nn * K + 4 * (Nn // 128) * (K // 128) + 2 * M * K + 2 * M * Nn
+        flops = 2 * M * Nn * K
+        res[f"M{M}"] = {"us": round(ms * 1e3, 2), "gbs": round(bytes_ / (ms / 1e3) / 1e9, 1),
+                        "hbm_frac": round(bytes_ / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
+                        "tflops": round(flops / (ms / 1e3) / 1e12, 2)}
+    return {"shape": "W [6144, 4096] E4M3 + [48, 32] FP32 scales; x BF16 [M, 4096]; "
+                     "M=1 is config 1, M>1 the config-5 sweep of this shape",
+            "results": res, "note": "M <= 16: tensor-core GEMV tiles; M > 16: mma.sync tile GEMM (BF16 x lut*s)"}
 
 
 def build_ep_layers(n_layers: int, rank: int, world: int, device, experts: int = E):
@@ -723,6 +764,8 @@ def main():
         line["stages_us"] = res["stages_us"]
     if "prefill_2048" in res:
         line["prefill_2048"] = res["prefill_2048"]
+    if "linear_config1" in res:
+        line["linear_config1"] = res["linear_config1"]
     if rank == 0 and world == 1 and not args.no_cpu:
         import torch
 
