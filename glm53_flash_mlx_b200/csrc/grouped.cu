@@ -586,6 +586,7 @@ static int grouped_moe_tc(const MoeWorkspace& w, const void* x, int64_t T, int64
   gu.swiglu = true;
   gu.limit = limit;
   gu.finite = finite;
+  gu.scaled = false;
   gu.out = w.hidden;
   gu.status = status;
   rc = grouped_tc(gu, st);
@@ -633,6 +634,7 @@ static int grouped_moe_tc(const MoeWorkspace& w, const void* x, int64_t T, int64
     sg.swiglu = true;
     sg.limit = limit;
     sg.finite = finite;
+    sg.scaled = false;
     sg.out = w.shared_hidden;
     sg.status = status;
     rc = grouped_tc(sg, st);

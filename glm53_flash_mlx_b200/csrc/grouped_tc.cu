@@ -8,7 +8,8 @@
 // (expert, first route, routes <= 64) and one 128-row weight tile:
 //   warp 0      TMA producer: raw E4M3 weight tiles [128 rows x 128 K] and
 //               activation tiles [64 routes x 128 K] (FP16, 128-byte swizzle)
-//               into a 4-stage shared-memory ring;
+//               into two shared-memory rings of their own depths (the
+//               weight ring, fed from HBM, is the deeper one);
 //   warp 1      allocates TMEM and issues tcgen05.mma (kind::f16, A from TMEM,
 //               B from shared memory, FP32 accumulation in TMEM);
 //   warps 2-5   decode each weight row exactly to FP16 (lut(c), or lut(c)/256
@@ -22,7 +23,17 @@
 //               the reference's BF16 SwiGLU to a gate tile and its up tile.
 // Products of FP16 weights (4 significant bits) and FP16 activations are
 // exact in FP32, so each 128-K block sum differs from the reference's FP32
-// sum only in summation order.  Activations are the BF16 inputs converted to
+// sum only in summation order.
+//
+// Scaled mode (SCALED, the prefill default): the decode warps fold the
+// 128x128 block scale into the A operand, FP16(lut(c) * s_kb * 2^p) with one
+// power of two 2^p per weight tile that keeps every value below 2^15, so the
+// MMAs accumulate the whole K in TMEM and the epilogue reads each tile once
+// (undoing 2^p exactly).  Each weight then carries one FP16 rounding (relative
+// 2^-11) and the per-block promotion round trip (MMA -> TMEM load -> FMA ->
+// release, two accumulators deep) leaves the critical path; the tile's
+// epilogue overlaps the next tile's MMAs.  The SwiGLU's BF16 sigmoid comes
+// from a 64K-entry table built on the device by the same sigmoid_bf16.  Activations are the BF16 inputs converted to
 // FP16 after multiplication by a power of two 2^-e per route (e chosen so the
 // row's largest magnitude stays below 2^15); the epilogue multiplies by 2^e.
 //
@@ -45,7 +56,27 @@ namespace tc {
 constexpr int kM = 128;        // weight rows per tile (MMA M)
 constexpr int kN = 64;         // routes per tile (MMA N)
 constexpr int kKB = 128;       // K per block-scale block
-constexpr int kStages = 4;     // raw weight / activation ring depth
+// Ring depths (weight ring from HBM, activation ring mostly from L2), as
+// deep as shared memory allows for each mode.
+#ifndef GLM53_TC_RAW_STAGES_SWIGLU
+#define GLM53_TC_RAW_STAGES_SWIGLU 5
+#endif
+#ifndef GLM53_TC_ACT_STAGES_SWIGLU
+#define GLM53_TC_ACT_STAGES_SWIGLU 4
+#endif
+#ifndef GLM53_TC_RAW_STAGES_PLAIN
+#define GLM53_TC_RAW_STAGES_PLAIN 8
+#endif
+#ifndef GLM53_TC_ACT_STAGES_PLAIN
+#define GLM53_TC_ACT_STAGES_PLAIN 5
+#endif
+constexpr int kMaxStages = 8;
+template <bool SWIGLU>
+struct Rings {
+  static constexpr int raw = SWIGLU ? GLM53_TC_RAW_STAGES_SWIGLU : GLM53_TC_RAW_STAGES_PLAIN;
+  static constexpr int act = SWIGLU ? GLM53_TC_ACT_STAGES_SWIGLU : GLM53_TC_ACT_STAGES_PLAIN;
+  static_assert(raw >= 2 && raw <= kMaxStages && act >= 2 && act <= kMaxStages, "ring depth");
+};
 constexpr int kThreads = 448;  // 14 warps
 constexpr int kEpiWarps = 8;   // two per TMEM lane quarter, 32 routes each
 constexpr int kRawBytes = kM * kKB;        // 16 KB of E4M3 per matrix and stage
@@ -208,23 +239,62 @@ __device__ __forceinline__ uint64_t make_sw128_desc(uint32_t saddr) {
 }
 
 // ---------------------------------------------------------------------------
+// Scaled-mode helpers
+// ---------------------------------------------------------------------------
+
+// sigmoid_bf16 of every BF16 bit pattern (built once per device).
+__device__ uint16_t g_sigmoid_tab[65536];
+
+__global__ void sigmoid_table_kernel() {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < 65536) g_sigmoid_tab[i] = f32_to_bf16_bits(sigmoid_bf16((uint16_t)i));
+}
+
+// swiglu_bf16 with the sigmoid looked up: the same operations and roundings.
+__device__ __forceinline__ uint16_t swiglu_bf16_tab(float gate_total, float up_total, float limit) {
+  const float gate_t = bf16_round(gate_total);
+  const float up_t = bf16_round(up_total);
+  const uint16_t ga = f32_to_bf16_bits(fminf(gate_t, limit));
+  const float ua = bf16_round(fminf(fmaxf(up_t, -limit), limit));
+  const float sig = bf16_bits_to_f32(__ldg(g_sigmoid_tab + ga));
+  const float silu = bf16_round(__fmul_rn(bf16_bits_to_f32(ga), sig));
+  return f32_to_bf16_bits(__fmul_rn(silu, ua));
+}
+
+// Tile exponent p: max|s| * 480 * 2^p < 2^15 (480 = the largest |lut|), so
+// FP16(lut(c) * s * 2^p) cannot overflow.  Warp-uniform; every lane calls it.
+__device__ __forceinline__ int tile_exponent(const float* srow, int n) {
+  const int lane = threadIdx.x & 31;
+  float m = 0.f;
+  for (int i = lane; i < n; i += 32) m = fmaxf(m, fabsf(__ldg(srow + i)));
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  int ex = 0;
+  frexpf(fminf(m, 1e30f) * 480.0f, &ex);
+  return 15 - ex;
+}
+
+__device__ __forceinline__ uint32_t hmul2_u32(uint32_t v, __half2 s) {
+  __half2 h = *reinterpret_cast<__half2*>(&v);
+  h = __hmul2(h, s);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// ---------------------------------------------------------------------------
 // Kernel
 // ---------------------------------------------------------------------------
 
 struct __align__(8) Bars {
-  uint64_t raw_full[kStages], raw_empty[kStages], act_full[kStages], act_empty[kStages];
+  uint64_t raw_full[kMaxStages], raw_empty[kMaxStages], act_full[kMaxStages], act_empty[kMaxStages];
   uint64_t a_full[2], a_empty[2], acc_full[2], acc_empty[2], drain;
   uint32_t tmem_base;
   int abort_flag;
 };
 
-// Output staging of one tile: BF16 gate (and up) totals, [matrix][route][row].
-constexpr int kOutBytes = 2 * kN * kM * 2;
-
 template <bool SWIGLU>
 constexpr size_t smem_bytes() {
-  return 1024 /* alignment slack */ + (size_t)kStages * (SWIGLU ? 2 : 1) * kRawBytes + (size_t)kStages * kActBytes +
-         (SWIGLU ? kOutBytes : 0) + sizeof(Bars);
+  return 1024 /* alignment slack */ + (size_t)Rings<SWIGLU>::raw * (SWIGLU ? 2 : 1) * kRawBytes +
+         (size_t)Rings<SWIGLU>::act * kActBytes + sizeof(Bars);
 }
 
 // Tile t of the persistent schedule: descriptor d = t / (mtiles * zsub), then
@@ -257,26 +327,28 @@ __device__ __forceinline__ Tile tile_at(const TcArgs& a, int t, int mtiles, int 
   return tl;
 }
 
-template <bool SWIGLU, bool FINITE>
+template <bool SWIGLU, bool FINITE, bool SCALED>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap umap,
                       const __grid_constant__ CUtensorMap xmap, TcArgs a, int ntiles, int mtiles, int zsub) {
   constexpr int NMAT = SWIGLU ? 2 : 1;
+  constexpr int RS = Rings<SWIGLU>::raw, AS = Rings<SWIGLU>::act;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  uint8_t* raw = smem;                                          // [stage][mat][128][128] E4M3, swizzled
-  uint8_t* act = raw + (size_t)kStages * NMAT * kRawBytes;      // [stage][box 2][64][128 B] FP16, swizzled
-  uint16_t* obuf = reinterpret_cast<uint16_t*>(act + (size_t)kStages * kActBytes);
-  Bars* bars = reinterpret_cast<Bars*>(reinterpret_cast<uint8_t*>(obuf) + (SWIGLU ? kOutBytes : 0));
+  uint8_t* raw = smem;                                     // [stage][mat][128][128] E4M3, swizzled
+  uint8_t* act = raw + (size_t)RS * NMAT * kRawBytes;      // [stage][box 2][64][128 B] FP16, swizzled
+  Bars* bars = reinterpret_cast<Bars*>(act + (size_t)AS * kActBytes);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nkb = a.K / kKB;
 
   auto bar = [&](uint64_t* p) { return smem_addr(p); };
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < RS; ++s) {
       mbar_init(bar(&bars->raw_full[s]), 1);
       mbar_init(bar(&bars->raw_empty[s]), 4);
+    }
+    for (int s = 0; s < AS; ++s) {
       mbar_init(bar(&bars->act_full[s]), 1);
       mbar_init(bar(&bars->act_empty[s]), 1);
     }
@@ -345,8 +417,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       while ((cr.t < ntiles || ca.t < ntiles) && !*abort_flag) {
         bool progress = false;
         if (cr.t < ntiles) {
-          const int s = cr.g % kStages;
-          if (mbar_try(bar(&bars->raw_empty[s]), ((cr.g / kStages) & 1u) ^ 1u)) {
+          const int s = cr.g % RS;
+          if (mbar_try(bar(&bars->raw_empty[s]), ((cr.g / RS) & 1u) ^ 1u)) {
             const uint32_t rf = bar(&bars->raw_full[s]);
             mbar_expect_tx(rf, NMAT * kRawBytes);
             uint8_t* rs = raw + (size_t)s * NMAT * kRawBytes;
@@ -359,8 +431,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (ca.t < ntiles) {
-          const int s = ca.g % kStages;
-          if (mbar_try(bar(&bars->act_empty[s]), ((ca.g / kStages) & 1u) ^ 1u)) {
+          const int s = ca.g % AS;
+          if (mbar_try(bar(&bars->act_empty[s]), ((ca.g / AS) & 1u) ^ 1u)) {
             const uint32_t af = bar(&bars->act_full[s]);
             mbar_expect_tx(af, kActBytes);
             uint8_t* as = act + (size_t)s * kActBytes;
@@ -383,45 +455,51 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // let every issued copy land before the CTA can exit
       int zero = 0;
-      for (uint32_t k = cr.g > (uint32_t)kStages ? cr.g - kStages : 0u; k < cr.g; ++k)
-        mbar_wait(bar(&bars->raw_full[k % kStages]), (k / kStages) & 1u, &zero);
-      for (uint32_t k = ca.g > (uint32_t)kStages ? ca.g - kStages : 0u; k < ca.g; ++k)
-        mbar_wait(bar(&bars->act_full[k % kStages]), (k / kStages) & 1u, &zero);
+      for (uint32_t k = cr.g > (uint32_t)RS ? cr.g - RS : 0u; k < cr.g; ++k)
+        mbar_wait(bar(&bars->raw_full[k % RS]), (k / RS) & 1u, &zero);
+      for (uint32_t k = ca.g > (uint32_t)AS ? ca.g - AS : 0u; k < ca.g; ++k)
+        mbar_wait(bar(&bars->act_full[k % AS]), (k / AS) & 1u, &zero);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc(kM, kN);
-      uint32_t g = 0;
+      uint32_t g = 0, tcount = 0;
       bool stop = false;
-      for (int t = blockIdx.x; t < ntiles && !stop; t += gridDim.x) {
-        if (tile_at(a, t, mtiles, zsub).len == 0) continue;
+      for (int t = blockIdx.x; t < ntiles && !stop; t += gridDim.x, ++tcount) {
+        if (tile_at(a, t, mtiles, zsub).len == 0) {
+          --tcount;
+          continue;
+        }
+        const int tb = tcount & 1;
+        if (SCALED && !mbar_wait(bar(&bars->acc_empty[tb]), ((tcount >> 1) & 1u) ^ 1u, abort_flag)) break;
         for (int kb = 0; kb < nkb; ++kb, ++g) {
-          const int s = g % kStages;
-          const uint32_t ph = (g / kStages) & 1u;
+          const int s = g % AS;
+          const uint32_t ph = (g / AS) & 1u;
           const int ab = g & 1;
           const uint32_t aph = (g >> 1) & 1u;
           if (!mbar_wait(bar(&bars->a_full[ab]), aph, abort_flag) ||
               !mbar_wait(bar(&bars->act_full[s]), ph, abort_flag) ||
-              !mbar_wait(bar(&bars->acc_empty[ab]), aph ^ 1u, abort_flag)) {
+              (!SCALED && !mbar_wait(bar(&bars->acc_empty[ab]), aph ^ 1u, abort_flag))) {
             stop = true;
             break;
           }
           tmem_fence_after();
           const uint32_t act_s = smem_addr(act + (size_t)s * kActBytes);
+          const int db = SCALED ? tb : ab;  // accumulator: per tile, or per k-block
 #pragma unroll
           for (int m = 0; m < NMAT; ++m) {
-            const uint32_t d_t = tmem + kAccCol + (ab * 2 + m) * kN;
+            const uint32_t d_t = tmem + kAccCol + (db * 2 + m) * kN;
 #pragma unroll
             for (int k16 = 0; k16 < kKB / 16; ++k16) {
               const uint32_t a_t = tmem + kACol + (ab * 2 + m) * 64 + k16 * 8;
               const uint64_t b_desc = make_sw128_desc(act_s + (k16 >> 2) * (kActBytes / 2) + (k16 & 3) * 32);
-              mma_f16_ts(d_t, a_t, b_desc, idesc, k16 > 0 ? 1u : 0u);
+              mma_f16_ts(d_t, a_t, b_desc, idesc, (k16 > 0 || (SCALED && kb > 0)) ? 1u : 0u);
             }
           }
           mma_commit(bar(&bars->a_empty[ab]));
           mma_commit(bar(&bars->act_empty[s]));
-          mma_commit(bar(&bars->acc_full[ab]));
+          if (!SCALED || kb == nkb - 1) mma_commit(bar(&bars->acc_full[db]));
         }
       }
       // every MMA issued so far has completed once this commit arrives
@@ -438,10 +516,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t g = 0;
     bool stop = false;
     for (int t = blockIdx.x; t < ntiles && !stop; t += gridDim.x) {
-      if (tile_at(a, t, mtiles, zsub).len == 0) continue;
+      const Tile tl = tile_at(a, t, mtiles, zsub);
+      if (tl.len == 0) continue;
+      // scaled mode: this tile's block scales and power of two, per matrix
+      WarpScales dsc[NMAT];
+      float dpow[NMAT];
+      if (SCALED) {
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m) {
+          const float* srow = (m ? a.s_up : a.s_gate) + (size_t)tl.e * a.s_expert + (size_t)tl.mt * nkb;
+          dsc[m].load(srow, nkb, true);
+          dpow[m] = ldexpf(decode_unscale<FINITE>(), tile_exponent(srow, nkb));
+        }
+      }
       for (int kb = 0; kb < nkb; ++kb, ++g) {
-        const int s = g % kStages;
-        const uint32_t ph = (g / kStages) & 1u;
+        const int s = g % RS;
+        const uint32_t ph = (g / RS) & 1u;
         const int ab = g & 1;
         const uint32_t aph = (g >> 1) & 1u;
         // the whole warp waits and leaves together (tcgen05.st is warp-wide)
@@ -455,6 +545,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int m = 0; m < NMAT; ++m) {
           const uint8_t* line = raw + (size_t)s * NMAT * kRawBytes + (size_t)m * kRawBytes + r * 128;
+          const __half2 hs = __float2half2_rn(SCALED ? dsc[m].at(kb) * dpow[m] : 1.0f);
 #pragma unroll
           for (int half = 0; half < 4; ++half) {  // 32 K codes -> 16 TMEM columns
             uint32_t v[16];
@@ -466,6 +557,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               e4m3x4_frag<FINITE>(w.y, v[cc * 8 + 2], v[cc * 8 + 3]);
               e4m3x4_frag<FINITE>(w.z, v[cc * 8 + 4], v[cc * 8 + 5]);
               e4m3x4_frag<FINITE>(w.w, v[cc * 8 + 6], v[cc * 8 + 7]);
+            }
+            if (SCALED) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) v[i] = hmul2_u32(v[i], hs);
             }
             tmem_st16(tmem + lane_base + kACol + (ab * 2 + m) * 64 + half * 16, v);
           }
@@ -487,7 +582,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = q * 32 + lane;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     const int scols = nkb;
-    uint32_t g = 0;
+    uint32_t g = 0, tcount = 0;
     bool stop = false;
     for (int t = blockIdx.x; t < ntiles && !stop; t += gridDim.x) {
       const Tile tl = tile_at(a, t, mtiles, zsub);
@@ -505,7 +600,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int n = 0; n < 32; ++n) tg[n] = 0.f;
 #pragma unroll
       for (int n = 0; n < (SWIGLU ? 32 : 1); ++n) tu[n] = 0.f;
-      for (int kb = 0; kb < nkb; ++kb, ++g) {
+      if (SCALED) {
+        // one read of the tile's accumulators, released before the SwiGLU
+        const int tb = tcount & 1;
+        const float mg = ldexpf(1.0f, -tile_exponent(sg_row, scols));
+        const float mu = SWIGLU ? ldexpf(1.0f, -tile_exponent(su_row, scols)) : 0.f;
+        if (!__all_sync(0xffffffffu, mbar_wait(bar(&bars->acc_full[tb]), (tcount >> 1) & 1u, abort_flag))) {
+          stop = true;
+          break;
+        }
+        tmem_fence_after();
+        uint32_t vg[32];
+        tmem_ld32(tmem + lane_base + kAccCol + (tb * 2) * kN + n0, vg);
+        if (SWIGLU) {
+          uint32_t vu[32];
+          tmem_ld32(tmem + lane_base + kAccCol + (tb * 2 + 1) * kN + n0, vu);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) tu[i] = __uint_as_float(vu[i]) * mu;
+        } else {
+          tmem_wait_ld();
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) tg[i] = __uint_as_float(vg[i]) * mg;
+        tmem_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(&bars->acc_empty[tb]));
+        ++tcount;
+      }
+      for (int kb = 0; kb < (SCALED ? 0 : nkb); ++kb, ++g) {
         const int ab = g & 1;
         const uint32_t aph = (g >> 1) & 1u;
         if (!__all_sync(0xffffffffu, mbar_wait(bar(&bars->acc_full[ab]), aph, abort_flag))) {
@@ -535,19 +658,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (stop) break;
       const int col = tl.mt * kM + r;
       if (SWIGLU) {
-        // BF16 gate/up (the reference's gate_up output rounding) parked one
-        // column per thread, then the SwiGLU over this half's routes
-#pragma unroll
+        // route n0 + n: the reference's BF16 SwiGLU of this row's gate and up
+        // totals; the totals shift down one register per route so that the
+        // rolled loop never indexes the arrays at run time
+#pragma unroll 1
         for (int n = 0; n < 32; ++n) {
           const float x = __shfl_sync(0xffffffffu, xs, n);
-          obuf[(n0 + n) * kM + r] = f32_to_bf16_bits(tg[n] * x);
-          obuf[(kN + n0 + n) * kM + r] = f32_to_bf16_bits(tu[n] * x);
-        }
-        for (uint32_t n = n0; n < min(n0 + 32u, tl.len); ++n) {
-          const uint16_t hv = swiglu_bf16(bf16_bits_to_f32(obuf[n * kM + r]), bf16_bits_to_f32(obuf[(kN + n) * kM + r]),
-                                          a.limit);
-          const __half hh = __float2half_rn(bf16_bits_to_f32(hv));
-          a.out[(size_t)(tl.start + n) * a.out_cols + col] = *reinterpret_cast<const uint16_t*>(&hh);
+          const float gv = tg[0] * x, uv = tu[0] * x;
+#pragma unroll
+          for (int i = 0; i < 31; ++i) {
+            tg[i] = tg[i + 1];
+            tu[i] = tu[i + 1];
+          }
+          if (n0 + n < tl.len) {
+            const uint16_t hv = swiglu_bf16_tab(gv, uv, a.limit);
+            const __half hh = __float2half_rn(bf16_bits_to_f32(hv));
+            a.out[(size_t)(tl.start + n0 + n) * a.out_cols + col] = *reinterpret_cast<const uint16_t*>(&hh);
+          }
         }
       } else {
 #pragma unroll
@@ -604,6 +731,27 @@ static int make_map(CUtensorMap* map, const void* base, CUtensorMapDataType type
     set_last_error("grouped_tc: cuTensorMapEncodeTiled failed (%d)", (int)r);
     return GLM53_ERR_CUDA;
   }
+  return GLM53_OK;
+}
+
+// Fill g_sigmoid_tab once per device, on the caller's stream.  Under stream
+// capture the fill is recorded into the graph (ahead of the kernel that needs
+// it) and the device is not marked, so a later eager call fills it too.
+static int ensure_sigmoid_table(cudaStream_t st) {
+  static std::mutex mu;
+  static bool done[64] = {false};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    set_last_error("grouped_tc: no current CUDA device");
+    return GLM53_ERR_CUDA;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (done[dev]) return GLM53_OK;
+  sigmoid_table_kernel<<<65536 / 256, 256, 0, st>>>();
+  int rc = check_launch("sigmoid_table_kernel");
+  if (rc) return rc;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs == cudaStreamCaptureStatusNone) done[dev] = true;
   return GLM53_OK;
 }
 
@@ -668,10 +816,18 @@ int grouped_tc(const TcGemm& g, cudaStream_t st) {
   void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, TcArgs, int, int, int);
   size_t smem;
   if (g.swiglu) {
-    kern = g.finite ? grouped_tc_kernel<true, true> : grouped_tc_kernel<true, false>;
+    rc = ensure_sigmoid_table(st);
+    if (rc) return rc;
+    if (g.scaled)
+      kern = g.finite ? grouped_tc_kernel<true, true, true> : grouped_tc_kernel<true, false, true>;
+    else
+      kern = g.finite ? grouped_tc_kernel<true, true, false> : grouped_tc_kernel<true, false, false>;
     smem = smem_bytes<true>();
   } else {
-    kern = g.finite ? grouped_tc_kernel<false, true> : grouped_tc_kernel<false, false>;
+    if (g.scaled)
+      kern = g.finite ? grouped_tc_kernel<false, true, true> : grouped_tc_kernel<false, false, true>;
+    else
+      kern = g.finite ? grouped_tc_kernel<false, true, false> : grouped_tc_kernel<false, false, false>;
     smem = smem_bytes<false>();
   }
   rc = ensure_max_smem((const void*)kern, smem);

@@ -80,6 +80,7 @@ struct TcGemm {
   bool swiglu;
   float limit;
   bool finite;            // no 0x7F/0xFF codes: hardware E4M3 conversion
+  bool scaled;            // block scales folded into the FP16 A operand (whole-K accumulation)
   uint16_t* out;
   uint32_t* status;
 };
