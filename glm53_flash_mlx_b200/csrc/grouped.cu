@@ -500,7 +500,7 @@ extern "C" int glm53_restore_and_reduce(const void* sorted_out, const float* sor
 namespace {
 // Routes per descriptor of the tensor-core (tcgen05) path; the fallback path
 // uses BM-route descriptors, and the capacity covers both.
-constexpr int kTcTileRows = 64;
+constexpr int kTcTileRows = 128;
 
 struct MoeWorkspace {
   uint32_t *order, *inverse, *sorted_experts, *route_offsets, *tile_offsets, *tile_experts, *tile_starts,
@@ -546,7 +546,7 @@ MoeWorkspace carve(void* base, int64_t T, int top_k, int64_t E, int64_t H, int64
 }
 }  // namespace
 
-// Tensor-core composition: route plan (64-route descriptors), sorted FP16
+// Tensor-core composition: route plan (128-route descriptors), sorted FP16
 // activations, tcgen05 gate/up with the SwiGLU epilogue (FP16 hidden rows),
 // tcgen05 down, the dense shared expert on the same kernels, combine.
 static int grouped_moe_tc(const MoeWorkspace& w, const void* x, int64_t T, int64_t H, const uint32_t* indices,
@@ -586,7 +586,6 @@ static int grouped_moe_tc(const MoeWorkspace& w, const void* x, int64_t T, int64
   gu.swiglu = true;
   gu.limit = limit;
   gu.finite = finite;
-  gu.scaled = false;
   gu.out = w.hidden;
   gu.status = status;
   rc = grouped_tc(gu, st);
@@ -634,7 +633,6 @@ static int grouped_moe_tc(const MoeWorkspace& w, const void* x, int64_t T, int64
     sg.swiglu = true;
     sg.limit = limit;
     sg.finite = finite;
-    sg.scaled = false;
     sg.out = w.shared_hidden;
     sg.status = status;
     rc = grouped_tc(sg, st);

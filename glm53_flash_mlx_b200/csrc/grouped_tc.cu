@@ -3,39 +3,47 @@
 // (glm53_flash_mlx/grouped_fp8.py:206-321, Metal kernel K12 at
 // grouped_fp8.py:30-154) and the dense shared expert.
 //
-// One CTA computes a tile of 128 weight rows x 64 routes (D = W . X^T, the
-// weights as the M operand) over the whole K, for one route descriptor
-// (expert, first route, routes <= 64) and one 128-row weight tile:
+// One CTA computes D = W . X^T for one tile of 128 weight rows x up to 128
+// routes over the whole K, for one route descriptor (expert, first route,
+// routes <= 128).  With the SwiGLU epilogue the 128 rows are 64 gate rows
+// stacked on the matching 64 up rows, so one M=128 MMA produces both halves
+// of 64 hidden rows.  Roles (persistent CTA, one per SM):
 //   warp 0      TMA producer: raw E4M3 weight tiles [128 rows x 128 K] and
-//               activation tiles [64 routes x 128 K] (FP16, 128-byte swizzle)
-//               into two shared-memory rings of their own depths (the
-//               weight ring, fed from HBM, is the deeper one);
-//   warp 1      allocates TMEM and issues tcgen05.mma (kind::f16, A from TMEM,
-//               B from shared memory, FP32 accumulation in TMEM);
+//               activation tiles [routes x 128 K] (FP16, two 64-K boxes,
+//               128-byte swizzle) into two rings of their own depths;
+//   warps 1, 15 issue tcgen05.mma (kind::f16, M128, N = 128, or 64 for a tile
+//               of <= 64 routes; A from TMEM, B from shared memory, FP32
+//               accumulation in TMEM), warp 1 the even k-blocks and warp 15
+//               the odd ones: consecutive k-blocks write different
+//               accumulators, and one thread's barrier wait and commit
+//               (~300 cycles each) would leave the tensor core idle between
+//               its k-blocks; each issuer waits on one barrier per k-block
+//               and commits to one; warp 1 also allocates TMEM;
 //   warps 2-5   decode each weight row exactly to FP16 (lut(c), or lut(c)/256
-//               on the bit-exact path for banks holding 0x7F/0xFF) and store
-//               it into TMEM as the A operand (one TMEM lane per weight row);
-//   warps 6-13  epilogue (two warps per TMEM lane quarter, 32 routes each):
-//               after every 128-K block, read the block's partial
-//               product from TMEM and promote it in FP32 with the 128x128
-//               block scale (tot += s_kb * P_kb), then apply the route's
-//               activation range scale and either store BF16 rows or apply
-//               the reference's BF16 SwiGLU to a gate tile and its up tile.
+//               on the bit-exact path for banks holding 0x7F/0xFF) into a
+//               4-deep TMEM ring (A operand, one TMEM lane per weight row);
+//   warp 14     gatekeeper: confirms that each k-block's activations have
+//               landed and that its accumulator is free, and counts as the
+//               fifth arrival of the k-block's A-operand barrier;
+//   warps 6-13  epilogue (two warps per TMEM lane quarter, 64 routes each):
+//               after every 128-K block, read the block's partial product
+//               from TMEM and promote it in FP32 with the 128x128 block scale
+//               (tot += s_kb * P_kb), then apply the route's activation range
+//               scale and either store BF16 rows, or hand the up rows to the
+//               gate rows' warps through shared memory and apply the
+//               reference's BF16 SwiGLU there.
 // Products of FP16 weights (4 significant bits) and FP16 activations are
 // exact in FP32, so each 128-K block sum differs from the reference's FP32
-// sum only in summation order.
-//
-// Scaled mode (SCALED, the prefill default): the decode warps fold the
-// 128x128 block scale into the A operand, FP16(lut(c) * s_kb * 2^p) with one
-// power of two 2^p per weight tile that keeps every value below 2^15, so the
-// MMAs accumulate the whole K in TMEM and the epilogue reads each tile once
-// (undoing 2^p exactly).  Each weight then carries one FP16 rounding (relative
-// 2^-11) and the per-block promotion round trip (MMA -> TMEM load -> FMA ->
-// release, two accumulators deep) leaves the critical path; the tile's
-// epilogue overlaps the next tile's MMAs.  The SwiGLU's BF16 sigmoid comes
-// from a 64K-entry table built on the device by the same sigmoid_bf16.  Activations are the BF16 inputs converted to
+// sum only in summation order.  Activations are the BF16 inputs converted to
 // FP16 after multiplication by a power of two 2^-e per route (e chosen so the
 // row's largest magnitude stays below 2^15); the epilogue multiplies by 2^e.
+// The SwiGLU's BF16 sigmoid comes from a 64K-entry table built on the device
+// by sigmoid_bf16 itself (bit-identical, without the FP64 exponential).
+//
+// Measured tcgen05 cost on B200 (one thread issuing back-to-back M128 K16
+// kind::f16 MMAs, A from TMEM or shared memory alike): 47 cycles at N=64, 64 at
+// N=128, 128 at N=256 -- N=64 runs at two thirds of the tensor-core rate,
+// hence the 128-route tiles.
 //
 // Every wait on an mbarrier is bounded (a deadline on the global timer); a
 // CTA that gives up sets GLM53_STATUS_WAIT_TIMEOUT, lets its copies and MMAs
@@ -53,36 +61,20 @@
 namespace glm53 {
 namespace tc {
 
-constexpr int kM = 128;        // weight rows per tile (MMA M)
-constexpr int kN = 64;         // routes per tile (MMA N)
-constexpr int kKB = 128;       // K per block-scale block
-// Ring depths (weight ring from HBM, activation ring mostly from L2), as
-// deep as shared memory allows for each mode.
-#ifndef GLM53_TC_RAW_STAGES_SWIGLU
-#define GLM53_TC_RAW_STAGES_SWIGLU 5
-#endif
-#ifndef GLM53_TC_ACT_STAGES_SWIGLU
-#define GLM53_TC_ACT_STAGES_SWIGLU 4
-#endif
-#ifndef GLM53_TC_RAW_STAGES_PLAIN
-#define GLM53_TC_RAW_STAGES_PLAIN 8
-#endif
-#ifndef GLM53_TC_ACT_STAGES_PLAIN
-#define GLM53_TC_ACT_STAGES_PLAIN 5
-#endif
-constexpr int kMaxStages = 8;
-template <bool SWIGLU>
-struct Rings {
-  static constexpr int raw = SWIGLU ? GLM53_TC_RAW_STAGES_SWIGLU : GLM53_TC_RAW_STAGES_PLAIN;
-  static constexpr int act = SWIGLU ? GLM53_TC_ACT_STAGES_SWIGLU : GLM53_TC_ACT_STAGES_PLAIN;
-  static_assert(raw >= 2 && raw <= kMaxStages && act >= 2 && act <= kMaxStages, "ring depth");
-};
-constexpr int kThreads = 448;  // 14 warps
-constexpr int kEpiWarps = 8;   // two per TMEM lane quarter, 32 routes each
-constexpr int kRawBytes = kM * kKB;        // 16 KB of E4M3 per matrix and stage
-constexpr int kActBytes = kN * kKB * 2;    // 16 KB of FP16 per stage (two 64-K boxes)
+constexpr int kM = 128;         // weight rows per tile (MMA M)
+constexpr int kN = 128;         // routes per tile (MMA N: 128, or 64 for short tiles)
+constexpr int kKB = 128;        // K per block-scale block
+constexpr int kRawStages = 7;   // weight ring (E4M3, 16 KB per stage): covers ~5,000-cycle HBM latency
+constexpr int kActStages = 3;   // activation ring (FP16, 32 KB per stage), mostly L2 hits
+constexpr int kRing = 4;        // decoded A operands in TMEM = k-block completion slots
+constexpr int kThreads = 512;   // 16 warps
+constexpr int kEpiWarps = 8;    // two per TMEM lane quarter, 64 routes each
+constexpr int kRawBytes = kM * kKB;      // 16 KB of E4M3 per stage
+constexpr int kActBox = kN * 64 * 2;     // one 64-K box of up to 128 routes (FP16)
+constexpr int kActBytes = 2 * kActBox;   // 32 KB per stage
+constexpr int kXchBytes = kN * 64 * 2;   // SwiGLU up rows handed to the gate rows: BF16 [route][64 rows]
 constexpr int kTmemCols = 512;
-// TMEM columns: accumulators [2 buffers][2 matrices][kN] at 0, A [2 stages][2 matrices][64] at 256
+// TMEM columns: accumulators [2][kN] at 0, A operands [kRing][64] at 256
 constexpr int kAccCol = 0;
 constexpr int kACol = 256;
 constexpr uint64_t kWaitNs = 200ull * 1000 * 1000;  // longest single wait
@@ -91,7 +83,7 @@ struct TcArgs {
   const uint32_t* tile_experts;
   const uint32_t* tile_starts;
   const uint32_t* tile_lengths;
-  int dense;             // descriptors implicit: (0, 64 d, min(64, R - 64 d))
+  int dense;             // descriptors implicit: (0, kN d, min(kN, R - kN d))
   int R;                 // activation rows
   int K;                 // reduction length
   int E;
@@ -239,7 +231,7 @@ __device__ __forceinline__ uint64_t make_sw128_desc(uint32_t saddr) {
 }
 
 // ---------------------------------------------------------------------------
-// Scaled-mode helpers
+// SwiGLU sigmoid table
 // ---------------------------------------------------------------------------
 
 // sigmoid_bf16 of every BF16 bit pattern (built once per device).
@@ -261,40 +253,26 @@ __device__ __forceinline__ uint16_t swiglu_bf16_tab(float gate_total, float up_t
   return f32_to_bf16_bits(__fmul_rn(silu, ua));
 }
 
-// Tile exponent p: max|s| * 480 * 2^p < 2^15 (480 = the largest |lut|), so
-// FP16(lut(c) * s * 2^p) cannot overflow.  Warp-uniform; every lane calls it.
-__device__ __forceinline__ int tile_exponent(const float* srow, int n) {
-  const int lane = threadIdx.x & 31;
-  float m = 0.f;
-  for (int i = lane; i < n; i += 32) m = fmaxf(m, fabsf(__ldg(srow + i)));
-#pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  int ex = 0;
-  frexpf(fminf(m, 1e30f) * 480.0f, &ex);
-  return 15 - ex;
-}
-
-__device__ __forceinline__ uint32_t hmul2_u32(uint32_t v, __half2 s) {
-  __half2 h = *reinterpret_cast<__half2*>(&v);
-  h = __hmul2(h, s);
-  return *reinterpret_cast<uint32_t*>(&h);
-}
-
 // ---------------------------------------------------------------------------
 // Kernel
 // ---------------------------------------------------------------------------
 
+// Barriers.  k-block g uses raw stage g % kRawStages and ring slot g % kRing
+// (activation stage, A operand, completion barrier kb_done) and accumulator
+// g % 2; kb_done[j] completes when the MMAs of k-block g = j (mod kRing) have
+// finished: the slot's activations and A operand are free again and the
+// accumulator holds the block's partial product.
 struct __align__(8) Bars {
-  uint64_t raw_full[kMaxStages], raw_empty[kMaxStages], act_full[kMaxStages], act_empty[kMaxStages];
-  uint64_t a_full[2], a_empty[2], acc_full[2], acc_empty[2], drain;
+  uint64_t raw_full[kRawStages], raw_empty[kRawStages], act_full[kActStages], a_full[kRing], kb_done[kRing];
+  uint64_t acc_empty[2], xch_full, xch_empty, drain;
   uint32_t tmem_base;
   int abort_flag;
 };
 
 template <bool SWIGLU>
 constexpr size_t smem_bytes() {
-  return 1024 /* alignment slack */ + (size_t)Rings<SWIGLU>::raw * (SWIGLU ? 2 : 1) * kRawBytes +
-         (size_t)Rings<SWIGLU>::act * kActBytes + sizeof(Bars);
+  return 1024 /* alignment slack */ + (size_t)kRawStages * kRawBytes + (size_t)kActStages * kActBytes +
+         (SWIGLU ? kXchBytes : 0) + sizeof(Bars);
 }
 
 // Tile t of the persistent schedule: descriptor d = t / (mtiles * zsub), then
@@ -327,43 +305,53 @@ __device__ __forceinline__ Tile tile_at(const TcArgs& a, int t, int mtiles, int 
   return tl;
 }
 
-template <bool SWIGLU, bool FINITE, bool SCALED>
+// Weight rows of tile mt: SwiGLU tiles hold hidden rows [64 mt, 64 mt + 64)
+// (gate rows in TMEM lanes 0-63, up rows in lanes 64-127); plain tiles hold
+// rows [128 mt, 128 mt + 128).
+template <bool SWIGLU>
+__device__ __forceinline__ int tile_row0(int mt) {
+  return SWIGLU ? 64 * mt : kM * mt;
+}
+
+// Tensor maps: w (and u) boxes of 64 rows (SwiGLU) or 128 rows (plain) x 128
+// K codes; x boxes of 128 routes and, for tiles of <= 64 routes, x64 boxes of
+// 64 routes, each x 64 K.
+template <bool SWIGLU, bool FINITE>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap umap,
-                      const __grid_constant__ CUtensorMap xmap, TcArgs a, int ntiles, int mtiles, int zsub) {
-  constexpr int NMAT = SWIGLU ? 2 : 1;
-  constexpr int RS = Rings<SWIGLU>::raw, AS = Rings<SWIGLU>::act;
+                      const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap xmap64, TcArgs a,
+                      int ntiles, int mtiles, int zsub) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  uint8_t* raw = smem;                                     // [stage][mat][128][128] E4M3, swizzled
-  uint8_t* act = raw + (size_t)RS * NMAT * kRawBytes;      // [stage][box 2][64][128 B] FP16, swizzled
-  Bars* bars = reinterpret_cast<Bars*>(act + (size_t)AS * kActBytes);
+  uint8_t* raw = smem;                                      // [stage][128][128] E4M3, swizzled
+  uint8_t* act = raw + (size_t)kRawStages * kRawBytes;      // [stage][box 2][routes][128 B] FP16, swizzled
+  uint16_t* xch = reinterpret_cast<uint16_t*>(act + (size_t)kActStages * kActBytes);  // [route][64] BF16
+  Bars* bars = reinterpret_cast<Bars*>(reinterpret_cast<uint8_t*>(xch) + (SWIGLU ? kXchBytes : 0));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nkb = a.K / kKB;
 
   auto bar = [&](uint64_t* p) { return smem_addr(p); };
   if (threadIdx.x == 0) {
-    for (int s = 0; s < RS; ++s) {
+    for (int s = 0; s < kRawStages; ++s) {
       mbar_init(bar(&bars->raw_full[s]), 1);
       mbar_init(bar(&bars->raw_empty[s]), 4);
     }
-    for (int s = 0; s < AS; ++s) {
-      mbar_init(bar(&bars->act_full[s]), 1);
-      mbar_init(bar(&bars->act_empty[s]), 1);
+    for (int s = 0; s < kActStages; ++s) mbar_init(bar(&bars->act_full[s]), 1);
+    for (int s = 0; s < kRing; ++s) {
+      mbar_init(bar(&bars->a_full[s]), 5);  // four decode warps + the gatekeeper
+      mbar_init(bar(&bars->kb_done[s]), 1);
     }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(bar(&bars->a_full[s]), 4);
-      mbar_init(bar(&bars->a_empty[s]), 1);
-      mbar_init(bar(&bars->acc_full[s]), 1);
-      mbar_init(bar(&bars->acc_empty[s]), kEpiWarps);
-    }
-    mbar_init(bar(&bars->drain), 1);
+    for (int s = 0; s < 2; ++s) mbar_init(bar(&bars->acc_empty[s]), kEpiWarps);
+    mbar_init(bar(&bars->xch_full), 4);   // the four up-row warps
+    mbar_init(bar(&bars->xch_empty), 4);  // the four gate-row warps
+    mbar_init(bar(&bars->drain), 2);      // one commit per MMA issuer
     bars->abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&wmap)) : "memory");
     if (SWIGLU) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&umap)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap64)) : "memory");
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -417,27 +405,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       while ((cr.t < ntiles || ca.t < ntiles) && !*abort_flag) {
         bool progress = false;
         if (cr.t < ntiles) {
-          const int s = cr.g % RS;
-          if (mbar_try(bar(&bars->raw_empty[s]), ((cr.g / RS) & 1u) ^ 1u)) {
+          const int s = cr.g % kRawStages;
+          if (mbar_try(bar(&bars->raw_empty[s]), ((cr.g / kRawStages) & 1u) ^ 1u)) {
             const uint32_t rf = bar(&bars->raw_full[s]);
-            mbar_expect_tx(rf, NMAT * kRawBytes);
-            uint8_t* rs = raw + (size_t)s * NMAT * kRawBytes;
-            tma_load_2d(smem_addr(rs), &wmap, cr.kb * kKB, (int)cr.tl.e * a.w_rows + cr.tl.mt * kM, rf);
+            mbar_expect_tx(rf, kRawBytes);
+            uint8_t* rs = raw + (size_t)s * kRawBytes;
+            const int row0 = tile_row0<SWIGLU>(cr.tl.mt);
+            tma_load_2d(smem_addr(rs), &wmap, cr.kb * kKB, (int)cr.tl.e * a.w_rows + row0, rf);
             if (SWIGLU)
-              tma_load_2d(smem_addr(rs + kRawBytes), &umap, cr.kb * kKB,
-                          (int)cr.tl.e * a.u_rows + a.u_off + cr.tl.mt * kM, rf);
+              tma_load_2d(smem_addr(rs + kRawBytes / 2), &umap, cr.kb * kKB, (int)cr.tl.e * a.u_rows + a.u_off + row0,
+                          rf);
             advance(cr);
             progress = true;
           }
         }
-        if (ca.t < ntiles) {
-          const int s = ca.g % AS;
-          if (mbar_try(bar(&bars->act_empty[s]), ((ca.g / AS) & 1u) ^ 1u)) {
+        // stage ca.g % kActStages is free once k-block ca.g - kActStages has completed
+        const uint32_t prev = ca.g - kActStages;
+        if (ca.t < ntiles &&
+            (ca.g < (uint32_t)kActStages || mbar_try(bar(&bars->kb_done[prev % kRing]), (prev / kRing) & 1u))) {
+          const int s = ca.g % kActStages;
+          {
             const uint32_t af = bar(&bars->act_full[s]);
-            mbar_expect_tx(af, kActBytes);
+            const bool wide = ca.tl.len > 64;
+            mbar_expect_tx(af, wide ? kActBytes : kActBytes / 2);
             uint8_t* as = act + (size_t)s * kActBytes;
-            tma_load_2d(smem_addr(as), &xmap, ca.kb * kKB, (int)ca.tl.start, af);
-            tma_load_2d(smem_addr(as + kActBytes / 2), &xmap, ca.kb * kKB + 64, (int)ca.tl.start, af);
+            const CUtensorMap* xm = wide ? &xmap : &xmap64;
+            tma_load_2d(smem_addr(as), xm, ca.kb * kKB, (int)ca.tl.start, af);
+            tma_load_2d(smem_addr(as + kActBox), xm, ca.kb * kKB + 64, (int)ca.tl.start, af);
             advance(ca);
             progress = true;
           }
@@ -455,115 +449,105 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // let every issued copy land before the CTA can exit
       int zero = 0;
-      for (uint32_t k = cr.g > (uint32_t)RS ? cr.g - RS : 0u; k < cr.g; ++k)
-        mbar_wait(bar(&bars->raw_full[k % RS]), (k / RS) & 1u, &zero);
-      for (uint32_t k = ca.g > (uint32_t)AS ? ca.g - AS : 0u; k < ca.g; ++k)
-        mbar_wait(bar(&bars->act_full[k % AS]), (k / AS) & 1u, &zero);
+      for (uint32_t k = cr.g > (uint32_t)kRawStages ? cr.g - kRawStages : 0u; k < cr.g; ++k)
+        mbar_wait(bar(&bars->raw_full[k % kRawStages]), (k / kRawStages) & 1u, &zero);
+      for (uint32_t k = ca.g > (uint32_t)kActStages ? ca.g - kActStages : 0u; k < ca.g; ++k)
+        mbar_wait(bar(&bars->act_full[k % kActStages]), (k / kActStages) & 1u, &zero);
     }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
+  } else if (warp == 1 || warp == 15) {
+    // ---------------- MMA issuers (even / odd k-blocks) ----------------
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc(kM, kN);
-      uint32_t g = 0, tcount = 0;
+      const uint32_t parity = warp == 1 ? 0u : 1u;
+      uint32_t g = 0;
       bool stop = false;
-      for (int t = blockIdx.x; t < ntiles && !stop; t += gridDim.x, ++tcount) {
-        if (tile_at(a, t, mtiles, zsub).len == 0) {
-          --tcount;
-          continue;
-        }
-        const int tb = tcount & 1;
-        if (SCALED && !mbar_wait(bar(&bars->acc_empty[tb]), ((tcount >> 1) & 1u) ^ 1u, abort_flag)) break;
+      for (int t = blockIdx.x; t < ntiles && !stop; t += gridDim.x) {
+        const Tile tl = tile_at(a, t, mtiles, zsub);
+        if (tl.len == 0) continue;
+        const uint32_t idesc = tl.len > 64 ? make_idesc(kM, kN) : make_idesc(kM, 64);
         for (int kb = 0; kb < nkb; ++kb, ++g) {
-          const int s = g % AS;
-          const uint32_t ph = (g / AS) & 1u;
-          const int ab = g & 1;
-          const uint32_t aph = (g >> 1) & 1u;
-          if (!mbar_wait(bar(&bars->a_full[ab]), aph, abort_flag) ||
-              !mbar_wait(bar(&bars->act_full[s]), ph, abort_flag) ||
-              (!SCALED && !mbar_wait(bar(&bars->acc_empty[ab]), aph ^ 1u, abort_flag))) {
+          if ((g & 1u) != parity) continue;
+          const int s = g % kRing;
+          const int as = g % kActStages;
+          const int cb = g & 1;
+          // a_full implies the activations landed and the accumulator is free
+          if (!mbar_wait(bar(&bars->a_full[s]), (g / kRing) & 1u, abort_flag)) {
             stop = true;
             break;
           }
           tmem_fence_after();
-          const uint32_t act_s = smem_addr(act + (size_t)s * kActBytes);
-          const int db = SCALED ? tb : ab;  // accumulator: per tile, or per k-block
+          const uint32_t act_s = smem_addr(act + (size_t)as * kActBytes);
+          const uint32_t d_t = tmem + kAccCol + cb * kN;
 #pragma unroll
-          for (int m = 0; m < NMAT; ++m) {
-            const uint32_t d_t = tmem + kAccCol + (db * 2 + m) * kN;
-#pragma unroll
-            for (int k16 = 0; k16 < kKB / 16; ++k16) {
-              const uint32_t a_t = tmem + kACol + (ab * 2 + m) * 64 + k16 * 8;
-              const uint64_t b_desc = make_sw128_desc(act_s + (k16 >> 2) * (kActBytes / 2) + (k16 & 3) * 32);
-              mma_f16_ts(d_t, a_t, b_desc, idesc, (k16 > 0 || (SCALED && kb > 0)) ? 1u : 0u);
-            }
+          for (int k16 = 0; k16 < kKB / 16; ++k16) {
+            const uint32_t a_t = tmem + kACol + s * 64 + k16 * 8;
+            const uint64_t b_desc = make_sw128_desc(act_s + (k16 >> 2) * kActBox + (k16 & 3) * 32);
+            mma_f16_ts(d_t, a_t, b_desc, idesc, k16 > 0 ? 1u : 0u);
           }
-          mma_commit(bar(&bars->a_empty[ab]));
-          mma_commit(bar(&bars->act_empty[s]));
-          if (!SCALED || kb == nkb - 1) mma_commit(bar(&bars->acc_full[db]));
+          mma_commit(bar(&bars->kb_done[s]));
         }
       }
-      // every MMA issued so far has completed once this commit arrives
+      // every MMA of both issuers has completed once both commits arrived
       int zero = 0;
       mma_commit(bar(&bars->drain));
       mbar_wait(bar(&bars->drain), 0, &zero);
     }
     __syncwarp();
+  } else if (warp == 14) {
+    // ---------------- gatekeeper ----------------
+    // k-block g may be issued once its activations are in shared memory and
+    // the epilogue has read accumulator g % 2 (k-block g - 2)
+    if (lane == 0) {
+      uint32_t g = 0;
+      bool stop = false;
+      for (int t = blockIdx.x; t < ntiles && !stop; t += gridDim.x) {
+        if (tile_at(a, t, mtiles, zsub).len == 0) continue;
+        for (int kb = 0; kb < nkb; ++kb, ++g) {
+          if (!mbar_wait(bar(&bars->act_full[g % kActStages]), (g / kActStages) & 1u, abort_flag) ||
+              !mbar_wait(bar(&bars->acc_empty[g & 1]), ((g >> 1) & 1u) ^ 1u, abort_flag)) {
+            stop = true;
+            break;
+          }
+          mbar_arrive(bar(&bars->a_full[g % kRing]));
+        }
+      }
+    }
+    __syncwarp();
   } else if (warp < 6) {
     // ---------------- weight decode into TMEM (A operand) ----------------
-    const int q = warp & 3;
+    const int q = warp & 3;       // TMEM lane quarter this warp may access
     const int r = q * 32 + lane;  // weight row of this thread = TMEM lane
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     uint32_t g = 0;
     bool stop = false;
     for (int t = blockIdx.x; t < ntiles && !stop; t += gridDim.x) {
-      const Tile tl = tile_at(a, t, mtiles, zsub);
-      if (tl.len == 0) continue;
-      // scaled mode: this tile's block scales and power of two, per matrix
-      WarpScales dsc[NMAT];
-      float dpow[NMAT];
-      if (SCALED) {
-#pragma unroll
-        for (int m = 0; m < NMAT; ++m) {
-          const float* srow = (m ? a.s_up : a.s_gate) + (size_t)tl.e * a.s_expert + (size_t)tl.mt * nkb;
-          dsc[m].load(srow, nkb, true);
-          dpow[m] = ldexpf(decode_unscale<FINITE>(), tile_exponent(srow, nkb));
-        }
-      }
+      if (tile_at(a, t, mtiles, zsub).len == 0) continue;
       for (int kb = 0; kb < nkb; ++kb, ++g) {
-        const int s = g % RS;
-        const uint32_t ph = (g / RS) & 1u;
-        const int ab = g & 1;
-        const uint32_t aph = (g >> 1) & 1u;
-        // the whole warp waits and leaves together (tcgen05.st is warp-wide)
-        bool ok = __all_sync(0xffffffffu, mbar_wait(bar(&bars->raw_full[s]), ph, abort_flag));
-        ok = ok && __all_sync(0xffffffffu, mbar_wait(bar(&bars->a_empty[ab]), aph ^ 1u, abort_flag));
+        const int s = g % kRawStages;
+        const int ab = g % kRing;
+        const uint32_t ring_ph = (g / kRing) & 1u;
+        // the whole warp waits and leaves together (tcgen05.st is warp-wide);
+        // the A slot is free once k-block g - kRing has completed
+        bool ok = __all_sync(0xffffffffu, mbar_wait(bar(&bars->raw_full[s]), (g / kRawStages) & 1u, abort_flag));
+        ok = ok && __all_sync(0xffffffffu, mbar_wait(bar(&bars->kb_done[ab]), ring_ph ^ 1u, abort_flag));
         if (!ok) {
           stop = true;
           break;
         }
         tmem_fence_after();
+        const uint8_t* line = raw + (size_t)s * kRawBytes + r * 128;
 #pragma unroll
-        for (int m = 0; m < NMAT; ++m) {
-          const uint8_t* line = raw + (size_t)s * NMAT * kRawBytes + (size_t)m * kRawBytes + r * 128;
-          const __half2 hs = __float2half2_rn(SCALED ? dsc[m].at(kb) * dpow[m] : 1.0f);
+        for (int half = 0; half < 4; ++half) {  // 32 K codes -> 16 TMEM columns
+          uint32_t v[16];
 #pragma unroll
-          for (int half = 0; half < 4; ++half) {  // 32 K codes -> 16 TMEM columns
-            uint32_t v[16];
-#pragma unroll
-            for (int cc = 0; cc < 2; ++cc) {
-              const int c = half * 2 + cc;  // 16-byte chunk (16 codes) of the 128-byte row
-              const uint4 w = *reinterpret_cast<const uint4*>(line + 16 * (c ^ (r & 7)));
-              e4m3x4_frag<FINITE>(w.x, v[cc * 8 + 0], v[cc * 8 + 1]);
-              e4m3x4_frag<FINITE>(w.y, v[cc * 8 + 2], v[cc * 8 + 3]);
-              e4m3x4_frag<FINITE>(w.z, v[cc * 8 + 4], v[cc * 8 + 5]);
-              e4m3x4_frag<FINITE>(w.w, v[cc * 8 + 6], v[cc * 8 + 7]);
-            }
-            if (SCALED) {
-#pragma unroll
-              for (int i = 0; i < 16; ++i) v[i] = hmul2_u32(v[i], hs);
-            }
-            tmem_st16(tmem + lane_base + kACol + (ab * 2 + m) * 64 + half * 16, v);
+          for (int cc = 0; cc < 2; ++cc) {
+            const int c = half * 2 + cc;  // 16-byte chunk (16 codes) of the 128-byte row
+            const uint4 w = *reinterpret_cast<const uint4*>(line + 16 * (c ^ (r & 7)));
+            e4m3x4_frag<FINITE>(w.x, v[cc * 8 + 0], v[cc * 8 + 1]);
+            e4m3x4_frag<FINITE>(w.y, v[cc * 8 + 2], v[cc * 8 + 3]);
+            e4m3x4_frag<FINITE>(w.z, v[cc * 8 + 4], v[cc * 8 + 5]);
+            e4m3x4_frag<FINITE>(w.w, v[cc * 8 + 6], v[cc * 8 + 7]);
           }
+          tmem_st16(tmem + lane_base + kACol + ab * 64 + half * 16, v);
         }
         tmem_wait_st();
         __syncwarp();
@@ -576,112 +560,89 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ---------------- epilogue: per-block promotion, then output ----------------
     // warp pair (w, w + 4) shares a TMEM lane quarter; half h takes routes
-    // [32 h, 32 h + 32) of the tile
+    // [64 h, 64 h + 64) of the tile
     const int q = warp & 3;
     const int h = (warp - 6) >> 2;
     const int r = q * 32 + lane;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-    const int scols = nkb;
+    const bool up_rows = SWIGLU && q >= 2;  // TMEM lanes 64-127 hold the up rows
     uint32_t g = 0, tcount = 0;
     bool stop = false;
     for (int t = blockIdx.x; t < ntiles && !stop; t += gridDim.x) {
       const Tile tl = tile_at(a, t, mtiles, zsub);
       if (tl.len == 0) continue;
-      const float* sg_row = a.s_gate + (size_t)tl.e * a.s_expert + (size_t)tl.mt * scols;
-      const float* su_row = a.s_up + (size_t)tl.e * a.s_expert + (size_t)tl.mt * scols;
-      WarpScales sgs, sus;
-      sgs.load(sg_row, scols, true);
-      sus.load(su_row, scols, SWIGLU);
-      const uint32_t n0 = (uint32_t)h * 32;
-      // this half's route range multipliers, one per lane
-      const float xs = (a.xscale && n0 + lane < tl.len) ? __ldg(a.xscale + tl.start + n0 + lane) : 1.0f;
-      float tg[32], tu[SWIGLU ? 32 : 1];
+      const int row0 = tile_row0<SWIGLU>(tl.mt);
+      const float* srow = (up_rows ? a.s_up : a.s_gate) + (size_t)tl.e * a.s_expert + (size_t)(row0 >> 7) * nkb;
+      WarpScales sc;
+      sc.load(srow, nkb, true);
+      const uint32_t n0 = (uint32_t)h * 64;
+      const bool active = n0 < tl.len;  // this half has routes
+      float tot[64];
 #pragma unroll
-      for (int n = 0; n < 32; ++n) tg[n] = 0.f;
-#pragma unroll
-      for (int n = 0; n < (SWIGLU ? 32 : 1); ++n) tu[n] = 0.f;
-      if (SCALED) {
-        // one read of the tile's accumulators, released before the SwiGLU
-        const int tb = tcount & 1;
-        const float mg = ldexpf(1.0f, -tile_exponent(sg_row, scols));
-        const float mu = SWIGLU ? ldexpf(1.0f, -tile_exponent(su_row, scols)) : 0.f;
-        if (!__all_sync(0xffffffffu, mbar_wait(bar(&bars->acc_full[tb]), (tcount >> 1) & 1u, abort_flag))) {
+      for (int n = 0; n < 64; ++n) tot[n] = 0.f;
+      for (int kb = 0; kb < nkb; ++kb, ++g) {
+        const int cb = g & 1;
+        if (!__all_sync(0xffffffffu, mbar_wait(bar(&bars->kb_done[g % kRing]), (g / kRing) & 1u, abort_flag))) {
           stop = true;
           break;
         }
         tmem_fence_after();
-        uint32_t vg[32];
-        tmem_ld32(tmem + lane_base + kAccCol + (tb * 2) * kN + n0, vg);
-        if (SWIGLU) {
-          uint32_t vu[32];
-          tmem_ld32(tmem + lane_base + kAccCol + (tb * 2 + 1) * kN + n0, vu);
+        const float sk = sc.at(kb) * decode_unscale<FINITE>();
+        if (active) {
+          uint32_t v[32];
+          tmem_ld32(tmem + lane_base + kAccCol + cb * kN + n0, v);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) tu[i] = __uint_as_float(vu[i]) * mu;
-        } else {
+          for (int i = 0; i < 32; ++i) tot[i] = fmaf(sk, __uint_as_float(v[i]), tot[i]);
+          tmem_ld32(tmem + lane_base + kAccCol + cb * kN + n0 + 32, v);
           tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) tot[32 + i] = fmaf(sk, __uint_as_float(v[i]), tot[32 + i]);
         }
-#pragma unroll
-        for (int i = 0; i < 32; ++i) tg[i] = __uint_as_float(vg[i]) * mg;
         tmem_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(bar(&bars->acc_empty[tb]));
-        ++tcount;
-      }
-      for (int kb = 0; kb < (SCALED ? 0 : nkb); ++kb, ++g) {
-        const int ab = g & 1;
-        const uint32_t aph = (g >> 1) & 1u;
-        if (!__all_sync(0xffffffffu, mbar_wait(bar(&bars->acc_full[ab]), aph, abort_flag))) {
-          stop = true;
-          break;
-        }
-        tmem_fence_after();
-        const float s_g = sgs.at(kb) * decode_unscale<FINITE>();
-        const float s_u = SWIGLU ? sus.at(kb) * decode_unscale<FINITE>() : 0.f;
-        uint32_t vg[32];
-        tmem_ld32(tmem + lane_base + kAccCol + (ab * 2) * kN + n0, vg);
-        if (SWIGLU) {
-          uint32_t vu[32];
-          tmem_ld32(tmem + lane_base + kAccCol + (ab * 2 + 1) * kN + n0, vu);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) tu[i] = fmaf(s_u, __uint_as_float(vu[i]), tu[i]);
-        } else {
-          tmem_wait_ld();
-        }
-#pragma unroll
-        for (int i = 0; i < 32; ++i) tg[i] = fmaf(s_g, __uint_as_float(vg[i]), tg[i]);
-        tmem_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(&bars->acc_empty[ab]));
+        if (lane == 0) mbar_arrive(bar(&bars->acc_empty[cb]));
       }
       if (stop) break;
-      const int col = tl.mt * kM + r;
-      if (SWIGLU) {
-        // route n0 + n: the reference's BF16 SwiGLU of this row's gate and up
-        // totals; the totals shift down one register per route so that the
-        // rolled loop never indexes the arrays at run time
-#pragma unroll 1
-        for (int n = 0; n < 32; ++n) {
-          const float x = __shfl_sync(0xffffffffu, xs, n);
-          const float gv = tg[0] * x, uv = tu[0] * x;
+      // route range multipliers of this half: lane l holds routes n0 + l and n0 + 32 + l
+      const float xa = (a.xscale && n0 + lane < tl.len) ? __ldg(a.xscale + tl.start + n0 + lane) : 1.0f;
+      const float xb = (a.xscale && n0 + 32 + lane < tl.len) ? __ldg(a.xscale + tl.start + n0 + 32 + lane) : 1.0f;
+      if (!SWIGLU) {
+        const int col = row0 + r;
 #pragma unroll
-          for (int i = 0; i < 31; ++i) {
-            tg[i] = tg[i + 1];
-            tu[i] = tu[i + 1];
-          }
-          if (n0 + n < tl.len) {
-            const uint16_t hv = swiglu_bf16_tab(gv, uv, a.limit);
-            const __half hh = __float2half_rn(bf16_bits_to_f32(hv));
-            a.out[(size_t)(tl.start + n0 + n) * a.out_cols + col] = *reinterpret_cast<const uint16_t*>(&hh);
-          }
+        for (int n = 0; n < 64; ++n) {
+          const float x = __shfl_sync(0xffffffffu, n < 32 ? xa : xb, n & 31);
+          if (n0 + n < tl.len) a.out[(size_t)(tl.start + n0 + n) * a.out_cols + col] = f32_to_bf16_bits(tot[n] * x);
         }
       } else {
+        const uint32_t xph = tcount & 1u;
+        if (up_rows) {
+          // up row r - 64: the reference's BF16 up value per route, [route][row]
+          if (!__all_sync(0xffffffffu, mbar_wait(bar(&bars->xch_empty), xph ^ 1u, abort_flag))) break;
+          const int u = r - 64;
 #pragma unroll
-        for (int n = 0; n < 32; ++n) {
-          const float x = __shfl_sync(0xffffffffu, xs, n);
-          if (n0 + n < tl.len) a.out[(size_t)(tl.start + n0 + n) * a.out_cols + col] = f32_to_bf16_bits(tg[n] * x);
+          for (int n = 0; n < 64; ++n) {
+            const float x = __shfl_sync(0xffffffffu, n < 32 ? xa : xb, n & 31);
+            xch[(n0 + n) * 64 + u] = f32_to_bf16_bits(tot[n] * x);
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(&bars->xch_full));
+        } else {
+          if (!__all_sync(0xffffffffu, mbar_wait(bar(&bars->xch_full), xph, abort_flag))) break;
+          const int col = row0 + r;
+#pragma unroll
+          for (int n = 0; n < 64; ++n) {
+            const float x = __shfl_sync(0xffffffffu, n < 32 ? xa : xb, n & 31);
+            if (n0 + n < tl.len) {
+              const uint16_t hv = swiglu_bf16_tab(tot[n] * x, bf16_bits_to_f32(xch[(n0 + n) * 64 + r]), a.limit);
+              const __half hh = __float2half_rn(bf16_bits_to_f32(hv));
+              a.out[(size_t)(tl.start + n0 + n) * a.out_cols + col] = *reinterpret_cast<const uint16_t*>(&hh);
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(&bars->xch_empty));
         }
+        ++tcount;
       }
     }
   }
@@ -758,7 +719,8 @@ static int ensure_sigmoid_table(cudaStream_t st) {
 }  // namespace tc
 
 bool grouped_tc_supported(int64_t K, int64_t N, float limit, bool swiglu) {
-  if (K % tc::kKB != 0 || N % tc::kM != 0 || K <= 0) return false;
+  // plain tiles are 128 output rows; SwiGLU tiles 64 hidden rows inside one 128-row scale block
+  if (K % tc::kKB != 0 || N % (swiglu ? 64 : tc::kM) != 0 || K <= 0) return false;
   // FP16 hidden rows: |SwiGLU| <= limit^2 must stay inside FP16 range
   if (swiglu && !(limit > 0.0f && limit <= 128.0f)) return false;
   return true;
@@ -773,18 +735,21 @@ int grouped_tc(const TcGemm& g, cudaStream_t st) {
     return GLM53_ERR_INVALID;
   }
   if (g.capacity == 0) return GLM53_OK;
-  CUtensorMap wmap, umap, xmap;
+  CUtensorMap wmap, umap, xmap, xmap64;
+  const uint32_t wbox = g.swiglu ? kM / 2 : kM;  // SwiGLU: 64 gate rows + 64 up rows per tile
   int rc = make_map(&wmap, g.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)g.K, (uint64_t)(g.E * g.w_rows), kKB,
-                    kM);
+                    wbox);
   if (rc) return rc;
   if (g.swiglu) {
     rc = make_map(&umap, g.w_up, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)g.K, (uint64_t)(g.E * g.u_rows), kKB,
-                  kM);
+                  wbox);
     if (rc) return rc;
   } else {
     umap = wmap;
   }
   rc = make_map(&xmap, g.x16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)g.K, (uint64_t)g.R, 64, kN);
+  if (rc) return rc;
+  rc = make_map(&xmap64, g.x16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)g.K, (uint64_t)g.R, 64, kN / 2);
   if (rc) return rc;
   TcArgs a{};
   a.tile_experts = g.tile_experts;
@@ -805,7 +770,7 @@ int grouped_tc(const TcGemm& g, cudaStream_t st) {
   a.out_cols = (int)cols;
   a.out = g.out;
   a.status = g.status;
-  const int mtiles = (int)(cols / kM);
+  const int mtiles = (int)(cols / wbox);
   const int zsub = g.dense ? 1 : (int)((g.max_rows + kN - 1) / kN);
   const int64_t ntiles = g.capacity * mtiles * zsub;
   if (ntiles > INT32_MAX) {
@@ -813,26 +778,20 @@ int grouped_tc(const TcGemm& g, cudaStream_t st) {
     return GLM53_ERR_INVALID;
   }
   const int grid = (int)std::min<int64_t>(ntiles, sm_count());
-  void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, TcArgs, int, int, int);
+  void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, TcArgs, int, int, int);
   size_t smem;
   if (g.swiglu) {
     rc = ensure_sigmoid_table(st);
     if (rc) return rc;
-    if (g.scaled)
-      kern = g.finite ? grouped_tc_kernel<true, true, true> : grouped_tc_kernel<true, false, true>;
-    else
-      kern = g.finite ? grouped_tc_kernel<true, true, false> : grouped_tc_kernel<true, false, false>;
+    kern = g.finite ? grouped_tc_kernel<true, true> : grouped_tc_kernel<true, false>;
     smem = smem_bytes<true>();
   } else {
-    if (g.scaled)
-      kern = g.finite ? grouped_tc_kernel<false, true, true> : grouped_tc_kernel<false, false, true>;
-    else
-      kern = g.finite ? grouped_tc_kernel<false, true, false> : grouped_tc_kernel<false, false, false>;
+    kern = g.finite ? grouped_tc_kernel<false, true> : grouped_tc_kernel<false, false>;
     smem = smem_bytes<false>();
   }
   rc = ensure_max_smem((const void*)kern, smem);
   if (rc) return rc;
-  kern<<<grid, kThreads, smem, st>>>(wmap, umap, xmap, a, (int)ntiles, mtiles, zsub);
+  kern<<<grid, kThreads, smem, st>>>(wmap, umap, xmap, xmap64, a, (int)ntiles, mtiles, zsub);
   return check_launch("grouped_tc_kernel");
 }
 

@@ -67,7 +67,7 @@ struct TcGemm {
   const uint32_t* tile_lengths;
   int64_t capacity;
   int64_t max_rows;       // longest descriptor (ignored when dense)
-  bool dense;             // descriptors implicit: (0, 64 d, min(64, R - 64 d))
+  bool dense;             // descriptors implicit: (0, 128 d, min(128, R - 128 d))
   const uint8_t* w;       // gate (or plain) weights, w_rows rows per expert
   const uint8_t* w_up;    // up weights (SwiGLU), u_rows rows per expert
   int64_t w_rows, u_rows, u_off;
@@ -80,7 +80,6 @@ struct TcGemm {
   bool swiglu;
   float limit;
   bool finite;            // no 0x7F/0xFF codes: hardware E4M3 conversion
-  bool scaled;            // block scales folded into the FP16 A operand (whole-K accumulation)
   uint16_t* out;
   uint32_t* status;
 };
