@@ -11,20 +11,19 @@
 //   warp 0      TMA producer: raw E4M3 weight tiles [128 rows x 128 K] and
 //               activation tiles [routes x 128 K] (FP16, two 64-K boxes,
 //               128-byte swizzle) into two rings of their own depths;
-//   warps 1, 15 issue tcgen05.mma (kind::f16, M128, N = 128, or 64 for a tile
+//   warps 1, 14 issue tcgen05.mma (kind::f16, M128, N = 128, or 64 for a tile
 //               of <= 64 routes; A from TMEM, B from shared memory, FP32
-//               accumulation in TMEM), warp 1 the even k-blocks and warp 15
+//               accumulation in TMEM), warp 1 the even k-blocks and warp 14
 //               the odd ones: consecutive k-blocks write different
-//               accumulators, and one thread's barrier wait and commit
+//               accumulators, and one thread's barrier waits and commit
 //               (~300 cycles each) would leave the tensor core idle between
-//               its k-blocks; each issuer waits on one barrier per k-block
-//               and commits to one; warp 1 also allocates TMEM;
+//               its k-blocks; per k-block an issuer checks that the
+//               activations landed, that the epilogue has read the
+//               accumulator, and that the A operand is decoded, then commits
+//               once; warp 1 also allocates TMEM;
 //   warps 2-5   decode each weight row exactly to FP16 (lut(c), or lut(c)/256
 //               on the bit-exact path for banks holding 0x7F/0xFF) into a
 //               4-deep TMEM ring (A operand, one TMEM lane per weight row);
-//   warp 14     gatekeeper: confirms that each k-block's activations have
-//               landed and that its accumulator is free, and counts as the
-//               fifth arrival of the k-block's A-operand barrier;
 //   warps 6-13  epilogue (two warps per TMEM lane quarter, 64 routes each):
 //               after every 128-K block, read the block's partial product
 //               from TMEM and promote it in FP32 with the 128x128 block scale
@@ -67,7 +66,7 @@ constexpr int kKB = 128;        // K per block-scale block
 constexpr int kRawStages = 7;   // weight ring (E4M3, 16 KB per stage): covers ~5,000-cycle HBM latency
 constexpr int kActStages = 3;   // activation ring (FP16, 32 KB per stage), mostly L2 hits
 constexpr int kRing = 4;        // decoded A operands in TMEM = k-block completion slots
-constexpr int kThreads = 512;   // 16 warps
+constexpr int kThreads = 480;   // 15 warps
 constexpr int kEpiWarps = 8;    // two per TMEM lane quarter, 64 routes each
 constexpr int kRawBytes = kM * kKB;      // 16 KB of E4M3 per stage
 constexpr int kActBox = kN * 64 * 2;     // one 64-K box of up to 128 routes (FP16)
@@ -339,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int s = 0; s < kActStages; ++s) mbar_init(bar(&bars->act_full[s]), 1);
     for (int s = 0; s < kRing; ++s) {
-      mbar_init(bar(&bars->a_full[s]), 5);  // four decode warps + the gatekeeper
+      mbar_init(bar(&bars->a_full[s]), 4);  // the four decode warps
       mbar_init(bar(&bars->kb_done[s]), 1);
     }
     for (int s = 0; s < 2; ++s) mbar_init(bar(&bars->acc_empty[s]), kEpiWarps);
@@ -454,7 +453,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (uint32_t k = ca.g > (uint32_t)kActStages ? ca.g - kActStages : 0u; k < ca.g; ++k)
         mbar_wait(bar(&bars->act_full[k % kActStages]), (k / kActStages) & 1u, &zero);
     }
-  } else if (warp == 1 || warp == 15) {
+  } else if (warp == 1 || warp == 14) {
     // ---------------- MMA issuers (even / odd k-blocks) ----------------
     if (lane == 0) {
       const uint32_t parity = warp == 1 ? 0u : 1u;
@@ -469,8 +468,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int s = g % kRing;
           const int as = g % kActStages;
           const int cb = g & 1;
-          // a_full implies the activations landed and the accumulator is free
-          if (!mbar_wait(bar(&bars->a_full[s]), (g / kRing) & 1u, abort_flag)) {
+          if (!mbar_wait(bar(&bars->act_full[as]), (g / kActStages) & 1u, abort_flag) ||
+              !mbar_wait(bar(&bars->acc_empty[g & 1]), ((g >> 1) & 1u) ^ 1u, abort_flag) ||
+              !mbar_wait(bar(&bars->a_full[s]), (g / kRing) & 1u, abort_flag)) {
             stop = true;
             break;
           }
@@ -490,26 +490,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       int zero = 0;
       mma_commit(bar(&bars->drain));
       mbar_wait(bar(&bars->drain), 0, &zero);
-    }
-    __syncwarp();
-  } else if (warp == 14) {
-    // ---------------- gatekeeper ----------------
-    // k-block g may be issued once its activations are in shared memory and
-    // the epilogue has read accumulator g % 2 (k-block g - 2)
-    if (lane == 0) {
-      uint32_t g = 0;
-      bool stop = false;
-      for (int t = blockIdx.x; t < ntiles && !stop; t += gridDim.x) {
-        if (tile_at(a, t, mtiles, zsub).len == 0) continue;
-        for (int kb = 0; kb < nkb; ++kb, ++g) {
-          if (!mbar_wait(bar(&bars->act_full[g % kActStages]), (g / kActStages) & 1u, abort_flag) ||
-              !mbar_wait(bar(&bars->acc_empty[g & 1]), ((g >> 1) & 1u) ^ 1u, abort_flag)) {
-            stop = true;
-            break;
-          }
-          mbar_arrive(bar(&bars->a_full[g % kRing]));
-        }
-      }
     }
     __syncwarp();
   } else if (warp < 6) {
