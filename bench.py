@@ -55,6 +55,8 @@ def parse_args():
     p.add_argument("--experts", type=int, default=E, help="routed experts per layer (profiling uses fewer)")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     p.add_argument("--no-e2e", action="store_true", help="skip the module-API end-to-end pass")
+    p.add_argument("--quick-linear", action="store_true", help="config-5 sweep at M in {1, 64, 512} only")
+    p.add_argument("--linear-only", action="store_true", help="run only the config-1/5 block-linear sweep")
     p.add_argument("--prefill-only", action="store_true",
                    help="profiling aid: only the T=2048 grouped prefill measurement (prints its JSON and exits)")
     p.add_argument("--prefill-reps", type=int, default=8, help="timed grouped prefill layers")
@@ -170,8 +172,9 @@ def measured_peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
-    return {"hbm_gbs": 6650.0, "source": "fallback"}
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d.get("bf16_tflops", 1590.0)),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
 # ---------------------------------------------------------------------------
@@ -383,49 +386,68 @@ def bench_b200(args, world, rank, local):
                            "note": "router and gate/up each timed alone (64 calls per CUDA graph)"}}
     if not args.no_prefill:
         extra["prefill_2048"] = bench_prefill(layers, dev, args)
-        extra["linear_config1"] = bench_linear(dev, args)
+        extra["linear_config1_5"] = bench_linear(dev, args)
     return {"value": value, "t_ms": t_ms, "clocks": clk, "roofline": roofline, "e2e": e2e,
             "gpu_launches": args.steps * 3, **extra}, layers, xs
 
 
 def bench_linear(dev, args):
     """Secondary: config 1 (block-FP8 GEMV y = x . W^T, W E4M3 [6144, 4096] +
-    128x128 scales, x BF16 [1, 4096]) and the same weights at larger M
-    (config 5 shapes).  8 weight copies rotate (201 MB > L2); 64 calls per CUDA
-    graph, CUDA events."""
+    128x128 scales, x BF16 [1, 4096]) and the config-5 sweep: W in {[6144, 4096],
+    [4096, 4096], [12288, 4096], [4096, 12288], [576, 4096]} at M in {1, 8, 64,
+    512, 2048, 8192}.  Weight copies rotate (>= 200 MB per shape, above L2); 64
+    calls per CUDA graph, CUDA events.  M <= 16 calls glm53_fp8_linear (GEMV
+    tiles), larger M glm53_fp8_linear_ws (tcgen05 GEMM), as block_fp8_linear does."""
     import torch
 
     from glm53_flash_mlx_b200 import _native as N
     from glm53_flash_mlx_b200 import synthetic as S
 
     lib = N.lib()
-    Nn, K, copies = 6144, 4096, 8
-    ws = []
-    for c in range(copies):
-        w, sc = S.random_block_fp8(Nn, K, seed=c, tensor=0, std=0.02, device=dev)
-        ws.append((w, sc))
-    fl = N.decode_flags(*[w for w, _ in ws])
     peaks = measured_peaks()
-    res = {}
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
     s = torch.cuda.Stream(device=dev)
-    for M in (1, 8, 64, 512):
-        x = S.random_bf16((M, K), seed=M, device=dev)
-        y = torch.empty((M, Nn), dtype=torch.bfloat16, device=dev)
+    shapes = [(6144, 4096), (4096, 4096), (12288, 4096), (4096, 12288), (576, 4096)]
+    ms_list = (1, 8, 64, 512, 2048, 8192) if not args.quick_linear else (1, 64, 512)
+    out = {}
+    for (Nn, K) in shapes:
+        copies = max(2, -(-200_000_000 // (Nn * K)))
+        wts = [S.random_block_fp8(Nn, K, seed=c, tensor=0, std=0.02, device=dev) for c in range(copies)]
+        fl = N.decode_flags(*[w for w, _ in wts])
+        res = {}
+        for M in ms_list:
+            x = S.random_bf16((M, K), seed=M, device=dev)
+            y = torch.empty((M, Nn), dtype=torch.bfloat16, device=dev)
+            wsb = lib.glm53_fp8_linear_workspace_bytes(M, K)
+            wsp = torch.zeros(max(wsb, 256), dtype=torch.uint8, device=dev)
 
-        def call(i, stream):
-            w, sc = ws[i % copies]
-            N.check(lib.glm53_fp8_linear(x.data_ptr(), M, K, w.data_ptr(), Nn, sc.data_ptr(), y.data_ptr(), fl,
-                                         stream), "linear")
+            def call(i, stream):
+                w, sc = wts[i % copies]
+                if M > 16:
+                    N.check(lib.glm53_fp8_linear_ws(x.data_ptr(), M, K, w.data_ptr(), Nn, sc.data_ptr(), y.data_ptr(),
+                                                    wsp.data_ptr(), wsp.numel(), status.data_ptr(), fl, stream),
+                            "linear_ws")
+                else:
+                    N.check(lib.glm53_fp8_linear(x.data_ptr(), M, K, w.data_ptr(), Nn, sc.data_ptr(), y.data_ptr(),
+                                                 fl, stream), "linear")
 
-        ms = time_stage_graph(call, 64, 8, s, dev)
-        bytes_ = Nn * K + 4 * (Nn // 128) * (K // 128) + 2 * M * K + 2 * M * Nn
-        flops = 2 * M * Nn * K
-        res[f"M{M}"] = {"us": round(ms * 1e3, 2), "gbs": round(bytes_ / (ms / 1e3) / 1e9, 1),
-                        "hbm_frac": round(bytes_ / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
-                        "tflops": round(flops / (ms / 1e3) / 1e12, 2)}
-    return {"shape": "W [6144, 4096] E4M3 + [48, 32] FP32 scales; x BF16 [M, 4096]; "
-                     "M=1 is config 1, M>1 the config-5 sweep of this shape",
-            "results": res, "note": "M <= 16: tensor-core GEMV tiles; M > 16: mma.sync tile GEMM (BF16 x lut*s)"}
+            n_calls = 64 if M <= 2048 else 16
+            ms = time_stage_graph(call, n_calls, 4, s, dev)
+            bytes_ = Nn * K + 4 * (-(-Nn // 128)) * (K // 128) + 2 * M * K + 2 * M * Nn
+            flops = 2 * M * Nn * K
+            res[f"M{M}"] = {"us": round(ms * 1e3, 2),
+                            "hbm_frac": round(bytes_ / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
+                            "tflops": round(flops / (ms / 1e3) / 1e12, 1),
+                            "tensor_frac": round(flops / (ms / 1e3) / 1e12 / peaks["bf16_tflops"], 4)}
+            del x, y, wsp
+        out[f"{Nn}x{K}"] = res
+        del wts
+    if int(status.item()) != 0:
+        raise RuntimeError(f"device status 0x{int(status.item()):x} in the linear sweep")
+    return {"shapes": "W [N, K] E4M3 + FP32 128x128 scales; x BF16 [M, K]; 6144x4096 at M=1 is config 1",
+            "results": out,
+            "note": "M <= 16: tensor-core GEMV tiles (HBM-bound); M > 16: tcgen05 GEMM (kind::f16, exact FP16 "
+                    "weights, FP32 promotion per 128-K block); tensor_frac against the measured BF16 peak"}
 
 
 def build_ep_layers(n_layers: int, rank: int, world: int, device, experts: int = E):
@@ -728,6 +750,12 @@ def main():
 
             dist.destroy_process_group()
         return
+    if args.linear_only:
+        import torch
+
+        if rank == 0:
+            print(json.dumps({"linear_config1_5": bench_linear(torch.device("cuda", local), args)}), flush=True)
+        return
     if args.prefill_only:
         import torch
 
@@ -764,8 +792,8 @@ def main():
         line["stages_us"] = res["stages_us"]
     if "prefill_2048" in res:
         line["prefill_2048"] = res["prefill_2048"]
-    if "linear_config1" in res:
-        line["linear_config1"] = res["linear_config1"]
+    if "linear_config1_5" in res:
+        line["linear_config1_5"] = res["linear_config1_5"]
     if rank == 0 and world == 1 and not args.no_cpu:
         import torch
 

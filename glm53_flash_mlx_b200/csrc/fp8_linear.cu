@@ -3,8 +3,9 @@
 // Replaces block_fp8_linear (glm53_flash_mlx/fp8.py:254-299) and its Metal
 // kernels K1/K2 (fp8.py:41-116).  Small M is HBM-bound: every weight byte is
 // read once with 16-byte streaming loads and decoded in registers into
-// tensor-core fragments (gemv_tile.cuh).  Large M goes to the grouped GEMM
-// with a single expert (grouped.cu).
+// tensor-core fragments (gemv_tile.cuh).  Large M goes to the tcgen05 GEMM
+// (grouped_tc.cu, one dense "expert") when the caller passes a workspace
+// (glm53_fp8_linear_ws), else to the mma.sync GEMM (grouped.cu).
 #include <algorithm>
 
 #include "common.cuh"
@@ -177,6 +178,55 @@ int fp8_linear_small_m(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w
 }  // namespace glm53
 
 using namespace glm53;
+
+// Workspace of glm53_fp8_linear_ws: FP16 activation rows and their power-of-two
+// multipliers for the tcgen05 path.
+static size_t linear_ws_bytes(int64_t M, int64_t K) {
+  return align_up((size_t)M * K * sizeof(__half), 256) + align_up((size_t)M * sizeof(float), 256);
+}
+
+extern "C" size_t glm53_fp8_linear_workspace_bytes(int64_t M, int64_t K) {
+  return M > 0 && K > 0 ? linear_ws_bytes(M, K) : 0;
+}
+
+extern "C" int glm53_fp8_linear_ws(const void* x, int64_t M, int64_t K, const uint8_t* w, int64_t N,
+                                   const float* scale_inv, void* y, void* workspace, size_t workspace_bytes,
+                                   uint32_t* status, uint32_t flags, void* stream) {
+  if (M < 0 || K <= 0 || N <= 0 || (M > 0 && (!x || !w || !scale_inv || !y))) {
+    set_last_error("glm53_fp8_linear_ws: invalid arguments M=%lld K=%lld N=%lld", (long long)M, (long long)K,
+                   (long long)N);
+    return GLM53_ERR_INVALID;
+  }
+  if (M == 0) return GLM53_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool aligned = ((((uintptr_t)x | (uintptr_t)w | (uintptr_t)workspace) & 15) == 0) && K % 8 == 0;
+  if (M > kGemvMaxRows && workspace && status && workspace_bytes >= linear_ws_bytes(M, K) && aligned &&
+      grouped_tc_supported(K, N, 0.0f, false) && M <= INT32_MAX / 2) {
+    __half* x16 = (__half*)workspace;
+    float* xscale = (float*)((char*)workspace + align_up((size_t)M * K * sizeof(__half), 256));
+    int rc = rows_to_f16((const uint16_t*)x, K, nullptr, 1, M, x16, xscale, st);
+    if (rc) return rc;
+    TcGemm g{};
+    g.x16 = x16;
+    g.xscale = xscale;
+    g.R = M;
+    g.K = K;
+    g.capacity = (M + 127) / 128;
+    g.max_rows = 128;
+    g.dense = true;
+    g.w = w;
+    g.w_rows = N;
+    g.s_gate = scale_inv;
+    g.E = 1;
+    g.N = N;
+    g.swiglu = false;
+    g.finite = (flags & GLM53_FLAG_E4M3_FINITE) != 0;
+    g.out = (uint16_t*)y;
+    g.status = status;
+    return grouped_tc(g, st);
+  }
+  return glm53_fp8_linear(x, M, K, w, N, scale_inv, y, flags, stream);
+}
 
 extern "C" int glm53_fp8_linear(const void* x, int64_t M, int64_t K, const uint8_t* w, int64_t N,
                                 const float* scale_inv, void* y, uint32_t flags, void* stream) {

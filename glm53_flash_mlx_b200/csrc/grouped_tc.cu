@@ -592,7 +592,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int n = 0; n < 64; ++n) {
           const float x = __shfl_sync(0xffffffffu, n < 32 ? xa : xb, n & 31);
-          if (n0 + n < tl.len) a.out[(size_t)(tl.start + n0 + n) * a.out_cols + col] = f32_to_bf16_bits(tot[n] * x);
+          // the last weight tile of a plain GEMM may extend past N (TMA zero-fills those rows)
+          if (n0 + n < tl.len && col < a.out_cols)
+            a.out[(size_t)(tl.start + n0 + n) * a.out_cols + col] = f32_to_bf16_bits(tot[n] * x);
         }
       } else {
         const uint32_t xph = tcount & 1u;
@@ -699,8 +701,9 @@ static int ensure_sigmoid_table(cudaStream_t st) {
 }  // namespace tc
 
 bool grouped_tc_supported(int64_t K, int64_t N, float limit, bool swiglu) {
-  // plain tiles are 128 output rows; SwiGLU tiles 64 hidden rows inside one 128-row scale block
-  if (K % tc::kKB != 0 || N % (swiglu ? 64 : tc::kM) != 0 || K <= 0) return false;
+  // SwiGLU tiles are 64 hidden rows inside one 128-row scale block; plain tiles
+  // are 128 output rows, the last one cut at N (8-row granularity)
+  if (K % tc::kKB != 0 || N <= 0 || N % (swiglu ? 64 : 8) != 0 || K <= 0) return false;
   // FP16 hidden rows: |SwiGLU| <= limit^2 must stay inside FP16 range
   if (swiglu && !(limit > 0.0f && limit <= 128.0f)) return false;
   return true;
@@ -709,7 +712,9 @@ bool grouped_tc_supported(int64_t K, int64_t N, float limit, bool swiglu) {
 int grouped_tc(const TcGemm& g, cudaStream_t st) {
   using namespace tc;
   const int64_t cols = g.swiglu ? g.I : g.N;
-  if (!grouped_tc_supported(g.K, cols, g.limit, g.swiglu) || g.R <= 0 || g.max_rows <= 0 ||
+  // a plain tile cut at N needs the rows past N to be out of the map (one expert)
+  const bool cut_ok = g.swiglu || g.N % kM == 0 || g.E == 1;
+  if (!grouped_tc_supported(g.K, cols, g.limit, g.swiglu) || !cut_ok || g.R <= 0 || g.max_rows <= 0 ||
       (((uintptr_t)g.x16 | (uintptr_t)g.w | (uintptr_t)(g.swiglu ? g.w_up : g.w)) & 15) != 0) {
     set_last_error("grouped_tc: unsupported geometry");
     return GLM53_ERR_INVALID;
@@ -750,7 +755,7 @@ int grouped_tc(const TcGemm& g, cudaStream_t st) {
   a.out_cols = (int)cols;
   a.out = g.out;
   a.status = g.status;
-  const int mtiles = (int)(cols / wbox);
+  const int mtiles = (int)((cols + wbox - 1) / wbox);
   const int zsub = g.dense ? 1 : (int)((g.max_rows + kN - 1) / kN);
   const int64_t ntiles = g.capacity * mtiles * zsub;
   if (ntiles > INT32_MAX) {

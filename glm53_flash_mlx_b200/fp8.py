@@ -26,6 +26,12 @@ def _scale_shape(out_features: int, in_features: int) -> tuple[int, int]:
     return ((out_features + BLOCK_SIZE - 1) // BLOCK_SIZE, (in_features + BLOCK_SIZE - 1) // BLOCK_SIZE)
 
 
+# Rows handled by the bandwidth GEMV (kGemvMaxRows in csrc/kernels.cuh); more
+# rows go to the tcgen05 GEMM through glm53_fp8_linear_ws.
+_GEMV_MAX_ROWS = 16
+_LINEAR_WS = N.Workspace()
+
+
 def block_fp8_linear(x: torch.Tensor, weight: torch.Tensor, scale_inv: torch.Tensor, *,
                      e4m3_finite: bool = False) -> torch.Tensor:
     """Compute ``x @ dequant(weight, scale_inv).T`` without expanding weight.
@@ -56,12 +62,25 @@ def block_fp8_linear(x: torch.Tensor, weight: torch.Tensor, scale_inv: torch.Ten
     weight = weight.contiguous()
     scale_inv = scale_inv.contiguous()
     out = torch.empty((flat.shape[0], out_features), dtype=x.dtype, device=x.device)
-    if flat.shape[0]:
+    M = flat.shape[0]
+    flags = N.FLAG_E4M3_FINITE if e4m3_finite else 0
+    if M > _GEMV_MAX_ROWS:
+        # tensor-core GEMM: scratch for the FP16 activation rows, one per device and stream
+        stream = N.stream(x.device)
+        ws = _LINEAR_WS.get(x.device, f"rows:{stream}", N.lib().glm53_fp8_linear_workspace_bytes(M, in_features))
+        status = _LINEAR_WS.get(x.device, "status", 4)
+        N.check(
+            N.lib().glm53_fp8_linear_ws(
+                flat.data_ptr(), M, in_features, weight.data_ptr(), out_features, scale_inv.data_ptr(),
+                out.data_ptr(), ws.data_ptr(), ws.numel(), status.data_ptr(), flags, stream,
+            ),
+            "glm53_fp8_linear_ws",
+        )
+    elif M:
         N.check(
             N.lib().glm53_fp8_linear(
-                flat.data_ptr(), flat.shape[0], in_features, weight.data_ptr(), out_features,
-                scale_inv.data_ptr(), out.data_ptr(), N.FLAG_E4M3_FINITE if e4m3_finite else 0,
-                N.stream(x.device),
+                flat.data_ptr(), M, in_features, weight.data_ptr(), out_features,
+                scale_inv.data_ptr(), out.data_ptr(), flags, N.stream(x.device),
             ),
             "glm53_fp8_linear",
         )

@@ -74,6 +74,21 @@ int glm53_fp8_linear(const void* x, int64_t M, int64_t K, const uint8_t* w,
                      int64_t N, const float* scale_inv, void* y, uint32_t flags,
                      void* stream);
 
+/* Workspace bytes of glm53_fp8_linear_ws for M rows of width K. */
+size_t glm53_fp8_linear_workspace_bytes(int64_t M, int64_t K);
+
+/* glm53_fp8_linear with caller scratch: for M > 16 rows, K % 128 == 0, N % 8
+ * == 0 and 16-byte aligned x / w / workspace it runs the tcgen05 GEMM (the
+ * activations converted once to FP16 x 2^-e rows in the workspace; exact FP16
+ * weight products, FP32 promotion per 128-K block); otherwise it is
+ * glm53_fp8_linear.  `status` (device word) receives GLM53_STATUS_WAIT_TIMEOUT
+ * if a bounded wait gave up.  Same results contract as glm53_fp8_linear.
+ * Replaces block_fp8_linear at large M, glm53_flash_mlx/fp8.py:254-299 (K2,
+ * fp8.py:73-116). */
+int glm53_fp8_linear_ws(const void* x, int64_t M, int64_t K, const uint8_t* w, int64_t N,
+                        const float* scale_inv, void* y, void* workspace, size_t workspace_bytes,
+                        uint32_t* status, uint32_t flags, void* stream);
+
 /* Count (into *nan_count, device memory, accumulated) the 4-byte words of
  * w[n] that hold an E4M3 code 0x7F or 0xFF; zero means GLM53_FLAG_E4M3_FINITE
  * may be passed for these weights.  w must be 16-byte aligned.

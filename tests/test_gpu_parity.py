@@ -484,3 +484,16 @@ def test_captured_decode_matches_module_call(G, S):
         got = cap(x.cpu().pin_memory()).clone()
         torch.cuda.synchronize()
         assert torch.equal(got, want), t
+
+
+@pytest.mark.parametrize("M,N_,K", [(64, 576, 4096), (300, 1024, 1536), (2048, 4096, 4096)])
+def test_block_linear_tensor_core_path_matches_oracle(G, S, oracle, M, N_, K):
+    """M > 16 runs the tcgen05 GEMM through glm53_fp8_linear_ws (N = 576 cuts the
+    last 128-row weight tile); the oracle checks a row subset at the largest M."""
+    w, s = S.random_block_fp8(N_, K, seed=M, tensor=3, std=0.02, device="cuda")
+    x = S.random_bf16((M, K), seed=M + 1, device="cuda", std=1.5)
+    y = G.block_fp8_linear(x, w, s)
+    torch.cuda.synchronize()
+    rows = np.arange(M) if M <= 300 else np.random.default_rng(M).choice(M, 48, replace=False)
+    ref = oracle.block_fp8_linear(bits(x)[rows], w.cpu().numpy(), s.cpu().numpy())
+    assert_layer_close(bits(y)[rows], ref, max_abs=0.03125)
