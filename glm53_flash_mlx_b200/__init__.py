@@ -14,6 +14,13 @@ from .abi import (  # noqa: F401
     PACKED_DECODE_KERNEL_ABI,
     PACKED_EXPERT_BANK_ABI,
 )
+from .checkpoint import (  # noqa: F401
+    CheckpointIndex,
+    load_packed_bank,
+    load_packed_moe,
+    load_router,
+    load_shared_expert,
+)
 from .fp8 import BlockFP8Linear, DirectFP8Expert, DirectFP8MoE, block_fp8_linear  # noqa: F401
 from .grouped_fp8 import (  # noqa: F401
     SortedGroupedFP8MoE,

@@ -5,7 +5,8 @@ Counterpart of glm53_flash_mlx/loader.py:167-254 (``install_packed_moe``,
 ``DirectFP8MoE`` layer is packed into a ``PackedFP8ExpertBank`` one layer at a
 time, the layer's module is swapped, the old per-expert modules are released,
 and a per-layer memory report is returned.  Installing twice converts nothing.
-Checkpoint loading is out of scope (no checkpoint exists here).
+Reading a block-FP8 safetensors checkpoint straight into packed banks (no
+DirectFP8MoE stage) is ``checkpoint.py``.
 """
 
 from __future__ import annotations
