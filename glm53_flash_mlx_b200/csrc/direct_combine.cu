@@ -1,0 +1,93 @@
+// Direct-module combine for a small batch of decode tokens.
+//
+// Replaces the scatter-add loop of DirectFP8MoE.__call__ for more than one
+// row (glm53_flash_mlx/fp8.py:384-399): for every touched expert in ascending
+// id, weighted = BF16(f32(expert_out) * f32(score)) is added into a BF16
+// result row (BF16(f32(a) + f32(b)), the order index_add applies them), and
+// the shared expert's BF16 output is added last.  The per-route expert
+// outputs come from glm53_routes_decode; one CTA per token sorts its slots by
+// expert id (a token selects an expert at most once, ties keep slot order)
+// and its threads sweep 8 columns each.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace glm53 {
+
+constexpr int kCombineMaxK = 32;
+
+__global__ void __launch_bounds__(256) direct_combine_kernel(const uint16_t* __restrict__ rows,
+                                                             const uint32_t* __restrict__ ids,
+                                                             const float* __restrict__ scores, int top_k, int H,
+                                                             const uint16_t* __restrict__ shared,
+                                                             uint16_t* __restrict__ out) {
+  __shared__ int order[kCombineMaxK];
+  const int t = blockIdx.x;
+  if (threadIdx.x == 0) {
+    for (int j = 0; j < top_k; ++j) order[j] = j;
+    for (int i = 1; i < top_k; ++i) {  // insertion sort by expert id, stable
+      const int v = order[i];
+      const uint32_t key = ids[(size_t)t * top_k + v];
+      int p = i - 1;
+      while (p >= 0 && ids[(size_t)t * top_k + order[p]] > key) {
+        order[p + 1] = order[p];
+        --p;
+      }
+      order[p + 1] = v;
+    }
+  }
+  __syncthreads();
+  for (int c = 8 * (blockIdx.y * blockDim.x + threadIdx.x); c < H; c += 8 * blockDim.x * gridDim.y) {
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    for (int j = 0; j < top_k; ++j) {
+      const int slot = t * top_k + order[j];
+      const float sc = scores[slot];
+      const uint4 v = *reinterpret_cast<const uint4*>(rows + (size_t)slot * H + c);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float lo = bf16_round(__fmul_rn(__uint_as_float(w[i] << 16), sc));
+        const float hi = bf16_round(__fmul_rn(__uint_as_float(w[i] & 0xFFFF0000u), sc));
+        acc[2 * i] = bf16_round(acc[2 * i] + lo);
+        acc[2 * i + 1] = bf16_round(acc[2 * i + 1] + hi);
+      }
+    }
+    if (shared) {
+      const uint4 v = *reinterpret_cast<const uint4*>(shared + (size_t)t * H + c);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        acc[2 * i] = bf16_round(acc[2 * i] + __uint_as_float(w[i] << 16));
+        acc[2 * i + 1] = bf16_round(acc[2 * i + 1] + __uint_as_float(w[i] & 0xFFFF0000u));
+      }
+    }
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      o[i] = (uint32_t)f32_to_bf16_bits(acc[2 * i]) | ((uint32_t)f32_to_bf16_bits(acc[2 * i + 1]) << 16);
+    *reinterpret_cast<uint4*>(out + (size_t)t * H + c) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+}  // namespace glm53
+
+using namespace glm53;
+
+extern "C" int glm53_direct_combine(const void* rows, const uint32_t* expert_ids, const float* scores, int64_t T,
+                                    int top_k, int64_t H, const void* shared, void* out, void* stream) {
+  if (T < 0 || top_k <= 0 || top_k > kCombineMaxK || H <= 0 || H % 8 != 0 || H > INT32_MAX / 2 ||
+      (T > 0 && (!rows || !expert_ids || !scores || !out)) ||
+      (((uintptr_t)rows | (uintptr_t)out | (uintptr_t)shared) & 15) != 0) {
+    set_last_error("glm53_direct_combine: invalid arguments T=%lld top_k=%d H=%lld", (long long)T, top_k,
+                   (long long)H);
+    return GLM53_ERR_INVALID;
+  }
+  if (T == 0) return GLM53_OK;
+  const int per = (int)((H / 8 + 255) / 256);
+  dim3 grid((unsigned)T, (unsigned)std::min(per, 8));
+  direct_combine_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
+      (const uint16_t*)rows, expert_ids, scores, top_k, (int)H, (const uint16_t*)shared, (uint16_t*)out);
+  return check_launch("direct_combine_kernel");
+}

@@ -162,6 +162,9 @@ class DirectFP8MoE(nn.Module):
 
     def forward(self, x):
         indices, scores = self.gate(x)
+        return self._forward_routes(x, indices, scores)
+
+    def _forward_routes(self, x, indices, scores):
         # Routing is a phase boundary: one readback gives the host the expert
         # buckets (glm53_flash_mlx/fp8.py:366-369).
         routes = indices.reshape(-1, self.config.num_experts_per_tok).to(torch.int64).cpu()

@@ -245,6 +245,58 @@ def packed_decode_moe(x: torch.Tensor, expert_ids: torch.Tensor, scores: torch.T
     return None if split == "shared" else out
 
 
+# Largest batch of decode rows the batched path takes: up to 16 rows no expert
+# gets more than 16 routes, so the Direct module's per-expert projections all
+# run on the GEMV tiles, whose FP32 sums the per-route decode reproduces.
+BATCHED_DECODE_MAX_ROWS = 16
+
+
+def batched_decode_moe(x: torch.Tensor, indices: torch.Tensor, scores: torch.Tensor, bank: PackedFP8ExpertBank,
+                       shared_experts, *, limit: float, workspace: N.Workspace | None = None,
+                       status: torch.Tensor | None = None) -> torch.Tensor:
+    """A few decode rows through the packed bank with the Direct module's
+    semantics (glm53_flash_mlx/fp8.py:384-399), bit for bit: per-route expert
+    outputs (``glm53_routes_decode``), their BF16 scatter-add in ascending
+    expert id (``glm53_direct_combine``), plus the shared expert module's
+    output.  x: BF16 [T, H]; indices / scores: [T, top_k]."""
+    dev = N.require_cuda(x, indices, scores, bank.gate_up_weight)
+    T, H = x.shape
+    if H != bank.hidden_size:
+        raise ValueError(f"decode input width {H} != bank hidden {bank.hidden_size}")
+    top_k = indices.shape[-1]
+    I = bank.intermediate_size
+    R = T * top_k
+    x = x.contiguous()
+    ids = indices.reshape(-1).to(torch.int32).contiguous()
+    sc = scores.reshape(-1).to(torch.float32).contiguous()
+    x_rows = x.repeat_interleave(top_k, dim=0)  # route t * top_k + j reads token t
+    wsp = workspace or N.Workspace()
+    ws = wsp.get(dev, "routes", N.lib().glm53_routes_decode_workspace_bytes(R, H, I))
+    if status is None:
+        status = wsp.get(dev, "status", 4)
+    rows = torch.empty((R, H), dtype=torch.bfloat16, device=dev)
+    flags = N.decode_flags(bank.gate_up_weight, bank.down_weight)
+    N.check(
+        N.lib().glm53_routes_decode(
+            x_rows.data_ptr(), R, H, ids.data_ptr(), bank.gate_up_weight.data_ptr(),
+            bank.gate_up_scale_inv.data_ptr(), bank.down_weight.data_ptr(), bank.down_scale_inv.data_ptr(),
+            bank.expert_count, I, float(limit), rows.data_ptr(), ws.data_ptr(), ws.numel(), status.data_ptr(),
+            flags, N.stream(dev),
+        ),
+        "glm53_routes_decode",
+    )
+    shared = shared_experts(x).contiguous() if shared_experts is not None else None
+    out = torch.empty_like(x)
+    N.check(
+        N.lib().glm53_direct_combine(rows.data_ptr(), ids.data_ptr(), sc.data_ptr(), T, top_k, H, N.ptr(shared),
+                                     out.data_ptr(), N.stream(dev)),
+        "glm53_direct_combine",
+    )
+    if _SYNC_STATUS:
+        check_status(status)
+    return out
+
+
 def check_status(status: torch.Tensor, *, clear: bool = True) -> None:
     """Raise for device-side fail-closed signals (one device->host read);
     the word is cleared first so the next call starts clean."""
@@ -320,7 +372,16 @@ class PackedFP8MoE(DirectFP8MoE):
     def forward(self, x):
         flat_x = x.reshape(-1, x.shape[-1])
         if flat_x.shape[0] != 1:
-            return super().forward(x)
+            if not 2 <= flat_x.shape[0] <= BATCHED_DECODE_MAX_ROWS:
+                return super().forward(x)
+            indices, scores = self.gate(x)
+            limit = self.config.swiglu_limit
+            if (indices.shape[-1] != DECODE_TOP_K or float(limit) != int(limit) or
+                    self.bank.hidden_size % BLOCK_SIZE or self.bank.intermediate_size % BLOCK_SIZE):
+                return self._forward_routes(x, indices, scores)
+            return batched_decode_moe(flat_x, indices.reshape(flat_x.shape[0], -1),
+                                      scores.reshape(flat_x.shape[0], -1), self.bank, self.shared_experts,
+                                      limit=limit, workspace=self._workspace).reshape(x.shape)
         indices, scores = self.gate(x)
         if indices.shape[-1] != DECODE_TOP_K:
             return super().forward(x)

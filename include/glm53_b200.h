@@ -205,6 +205,16 @@ int glm53_routes_decode(const void* x_rows, int64_t R, int64_t H, const uint32_t
                         float limit, void* out_rows, void* workspace, size_t workspace_bytes,
                         uint32_t* status, uint32_t flags, void* stream);
 
+/* Direct-module combine of a small decode batch: out[t] = the BF16 sum, in
+ * ascending expert id of token t's top_k routes, of BF16(f32(rows[t*top_k+j])
+ * * scores[t*top_k+j]) (each add rounded to BF16), then + shared[t] (BF16 add;
+ * shared may be NULL).  rows BF16 [T*top_k, H] (e.g. from glm53_routes_decode),
+ * expert_ids / scores [T*top_k], out BF16 [T, H]; H % 8 == 0, 16-byte aligned
+ * rows.  Replaces the expert-bucket scatter-add of DirectFP8MoE.__call__,
+ * glm53_flash_mlx/fp8.py:384-399. */
+int glm53_direct_combine(const void* rows, const uint32_t* expert_ids, const float* scores, int64_t T,
+                         int top_k, int64_t H, const void* shared, void* out, void* stream);
+
 /* Expert-parallel dispatch packing on the tokens' home rank.  Experts are
  * split into `world` contiguous ranges of E / world; route (t, j) with expert
  * e goes to rank d = e / (E / world), into the next free of `capacity` slots

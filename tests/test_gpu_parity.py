@@ -497,3 +497,45 @@ def test_block_linear_tensor_core_path_matches_oracle(G, S, oracle, M, N_, K):
     rows = np.arange(M) if M <= 300 else np.random.default_rng(M).choice(M, 48, replace=False)
     ref = oracle.block_fp8_linear(bits(x)[rows], w.cpu().numpy(), s.cpu().numpy())
     assert_layer_close(bits(y)[rows], ref, max_abs=0.03125)
+
+
+@pytest.mark.parametrize("T,E,H,I", [(2, 16, 1024, 256), (9, 32, 2048, 512), (16, 288, 4096, 1536)])
+def test_batched_decode_matches_oracle_and_direct_loop(G, S, oracle, T, E, H, I):
+    """2..16 decode rows: PackedFP8MoE's batched path (per-route decode + BF16
+    scatter-add in ascending expert id, glm53_flash_mlx/fp8.py:384-399) against
+    the oracle of that order, and against the Direct module's per-expert loop
+    over the same bank (whose GEMV splits K across warps, so an FP32 rounding may
+    differ: nearly all bits agree).  The Direct order adds eight weighted rows in
+    BF16, each add rounded, so one route's 1-ulp difference can surface as 2 ulps
+    of the sum (measured at config-2 size: the module's own Direct loop shows the
+    same 0.03125 at |y| in [2, 4) against the oracle); the bound here is
+    max(2e-2, 2 BF16 ulps), cosine 0.9999, and the batched path may not do worse
+    than the loop."""
+    from glm53_flash_mlx_b200.packed import shared_fp8_tensors
+    from glm53_flash_mlx_b200.router import Float32Gate
+
+    cfg = S.moe_config(H, I, E, 8, 10.0)
+    bank = S.make_bank(E, H, I, seed=T + 7, device="cuda")
+    shared = S.make_shared(H, I, seed=T + 8, device="cuda")
+    gate = Float32Gate(cfg, device="cuda")
+    w, b = S.make_router(E, H, seed=T + 9, device="cuda")
+    gate.weight.copy_(w)
+    gate.e_score_correction_bias.copy_(b)
+    mod = G.PackedFP8MoE(bank, cfg, gate, shared)
+    sh = shared_host(shared_fp8_tensors(shared))
+    for trial in range(2):
+        x = S.random_bf16((1, T, H), seed=100 * T + trial, device="cuda", std=1.5)
+        got = mod(x)
+        idx, sc = mod.gate(x)
+        loop = mod._forward_routes(x, idx, sc)
+        torch.cuda.synchronize()
+        ids = idx.reshape(T, 8).cpu().numpy().astype(np.int64)
+        scs = sc.reshape(T, 8).cpu().numpy()
+        touched, local = np.unique(ids, return_inverse=True)  # ascending ids keep the loop order
+        ref = oracle.direct_moe(bits(x.reshape(T, H)), local.reshape(T, 8), scs, bank_host(bank, touched), sh, 10.0)
+        stats = assert_layer_close(bits(got.reshape(T, H)), ref, ulps=2)
+        loop_stats = assert_layer_close(bits(loop.reshape(T, H)), ref, ulps=2)
+        assert stats["bit_identical"] >= 0.99, stats
+        assert stats["max_abs"] <= max(loop_stats["max_abs"], 2 ** -5), (stats, loop_stats)
+        same = float((bits(got) == bits(loop)).mean())
+        assert same >= 0.99, same
