@@ -387,8 +387,56 @@ def bench_b200(args, world, rank, local):
     if not args.no_prefill:
         extra["prefill_2048"] = bench_prefill(layers, dev, args)
         extra["linear_config1_5"] = bench_linear(dev, args)
+        extra["batched_decode"] = bench_batched(layers, dev, args)
     return {"value": value, "t_ms": t_ms, "clocks": clk, "roofline": roofline, "e2e": e2e,
             "gpu_launches": args.steps * 3, **extra}, layers, xs
+
+
+def bench_batched(layers, dev, args):
+    """Secondary: config 4's batched decode on one GPU -- B = 16 tokens through
+    PackedFP8MoE (router + batched per-route decode + BF16 combine + shared
+    expert) versus the Direct module's per-expert loop on the same layer."""
+    import torch
+
+    import glm53_flash_mlx_b200 as G
+    from glm53_flash_mlx_b200 import synthetic as S
+    from glm53_flash_mlx_b200.router import Float32Gate
+
+    L = layers[0]
+    n_exp = L["bank"].expert_count
+    cfg = S.moe_config(H, I, n_exp, TOP_K, LIMIT)
+    gate = Float32Gate(cfg, device=dev)
+    gate.weight.copy_(L["router_w"])
+    gate.e_score_correction_bias.copy_(L["router_b"])
+    mod = G.PackedFP8MoE(L["bank"], cfg, gate, L["shared_mod"])
+    out = {}
+    for B in (16,):
+        xs = [S.random_bf16((1, B, H), seed=500 + i, device=dev) for i in range(8)]
+        for i in range(3):
+            mod(xs[i % 8])
+        torch.cuda.synchronize()
+        st, sp = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n = 40
+        st.record()
+        for i in range(n):
+            mod(xs[i % 8])
+        sp.record()
+        torch.cuda.synchronize()
+        us = st.elapsed_time(sp) * 1e3 / n
+        idx, sc = mod.gate(xs[0])
+        mod._forward_routes(xs[0], idx, sc)
+        torch.cuda.synchronize()
+        st.record()
+        for i in range(3):
+            idx, sc = mod.gate(xs[i % 8])
+            mod._forward_routes(xs[i % 8], idx, sc)
+        sp.record()
+        torch.cuda.synchronize()
+        loop_us = st.elapsed_time(sp) * 1e3 / 3
+        touched = int(torch.unique(idx).numel())
+        out[f"B{B}"] = {"us": round(us, 1), "tokens_per_s": round(B / (us / 1e6), 1), "touched_experts": touched,
+                        "direct_loop_us": round(loop_us, 1)}
+    return out
 
 
 def bench_linear(dev, args):
@@ -794,6 +842,8 @@ def main():
         line["prefill_2048"] = res["prefill_2048"]
     if "linear_config1_5" in res:
         line["linear_config1_5"] = res["linear_config1_5"]
+    if "batched_decode" in res:
+        line["batched_decode"] = res["batched_decode"]
     if rank == 0 and world == 1 and not args.no_cpu:
         import torch
 
