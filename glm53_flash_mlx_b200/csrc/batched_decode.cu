@@ -1,0 +1,357 @@
+// Coalesced decode of a small batch: every touched expert streams its
+// weights once for all of the batch's routes to it.
+//
+// The expert side of the Direct module's multi-row path
+// (glm53_flash_mlx/fp8.py:384-399: per touched expert, gate/up, SwiGLU and
+// down over the rows routed to it), for up to a few dozen routes.  The routes
+// are sorted by expert (route_plan, descriptors of up to kBdCols routes); a
+// descriptor's routes ride in the N columns of the m16n8k16 GEMV tiles of
+// gemv_tile.cuh (the single-token decode uses column 0 only), so each weight
+// tile is loaded once per descriptor instead of once per route.  Every output
+// column of an MMA is its own dot product, so a route's values are those of
+// the per-route decode (glm53_routes_decode).
+//   batched_gate_up_kernel: work item = (descriptor, 32 hidden rows); four
+//     warps of 8 gate + 8 up rows over the whole K; BF16 SwiGLU per column;
+//     hidden rows in sorted route order.
+//   batched_down_kernel: work item = (descriptor, 64 output rows); four warps
+//     of 16 rows over the whole K = I; BF16 down rows in sorted route order.
+// Both are persistent over the device-side descriptor count (no host sync).
+#include <algorithm>
+
+#include "common.cuh"
+#include "gemv_tile.cuh"
+#include "kernels.cuh"
+
+namespace glm53 {
+
+constexpr int kBdWarps = 4;
+constexpr int kBdCols = 4;        // routes per descriptor (MMA N columns used)
+constexpr int kBdRing = 8;        // gate/up: K slices in flight per warp
+constexpr int kBdRingDown = 12;   // down: its K streams are short
+constexpr int kBdMaxRoutes = 4096;
+
+__host__ __device__ __forceinline__ int bd_align16(int v) { return (v + 15) & ~15; }
+
+struct BatchedArgs {
+  const uint16_t* x;  // [T, H] BF16 tokens
+  int H, I, E, top_k;
+  const uint32_t* order;  // sorted position -> route t * top_k + j
+  const uint32_t* tile_experts;
+  const uint32_t* tile_starts;
+  const uint32_t* tile_lengths;
+  const uint32_t* descriptor_count;
+  const uint8_t* gu_w;
+  const float* gu_s;
+  const uint8_t* d_w;
+  const float* d_s;
+  float limit;
+  uint16_t* hidden;  // [R, I] sorted route order
+  uint16_t* rows;    // [R, H] sorted route order
+  uint32_t* status;
+};
+
+// Stage `ncols` token rows (route order[c] reads token order[c] / top_k) into
+// shared memory as FP16 * 2^-e; returns 2^e (stage_f16's rule, gathered).
+__device__ __forceinline__ float stage_routes_f16(__half* xs, int stride, const uint16_t* x, const uint32_t* order,
+                                                  int top_k, int ncols, int K, float* red) {
+  const int n8 = K >> 3;
+  float m = 0.f;
+  for (int i = threadIdx.x; i < ncols * n8; i += blockDim.x) {
+    const int c = i / n8, j = i - c * n8;
+    const uint16_t* src = x + (size_t)(__ldg(order + c) / (uint32_t)top_k) * K + 8 * j;
+    const uint4 v = *reinterpret_cast<const uint4*>(src);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      m = fmaxf(m, fabsf(__uint_as_float(w[t] << 16)));
+      m = fmaxf(m, fabsf(__uint_as_float(w[t] & 0xFFFF0000u)));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float mx = red[0];
+  int e = 0;
+  if (mx >= 16384.0f) {
+    int ex;
+    frexpf(mx, &ex);
+    e = ex - 14;
+  }
+  const float down = ldexpf(1.0f, -e);
+  for (int i = threadIdx.x; i < ncols * n8; i += blockDim.x) {
+    const int c = i / n8, j = i - c * n8;
+    const uint16_t* src = x + (size_t)(__ldg(order + c) / (uint32_t)top_k) * K + 8 * j;
+    const uint4 v = *reinterpret_cast<const uint4*>(src);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      __half2 h = __floats2half2_rn(__uint_as_float(w[t] << 16) * down, __uint_as_float(w[t] & 0xFFFF0000u) * down);
+      o[t] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    *reinterpret_cast<uint4*>(xs + c * stride + 8 * j) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  __syncthreads();
+  return ldexpf(1.0f, e);
+}
+
+template <bool FINITE>
+__global__ void __launch_bounds__(32 * kBdWarps) batched_gate_up_kernel(BatchedArgs a) {
+  constexpr int P = kBdRing;
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+  uint4* ring = reinterpret_cast<uint4*>(smem) + (size_t)warp * P * 64;
+  __half* xs = reinterpret_cast<__half*>(reinterpret_cast<uint4*>(smem) + (size_t)kBdWarps * P * 64);
+  const int stride = bd_align16(a.H + 8);
+  float* red = reinterpret_cast<float*>(xs + (size_t)kBdCols * stride);
+  const int groups = a.I / (8 * kBdWarps);
+  const int nwork = (int)__ldg(a.descriptor_count) * groups;
+  const int cols = a.H >> 7, half = a.I >> 7;
+  const int nslice = a.H >> 6;
+  for (int w = blockIdx.x; w < nwork; w += gridDim.x) {
+    const int d = w / groups, grp = w - d * groups;
+    const uint32_t e = __ldg(a.tile_experts + d), start = __ldg(a.tile_starts + d);
+    const int len = (int)min(__ldg(a.tile_lengths + d), (uint32_t)kBdCols);
+    const bool valid = e < (uint32_t)a.E;
+    const uint32_t es = valid ? e : 0u;
+    const int r0 = grp * 8 * kBdWarps + warp * 8;
+    const uint8_t* gw = a.gu_w + ((size_t)es * 2 * a.I + r0) * a.H;
+    const uint8_t* uw = gw + (size_t)a.I * a.H;
+    const float* gs = a.gu_s + ((size_t)es * 2 * half + (r0 >> 7)) * cols;
+    const float* us = gs + (size_t)half * cols;
+    const uint8_t* pg = gw + (size_t)g * a.H + 16 * q;
+    const uint8_t* pu = uw + (size_t)g * a.H + 16 * q;
+    auto issue = [&](int sl) {
+      uint4* dst = ring + (sl % P) * 64 + lane;
+      cp_async_16(dst, valid ? (const void*)(pg + 64 * sl) : (const void*)a.x, valid);
+      cp_async_16(dst + 32, valid ? (const void*)(pu + 64 * sl) : (const void*)a.x, valid);
+    };
+#pragma unroll
+    for (int s = 0; s < P - 1; ++s) {
+      if (s < nslice) issue(s);
+      cp_async_commit_group();
+    }
+    WarpScales ssg, ssu;
+    ssg.load(gs, cols, valid);
+    ssu.load(us, cols, valid);
+    const float smul =
+        decode_unscale<FINITE>() * stage_routes_f16(xs, stride, a.x, a.order + start, a.top_k, len, a.H, red);
+    float part[4] = {0.f, 0.f, 0.f, 0.f}, tot[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int sl = 0; sl < nslice; ++sl) {
+      if (sl + P - 1 < nslice) issue(sl + P - 1);
+      cp_async_commit_group();
+      cp_async_wait_group<P - 1>();
+      const uint4* src = ring + (sl % P) * 64 + lane;
+      const uint4 fg = src[0], fu = src[32];
+      uint32_t xw[8];
+      load_x_frag(xw, xs + g * stride + 64 * sl + 16 * q, g < len);
+      mma_slice<FINITE>(part, fg, fu, xw);
+      if (sl & 1) promote2(tot, part, ssg.at(sl >> 1) * smul, ssu.at(sl >> 1) * smul);
+    }
+    cp_async_wait_group<0>();
+    // lane (g, q) holds gate / up of hidden row r0 + g for columns 2q and 2q + 1
+#pragma unroll
+    for (int cc = 0; cc < 2; ++cc) {
+      const int c = 2 * q + cc;
+      if (c < len) a.hidden[(size_t)(start + c) * a.I + r0 + g] = valid ? swiglu_bf16(tot[cc], tot[2 + cc], a.limit)
+                                                                         : (uint16_t)0;
+    }
+    if (!valid && threadIdx.x == 0) atomicOr(a.status, kStatusBadExpert);
+    __syncthreads();  // every warp is done with xs before the next item stages
+  }
+}
+
+template <bool FINITE>
+__global__ void __launch_bounds__(32 * kBdWarps) batched_down_kernel(BatchedArgs a) {
+  constexpr int P = kBdRingDown;
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+  const int K = a.I;
+  uint4* ring = reinterpret_cast<uint4*>(smem) + (size_t)warp * P * 64;
+  __half* hs = reinterpret_cast<__half*>(reinterpret_cast<uint4*>(smem) + (size_t)kBdWarps * P * 64);
+  const int stride = bd_align16(K + 8);
+  float* red = reinterpret_cast<float*>(hs + (size_t)kBdCols * stride);
+  const int groups = a.H / (16 * kBdWarps);
+  const int nwork = (int)__ldg(a.descriptor_count) * groups;
+  const int cols = K >> 7;
+  const int nslice = K >> 6;
+  for (int w = blockIdx.x; w < nwork; w += gridDim.x) {
+    const int d = w / groups, grp = w - d * groups;
+    const uint32_t e = __ldg(a.tile_experts + d), start = __ldg(a.tile_starts + d);
+    const int len = (int)min(__ldg(a.tile_lengths + d), (uint32_t)kBdCols);
+    const bool valid = e < (uint32_t)a.E;
+    const uint32_t es = valid ? e : 0u;
+    const int row0 = grp * 16 * kBdWarps + warp * 16;
+    const uint8_t* w0 = a.d_w + ((size_t)es * a.H + row0) * K;
+    const float* srow = a.d_s + ((size_t)es * (a.H >> 7) + (row0 >> 7)) * cols;
+    const uint8_t* p0 = w0 + (size_t)g * K + 16 * q;
+    const uint8_t* p8 = p0 + (size_t)8 * K;
+    auto issue = [&](int sl) {
+      uint4* dst = ring + (sl % P) * 64 + lane;
+      cp_async_16(dst, valid ? (const void*)(p0 + 64 * sl) : (const void*)a.x, valid);
+      cp_async_16(dst + 32, valid ? (const void*)(p8 + 64 * sl) : (const void*)a.x, valid);
+    };
+#pragma unroll
+    for (int s = 0; s < P - 1; ++s) {
+      if (s < nslice) issue(s);
+      cp_async_commit_group();
+    }
+    WarpScales sd;
+    sd.load(srow, cols, valid);
+    const float hmul = decode_unscale<FINITE>() *
+                       stage_f16(hs, stride, a.hidden + (size_t)start * K, K, len, K, red);
+    float part[4] = {0.f, 0.f, 0.f, 0.f}, tot[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int sl = 0; sl < nslice; ++sl) {
+      if (sl + P - 1 < nslice) issue(sl + P - 1);
+      cp_async_commit_group();
+      cp_async_wait_group<P - 1>();
+      const uint4* src = ring + (sl % P) * 64 + lane;
+      const uint4 f0 = src[0], f8 = src[32];
+      uint32_t xw[8];
+      load_x_frag(xw, hs + g * stride + 64 * sl + 16 * q, g < len);
+      mma_slice<FINITE>(part, f0, f8, xw);
+      if (sl & 1) promote(tot, part, sd.at(sl >> 1) * hmul);
+    }
+    cp_async_wait_group<0>();
+    // lane (g, q): rows row0 + g (tot[0..1]) and row0 + g + 8 (tot[2..3]), columns 2q, 2q + 1
+#pragma unroll
+    for (int cc = 0; cc < 2; ++cc) {
+      const int c = 2 * q + cc;
+      if (c < len) {
+        uint16_t* dst = a.rows + (size_t)(start + c) * a.H + row0;
+        dst[g] = valid ? f32_to_bf16_bits(tot[cc]) : (uint16_t)0;
+        dst[g + 8] = valid ? f32_to_bf16_bits(tot[2 + cc]) : (uint16_t)0;
+      }
+    }
+    if (!valid && threadIdx.x == 0) atomicOr(a.status, kStatusBadExpert);
+    __syncthreads();
+  }
+}
+
+// Workspace: route plan (order, inverse, sorted experts / scores, offsets,
+// descriptors, counts) | hidden [R, I] | rows [R, H].
+struct BatchedWorkspace {
+  size_t order, inverse, sorted_experts, sorted_scores, route_offsets, tile_offsets, tile_experts, tile_starts,
+      tile_lengths, counts, hidden, rows, bytes;
+};
+
+static BatchedWorkspace batched_workspace(int64_t R, int64_t E, int64_t H, int64_t I) {
+  BatchedWorkspace w;
+  const int64_t cap = (R + kBdCols - 1) / kBdCols + E;
+  size_t off = 0;
+  auto take = [&](size_t n) {
+    const size_t o = off;
+    off = align_up(off + n, 256);
+    return o;
+  };
+  w.order = take(R * 4);
+  w.inverse = take(R * 4);
+  w.sorted_experts = take(R * 4);
+  w.sorted_scores = take(R * 4);
+  w.route_offsets = take((E + 1) * 4);
+  w.tile_offsets = take((E + 1) * 4);
+  w.tile_experts = take(cap * 4);
+  w.tile_starts = take(cap * 4);
+  w.tile_lengths = take(cap * 4);
+  w.counts = take(2 * 4);
+  w.hidden = take((size_t)R * I * 2);
+  w.rows = take((size_t)R * H * 2);
+  w.bytes = off;
+  return w;
+}
+
+template <bool FINITE>
+static int launch_batched(const BatchedArgs& a, int64_t capacity, cudaStream_t st) {
+  const size_t smem_gu = (size_t)kBdWarps * kBdRing * 64 * 16 + (size_t)kBdCols * bd_align16(a.H + 8) * 2 +
+                         32 * sizeof(float);
+  const size_t smem_dn = (size_t)kBdWarps * kBdRingDown * 64 * 16 + (size_t)kBdCols * bd_align16(a.I + 8) * 2 +
+                         32 * sizeof(float);
+  int rc = ensure_max_smem((const void*)batched_gate_up_kernel<FINITE>, smem_gu);
+  if (rc) return rc;
+  rc = ensure_max_smem((const void*)batched_down_kernel<FINITE>, smem_dn);
+  if (rc) return rc;
+  const int resident = 4 * sm_count();
+  const int64_t gu_items = capacity * (a.I / (8 * kBdWarps)), dn_items = capacity * (a.H / (16 * kBdWarps));
+  batched_gate_up_kernel<FINITE><<<(unsigned)std::min<int64_t>(gu_items, resident), 32 * kBdWarps, smem_gu, st>>>(a);
+  rc = check_launch("batched_gate_up_kernel");
+  if (rc) return rc;
+  batched_down_kernel<FINITE><<<(unsigned)std::min<int64_t>(dn_items, resident), 32 * kBdWarps, smem_dn, st>>>(a);
+  return check_launch("batched_down_kernel");
+}
+
+// Combine through the sorted-order rows (direct_combine.cu).
+int direct_combine_rows(const uint16_t* rows, const uint32_t* row_of_slot, const uint32_t* expert_ids,
+                        const float* scores, int64_t T, int top_k, int64_t H, int64_t E, const uint16_t* shared,
+                        uint16_t* out, uint32_t* status, cudaStream_t st);
+
+}  // namespace glm53
+
+using namespace glm53;
+
+extern "C" size_t glm53_batched_decode_workspace_bytes(int64_t T, int top_k, int64_t E, int64_t H, int64_t I) {
+  return batched_workspace(T * top_k, E, H, I).bytes;
+}
+
+extern "C" int glm53_batched_decode_moe(const void* x, int64_t T, int64_t H, const uint32_t* expert_ids,
+                                        const float* scores, int top_k, const uint8_t* gate_up_w,
+                                        const float* gate_up_s, const uint8_t* down_w, const float* down_s,
+                                        int64_t E, int64_t I, float limit, const void* shared, void* out,
+                                        void* workspace, size_t workspace_bytes, uint32_t* status, uint32_t flags,
+                                        void* stream) {
+  const int64_t R = T * top_k;
+  if (T < 0 || top_k <= 0 || top_k > 32 || H <= 0 || I <= 0 || E <= 0 || H % 128 != 0 || I % 128 != 0 ||
+      H > 32768 || I > 32768 || R > kBdMaxRoutes) {
+    set_last_error("glm53_batched_decode_moe: unsupported geometry T=%lld top_k=%d H=%lld I=%lld", (long long)T,
+                   top_k, (long long)H, (long long)I);
+    return GLM53_ERR_INVALID;
+  }
+  if (T == 0) return GLM53_OK;
+  const BatchedWorkspace wl = batched_workspace(R, E, H, I);
+  if (!x || !expert_ids || !scores || !gate_up_w || !gate_up_s || !down_w || !down_s || !out || !workspace ||
+      !status || workspace_bytes < wl.bytes ||
+      (((uintptr_t)x | (uintptr_t)gate_up_w | (uintptr_t)down_w | (uintptr_t)out | (uintptr_t)shared) & 15) != 0) {
+    set_last_error("glm53_batched_decode_moe: missing pointer, misaligned tensor or workspace too small");
+    return GLM53_ERR_INVALID;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  char* ws = (char*)workspace;
+  BatchedArgs a{};
+  a.x = (const uint16_t*)x;
+  a.H = (int)H;
+  a.I = (int)I;
+  a.E = (int)E;
+  a.top_k = top_k;
+  a.order = (const uint32_t*)(ws + wl.order);
+  a.tile_experts = (const uint32_t*)(ws + wl.tile_experts);
+  a.tile_starts = (const uint32_t*)(ws + wl.tile_starts);
+  a.tile_lengths = (const uint32_t*)(ws + wl.tile_lengths);
+  a.descriptor_count = (const uint32_t*)(ws + wl.counts);
+  a.gu_w = gate_up_w;
+  a.gu_s = gate_up_s;
+  a.d_w = down_w;
+  a.d_s = down_s;
+  a.limit = limit;
+  a.hidden = (uint16_t*)(ws + wl.hidden);
+  a.rows = (uint16_t*)(ws + wl.rows);
+  a.status = status;
+  int rc = route_plan(expert_ids, R, E, kBdCols, scores, (uint32_t*)(ws + wl.order), (uint32_t*)(ws + wl.inverse),
+                      (uint32_t*)(ws + wl.sorted_experts), (float*)(ws + wl.sorted_scores),
+                      (uint32_t*)(ws + wl.route_offsets), (uint32_t*)(ws + wl.tile_experts),
+                      (uint32_t*)(ws + wl.tile_starts), (uint32_t*)(ws + wl.tile_lengths),
+                      (uint32_t*)(ws + wl.tile_offsets), (uint32_t*)(ws + wl.counts),
+                      (uint32_t*)(ws + wl.counts) + 1, st);
+  if (rc) return rc;
+  const int64_t capacity = (R + kBdCols - 1) / kBdCols + E;
+  rc = (flags & GLM53_FLAG_E4M3_FINITE) ? launch_batched<true>(a, capacity, st) : launch_batched<false>(a, capacity, st);
+  if (rc) return rc;
+  return direct_combine_rows(a.rows, (const uint32_t*)(ws + wl.inverse), expert_ids, scores, T, top_k, H, E,
+                             (const uint16_t*)shared, (uint16_t*)out, status, st);
+}

@@ -16,9 +16,13 @@ namespace glm53 {
 
 constexpr int kCombineMaxK = 32;
 
+// row_of_slot (optional) maps route slot -> row of `rows` (sorted order);
+// slots whose expert id is >= E are skipped and flagged in *status.
 __global__ void __launch_bounds__(256) direct_combine_kernel(const uint16_t* __restrict__ rows,
+                                                             const uint32_t* __restrict__ row_of_slot,
                                                              const uint32_t* __restrict__ ids,
                                                              const float* __restrict__ scores, int top_k, int H,
+                                                             uint32_t E, uint32_t* status,
                                                              const uint16_t* __restrict__ shared,
                                                              uint16_t* __restrict__ out) {
   __shared__ int order[kCombineMaxK];
@@ -43,8 +47,13 @@ __global__ void __launch_bounds__(256) direct_combine_kernel(const uint16_t* __r
     for (int i = 0; i < 8; ++i) acc[i] = 0.f;
     for (int j = 0; j < top_k; ++j) {
       const int slot = t * top_k + order[j];
+      if (ids[slot] >= E) {
+        if (status && c == 8 * threadIdx.x && blockIdx.y == 0) atomicOr(status, kStatusBadExpert);
+        continue;
+      }
       const float sc = scores[slot];
-      const uint4 v = *reinterpret_cast<const uint4*>(rows + (size_t)slot * H + c);
+      const size_t row = row_of_slot ? (size_t)row_of_slot[slot] : (size_t)slot;
+      const uint4 v = *reinterpret_cast<const uint4*>(rows + row * H + c);
       const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -71,6 +80,19 @@ __global__ void __launch_bounds__(256) direct_combine_kernel(const uint16_t* __r
   }
 }
 
+static dim3 combine_grid(int64_t T, int64_t H) {
+  const int per = (int)((H / 8 + 255) / 256);
+  return dim3((unsigned)T, (unsigned)std::min(per, 8));
+}
+
+int direct_combine_rows(const uint16_t* rows, const uint32_t* row_of_slot, const uint32_t* expert_ids,
+                        const float* scores, int64_t T, int top_k, int64_t H, int64_t E, const uint16_t* shared,
+                        uint16_t* out, uint32_t* status, cudaStream_t st) {
+  direct_combine_kernel<<<combine_grid(T, H), 256, 0, st>>>(rows, row_of_slot, expert_ids, scores, top_k, (int)H,
+                                                            (uint32_t)E, status, shared, out);
+  return check_launch("direct_combine_kernel");
+}
+
 }  // namespace glm53
 
 using namespace glm53;
@@ -85,9 +107,6 @@ extern "C" int glm53_direct_combine(const void* rows, const uint32_t* expert_ids
     return GLM53_ERR_INVALID;
   }
   if (T == 0) return GLM53_OK;
-  const int per = (int)((H / 8 + 255) / 256);
-  dim3 grid((unsigned)T, (unsigned)std::min(per, 8));
-  direct_combine_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
-      (const uint16_t*)rows, expert_ids, scores, top_k, (int)H, (const uint16_t*)shared, (uint16_t*)out);
-  return check_launch("direct_combine_kernel");
+  return direct_combine_rows((const uint16_t*)rows, nullptr, expert_ids, scores, T, top_k, H, 0xFFFFFFFFll,
+                             (const uint16_t*)shared, (uint16_t*)out, nullptr, (cudaStream_t)stream);
 }

@@ -18,7 +18,7 @@
 
 namespace glm53 {
 
-constexpr int kRouterSmallT = 8;   // tokens handled by the fused GEMV+top-k launch
+constexpr int kRouterSmallT = 32;  // tokens handled by the fused GEMV+top-k launch (decode batches)
 constexpr int kRouterMaxE = 1024;  // 32 lanes x 32 values per lane
 constexpr int kRouterMaxK = 32;
 
@@ -219,9 +219,9 @@ __global__ void __launch_bounds__(256) router_small_kernel(
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  if (warp < T) {
-    warp_topk_keys<PER>(key_buf + (size_t)warp * p.E, sig_buf + (size_t)warp * p.E, p,
-                        idx + (size_t)warp * p.top_k, scores + (size_t)warp * p.top_k, choice_smem[warp]);
+  for (int t = warp; t < T; t += 8) {  // one warp per token
+    warp_topk_keys<PER>(key_buf + (size_t)t * p.E, sig_buf + (size_t)t * p.E, p, idx + (size_t)t * p.top_k,
+                        scores + (size_t)t * p.top_k, choice_smem[warp]);
   }
   if (threadIdx.x == 0) *counter = 0u;  // leave the workspace reusable
 }
@@ -412,6 +412,9 @@ static int launch_small(const uint16_t* x, int T, int H, const float* w, const f
   int blocks = p.E;
   if (T <= 1)
     router_small_kernel<1, PER><<<blocks, 256, 0, st>>>(x, T, H, w, bias, p, r.logits, r.sig, r.key, r.counter,
+                                                        idx, scores);
+  else if (T <= 8)
+    router_small_kernel<8, PER><<<blocks, 256, 0, st>>>(x, T, H, w, bias, p, r.logits, r.sig, r.key, r.counter,
                                                         idx, scores);
   else
     router_small_kernel<kRouterSmallT, PER><<<blocks, 256, 0, st>>>(x, T, H, w, bias, p, r.logits, r.sig, r.key,

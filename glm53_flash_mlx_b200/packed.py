@@ -255,42 +255,33 @@ def batched_decode_moe(x: torch.Tensor, indices: torch.Tensor, scores: torch.Ten
                        shared_experts, *, limit: float, workspace: N.Workspace | None = None,
                        status: torch.Tensor | None = None) -> torch.Tensor:
     """A few decode rows through the packed bank with the Direct module's
-    semantics (glm53_flash_mlx/fp8.py:384-399), bit for bit: per-route expert
-    outputs (``glm53_routes_decode``), their BF16 scatter-add in ascending
-    expert id (``glm53_direct_combine``), plus the shared expert module's
-    output.  x: BF16 [T, H]; indices / scores: [T, top_k]."""
+    semantics (glm53_flash_mlx/fp8.py:384-399): each touched expert streams its
+    weights once for all its routes, the weighted rows are added in BF16 in
+    ascending expert id (``glm53_batched_decode_moe``), plus the shared expert
+    module's output.  x: BF16 [T, H]; indices / scores: [T, top_k]."""
     dev = N.require_cuda(x, indices, scores, bank.gate_up_weight)
     T, H = x.shape
     if H != bank.hidden_size:
         raise ValueError(f"decode input width {H} != bank hidden {bank.hidden_size}")
     top_k = indices.shape[-1]
-    I = bank.intermediate_size
-    R = T * top_k
+    E, I = bank.expert_count, bank.intermediate_size
     x = x.contiguous()
     ids = indices.reshape(-1).to(torch.int32).contiguous()
     sc = scores.reshape(-1).to(torch.float32).contiguous()
-    x_rows = x.repeat_interleave(top_k, dim=0)  # route t * top_k + j reads token t
     wsp = workspace or N.Workspace()
-    ws = wsp.get(dev, "routes", N.lib().glm53_routes_decode_workspace_bytes(R, H, I))
+    ws = wsp.get(dev, "batched", N.lib().glm53_batched_decode_workspace_bytes(T, top_k, E, H, I))
     if status is None:
         status = wsp.get(dev, "status", 4)
-    rows = torch.empty((R, H), dtype=torch.bfloat16, device=dev)
-    flags = N.decode_flags(bank.gate_up_weight, bank.down_weight)
-    N.check(
-        N.lib().glm53_routes_decode(
-            x_rows.data_ptr(), R, H, ids.data_ptr(), bank.gate_up_weight.data_ptr(),
-            bank.gate_up_scale_inv.data_ptr(), bank.down_weight.data_ptr(), bank.down_scale_inv.data_ptr(),
-            bank.expert_count, I, float(limit), rows.data_ptr(), ws.data_ptr(), ws.numel(), status.data_ptr(),
-            flags, N.stream(dev),
-        ),
-        "glm53_routes_decode",
-    )
     shared = shared_experts(x).contiguous() if shared_experts is not None else None
     out = torch.empty_like(x)
     N.check(
-        N.lib().glm53_direct_combine(rows.data_ptr(), ids.data_ptr(), sc.data_ptr(), T, top_k, H, N.ptr(shared),
-                                     out.data_ptr(), N.stream(dev)),
-        "glm53_direct_combine",
+        N.lib().glm53_batched_decode_moe(
+            x.data_ptr(), T, H, ids.data_ptr(), sc.data_ptr(), top_k, bank.gate_up_weight.data_ptr(),
+            bank.gate_up_scale_inv.data_ptr(), bank.down_weight.data_ptr(), bank.down_scale_inv.data_ptr(), E, I,
+            float(limit), N.ptr(shared), out.data_ptr(), ws.data_ptr(), ws.numel(), status.data_ptr(),
+            N.decode_flags(bank.gate_up_weight, bank.down_weight), N.stream(dev),
+        ),
+        "glm53_batched_decode_moe",
     )
     if _SYNC_STATUS:
         check_status(status)

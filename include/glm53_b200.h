@@ -215,6 +215,26 @@ int glm53_routes_decode(const void* x_rows, int64_t R, int64_t H, const uint32_t
 int glm53_direct_combine(const void* rows, const uint32_t* expert_ids, const float* scores, int64_t T,
                          int top_k, int64_t H, const void* shared, void* out, void* stream);
 
+/* Workspace bytes of glm53_batched_decode_moe. */
+size_t glm53_batched_decode_workspace_bytes(int64_t T, int top_k, int64_t E, int64_t H, int64_t I);
+
+/* A small decode batch (T tokens, T * top_k <= 4096 routes) through the packed
+ * bank with the Direct module's multi-row semantics: the routes are sorted by
+ * expert on the device (glm53_route_plan, descriptors of up to 4 routes), each
+ * descriptor streams its expert's weights once for all its routes (per-route
+ * values identical to glm53_routes_decode), and glm53_direct_combine's BF16
+ * scatter-add in ascending expert id adds them per token, then `shared`
+ * (BF16 [T, H], the shared expert's output, or NULL).  Route ids >= E are
+ * skipped and raise GLM53_STATUS_BAD_EXPERT.  H, I multiples of 128.
+ * Replaces DirectFP8MoE.__call__'s expert loop for more than one row,
+ * glm53_flash_mlx/fp8.py:384-399. */
+int glm53_batched_decode_moe(const void* x, int64_t T, int64_t H, const uint32_t* expert_ids,
+                             const float* scores, int top_k, const uint8_t* gate_up_w,
+                             const float* gate_up_s, const uint8_t* down_w, const float* down_s,
+                             int64_t E, int64_t I, float limit, const void* shared, void* out,
+                             void* workspace, size_t workspace_bytes, uint32_t* status,
+                             uint32_t flags, void* stream);
+
 /* Expert-parallel dispatch packing on the tokens' home rank.  Experts are
  * split into `world` contiguous ranges of E / world; route (t, j) with expert
  * e goes to rank d = e / (E / world), into the next free of `capacity` slots

@@ -125,7 +125,7 @@ def _logit_rel_err(gpu, ref64):
     return float((np.abs(gpu - ref64) / np.maximum(np.abs(ref64), floor)).max())
 
 
-@pytest.mark.parametrize("T", [1, 5, 8, 64, 300])
+@pytest.mark.parametrize("T", [1, 5, 8, 16, 32, 64, 300])
 def test_router_matches_oracle(G, S, oracle, T):
     E, H = 288, 4096
     w, b = S.make_router(E, H, seed=1, device="cuda", zipf_alpha=0.5 if T > 8 else 0.0)
@@ -539,3 +539,44 @@ def test_batched_decode_matches_oracle_and_direct_loop(G, S, oracle, T, E, H, I)
         assert stats["max_abs"] <= max(loop_stats["max_abs"], 2 ** -5), (stats, loop_stats)
         same = float((bits(got) == bits(loop)).mean())
         assert same >= 0.99, same
+
+
+@pytest.mark.parametrize("T,E,H,I", [(3, 8, 1024, 256), (16, 64, 2048, 768)])
+def test_coalesced_batched_decode_equals_per_route_decode_bitwise(G, S, T, E, H, I):
+    """glm53_batched_decode_moe (each expert's weights streamed once for all of
+    its routes, the routes in the MMA's N columns) gives the bits of the
+    per-route decode (glm53_routes_decode) followed by glm53_direct_combine."""
+    from glm53_flash_mlx_b200 import _native as N
+    from glm53_flash_mlx_b200.ep import routes_decode
+    from glm53_flash_mlx_b200.packed import batched_decode_moe
+
+    bank = S.make_bank(E, H, I, seed=T + 21, device="cuda")
+    gen = torch.Generator().manual_seed(T)
+    # few experts, so several routes share one (and descriptors hold 1..4 routes)
+    ids = torch.stack([torch.randperm(E, generator=gen)[:8] for _ in range(T)]).to(torch.int32).cuda()
+    sc = (torch.rand((T, 8), generator=gen) * 0.25 + 0.05).cuda()
+    x = S.random_bf16((T, H), seed=T + 22, device="cuda", std=1.5)
+    got = batched_decode_moe(x, ids, sc, bank, None, limit=10.0)
+    tensors = (bank.gate_up_weight, bank.gate_up_scale_inv, bank.down_weight, bank.down_scale_inv)
+    rows = routes_decode(x.repeat_interleave(8, dim=0), ids.reshape(-1), tensors, limit=10.0)
+    want = torch.empty_like(x)
+    N.check(N.lib().glm53_direct_combine(rows.data_ptr(), ids.data_ptr(), sc.data_ptr(), T, 8, H, None,
+                                         want.data_ptr(), N.stream()), "combine")
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+
+
+def test_batched_decode_flags_bad_expert_without_trapping(G, S):
+    from glm53_flash_mlx_b200 import _native as N
+    from glm53_flash_mlx_b200.packed import batched_decode_moe
+
+    E, H, I = 8, 256, 128
+    bank = S.make_bank(E, H, I, seed=5, device="cuda")
+    ids = torch.tensor([[0, 1, 2, 3, 4, 5, 6, 7], [7, 6, 5, 4, 3, 2, 1, 99]], dtype=torch.int32, device="cuda")
+    sc = torch.full((2, 8), 0.1, device="cuda")
+    x = S.random_bf16((2, H), seed=6, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = batched_decode_moe(x, ids, sc, bank, None, limit=10.0, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) & N.STATUS_BAD_EXPERT
+    assert torch.isfinite(out.float()).all()
