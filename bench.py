@@ -57,6 +57,7 @@ def parse_args():
     p.add_argument("--no-e2e", action="store_true", help="skip the module-API end-to-end pass")
     p.add_argument("--quick-linear", action="store_true", help="config-5 sweep at M in {1, 64, 512} only")
     p.add_argument("--linear-only", action="store_true", help="run only the config-1/5 block-linear sweep")
+    p.add_argument("--batched-only", action="store_true", help="run only the batched (B=16) decode measurement")
     p.add_argument("--prefill-only", action="store_true",
                    help="profiling aid: only the T=2048 grouped prefill measurement (prints its JSON and exits)")
     p.add_argument("--prefill-reps", type=int, default=8, help="timed grouped prefill layers")
@@ -803,6 +804,14 @@ def main():
 
         if rank == 0:
             print(json.dumps({"linear_config1_5": bench_linear(torch.device("cuda", local), args)}), flush=True)
+        return
+    if args.batched_only:
+        import torch
+
+        dev = torch.device("cuda", local)
+        layers = build_layers(1, 1000 + 101 * rank, dev, args.experts)
+        if rank == 0:
+            print(json.dumps({"batched_decode": bench_batched(layers, dev, args)}), flush=True)
         return
     if args.prefill_only:
         import torch
