@@ -13,9 +13,11 @@
 //   glm53_ep_owner_decode_p2p  gate/up waits until all world * capacity
 //                          arrivals of this step are in, then the per-route
 //                          decode; down stores each BF16 row into the home
-//                          rank's back buffer and counts one arrival per CTA;
-//   glm53_ep_combine_p2p   waits for all rows, reduces in slot order, adds
-//                          the shared rows, and advances the step counter.
+//                          rank's back buffer and counts one arrival per CTA
+//                          of a routed row (empty slots count nothing);
+//   glm53_ep_combine_p2p   waits until the rows of every route it sent are
+//                          in, reduces in slot order, adds the shared rows,
+//                          and advances the step counter.
 // Buffers are single: a rank only writes step n + 1 into a peer after its own
 // combine of step n, which waited for that peer's down stage of step n, which
 // ran after the peer's gate/up finished reading its slots.  Every wait is
@@ -102,15 +104,21 @@ __global__ void p2p_dispatch_kernel(const uint16_t* __restrict__ x, int H, int t
   if (threadIdx.x == 0) atomicAdd(reinterpret_cast<unsigned long long*>(base + lay.cnt_dispatch), 1ull);
 }
 
-// Combine after waiting for every owner's rows of this step.
+// Combine after waiting for every owner's rows of this step: each routed
+// slot this rank sent comes back as cta_per_row arrivals (the owners' down
+// CTAs of that row), so this step expects cta_per_row x (sent routes) more
+// than the running total kept in the buffer.
 __global__ void p2p_combine_kernel(const char* __restrict__ buf, EpLayout lay, const float* __restrict__ slot_scores,
                                    const uint32_t* __restrict__ route_pos, int64_t T, int top_k, int64_t H,
                                    const uint16_t* __restrict__ shared, uint16_t* __restrict__ out,
-                                   unsigned long long per_step, uint32_t* status) {
+                                   unsigned long long cta_per_row, uint32_t* status) {
+  __shared__ unsigned long long s_step;
   if (threadIdx.x == 0) {
-    const unsigned long long epoch = *reinterpret_cast<const unsigned long long*>(buf + lay.epoch);
-    wait_counter_geq(reinterpret_cast<const unsigned long long*>(buf + lay.cnt_back), (epoch + 1ull) * per_step,
-                     status);
+    unsigned long long sent = 0;
+    for (int64_t r = 0; r < T * top_k; ++r) sent += route_pos[r] != kP2pEmpty ? 1ull : 0ull;
+    s_step = sent * cta_per_row;
+    const unsigned long long before = *reinterpret_cast<const unsigned long long*>(buf + lay.expected);
+    wait_counter_geq(reinterpret_cast<const unsigned long long*>(buf + lay.cnt_back), before + s_step, status);
   }
   __syncthreads();
   const uint16_t* rows = reinterpret_cast<const uint16_t*>(buf + lay.back);
@@ -155,6 +163,7 @@ __global__ void p2p_combine_kernel(const char* __restrict__ buf, EpLayout lay, c
     char* b = const_cast<char*>(buf);
     unsigned int* done = reinterpret_cast<unsigned int*>(b + lay.done);
     if (atomicAdd(done, 1u) == gridDim.x - 1) {
+      *reinterpret_cast<unsigned long long*>(b + lay.expected) += s_step;
       *reinterpret_cast<unsigned long long*>(b + lay.epoch) += 1ull;
       *done = 0u;
       __threadfence();
@@ -262,11 +271,11 @@ extern "C" int glm53_ep_combine_p2p(void* buffer, const uint32_t* route_pos, con
   }
   cudaStream_t st = (cudaStream_t)stream;
   const EpLayout lay = ep_layout(world, (int)capacity, H);
-  // every owner's down stage counts one arrival per CTA: H / 64 CTAs per slot
-  const unsigned long long per_step = (unsigned long long)world * capacity * (H / 64);
+  // an owner's down stage counts one arrival per CTA of a routed row: H / 64
+  const unsigned long long cta_per_row = (unsigned long long)(H / 64);
   const int64_t n = std::max<int64_t>(T * (H / 8), 1);
   const int blocks = (int)std::min<int64_t>((n + 255) / 256, 1024);
   p2p_combine_kernel<<<blocks, 256, 0, st>>>((const char*)buffer, lay, slot_scores, route_pos, T, top_k, H,
-                                             (const uint16_t*)shared, (uint16_t*)out, per_step, status);
+                                             (const uint16_t*)shared, (uint16_t*)out, cta_per_row, status);
   return check_launch("p2p_combine_kernel");
 }

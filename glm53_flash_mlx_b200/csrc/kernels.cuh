@@ -97,7 +97,7 @@ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 // written by rank src; slot (owner, s) of back by rank owner; the counters
 // only grow (one per arriving CTA), the epoch counts this rank's steps.
 struct EpLayout {
-  size_t recv_x, recv_e, back, cnt_dispatch, cnt_back, epoch, done, bytes;
+  size_t recv_x, recv_e, back, cnt_dispatch, cnt_back, epoch, done, expected, bytes;
 };
 
 inline EpLayout ep_layout(int world, int cap, int64_t H) {
@@ -110,7 +110,8 @@ inline EpLayout ep_layout(int world, int cap, int64_t H) {
   l.cnt_back = l.cnt_dispatch + 256;
   l.epoch = l.cnt_back + 256;
   l.done = l.epoch + 256;
-  l.bytes = l.done + 256;
+  l.expected = l.done + 256;  // back-buffer arrivals expected up to the last finished step
+  l.bytes = l.expected + 256;
   return l;
 }
 

@@ -225,8 +225,8 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_gate_up_v4(DecodeA
 // acquire of the arrival counter (which gate/up already saw complete), the
 // weights start streaming, and only then does the CTA wait for the gate/up
 // grid; the BF16 rows go straight into the home rank's back buffer and one
-// arrival per CTA is counted there (empty slots count too).  Shared-expert
-// slots (jb >= top_k) write their rows locally and count nothing.
+// arrival per CTA is counted there.  Empty slots and shared-expert slots
+// (jb >= top_k, rows written locally) count nothing.
 template <bool FINITE>
 __device__ __forceinline__ void decode_down_peer(const DecodeArgs& a, int jb) {
   constexpr int P = kRingDown;
@@ -294,7 +294,7 @@ __device__ __forceinline__ void decode_down_peer(const DecodeArgs& a, int jb) {
     }
     if (!valid && lane == 0) atomicOr(a.status, kStatusBadExpert);
   }
-  if (routed) {
+  if (routed && e != kEmptySlot) {  // empty slots send nothing home and count nothing
     __threadfence_system();
     __syncthreads();
     if (threadIdx.x == 0) atomicAdd(reinterpret_cast<unsigned long long*>(hb + a.back_cnt_off), 1ull);
