@@ -87,6 +87,9 @@ struct DecodeArgs {
   // partials the last-arriver reduce waits for (0 = every slot)
   int gu_begin, gu_end, dn_begin, dn_end, dn_expect;
   bool dn_no_reduce;
+  // peer-memory owners: the shared-expert slots (which wait for no arrival)
+  // take the first CTAs of both grids instead of the last
+  bool shared_first;
 };
 
 constexpr uint32_t kEmptySlot = 0xFFFFFFFFu;
@@ -164,11 +167,16 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_gate_up_v4(DecodeA
   float* scratch = reinterpret_cast<float*>(xs + align16i(a.H + 8));
   const int routed_units = a.top_k * (a.I >> 3);
   const int nunits = a.gu_end ? a.gu_end : routed_units + shared_slots(a) * (a.Is >> 3);
-  const int unit = a.gu_begin + blockIdx.x * kWarpsPerBlock + warp;
-  const bool active = unit < nunits;
+  int unit = a.gu_begin + blockIdx.x * kWarpsPerBlock + warp;
   // every unit of a block belongs to one slot (I/8 and I_shared/8 are
   // multiples of 4 here)
-  const int unit0 = a.gu_begin + blockIdx.x * kWarpsPerBlock;
+  int unit0 = a.gu_begin + blockIdx.x * kWarpsPerBlock;
+  if (a.shared_first) {  // physical order: shared units, then routed units
+    const int S = nunits - routed_units;
+    unit = unit < S ? routed_units + unit : unit - S;
+    unit0 = unit0 < S ? routed_units + unit0 : unit0 - S;
+  }
+  const bool active = unit < nunits;
   const int jb = unit0 < routed_units ? unit0 / (a.I >> 3) : a.top_k + (unit0 - routed_units) / (a.Is >> 3);
   if (a.arrivals && jb < a.top_k) {  // peer-memory dispatch: wait for every rank's slots
     if (threadIdx.x == 0) wait_counter_geq(a.arrivals, (*a.epoch + 1ull) * a.arrivals_per_step, a.status);
@@ -228,7 +236,7 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_gate_up_v4(DecodeA
 // arrival per CTA is counted there.  Empty slots and shared-expert slots
 // (jb >= top_k, rows written locally) count nothing.
 template <bool FINITE>
-__device__ __forceinline__ void decode_down_peer(const DecodeArgs& a, int jb) {
+__device__ __forceinline__ void decode_down_peer(const DecodeArgs& a, int jb, int unit0) {
   constexpr int P = kRingDown;
   extern __shared__ __align__(16) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
@@ -237,7 +245,7 @@ __device__ __forceinline__ void decode_down_peer(const DecodeArgs& a, int jb) {
   __half* xs = reinterpret_cast<__half*>(reinterpret_cast<uint4*>(smem) + (size_t)kWarpsPerBlock * P * 64);
   float* scratch = reinterpret_cast<float*>(xs + align16i(K + 8));
   const int rtiles = a.H >> 4;
-  const int tile = blockIdx.x * kWarpsPerBlock + warp - jb * rtiles;
+  const int tile = unit0 + warp - jb * rtiles;
   const int row0 = tile << 4;
   const int cols = K >> 7;
   const bool routed = jb < a.top_k;
@@ -322,7 +330,12 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_down_v4(DecodeArgs
   // every unit of a block belongs to one slot (H/16 is a multiple of 4 here)
   const int jb = min((int)(a.dn_begin + blockIdx.x * kWarpsPerBlock) / rtiles, ns - 1);
   if (a.peer_base) {
-    decode_down_peer<FINITE>(a, jb);
+    int u0 = a.dn_begin + blockIdx.x * kWarpsPerBlock;
+    if (a.shared_first) {  // physical order: shared slots' tiles, then routed
+      const int S = (ns - a.top_k) * rtiles;
+      u0 = u0 < S ? a.top_k * rtiles + u0 : u0 - S;
+    }
+    decode_down_peer<FINITE>(a, u0 / rtiles, u0);
     return;
   }
   if (a.route_out && jb < a.top_k && a.ids[jb] == kEmptySlot) return;
@@ -875,6 +888,7 @@ extern "C" int glm53_ep_owner_decode_p2p(void* buffer, int64_t H, int world, int
   a.rank = rank;
   a.cap = (int)capacity;
   if (has_shared) {  // the home tokens' shared expert rides in the same launches
+    a.shared_first = true;
     a.Is = (int)I_shared;
     a.n_shared = (int)T_shared;
     a.shared_x = (const uint16_t*)shared_x;
