@@ -88,9 +88,18 @@ struct DecodeArgs {
   int gu_begin, gu_end, dn_begin, dn_end, dn_expect;
   bool dn_no_reduce;
   // peer-memory owners: the shared-expert slots (which wait for no arrival)
-  // take the first CTAs of both grids instead of the last
+  // take the first CTAs of both grids instead of the last, and the routed
+  // slots run in slot-position-major order, (src 0, s 0), (src 1, s 0), ...:
+  // routes fill each source's slots from s = 0, so the occupied slots come
+  // first and the empty ones (which only wait and exit) last
   bool shared_first;
 };
+
+// Physical routed slot p of a peer-memory owner grid -> slot (src, s) = src * cap + s.
+__host__ __device__ __forceinline__ int owner_slot(const DecodeArgs& a, int p) {
+  const int world = a.top_k / a.cap;
+  return (p % world) * a.cap + p / world;
+}
 
 constexpr uint32_t kEmptySlot = 0xFFFFFFFFu;
 
@@ -171,10 +180,16 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_gate_up_v4(DecodeA
   // every unit of a block belongs to one slot (I/8 and I_shared/8 are
   // multiples of 4 here)
   int unit0 = a.gu_begin + blockIdx.x * kWarpsPerBlock;
-  if (a.shared_first) {  // physical order: shared units, then routed units
-    const int S = nunits - routed_units;
-    unit = unit < S ? routed_units + unit : unit - S;
-    unit0 = unit0 < S ? routed_units + unit0 : unit0 - S;
+  if (a.shared_first) {  // physical order: shared units, then routed units by slot position
+    const int S = nunits - routed_units, per = a.I >> 3;
+    auto logical = [&](int u) {
+      if (u < S) return routed_units + u;
+      u -= S;
+      const int p = u / per;
+      return owner_slot(a, p) * per + (u - p * per);
+    };
+    unit = logical(unit);
+    unit0 = logical(unit0);
   }
   const bool active = unit < nunits;
   const int jb = unit0 < routed_units ? unit0 / (a.I >> 3) : a.top_k + (unit0 - routed_units) / (a.Is >> 3);
@@ -331,9 +346,15 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_down_v4(DecodeArgs
   const int jb = min((int)(a.dn_begin + blockIdx.x * kWarpsPerBlock) / rtiles, ns - 1);
   if (a.peer_base) {
     int u0 = a.dn_begin + blockIdx.x * kWarpsPerBlock;
-    if (a.shared_first) {  // physical order: shared slots' tiles, then routed
+    if (a.shared_first) {  // physical order: shared slots' tiles, then routed by slot position
       const int S = (ns - a.top_k) * rtiles;
-      u0 = u0 < S ? a.top_k * rtiles + u0 : u0 - S;
+      if (u0 < S) {
+        u0 = a.top_k * rtiles + u0;
+      } else {
+        u0 -= S;
+        const int p = u0 / rtiles;
+        u0 = owner_slot(a, p) * rtiles + (u0 - p * rtiles);
+      }
     }
     decode_down_peer<FINITE>(a, u0 / rtiles, u0);
     return;
@@ -887,8 +908,8 @@ extern "C" int glm53_ep_owner_decode_p2p(void* buffer, int64_t H, int world, int
   a.back_cnt_off = (int64_t)lay.cnt_back;
   a.rank = rank;
   a.cap = (int)capacity;
+  a.shared_first = true;  // owner grid order (see DecodeArgs)
   if (has_shared) {  // the home tokens' shared expert rides in the same launches
-    a.shared_first = true;
     a.Is = (int)I_shared;
     a.n_shared = (int)T_shared;
     a.shared_x = (const uint16_t*)shared_x;
