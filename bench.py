@@ -272,7 +272,7 @@ def bench_b200(args, world, rank, local):
             bank.gate_up_scale_inv.data_ptr(), bank.down_weight.data_ptr(), bank.down_scale_inv.data_ptr(), n_exp,
             I, sh[0].data_ptr(), sh[1].data_ptr(), sh[2].data_ptr(), sh[3].data_ptr(), sh[4].data_ptr(),
             sh[5].data_ptr(), I, LIMIT, outs[i].data_ptr(), dws.data_ptr(), dws.numel(), status.data_ptr(),
-            flags[i % args.layers], stream), "decode")
+            flags[i % args.layers] | N.FLAG_AFTER_ROUTER, stream), "decode")
 
     # A model's decode graph chains its layers back to back; here one CUDA
     # graph chains GRAPH_STEPS steps (rotating layers and inputs), and a

@@ -25,6 +25,7 @@ GLM53_ERR_INDEX = 3
 FLAG_E4M3_FINITE = 1
 FLAG_SHARED_ONLY = 2
 FLAG_SKIP_SHARED = 4
+FLAG_AFTER_ROUTER = 8
 
 STATUS_BAD_EXPERT = 1
 STATUS_WAIT_TIMEOUT = 2
@@ -222,6 +223,11 @@ def decode_flags(*weights: torch.Tensor) -> int:
     return FLAG_E4M3_FINITE if e4m3_finite(*weights) else 0
 
 
+def e4m3_scanned(*weights: torch.Tensor) -> bool:
+    """True when e4m3_finite(*weights) answers from its cache (no device pass)."""
+    return all((w.data_ptr(), tuple(w.shape), w._version, w.device.index) in _finite_cache for w in weights)
+
+
 class Workspace:
     """Per-device, grow-only, zero-initialised scratch buffers owned by a plan.
 
@@ -230,6 +236,11 @@ class Workspace:
 
     def __init__(self) -> None:
         self._buffers: dict[tuple, torch.Tensor] = {}
+
+    def has(self, device: torch.device, key: str, nbytes: int) -> bool:
+        """True when get() would return an existing buffer (no allocation)."""
+        buf = self._buffers.get((device, key))
+        return buf is not None and buf.numel() >= nbytes
 
     def get(self, device: torch.device, key: str, nbytes: int) -> torch.Tensor:
         k = (device, key)

@@ -87,12 +87,16 @@ struct DecodeArgs {
   // partials the last-arriver reduce waits for (0 = every slot)
   int gu_begin, gu_end, dn_begin, dn_end, dn_expect;
   bool dn_no_reduce;
-  // peer-memory owners: the shared-expert slots (which wait for no arrival)
-  // take the first CTAs of both grids instead of the last, and the routed
-  // slots run in slot-position-major order, (src 0, s 0), (src 1, s 0), ...:
+  // the shared-expert slots (which wait for nothing) take the first CTAs of
+  // both grids instead of the last.  Peer-memory owners then run the routed
+  // slots in slot-position-major order, (src 0, s 0), (src 1, s 0), ...:
   // routes fill each source's slots from s = 0, so the occupied slots come
   // first and the empty ones (which only wait and exit) last
   bool shared_first;
+  // GLM53_FLAG_AFTER_ROUTER: gate/up is a programmatic dependent of the
+  // router; its routed CTAs wait for the router (griddepcontrol.wait) before
+  // they read the expert ids and only then let the down grid launch
+  bool after_router;
 };
 
 // Physical routed slot p of a peer-memory owner grid -> slot (src, s) = src * cap + s.
@@ -114,6 +118,13 @@ __host__ __device__ __forceinline__ int align16i(int v) { return (v + 15) & ~15;
 constexpr int kWarpsPerBlock = 4;
 constexpr int kRing = 8;       // gate/up: 64-wide K slices in flight per warp (1 KB each)
 constexpr int kRingDown = 12;  // down: its per-warp streams are short (I/64 slices), so deeper
+// Gate/up launched as a programmatic dependent of the router: the block
+// scheduler fills the SMs one after another for such a grid, so 4-warp CTAs
+// would crowd about 60% of the SMs.  One 12-warp CTA per SM instead (its
+// shared memory is at least half an SM's), which still leaves room for two
+// down CTAs to prefetch beside it.
+constexpr int kWideWarps = 12;
+constexpr int kWideRing = 9;
 
 // ---------------------------------------------------------------------------
 // Gate / up / SwiGLU
@@ -166,25 +177,26 @@ __device__ __forceinline__ GateUpRows gate_up_rows(const DecodeArgs& a, int unit
   return r;
 }
 
-template <bool FINITE>
-__global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_gate_up_v4(DecodeArgs a) {
-  constexpr int P = kRing;
+// W warps per CTA, one unit (8 gate + 8 up rows) per warp, P slices in flight per warp.
+template <bool FINITE, int W, int P>
+__global__ void __launch_bounds__(32 * W) decode_gate_up_v4(DecodeArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
   uint4* ring = reinterpret_cast<uint4*>(smem) + (size_t)warp * P * 64;
-  __half* xs = reinterpret_cast<__half*>(reinterpret_cast<uint4*>(smem) + (size_t)kWarpsPerBlock * P * 64);
+  __half* xs = reinterpret_cast<__half*>(reinterpret_cast<uint4*>(smem) + (size_t)W * P * 64);
   float* scratch = reinterpret_cast<float*>(xs + align16i(a.H + 8));
   const int routed_units = a.top_k * (a.I >> 3);
   const int nunits = a.gu_end ? a.gu_end : routed_units + shared_slots(a) * (a.Is >> 3);
-  int unit = a.gu_begin + blockIdx.x * kWarpsPerBlock + warp;
+  int unit = a.gu_begin + blockIdx.x * W + warp;
   // every unit of a block belongs to one slot (I/8 and I_shared/8 are
-  // multiples of 4 here)
-  int unit0 = a.gu_begin + blockIdx.x * kWarpsPerBlock;
-  if (a.shared_first) {  // physical order: shared units, then routed units by slot position
+  // multiples of W here)
+  int unit0 = a.gu_begin + blockIdx.x * W;
+  if (a.shared_first) {  // physical order: shared units, then routed units (owners: by slot position)
     const int S = nunits - routed_units, per = a.I >> 3;
     auto logical = [&](int u) {
       if (u < S) return routed_units + u;
       u -= S;
+      if (!a.arrivals) return u;
       const int p = u / per;
       return owner_slot(a, p) * per + (u - p * per);
     };
@@ -193,11 +205,13 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_gate_up_v4(DecodeA
   }
   const bool active = unit < nunits;
   const int jb = unit0 < routed_units ? unit0 / (a.I >> 3) : a.top_k + (unit0 - routed_units) / (a.Is >> 3);
+  if (a.after_router && jb < a.top_k) pdl_wait();  // the expert ids come from the router
   if (a.arrivals && jb < a.top_k) {  // peer-memory dispatch: wait for every rank's slots
     if (threadIdx.x == 0) wait_counter_geq(a.arrivals, (*a.epoch + 1ull) * a.arrivals_per_step, a.status);
     __syncthreads();
   }
-  // the down stage may launch now: its prologue only streams weights
+  // the down stage may launch now: its prologue only streams weights (and,
+  // after the router, reads expert ids that every routed CTA has seen final)
   pdl_trigger();
   if (a.route_out && jb < a.top_k && a.ids[jb] == kEmptySlot) return;
   GateUpRows rw{};
@@ -371,7 +385,7 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_down_v4(DecodeArgs
       w0 = a.td_w[j] + (size_t)row0 * K;
       srow = a.td_s[j] + (size_t)(row0 >> 7) * cols;
     } else {
-      const uint32_t e = a.ids[j];
+      const uint32_t e = __ldcg(a.ids + j);  // from L2: the router wrote it while this grid's producer ran
       valid = e < (uint32_t)a.E;
       const uint32_t es = valid ? e : 0u;
       w0 = a.d_w + ((size_t)es * a.H + row0) * K;
@@ -580,10 +594,10 @@ static bool tensor_core_shape(const DecodeArgs& a) {
 // start before the previous kernel on the stream has finished; it orders
 // itself with pdl_wait).
 static cudaError_t launch_decode(void (*kernel)(DecodeArgs), int blocks, size_t smem, cudaStream_t st, bool pdl,
-                                 const DecodeArgs& a) {
+                                 const DecodeArgs& a, int warps = kWarpsPerBlock) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)blocks);
-  cfg.blockDim = dim3(32 * kWarpsPerBlock);
+  cfg.blockDim = dim3(32 * warps);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -594,18 +608,39 @@ static cudaError_t launch_decode(void (*kernel)(DecodeArgs), int blocks, size_t 
   return cudaLaunchKernelEx(&cfg, kernel, a);
 }
 
+// Shared memory of one SM and the per-CTA reservation on the current device.
+static void sm_smem(size_t& per_sm, size_t& reserved) {
+  int dev = 0, v = 0, r = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+  cudaDeviceGetAttribute(&r, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+  per_sm = (size_t)v;
+  reserved = (size_t)r;
+}
+
+template <bool FINITE, int W, int P>
+static int launch_gate_up(const DecodeArgs& a, cudaStream_t st, bool pdl, size_t min_smem) {
+  const size_t smem = std::max(min_smem, (size_t)W * P * 64 * 16 + (size_t)align16i(a.H + 8) * 2 + 32 * sizeof(float));
+  if (smem > 48 * 1024) {
+    int rc = ensure_max_smem((const void*)decode_gate_up_v4<FINITE, W, P>, smem);
+    if (rc) return rc;
+  }
+  const int units = (a.gu_end ? a.gu_end : a.top_k * (a.I >> 3) + shared_slots(a) * (a.Is >> 3)) - a.gu_begin;
+  launch_decode(decode_gate_up_v4<FINITE, W, P>, (units + W - 1) / W, smem, st, pdl, a, W);
+  return check_launch("decode_gate_up_v4");
+}
+
 template <bool FINITE>
 static int launch_v4(const DecodeArgs& a, cudaStream_t st, bool gate_up_only) {
-  const size_t ring = (size_t)kWarpsPerBlock * kRing * 64 * 16;
   {
-    const size_t smem = ring + (size_t)align16i(a.H + 8) * 2 + 32 * sizeof(float);
-    if (smem > 48 * 1024) {
-      int rc = ensure_max_smem((const void*)decode_gate_up_v4<FINITE>, smem);
-      if (rc) return rc;
+    int rc;
+    if (a.after_router && (a.I >> 3) % kWideWarps == 0 && (a.Is >> 3) % kWideWarps == 0) {
+      size_t per_sm = 0, reserved = 0;
+      sm_smem(per_sm, reserved);
+      rc = launch_gate_up<FINITE, kWideWarps, kWideRing>(a, st, true, per_sm / 2 + 16 - std::min(reserved, per_sm / 2));
+    } else {
+      rc = launch_gate_up<FINITE, kWarpsPerBlock, kRing>(a, st, a.after_router, 0);
     }
-    const int units = (a.gu_end ? a.gu_end : a.top_k * (a.I >> 3) + shared_slots(a) * (a.Is >> 3)) - a.gu_begin;
-    launch_decode(decode_gate_up_v4<FINITE>, (units + kWarpsPerBlock - 1) / kWarpsPerBlock, smem, st, false, a);
-    int rc = check_launch("decode_gate_up_v4");
     if (rc || gate_up_only) return rc;
   }
   const size_t smem = (size_t)kWarpsPerBlock * kRingDown * 64 * 16 + (size_t)align16i(a.I + 8) * 2 + 32 * sizeof(float);
@@ -641,6 +676,8 @@ int packed_decode(const DecodeArgs& a_in, cudaStream_t st, bool gate_up_only, ui
       a.dn_expect = a.top_k;
     }
   }
+  if (shared_only || skip_shared) a.after_router = false;
+  a.shared_first = a.shared_first || a.after_router;
   if (!tensor_core_shape(a)) {
     const int items = a.top_k * a.I + a.Is;
     decode_gate_up_scalar_kernel<<<(items + 7) / 8, 256, 0, st>>>(a);
@@ -737,6 +774,7 @@ extern "C" int glm53_packed_decode_moe(const void* x, int64_t H, const uint32_t*
   a.gu_s = gate_up_s;
   a.d_w = down_w;
   a.d_s = down_s;
+  a.after_router = (flags & GLM53_FLAG_AFTER_ROUTER) != 0;
   return packed_decode(a, (cudaStream_t)stream, false, flags);
 }
 

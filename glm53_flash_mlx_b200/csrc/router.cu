@@ -166,7 +166,10 @@ __device__ void warp_topk_keys(const uint32_t* keys, const float* sigs, const To
 
 // FP32 GEMV for T <= kRouterSmallT tokens: one block per expert row, each
 // thread sums float4 slices k = 4*tid + 1024*i in K order, then an ordered
-// warp / block reduction.  The last block to finish runs the top-k.
+// warp / block reduction.  The last block to finish runs the top-k.  The
+// group-mask scratch (8 warps x E floats) is dynamic shared memory, present
+// only when n_group > 1, so that the router's blocks leave room on the SMs
+// for a decode stage launched as their programmatic dependent.
 template <int T_MAX, int PER>
 __global__ void __launch_bounds__(256) router_small_kernel(
     const uint16_t* __restrict__ x, int T, int H, const float* __restrict__ w,
@@ -174,7 +177,10 @@ __global__ void __launch_bounds__(256) router_small_kernel(
     uint32_t* counter, uint32_t* __restrict__ idx, float* __restrict__ scores) {
   __shared__ float part[8][T_MAX];
   __shared__ bool is_last;
-  __shared__ float choice_smem[8][kRouterMaxE];
+  extern __shared__ float choice_dyn[];  // [8][E] when n_group > 1
+  // a dependent launched with programmatic serialisation may start now; it
+  // waits (griddepcontrol.wait) before it reads this kernel's results
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e = blockIdx.x;
   const float* wr = w + (size_t)e * H;
@@ -221,7 +227,7 @@ __global__ void __launch_bounds__(256) router_small_kernel(
   __threadfence();
   for (int t = warp; t < T; t += 8) {  // one warp per token
     warp_topk_keys<PER>(key_buf + (size_t)t * p.E, sig_buf + (size_t)t * p.E, p, idx + (size_t)t * p.top_k,
-                        scores + (size_t)t * p.top_k, choice_smem[warp]);
+                        scores + (size_t)t * p.top_k, choice_dyn + (size_t)warp * p.E);
   }
   if (threadIdx.x == 0) *counter = 0u;  // leave the workspace reusable
 }
@@ -410,15 +416,16 @@ template <int PER>
 static int launch_small(const uint16_t* x, int T, int H, const float* w, const float* bias, TopkParams p,
                         const RouterScratch& r, uint32_t* idx, float* scores, cudaStream_t st) {
   int blocks = p.E;
+  const size_t dyn = p.n_group > 1 ? (size_t)8 * p.E * sizeof(float) : 0;  // <= 32 KB (E <= 1024)
   if (T <= 1)
-    router_small_kernel<1, PER><<<blocks, 256, 0, st>>>(x, T, H, w, bias, p, r.logits, r.sig, r.key, r.counter,
-                                                        idx, scores);
+    router_small_kernel<1, PER><<<blocks, 256, dyn, st>>>(x, T, H, w, bias, p, r.logits, r.sig, r.key, r.counter,
+                                                          idx, scores);
   else if (T <= 8)
-    router_small_kernel<8, PER><<<blocks, 256, 0, st>>>(x, T, H, w, bias, p, r.logits, r.sig, r.key, r.counter,
-                                                        idx, scores);
+    router_small_kernel<8, PER><<<blocks, 256, dyn, st>>>(x, T, H, w, bias, p, r.logits, r.sig, r.key, r.counter,
+                                                          idx, scores);
   else
-    router_small_kernel<kRouterSmallT, PER><<<blocks, 256, 0, st>>>(x, T, H, w, bias, p, r.logits, r.sig, r.key,
-                                                                    r.counter, idx, scores);
+    router_small_kernel<kRouterSmallT, PER><<<blocks, 256, dyn, st>>>(x, T, H, w, bias, p, r.logits, r.sig, r.key,
+                                                                      r.counter, idx, scores);
   return check_launch("router_small_kernel");
 }
 

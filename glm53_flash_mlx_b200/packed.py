@@ -19,6 +19,7 @@ from torch import nn
 from . import _native as N
 from .abi import PACKED_EXPERT_BANK_ABI  # noqa: F401
 from .fp8 import BLOCK_SIZE, DECODE_TOP_K, DirectFP8MoE, block_fp8_linear, swiglu_pair
+from .router import Float32Gate
 from .ownership import (
     ResidentTensor,
     TensorLayout,
@@ -196,20 +197,30 @@ def shared_fp8_tensors(shared) -> tuple | None:
 
 def packed_decode_moe(x: torch.Tensor, expert_ids: torch.Tensor, scores: torch.Tensor, bank: PackedFP8ExpertBank,
                       shared: tuple | None, *, limit: float, workspace: N.Workspace | None = None,
-                      status: torch.Tensor | None = None, split: str | None = None) -> torch.Tensor | None:
+                      status: torch.Tensor | None = None, split: str | None = None,
+                      after_router: bool = False) -> torch.Tensor | None:
     """One-token routed MoE (+ shared expert) over the packed bank.
 
     x: BF16 [H]; expert_ids: int32/uint32 [top_k]; scores: float32 [top_k].
     Returns BF16 [H].  ``split="shared"`` computes only the shared expert into
     ``workspace`` (ids and scores unread, returns None); a later
     ``split="routed"`` call on the same workspace, ordered after it, finishes
-    the layer (GLM53_FLAG_SHARED_ONLY / GLM53_FLAG_SKIP_SHARED)."""
+    the layer (GLM53_FLAG_SHARED_ONLY / GLM53_FLAG_SKIP_SHARED).
+    ``after_router=True`` states that the last kernel on the current stream
+    is the router that produced ``expert_ids``/``scores`` from ``x``: when no
+    argument needs a copy here, the shared expert then streams while that
+    router still runs (GLM53_FLAG_AFTER_ROUTER; same result bits)."""
     dev = N.require_cuda(x, expert_ids, scores, bank.gate_up_weight)
     H = bank.hidden_size
     I = bank.intermediate_size
     top_k = expert_ids.numel()
     if x.numel() != H:
         raise ValueError(f"decode input width {x.numel()} != bank hidden {H}")
+    # no kernel may run between the router and this call's launch for the
+    # programmatic overlap: every argument must be usable as it is
+    overlap = (after_router and split is None and x.is_contiguous() and expert_ids.is_contiguous() and
+               scores.is_contiguous() and expert_ids.dtype == torch.int32 and
+               scores.dtype == torch.float32)
     x = x.reshape(H).contiguous()
     ids = expert_ids.reshape(-1).to(torch.int32).contiguous()
     sc = scores.reshape(-1).to(torch.float32).contiguous()
@@ -219,16 +230,21 @@ def packed_decode_moe(x: torch.Tensor, expert_ids: torch.Tensor, scores: torch.T
     else:
         sg_w = sg_s = su_w = su_s = sd_w = sd_s = None
         Is = 0
-    flags = N.decode_flags(bank.gate_up_weight, bank.down_weight, *(() if shared is None else (sg_w, su_w, sd_w)))
+    weights = (bank.gate_up_weight, bank.down_weight, *(() if shared is None else (sg_w, su_w, sd_w)))
+    overlap = overlap and N.e4m3_scanned(*weights)
+    flags = N.decode_flags(*weights)
     if split is not None:
         if shared is None or split not in ("shared", "routed"):
             raise ValueError("split decode needs a shared expert and split='shared' or 'routed'")
         flags |= N.FLAG_SHARED_ONLY if split == "shared" else N.FLAG_SKIP_SHARED
     ws_bytes = N.lib().glm53_packed_decode_workspace_bytes(top_k, H, I, Is)
     wsp = workspace or N.Workspace()
+    overlap = overlap and wsp.has(dev, "decode", ws_bytes) and (status is not None or wsp.has(dev, "status", 4))
     ws = wsp.get(dev, "decode", ws_bytes)
     if status is None:
         status = wsp.get(dev, "status", 4)
+    if overlap:  # nothing was launched since the router: no copy, scan or zero-fill above
+        flags |= N.FLAG_AFTER_ROUTER
     out = torch.empty(H, dtype=torch.bfloat16, device=dev)
     N.check(
         N.lib().glm53_packed_decode_moe(
@@ -381,7 +397,8 @@ class PackedFP8MoE(DirectFP8MoE):
             raise ValueError("exact fused packed decode requires an integral clamp limit")
         shared = shared_fp8_tensors(self.shared_experts)
         result = packed_decode_moe(flat_x[0], indices.reshape(-1), scores.reshape(-1), self.bank, shared,
-                                   limit=limit, workspace=self._workspace).reshape(x.shape)
+                                   limit=limit, workspace=self._workspace,
+                                   after_router=isinstance(self.gate, Float32Gate)).reshape(x.shape)
         if shared is None and self.shared_experts is not None:
             result = result + self.shared_experts(x)
         return result

@@ -59,6 +59,16 @@ extern "C" {
 #define GLM53_FLAG_SHARED_ONLY 2u
 #define GLM53_FLAG_SKIP_SHARED 4u
 
+/* `flags` bit of glm53_packed_decode_moe: the kernel launched just before this
+ * call on the same stream is the glm53_router_topk that produced expert_ids
+ * and scores (or a kernel that only converts them).  The gate/up stage is then
+ * launched as a programmatic dependent of it: the shared expert's rows, which
+ * need no routing, stream while the router still runs, and the routed rows
+ * wait on the device for the router's results.  The caller guarantees that x
+ * and the workspace are not written by that previous kernel.  Same bits as
+ * without the flag; ignored together with the split flags. */
+#define GLM53_FLAG_AFTER_ROUTER 8u
+
 /* Kernel ABI identity string (replaces glm53_flash_mlx/abi.py:3-15 for the
  * CUDA kernels; part of any cache identity that depends on kernel numerics). */
 const char* glm53_kernel_abi(void);

@@ -233,6 +233,77 @@ def test_split_decode_matches_single_call_bitwise(G, S):
         assert torch.equal(full, part), t
 
 
+def test_decode_after_router_overlap_bitwise(G, S):
+    """GLM53_FLAG_AFTER_ROUTER (gate/up launched as a programmatic dependent
+    of the router, the shared expert streaming while the router runs) gives
+    the bits of the serial launch: through the module (eager and as a CUDA
+    graph of several layers back to back) and through the C-ABI."""
+    from glm53_flash_mlx_b200 import _native as N
+    from glm53_flash_mlx_b200.packed import packed_decode_moe, shared_fp8_tensors
+    from glm53_flash_mlx_b200.router import Float32Gate
+
+    E, H, I = 64, 4096, 1536
+    cfg = S.moe_config(H, I, E, 8, 10.0)
+    mods = []
+    for layer in range(3):
+        gate = Float32Gate(cfg, device="cuda")
+        w, b = S.make_router(E, H, seed=80 + layer, device="cuda")
+        gate.weight.copy_(w)
+        gate.e_score_correction_bias.copy_(b)
+        mods.append(G.PackedFP8MoE(S.make_bank(E, H, I, seed=90 + layer, device="cuda"), cfg, gate,
+                                   S.make_shared(H, I, seed=95 + layer, device="cuda")))
+
+    def serial(m, x):
+        idx, sc = m.gate(x)
+        return packed_decode_moe(x.reshape(-1), idx.reshape(-1), sc.reshape(-1), m.bank,
+                                 shared_fp8_tensors(m.shared_experts), limit=10.0, workspace=N.Workspace())
+
+    xs = [S.random_bf16((1, 1, H), seed=100 + t, device="cuda") for t in range(6)]
+    for t, x in enumerate(xs):  # module forward: the flag is set from the second call on
+        for m in mods:
+            got = m(x)
+            assert torch.equal(got.reshape(-1), serial(m, x)), (t, "module")
+    # raw C-ABI: router then decode with the flag, the same workspace every layer
+    lib = N.lib()
+    ws = N.Workspace()
+    dws = ws.get(torch.device("cuda"), "d", lib.glm53_packed_decode_workspace_bytes(8, H, I, I))
+    rws = ws.get(torch.device("cuda"), "r", lib.glm53_router_workspace_bytes(1, E))
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    idx = torch.empty(8, dtype=torch.int32, device="cuda")
+    sc = torch.empty(8, dtype=torch.float32, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    for t, x in enumerate(xs):
+        for m in mods:
+            sh = shared_fp8_tensors(m.shared_experts)
+            out = torch.empty(H, dtype=torch.bfloat16, device="cuda")
+            N.check(lib.glm53_router_topk(x.data_ptr(), 1, H, m.gate.weight.data_ptr(), E,
+                                          m.gate.e_score_correction_bias.data_ptr(), 8, 1, 1, 1, 1.0,
+                                          idx.data_ptr(), sc.data_ptr(), None, rws.data_ptr(), rws.numel(), st), "r")
+            N.check(lib.glm53_packed_decode_moe(
+                x.data_ptr(), H, idx.data_ptr(), sc.data_ptr(), 8, m.bank.gate_up_weight.data_ptr(),
+                m.bank.gate_up_scale_inv.data_ptr(), m.bank.down_weight.data_ptr(), m.bank.down_scale_inv.data_ptr(),
+                E, I, *(p.data_ptr() for p in sh), I, 10.0, out.data_ptr(), dws.data_ptr(), dws.numel(),
+                status.data_ptr(), N.FLAG_E4M3_FINITE | N.FLAG_AFTER_ROUTER, st), "d")
+            assert torch.equal(out, serial(m, x)), (t, "c-abi")
+    assert int(status.item()) == 0
+    # CUDA graph: three layers chained, replayed over several inputs
+    static_x = xs[0].clone()
+    for m in mods:
+        m(static_x)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        h = static_x
+        outs = []
+        for m in mods:
+            outs.append(m(h))
+    for t, x in enumerate(xs):
+        static_x.copy_(x)
+        g.replay()
+        torch.cuda.synchronize()
+        for m, o in zip(mods, outs):
+            assert torch.equal(o.reshape(-1), serial(m, x)), (t, "graph")
+
+
 def test_packed_moe_module_matches_direct_module_bitwise(G, S):
     """tests/test_fp8_metal.py:87-151: packed decode and 9-row prefill are
     bit-equal to the Direct module over the same expert tensors."""
