@@ -377,8 +377,9 @@ def bench_b200(args, world, rank, local):
         e_ms = max_over_ranks(e_start.elapsed_time(e_stop), world)
         e2e = {"value": round(tokens / (e_ms / 1e3), 2), "unit": "tokens/s", "h2d_bytes_per_step": H * 2,
                "d2h_bytes_per_step": H * 2,
-               "api": "PackedFP8MoE.capture_decode() replays (Float32Gate router + packed decode), pinned host "
-                      "input copied in and output copied out every step"}
+               "api": "PackedFP8MoE.capture_decode() step per token: one glm53_decode_step_host call (a kernel "
+                      "reads the pinned host input row, Float32Gate router, packed decode writing the pinned host "
+                      "output row)"}
         del caps
 
     step_us = t_ms / args.steps * 1e3

@@ -44,6 +44,7 @@ SIGNATURES: dict[str, tuple] = {
     "glm53_last_error": (ctypes.c_char_p, []),
     "glm53_fp8_linear": (_int, [_vp, _i64, _i64, _vp, _i64, _vp, _vp, _u32, _vp]),
     "glm53_e4m3_scan": (_int, [_vp, _i64, _vp, _vp]),
+    "glm53_graph_step": (_int, [_vp, _vp, _vp, _sz, _vp, _vp, _sz, _vp]),
     "glm53_router_workspace_bytes": (_sz, [_i64, _i64]),
     "glm53_router_topk": (
         _int,
@@ -120,7 +121,26 @@ SIGNATURES: dict[str, tuple] = {
          _i64, _f, _vp, _vp, _sz, _vp, _u32, _vp],
     ),
     "glm53_sigmoid_bf16": (_int, [_vp, _i64, _vp, _vp]),
+    "glm53_decode_step_host": (_int, [_vp, _vp, _vp, _vp]),
 }
+
+
+class DecodeStepDesc(ctypes.Structure):
+    """glm53_decode_step_desc (include/glm53_b200.h), field for field."""
+
+    _fields_ = [
+        ("H", _i64), ("E", _i64), ("I", _i64), ("I_shared", _i64),
+        ("top_k", _int), ("n_group", _int), ("topk_group", _int), ("norm_topk_prob", _int),
+        ("routed_scaling_factor", _f), ("limit", _f), ("flags", _u32),
+        ("router_w", _vp), ("router_bias", _vp),
+        ("gate_up_w", _vp), ("gate_up_s", _vp), ("down_w", _vp), ("down_s", _vp),
+        ("shared_gate_w", _vp), ("shared_gate_s", _vp), ("shared_up_w", _vp), ("shared_up_s", _vp),
+        ("shared_down_w", _vp), ("shared_down_s", _vp),
+        ("x", _vp), ("expert_ids", _vp), ("scores", _vp), ("out", _vp),
+        ("router_workspace", _vp), ("router_workspace_bytes", _sz),
+        ("decode_workspace", _vp), ("decode_workspace_bytes", _sz),
+        ("status", _vp),
+    ]
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
@@ -174,7 +194,13 @@ def ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream(device: torch.device | None = None) -> int:
+    """The current CUDA stream of `device` as a raw handle."""
+    if _raw_stream is not None and isinstance(device, torch.device) and device.index is not None:
+        return _raw_stream(device.index)
     return torch.cuda.current_stream(device).cuda_stream
 
 

@@ -131,8 +131,8 @@ __global__ void __launch_bounds__(32 * kBdWarps) batched_gate_up_kernel(BatchedA
     const uint8_t* pu = uw + (size_t)g * a.H + 16 * q;
     auto issue = [&](int sl) {
       uint4* dst = ring + (sl % P) * 64 + lane;
-      cp_async_16(dst, valid ? (const void*)(pg + 64 * sl) : (const void*)a.x, valid);
-      cp_async_16(dst + 32, valid ? (const void*)(pu + 64 * sl) : (const void*)a.x, valid);
+      cp_async_16_l2_256(dst, valid ? (const void*)(pg + 64 * sl) : (const void*)a.x, valid);
+      cp_async_16_l2_256(dst + 32, valid ? (const void*)(pu + 64 * sl) : (const void*)a.x, valid);
     };
 #pragma unroll
     for (int s = 0; s < P - 1; ++s) {
@@ -196,8 +196,8 @@ __global__ void __launch_bounds__(32 * kBdWarps) batched_down_kernel(BatchedArgs
     const uint8_t* p8 = p0 + (size_t)8 * K;
     auto issue = [&](int sl) {
       uint4* dst = ring + (sl % P) * 64 + lane;
-      cp_async_16(dst, valid ? (const void*)(p0 + 64 * sl) : (const void*)a.x, valid);
-      cp_async_16(dst + 32, valid ? (const void*)(p8 + 64 * sl) : (const void*)a.x, valid);
+      cp_async_16_l2_256(dst, valid ? (const void*)(p0 + 64 * sl) : (const void*)a.x, valid);
+      cp_async_16_l2_256(dst + 32, valid ? (const void*)(p8 + 64 * sl) : (const void*)a.x, valid);
     };
 #pragma unroll
     for (int s = 0; s < P - 1; ++s) {

@@ -1,9 +1,11 @@
 // Error plumbing, identity and small diagnostic entry points of the C ABI.
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
 
 #include "common.cuh"
+#include "kernels.cuh"
 
 namespace glm53 {
 
@@ -80,6 +82,62 @@ extern "C" const char* glm53_kernel_abi(void) {
 }
 
 extern "C" const char* glm53_last_error(void) { return g_last_error; }
+
+namespace glm53 {
+
+// 16-byte copy between device memory and pinned (device-mapped) host memory.
+// A programmatic dependent (the router of a host decode step) may launch at
+// once; it waits for this grid before it reads the copy.
+__global__ void __launch_bounds__(256) copy16_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst,
+                                                     size_t n16) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (size_t)gridDim.x * blockDim.x)
+    dst[i] = src[i];
+}
+
+void* mapped_host(const void* p) {
+  cudaPointerAttributes at;
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  return at.type == cudaMemoryTypeHost ? at.devicePointer : nullptr;
+}
+
+// Small host <-> device copy: a kernel over the pinned buffer's device
+// mapping (a copy-engine transfer of a few KB costs 7-10 us of stream time
+// on B200, the kernel about 2), else cudaMemcpyAsync.
+cudaError_t small_copy(void* dst, const void* src, size_t bytes, bool to_device, cudaStream_t st, bool* by_kernel) {
+  const void* host = to_device ? src : dst;
+  void* mapped = (bytes % 16 == 0 && ((uintptr_t)src | (uintptr_t)dst) % 16 == 0) ? mapped_host(host) : nullptr;
+  if (by_kernel) *by_kernel = mapped != nullptr;
+  if (!mapped)
+    return cudaMemcpyAsync(dst, src, bytes, to_device ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToHost, st);
+  const size_t n16 = bytes / 16;
+  const unsigned blocks = (unsigned)std::min<size_t>((n16 + 255) / 256, 64);
+  copy16_kernel<<<blocks, 256, 0, st>>>((const uint4*)(to_device ? mapped : src),
+                                        (uint4*)(to_device ? dst : mapped), n16);
+  return cudaGetLastError();
+}
+
+}  // namespace glm53
+
+extern "C" int glm53_graph_step(void* graph_exec, const void* x_host, void* x_dev, size_t x_bytes, const void* out_dev,
+                                void* out_host, size_t out_bytes, void* stream) {
+  if (!graph_exec || (x_bytes && (!x_host || !x_dev)) || (out_host && (!out_dev || !out_bytes))) {
+    set_last_error("glm53_graph_step: invalid arguments");
+    return GLM53_ERR_INVALID;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaError_t e = x_bytes ? small_copy(x_dev, x_host, x_bytes, true, st, nullptr) : cudaSuccess;
+  if (e == cudaSuccess) e = cudaGraphLaunch((cudaGraphExec_t)graph_exec, st);
+  if (e == cudaSuccess && out_host) e = small_copy(out_host, out_dev, out_bytes, false, st, nullptr);
+  if (e != cudaSuccess) {
+    set_last_error("glm53_graph_step: %s", cudaGetErrorString(e));
+    return GLM53_ERR_CUDA;
+  }
+  return GLM53_OK;
+}
 
 extern "C" int glm53_sigmoid_bf16(const void* gate, int64_t n, void* out, void* stream) {
   if (n < 0 || (n > 0 && (!gate || !out))) {

@@ -49,8 +49,8 @@ __global__ void __launch_bounds__(32 * KS) gemv_stream_kernel(const uint16_t* __
       const int k = kw + 64 * i_sl;
       uint4* dst = ring + ((i_it * nslice + i_sl) % P) * 64 + lane;
       const bool v0 = row0 + g < N, v8 = row0 + g + 8 < N;
-      cp_async_16(dst, v0 ? (const void*)(w + (size_t)(row0 + g) * K + k) : (const void*)w, v0);
-      cp_async_16(dst + 32, v8 ? (const void*)(w + (size_t)(row0 + g + 8) * K + k) : (const void*)w, v8);
+      cp_async_16_l2_256(dst, v0 ? (const void*)(w + (size_t)(row0 + g) * K + k) : (const void*)w, v0);
+      cp_async_16_l2_256(dst + 32, v8 ? (const void*)(w + (size_t)(row0 + g + 8) * K + k) : (const void*)w, v8);
       if (++i_sl == nslice) {
         i_sl = 0;
         ++i_it;

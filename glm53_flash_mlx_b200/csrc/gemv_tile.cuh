@@ -117,6 +117,14 @@ __device__ __forceinline__ void cp_async_16(void* dst, const void* src, bool val
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_addr(dst)), "l"(src),
                "r"(valid ? 16 : 0));
 }
+// As cp_async_16, with the hint that L2 fetch the whole aligned 256-byte
+// block around the source from DRAM.  The decode streams read each weight row
+// 64 bytes per slice; the longer DRAM bursts measured about 1 us less per
+// config-2 decode step on B200 (the 128-byte hint: no change).
+__device__ __forceinline__ void cp_async_16_l2_256(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16, %2;\n" ::"r"(smem_addr(dst)), "l"(src),
+               "r"(valid ? 16 : 0));
+}
 __device__ __forceinline__ void cp_async_commit_group() { asm volatile("cp.async.commit_group;\n" ::); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait_group() {

@@ -92,6 +92,20 @@ int rows_to_f16(const uint16_t* x, int64_t H, const uint32_t* order, int div, in
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// glm53_router_topk; with pdl the small-T kernel is launched as a
+// programmatic dependent of the previous kernel on the stream (router.cu).
+int router_topk(const void* x, int64_t T, int64_t H, const float* w, int64_t E, const float* bias, int top_k,
+                int n_group, int topk_group, int norm_topk_prob, float routed_scaling_factor, uint32_t* indices,
+                float* scores, float* logits, void* workspace, size_t workspace_bytes, cudaStream_t st, bool pdl);
+
+// Device address of a pinned (device-mapped) host buffer, or nullptr for
+// pageable memory (capi.cu).
+void* mapped_host(const void* p);
+// Small host <-> device copy: a kernel over the pinned buffer's mapping when
+// both addresses and the size are 16-byte multiples (*by_kernel = true), else
+// cudaMemcpyAsync (capi.cu).
+cudaError_t small_copy(void* dst, const void* src, size_t bytes, bool to_device, cudaStream_t st, bool* by_kernel);
+
 // Peer-memory expert parallelism: every rank allocates one buffer of this
 // layout and maps every peer's (CUDA IPC).  Slot (src, s) of recv_x/recv_e is
 // written by rank src; slot (owner, s) of back by rank owner; the counters

@@ -21,6 +21,7 @@
 // weight copies are issued before the activations are staged.
 // Shapes the tiles do not cover take a scalar path, one warp per dot product.
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -222,8 +223,8 @@ __global__ void __launch_bounds__(32 * W) decode_gate_up_v4(DecodeArgs a) {
   const int nslice = a.H >> 6;
   auto issue = [&](int sl) {
     uint4* d = ring + (sl % P) * 64 + lane;
-    cp_async_16(d, ld ? (const void*)(pg + 64 * sl) : (const void*)a.x, ld);
-    cp_async_16(d + 32, ld ? (const void*)(pu + 64 * sl) : (const void*)a.x, ld);
+    cp_async_16_l2_256(d, ld ? (const void*)(pg + 64 * sl) : (const void*)a.x, ld);
+    cp_async_16_l2_256(d + 32, ld ? (const void*)(pu + 64 * sl) : (const void*)a.x, ld);
   };
 #pragma unroll
   for (int s = 0; s < P - 1; ++s) {
@@ -297,8 +298,8 @@ __device__ __forceinline__ void decode_down_peer(const DecodeArgs& a, int jb, in
     const int nslice = K >> 6;
     auto issue = [&](int sl) {
       uint4* d = ring + (sl % P) * 64 + lane;
-      cp_async_16(d, valid ? (const void*)(p0 + 64 * sl) : (const void*)a.x, valid);
-      cp_async_16(d + 32, valid ? (const void*)(p8 + 64 * sl) : (const void*)a.x, valid);
+      cp_async_16_l2_256(d, valid ? (const void*)(p0 + 64 * sl) : (const void*)a.x, valid);
+      cp_async_16_l2_256(d + 32, valid ? (const void*)(p8 + 64 * sl) : (const void*)a.x, valid);
     };
 #pragma unroll
     for (int k = 0; k < P - 1; ++k) {
@@ -398,8 +399,8 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_down_v4(DecodeArgs
   const int nslice = K >> 6;
   auto issue = [&](int sl) {
     uint4* d = ring + (sl % P) * 64 + lane;
-    cp_async_16(d, ld ? (const void*)(p0 + 64 * sl) : (const void*)a.x, ld);
-    cp_async_16(d + 32, ld ? (const void*)(p8 + 64 * sl) : (const void*)a.x, ld);
+    cp_async_16_l2_256(d, ld ? (const void*)(p0 + 64 * sl) : (const void*)a.x, ld);
+    cp_async_16_l2_256(d + 32, ld ? (const void*)(p8 + 64 * sl) : (const void*)a.x, ld);
   };
 #pragma unroll
   for (int s = 0; s < P - 1; ++s) {
@@ -608,12 +609,23 @@ static cudaError_t launch_decode(void (*kernel)(DecodeArgs), int blocks, size_t 
   return cudaLaunchKernelEx(&cfg, kernel, a);
 }
 
-// Shared memory of one SM and the per-CTA reservation on the current device.
+// Shared memory of one SM and the per-CTA reservation on the current device
+// (queried once per device).
 static void sm_smem(size_t& per_sm, size_t& reserved) {
-  int dev = 0, v = 0, r = 0;
+  constexpr int kMaxDevices = 64;
+  static std::atomic<int> cache[kMaxDevices][2];  // zero-initialised: not yet queried
+  int dev = 0;
   cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
-  cudaDeviceGetAttribute(&r, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+  int v = dev < kMaxDevices ? cache[dev][0].load(std::memory_order_acquire) : 0;
+  int r = dev < kMaxDevices ? cache[dev][1].load(std::memory_order_relaxed) : 0;
+  if (v == 0) {
+    cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+    cudaDeviceGetAttribute(&r, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+    if (dev < kMaxDevices) {
+      cache[dev][1].store(r, std::memory_order_relaxed);
+      cache[dev][0].store(v, std::memory_order_release);
+    }
+  }
   per_sm = (size_t)v;
   reserved = (size_t)r;
 }
@@ -815,6 +827,43 @@ extern "C" int glm53_selected_decode_moe(const void* x, int64_t H, const float* 
     a.td_s[j] = down_s[j];
   }
   return packed_decode(a, (cudaStream_t)stream, false, flags);
+}
+
+extern "C" int glm53_decode_step_host(const glm53_decode_step_desc* d, const void* x_host, void* out_host,
+                                      void* stream) {
+  const char* fn = "glm53_decode_step_host";
+  if (!d || !d->x || !d->out || d->top_k != 8 || d->H <= 0 || d->H % 128 != 0 || d->I <= 0 || d->I % 128 != 0 ||
+      d->I_shared % 128 != 0 || (((uintptr_t)d->x | (uintptr_t)d->out) & 15) != 0) {
+    set_last_error("%s: invalid descriptor (top_k 8, H and I multiples of 128, 16-byte aligned x and out)", fn);
+    return GLM53_ERR_INVALID;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  const size_t row = (size_t)d->H * 2;
+  bool copy_kernel = false;
+  if (x_host) {
+    cudaError_t e = small_copy(d->x, x_host, row, true, st, &copy_kernel);
+    if (e != cudaSuccess) {
+      set_last_error("%s: input copy: %s", fn, cudaGetErrorString(e));
+      return GLM53_ERR_CUDA;
+    }
+  }
+  int rc = router_topk(d->x, 1, d->H, d->router_w, d->E, d->router_bias, d->top_k, d->n_group, d->topk_group,
+                       d->norm_topk_prob, d->routed_scaling_factor, d->expert_ids, d->scores, nullptr,
+                       d->router_workspace, d->router_workspace_bytes, st, copy_kernel);
+  if (rc) return rc;
+  void* mapped_out = out_host && (((uintptr_t)out_host) & 15) == 0 ? mapped_host(out_host) : nullptr;
+  rc = glm53_packed_decode_moe(d->x, d->H, d->expert_ids, d->scores, d->top_k, d->gate_up_w, d->gate_up_s, d->down_w,
+                               d->down_s, d->E, d->I, d->shared_gate_w, d->shared_gate_s, d->shared_up_w,
+                               d->shared_up_s, d->shared_down_w, d->shared_down_s, d->I_shared, d->limit,
+                               mapped_out ? mapped_out : d->out, d->decode_workspace, d->decode_workspace_bytes,
+                               d->status, d->flags | GLM53_FLAG_AFTER_ROUTER, stream);
+  if (rc || !out_host || mapped_out) return rc;
+  const cudaError_t e = cudaMemcpyAsync(out_host, d->out, row, cudaMemcpyDeviceToHost, st);
+  if (e != cudaSuccess) {
+    set_last_error("%s: output copy: %s", fn, cudaGetErrorString(e));
+    return GLM53_ERR_CUDA;
+  }
+  return GLM53_OK;
 }
 
 extern "C" int glm53_packed_decode_gate_up(const void* x, int64_t H, const uint32_t* expert_ids, int top_k,

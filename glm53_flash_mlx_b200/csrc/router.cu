@@ -178,8 +178,11 @@ __global__ void __launch_bounds__(256) router_small_kernel(
   __shared__ float part[8][T_MAX];
   __shared__ bool is_last;
   extern __shared__ float choice_dyn[];  // [8][E] when n_group > 1
-  // a dependent launched with programmatic serialisation may start now; it
-  // waits (griddepcontrol.wait) before it reads this kernel's results
+  // launched as a programmatic dependent of the kernel that writes x: wait
+  // for it (a no-op otherwise).  Then a dependent launched with programmatic
+  // serialisation may start; it waits (griddepcontrol.wait) before it reads
+  // this kernel's results, and may read x right away.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e = blockIdx.x;
@@ -412,20 +415,32 @@ struct RouterScratch {
   uint32_t* counter;
 };
 
+template <int T_MAX, int PER>
+static void launch_small_t(const uint16_t* x, int T, int H, const float* w, const float* bias, TopkParams p,
+                           const RouterScratch& r, uint32_t* idx, float* scores, cudaStream_t st, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)p.E);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = p.n_group > 1 ? (size_t)8 * p.E * sizeof(float) : 0;  // <= 32 KB (E <= 1024)
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, router_small_kernel<T_MAX, PER>, x, T, H, w, bias, p, r.logits, r.sig, r.key, r.counter,
+                     idx, scores);
+}
+
 template <int PER>
 static int launch_small(const uint16_t* x, int T, int H, const float* w, const float* bias, TopkParams p,
-                        const RouterScratch& r, uint32_t* idx, float* scores, cudaStream_t st) {
-  int blocks = p.E;
-  const size_t dyn = p.n_group > 1 ? (size_t)8 * p.E * sizeof(float) : 0;  // <= 32 KB (E <= 1024)
+                        const RouterScratch& r, uint32_t* idx, float* scores, cudaStream_t st, bool pdl) {
   if (T <= 1)
-    router_small_kernel<1, PER><<<blocks, 256, dyn, st>>>(x, T, H, w, bias, p, r.logits, r.sig, r.key, r.counter,
-                                                          idx, scores);
+    launch_small_t<1, PER>(x, T, H, w, bias, p, r, idx, scores, st, pdl);
   else if (T <= 8)
-    router_small_kernel<8, PER><<<blocks, 256, dyn, st>>>(x, T, H, w, bias, p, r.logits, r.sig, r.key, r.counter,
-                                                          idx, scores);
+    launch_small_t<8, PER>(x, T, H, w, bias, p, r, idx, scores, st, pdl);
   else
-    router_small_kernel<kRouterSmallT, PER><<<blocks, 256, dyn, st>>>(x, T, H, w, bias, p, r.logits, r.sig, r.key,
-                                                                      r.counter, idx, scores);
+    launch_small_t<kRouterSmallT, PER>(x, T, H, w, bias, p, r, idx, scores, st, pdl);
   return check_launch("router_small_kernel");
 }
 
@@ -438,11 +453,13 @@ extern "C" size_t glm53_router_workspace_bytes(int64_t T, int64_t E) {
   return 3 * align_up((size_t)std::max<int64_t>(T, 1) * (size_t)E * sizeof(float), 256) + 256;
 }
 
-extern "C" int glm53_router_topk(const void* x, int64_t T, int64_t H, const float* w, int64_t E,
-                                 const float* bias, int top_k, int n_group, int topk_group,
-                                 int norm_topk_prob, float routed_scaling_factor, uint32_t* indices,
-                                 float* scores, float* logits, void* workspace, size_t workspace_bytes,
-                                 void* stream) {
+namespace glm53 {
+
+// glm53_router_topk; with pdl the small-T kernel is launched as a
+// programmatic dependent of the previous kernel on the stream (which writes x).
+int router_topk(const void* x, int64_t T, int64_t H, const float* w, int64_t E, const float* bias, int top_k,
+                int n_group, int topk_group, int norm_topk_prob, float routed_scaling_factor, uint32_t* indices,
+                float* scores, float* logits, void* workspace, size_t workspace_bytes, cudaStream_t st, bool pdl) {
   if (T < 0 || H <= 0 || E <= 0 || E > kRouterMaxE || top_k <= 0 || top_k > kRouterMaxK || top_k > E) {
     set_last_error("glm53_router_topk: unsupported geometry T=%lld H=%lld E=%lld top_k=%d",
                    (long long)T, (long long)H, (long long)E, top_k);
@@ -458,7 +475,6 @@ extern "C" int glm53_router_topk(const void* x, int64_t T, int64_t H, const floa
     set_last_error("glm53_router_topk: missing pointer or workspace too small");
     return GLM53_ERR_INVALID;
   }
-  cudaStream_t st = (cudaStream_t)stream;
   char* ws = (char*)workspace;
   const size_t plane = align_up((size_t)T * E * sizeof(float), 256);
   float* lbuf = logits ? logits : (float*)ws;
@@ -467,9 +483,11 @@ extern "C" int glm53_router_topk(const void* x, int64_t T, int64_t H, const floa
   const bool vec = (H % 4 == 0) && (((uintptr_t)w & 15) == 0) && (((uintptr_t)x & 7) == 0);
   const int per = (int)((E + 31) / 32);
   if (T <= kRouterSmallT && vec) {
-    if (per <= 4) return launch_small<4>((const uint16_t*)x, (int)T, (int)H, w, bias, p, rs, indices, scores, st);
-    if (per <= 10) return launch_small<10>((const uint16_t*)x, (int)T, (int)H, w, bias, p, rs, indices, scores, st);
-    return launch_small<32>((const uint16_t*)x, (int)T, (int)H, w, bias, p, rs, indices, scores, st);
+    if (per <= 4)
+      return launch_small<4>((const uint16_t*)x, (int)T, (int)H, w, bias, p, rs, indices, scores, st, pdl);
+    if (per <= 10)
+      return launch_small<10>((const uint16_t*)x, (int)T, (int)H, w, bias, p, rs, indices, scores, st, pdl);
+    return launch_small<32>((const uint16_t*)x, (int)T, (int)H, w, bias, p, rs, indices, scores, st, pdl);
   }
   dim3 grid((unsigned)((T + 63) / 64), (unsigned)((E + 63) / 64));
   int rc;
@@ -484,4 +502,15 @@ extern "C" int glm53_router_topk(const void* x, int64_t T, int64_t H, const floa
   if (per <= 4) return launch_topk<4>(lbuf, (int)T, bias, p, indices, scores, st);
   if (per <= 10) return launch_topk<10>(lbuf, (int)T, bias, p, indices, scores, st);
   return launch_topk<32>(lbuf, (int)T, bias, p, indices, scores, st);
+}
+
+}  // namespace glm53
+
+extern "C" int glm53_router_topk(const void* x, int64_t T, int64_t H, const float* w, int64_t E,
+                                 const float* bias, int top_k, int n_group, int topk_group,
+                                 int norm_topk_prob, float routed_scaling_factor, uint32_t* indices,
+                                 float* scores, float* logits, void* workspace, size_t workspace_bytes,
+                                 void* stream) {
+  return router_topk(x, T, H, w, E, bias, top_k, n_group, topk_group, norm_topk_prob, routed_scaling_factor,
+                     indices, scores, logits, workspace, workspace_bytes, (cudaStream_t)stream, false);
 }

@@ -10,6 +10,7 @@ FP32 weighted reduce + BF16 shared add) with the reference's rounding points.
 
 from __future__ import annotations
 
+import ctypes
 import math
 import os
 
@@ -327,6 +328,8 @@ class CapturedDecode:
     static output (or copies it into ``out``, e.g. pinned host memory); the
     static output is overwritten by the next call.  Every operation stays
     stream-ordered, so host buffers may be pinned and the copies asynchronous.
+    With a host input (and a host ``out`` or none) the copy in, the replay and
+    the copy out are one library call (``glm53_graph_step``).
     """
 
     def __init__(self, module: nn.Module, hidden: int, device):
@@ -341,13 +344,114 @@ class CapturedDecode:
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph, stream=side):
             self.out = module(self.x)
+        if self.out.dtype != self.x.dtype or self.out.numel() != self.x.numel():
+            raise ValueError("CapturedDecode needs a module whose output has its input's shape and dtype")
+        self._exec = self.graph.raw_cuda_graph_exec()  # instantiated at the end of the capture
+        if not self._exec:
+            raise RuntimeError("CapturedDecode: the captured graph has no executable instance")
 
     def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        nbytes = self.x.numel() * self.x.element_size()
+        host_in = x.device.type == "cpu" and x.dtype == self.x.dtype and x.is_contiguous() and x.numel() == self.x.numel()
+        host_out = out is not None and out.device.type == "cpu" and out.dtype == self.out.dtype and \
+            out.is_contiguous() and out.numel() == self.out.numel()
+        if host_in and (out is None or host_out):
+            # host buffers: H2D copy, graph launch and D2H copy in one library call
+            N.check(N.lib().glm53_graph_step(self._exec, x.data_ptr(), self.x.data_ptr(), nbytes, self.out.data_ptr(),
+                                             out.data_ptr() if host_out else None, nbytes, N.stream(self.x.device)),
+                    "glm53_graph_step")
+            return self.out if out is None else out
         self.x.copy_(x.reshape(self.x.shape), non_blocking=True)
         self.graph.replay()
         if out is None:
             return self.out
         out.copy_(self.out.reshape(out.shape), non_blocking=True)
+        return out
+
+
+class PackedDecodeStep:
+    """One decode token through a PackedFP8MoE layer (its Float32Gate router
+    and the packed decode) as one library call per step, on static device
+    buffers (``glm53_decode_step_host``).
+
+    ``step(x, out=None)`` takes the ``hidden``-wide BF16 row on the host (a
+    pinned row is read by a kernel through its device mapping) or on the
+    device; the result goes into ``out`` (host or device; into a pinned host
+    ``out`` straight from the decode kernel) or, with ``out=None``, into the
+    static output that is returned and overwritten by the next call.  Every
+    operation is ordered on the current stream.  Same bits as the module call.
+    """
+
+    def __init__(self, module: PackedFP8MoE):
+        bank, gate = module.bank, module.gate
+        dev = bank.gate_up_weight.device
+        H, I, E = bank.hidden_size, bank.intermediate_size, bank.expert_count
+        shared = shared_fp8_tensors(module.shared_experts)
+        Is = shared[0].shape[0] if shared is not None else 0
+        lib = N.lib()
+        self.x = torch.zeros((1, 1, H), dtype=torch.bfloat16, device=dev)
+        self.out = torch.zeros((1, 1, H), dtype=torch.bfloat16, device=dev)
+        self._ids = torch.zeros(DECODE_TOP_K, dtype=torch.int32, device=dev)
+        self._scores = torch.zeros(DECODE_TOP_K, dtype=torch.float32, device=dev)
+        ws = module._workspace
+        rws = ws.get(dev, "step_router", lib.glm53_router_workspace_bytes(1, E))
+        dws = ws.get(dev, "step_decode", lib.glm53_packed_decode_workspace_bytes(DECODE_TOP_K, H, I, Is))
+        status = module.status
+        weights = (bank.gate_up_weight, bank.down_weight, *(() if shared is None else shared[0::2]))
+        router_w = gate.weight.contiguous()
+        router_b = gate.e_score_correction_bias.contiguous()
+        sh = shared if shared is not None else (None,) * 6
+        self._keep = (router_w, router_b, rws, dws, status, sh)
+        self._desc = N.DecodeStepDesc(
+            H=H, E=E, I=I, I_shared=Is, top_k=DECODE_TOP_K, n_group=gate.n_group, topk_group=gate.topk_group,
+            norm_topk_prob=int(gate.norm_topk_prob), routed_scaling_factor=gate.routed_scaling_factor,
+            limit=float(module.config.swiglu_limit), flags=N.decode_flags(*weights),
+            router_w=router_w.data_ptr(), router_bias=router_b.data_ptr(),
+            gate_up_w=bank.gate_up_weight.data_ptr(), gate_up_s=bank.gate_up_scale_inv.data_ptr(),
+            down_w=bank.down_weight.data_ptr(), down_s=bank.down_scale_inv.data_ptr(),
+            shared_gate_w=N.ptr(sh[0]), shared_gate_s=N.ptr(sh[1]), shared_up_w=N.ptr(sh[2]),
+            shared_up_s=N.ptr(sh[3]), shared_down_w=N.ptr(sh[4]), shared_down_s=N.ptr(sh[5]),
+            x=self.x.data_ptr(), expert_ids=self._ids.data_ptr(), scores=self._scores.data_ptr(),
+            out=self.out.data_ptr(), router_workspace=rws.data_ptr(), router_workspace_bytes=rws.numel(),
+            decode_workspace=dws.data_ptr(), decode_workspace_bytes=dws.numel(), status=status.data_ptr())
+        self._pdesc = ctypes.pointer(self._desc)
+
+    @staticmethod
+    def supported(module) -> bool:
+        from .router import Float32Gate
+
+        bank = module.bank
+        shared = shared_fp8_tensors(module.shared_experts)
+        limit = module.config.swiglu_limit
+        return (isinstance(module.gate, Float32Gate) and module.gate.top_k == DECODE_TOP_K and
+                float(limit) == int(limit) and bank.hidden_size % BLOCK_SIZE == 0 and
+                bank.intermediate_size % BLOCK_SIZE == 0 and
+                (module.shared_experts is None or (shared is not None and shared[0].shape[0] % BLOCK_SIZE == 0)))
+
+    def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        H = self.x.numel()
+        if x.numel() != H:
+            raise ValueError(f"decode step input has {x.numel()} values, layer width {H}")
+        if x.device.type == "cpu":
+            x = x.to(torch.bfloat16).contiguous()
+            x_host = x.data_ptr()
+        else:
+            self.x.copy_(x.reshape(self.x.shape))
+            x_host = None
+        out_host = None
+        if out is not None:
+            if out.numel() != H or out.dtype != torch.bfloat16 or not out.is_contiguous():
+                raise ValueError("decode step output must be a contiguous BF16 row of the layer width")
+            if out.device.type == "cpu":
+                out_host = out.data_ptr()
+        N.check(N.lib().glm53_decode_step_host(self._pdesc, x_host, out_host, N.stream(self.x.device)),
+                "glm53_decode_step_host")
+        if _SYNC_STATUS:
+            check_status(self._keep[4])
+        if out is None:
+            return self.out
+        if out_host is None:
+            out.copy_(self.out.reshape(out.shape))
         return out
 
 
@@ -372,8 +476,13 @@ class PackedFP8MoE(DirectFP8MoE):
     def status(self) -> torch.Tensor:
         return self._workspace.get(self.bank.gate_up_weight.device, "status", 4)
 
-    def capture_decode(self) -> CapturedDecode:
-        """This layer's one-token decode as a replayable CUDA graph."""
+    def capture_decode(self) -> PackedDecodeStep | CapturedDecode:
+        """This layer's one-token decode on static buffers, called once per
+        token: one library call (router + packed decode, host or device row)
+        when the layer has the Float32Gate router and the tensor-core shapes,
+        else a replayable CUDA graph of the module call."""
+        if PackedDecodeStep.supported(self):
+            return PackedDecodeStep(self)
         return CapturedDecode(self, self.bank.hidden_size, self.bank.gate_up_weight.device)
 
     def forward(self, x):

@@ -99,6 +99,17 @@ int glm53_fp8_linear_ws(const void* x, int64_t M, int64_t K, const uint8_t* w, i
                         const float* scale_inv, void* y, void* workspace, size_t workspace_bytes,
                         uint32_t* status, uint32_t flags, void* stream);
 
+/* One replay of a captured decode step with host buffers, as one call:
+ * copy x_bytes from x_host into the graph's static input x_dev, launch
+ * graph_exec (a cudaGraphExec_t, e.g. a captured router + packed decode), and
+ * copy out_bytes of its static output out_dev into out_host (skipped when
+ * out_host is NULL), all stream-ordered on `stream`.  Pinned host buffers
+ * keep the copies asynchronous.  Serves CapturedDecode's host-buffer step
+ * (the per-token PackedFP8MoE call, glm53_flash_mlx/packed.py:896-923, with
+ * the input and result on the host). */
+int glm53_graph_step(void* graph_exec, const void* x_host, void* x_dev, size_t x_bytes, const void* out_dev,
+                     void* out_host, size_t out_bytes, void* stream);
+
 /* Count (into *nan_count, device memory, accumulated) the 4-byte words of
  * w[n] that hold an E4M3 code 0x7F or 0xFF; zero means GLM53_FLAG_E4M3_FINITE
  * may be passed for these weights.  w must be 16-byte aligned.
@@ -195,6 +206,54 @@ int glm53_packed_decode_moe_static_scratch(const void* x, int64_t H, const uint3
                                            const float* shared_down_s, int64_t I_shared,
                                            float limit, void* out, uint32_t* status,
                                            uint32_t flags, void* stream);
+
+/* One token through one packed MoE layer (router + packed decode), with the
+ * input and the result in host memory: what PackedFP8MoE's per-token call
+ * (glm53_flash_mlx/packed.py:896-923, gate at patch.py:131-142) computes for
+ * a host row, as one library call.  `d` describes the layer and the caller's
+ * device buffers (all pointers device memory unless stated).  The call
+ *   1. copies H BF16 values from x_host into d->x: a kernel reads the host
+ *      row through its device mapping when x_host is pinned (page-locked by
+ *      the CUDA runtime), else cudaMemcpyAsync;
+ *   2. runs glm53_router_topk on d->x into d->expert_ids / d->scores (launched
+ *      as a programmatic dependent of the copy kernel, waiting for it);
+ *   3. runs glm53_packed_decode_moe with GLM53_FLAG_AFTER_ROUTER, writing the
+ *      result straight into out_host through its device mapping when out_host
+ *      is pinned, else into d->out followed by a copy to out_host (or only
+ *      into d->out when out_host is NULL).
+ * x_host NULL: d->x already holds the input (no copy; the router waits for
+ * nothing).  Results are those of the separate calls; every step is ordered
+ * on `stream`.  Requires top_k == 8 and H, I (and I_shared when non-zero)
+ * multiples of 128. */
+typedef struct glm53_decode_step_desc {
+  int64_t H, E, I, I_shared;
+  int top_k, n_group, topk_group, norm_topk_prob;
+  float routed_scaling_factor, limit;
+  uint32_t flags;               /* GLM53_FLAG_E4M3_FINITE or 0 */
+  const float* router_w;        /* [E, H] FP32 */
+  const float* router_bias;     /* [E] FP32 */
+  const uint8_t* gate_up_w;
+  const float* gate_up_s;
+  const uint8_t* down_w;
+  const float* down_s;
+  const uint8_t* shared_gate_w; /* shared expert, or NULL when I_shared == 0 */
+  const float* shared_gate_s;
+  const uint8_t* shared_up_w;
+  const float* shared_up_s;
+  const uint8_t* shared_down_w;
+  const float* shared_down_s;
+  void* x;                      /* [H] BF16: the step's input row */
+  uint32_t* expert_ids;         /* [top_k] */
+  float* scores;                /* [top_k] */
+  void* out;                    /* [H] BF16 */
+  void* router_workspace;
+  size_t router_workspace_bytes;
+  void* decode_workspace;
+  size_t decode_workspace_bytes;
+  uint32_t* status;
+} glm53_decode_step_desc;
+
+int glm53_decode_step_host(const glm53_decode_step_desc* d, const void* x_host, void* out_host, void* stream);
 
 /* Workspace bytes needed by glm53_routes_decode for R route slots. */
 size_t glm53_routes_decode_workspace_bytes(int64_t R, int64_t H, int64_t I);

@@ -65,3 +65,29 @@ def test_oracle_library_is_separate_from_product():
     for path in (ROOT / "glm53_flash_mlx_b200").rglob("*.py"):
         text = path.read_text()
         assert "import oracle" not in text and "from oracle" not in text, path
+
+
+def test_decode_step_descriptor_layout_matches_header(tmp_path):
+    """The ctypes mirror of glm53_decode_step_desc has the C struct's size and
+    field offsets (gcc compiles the header and prints offsetof for each)."""
+    import shutil
+    import subprocess
+
+    import pytest
+
+    from glm53_flash_mlx_b200 import _native as N
+
+    if shutil.which("gcc") is None:
+        pytest.skip("gcc not available")
+    fields = [f for f, _ in N.DecodeStepDesc._fields_]
+    src = tmp_path / "desc.c"
+    body = "".join(f'  printf("{f} %zu\\n", offsetof(glm53_decode_step_desc, {f}));\n' for f in fields)
+    src.write_text("#include <stddef.h>\n#include <stdio.h>\n#include \"glm53_b200.h\"\nint main(void) {\n"
+                   f'  printf("sizeof %zu\\n", sizeof(glm53_decode_step_desc));\n{body}  return 0;\n}}\n')
+    exe = tmp_path / "desc"
+    subprocess.run(["gcc", "-I", str(ROOT / "include"), str(src), "-o", str(exe)], check=True)
+    got = dict(line.split() for line in subprocess.run([str(exe)], check=True, capture_output=True,
+                                                        text=True).stdout.splitlines())
+    assert int(got["sizeof"]) == ctypes.sizeof(N.DecodeStepDesc)
+    for f in fields:
+        assert int(got[f]) == getattr(N.DecodeStepDesc, f).offset, f

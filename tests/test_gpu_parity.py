@@ -535,26 +535,78 @@ def test_exact_decode_handles_0x7f_as_480(G, oracle):
     assert torch.all(y.float() == 480.0 - 240.0)
 
 
-def test_captured_decode_matches_module_call(G, S):
-    """PackedFP8MoE.capture_decode() replays give the module's own bits."""
+@pytest.mark.parametrize("E,H,I,with_shared", [(16, 1024, 256, True), (64, 4096, 1536, True),
+                                                (16, 1024, 384, False)])
+def test_captured_decode_matches_module_call(G, S, E, H, I, with_shared):
+    """PackedFP8MoE.capture_decode() (one glm53_decode_step_host call per
+    token: input copy kernel, router, packed decode writing a pinned output
+    directly) gives the module's own bits for host and device rows."""
+    from glm53_flash_mlx_b200.packed import PackedDecodeStep
     from glm53_flash_mlx_b200.router import Float32Gate
 
-    E, H, I = 16, 1024, 256
     cfg = S.moe_config(H, I, E, 8, 10.0)
     bank = S.make_bank(E, H, I, seed=81, device="cuda")
-    shared = S.make_shared(H, I, seed=82, device="cuda")
+    shared = S.make_shared(H, I, seed=82, device="cuda") if with_shared else None
     gate = Float32Gate(cfg, device="cuda")
     w, b = S.make_router(E, H, seed=83, device="cuda")
     gate.weight.copy_(w)
     gate.e_score_correction_bias.copy_(b)
     mod = G.PackedFP8MoE(bank, cfg, gate, shared)
     cap = mod.capture_decode()
-    for t in range(3):
+    assert isinstance(cap, PackedDecodeStep)
+    y_pinned = torch.empty((1, 1, H), dtype=torch.bfloat16).pin_memory()
+    for t in range(4):
         x = S.random_bf16((1, 1, H), seed=84 + t, device="cuda")
         want = mod(x).clone()
-        got = cap(x.cpu().pin_memory()).clone()
+        got = cap(x.cpu().pin_memory()).clone()  # host in, device out
         torch.cuda.synchronize()
         assert torch.equal(got, want), t
+        cap(x.cpu().pin_memory(), out=y_pinned)  # host in and out, output written by the decode kernel
+        torch.cuda.synchronize()
+        assert torch.equal(y_pinned, want.cpu()), t
+        y_page = torch.empty((1, 1, H), dtype=torch.bfloat16)
+        cap(x.cpu(), out=y_page)  # pageable host buffers
+        torch.cuda.synchronize()
+        assert torch.equal(y_page, want.cpu()), t
+        assert torch.equal(cap(x).clone(), want), t  # device in
+        y_dev = torch.empty((1, 1, H), dtype=torch.bfloat16, device="cuda")
+        cap(x.cpu().pin_memory(), out=y_dev)  # host in, device out
+        assert torch.equal(y_dev, want), t
+    assert int(mod.status.view(torch.int32)[0].item()) == 0
+
+
+def test_captured_graph_decode_host_buffers(G, S):
+    """A layer whose gate is not the Float32Gate gets the CUDA-graph form of
+    capture_decode (glm53_graph_step: copy kernels over pinned buffers around
+    the replay, cudaMemcpyAsync for pageable ones); same bits as the module."""
+    from glm53_flash_mlx_b200.packed import CapturedDecode
+
+    E, H, I = 16, 1024, 256
+    cfg = S.moe_config(H, I, E, 8, 10.0)
+    bank = S.make_bank(E, H, I, seed=85, device="cuda")
+    shared = S.make_shared(H, I, seed=86, device="cuda")
+    routes = torch.tensor([[3, 9, 1, 14, 0, 7, 11, 5]], dtype=torch.int32, device="cuda")
+    scores = torch.tensor([[0.2, 0.17, 0.15, 0.13, 0.11, 0.1, 0.08, 0.06]], device="cuda")
+
+    class FixedGate(torch.nn.Module):
+        def forward(self, x):
+            shape = (*x.shape[:-1], 8)
+            return routes.expand(shape), scores.expand(shape)
+
+    mod = G.PackedFP8MoE(bank, cfg, FixedGate(), shared)
+    cap = mod.capture_decode()
+    assert isinstance(cap, CapturedDecode)
+    y_pinned = torch.empty((1, 1, H), dtype=torch.bfloat16).pin_memory()
+    for t in range(3):
+        x = S.random_bf16((1, 1, H), seed=87 + t, device="cuda")
+        want = mod(x).clone()
+        cap(x.cpu().pin_memory(), out=y_pinned)
+        torch.cuda.synchronize()
+        assert torch.equal(y_pinned, want.cpu()), t
+        y_page = torch.empty((1, 1, H), dtype=torch.bfloat16)
+        cap(x.cpu(), out=y_page)
+        torch.cuda.synchronize()
+        assert torch.equal(y_page, want.cpu()), t
 
 
 @pytest.mark.parametrize("M,N_,K", [(64, 576, 4096), (300, 1024, 1536), (2048, 4096, 4096)])
