@@ -291,9 +291,14 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(const uint16_t* __rest
 // as a BF16 MMA operand; every FP32 weight splits exactly into three BF16
 // numbers w = hi + mid + lo (8 + 8 + 8 significant bits).  For each 16-wide
 // K slice three m16n8k16 BF16 MMAs with a zero accumulator give the slice's
-// exact products summed in FP32, and their sum is added into FP64
-// accumulators: the slice-then-FP64 scheme of router_gemm_kernel on the
-// tensor cores.  Block tile 64 tokens x 64 experts, 4 warps of 32 x 32.
+// exact products summed in FP32, and their sum is added into a double-FP32
+// accumulator (sum s plus error term c, Knuth's TwoSum: s + c carries about
+// 48 significant bits, so the accumulation adds no error an FP64 one would
+// not) -- the slice-then-FP64 scheme of router_gemm_kernel on the tensor
+// cores without FP64 arithmetic, which is slow on this part.  Block tile 64 tokens x 64 experts, 4 warps of 32 x 32.
+// With `partial`, blockIdx.z takes K range [z k_len, (z+1) k_len) and
+// stores its FP64 sums to partial[z][t][e] (router_logits_reduce adds the
+// ranges in z order); otherwise one CTA covers all of K and stores FP32.
 constexpr int kRmBT = 64, kRmBE = 64, kRmBK = 32;
 
 __device__ __forceinline__ void mma_16816_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
@@ -317,20 +322,22 @@ __device__ __forceinline__ void split3_bf16x2(float a, float b, uint32_t& hi, ui
 
 __global__ void __launch_bounds__(128) router_mma_kernel(const uint16_t* __restrict__ x, int T, int H,
                                                          const float* __restrict__ w, int E,
-                                                         float* __restrict__ logits) {
+                                                         float* __restrict__ logits, int k_len,
+                                                         double* __restrict__ partial) {
   __shared__ __align__(16) uint16_t xs[kRmBT][kRmBK + 8];
   __shared__ __align__(16) float ws[kRmBE][kRmBK + 4];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
   const int t0 = blockIdx.x * kRmBT, e0 = blockIdx.y * kRmBE;
   const int wt = (warp >> 1) * 32, we = (warp & 1) * 32;
-  double acc[2][4][4];
+  float acc[2][4][4], err[2][4][4];
 #pragma unroll
   for (int m = 0; m < 2; ++m)
 #pragma unroll
     for (int n = 0; n < 4; ++n)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) acc[m][n][c] = 0.0;
-  for (int k0 = 0; k0 < H; k0 += kRmBK) {
+      for (int c = 0; c < 4; ++c) acc[m][n][c] = err[m][n][c] = 0.f;
+  const int k_begin = blockIdx.z * k_len, k_end = min(H, k_begin + k_len);
+  for (int k0 = k_begin; k0 < k_end; k0 += kRmBK) {
     for (int i = threadIdx.x; i < kRmBT * (kRmBK / 8); i += blockDim.x) {
       const int r = i / (kRmBK / 8), c = i - r * (kRmBK / 8);
       uint4 v = make_uint4(0, 0, 0, 0);
@@ -370,7 +377,14 @@ __global__ void __launch_bounds__(128) router_mma_kernel(const uint16_t* __restr
           mma_16816_bf16(dm, a[m], bm0, bm1);
           mma_16816_bf16(dl, a[m], bl0, bl1);
 #pragma unroll
-          for (int c = 0; c < 4; ++c) acc[m][n][c] += (double)(dh[c] + (dm[c] + dl[c]));
+          for (int c = 0; c < 4; ++c) {  // TwoSum(acc, v): acc + v = t + (error, added to err)
+            const float v = __fadd_rn(dh[c], __fadd_rn(dm[c], dl[c]));
+            const float t = __fadd_rn(acc[m][n][c], v);
+            const float bp = __fsub_rn(t, acc[m][n][c]);
+            const float e = __fadd_rn(__fsub_rn(acc[m][n][c], __fsub_rn(t, bp)), __fsub_rn(v, bp));
+            err[m][n][c] = __fadd_rn(err[m][n][c], e);
+            acc[m][n][c] = t;
+          }
         }
       }
     }
@@ -384,8 +398,32 @@ __global__ void __launch_bounds__(128) router_mma_kernel(const uint16_t* __restr
       for (int c = 0; c < 4; ++c) {
         const int t = t0 + wt + 16 * m + g + (c >= 2 ? 8 : 0);
         const int e = e0 + we + 8 * n + 2 * q + (c & 1);
-        if (t < T && e < E) logits[(size_t)t * E + e] = (float)acc[m][n][c];
+        if (t >= T || e >= E) continue;
+        const double v = (double)acc[m][n][c] + (double)err[m][n][c];
+        if (partial)
+          partial[((size_t)blockIdx.z * T + t) * E + e] = v;
+        else
+          logits[(size_t)t * E + e] = (float)v;
       }
+}
+
+// logits[t][e] = FP32 of the K ranges' FP64 sums added in range order.
+__global__ void __launch_bounds__(256) router_logits_reduce(const double* __restrict__ partial, int splits,
+                                                            int64_t n, float* __restrict__ logits) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    double v = partial[i];
+    for (int z = 1; z < splits; ++z) v += partial[(size_t)z * n + i];
+    logits[i] = (float)v;
+  }
+}
+
+// K ranges of the tensor-core router for T tokens and E experts: enough
+// CTAs (about 1280, over eight per SM) to hide the tile loads, at most 8.
+static int router_splits(int64_t T, int64_t E) {
+  const int64_t base = ((T + kRmBT - 1) / kRmBT) * ((E + kRmBE - 1) / kRmBE);
+  int s = 1;
+  while (s < 8 && base * s * 2 <= 1280) s *= 2;
+  return s;
 }
 
 template <int PER>
@@ -448,9 +486,12 @@ static int launch_small(const uint16_t* x, int T, int H, const float* w, const f
 
 using namespace glm53;
 
-// Workspace: logits | sigmoids | keys (T x E each) | completion counter.
+// Workspace: logits | sigmoids | keys (T x E each) | completion counter |
+// FP64 partial logits of the K ranges (tensor-core path, T > 32).
 extern "C" size_t glm53_router_workspace_bytes(int64_t T, int64_t E) {
-  return 3 * align_up((size_t)std::max<int64_t>(T, 1) * (size_t)E * sizeof(float), 256) + 256;
+  const size_t base = 3 * align_up((size_t)std::max<int64_t>(T, 1) * (size_t)E * sizeof(float), 256) + 256;
+  const int s = T > kRouterSmallT ? router_splits(T, E) : 1;
+  return base + (s > 1 ? align_up((size_t)s * (size_t)T * (size_t)E * sizeof(double), 256) : 0);
 }
 
 namespace glm53 {
@@ -492,8 +533,19 @@ int router_topk(const void* x, int64_t T, int64_t H, const float* w, int64_t E, 
   dim3 grid((unsigned)((T + 63) / 64), (unsigned)((E + 63) / 64));
   int rc;
   if (H % kRmBK == 0 && (((uintptr_t)x | (uintptr_t)w) & 15) == 0) {
-    router_mma_kernel<<<grid, 128, 0, st>>>((const uint16_t*)x, (int)T, (int)H, w, (int)E, lbuf);
+    int splits = router_splits(T, E);
+    while (splits > 1 && (H / kRmBK) % splits != 0) splits /= 2;
+    double* partial = splits > 1 ? (double*)(ws + 3 * plane + 256) : nullptr;
+    grid.z = (unsigned)splits;
+    router_mma_kernel<<<grid, 128, 0, st>>>((const uint16_t*)x, (int)T, (int)H, w, (int)E, lbuf,
+                                            (int)(H / splits), partial);
     rc = check_launch("router_mma_kernel");
+    if (!rc && partial) {
+      const int64_t n = T * E;
+      router_logits_reduce<<<(unsigned)std::min<int64_t>((n + 255) / 256, 1184), 256, 0, st>>>(partial, splits, n,
+                                                                                               lbuf);
+      rc = check_launch("router_logits_reduce");
+    }
   } else {
     router_gemm_kernel<<<grid, 256, 0, st>>>((const uint16_t*)x, (int)T, (int)H, w, (int)E, lbuf);
     rc = check_launch("router_gemm_kernel");
