@@ -63,8 +63,13 @@ namespace tc {
 constexpr int kM = 128;         // weight rows per tile (MMA M)
 constexpr int kN = 128;         // routes per tile (MMA N: 128, or 64 for short tiles)
 constexpr int kKB = 128;        // K per block-scale block
-constexpr int kRawStages = 7;   // weight ring (E4M3, 16 KB per stage): covers ~5,000-cycle HBM latency
-constexpr int kActStages = 3;   // activation ring (FP16, 32 KB per stage), mostly L2 hits
+// Ring depths: a clock64 trace of one CTA per role put the k-block period at
+// ~1,100 cycles with the MMA issuer waiting ~450 of them for activations; a
+// 4-deep activation ring with a 4-deep weight ring (whose copies then queue
+// less: ~3,100 cycles from issue to landing instead of ~6,500) measured 3%
+// faster than 7 + 3.
+constexpr int kRawStages = 4;   // weight ring (E4M3, 16 KB per stage)
+constexpr int kActStages = 4;   // activation ring (FP16, 32 KB per stage), mostly L2 hits
 constexpr int kRing = 4;        // decoded A operands in TMEM = k-block completion slots
 constexpr int kThreads = 480;   // 15 warps
 constexpr int kEpiWarps = 8;    // two per TMEM lane quarter, 64 routes each
