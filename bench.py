@@ -188,6 +188,11 @@ GATE_UP_BYTES = (TOP_K + 1) * 2 * I * H + TOP_K * 2 * (I // 128) * (H // 128) * 
     + H * 2 + (TOP_K * I + I) * 2 + TOP_K * 4
 DOWN_BYTES = (TOP_K + 1) * H * I + (TOP_K + 1) * (H // 128) * (I // 128) * 4 + (TOP_K * I + I) * 2 + H * 2 + TOP_K * 8
 STEP_BYTES = ROUTER_BYTES + GATE_UP_BYTES + DOWN_BYTES
+# DRAM bytes (read + write) of one gate/up launch in one ncu capture of the
+# decode (dram__bytes_read.sum 113,314,304 + dram__bytes_write.sum 3,461,888;
+# 64-expert bank of these shapes, 1.2 GB > L2, so every weight byte came from
+# DRAM): the same nine experts' bytes as any config-2 step.
+GATE_UP_TRAFFIC = 113_314_304 + 3_461_888
 
 
 def build_layers(n_layers: int, seed0: int, device, experts: int = E):
@@ -345,7 +350,8 @@ def bench_b200(args, world, rank, local):
     achieved = GATE_UP_BYTES / (k_ms / 1e3) / 1e9
     roofline = {"kernel": "decode_gate_up_v4", "bound": "hbm", "achieved": round(achieved, 1),
                 "peak": peaks["hbm_gbs"], "peak_source": peaks["source"], "unit": "GB/s",
-                "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
+                "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": GATE_UP_TRAFFIC,
+                "traffic_source": "ncu capture (dram__bytes_read.sum + dram__bytes_write.sum), 64-expert case",
                 "algorithmic_bytes_per_launch": GATE_UP_BYTES, "avg_launch_us": round(k_ms * 1e3, 2),
                 "launches_timed": reps * 64, "step_bytes": STEP_BYTES,
                 "step_frac": round(STEP_BYTES / (t_ms / args.steps / 1e3) / 1e9 / peaks["hbm_gbs"], 4)}
