@@ -271,12 +271,15 @@ def _nccl_rank(rank, world, port, result_dir, transport):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("transport", ["nccl", "p2p"])
-def test_expert_parallel_decode_two_gpus(tmp_path, transport):
+def test_expert_parallel_decode_gpus(tmp_path, transport, world):
+    """One process per GPU: every rank's tokens through expert-parallel decode
+    (3 consecutive steps) equal the one-GPU packed decode bit for bit."""
     import torch.multiprocessing as mp
 
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
-    mp.start_processes(_nccl_rank, args=(2, _free_port(), str(tmp_path), transport), nprocs=2,
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    mp.start_processes(_nccl_rank, args=(world, _free_port(), str(tmp_path), transport), nprocs=world,
                        start_method="spawn")
-    assert [(tmp_path / f"ok{r}").read_text() for r in range(2)] == ["1", "1"]
+    assert [(tmp_path / f"ok{r}").read_text() for r in range(world)] == ["1"] * world
