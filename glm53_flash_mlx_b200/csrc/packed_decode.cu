@@ -206,14 +206,23 @@ __global__ void __launch_bounds__(32 * W) decode_gate_up_v4(DecodeArgs a) {
   }
   const bool active = unit < nunits;
   const int jb = unit0 < routed_units ? unit0 / (a.I >> 3) : a.top_k + (unit0 - routed_units) / (a.Is >> 3);
-  if (a.after_router && jb < a.top_k) pdl_wait();  // the expert ids come from the router
+  const uint16_t* xb = jb < a.top_k ? a.x + (size_t)jb * a.x_stride
+                                    : (a.shared_x ? a.shared_x + (size_t)(jb - a.top_k) * a.H : a.x);
+  const bool wait_router = a.after_router && jb < a.top_k;  // CTA-uniform
+  float xmul = 0.f;
+  if (wait_router) {
+    // the activation row does not depend on routing: stage it while the router runs
+    xmul = stage_f16(xs, a.H + 8, xb, 0, 1, a.H, scratch);
+    pdl_wait();  // the router's results
+  }
   if (a.arrivals && jb < a.top_k) {  // peer-memory dispatch: wait for every rank's slots
     if (threadIdx.x == 0) wait_counter_geq(a.arrivals, (*a.epoch + 1ull) * a.arrivals_per_step, a.status);
     __syncthreads();
   }
-  // the down stage may launch now: its prologue only streams weights (and,
-  // after the router, reads expert ids that every routed CTA has seen final)
-  pdl_trigger();
+  // the down stage may launch now: its prologue only streams weights.  After
+  // the router, the routed CTAs let it launch once their own weight streams
+  // are issued (measured 1.1 us faster per step than at once).
+  if (!wait_router) pdl_trigger();
   if (a.route_out && jb < a.top_k && a.ids[jb] == kEmptySlot) return;
   GateUpRows rw{};
   if (active) rw = gate_up_rows(a, unit);
@@ -231,12 +240,12 @@ __global__ void __launch_bounds__(32 * W) decode_gate_up_v4(DecodeArgs a) {
     if (s < nslice) issue(s);
     cp_async_commit_group();
   }
+  if (wait_router) pdl_trigger();  // the down prologue reads expert ids this CTA has seen final
   WarpScales ssg, ssu;
   ssg.load(rw.sg, a.H >> 7, ld);
   ssu.load(rw.su, a.H >> 7, ld);
-  const uint16_t* xb = jb < a.top_k ? a.x + (size_t)jb * a.x_stride
-                                    : (a.shared_x ? a.shared_x + (size_t)(jb - a.top_k) * a.H : a.x);
-  const float smul = decode_unscale<FINITE>() * stage_f16(xs, a.H + 8, xb, 0, 1, a.H, scratch);
+  const float smul =
+      decode_unscale<FINITE>() * (wait_router ? xmul : stage_f16(xs, a.H + 8, xb, 0, 1, a.H, scratch));
   float part[4] = {0.f, 0.f, 0.f, 0.f}, tot[4] = {0.f, 0.f, 0.f, 0.f};
   for (int sl = 0; sl < nslice; ++sl) {
     if (sl + P - 1 < nslice) issue(sl + P - 1);
