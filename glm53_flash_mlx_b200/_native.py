@@ -70,6 +70,12 @@ SIGNATURES: dict[str, tuple] = {
     ),
     "glm53_direct_combine": (_int, [_vp, _vp, _vp, _i64, _int, _i64, _vp, _vp, _vp]),
     "glm53_batched_decode_workspace_bytes": (_sz, [_i64, _int, _i64, _i64, _i64]),
+    "glm53_batched_decode_shared_workspace_bytes": (_sz, [_i64, _int, _i64, _i64, _i64]),
+    "glm53_batched_decode_moe_shared": (
+        _int,
+        [_vp, _i64, _i64, _vp, _vp, _int, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _f, _vp, _vp,
+         _sz, _vp, _u32, _vp],
+    ),
     "glm53_batched_decode_moe": (
         _int,
         [_vp, _i64, _i64, _vp, _vp, _int, _vp, _vp, _vp, _vp, _i64, _i64, _f, _vp, _vp, _vp, _sz, _vp, _u32, _vp],

@@ -44,6 +44,13 @@ struct BatchedArgs {
   const float* gu_s;
   const uint8_t* d_w;
   const float* d_s;
+  // shared expert as expert id E (routes of weight 1.0), or null
+  const uint8_t* sg_w;
+  const float* sg_s;
+  const uint8_t* su_w;
+  const float* su_s;
+  const uint8_t* sd_w;
+  const float* sd_s;
   float limit;
   uint16_t* hidden;  // [R, I] sorted route order
   uint16_t* rows;    // [R, H] sorted route order
@@ -120,13 +127,14 @@ __global__ void __launch_bounds__(32 * kBdWarps) batched_gate_up_kernel(BatchedA
     const int d = w / groups, grp = w - d * groups;
     const uint32_t e = __ldg(a.tile_experts + d), start = __ldg(a.tile_starts + d);
     const int len = (int)min(__ldg(a.tile_lengths + d), (uint32_t)kBdCols);
-    const bool valid = e < (uint32_t)a.E;
-    const uint32_t es = valid ? e : 0u;
+    const bool shared = a.sg_w && e == (uint32_t)a.E;
+    const bool valid = e < (uint32_t)a.E || shared;
+    const uint32_t es = e < (uint32_t)a.E ? e : 0u;
     const int r0 = grp * 8 * kBdWarps + warp * 8;
-    const uint8_t* gw = a.gu_w + ((size_t)es * 2 * a.I + r0) * a.H;
-    const uint8_t* uw = gw + (size_t)a.I * a.H;
-    const float* gs = a.gu_s + ((size_t)es * 2 * half + (r0 >> 7)) * cols;
-    const float* us = gs + (size_t)half * cols;
+    const uint8_t* gw = shared ? a.sg_w + (size_t)r0 * a.H : a.gu_w + ((size_t)es * 2 * a.I + r0) * a.H;
+    const uint8_t* uw = shared ? a.su_w + (size_t)r0 * a.H : gw + (size_t)a.I * a.H;
+    const float* gs = shared ? a.sg_s + (size_t)(r0 >> 7) * cols : a.gu_s + ((size_t)es * 2 * half + (r0 >> 7)) * cols;
+    const float* us = shared ? a.su_s + (size_t)(r0 >> 7) * cols : gs + (size_t)half * cols;
     const uint8_t* pg = gw + (size_t)g * a.H + 16 * q;
     const uint8_t* pu = uw + (size_t)g * a.H + 16 * q;
     auto issue = [&](int sl) {
@@ -187,11 +195,13 @@ __global__ void __launch_bounds__(32 * kBdWarps) batched_down_kernel(BatchedArgs
     const int d = w / groups, grp = w - d * groups;
     const uint32_t e = __ldg(a.tile_experts + d), start = __ldg(a.tile_starts + d);
     const int len = (int)min(__ldg(a.tile_lengths + d), (uint32_t)kBdCols);
-    const bool valid = e < (uint32_t)a.E;
-    const uint32_t es = valid ? e : 0u;
+    const bool shared = a.sd_w && e == (uint32_t)a.E;
+    const bool valid = e < (uint32_t)a.E || shared;
+    const uint32_t es = e < (uint32_t)a.E ? e : 0u;
     const int row0 = grp * 16 * kBdWarps + warp * 16;
-    const uint8_t* w0 = a.d_w + ((size_t)es * a.H + row0) * K;
-    const float* srow = a.d_s + ((size_t)es * (a.H >> 7) + (row0 >> 7)) * cols;
+    const uint8_t* w0 = shared ? a.sd_w + (size_t)row0 * K : a.d_w + ((size_t)es * a.H + row0) * K;
+    const float* srow = shared ? a.sd_s + (size_t)(row0 >> 7) * cols
+                               : a.d_s + ((size_t)es * (a.H >> 7) + (row0 >> 7)) * cols;
     const uint8_t* p0 = w0 + (size_t)g * K + 16 * q;
     const uint8_t* p8 = p0 + (size_t)8 * K;
     auto issue = [&](int sl) {
@@ -287,6 +297,24 @@ static int launch_batched(const BatchedArgs& a, int64_t capacity, cudaStream_t s
   return check_launch("batched_down_kernel");
 }
 
+// Every token's routes plus one route to the shared expert (id E, weight
+// 1.0, last in the token's slots); ids >= E become 0xFFFFFFFF (still bad).
+__global__ void extend_routes_kernel(const uint32_t* __restrict__ ids, const float* __restrict__ scores, int64_t T,
+                                     int top_k, uint32_t E, uint32_t* __restrict__ ids2, float* __restrict__ scores2) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= T * (top_k + 1)) return;
+  const int64_t t = i / (top_k + 1);
+  const int j = (int)(i - t * (top_k + 1));
+  if (j == top_k) {
+    ids2[i] = E;
+    scores2[i] = 1.0f;
+  } else {
+    const uint32_t e = ids[t * top_k + j];
+    ids2[i] = e < E ? e : 0xFFFFFFFFu;
+    scores2[i] = scores[t * top_k + j];
+  }
+}
+
 // Combine through the sorted-order rows (direct_combine.cu).
 int direct_combine_rows(const uint16_t* rows, const uint32_t* row_of_slot, const uint32_t* expert_ids,
                         const float* scores, int64_t T, int top_k, int64_t H, int64_t E, const uint16_t* shared,
@@ -300,17 +328,35 @@ extern "C" size_t glm53_batched_decode_workspace_bytes(int64_t T, int top_k, int
   return batched_workspace(T * top_k, E, H, I).bytes;
 }
 
-extern "C" int glm53_batched_decode_moe(const void* x, int64_t T, int64_t H, const uint32_t* expert_ids,
-                                        const float* scores, int top_k, const uint8_t* gate_up_w,
-                                        const float* gate_up_s, const uint8_t* down_w, const float* down_s,
-                                        int64_t E, int64_t I, float limit, const void* shared, void* out,
-                                        void* workspace, size_t workspace_bytes, uint32_t* status, uint32_t flags,
-                                        void* stream) {
+// The plan of T * (top_k + 1) routes over E + 1 experts, then the extended
+// ids and scores.
+extern "C" size_t glm53_batched_decode_shared_workspace_bytes(int64_t T, int top_k, int64_t E, int64_t H, int64_t I) {
+  const int64_t R = T * (top_k + 1);
+  return batched_workspace(R, E + 1, H, I).bytes + 2 * align_up((size_t)R * 4, 256);
+}
+
+// Shared expert weights of glm53_batched_decode_moe_shared (all null: none).
+struct SharedWeights {
+  const uint8_t* g_w;
+  const float* g_s;
+  const uint8_t* u_w;
+  const float* u_s;
+  const uint8_t* d_w;
+  const float* d_s;
+};
+
+// top_k / E here count the shared-expert route and expert when sw.g_w is set
+// (the caller extended the routes).
+static int batched_decode(const char* fn, const void* x, int64_t T, int64_t H, const uint32_t* expert_ids,
+                          const float* scores, int top_k, const uint8_t* gate_up_w, const float* gate_up_s,
+                          const uint8_t* down_w, const float* down_s, int64_t E, int64_t I, float limit,
+                          const void* shared, const SharedWeights& sw, void* out, void* workspace,
+                          size_t workspace_bytes, uint32_t* status, uint32_t flags, cudaStream_t st) {
   const int64_t R = T * top_k;
   if (T < 0 || top_k <= 0 || top_k > 32 || H <= 0 || I <= 0 || E <= 0 || H % 128 != 0 || I % 128 != 0 ||
       H > 32768 || I > 32768 || R > kBdMaxRoutes) {
-    set_last_error("glm53_batched_decode_moe: unsupported geometry T=%lld top_k=%d H=%lld I=%lld", (long long)T,
-                   top_k, (long long)H, (long long)I);
+    set_last_error("%s: unsupported geometry T=%lld top_k=%d H=%lld I=%lld", fn, (long long)T, top_k, (long long)H,
+                   (long long)I);
     return GLM53_ERR_INVALID;
   }
   if (T == 0) return GLM53_OK;
@@ -318,10 +364,9 @@ extern "C" int glm53_batched_decode_moe(const void* x, int64_t T, int64_t H, con
   if (!x || !expert_ids || !scores || !gate_up_w || !gate_up_s || !down_w || !down_s || !out || !workspace ||
       !status || workspace_bytes < wl.bytes ||
       (((uintptr_t)x | (uintptr_t)gate_up_w | (uintptr_t)down_w | (uintptr_t)out | (uintptr_t)shared) & 15) != 0) {
-    set_last_error("glm53_batched_decode_moe: missing pointer, misaligned tensor or workspace too small");
+    set_last_error("%s: missing pointer, misaligned tensor or workspace too small", fn);
     return GLM53_ERR_INVALID;
   }
-  cudaStream_t st = (cudaStream_t)stream;
   char* ws = (char*)workspace;
   BatchedArgs a{};
   a.x = (const uint16_t*)x;
@@ -338,6 +383,13 @@ extern "C" int glm53_batched_decode_moe(const void* x, int64_t T, int64_t H, con
   a.gu_s = gate_up_s;
   a.d_w = down_w;
   a.d_s = down_s;
+  a.sg_w = sw.g_w;
+  a.sg_s = sw.g_s;
+  a.su_w = sw.u_w;
+  a.su_s = sw.u_s;
+  a.sd_w = sw.d_w;
+  a.sd_s = sw.d_s;
+  if (sw.g_w) a.E = (int)(E - 1);  // the shared expert is id E - 1 of the extended routes
   a.limit = limit;
   a.hidden = (uint16_t*)(ws + wl.hidden);
   a.rows = (uint16_t*)(ws + wl.rows);
@@ -354,4 +406,47 @@ extern "C" int glm53_batched_decode_moe(const void* x, int64_t T, int64_t H, con
   if (rc) return rc;
   return direct_combine_rows(a.rows, (const uint32_t*)(ws + wl.inverse), expert_ids, scores, T, top_k, H, E,
                              (const uint16_t*)shared, (uint16_t*)out, status, st);
+}
+
+extern "C" int glm53_batched_decode_moe(const void* x, int64_t T, int64_t H, const uint32_t* expert_ids,
+                                        const float* scores, int top_k, const uint8_t* gate_up_w,
+                                        const float* gate_up_s, const uint8_t* down_w, const float* down_s,
+                                        int64_t E, int64_t I, float limit, const void* shared, void* out,
+                                        void* workspace, size_t workspace_bytes, uint32_t* status, uint32_t flags,
+                                        void* stream) {
+  return batched_decode("glm53_batched_decode_moe", x, T, H, expert_ids, scores, top_k, gate_up_w, gate_up_s, down_w,
+                        down_s, E, I, limit, shared, SharedWeights{}, out, workspace, workspace_bytes, status, flags,
+                        (cudaStream_t)stream);
+}
+
+extern "C" int glm53_batched_decode_moe_shared(const void* x, int64_t T, int64_t H, const uint32_t* expert_ids,
+                                               const float* scores, int top_k, const uint8_t* gate_up_w,
+                                               const float* gate_up_s, const uint8_t* down_w, const float* down_s,
+                                               int64_t E, int64_t I, const uint8_t* shared_gate_w,
+                                               const float* shared_gate_s, const uint8_t* shared_up_w,
+                                               const float* shared_up_s, const uint8_t* shared_down_w,
+                                               const float* shared_down_s, float limit, void* out, void* workspace,
+                                               size_t workspace_bytes, uint32_t* status, uint32_t flags,
+                                               void* stream) {
+  const char* fn = "glm53_batched_decode_moe_shared";
+  if (T < 0 || top_k <= 0 || top_k >= 32 || E <= 0 || E >= 0x7FFFFFFF || !expert_ids || !scores || !workspace ||
+      !shared_gate_w || !shared_gate_s || !shared_up_w || !shared_up_s || !shared_down_w || !shared_down_s ||
+      (((uintptr_t)shared_gate_w | (uintptr_t)shared_up_w | (uintptr_t)shared_down_w) & 15) != 0 ||
+      workspace_bytes < glm53_batched_decode_shared_workspace_bytes(T, top_k, E, H, I)) {
+    set_last_error("%s: invalid arguments or workspace too small", fn);
+    return GLM53_ERR_INVALID;
+  }
+  if (T == 0) return GLM53_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t R = T * (top_k + 1);
+  const size_t plan = batched_workspace(R, E + 1, H, I).bytes;
+  uint32_t* ids2 = (uint32_t*)((char*)workspace + plan);
+  float* scores2 = (float*)((char*)workspace + plan + align_up((size_t)R * 4, 256));
+  extend_routes_kernel<<<(unsigned)((R + 255) / 256), 256, 0, st>>>(expert_ids, scores, T, top_k, (uint32_t)E, ids2,
+                                                                   scores2);
+  int rc = check_launch("extend_routes_kernel");
+  if (rc) return rc;
+  const SharedWeights sw{shared_gate_w, shared_gate_s, shared_up_w, shared_up_s, shared_down_w, shared_down_s};
+  return batched_decode(fn, x, T, H, ids2, scores2, top_k + 1, gate_up_w, gate_up_s, down_w, down_s, E + 1, I, limit,
+                        nullptr, sw, out, workspace, plan, status, flags, st);
 }

@@ -275,7 +275,10 @@ def batched_decode_moe(x: torch.Tensor, indices: torch.Tensor, scores: torch.Ten
     semantics (glm53_flash_mlx/fp8.py:384-399): each touched expert streams its
     weights once for all its routes, the weighted rows are added in BF16 in
     ascending expert id (``glm53_batched_decode_moe``), plus the shared expert
-    module's output.  x: BF16 [T, H]; indices / scores: [T, top_k]."""
+    module's output.  A block-FP8 shared expert of the routed experts' width
+    rides in the same kernels as one more route per token of weight 1.0
+    (``glm53_batched_decode_moe_shared``).  x: BF16 [T, H]; indices / scores:
+    [T, top_k]."""
     dev = N.require_cuda(x, indices, scores, bank.gate_up_weight)
     T, H = x.shape
     if H != bank.hidden_size:
@@ -286,11 +289,28 @@ def batched_decode_moe(x: torch.Tensor, indices: torch.Tensor, scores: torch.Ten
     ids = indices.reshape(-1).to(torch.int32).contiguous()
     sc = scores.reshape(-1).to(torch.float32).contiguous()
     wsp = workspace or N.Workspace()
-    ws = wsp.get(dev, "batched", N.lib().glm53_batched_decode_workspace_bytes(T, top_k, E, H, I))
     if status is None:
         status = wsp.get(dev, "status", 4)
-    shared = shared_experts(x).contiguous() if shared_experts is not None else None
     out = torch.empty_like(x)
+    sw = shared_fp8_tensors(shared_experts)
+    flags = N.decode_flags(bank.gate_up_weight, bank.down_weight, *(() if sw is None else sw[0::2]))
+    if sw is not None and sw[0].shape == (I, H) and sw[4].shape == (H, I) and top_k < 32:
+        # the shared expert rides in the coalesced kernels as one more route per token
+        ws = wsp.get(dev, "batched_shared", N.lib().glm53_batched_decode_shared_workspace_bytes(T, top_k, E, H, I))
+        N.check(
+            N.lib().glm53_batched_decode_moe_shared(
+                x.data_ptr(), T, H, ids.data_ptr(), sc.data_ptr(), top_k, bank.gate_up_weight.data_ptr(),
+                bank.gate_up_scale_inv.data_ptr(), bank.down_weight.data_ptr(), bank.down_scale_inv.data_ptr(), E, I,
+                *(t.data_ptr() for t in sw), float(limit), out.data_ptr(), ws.data_ptr(), ws.numel(),
+                status.data_ptr(), flags, N.stream(dev),
+            ),
+            "glm53_batched_decode_moe_shared",
+        )
+        if _SYNC_STATUS:
+            check_status(status)
+        return out
+    ws = wsp.get(dev, "batched", N.lib().glm53_batched_decode_workspace_bytes(T, top_k, E, H, I))
+    shared = shared_experts(x).contiguous() if shared_experts is not None else None
     N.check(
         N.lib().glm53_batched_decode_moe(
             x.data_ptr(), T, H, ids.data_ptr(), sc.data_ptr(), top_k, bank.gate_up_weight.data_ptr(),

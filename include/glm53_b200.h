@@ -304,6 +304,28 @@ int glm53_batched_decode_moe(const void* x, int64_t T, int64_t H, const uint32_t
                              void* workspace, size_t workspace_bytes, uint32_t* status,
                              uint32_t flags, void* stream);
 
+/* Workspace bytes of glm53_batched_decode_moe_shared. */
+size_t glm53_batched_decode_shared_workspace_bytes(int64_t T, int top_k, int64_t E, int64_t H, int64_t I);
+
+/* glm53_batched_decode_moe with the shared expert computed in the same
+ * coalesced kernels instead of passed in as BF16 rows: every token gets one
+ * more route, to the shared expert (gate [I, H], up [I, H], down [H, I] E4M3
+ * with their 128x128 block scales; its intermediate size equals the routed
+ * experts' I) with weight 1.0.  Its weighted BF16 row is the shared expert's
+ * BF16 output exactly, and the ascending-id combine adds it last, after the
+ * routed experts, as DirectFP8MoE.__call__ adds the shared output
+ * (glm53_flash_mlx/fp8.py:384-397).  The shared expert's weights stream once
+ * per 4 tokens (L2 hits after the first).  Same limits as
+ * glm53_batched_decode_moe with top_k < 32. */
+int glm53_batched_decode_moe_shared(const void* x, int64_t T, int64_t H, const uint32_t* expert_ids,
+                                    const float* scores, int top_k, const uint8_t* gate_up_w,
+                                    const float* gate_up_s, const uint8_t* down_w, const float* down_s,
+                                    int64_t E, int64_t I, const uint8_t* shared_gate_w,
+                                    const float* shared_gate_s, const uint8_t* shared_up_w,
+                                    const float* shared_up_s, const uint8_t* shared_down_w,
+                                    const float* shared_down_s, float limit, void* out, void* workspace,
+                                    size_t workspace_bytes, uint32_t* status, uint32_t flags, void* stream);
+
 /* Expert-parallel dispatch packing on the tokens' home rank.  Experts are
  * split into `world` contiguous ranges of E / world; route (t, j) with expert
  * e goes to rank d = e / (E / world), into the next free of `capacity` slots
