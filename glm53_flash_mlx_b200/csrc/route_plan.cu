@@ -34,10 +34,17 @@ __global__ void __launch_bounds__(kPlanThreads) route_plan_kernel(
   for (int i = tid; i < B; i += kPlanThreads) cursor[i] = 0;
   for (int i = tid; i < kPlanWarps * B; i += kPlanThreads) wcount[i] = 0;
   __syncthreads();
-  // 1. histogram
-  for (int r = tid; r < R; r += kPlanThreads) {
-    uint32_t e = ids[r];
-    atomicAdd(&cursor[e < (uint32_t)E ? e : (uint32_t)E], 1u);
+  // 1. histogram (eight loads in flight per thread: the ids come from L2/HBM)
+  for (int r0 = tid; r0 < R; r0 += 8 * kPlanThreads) {
+    uint32_t ev[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int r = r0 + u * kPlanThreads;
+      ev[u] = r < R ? __ldg(ids + r) : 0xffffffffu;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (r0 + u * kPlanThreads < R) atomicAdd(&cursor[ev[u] < (uint32_t)E ? ev[u] : (uint32_t)E], 1u);
   }
   __syncthreads();
   // 2. exclusive prefix of route counts and tile counts (warp 0)
@@ -74,15 +81,21 @@ __global__ void __launch_bounds__(kPlanThreads) route_plan_kernel(
     cursor[i] = roff[i];
   }
   __syncthreads();
-  // 3. stable scatter, 1024 routes per step
+  // 3. stable scatter, 1024 routes per step (the next step's id and score
+  // are loaded while this one is placed)
+  uint32_t next_e = tid < R ? __ldg(ids + tid) : 0u;
+  float next_s = (tid < R && scores && sorted_scores) ? __ldg(scores + tid) : 0.f;
   for (int base = 0; base < R; base += kPlanThreads) {
     const int r = base + tid;
     const bool live = r < R;
-    uint32_t key = 0xffffffffu;
-    if (live) {
-      uint32_t e = ids[r];
-      key = e < (uint32_t)E ? e : (uint32_t)E;
+    const uint32_t e_r = next_e;
+    const float s_r = next_s;
+    if (r + kPlanThreads < R) {
+      next_e = __ldg(ids + r + kPlanThreads);
+      if (scores && sorted_scores) next_s = __ldg(scores + r + kPlanThreads);
     }
+    uint32_t key = 0xffffffffu;
+    if (live) key = e_r < (uint32_t)E ? e_r : (uint32_t)E;
     const uint32_t peers = __match_any_sync(0xffffffffu, key);
     const uint32_t rank = __popc(peers & ((1u << lane) - 1u));
     if (live && rank == 0) wcount[warp * B + key] = __popc(peers);
@@ -93,8 +106,8 @@ __global__ void __launch_bounds__(kPlanThreads) route_plan_kernel(
       const uint32_t pos = cursor[key] + before + rank;
       order[pos] = (uint32_t)r;
       inverse[r] = pos;
-      sorted_experts[pos] = ids[r];
-      if (scores && sorted_scores) sorted_scores[pos] = scores[r];
+      sorted_experts[pos] = e_r;
+      if (scores && sorted_scores) sorted_scores[pos] = s_r;
     }
     __syncthreads();
     for (int k = tid; k < B; k += kPlanThreads) {
