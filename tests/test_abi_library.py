@@ -91,3 +91,25 @@ def test_decode_step_descriptor_layout_matches_header(tmp_path):
     assert int(got["sizeof"]) == ctypes.sizeof(N.DecodeStepDesc)
     for f in fields:
         assert int(got[f]) == getattr(N.DecodeStepDesc, f).offset, f
+
+
+def test_new_entry_points_fail_closed_before_touching_cuda():
+    """Argument checks of the step, graph-step and batched shared-expert entry
+    points reject bad calls with GLM53_ERR_INVALID and a message, before any
+    CUDA call (so this runs without a GPU)."""
+    from glm53_flash_mlx_b200 import _native as N
+
+    lib = N.load_library()
+    assert lib.glm53_graph_step(None, None, None, 0, None, None, 0, None) == N.GLM53_ERR_INVALID
+    assert b"glm53_graph_step" in lib.glm53_last_error()
+    assert lib.glm53_decode_step_host(None, None, None, None) == N.GLM53_ERR_INVALID
+    bad = N.DecodeStepDesc(H=4096, E=288, I=1536, top_k=7)  # no buffers, top_k != 8
+    assert lib.glm53_decode_step_host(ctypes.pointer(bad), None, None, None) == N.GLM53_ERR_INVALID
+    assert b"glm53_decode_step_host" in lib.glm53_last_error()
+    # batched shared-expert entry: missing shared weights / workspace
+    assert lib.glm53_batched_decode_moe_shared(None, 2, 4096, None, None, 8, None, None, None, None, 288, 1536,
+                                               None, None, None, None, None, None, 10.0, None, None, 0, None, 0,
+                                               None) == N.GLM53_ERR_INVALID
+    assert b"glm53_batched_decode_moe_shared" in lib.glm53_last_error()
+    need = lib.glm53_batched_decode_shared_workspace_bytes(16, 8, 288, 4096, 1536)
+    assert need > lib.glm53_batched_decode_workspace_bytes(16, 8, 288, 4096, 1536)
