@@ -45,6 +45,11 @@ __global__ void p2p_dispatch_kernel(const uint16_t* __restrict__ x, int H, int t
                                     EpLayout lay, float* __restrict__ slot_scores, uint32_t* __restrict__ route_pos,
                                     uint32_t* __restrict__ status) {
   __shared__ uint32_t s_route;
+  // launched as a programmatic dependent of the router: the owner decode may
+  // launch at once (its routed CTAs wait for the arrivals, its shared-expert
+  // CTAs for this grid), and the routes are read after the router finished
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int k = blockIdx.x, d = k / cap, s = k - d * cap;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int per_rank = E / world;
@@ -113,6 +118,9 @@ __global__ void p2p_combine_kernel(const char* __restrict__ buf, EpLayout lay, c
                                    const uint16_t* __restrict__ shared, uint16_t* __restrict__ out,
                                    unsigned long long cta_per_row, uint32_t* status) {
   __shared__ unsigned long long s_step;
+  // launched as a programmatic dependent of the owner's down stage: the home
+  // tokens' shared rows come from that grid
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   if (threadIdx.x == 0) {
     unsigned long long sent = 0;
     for (int64_t r = 0; r < T * top_k; ++r) sent += route_pos[r] != kP2pEmpty ? 1ull : 0ull;
@@ -169,6 +177,23 @@ __global__ void p2p_combine_kernel(const char* __restrict__ buf, EpLayout lay, c
       __threadfence();
     }
   }
+}
+
+// 256-thread launch with programmatic stream serialisation: the kernel may
+// start before the previous kernel on the stream has finished and orders
+// itself with griddepcontrol.wait.
+template <typename... KArgs, typename... Args>
+static void launch_pdl(void (*kernel)(KArgs...), dim3 grid, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(256);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
 static bool p2p_geometry(int world, int rank, int64_t cap, int64_t H) {
@@ -254,9 +279,9 @@ extern "C" int glm53_ep_dispatch_p2p(const void* x, int64_t T, int64_t H, const 
   (void)slot_route;
   cudaStream_t st = (cudaStream_t)stream;
   const EpLayout lay = ep_layout(world, (int)capacity, H);
-  p2p_dispatch_kernel<<<(unsigned)(world * capacity), 256, 0, st>>>(
-      (const uint16_t*)x, (int)H, top_k, expert_ids, scores, (int)(T * top_k), (int)E, world, rank, (int)capacity,
-      peer_base, lay, slot_scores, route_pos, status);
+  launch_pdl(p2p_dispatch_kernel, dim3((unsigned)(world * capacity)), st, (const uint16_t*)x, (int)H, top_k,
+             expert_ids, scores, (int)(T * top_k), (int)E, world, rank, (int)capacity, peer_base, lay, slot_scores,
+             route_pos, status);
   return check_launch("p2p_dispatch_kernel");
 }
 
@@ -275,7 +300,7 @@ extern "C" int glm53_ep_combine_p2p(void* buffer, const uint32_t* route_pos, con
   const unsigned long long cta_per_row = (unsigned long long)(H / 64);
   const int64_t n = std::max<int64_t>(T * (H / 8), 1);
   const int blocks = (int)std::min<int64_t>((n + 255) / 256, 1024);
-  p2p_combine_kernel<<<blocks, 256, 0, st>>>((const char*)buffer, lay, slot_scores, route_pos, T, top_k, H,
-                                             (const uint16_t*)shared, (uint16_t*)out, cta_per_row, status);
+  launch_pdl(p2p_combine_kernel, dim3((unsigned)blocks), st, (const char*)buffer, lay, slot_scores, route_pos, T,
+             top_k, H, (const uint16_t*)shared, (uint16_t*)out, cta_per_row, status);
   return check_launch("p2p_combine_kernel");
 }

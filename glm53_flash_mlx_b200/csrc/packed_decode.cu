@@ -98,6 +98,11 @@ struct DecodeArgs {
   // router; its routed CTAs wait for the router (griddepcontrol.wait) before
   // they read the expert ids and only then let the down grid launch
   bool after_router;
+  // peer-memory owners: gate/up is launched as a programmatic dependent of
+  // the dispatch (its CTAs are resident and wait for the dispatch grid, then
+  // the routed ones for their arrivals), and the down stage lets the combine
+  // launch early
+  bool pdl_owner;
 };
 
 // Physical routed slot p of a peer-memory owner grid -> slot (src, s) = src * cap + s.
@@ -209,6 +214,9 @@ __global__ void __launch_bounds__(32 * W) decode_gate_up_v4(DecodeArgs a) {
   const uint16_t* xb = jb < a.top_k ? a.x + (size_t)jb * a.x_stride
                                     : (a.shared_x ? a.shared_x + (size_t)(jb - a.top_k) * a.H : a.x);
   const bool wait_router = a.after_router && jb < a.top_k;  // CTA-uniform
+  // after the dispatch grid (the home rows; and so that this grid's
+  // completion implies the dispatch's, which the combine relies on)
+  if (a.pdl_owner) pdl_wait();
   float xmul = 0.f;
   if (wait_router) {
     // the activation row does not depend on routing: stage it while the router runs
@@ -317,6 +325,7 @@ __device__ __forceinline__ void decode_down_peer(const DecodeArgs& a, int jb, in
     }
     WarpScales sd;
     sd.load(srow, cols, valid);
+    if (a.pdl_owner) pdl_trigger();  // the combine may launch; it waits for this grid
     pdl_wait();  // the hidden rows come from the gate/up grid
     const float smul =
         decode_unscale<FINITE>() * stage_f16(xs, K + 8, a.hidden + (size_t)jb * a.I, 0, 1, K, scratch);
@@ -660,7 +669,7 @@ static int launch_v4(const DecodeArgs& a, cudaStream_t st, bool gate_up_only) {
       sm_smem(per_sm, reserved);
       rc = launch_gate_up<FINITE, kWideWarps, kWideRing>(a, st, true, per_sm / 2 + 16 - std::min(reserved, per_sm / 2));
     } else {
-      rc = launch_gate_up<FINITE, kWarpsPerBlock, kRing>(a, st, a.after_router, 0);
+      rc = launch_gate_up<FINITE, kWarpsPerBlock, kRing>(a, st, a.after_router || a.pdl_owner, 0);
     }
     if (rc || gate_up_only) return rc;
   }
@@ -1005,6 +1014,7 @@ extern "C" int glm53_ep_owner_decode_p2p(void* buffer, int64_t H, int world, int
   a.rank = rank;
   a.cap = (int)capacity;
   a.shared_first = true;  // owner grid order (see DecodeArgs)
+  a.pdl_owner = true;     // launched right after glm53_ep_dispatch_p2p (see DecodeArgs)
   if (has_shared) {  // the home tokens' shared expert rides in the same launches
     a.Is = (int)I_shared;
     a.n_shared = (int)T_shared;
