@@ -123,7 +123,13 @@ __global__ void __launch_bounds__(32 * kBdWarps) batched_gate_up_kernel(BatchedA
   const int nwork = (int)__ldg(a.descriptor_count) * groups;
   const int cols = a.H >> 7, half = a.I >> 7;
   const int nslice = a.H >> 6;
-  for (int w = blockIdx.x; w < nwork; w += gridDim.x) {
+  // a contiguous run of work items per CTA: consecutive items share their
+  // descriptor, whose route rows are staged once
+  const int per = (nwork + (int)gridDim.x - 1) / (int)gridDim.x;
+  const int w_end = min(nwork, ((int)blockIdx.x + 1) * per);
+  int staged = -1;
+  float staged_mul = 0.f;
+  for (int w = blockIdx.x * per; w < w_end; ++w) {
     const int d = w / groups, grp = w - d * groups;
     const uint32_t e = __ldg(a.tile_experts + d), start = __ldg(a.tile_starts + d);
     const int len = (int)min(__ldg(a.tile_lengths + d), (uint32_t)kBdCols);
@@ -150,8 +156,11 @@ __global__ void __launch_bounds__(32 * kBdWarps) batched_gate_up_kernel(BatchedA
     WarpScales ssg, ssu;
     ssg.load(gs, cols, valid);
     ssu.load(us, cols, valid);
-    const float smul =
-        decode_unscale<FINITE>() * stage_routes_f16(xs, stride, a.x, a.order + start, a.top_k, len, a.H, red);
+    if (d != staged) {
+      staged_mul = stage_routes_f16(xs, stride, a.x, a.order + start, a.top_k, len, a.H, red);
+      staged = d;
+    }
+    const float smul = decode_unscale<FINITE>() * staged_mul;
     float part[4] = {0.f, 0.f, 0.f, 0.f}, tot[4] = {0.f, 0.f, 0.f, 0.f};
     for (int sl = 0; sl < nslice; ++sl) {
       if (sl + P - 1 < nslice) issue(sl + P - 1);
@@ -191,7 +200,11 @@ __global__ void __launch_bounds__(32 * kBdWarps) batched_down_kernel(BatchedArgs
   const int nwork = (int)__ldg(a.descriptor_count) * groups;
   const int cols = K >> 7;
   const int nslice = K >> 6;
-  for (int w = blockIdx.x; w < nwork; w += gridDim.x) {
+  const int per = (nwork + (int)gridDim.x - 1) / (int)gridDim.x;  // contiguous items, as in gate/up
+  const int w_end = min(nwork, ((int)blockIdx.x + 1) * per);
+  int staged = -1;
+  float staged_mul = 0.f;
+  for (int w = blockIdx.x * per; w < w_end; ++w) {
     const int d = w / groups, grp = w - d * groups;
     const uint32_t e = __ldg(a.tile_experts + d), start = __ldg(a.tile_starts + d);
     const int len = (int)min(__ldg(a.tile_lengths + d), (uint32_t)kBdCols);
@@ -216,8 +229,11 @@ __global__ void __launch_bounds__(32 * kBdWarps) batched_down_kernel(BatchedArgs
     }
     WarpScales sd;
     sd.load(srow, cols, valid);
-    const float hmul = decode_unscale<FINITE>() *
-                       stage_f16(hs, stride, a.hidden + (size_t)start * K, K, len, K, red);
+    if (d != staged) {
+      staged_mul = stage_f16(hs, stride, a.hidden + (size_t)start * K, K, len, K, red);
+      staged = d;
+    }
+    const float hmul = decode_unscale<FINITE>() * staged_mul;
     float part[4] = {0.f, 0.f, 0.f, 0.f}, tot[4] = {0.f, 0.f, 0.f, 0.f};
     for (int sl = 0; sl < nslice; ++sl) {
       if (sl + P - 1 < nslice) issue(sl + P - 1);
