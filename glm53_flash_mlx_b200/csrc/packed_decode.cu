@@ -128,9 +128,13 @@ constexpr int kRingDown = 12;  // down: its per-warp streams are short (I/64 sli
 // scheduler fills the SMs one after another for such a grid, so 4-warp CTAs
 // would crowd about 60% of the SMs.  One 12-warp CTA per SM instead (its
 // shared memory is at least half an SM's), which still leaves room for two
-// down CTAs to prefetch beside it.
+// down CTAs to prefetch beside it; 16-warp CTAs with a 7-deep ring where the
+// slot's I/8 units divide by 16 but not by 12 (I = 2048).  Shapes that fit
+// neither launch the 4-warp CTAs after the router completes.
 constexpr int kWideWarps = 12;
 constexpr int kWideRing = 9;
+constexpr int kWide16Warps = 16;
+constexpr int kWide16Ring = 7;
 
 // ---------------------------------------------------------------------------
 // Gate / up / SwiGLU
@@ -664,12 +668,16 @@ template <bool FINITE>
 static int launch_v4(const DecodeArgs& a, cudaStream_t st, bool gate_up_only) {
   {
     int rc;
-    if (a.after_router && (a.I >> 3) % kWideWarps == 0 && (a.Is >> 3) % kWideWarps == 0) {
+    auto fits = [&](int w) { return (a.I >> 3) % w == 0 && (a.Is >> 3) % w == 0; };
+    if (a.after_router && (fits(kWideWarps) || fits(kWide16Warps))) {
       size_t per_sm = 0, reserved = 0;
       sm_smem(per_sm, reserved);
-      rc = launch_gate_up<FINITE, kWideWarps, kWideRing>(a, st, true, per_sm / 2 + 16 - std::min(reserved, per_sm / 2));
+      const size_t half_sm = per_sm / 2 + 16 - std::min(reserved, per_sm / 2);  // one CTA per SM
+      rc = fits(kWideWarps) ? launch_gate_up<FINITE, kWideWarps, kWideRing>(a, st, true, half_sm)
+                            : launch_gate_up<FINITE, kWide16Warps, kWide16Ring>(a, st, true, half_sm);
     } else {
-      rc = launch_gate_up<FINITE, kWarpsPerBlock, kRing>(a, st, a.after_router || a.pdl_owner, 0);
+      // not as a dependent of the router: griddepcontrol.wait then returns at once
+      rc = launch_gate_up<FINITE, kWarpsPerBlock, kRing>(a, st, a.pdl_owner, 0);
     }
     if (rc || gate_up_only) return rc;
   }

@@ -233,7 +233,8 @@ def test_split_decode_matches_single_call_bitwise(G, S):
         assert torch.equal(full, part), t
 
 
-def test_decode_after_router_overlap_bitwise(G, S):
+@pytest.mark.parametrize("I", [1536, 2048])  # 12-warp and 16-warp overlapped gate/up CTAs
+def test_decode_after_router_overlap_bitwise(G, S, I):
     """GLM53_FLAG_AFTER_ROUTER (gate/up launched as a programmatic dependent
     of the router, the shared expert streaming while the router runs) gives
     the bits of the serial launch: through the module (eager and as a CUDA
@@ -242,7 +243,7 @@ def test_decode_after_router_overlap_bitwise(G, S):
     from glm53_flash_mlx_b200.packed import packed_decode_moe, shared_fp8_tensors
     from glm53_flash_mlx_b200.router import Float32Gate
 
-    E, H, I = 64, 4096, 1536
+    E, H = 64, 4096
     cfg = S.moe_config(H, I, E, 8, 10.0)
     mods = []
     for layer in range(3):
