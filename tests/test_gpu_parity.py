@@ -704,3 +704,48 @@ def test_batched_decode_flags_bad_expert_without_trapping(G, S):
     torch.cuda.synchronize()
     assert int(status.item()) & N.STATUS_BAD_EXPERT
     assert torch.isfinite(out.float()).all()
+
+
+@pytest.mark.parametrize("T,E,H,I", [(3, 8, 1024, 256), (16, 288, 4096, 1536)])
+def test_batched_shared_expert_route_equals_shared_rows_added_last(G, S, T, E, H, I):
+    """glm53_batched_decode_moe_shared (the shared expert as one more route per
+    token, weight 1.0) gives the bits of glm53_batched_decode_moe given the
+    shared expert's per-route decode rows as `shared` (added after the routed
+    experts); a bad routed id is flagged and skipped in both."""
+    from glm53_flash_mlx_b200 import _native as N
+    from glm53_flash_mlx_b200.ep import routes_decode
+    from glm53_flash_mlx_b200.packed import shared_fp8_tensors
+
+    bank = S.make_bank(E, H, I, seed=T + 31, device="cuda")
+    sh = shared_fp8_tensors(S.make_shared(H, I, seed=T + 32, device="cuda"))
+    gen = torch.Generator().manual_seed(T + 33)
+    ids = torch.stack([torch.randperm(E, generator=gen)[:8] for _ in range(T)]).to(torch.int32)
+    ids[T - 1, 7] = E + 5  # out of range: skipped and flagged
+    ids = ids.cuda()
+    sc = (torch.rand((T, 8), generator=gen) * 0.25 + 0.05).cuda()
+    x = S.random_bf16((T, H), seed=T + 34, device="cuda", std=1.5)
+    lib = N.lib()
+    flags = N.decode_flags(bank.gate_up_weight, bank.down_weight, sh[0], sh[2], sh[4])
+    # the shared expert as a one-expert bank: its per-route decode rows
+    one = (torch.cat([sh[0], sh[2]]).unsqueeze(0).contiguous(), torch.cat([sh[1], sh[3]]).unsqueeze(0).contiguous(),
+           sh[4].unsqueeze(0).contiguous(), sh[5].unsqueeze(0).contiguous())
+    rows = routes_decode(x, torch.zeros(T, dtype=torch.int32, device="cuda"), one, limit=10.0, flags=flags)
+    st_a = torch.zeros(1, dtype=torch.int32, device="cuda")
+    st_b = torch.zeros(1, dtype=torch.int32, device="cuda")
+    want = torch.empty_like(x)
+    ws = torch.zeros(lib.glm53_batched_decode_workspace_bytes(T, 8, E, H, I), dtype=torch.uint8, device="cuda")
+    N.check(lib.glm53_batched_decode_moe(
+        x.data_ptr(), T, H, ids.data_ptr(), sc.data_ptr(), 8, bank.gate_up_weight.data_ptr(),
+        bank.gate_up_scale_inv.data_ptr(), bank.down_weight.data_ptr(), bank.down_scale_inv.data_ptr(), E, I, 10.0,
+        rows.data_ptr(), want.data_ptr(), ws.data_ptr(), ws.numel(), st_a.data_ptr(), flags, N.stream()), "old")
+    got = torch.empty_like(x)
+    ws2 = torch.zeros(lib.glm53_batched_decode_shared_workspace_bytes(T, 8, E, H, I), dtype=torch.uint8,
+                      device="cuda")
+    N.check(lib.glm53_batched_decode_moe_shared(
+        x.data_ptr(), T, H, ids.data_ptr(), sc.data_ptr(), 8, bank.gate_up_weight.data_ptr(),
+        bank.gate_up_scale_inv.data_ptr(), bank.down_weight.data_ptr(), bank.down_scale_inv.data_ptr(), E, I,
+        *(t.data_ptr() for t in sh), 10.0, got.data_ptr(), ws2.data_ptr(), ws2.numel(), st_b.data_ptr(), flags,
+        N.stream()), "shared")
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+    assert int(st_a.item()) & N.STATUS_BAD_EXPERT and int(st_b.item()) & N.STATUS_BAD_EXPERT
