@@ -98,13 +98,16 @@ def _gloo_rank(rank, world, port, case, result_dir):
         dist.destroy_process_group()
 
 
-def test_expert_parallel_protocol_is_bit_identical_on_gloo(oracle, tmp_path):
+@pytest.mark.parametrize("world", [2, 4])
+def test_expert_parallel_protocol_is_bit_identical_on_gloo(oracle, tmp_path, world):
+    """gloo ranks on CPU (the oracle playing the kernels) carry the dispatch
+    and combine all-to-alls; every rank's tokens equal the one-device MoE."""
     import torch.multiprocessing as mp
 
     from glm53_flash_mlx_b200 import synthetic as S
     from glm53_flash_mlx_b200.packed import shared_fp8_tensors
 
-    world, E, H, I, T = 2, 8, 256, 128, 3
+    E, H, I, T = 8, 256, 128, 3
     bank_t = S.make_bank(E, H, I, seed=31)
     bank = tuple(t.numpy() for t in (bank_t.gate_up_weight, bank_t.gate_up_scale_inv, bank_t.down_weight,
                                       bank_t.down_scale_inv))
