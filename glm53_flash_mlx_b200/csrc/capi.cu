@@ -101,7 +101,7 @@ void* mapped_host(const void* p) {
     cudaGetLastError();
     return nullptr;
   }
-  return at.type == cudaMemoryTypeHost ? at.devicePointer : nullptr;
+  return at.type == cudaMemoryTypeHost ? at.devicePointer : nullptr;  // null when not device-mapped
 }
 
 // Small host <-> device copy: a kernel over the pinned buffer's device
