@@ -179,7 +179,8 @@ int glm53_selected_decode_moe(const void* x, int64_t H, const float* scores, int
                               uint32_t* status, uint32_t flags, void* stream);
 
 /* Size of the fixed scratch area of glm53_packed_decode_moe_static_scratch:
- * 1 MiB of device memory per device, reserved when the library is loaded. */
+ * 1 MiB of device memory on every device that loads the library, held until
+ * the process exits. */
 #define GLM53_STATIC_SCRATCH_BYTES (1u << 20)
 
 /* glm53_packed_decode_moe without a workspace argument: it allocates no device
@@ -192,7 +193,8 @@ int glm53_selected_decode_moe(const void* x, int64_t H, const float* scores, int
  * (top_k, H, I, I_shared) exceeds that returns GLM53_ERR_INVALID (config 2,
  * top_k 8, H 4096, I = I_shared = 1536, needs 176 KiB).  The calling thread's
  * current device must own `stream` and the pointers; the first call on each
- * device looks up the array's address.  Each call clears the array's
+ * device looks up the array's address (cudaGetSymbolAddress), so make that
+ * first call before any stream capture.  Each call clears the array's
  * completion counters on `stream` before its kernels run.  All calls on one
  * device share the array, so calls whose GPU work overlaps (other streams,
  * other host threads) race and must be serialised by the caller. */
