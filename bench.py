@@ -61,6 +61,9 @@ def parse_args():
     p.add_argument("--prefill-only", action="store_true",
                    help="profiling aid: only the T=2048 grouped prefill measurement (prints its JSON and exits)")
     p.add_argument("--prefill-reps", type=int, default=8, help="timed grouped prefill layers")
+    p.add_argument("--hc-only", action="store_true",
+                   help="run only the FFN-boundary (mHC collapse + RMSNorm, hc expand) measurement")
+    p.add_argument("--hc-tokens", default="1,256,2048", help="token counts of the FFN-boundary measurement")
     p.add_argument("--ep-transport", choices=["p2p", "nccl"], default="p2p",
                    help="N > 1: expert-parallel dispatch/combine through peer memory or NCCL all-to-alls")
     return p.parse_args()
@@ -396,6 +399,7 @@ def bench_b200(args, world, rank, local):
         extra["prefill_2048"] = bench_prefill(layers, dev, args)
         extra["linear_config1_5"] = bench_linear(dev, args)
         extra["batched_decode"] = bench_batched(layers, dev, args)
+        extra["ffn_boundary"] = bench_hc(dev, args)
     return {"value": value, "t_ms": t_ms, "clocks": clk, "roofline": roofline, "e2e": e2e,
             "gpu_launches": args.steps * 3, **extra}, layers, xs
 
@@ -706,6 +710,65 @@ def bench_prefill(layers, dev, args):
             "note": "router + route plan + grouped gate/up (SwiGLU epilogue) + grouped down + shared + combine"}
 
 
+def bench_hc(dev, args):
+    """Secondary: the FFN boundary around the MoE -- mHC collapse + post-attention
+    RMSNorm before the router (2 launches), hc expand after the MoE (1 launch) --
+    at T = 1 (decode), 256 (the reference's profiled prefill) and 2048.  Inputs
+    rotate through enough sets to exceed L2 (fn sets at T = 1, states above)."""
+    import torch
+
+    from glm53_flash_mlx_b200 import _native as N
+    from glm53_flash_mlx_b200 import synthetic as S
+
+    lib = N.lib()
+    peaks = measured_peaks()
+    K = 4 * H
+    stream = torch.cuda.Stream(device=dev)
+    res = {}
+    plan = {1: (192, 20), 256: (16, 20), 2048: (4, 10)}
+    for T in (int(v) for v in args.hc_tokens.split(",")):
+        sets, reps = plan.get(T, (4, 10))
+        n_fn = sets if T == 1 else 1
+        fns = [S.random_bf16((24, K), seed=5000 + i, device=dev, std=1.0 / 128) for i in range(n_fn)]
+        scale = torch.tensor([1.0, 0.8, 1.5], dtype=torch.float32, device=dev)
+        base = torch.randn(24, generator=torch.Generator(device=dev).manual_seed(5), device=dev) * 0.5
+        norm_w = S.random_bf16((H,), seed=5999, device=dev, std=0.1) + 1.0
+        states = [S.random_bf16((T, 4, H), seed=6000 + i, device=dev) for i in range(sets)]
+        moes = [S.random_bf16((T, H), seed=7000 + i, device=dev) for i in range(sets)]
+        collapsed = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+        normalized = torch.empty_like(collapsed)
+        post = torch.empty((sets, T, 4), dtype=torch.float32, device=dev)
+        comb = torch.empty((sets, T, 4, 4), dtype=torch.float32, device=dev)
+        outs = [torch.empty((T, 4, H), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+        ws_bytes = lib.glm53_hc_collapse_workspace_bytes(T, H)
+        ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
+
+        def collapse(i, s):
+            N.check(lib.glm53_hc_collapse_norm(
+                states[i].data_ptr(), T, H, 4, fns[i % n_fn].data_ptr(), scale.data_ptr(), base.data_ptr(), 20,
+                1e-6, 1e-6, norm_w.data_ptr(), 1e-6, collapsed.data_ptr(), normalized.data_ptr(),
+                post[i].data_ptr(), comb[i].data_ptr(), ws.data_ptr(), ws_bytes, s), "glm53_hc_collapse_norm")
+
+        def expand(i, s):
+            N.check(lib.glm53_hc_expand(moes[i].data_ptr(), states[i].data_ptr(), post[i].data_ptr(),
+                                        comb[i].data_ptr(), T, H, 4, outs[i % 2].data_ptr(), s), "glm53_hc_expand")
+
+        c_ms = time_stage_graph(collapse, sets, reps, stream, dev)
+        e_ms = time_stage_graph(expand, sets, reps, stream, dev)
+        c_bytes = T * 4 * H * 2 + 24 * K * 2 + H * 2 + 2 * T * H * 2 + T * 20 * 4
+        e_bytes = T * H * 2 + 2 * T * 4 * H * 2 + T * 20 * 4
+        res[f"T{T}"] = {
+            "collapse_norm_us": round(c_ms * 1e3, 2), "collapse_norm_bytes": c_bytes,
+            "collapse_norm_hbm_frac": round(c_bytes / (c_ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
+            "expand_us": round(e_ms * 1e3, 2), "expand_bytes": e_bytes,
+            "expand_hbm_frac": round(e_bytes / (e_ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
+        }
+        del fns, states, moes, outs, ws
+    res["note"] = ("glm53_hc_collapse_norm (hc_mix_kernel + hc_finish_kernel) and glm53_hc_expand, each timed "
+                   "alone in CUDA graphs of one call per input set; fraction of measured HBM copy bandwidth")
+    return res
+
+
 # ---------------------------------------------------------------------------
 # CPU side (oracle port of the reference kernels)
 # ---------------------------------------------------------------------------
@@ -830,6 +893,12 @@ def main():
         if rank == 0:
             print(json.dumps({"batched_decode": bench_batched(layers, dev, args)}), flush=True)
         return
+    if args.hc_only:
+        import torch
+
+        if rank == 0:
+            print(json.dumps({"ffn_boundary": bench_hc(torch.device("cuda", local), args)}), flush=True)
+        return
     if args.prefill_only:
         import torch
 
@@ -870,6 +939,8 @@ def main():
         line["linear_config1_5"] = res["linear_config1_5"]
     if "batched_decode" in res:
         line["batched_decode"] = res["batched_decode"]
+    if "ffn_boundary" in res:
+        line["ffn_boundary"] = res["ffn_boundary"]
     if rank == 0 and world == 1 and not args.no_cpu:
         import torch
 

@@ -128,6 +128,13 @@ SIGNATURES: dict[str, tuple] = {
     ),
     "glm53_sigmoid_bf16": (_int, [_vp, _i64, _vp, _vp]),
     "glm53_decode_step_host": (_int, [_vp, _vp, _vp, _vp]),
+    "glm53_hc_collapse_workspace_bytes": (_sz, [_i64, _i64]),
+    "glm53_hc_collapse_norm": (
+        _int,
+        [_vp, _i64, _i64, _int, _vp, _vp, _vp, _int, _f, _f, _vp, _f, _vp, _vp, _vp, _vp, _vp, _sz, _vp],
+    ),
+    "glm53_rms_norm": (_int, [_vp, _i64, _i64, _vp, _f, _vp, _vp]),
+    "glm53_hc_expand": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _int, _vp, _vp]),
 }
 
 

@@ -1,0 +1,437 @@
+// FFN boundary of a GLM-5.3 layer around the MoE: the mHC collapse of the
+// 4-branch residual state with the post-attention RMSNorm that feeds the
+// router, and the hc expand of the MoE output back into the 4-branch state.
+//
+// Reference flow (scripts/trace_grouped_fp8_route_amplification.py:178-214,
+// scripts/profile_native_prefill_ffn_entry_seam.py:79-87):
+//   collapsed, post, comb = layer.ffn_hc(state)      # mlx-vlm deepseek_v4
+//   normalized = layer.post_attention_layernorm(collapsed)
+//   moe = layer.mlp(normalized)
+//   state = hc_expand(moe, state, post, comb)       # native_indexer_plan.metal:2362-2389
+//
+// Collapse (two launches):
+//   hc_mix_kernel      the mixing projection m = x . fn^T over K = 4H per
+//                      token (24 outputs) and the token's sum of squares,
+//                      split over K: BF16 mma.sync m16n8k16 with FP32
+//                      accumulation, 16 tokens x 24 outputs per CTA, each
+//                      lane streaming 16-byte runs of the state and of fn;
+//                      partial sums to caller workspace [T][ksplit][25].
+//   hc_finish_kernel   one CTA per token: sums the partials in split order,
+//                      r = 1/sqrt(mean(x^2) + eps), pre/post by sigmoid,
+//                      comb by softmax + Sinkhorn on 16 lanes (row sums by
+//                      lane shuffles within a row group, column sums across
+//                      groups), collapsed = BF16(sum_b pre[b] x[b]) kept in
+//                      registers, then the RMSNorm of the collapsed row.
+// Expand (one launch): one thread per 8 hidden columns of a token writes all
+//   4 branches, so each residual run is read once and used 4 times.
+#include "common.cuh"
+
+namespace glm53 {
+namespace {
+
+constexpr int kHcBranches = 4;
+constexpr int kHcMix = (2 + kHcBranches) * kHcBranches;  // 24 mixing outputs
+constexpr int kHcPart = kHcMix + 1;                      // + sum of squares
+constexpr int kHcTileTokens = 16;
+constexpr int kHcMixThreads = 128;
+constexpr int kHcFinishThreads = 256;
+constexpr int kHcMaxChunks = 4;  // 8-column chunks per finish thread: H <= 8192
+constexpr int kHcMaxSplit = 64;
+
+__device__ __forceinline__ void mma_bf16_16816(float c[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ float sq_sum8(uint4 v) {
+  float s = 0.0f;
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float lo = __uint_as_float(w[i] << 16), hi = __uint_as_float(w[i] & 0xffff0000u);
+    s = fmaf(lo, lo, s);
+    s = fmaf(hi, hi, s);
+  }
+  return s;
+}
+
+// Grid (ceil(T/16), ksplit), 4 warps.  Warp w of split y takes the 32-column
+// K blocks kb = 4y + w, 4y + w + 4*ksplit, ...  Lane (g = lane/4, q = lane%4)
+// loads 8 consecutive K values of token rows g and g+8 and of fn rows g,
+// g+8, g+16; two k16 MMA steps use values 0-3 and 4-7 of each run.  The MMA
+// sums over its 16 K positions in any pairing of A and B that agrees, and
+// both operands use the same one: logical k = 2q+e <- 8q+e and 2q+8+e <-
+// 8q+2+e in the first step (+4 in the second).
+__global__ void __launch_bounds__(kHcMixThreads) hc_mix_kernel(const uint16_t* __restrict__ state,
+                                                                const uint16_t* __restrict__ fn, int64_t T,
+                                                                int64_t K, int ksplit, float* __restrict__ part) {
+  __shared__ float red[kHcMixThreads / 32][kHcTileTokens][kHcPart];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const int64_t t0 = (int64_t)blockIdx.x * kHcTileTokens;
+  const bool ok0 = t0 + g < T, ok1 = t0 + g + 8 < T;
+  const uint16_t* a0p = state + (ok0 ? (t0 + g) * K : 0) + q * 8;
+  const uint16_t* a1p = state + (ok1 ? (t0 + g + 8) * K : 0) + q * 8;
+  const uint16_t* bp = fn + (int64_t)g * K + q * 8;
+  const int64_t nkb = K / 32;
+  const int64_t step = (int64_t)ksplit * (kHcMixThreads / 32);
+  float acc[3][4];
+#pragma unroll
+  for (int j = 0; j < 3; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
+  float sq0 = 0.0f, sq1 = 0.0f;
+  const uint4 zero = make_uint4(0, 0, 0, 0);
+  int64_t kb = (int64_t)blockIdx.y * (kHcMixThreads / 32) + warp;
+  constexpr int U = 4;
+  for (; kb < nkb; kb += U * step) {
+    uint4 a0[U], a1[U], b[U][3];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t k = (kb + u * step) * 32;
+      const bool in = kb + u * step < nkb;
+      a0[u] = (in && ok0) ? ldg_stream(reinterpret_cast<const uint4*>(a0p + k)) : zero;
+      a1[u] = (in && ok1) ? ldg_stream(reinterpret_cast<const uint4*>(a1p + k)) : zero;
+#pragma unroll
+      for (int j = 0; j < 3; ++j)
+        b[u][j] = in ? __ldg(reinterpret_cast<const uint4*>(bp + (int64_t)j * 8 * K + k)) : zero;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      sq0 += sq_sum8(a0[u]);
+      sq1 += sq_sum8(a1[u]);
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        mma_bf16_16816(acc[j], a0[u].x, a1[u].x, a0[u].y, a1[u].y, b[u][j].x, b[u][j].y);
+        mma_bf16_16816(acc[j], a0[u].z, a1[u].z, a0[u].w, a1[u].w, b[u][j].z, b[u][j].w);
+      }
+    }
+  }
+  sq0 += __shfl_xor_sync(0xffffffffu, sq0, 1);
+  sq0 += __shfl_xor_sync(0xffffffffu, sq0, 2);
+  sq1 += __shfl_xor_sync(0xffffffffu, sq1, 1);
+  sq1 += __shfl_xor_sync(0xffffffffu, sq1, 2);
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    red[warp][g][8 * j + 2 * q] = acc[j][0];
+    red[warp][g][8 * j + 2 * q + 1] = acc[j][1];
+    red[warp][g + 8][8 * j + 2 * q] = acc[j][2];
+    red[warp][g + 8][8 * j + 2 * q + 1] = acc[j][3];
+  }
+  if (q == 0) {
+    red[warp][g][kHcMix] = sq0;
+    red[warp][g + 8][kHcMix] = sq1;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < kHcTileTokens * kHcPart; i += kHcMixThreads) {
+    const int r = i / kHcPart, c = i % kHcPart;
+    if (t0 + r >= T) continue;
+    const float v = ((red[0][r][c] + red[1][r][c]) + red[2][r][c]) + red[3][r][c];
+    part[((t0 + r) * ksplit + blockIdx.y) * kHcPart + c] = v;
+  }
+}
+
+__device__ __forceinline__ float sigmoid_f32(float z) {
+  return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-z)));
+}
+
+// Pairwise sum (v0 + v1) + (v2 + v3) of the four lanes {l, l^m, l^2m, l^3m}
+// (m = 1 for a comb row, 4 for a column); every lane of the group gets it.
+__device__ __forceinline__ float group4_sum(float v, int m) {
+  const float pair = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, m));
+  return __fadd_rn(pair, __shfl_xor_sync(0xffffffffu, pair, 2 * m));
+}
+
+__device__ __forceinline__ float block_sum_256(float v, float* scratch) {
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) scratch[warp] = v;
+  __syncthreads();
+  float s = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kHcFinishThreads / 32; ++w) s += scratch[w];
+  return s;
+}
+
+struct HcFinishArgs {
+  const uint16_t* x;  // COLLAPSE: state [T, 4, H]; else rows [T, H]
+  const float* part;
+  int ksplit;
+  int64_t H;
+  const float* scale;
+  const float* base;
+  int iters;
+  float eps, norm_eps;
+  const uint16_t* norm_w;  // nullptr: no RMSNorm
+  float rms_eps;
+  uint16_t* collapsed;   // may be nullptr
+  uint16_t* normalized;  // nullptr iff norm_w is nullptr
+  float* post;
+  float* comb;
+};
+
+// COLLAPSE = true: the full collapse + RMSNorm of one token; false: only the
+// RMSNorm of one BF16 row (MLX fast rms_norm).
+template <bool COLLAPSE>
+__global__ void __launch_bounds__(kHcFinishThreads) hc_finish_kernel(HcFinishArgs a) {
+  __shared__ float s_mix[kHcPart];
+  __shared__ float s_pre[kHcBranches];
+  __shared__ float s_red[kHcFinishThreads / 32];
+  const int64_t t = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int64_t H = a.H;
+  const int nchunks = (int)(H / 8);
+  uint4 cv[kHcMaxChunks];
+  float ss = 0.0f;
+  if constexpr (COLLAPSE) {
+    if (tid < kHcPart) {
+      const float* p = a.part + t * a.ksplit * kHcPart + tid;
+      float s = 0.0f;
+      for (int i = 0; i < a.ksplit; ++i) s = __fadd_rn(s, p[(int64_t)i * kHcPart]);
+      s_mix[tid] = s;
+    }
+    __syncthreads();
+    if (tid < 32) {
+      const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s_mix[kHcMix], (float)(kHcBranches * H)),
+                                                        a.norm_eps)));
+      const int l = tid;
+      if (l < kHcBranches) {
+        const float zp = __fadd_rn(__fmul_rn(__fmul_rn(s_mix[l], r), a.scale[0]), a.base[l]);
+        s_pre[l] = __fadd_rn(sigmoid_f32(zp), a.eps);
+        const float zq = __fadd_rn(__fmul_rn(__fmul_rn(s_mix[kHcBranches + l], r), a.scale[1]),
+                                   a.base[kHcBranches + l]);
+        a.post[t * kHcBranches + l] = __fmul_rn(2.0f, sigmoid_f32(zq));
+      }
+      // Lane l < 16 holds comb[i = l/4][j = l%4]; lanes 16-31 mirror the
+      // arithmetic on a copy so every shuffle has all 32 lanes.
+      const int li = l & 15;
+      const float z = __fadd_rn(__fmul_rn(__fmul_rn(s_mix[2 * kHcBranches + li], r), a.scale[2]),
+                                a.base[2 * kHcBranches + li]);
+      float mx = fmaxf(z, __shfl_xor_sync(0xffffffffu, z, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float e = expf(__fadd_rn(z, -mx));
+      float c = __fadd_rn(__fdiv_rn(e, group4_sum(e, 1)), a.eps);
+      for (int it = 0; it < a.iters; ++it) {
+        if (it > 0) c = __fdiv_rn(c, __fadd_rn(group4_sum(c, 1), a.eps));
+        c = __fdiv_rn(c, __fadd_rn(group4_sum(c, 4), a.eps));
+      }
+      if (l < 16) a.comb[t * 16 + l] = c;
+    }
+    __syncthreads();
+    const float p0 = s_pre[0], p1 = s_pre[1], p2 = s_pre[2], p3 = s_pre[3];
+    const uint16_t* xs = a.x + t * kHcBranches * H;
+#pragma unroll
+    for (int i = 0; i < kHcMaxChunks; ++i) {
+      const int c = tid + i * kHcFinishThreads;
+      if (c >= nchunks) break;
+      const uint4 x0 = ldg_stream(reinterpret_cast<const uint4*>(xs + c * 8));
+      const uint4 x1 = ldg_stream(reinterpret_cast<const uint4*>(xs + H + c * 8));
+      const uint4 x2 = ldg_stream(reinterpret_cast<const uint4*>(xs + 2 * H + c * 8));
+      const uint4 x3 = ldg_stream(reinterpret_cast<const uint4*>(xs + 3 * H + c * 8));
+      const uint16_t* h0 = reinterpret_cast<const uint16_t*>(&x0);
+      const uint16_t* h1 = reinterpret_cast<const uint16_t*>(&x1);
+      const uint16_t* h2 = reinterpret_cast<const uint16_t*>(&x2);
+      const uint16_t* h3 = reinterpret_cast<const uint16_t*>(&x3);
+      uint16_t o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float y = __fmul_rn(p0, bf16_bits_to_f32(h0[e]));
+        y = __fadd_rn(y, __fmul_rn(p1, bf16_bits_to_f32(h1[e])));
+        y = __fadd_rn(y, __fmul_rn(p2, bf16_bits_to_f32(h2[e])));
+        y = __fadd_rn(y, __fmul_rn(p3, bf16_bits_to_f32(h3[e])));
+        o[e] = f32_to_bf16_bits(y);
+      }
+      cv[i] = *reinterpret_cast<const uint4*>(o);
+      if (a.collapsed) *reinterpret_cast<uint4*>(a.collapsed + t * H + c * 8) = cv[i];
+      ss += sq_sum8(cv[i]);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < kHcMaxChunks; ++i) {
+      const int c = tid + i * kHcFinishThreads;
+      if (c >= nchunks) break;
+      cv[i] = __ldg(reinterpret_cast<const uint4*>(a.x + t * H + c * 8));
+      ss += sq_sum8(cv[i]);
+    }
+  }
+  if (a.norm_w == nullptr) return;
+  const float total = block_sum_256(ss, s_red);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, (float)H), a.rms_eps)));
+#pragma unroll
+  for (int i = 0; i < kHcMaxChunks; ++i) {
+    const int c = tid + i * kHcFinishThreads;
+    if (c >= nchunks) break;
+    const uint4 wv = __ldg(reinterpret_cast<const uint4*>(a.norm_w + c * 8));
+    const uint16_t* w = reinterpret_cast<const uint16_t*>(&wv);
+    const uint16_t* xv = reinterpret_cast<const uint16_t*>(&cv[i]);
+    uint16_t o[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      o[e] = f32_to_bf16_bits(__fmul_rn(bf16_bits_to_f32(w[e]), bf16_round(__fmul_rn(bf16_bits_to_f32(xv[e]), inv))));
+    *reinterpret_cast<uint4*>(a.normalized + t * H + c * 8) = *reinterpret_cast<const uint4*>(o);
+  }
+}
+
+// out[t][b][d] = BF16(post[t][b] * moe[t][d] + sum_s fma-chain comb[t][s][b] *
+// residual[t][s][d]), the order of native_indexer_plan.metal:2377-2388.
+__global__ void __launch_bounds__(256) hc_expand_kernel(const uint16_t* __restrict__ moe,
+                                                         const uint16_t* __restrict__ residual,
+                                                         const float* __restrict__ post,
+                                                         const float* __restrict__ comb, int64_t T, int64_t H,
+                                                         uint16_t* __restrict__ out) {
+  const int64_t chunks = H / 8;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= T * chunks) return;
+  const int64_t t = idx / chunks, d = (idx % chunks) * 8;
+  const uint4 mv = ldg_stream(reinterpret_cast<const uint4*>(moe + t * H + d));
+  uint4 rv[kHcBranches];
+#pragma unroll
+  for (int s = 0; s < kHcBranches; ++s)
+    rv[s] = ldg_stream(reinterpret_cast<const uint4*>(residual + (t * kHcBranches + s) * H + d));
+  const float4 pv = __ldg(reinterpret_cast<const float4*>(post + t * kHcBranches));
+  float cm[16];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float4 c4 = __ldg(reinterpret_cast<const float4*>(comb + t * 16) + i);
+    cm[4 * i] = c4.x;
+    cm[4 * i + 1] = c4.y;
+    cm[4 * i + 2] = c4.z;
+    cm[4 * i + 3] = c4.w;
+  }
+  const float pb[4] = {pv.x, pv.y, pv.z, pv.w};
+  const uint16_t* m = reinterpret_cast<const uint16_t*>(&mv);
+#pragma unroll
+  for (int b = 0; b < kHcBranches; ++b) {
+    uint16_t o[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float mixed = 0.0f;
+#pragma unroll
+      for (int s = 0; s < kHcBranches; ++s)
+        mixed = __fmaf_rn(cm[s * 4 + b], bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(&rv[s])[e]), mixed);
+      o[e] = f32_to_bf16_bits(__fadd_rn(__fmul_rn(pb[b], bf16_bits_to_f32(m[e])), mixed));
+    }
+    *reinterpret_cast<uint4*>(out + (t * kHcBranches + b) * H + d) = *reinterpret_cast<const uint4*>(o);
+  }
+}
+
+bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+// K split of the mixing projection: about four CTAs per SM in total, at
+// least one 32-column K block per warp, a power of two up to 64.
+int hc_split(int64_t T, int64_t H) {
+  const int64_t tiles = (T + kHcTileTokens - 1) / kHcTileTokens;
+  const int64_t nkb = kHcBranches * H / 32;
+  int s = 1;
+  while (s < kHcMaxSplit && tiles * s < 4 * kNumSMs && (int64_t)(2 * s) * (kHcMixThreads / 32) <= nkb) s *= 2;
+  return s;
+}
+
+bool hc_geometry_ok(int64_t H) { return H > 0 && H % 8 == 0 && H / 8 <= kHcMaxChunks * kHcFinishThreads; }
+
+}  // namespace
+}  // namespace glm53
+
+using namespace glm53;
+
+extern "C" size_t glm53_hc_collapse_workspace_bytes(int64_t T, int64_t H) {
+  if (T <= 0 || !hc_geometry_ok(H)) return 0;
+  return (size_t)T * hc_split(T, H) * kHcPart * sizeof(float);
+}
+
+extern "C" int glm53_hc_collapse_norm(const void* state, int64_t T, int64_t H, int branches, const void* hc_fn,
+                                      const float* hc_scale, const float* hc_base, int sinkhorn_iters,
+                                      float hc_eps, float hc_norm_eps, const void* norm_weight, float rms_eps,
+                                      void* collapsed, void* normalized, float* post, float* comb,
+                                      void* workspace, size_t workspace_bytes, void* stream) {
+  if (branches != kHcBranches) {
+    set_last_error("glm53_hc_collapse_norm: %d branches; the kernels are built for 4", branches);
+    return GLM53_ERR_INVALID;
+  }
+  if (T < 0 || !hc_geometry_ok(H)) {
+    set_last_error("glm53_hc_collapse_norm: hidden size %lld must be a positive multiple of 8 up to %d",
+                   (long long)H, kHcMaxChunks * kHcFinishThreads * 8);
+    return GLM53_ERR_INVALID;
+  }
+  if (sinkhorn_iters < 1 || sinkhorn_iters > 1000) {
+    set_last_error("glm53_hc_collapse_norm: sinkhorn_iters %d outside [1, 1000]", sinkhorn_iters);
+    return GLM53_ERR_INVALID;
+  }
+  if ((norm_weight == nullptr) != (normalized == nullptr)) {
+    set_last_error("glm53_hc_collapse_norm: norm_weight and normalized must both be given or both be NULL");
+    return GLM53_ERR_INVALID;
+  }
+  if (T == 0) return GLM53_OK;
+  if (!state || !hc_fn || !hc_scale || !hc_base || !post || !comb || !workspace) {
+    set_last_error("glm53_hc_collapse_norm: NULL argument");
+    return GLM53_ERR_INVALID;
+  }
+  if (!aligned16(state) || !aligned16(hc_fn) || !aligned16(post) || !aligned16(comb) || !aligned16(workspace) ||
+      (collapsed && !aligned16(collapsed)) || (normalized && !aligned16(normalized)) ||
+      (norm_weight && !aligned16(norm_weight))) {
+    set_last_error("glm53_hc_collapse_norm: state, fn, norm weight, outputs and workspace must be 16-byte aligned");
+    return GLM53_ERR_INVALID;
+  }
+  const size_t need = glm53_hc_collapse_workspace_bytes(T, H);
+  if (workspace_bytes < need) {
+    set_last_error("glm53_hc_collapse_norm: workspace %zu bytes < %zu", workspace_bytes, need);
+    return GLM53_ERR_INVALID;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  const int ksplit = hc_split(T, H);
+  const int64_t K = kHcBranches * H;
+  float* part = static_cast<float*>(workspace);
+  dim3 grid((unsigned)((T + kHcTileTokens - 1) / kHcTileTokens), (unsigned)ksplit);
+  hc_mix_kernel<<<grid, kHcMixThreads, 0, st>>>((const uint16_t*)state, (const uint16_t*)hc_fn, T, K, ksplit, part);
+  int rc = check_launch("hc_mix_kernel");
+  if (rc) return rc;
+  HcFinishArgs a{(const uint16_t*)state, part, ksplit, H, hc_scale, hc_base, sinkhorn_iters, hc_eps, hc_norm_eps,
+                 (const uint16_t*)norm_weight, rms_eps, (uint16_t*)collapsed, (uint16_t*)normalized, post, comb};
+  hc_finish_kernel<true><<<(unsigned)T, kHcFinishThreads, 0, st>>>(a);
+  return check_launch("hc_finish_kernel");
+}
+
+extern "C" int glm53_rms_norm(const void* x, int64_t T, int64_t H, const void* weight, float eps, void* out,
+                              void* stream) {
+  if (T < 0 || !hc_geometry_ok(H)) {
+    set_last_error("glm53_rms_norm: hidden size %lld must be a positive multiple of 8 up to %d", (long long)H,
+                   kHcMaxChunks * kHcFinishThreads * 8);
+    return GLM53_ERR_INVALID;
+  }
+  if (T == 0) return GLM53_OK;
+  if (!x || !weight || !out || !aligned16(x) || !aligned16(weight) || !aligned16(out)) {
+    set_last_error("glm53_rms_norm: x, weight and out must be non-NULL and 16-byte aligned");
+    return GLM53_ERR_INVALID;
+  }
+  HcFinishArgs a{(const uint16_t*)x, nullptr, 0, H, nullptr, nullptr, 0, 0.0f, 0.0f, (const uint16_t*)weight, eps,
+                 nullptr, (uint16_t*)out, nullptr, nullptr};
+  hc_finish_kernel<false><<<(unsigned)T, kHcFinishThreads, 0, (cudaStream_t)stream>>>(a);
+  return check_launch("hc_finish_kernel<rms_norm>");
+}
+
+extern "C" int glm53_hc_expand(const void* moe, const void* residual, const float* post, const float* comb,
+                               int64_t T, int64_t H, int branches, void* out, void* stream) {
+  if (branches != kHcBranches) {
+    set_last_error("glm53_hc_expand: %d branches; the kernel is built for 4", branches);
+    return GLM53_ERR_INVALID;
+  }
+  if (T < 0 || H <= 0 || H % 8 != 0) {
+    set_last_error("glm53_hc_expand: hidden size %lld must be a positive multiple of 8", (long long)H);
+    return GLM53_ERR_INVALID;
+  }
+  if (T == 0) return GLM53_OK;
+  if (!moe || !residual || !post || !comb || !out) {
+    set_last_error("glm53_hc_expand: NULL argument");
+    return GLM53_ERR_INVALID;
+  }
+  if (!aligned16(moe) || !aligned16(residual) || !aligned16(post) || !aligned16(comb) || !aligned16(out)) {
+    set_last_error("glm53_hc_expand: tensors must be 16-byte aligned");
+    return GLM53_ERR_INVALID;
+  }
+  const int64_t threads = T * (H / 8);
+  hc_expand_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+      (const uint16_t*)moe, (const uint16_t*)residual, post, comb, T, H, (uint16_t*)out);
+  return check_launch("hc_expand_kernel");
+}

@@ -492,6 +492,54 @@ int glm53_grouped_moe(const void* x, int64_t T, int64_t H,
  * native_execution/native_indexer_plan.metal:323-366). */
 int glm53_sigmoid_bf16(const void* gate, int64_t n, void* out, void* stream);
 
+/* ---- FFN boundary around the MoE (mHC collapse + RMSNorm, hc expand) ---- */
+
+/* Workspace bytes of glm53_hc_collapse_norm for T tokens (0 if H is not
+ * supported). */
+size_t glm53_hc_collapse_workspace_bytes(int64_t T, int64_t H);
+
+/* mHC collapse of the 4-branch residual state and the post-attention RMSNorm
+ * that feeds the router, for T tokens:
+ *   state BF16 [T, 4, H]; hc_fn BF16 [24, 4H]; hc_scale FP32 [3];
+ *   hc_base FP32 [24]; norm_weight BF16 [H] (or NULL: no RMSNorm);
+ *   collapsed BF16 [T, H] (may be NULL); normalized BF16 [T, H] (NULL iff
+ *   norm_weight is); post FP32 [T, 4]; comb FP32 [T, 4, 4] ([source][branch]).
+ * m = (x . fn^T) / sqrt(mean(x^2) + hc_norm_eps) over x = state[t] (4H);
+ * pre = sigmoid(m[0:4] scale[0] + base[0:4]) + hc_eps;
+ * post = 2 sigmoid(m[4:8] scale[1] + base[4:8]);
+ * comb = Sinkhorn(softmax(m[8:24] scale[2] + base[8:24]) + hc_eps,
+ *                 sinkhorn_iters, hc_eps);
+ * collapsed = BF16(sum_b pre[b] state[t][b]);
+ * normalized = BF16(w * BF16(collapsed / sqrt(mean(collapsed^2) + rms_eps))).
+ * branches must be 4 and H a multiple of 8 up to 8192; pointers 16-byte
+ * aligned.  Replaces layer.ffn_hc (mlx-vlm deepseek_v4 hyper connection, not
+ * in the reference) followed by layer.post_attention_layernorm, the sequence
+ * of scripts/profile_native_prefill_ffn_entry_seam.py:79-81. */
+int glm53_hc_collapse_norm(const void* state, int64_t T, int64_t H, int branches,
+                           const void* hc_fn, const float* hc_scale,
+                           const float* hc_base, int sinkhorn_iters, float hc_eps,
+                           float hc_norm_eps, const void* norm_weight,
+                           float rms_eps, void* collapsed, void* normalized,
+                           float* post, float* comb, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
+/* RMSNorm of T BF16 rows of H: out = BF16(w * BF16(x / sqrt(mean(x^2) + eps))).
+ * Replaces MLX's fast rms_norm as layer.post_attention_layernorm
+ * (scripts/profile_native_prefill_ffn_entry_seam.py:80). */
+int glm53_rms_norm(const void* x, int64_t T, int64_t H, const void* weight,
+                   float eps, void* out, void* stream);
+
+/* hc expand of the MoE output into the 4-branch state:
+ * out[t][b][d] = BF16(post[t][b] * moe[t][d] + mixed), mixed the FMA chain
+ * over source s = 0..3 of comb[t][s][b] * residual[t][s][d].
+ * moe BF16 [T, H]; residual, out BF16 [T, 4, H]; post FP32 [T, 4];
+ * comb FP32 [T, 4, 4].  Replaces glm53_native_prefill_post_attention_hc_expand
+ * (native_execution/native_indexer_plan.metal:2362-2389) as run by
+ * NativePrefillMoEPlan::finish_hc (native_prefill_moe_plan.cpp:136-161). */
+int glm53_hc_expand(const void* moe, const void* residual, const float* post,
+                    const float* comb, int64_t T, int64_t H, int branches,
+                    void* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -654,3 +654,168 @@ void orc_swiglu_bf16_vec(const uint16_t* gate, const uint16_t* up, int64_t n,
   for (int64_t i = 0; i < n; ++i)
     out[i] = orc_swiglu_bf16(f32_from_bf16(gate[i]), f32_from_bf16(up[i]), limit);
 }
+
+/* ------------------------------------------------------------------------ */
+/* FFN boundary: mHC collapse + post-attention RMSNorm, and hc expand       */
+/* ------------------------------------------------------------------------ */
+
+/* The FFN half of a GLM-5.3 layer (scripts/trace_grouped_fp8_route_amplification.py:
+ * 178-214, scripts/profile_native_prefill_ffn_entry_seam.py:79-87):
+ *   collapsed, post, comb = layer.ffn_hc(state)        # mHC collapse
+ *   normalized = layer.post_attention_layernorm(collapsed)
+ *   moe = mlp(normalized)                                # router + MoE
+ *   state' = hc_expand(moe, state, post, comb)
+ *
+ * ffn_hc is mlx-vlm's deepseek_v4 hyper-connection module (mlx-vlm 0.6.17
+ * @ e82d557d, absent here).  It is restated from the published mHC
+ * algorithm (DeepSeek-V4 inference hc_pre / hc_split_sinkhorn) with the
+ * parameter dtypes the reference loads (hc fn BF16 [(2+n)n, nH]; hc scale
+ * FP32 [3] and base FP32 [(2+n)n], glm53_flash_mlx/patch.py:296-318):
+ *   x = f32(state[t]) flattened (n*H);  r = 1/sqrt(mean(x^2) + norm_eps)
+ *   m = (x . fn^T) * r
+ *   pre  = sigmoid(m[0:n] * scale[0] + base[0:n]) + eps
+ *   post = 2 * sigmoid(m[n:2n] * scale[1] + base[n:2n])
+ *   comb = softmax_j(m[2n:] * scale[2] + base[2n:]) + eps   (n x n, [src][dst])
+ *   comb /= colsum + eps; then (iters-1) x (comb /= rowsum + eps; comb /= colsum + eps)
+ *   collapsed = BF16(sum_b pre[b] * x[b])
+ * PARITY UNPINNED for the collapse: no golden vector of mlx-vlm's module
+ * exists in the reference.  Dot products and the mean square accumulate in
+ * double here (the GPU's FP32 split sums are compared with a tolerance);
+ * the 4-term sums are pairwise, (a0 + a1) + (a2 + a3).
+ * post_attention_layernorm is MLX's fast RMSNorm:
+ *   out = BF16(f32(w) * BF16(x * (1 / sqrt(mean(x^2) + eps)))). */
+typedef struct {
+  const uint16_t* state;
+  int64_t H;
+  const uint16_t* fn;
+  const float* scale;
+  const float* base;
+  int iters;
+  float eps, norm_eps;
+  const uint16_t* norm_w;
+  float rms_eps;
+  uint16_t *collapsed, *normalized;
+  float *post, *comb, *mixes;
+} hc_ctx;
+
+static inline float orc_sigmoidf(float z) { return 1.0f / (1.0f + expf(-z)); }
+static inline float sum4(const float* v, int stride) {
+  return (v[0] + v[stride]) + (v[2 * stride] + v[3 * stride]);
+}
+
+static void hc_row(void* p, int64_t t) {
+  const hc_ctx* c = (const hc_ctx*)p;
+  const int n = 4;
+  const int64_t H = c->H, K = n * H;
+  const uint16_t* x = c->state + t * K;
+  double ss = 0.0;
+  for (int64_t k = 0; k < K; ++k) {
+    double v = f32_from_bf16(x[k]);
+    ss += v * v;
+  }
+  float r = 1.0f / sqrtf((float)ss / (float)K + c->norm_eps);
+  float m[24];
+  for (int j = 0; j < (2 + n) * n; ++j) {
+    const uint16_t* w = c->fn + (int64_t)j * K;
+    double acc = 0.0;
+    for (int64_t k = 0; k < K; ++k) acc += (double)f32_from_bf16(x[k]) * (double)f32_from_bf16(w[k]);
+    m[j] = (float)acc * r;
+    if (c->mixes) c->mixes[t * (2 + n) * n + j] = m[j];
+  }
+  float pre[4], cm[16];
+  for (int b = 0; b < n; ++b) {
+    pre[b] = orc_sigmoidf(m[b] * c->scale[0] + c->base[b]) + c->eps;
+    c->post[t * n + b] = 2.0f * orc_sigmoidf(m[n + b] * c->scale[1] + c->base[n + b]);
+  }
+  for (int i = 0; i < n; ++i) {
+    float z[4], mx = -INFINITY;
+    for (int j = 0; j < n; ++j) {
+      z[j] = m[2 * n + i * n + j] * c->scale[2] + c->base[2 * n + i * n + j];
+      if (z[j] > mx) mx = z[j];
+    }
+    for (int j = 0; j < n; ++j) z[j] = expf(z[j] - mx);
+    float s = sum4(z, 1);
+    for (int j = 0; j < n; ++j) cm[i * n + j] = z[j] / s + c->eps;
+  }
+  for (int it = 0; it < c->iters; ++it) {
+    if (it > 0) {
+      for (int i = 0; i < n; ++i) {
+        float s = sum4(cm + i * n, 1) + c->eps;
+        for (int j = 0; j < n; ++j) cm[i * n + j] = cm[i * n + j] / s;
+      }
+    }
+    float cs[4];
+    for (int j = 0; j < n; ++j) cs[j] = sum4(cm + j, n) + c->eps;
+    for (int i = 0; i < n; ++i)
+      for (int j = 0; j < n; ++j) cm[i * n + j] = cm[i * n + j] / cs[j];
+  }
+  memcpy(c->comb + t * n * n, cm, sizeof(cm));
+  double ss2 = 0.0;
+  uint16_t* col = c->collapsed + t * H;
+  for (int64_t d = 0; d < H; ++d) {
+    float y = pre[0] * f32_from_bf16(x[d]);
+    y = y + pre[1] * f32_from_bf16(x[H + d]);
+    y = y + pre[2] * f32_from_bf16(x[2 * H + d]);
+    y = y + pre[3] * f32_from_bf16(x[3 * H + d]);
+    col[d] = bf16_from_f32(y);
+    double v = f32_from_bf16(col[d]);
+    ss2 += v * v;
+  }
+  if (c->norm_w && c->normalized) {
+    float inv = 1.0f / sqrtf((float)ss2 / (float)H + c->rms_eps);
+    for (int64_t d = 0; d < H; ++d)
+      c->normalized[t * H + d] =
+          bf16_from_f32(f32_from_bf16(c->norm_w[d]) * bfr(f32_from_bf16(col[d]) * inv));
+  }
+}
+
+/* Returns 0, or 1 for an unsupported geometry (branches != 4). */
+int orc_hc_collapse_norm(const uint16_t* state, int64_t T, int64_t H, int branches,
+                         const uint16_t* fn, const float* scale, const float* base,
+                         int sinkhorn_iters, float eps, float norm_eps,
+                         const uint16_t* norm_w, float rms_eps, uint16_t* collapsed,
+                         uint16_t* normalized, float* post, float* comb, float* mixes,
+                         int threads) {
+  if (branches != 4 || H <= 0 || sinkhorn_iters < 1) return 1;
+  hc_ctx c = {state, H, fn, scale, base, sinkhorn_iters, eps, norm_eps, norm_w, rms_eps,
+              collapsed, normalized, post, comb, mixes};
+  parallel_for(T, threads, hc_row, &c);
+  return 0;
+}
+
+/* MLX fast RMSNorm on BF16 rows (post_attention_layernorm), as above. */
+void orc_rms_norm_bf16(const uint16_t* x, int64_t T, int64_t H, const uint16_t* w,
+                       float rms_eps, uint16_t* out) {
+  for (int64_t t = 0; t < T; ++t) {
+    double ss = 0.0;
+    for (int64_t d = 0; d < H; ++d) {
+      double v = f32_from_bf16(x[t * H + d]);
+      ss += v * v;
+    }
+    float inv = 1.0f / sqrtf((float)ss / (float)H + rms_eps);
+    for (int64_t d = 0; d < H; ++d)
+      out[t * H + d] = bf16_from_f32(f32_from_bf16(w[d]) * bfr(f32_from_bf16(x[t * H + d]) * inv));
+  }
+}
+
+/* hc expand after the MoE, restating the reference's own kernel
+ * glm53_native_prefill_post_attention_hc_expand
+ * (native_execution/native_indexer_plan.metal:2362-2389), used on the MoE
+ * output by NativePrefillMoEPlan::finish_hc (native_prefill_moe_plan.cpp:
+ * 136-161):
+ *   mixed = fma chain over source s = 0..3 of comb[t][s][b] * residual[t][s][d]
+ *   out[t][b][d] = BF16(post[t][b] * moe[t][d] + mixed)   (product rounded,
+ *   then the add; no contraction). */
+void orc_hc_expand(const uint16_t* moe, const uint16_t* residual, const float* post,
+                   const float* comb, int64_t T, int64_t H, uint16_t* out) {
+  const int n = 4;
+  for (int64_t t = 0; t < T; ++t)
+    for (int b = 0; b < n; ++b)
+      for (int64_t d = 0; d < H; ++d) {
+        float mixed = 0.0f;
+        for (int s = 0; s < n; ++s)
+          mixed = fmaf(comb[(t * n + s) * n + b], f32_from_bf16(residual[(t * n + s) * H + d]), mixed);
+        float branch = post[t * n + b] * f32_from_bf16(moe[t * H + d]);
+        out[(t * n + b) * H + d] = bf16_from_f32(branch + mixed);
+      }
+}

@@ -36,6 +36,9 @@ __all__ = [
     "direct_moe",
     "grouped_moe",
     "default_threads",
+    "hc_collapse_norm",
+    "rms_norm",
+    "hc_expand",
 ]
 
 _HERE = Path(__file__).resolve().parent
@@ -91,6 +94,13 @@ def oracle_lib():
                 "orc_activate_gate_up": (None, [_u16, _i64, _i64, ctypes.c_float, _u16]),
                 "orc_restore_and_reduce": (None, [_u16, _f32, _u32, _i64, ctypes.c_int, _i64, _u16]),
                 "orc_bf16_add": (None, [_u16, _u16, _i64, _u16]),
+                "orc_hc_collapse_norm": (
+                    ctypes.c_int,
+                    [_u16, _i64, _i64, ctypes.c_int, _u16, _f32, _f32, ctypes.c_int, ctypes.c_float,
+                     ctypes.c_float, _u16, ctypes.c_float, _u16, _u16, _f32, _f32, _f32, ctypes.c_int],
+                ),
+                "orc_rms_norm_bf16": (None, [_u16, _i64, _i64, _u16, ctypes.c_float, _u16]),
+                "orc_hc_expand": (None, [_u16, _u16, _f32, _f32, _i64, _i64, _u16]),
             }
             for name, (res, args) in sig.items():
                 fn = getattr(lib, name)
@@ -410,3 +420,62 @@ def grouped_moe(x_bits, indices, scores, bank, shared, limit: float, *,
     if shared is not None:
         result = bf16_add(result, shared_expert(flat, shared, limit, threads=threads))
     return result.reshape(x.shape)
+
+
+# ----------------------------------------------------------------------------
+# FFN boundary: mHC collapse + RMSNorm (before the router), hc expand (after)
+# ----------------------------------------------------------------------------
+
+def hc_collapse_norm(state_bits, fn_bits, scale, base, norm_weight_bits=None, *,
+                     sinkhorn_iters: int = 20, eps: float = 1e-6, norm_eps: float = 1e-6,
+                     rms_eps: float = 1e-6, threads: int | None = None):
+    """mHC collapse of ``state`` [T, 4, H] and the post-attention RMSNorm
+    (the ``layer.ffn_hc`` -> ``layer.post_attention_layernorm`` sequence of
+    scripts/profile_native_prefill_ffn_entry_seam.py:79-81).  Returns
+    ``(collapsed [T,H] u16, normalized [T,H] u16 or None, post [T,4] f32,
+    comb [T,4,4] f32, mixes [T,24] f32)``.  Parity of the collapse itself is
+    unpinned (mlx-vlm's module is absent); see ``orc_hc_collapse_norm``."""
+    state = _c(state_bits, np.uint16)
+    T, n, H = state.shape
+    fn = _c(fn_bits, np.uint16)
+    if fn.shape != ((2 + n) * n, n * H):
+        raise ValueError(f"hc fn shape {fn.shape} != {((2 + n) * n, n * H)}")
+    scale = _c(scale, np.float32)
+    base = _c(base, np.float32)
+    w = None if norm_weight_bits is None else _c(norm_weight_bits, np.uint16)
+    collapsed = np.zeros((T, H), np.uint16)
+    normalized = None if w is None else np.zeros((T, H), np.uint16)
+    post = np.zeros((T, n), np.float32)
+    comb = np.zeros((T, n, n), np.float32)
+    mixes = np.zeros((T, (2 + n) * n), np.float32)
+    rc = oracle_lib().orc_hc_collapse_norm(
+        _p(state, _u16), T, H, n, _p(fn, _u16), _p(scale, _f32), _p(base, _f32), sinkhorn_iters,
+        eps, norm_eps, _p(w, _u16), rms_eps, _p(collapsed, _u16), _p(normalized, _u16),
+        _p(post, _f32), _p(comb, _f32), _p(mixes, _f32), threads or default_threads())
+    if rc:
+        raise ValueError("oracle hc_collapse_norm: unsupported geometry")
+    return collapsed, normalized, post, comb, mixes
+
+
+def rms_norm(x_bits, weight_bits, eps: float = 1e-6) -> np.ndarray:
+    """MLX fast RMSNorm over BF16 rows: BF16(w * BF16(x * rsqrt(mean(x^2)+eps)))."""
+    x = _c(x_bits, np.uint16)
+    T, H = x.reshape(-1, x.shape[-1]).shape
+    w = _c(weight_bits, np.uint16)
+    out = np.zeros_like(x)
+    oracle_lib().orc_rms_norm_bf16(_p(x, _u16), T, H, _p(w, _u16), eps, _p(out, _u16))
+    return out
+
+
+def hc_expand(moe_bits, residual_bits, post, comb) -> np.ndarray:
+    """hc expand of the MoE output into the 4-branch state
+    (native_execution/native_indexer_plan.metal:2362-2389)."""
+    moe = _c(moe_bits, np.uint16)
+    residual = _c(residual_bits, np.uint16)
+    T, n, H = residual.shape
+    post = _c(post, np.float32)
+    comb = _c(comb, np.float32)
+    out = np.zeros((T, n, H), np.uint16)
+    oracle_lib().orc_hc_expand(_p(moe, _u16), _p(residual, _u16), _p(post, _f32), _p(comb, _f32),
+                               T, H, _p(out, _u16))
+    return out
