@@ -16,12 +16,13 @@
 //                      accumulation, 16 tokens x 24 outputs per CTA, each
 //                      lane streaming 16-byte runs of the state and of fn;
 //                      partial sums to caller workspace [T][ksplit][25].
-//   hc_finish_kernel   one CTA per token: sums the partials in split order,
-//                      r = 1/sqrt(mean(x^2) + eps), pre/post by sigmoid,
-//                      comb by softmax + Sinkhorn on 16 lanes (row sums by
-//                      lane shuffles within a row group, column sums across
-//                      groups), collapsed = BF16(sum_b pre[b] x[b]) kept in
-//                      registers, then the RMSNorm of the collapsed row.
+//   hc_finish_*        sums the partials in a fixed order, r = 1/sqrt(mean(x^2)
+//                      + eps), pre/post by sigmoid, comb by softmax + Sinkhorn
+//                      on 16 lanes of a warp (row sums by lane shuffles within
+//                      a row group, column sums across groups), collapsed =
+//                      BF16(sum_b pre[b] x[b]) in registers, then the RMSNorm
+//                      of the collapsed row.  One CTA per token for small T;
+//                      eight tokens per CTA (one Sinkhorn per warp) for large T.
 // Expand (one launch): one thread per 8 hidden columns of a token writes all
 //   4 branches, so each residual run is read once and used 4 times.
 #include "common.cuh"
@@ -59,8 +60,9 @@ __device__ __forceinline__ float sq_sum8(uint4 v) {
   return s;
 }
 
-// Grid (ceil(T/16), ksplit), 4 warps.  Warp w of split y takes the 32-column
-// K blocks kb = 4y + w, 4y + w + 4*ksplit, ...  Lane (g = lane/4, q = lane%4)
+// Grid (ceil(T/16), ksplit), 4 warps.  Warp w of split y takes a contiguous
+// run of 32-column K blocks (the (4y + w)-th of 4*ksplit equal runs), so
+// consecutive loads of a lane stay in one DRAM page of each row.  Lane (g = lane/4, q = lane%4)
 // loads 8 consecutive K values of token rows g and g+8 and of fn rows g,
 // g+8, g+16; two k16 MMA steps use values 0-3 and 4-7 of each run.  The MMA
 // sums over its 16 K positions in any pairing of A and B that agrees, and
@@ -70,6 +72,9 @@ __global__ void __launch_bounds__(kHcMixThreads) hc_mix_kernel(const uint16_t* _
                                                                 const uint16_t* __restrict__ fn, int64_t T,
                                                                 int64_t K, int ksplit, float* __restrict__ part) {
   __shared__ float red[kHcMixThreads / 32][kHcTileTokens][kHcPart];
+  // The finish kernel is this grid's programmatic dependent: it may start
+  // (and load the state) now; it reads the partial sums after griddepcontrol.wait.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, q = lane & 3;
   const int64_t t0 = (int64_t)blockIdx.x * kHcTileTokens;
@@ -78,20 +83,22 @@ __global__ void __launch_bounds__(kHcMixThreads) hc_mix_kernel(const uint16_t* _
   const uint16_t* a1p = state + (ok1 ? (t0 + g + 8) * K : 0) + q * 8;
   const uint16_t* bp = fn + (int64_t)g * K + q * 8;
   const int64_t nkb = K / 32;
-  const int64_t step = (int64_t)ksplit * (kHcMixThreads / 32);
+  const int64_t warps = (int64_t)ksplit * (kHcMixThreads / 32);
+  const int64_t per = (nkb + warps - 1) / warps;
+  const int64_t kb_begin = ((int64_t)blockIdx.y * (kHcMixThreads / 32) + warp) * per;
+  const int64_t kb_end = kb_begin + per < nkb ? kb_begin + per : nkb;
   float acc[3][4];
 #pragma unroll
   for (int j = 0; j < 3; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
   float sq0 = 0.0f, sq1 = 0.0f;
   const uint4 zero = make_uint4(0, 0, 0, 0);
-  int64_t kb = (int64_t)blockIdx.y * (kHcMixThreads / 32) + warp;
   constexpr int U = 4;
-  for (; kb < nkb; kb += U * step) {
+  for (int64_t kb = kb_begin; kb < kb_end; kb += U) {
     uint4 a0[U], a1[U], b[U][3];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int64_t k = (kb + u * step) * 32;
-      const bool in = kb + u * step < nkb;
+      const int64_t k = (kb + u) * 32;
+      const bool in = kb + u < kb_end;
       a0[u] = (in && ok0) ? ldg_stream(reinterpret_cast<const uint4*>(a0p + k)) : zero;
       a1[u] = (in && ok1) ? ldg_stream(reinterpret_cast<const uint4*>(a1p + k)) : zero;
 #pragma unroll
@@ -156,10 +163,10 @@ __device__ __forceinline__ float block_sum_256(float v, float* scratch) {
 }
 
 struct HcFinishArgs {
-  const uint16_t* x;  // COLLAPSE: state [T, 4, H]; else rows [T, H]
-  const float* part;
+  const uint16_t* state;  // [T, 4, H]
+  const float* part;      // [T][ksplit][25]
   int ksplit;
-  int64_t H;
+  int64_t T, H;
   const float* scale;
   const float* base;
   int iters;
@@ -172,105 +179,237 @@ struct HcFinishArgs {
   float* comb;
 };
 
-// COLLAPSE = true: the full collapse + RMSNorm of one token; false: only the
-// RMSNorm of one BF16 row (MLX fast rms_norm).
-template <bool COLLAPSE>
-__global__ void __launch_bounds__(kHcFinishThreads) hc_finish_kernel(HcFinishArgs a) {
+// One warp: pre, post and comb of token t from its 25 reduced sums mix[]
+// (shared memory, visible to the warp).  pre goes to pre_out[0..3].  Lane
+// l < 16 holds comb[i = l/4][j = l%4]; lanes 16-31 mirror the arithmetic on a
+// copy so every shuffle has all 32 lanes.
+__device__ __forceinline__ void hc_coefficients(const HcFinishArgs& a, int64_t t, const float* mix,
+                                                float* pre_out) {
+  const int l = threadIdx.x & 31;
+  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(mix[kHcMix], (float)(kHcBranches * a.H)),
+                                                    a.norm_eps)));
+  if (l < kHcBranches) {
+    const float zp = __fadd_rn(__fmul_rn(__fmul_rn(mix[l], r), a.scale[0]), a.base[l]);
+    pre_out[l] = __fadd_rn(sigmoid_f32(zp), a.eps);
+    const float zq = __fadd_rn(__fmul_rn(__fmul_rn(mix[kHcBranches + l], r), a.scale[1]), a.base[kHcBranches + l]);
+    a.post[t * kHcBranches + l] = __fmul_rn(2.0f, sigmoid_f32(zq));
+  }
+  const int li = l & 15;
+  const float z = __fadd_rn(__fmul_rn(__fmul_rn(mix[2 * kHcBranches + li], r), a.scale[2]),
+                            a.base[2 * kHcBranches + li]);
+  float mx = fmaxf(z, __shfl_xor_sync(0xffffffffu, z, 1));
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+  const float e = expf(__fadd_rn(z, -mx));
+  float c = __fadd_rn(__fdiv_rn(e, group4_sum(e, 1)), a.eps);
+  for (int it = 0; it < a.iters; ++it) {
+    if (it > 0) c = __fdiv_rn(c, __fadd_rn(group4_sum(c, 1), a.eps));
+    c = __fdiv_rn(c, __fadd_rn(group4_sum(c, 4), a.eps));
+  }
+  if (l < 16) a.comb[t * 16 + l] = c;
+}
+
+// The four branch runs of 8 columns at chunk c of token t.
+__device__ __forceinline__ void load_branches(const HcFinishArgs& a, int64_t t, int c, uint4 x[kHcBranches]) {
+  const uint16_t* xs = a.state + t * kHcBranches * a.H + (int64_t)c * 8;
+#pragma unroll
+  for (int b = 0; b < kHcBranches; ++b) x[b] = ldg_stream(reinterpret_cast<const uint4*>(xs + b * a.H));
+}
+
+// collapsed = BF16(((p0 x0 + p1 x1) + p2 x2) + p3 x3) for 8 columns, products
+// and sums rounded one by one.
+__device__ __forceinline__ uint4 collapse8(const uint4 x[kHcBranches], const float* pre) {
+  const float p0 = pre[0], p1 = pre[1], p2 = pre[2], p3 = pre[3];
+  const uint16_t* h0 = reinterpret_cast<const uint16_t*>(&x[0]);
+  const uint16_t* h1 = reinterpret_cast<const uint16_t*>(&x[1]);
+  const uint16_t* h2 = reinterpret_cast<const uint16_t*>(&x[2]);
+  const uint16_t* h3 = reinterpret_cast<const uint16_t*>(&x[3]);
+  uint16_t o[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    float y = __fmul_rn(p0, bf16_bits_to_f32(h0[e]));
+    y = __fadd_rn(y, __fmul_rn(p1, bf16_bits_to_f32(h1[e])));
+    y = __fadd_rn(y, __fmul_rn(p2, bf16_bits_to_f32(h2[e])));
+    y = __fadd_rn(y, __fmul_rn(p3, bf16_bits_to_f32(h3[e])));
+    o[e] = f32_to_bf16_bits(y);
+  }
+  return *reinterpret_cast<const uint4*>(o);
+}
+
+// out = BF16(w * BF16(x * inv)) for 8 columns (MLX fast rms_norm rounding).
+__device__ __forceinline__ uint4 norm8(uint4 xv, uint4 wv, float inv) {
+  const uint16_t* w = reinterpret_cast<const uint16_t*>(&wv);
+  const uint16_t* x = reinterpret_cast<const uint16_t*>(&xv);
+  uint16_t o[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e)
+    o[e] = f32_to_bf16_bits(__fmul_rn(bf16_bits_to_f32(w[e]), bf16_round(__fmul_rn(bf16_bits_to_f32(x[e]), inv))));
+  return *reinterpret_cast<const uint4*>(o);
+}
+
+__device__ __forceinline__ float rms_inv(float sumsq, int64_t H, float eps) {
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sumsq, (float)H), eps)));
+}
+
+// Small T: one CTA per token.  Each thread issues the loads of its state
+// chunks first, so they are in flight while the 25 sums are reduced (8 groups
+// of splits g, g+8, ... in parallel, then the groups in order) and warp 0 runs
+// the Sinkhorn iterations; then all threads collapse and normalise the row.
+template <int MAXC>
+__global__ void __launch_bounds__(kHcFinishThreads) hc_finish_token_kernel(HcFinishArgs a) {
+  __shared__ float s_red[8][kHcPart];
   __shared__ float s_mix[kHcPart];
   __shared__ float s_pre[kHcBranches];
-  __shared__ float s_red[kHcFinishThreads / 32];
+  __shared__ float s_sum[kHcFinishThreads / 32];
   const int64_t t = blockIdx.x;
   const int tid = threadIdx.x;
-  const int64_t H = a.H;
-  const int nchunks = (int)(H / 8);
-  uint4 cv[kHcMaxChunks];
+  const int nchunks = (int)(a.H / 8);
+  uint4 xv[MAXC][kHcBranches];
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = tid + i * kHcFinishThreads;
+    if (c < nchunks) load_branches(a, t, c, xv[i]);
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the mix kernel's partial sums
+  if (tid < 8 * kHcPart) {
+    const int g = tid / kHcPart, col = tid % kHcPart;
+    const float* p = a.part + t * a.ksplit * kHcPart + col;
+    float v[kHcMaxSplit / 8];
+#pragma unroll
+    for (int j = 0; j < kHcMaxSplit / 8; ++j) {
+      const int s = g + 8 * j;
+      v[j] = s < a.ksplit ? p[(int64_t)s * kHcPart] : 0.0f;
+    }
+    float acc = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kHcMaxSplit / 8; ++j) acc = __fadd_rn(acc, v[j]);
+    s_red[g][col] = acc;
+  }
+  __syncthreads();
+  if (tid < kHcPart) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) acc = __fadd_rn(acc, s_red[g][tid]);
+    s_mix[tid] = acc;
+  }
+  __syncthreads();
+  if (tid < 32) hc_coefficients(a, t, s_mix, s_pre);
+  __syncthreads();
+  uint4 cv[MAXC];
   float ss = 0.0f;
-  if constexpr (COLLAPSE) {
-    if (tid < kHcPart) {
-      const float* p = a.part + t * a.ksplit * kHcPart + tid;
-      float s = 0.0f;
-      for (int i = 0; i < a.ksplit; ++i) s = __fadd_rn(s, p[(int64_t)i * kHcPart]);
-      s_mix[tid] = s;
-    }
-    __syncthreads();
-    if (tid < 32) {
-      const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s_mix[kHcMix], (float)(kHcBranches * H)),
-                                                        a.norm_eps)));
-      const int l = tid;
-      if (l < kHcBranches) {
-        const float zp = __fadd_rn(__fmul_rn(__fmul_rn(s_mix[l], r), a.scale[0]), a.base[l]);
-        s_pre[l] = __fadd_rn(sigmoid_f32(zp), a.eps);
-        const float zq = __fadd_rn(__fmul_rn(__fmul_rn(s_mix[kHcBranches + l], r), a.scale[1]),
-                                   a.base[kHcBranches + l]);
-        a.post[t * kHcBranches + l] = __fmul_rn(2.0f, sigmoid_f32(zq));
-      }
-      // Lane l < 16 holds comb[i = l/4][j = l%4]; lanes 16-31 mirror the
-      // arithmetic on a copy so every shuffle has all 32 lanes.
-      const int li = l & 15;
-      const float z = __fadd_rn(__fmul_rn(__fmul_rn(s_mix[2 * kHcBranches + li], r), a.scale[2]),
-                                a.base[2 * kHcBranches + li]);
-      float mx = fmaxf(z, __shfl_xor_sync(0xffffffffu, z, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      const float e = expf(__fadd_rn(z, -mx));
-      float c = __fadd_rn(__fdiv_rn(e, group4_sum(e, 1)), a.eps);
-      for (int it = 0; it < a.iters; ++it) {
-        if (it > 0) c = __fdiv_rn(c, __fadd_rn(group4_sum(c, 1), a.eps));
-        c = __fdiv_rn(c, __fadd_rn(group4_sum(c, 4), a.eps));
-      }
-      if (l < 16) a.comb[t * 16 + l] = c;
-    }
-    __syncthreads();
-    const float p0 = s_pre[0], p1 = s_pre[1], p2 = s_pre[2], p3 = s_pre[3];
-    const uint16_t* xs = a.x + t * kHcBranches * H;
 #pragma unroll
-    for (int i = 0; i < kHcMaxChunks; ++i) {
-      const int c = tid + i * kHcFinishThreads;
-      if (c >= nchunks) break;
-      const uint4 x0 = ldg_stream(reinterpret_cast<const uint4*>(xs + c * 8));
-      const uint4 x1 = ldg_stream(reinterpret_cast<const uint4*>(xs + H + c * 8));
-      const uint4 x2 = ldg_stream(reinterpret_cast<const uint4*>(xs + 2 * H + c * 8));
-      const uint4 x3 = ldg_stream(reinterpret_cast<const uint4*>(xs + 3 * H + c * 8));
-      const uint16_t* h0 = reinterpret_cast<const uint16_t*>(&x0);
-      const uint16_t* h1 = reinterpret_cast<const uint16_t*>(&x1);
-      const uint16_t* h2 = reinterpret_cast<const uint16_t*>(&x2);
-      const uint16_t* h3 = reinterpret_cast<const uint16_t*>(&x3);
-      uint16_t o[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        float y = __fmul_rn(p0, bf16_bits_to_f32(h0[e]));
-        y = __fadd_rn(y, __fmul_rn(p1, bf16_bits_to_f32(h1[e])));
-        y = __fadd_rn(y, __fmul_rn(p2, bf16_bits_to_f32(h2[e])));
-        y = __fadd_rn(y, __fmul_rn(p3, bf16_bits_to_f32(h3[e])));
-        o[e] = f32_to_bf16_bits(y);
-      }
-      cv[i] = *reinterpret_cast<const uint4*>(o);
-      if (a.collapsed) *reinterpret_cast<uint4*>(a.collapsed + t * H + c * 8) = cv[i];
-      ss += sq_sum8(cv[i]);
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < kHcMaxChunks; ++i) {
-      const int c = tid + i * kHcFinishThreads;
-      if (c >= nchunks) break;
-      cv[i] = __ldg(reinterpret_cast<const uint4*>(a.x + t * H + c * 8));
-      ss += sq_sum8(cv[i]);
-    }
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = tid + i * kHcFinishThreads;
+    if (c >= nchunks) break;
+    cv[i] = collapse8(xv[i], s_pre);
+    if (a.collapsed) *reinterpret_cast<uint4*>(a.collapsed + t * a.H + c * 8) = cv[i];
+    ss += sq_sum8(cv[i]);
   }
   if (a.norm_w == nullptr) return;
-  const float total = block_sum_256(ss, s_red);
-  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, (float)H), a.rms_eps)));
+  const float inv = rms_inv(block_sum_256(ss, s_sum), a.H, a.rms_eps);
 #pragma unroll
-  for (int i = 0; i < kHcMaxChunks; ++i) {
+  for (int i = 0; i < MAXC; ++i) {
     const int c = tid + i * kHcFinishThreads;
     if (c >= nchunks) break;
     const uint4 wv = __ldg(reinterpret_cast<const uint4*>(a.norm_w + c * 8));
-    const uint16_t* w = reinterpret_cast<const uint16_t*>(&wv);
-    const uint16_t* xv = reinterpret_cast<const uint16_t*>(&cv[i]);
-    uint16_t o[8];
+    *reinterpret_cast<uint4*>(a.normalized + t * a.H + c * 8) = norm8(cv[i], wv, inv);
+  }
+}
+
+// Large T (ksplit <= 8, H <= 4096): eight tokens per CTA.  Warp w reduces the
+// sums of token t0 + w (lane = column, its ksplit loads in flight together)
+// and runs that token's Sinkhorn, so eight run at once per CTA; then all
+// threads collapse and normalise the eight rows in turn, the next row's state
+// loads issued before the current row's norm reduction.
+__global__ void __launch_bounds__(kHcFinishThreads) hc_finish_group_kernel(HcFinishArgs a) {
+  constexpr int TPC = 8, MAXC = 2;
+  __shared__ float s_mix[TPC][kHcPart];
+  __shared__ float s_pre[TPC][kHcBranches];
+  __shared__ float s_sum[2][kHcFinishThreads / 32];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t t0 = (int64_t)blockIdx.x * TPC;
+  const int ntok = (int)(a.T - t0 < TPC ? a.T - t0 : TPC);
+  const int nchunks = (int)(a.H / 8);
+  uint4 xv[MAXC][kHcBranches];
 #pragma unroll
-    for (int e = 0; e < 8; ++e)
-      o[e] = f32_to_bf16_bits(__fmul_rn(bf16_bits_to_f32(w[e]), bf16_round(__fmul_rn(bf16_bits_to_f32(xv[e]), inv))));
-    *reinterpret_cast<uint4*>(a.normalized + t * H + c * 8) = *reinterpret_cast<const uint4*>(o);
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = tid + i * kHcFinishThreads;
+    if (c < nchunks) load_branches(a, t0, c, xv[i]);
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the mix kernel's partial sums
+  if (warp < ntok) {
+    const int64_t t = t0 + warp;
+    if (lane < kHcPart) {
+      const float* p = a.part + t * a.ksplit * kHcPart + lane;
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = j < a.ksplit ? p[(int64_t)j * kHcPart] : 0.0f;
+      float acc = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, v[j]);
+      s_mix[warp][lane] = acc;
+    }
+    __syncwarp();
+    hc_coefficients(a, t, s_mix[warp], s_pre[warp]);
+  }
+  __syncthreads();
+  for (int k = 0; k < ntok; ++k) {
+    const int64_t t = t0 + k;
+    uint4 cv[MAXC];
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = tid + i * kHcFinishThreads;
+      if (c >= nchunks) break;
+      cv[i] = collapse8(xv[i], s_pre[k]);
+      if (a.collapsed) *reinterpret_cast<uint4*>(a.collapsed + t * a.H + c * 8) = cv[i];
+      ss += sq_sum8(cv[i]);
+    }
+    if (k + 1 < ntok) {
+#pragma unroll
+      for (int i = 0; i < MAXC; ++i) {
+        const int c = tid + i * kHcFinishThreads;
+        if (c < nchunks) load_branches(a, t + 1, c, xv[i]);
+      }
+    }
+    if (a.norm_w == nullptr) continue;
+    // Alternate scratch rows: a row is rewritten only two tokens later, after
+    // every thread has passed the intervening token's barrier.
+    const float inv = rms_inv(block_sum_256(ss, s_sum[k & 1]), a.H, a.rms_eps);
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = tid + i * kHcFinishThreads;
+      if (c >= nchunks) break;
+      const uint4 wv = __ldg(reinterpret_cast<const uint4*>(a.norm_w + c * 8));
+      *reinterpret_cast<uint4*>(a.normalized + t * a.H + c * 8) = norm8(cv[i], wv, inv);
+    }
+  }
+}
+
+// RMSNorm of BF16 rows alone: one CTA per row.
+template <int MAXC>
+__global__ void __launch_bounds__(kHcFinishThreads) rms_norm_kernel(const uint16_t* __restrict__ x, int64_t H,
+                                                                    const uint16_t* __restrict__ w, float eps,
+                                                                    uint16_t* __restrict__ out) {
+  __shared__ float s_sum[kHcFinishThreads / 32];
+  const int64_t t = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int nchunks = (int)(H / 8);
+  uint4 xv[MAXC];
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = tid + i * kHcFinishThreads;
+    if (c >= nchunks) break;
+    xv[i] = __ldg(reinterpret_cast<const uint4*>(x + t * H + c * 8));
+    ss += sq_sum8(xv[i]);
+  }
+  const float inv = rms_inv(block_sum_256(ss, s_sum), H, eps);
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = tid + i * kHcFinishThreads;
+    if (c >= nchunks) break;
+    const uint4 wv = __ldg(reinterpret_cast<const uint4*>(w + c * 8));
+    *reinterpret_cast<uint4*>(out + t * H + c * 8) = norm8(xv[i], wv, inv);
   }
 }
 
@@ -387,9 +526,29 @@ extern "C" int glm53_hc_collapse_norm(const void* state, int64_t T, int64_t H, i
   hc_mix_kernel<<<grid, kHcMixThreads, 0, st>>>((const uint16_t*)state, (const uint16_t*)hc_fn, T, K, ksplit, part);
   int rc = check_launch("hc_mix_kernel");
   if (rc) return rc;
-  HcFinishArgs a{(const uint16_t*)state, part, ksplit, H, hc_scale, hc_base, sinkhorn_iters, hc_eps, hc_norm_eps,
-                 (const uint16_t*)norm_weight, rms_eps, (uint16_t*)collapsed, (uint16_t*)normalized, post, comb};
-  hc_finish_kernel<true><<<(unsigned)T, kHcFinishThreads, 0, st>>>(a);
+  HcFinishArgs a{(const uint16_t*)state, part, ksplit, T, H, hc_scale, hc_base, sinkhorn_iters, hc_eps,
+                 hc_norm_eps, (const uint16_t*)norm_weight, rms_eps, (uint16_t*)collapsed, (uint16_t*)normalized,
+                 post, comb};
+  // Launched as the mix kernel's programmatic dependent (the state loads of
+  // its first row overlap the mix kernel; griddepcontrol.wait orders the rest).
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(kHcFinishThreads);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (ksplit <= 8 && H <= 2 * 8 * kHcFinishThreads && T >= 512) {
+    cfg.gridDim = dim3((unsigned)((T + 7) / 8));
+    cudaLaunchKernelEx(&cfg, hc_finish_group_kernel, a);
+  } else if (H <= 2 * 8 * kHcFinishThreads) {
+    cfg.gridDim = dim3((unsigned)T);
+    cudaLaunchKernelEx(&cfg, hc_finish_token_kernel<2>, a);
+  } else {
+    cfg.gridDim = dim3((unsigned)T);
+    cudaLaunchKernelEx(&cfg, hc_finish_token_kernel<kHcMaxChunks>, a);
+  }
   return check_launch("hc_finish_kernel");
 }
 
@@ -405,10 +564,15 @@ extern "C" int glm53_rms_norm(const void* x, int64_t T, int64_t H, const void* w
     set_last_error("glm53_rms_norm: x, weight and out must be non-NULL and 16-byte aligned");
     return GLM53_ERR_INVALID;
   }
-  HcFinishArgs a{(const uint16_t*)x, nullptr, 0, H, nullptr, nullptr, 0, 0.0f, 0.0f, (const uint16_t*)weight, eps,
-                 nullptr, (uint16_t*)out, nullptr, nullptr};
-  hc_finish_kernel<false><<<(unsigned)T, kHcFinishThreads, 0, (cudaStream_t)stream>>>(a);
-  return check_launch("hc_finish_kernel<rms_norm>");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (H <= 2 * 8 * kHcFinishThreads)
+    rms_norm_kernel<2><<<(unsigned)T, kHcFinishThreads, 0, st>>>((const uint16_t*)x, H, (const uint16_t*)weight, eps,
+                                                                 (uint16_t*)out);
+  else
+    rms_norm_kernel<kHcMaxChunks><<<(unsigned)T, kHcFinishThreads, 0, st>>>((const uint16_t*)x, H,
+                                                                            (const uint16_t*)weight, eps,
+                                                                            (uint16_t*)out);
+  return check_launch("rms_norm_kernel");
 }
 
 extern "C" int glm53_hc_expand(const void* moe, const void* residual, const float* post, const float* comb,

@@ -5,15 +5,18 @@ CPU tests pin the oracle against an independent float64 numpy restatement and
 known answers; GPU tests (-m gpu) compare the sm_100a kernels with the oracle.
 Tolerances: the hc expand is bit-exact (same FMA chain, same inputs);
 ``post``/``comb`` within atol 1e-5 + rtol 1e-5 (FP32 mixing sums over 4H
-terms in another order); collapsed within 1 BF16 ulp and normalized within 2
-(one ulp of the collapse can move the norm by one more), cosine >= 0.9999.
+terms in another order).  ``collapsed`` = BF16(sum_b pre[b] x[b]) within one
+BF16 ulp plus 1e-5 * sum_b |x[b]| (a 1e-5 change of ``pre`` moves a sum that
+cancels by that much, i.e. by several ulps of a small result); collapsed and
+normalized also meet the layer bar (max(2e-2, 1 ulp), cosine >= 0.9999) with
+at least 99% of elements bit-identical.
 """
 
 import numpy as np
 import pytest
 import torch
 
-from gpu_util import bits, from_bits
+from gpu_util import assert_layer_close, bf16_ulp, bits, f32, from_bits
 
 H_CFG = 4096
 N_BR = 4
@@ -155,12 +158,6 @@ def _module(G, fn, scale, base, H, dev):
     return hc
 
 
-def _cos(a_bits, b_bits, oracle):
-    a = oracle.f32_from_bf16(a_bits).astype(np.float64).ravel()
-    b = oracle.f32_from_bf16(b_bits).astype(np.float64).ravel()
-    return float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b) + 1e-300))
-
-
 @pytest.mark.gpu
 @pytest.mark.parametrize("T,H", [(1, H_CFG), (3, H_CFG), (16, H_CFG), (37, H_CFG), (256, H_CFG),
                                  (2048, H_CFG), (5, 256), (2, 8192)])
@@ -177,9 +174,12 @@ def test_hc_collapse_norm_matches_oracle(oracle, T, H):
     torch.cuda.synchronize()
     np.testing.assert_allclose(post.cpu().numpy(), post_o, rtol=1e-5, atol=1e-5)
     np.testing.assert_allclose(comb.cpu().numpy(), comb_o, rtol=1e-5, atol=1e-5)
-    assert _ulps(bits(col), col_o).max() <= 1
-    assert _ulps(bits(nor), nor_o).max() <= 2
-    assert _cos(bits(nor), nor_o, oracle) >= 0.9999
+    g, r = f32(bits(col)), f32(col_o)
+    scale_x = np.abs(f32(state)).sum(1)
+    assert (np.abs(g - r) <= bf16_ulp(r) + 1e-5 * scale_x).all()
+    for gpu_bits, ref_bits in ((bits(col), col_o), (bits(nor), nor_o)):
+        stats = assert_layer_close(gpu_bits, ref_bits)
+        assert stats["bit_identical"] >= 0.99, stats
     # the module call without the norm returns the same collapse
     col2, post2, comb2 = hc(from_bits(state, dev))
     assert torch.equal(col2, col) and torch.equal(post2, post) and torch.equal(comb2, comb)
