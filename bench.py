@@ -764,9 +764,45 @@ def bench_hc(dev, args):
             "expand_hbm_frac": round(e_bytes / (e_ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
         }
         del fns, states, moes, outs, ws
+    if 256 in (int(v) for v in args.hc_tokens.split(",")):
+        res["post_attention_q256"] = bench_dsa_output(dev, stream, peaks)
     res["note"] = ("glm53_hc_collapse_norm (hc_mix_kernel + hc_finish_kernel) and glm53_hc_expand, each timed "
                    "alone in CUDA graphs of one call per input set; fraction of measured HBM copy bandwidth")
     return res
+
+
+def bench_dsa_output(dev, stream, peaks):
+    """The reference's post-attention seam at its geometry (Q256: 64 heads x 256
+    rows x 256 values, o_proj [4096, 16384], 4 branches): head-major layout,
+    block-FP8 o_proj (tcgen05 GEMM) and hc expand, through
+    DSAOutputProjection.execute_hc; four weight sets (256 MB) rotate past L2."""
+    import torch
+
+    import glm53_flash_mlx_b200 as G
+    from glm53_flash_mlx_b200 import synthetic as S
+
+    heads, rows, dim, hidden, sets = 64, 256, 256, 4096, 4
+    weights = [S.random_block_fp8(hidden, heads * dim, seed=8000 + i, device=dev) for i in range(sets)]
+    hms = [S.random_bf16((heads, rows, dim), seed=8100 + i, device=dev) for i in range(sets)]
+    residual = S.random_bf16((rows, 4, hidden), seed=8200, device=dev)
+    post = torch.rand((rows, 4), generator=torch.Generator(device=dev).manual_seed(1), device=dev) * 2
+    comb = torch.rand((rows, 4, 4), generator=torch.Generator(device=dev).manual_seed(2), device=dev)
+    plan = G.DSAOutputProjection()
+
+    def step(i, s):
+        w, sc = weights[i % sets]
+        plan.execute_hc(hms[i % sets], w, sc, residual, post, comb)
+
+    ms = time_stage_graph(step, sets, 10, stream, dev)
+    flops = 2 * rows * hidden * heads * dim
+    bytes_ = hidden * heads * dim + rows * heads * dim * 2 * 3 + rows * hidden * 2 * 10
+    del weights, hms
+    return {"us": round(ms * 1e3, 2), "flops": flops, "tflops": round(flops / (ms / 1e3) / 1e12, 1),
+            "bf16_frac": round(flops / (ms / 1e3) / 1e12 / peaks["bf16_tflops"], 4), "algorithmic_bytes": bytes_,
+            "reference_m3ultra_ms": 25.45,
+            "note": "head-major layout + o_proj + hc expand (DSAOutputProjection.execute_hc), 3 launches + the "
+                    "GEMM's activation conversion; reference_m3ultra_ms = the reference's native plan on its "
+                    "M3 Ultra (bench-results/m3ultra512-native-prefill-post-attention-hc-20260909.json)"}
 
 
 # ---------------------------------------------------------------------------

@@ -34,3 +34,4 @@ from .grouped_fp8 import (  # noqa: F401
 from .packed import PackedFP8ExpertBank, PackedFP8MoE, packed_decode_moe  # noqa: F401
 from .router import Float32Gate, router_topk  # noqa: F401
 from .hyper_connection import FFNBoundary, HyperConnection, RMSNorm, hc_expand, rms_norm  # noqa: F401
+from .dsa_output import DSAOutputProjection, head_major_to_rows  # noqa: F401

@@ -135,6 +135,7 @@ SIGNATURES: dict[str, tuple] = {
     ),
     "glm53_rms_norm": (_int, [_vp, _i64, _i64, _vp, _f, _vp, _vp]),
     "glm53_hc_expand": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _int, _vp, _vp]),
+    "glm53_head_major_to_rows": (_int, [_vp, _i64, _i64, _i64, _vp, _vp]),
 }
 
 

@@ -540,6 +540,15 @@ int glm53_hc_expand(const void* moe, const void* residual, const float* post,
                     const float* comb, int64_t T, int64_t H, int branches,
                     void* out, void* stream);
 
+/* Sparse-attention output layout: head_major BF16 [heads, rows, dim] ->
+ * row_major BF16 [rows, heads * dim] (a pure copy; dim a multiple of 8,
+ * 16-byte aligned tensors), the o_proj input.  Replaces
+ * glm53_native_prefill_dsa_head_to_row_bfloat16
+ * (native_execution/native_indexer_plan.metal:2290-2304) of
+ * NativePrefillDSAOutputPlan::execute (native_prefill_dsa_output_plan.cpp:68-106). */
+int glm53_head_major_to_rows(const void* head_major, int64_t heads, int64_t rows,
+                             int64_t dim, void* row_major, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -39,6 +39,7 @@ __all__ = [
     "hc_collapse_norm",
     "rms_norm",
     "hc_expand",
+    "head_major_to_rows",
 ]
 
 _HERE = Path(__file__).resolve().parent
@@ -479,3 +480,18 @@ def hc_expand(moe_bits, residual_bits, post, comb) -> np.ndarray:
     oracle_lib().orc_hc_expand(_p(moe, _u16), _p(residual, _u16), _p(post, _f32), _p(comb, _f32),
                                T, H, _p(out, _u16))
     return out
+
+
+def head_major_to_rows(head_major_bits) -> np.ndarray:
+    """[heads, rows, dim] -> [rows, heads * dim]: the index map of
+    glm53_native_prefill_dsa_head_to_row_bfloat16
+    (native_execution/native_indexer_plan.metal:2290-2304), position
+    (head, row, d) -> row_major[(row * heads + head) * dim + d]."""
+    hm = np.asarray(head_major_bits)
+    heads, rows, dim = hm.shape
+    out = np.empty(rows * heads * dim, dtype=hm.dtype)
+    for head in range(heads):
+        for row in range(rows):
+            start = (row * heads + head) * dim
+            out[start:start + dim] = hm[head, row]
+    return out.reshape(rows, heads * dim)
