@@ -14,7 +14,8 @@
 //                      token (24 outputs) and the token's sum of squares,
 //                      split over K: BF16 mma.sync m16n8k16 with FP32
 //                      accumulation, 16 tokens x 24 outputs per CTA, each
-//                      lane streaming 16-byte runs of the state and of fn;
+//                      lane streaming 16-byte runs of the state and of fn
+//                      (through a per-warp cp.async ring for one tile);
 //                      partial sums to caller workspace [T][ksplit][25].
 //   hc_finish_*        sums the partials in a fixed order, r = 1/sqrt(mean(x^2)
 //                      + eps), pre/post by sigmoid, comb by softmax + Sinkhorn
@@ -26,6 +27,7 @@
 // Expand (one launch): one thread per 8 hidden columns of a token writes all
 //   4 branches, so each residual run is read once and used 4 times.
 #include "common.cuh"
+#include "gemv_tile.cuh"
 
 namespace glm53 {
 namespace {
@@ -38,6 +40,8 @@ constexpr int kHcMixThreads = 128;
 constexpr int kHcFinishThreads = 256;
 constexpr int kHcMaxChunks = 4;  // 8-column chunks per finish thread: H <= 8192
 constexpr int kHcMaxSplit = 64;
+constexpr int kHcStages = 4;  // cp.async ring depth of a mix warp, in 32-column K blocks
+constexpr int kHcPieces = 5;  // 16-byte pieces per lane per K block: 2 state rows + 3 fn rows
 
 __device__ __forceinline__ void mma_bf16_16816(float c[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                                uint32_t b0, uint32_t b1) {
@@ -60,6 +64,97 @@ __device__ __forceinline__ float sq_sum8(uint4 v) {
   return s;
 }
 
+// One token tile (T <= 16, decode): the mixing projection through a per-warp
+// cp.async ring.  Grid (1, ksplit), 4 warps.  Warp w of split y takes a
+// contiguous run of 32-column K blocks (the (4y + w)-th of 4*ksplit equal
+// runs), so consecutive copies stay in one DRAM page of each row.  Lane (g = lane/4,
+// q = lane%4) copies 8 consecutive K values of token rows g and g+8 and of fn
+// rows g, g+8, g+16 per block into its own slots of a per-warp cp.async ring
+// kHcStages blocks deep (bytes in flight cost no registers) and reads back
+// exactly what it copied, so the ring needs no barrier.  Two k16 MMA steps
+// use values 0-3 and 4-7 of each run: the MMA sums over its 16 K positions in
+// any pairing of A and B that agrees, and both operands use the same one
+// (logical k = 2q+e <- 8q+e and 2q+8+e <- 8q+2+e in the first step, +4 in the
+// second).
+__global__ void __launch_bounds__(kHcMixThreads) hc_mix_ring_kernel(const uint16_t* __restrict__ state,
+                                                                const uint16_t* __restrict__ fn, int64_t T,
+                                                                int64_t K, int ksplit, float* __restrict__ part) {
+  __shared__ uint4 ring[kHcMixThreads / 32][kHcStages][32][kHcPieces];
+  __shared__ float red[kHcMixThreads / 32][kHcTileTokens][kHcPart];
+  // The finish kernel is this grid's programmatic dependent: it may start
+  // (and load the state) now; it reads the partial sums after griddepcontrol.wait.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const int64_t t0 = (int64_t)blockIdx.x * kHcTileTokens;
+  const bool ok0 = t0 + g < T, ok1 = t0 + g + 8 < T;
+  const uint16_t* src[kHcPieces] = {state + (ok0 ? (t0 + g) * K : 0) + q * 8,
+                                    state + (ok1 ? (t0 + g + 8) * K : 0) + q * 8, fn + (int64_t)g * K + q * 8,
+                                    fn + (int64_t)(g + 8) * K + q * 8, fn + (int64_t)(g + 16) * K + q * 8};
+  const bool valid[kHcPieces] = {ok0, ok1, true, true, true};
+  const int64_t nkb = K / 32;
+  const int64_t warps = (int64_t)ksplit * (kHcMixThreads / 32);
+  const int64_t per = (nkb + warps - 1) / warps;
+  const int64_t kb_begin = ((int64_t)blockIdx.y * (kHcMixThreads / 32) + warp) * per;
+  const int64_t kb_end = kb_begin + per < nkb ? kb_begin + per : nkb;
+  const int64_t n = kb_end > kb_begin ? kb_end - kb_begin : 0;
+  uint4 (*slots)[32][kHcPieces] = ring[warp];
+  // Copy K block kb_begin + i into slot i % kHcStages (zeros past the run).
+  auto issue = [&](int64_t i) {
+    const bool in = i < n;
+    const int64_t k = in ? (kb_begin + i) * 32 : 0;
+#pragma unroll
+    for (int p = 0; p < kHcPieces; ++p)
+      cp_async_16(&slots[i % kHcStages][lane][p], src[p] + k, in && valid[p]);
+    cp_async_commit_group();
+  };
+  float acc[3][4];
+#pragma unroll
+  for (int j = 0; j < 3; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
+  float sq0 = 0.0f, sq1 = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kHcStages - 1; ++i) issue(i);
+  for (int64_t i = 0; i < n; ++i) {
+    issue(i + kHcStages - 1);
+    cp_async_wait_group<kHcStages - 1>();
+    const uint4* r = slots[i % kHcStages][lane];
+    const uint4 a0 = r[0], a1 = r[1], b0 = r[2], b1 = r[3], b2 = r[4];
+    sq0 += sq_sum8(a0);
+    sq1 += sq_sum8(a1);
+    mma_bf16_16816(acc[0], a0.x, a1.x, a0.y, a1.y, b0.x, b0.y);
+    mma_bf16_16816(acc[0], a0.z, a1.z, a0.w, a1.w, b0.z, b0.w);
+    mma_bf16_16816(acc[1], a0.x, a1.x, a0.y, a1.y, b1.x, b1.y);
+    mma_bf16_16816(acc[1], a0.z, a1.z, a0.w, a1.w, b1.z, b1.w);
+    mma_bf16_16816(acc[2], a0.x, a1.x, a0.y, a1.y, b2.x, b2.y);
+    mma_bf16_16816(acc[2], a0.z, a1.z, a0.w, a1.w, b2.z, b2.w);
+  }
+  cp_async_wait_group<0>();
+  sq0 += __shfl_xor_sync(0xffffffffu, sq0, 1);
+  sq0 += __shfl_xor_sync(0xffffffffu, sq0, 2);
+  sq1 += __shfl_xor_sync(0xffffffffu, sq1, 1);
+  sq1 += __shfl_xor_sync(0xffffffffu, sq1, 2);
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    red[warp][g][8 * j + 2 * q] = acc[j][0];
+    red[warp][g][8 * j + 2 * q + 1] = acc[j][1];
+    red[warp][g + 8][8 * j + 2 * q] = acc[j][2];
+    red[warp][g + 8][8 * j + 2 * q + 1] = acc[j][3];
+  }
+  if (q == 0) {
+    red[warp][g][kHcMix] = sq0;
+    red[warp][g + 8][kHcMix] = sq1;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < kHcTileTokens * kHcPart; i += kHcMixThreads) {
+    const int r = i / kHcPart, c = i % kHcPart;
+    if (t0 + r >= T) continue;
+    const float v = ((red[0][r][c] + red[1][r][c]) + red[2][r][c]) + red[3][r][c];
+    part[((t0 + r) * ksplit + blockIdx.y) * kHcPart + c] = v;
+  }
+}
+
+// More than one token tile: the same work with each lane loading its 16-byte
+// runs into registers (measured faster than the ring at T = 256 and 2048).
 // Grid (ceil(T/16), ksplit), 4 warps.  Warp w of split y takes a contiguous
 // run of 32-column K blocks (the (4y + w)-th of 4*ksplit equal runs), so
 // consecutive loads of a lane stay in one DRAM page of each row.  Lane (g = lane/4, q = lane%4)
@@ -523,7 +618,11 @@ extern "C" int glm53_hc_collapse_norm(const void* state, int64_t T, int64_t H, i
   const int64_t K = kHcBranches * H;
   float* part = static_cast<float*>(workspace);
   dim3 grid((unsigned)((T + kHcTileTokens - 1) / kHcTileTokens), (unsigned)ksplit);
-  hc_mix_kernel<<<grid, kHcMixThreads, 0, st>>>((const uint16_t*)state, (const uint16_t*)hc_fn, T, K, ksplit, part);
+  if (T <= kHcTileTokens)
+    hc_mix_ring_kernel<<<grid, kHcMixThreads, 0, st>>>((const uint16_t*)state, (const uint16_t*)hc_fn, T, K, ksplit,
+                                                       part);
+  else
+    hc_mix_kernel<<<grid, kHcMixThreads, 0, st>>>((const uint16_t*)state, (const uint16_t*)hc_fn, T, K, ksplit, part);
   int rc = check_launch("hc_mix_kernel");
   if (rc) return rc;
   HcFinishArgs a{(const uint16_t*)state, part, ksplit, T, H, hc_scale, hc_base, sinkhorn_iters, hc_eps,
