@@ -22,7 +22,8 @@
 //                      on 16 lanes of a warp (row sums by lane shuffles within
 //                      a row group, column sums across groups), collapsed =
 //                      BF16(sum_b pre[b] x[b]) in registers, then the RMSNorm
-//                      of the collapsed row.  One CTA per token for small T;
+//                      of the collapsed row.  One CTA per token for small T
+//                      (a ninth warp runs the Sinkhorn beside the collapse);
 //                      eight tokens per CTA (one Sinkhorn per warp) for large T.
 // Expand (one launch): one thread per 8 hidden columns of a token writes all
 //   4 branches, so each residual run is read once and used 4 times.
@@ -38,6 +39,7 @@ constexpr int kHcPart = kHcMix + 1;                      // + sum of squares
 constexpr int kHcTileTokens = 16;
 constexpr int kHcMixThreads = 128;
 constexpr int kHcFinishThreads = 256;
+constexpr int kHcTokenThreads = kHcFinishThreads + 32;  // + the coefficient warp
 constexpr int kHcMaxChunks = 4;  // 8-column chunks per finish thread: H <= 8192
 constexpr int kHcMaxSplit = 64;
 constexpr int kHcStages = 4;  // cp.async ring depth of a mix warp, in 32-column K blocks
@@ -274,21 +276,26 @@ struct HcFinishArgs {
   float* comb;
 };
 
-// One warp: pre, post and comb of token t from its 25 reduced sums mix[]
-// (shared memory, visible to the warp).  pre goes to pre_out[0..3].  Lane
-// l < 16 holds comb[i = l/4][j = l%4]; lanes 16-31 mirror the arithmetic on a
-// copy so every shuffle has all 32 lanes.
-__device__ __forceinline__ void hc_coefficients(const HcFinishArgs& a, int64_t t, const float* mix,
-                                                float* pre_out) {
+// One warp, token t, from its 25 reduced sums mix[] (shared memory, visible
+// to the warp): lanes 0-3 write pre[b] to pre_out and post[b] to global memory.
+__device__ __forceinline__ void hc_pre_post(const HcFinishArgs& a, int64_t t, const float* mix, float* pre_out) {
+  const int l = threadIdx.x & 31;
+  if (l >= kHcBranches) return;
+  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(mix[kHcMix], (float)(kHcBranches * a.H)),
+                                                    a.norm_eps)));
+  const float zp = __fadd_rn(__fmul_rn(__fmul_rn(mix[l], r), a.scale[0]), a.base[l]);
+  pre_out[l] = __fadd_rn(sigmoid_f32(zp), a.eps);
+  const float zq = __fadd_rn(__fmul_rn(__fmul_rn(mix[kHcBranches + l], r), a.scale[1]), a.base[kHcBranches + l]);
+  a.post[t * kHcBranches + l] = __fmul_rn(2.0f, sigmoid_f32(zq));
+}
+
+// One whole warp, token t: comb by softmax + Sinkhorn.  Lane l < 16 holds
+// comb[i = l/4][j = l%4]; lanes 16-31 mirror the arithmetic on a copy so every
+// shuffle has all 32 lanes.
+__device__ __forceinline__ void hc_comb(const HcFinishArgs& a, int64_t t, const float* mix) {
   const int l = threadIdx.x & 31;
   const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(mix[kHcMix], (float)(kHcBranches * a.H)),
                                                     a.norm_eps)));
-  if (l < kHcBranches) {
-    const float zp = __fadd_rn(__fmul_rn(__fmul_rn(mix[l], r), a.scale[0]), a.base[l]);
-    pre_out[l] = __fadd_rn(sigmoid_f32(zp), a.eps);
-    const float zq = __fadd_rn(__fmul_rn(__fmul_rn(mix[kHcBranches + l], r), a.scale[1]), a.base[kHcBranches + l]);
-    a.post[t * kHcBranches + l] = __fmul_rn(2.0f, sigmoid_f32(zq));
-  }
   const int li = l & 15;
   const float z = __fadd_rn(__fmul_rn(__fmul_rn(mix[2 * kHcBranches + li], r), a.scale[2]),
                             a.base[2 * kHcBranches + li]);
@@ -301,6 +308,12 @@ __device__ __forceinline__ void hc_coefficients(const HcFinishArgs& a, int64_t t
     c = __fdiv_rn(c, __fadd_rn(group4_sum(c, 4), a.eps));
   }
   if (l < 16) a.comb[t * 16 + l] = c;
+}
+
+__device__ __forceinline__ void hc_coefficients(const HcFinishArgs& a, int64_t t, const float* mix,
+                                                float* pre_out) {
+  hc_pre_post(a, t, mix, pre_out);
+  hc_comb(a, t, mix);
 }
 
 // The four branch runs of 8 columns at chunk c of token t.
@@ -345,24 +358,41 @@ __device__ __forceinline__ float rms_inv(float sumsq, int64_t H, float eps) {
   return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sumsq, (float)H), eps)));
 }
 
-// Small T: one CTA per token.  Each thread issues the loads of its state
-// chunks first, so they are in flight while the 25 sums are reduced (8 groups
-// of splits g, g+8, ... in parallel, then the groups in order) and warp 0 runs
-// the Sinkhorn iterations; then all threads collapse and normalise the row.
+// Sum over the 256 collapse threads of a token CTA (warps 0-7), on named
+// barrier 1 so that the coefficient warp (warp 8) is not waited for.
+__device__ __forceinline__ float collapse_warps_sum(float v, float* scratch) {
+  v = warp_sum(v);
+  if ((threadIdx.x & 31) == 0) scratch[threadIdx.x >> 5] = v;
+  asm volatile("bar.sync 1, %0;" ::"n"(kHcFinishThreads) : "memory");
+  float s = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kHcFinishThreads / 32; ++w) s += scratch[w];
+  return s;
+}
+
+// Small T: one CTA per token, 8 collapse warps + 1 coefficient warp.  The
+// collapse threads issue the loads of their state chunks first; the 25 sums
+// are reduced (8 groups of splits g, g+8, ... in parallel, then the groups in
+// order); the coefficient warp computes pre and post, then runs the Sinkhorn
+// iterations for comb while warps 0-7 collapse and normalise the row (which
+// need only pre).  Barrier 0 is last used before that split.
 template <int MAXC>
-__global__ void __launch_bounds__(kHcFinishThreads) hc_finish_token_kernel(HcFinishArgs a) {
+__global__ void __launch_bounds__(kHcTokenThreads) hc_finish_token_kernel(HcFinishArgs a) {
   __shared__ float s_red[8][kHcPart];
   __shared__ float s_mix[kHcPart];
   __shared__ float s_pre[kHcBranches];
   __shared__ float s_sum[kHcFinishThreads / 32];
   const int64_t t = blockIdx.x;
   const int tid = threadIdx.x;
+  const bool coef_warp = tid >= kHcFinishThreads;
   const int nchunks = (int)(a.H / 8);
   uint4 xv[MAXC][kHcBranches];
+  if (!coef_warp) {
 #pragma unroll
-  for (int i = 0; i < MAXC; ++i) {
-    const int c = tid + i * kHcFinishThreads;
-    if (c < nchunks) load_branches(a, t, c, xv[i]);
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = tid + i * kHcFinishThreads;
+      if (c < nchunks) load_branches(a, t, c, xv[i]);
+    }
   }
   asm volatile("griddepcontrol.wait;" ::: "memory");  // the mix kernel's partial sums
   if (tid < 8 * kHcPart) {
@@ -387,8 +417,12 @@ __global__ void __launch_bounds__(kHcFinishThreads) hc_finish_token_kernel(HcFin
     s_mix[tid] = acc;
   }
   __syncthreads();
-  if (tid < 32) hc_coefficients(a, t, s_mix, s_pre);
+  if (coef_warp) hc_pre_post(a, t, s_mix, s_pre);
   __syncthreads();
+  if (coef_warp) {
+    hc_comb(a, t, s_mix);
+    return;
+  }
   uint4 cv[MAXC];
   float ss = 0.0f;
 #pragma unroll
@@ -400,7 +434,7 @@ __global__ void __launch_bounds__(kHcFinishThreads) hc_finish_token_kernel(HcFin
     ss += sq_sum8(cv[i]);
   }
   if (a.norm_w == nullptr) return;
-  const float inv = rms_inv(block_sum_256(ss, s_sum), a.H, a.rms_eps);
+  const float inv = rms_inv(collapse_warps_sum(ss, s_sum), a.H, a.rms_eps);
 #pragma unroll
   for (int i = 0; i < MAXC; ++i) {
     const int c = tid + i * kHcFinishThreads;
@@ -643,9 +677,11 @@ extern "C" int glm53_hc_collapse_norm(const void* state, int64_t T, int64_t H, i
     cudaLaunchKernelEx(&cfg, hc_finish_group_kernel, a);
   } else if (H <= 2 * 8 * kHcFinishThreads) {
     cfg.gridDim = dim3((unsigned)T);
+    cfg.blockDim = dim3(kHcTokenThreads);
     cudaLaunchKernelEx(&cfg, hc_finish_token_kernel<2>, a);
   } else {
     cfg.gridDim = dim3((unsigned)T);
+    cfg.blockDim = dim3(kHcTokenThreads);
     cudaLaunchKernelEx(&cfg, hc_finish_token_kernel<kHcMaxChunks>, a);
   }
   return check_launch("hc_finish_kernel");
