@@ -766,9 +766,41 @@ def bench_hc(dev, args):
         del fns, states, moes, outs, ws
     if 256 in (int(v) for v in args.hc_tokens.split(",")):
         res["post_attention_q256"] = bench_dsa_output(dev, stream, peaks)
+        res["T256"]["reference_m3ultra_ms"] = {"ffn_hc_collapse": 0.435, "post_attention_norm": 0.2255}
+        if not args.no_cpu:
+            res["cpu_oracle_T256"] = cpu_hc(256)
     res["note"] = ("glm53_hc_collapse_norm (hc_mix_kernel + hc_finish_kernel) and glm53_hc_expand, each timed "
                    "alone in CUDA graphs of one call per input set; fraction of measured HBM copy bandwidth")
     return res
+
+
+def cpu_hc(T: int) -> dict:
+    """The CPU restatement (oracle port) of the collapse + RMSNorm and of the hc
+    expand on seeded inputs of T tokens, all host threads, a few repetitions."""
+    import oracle as O
+
+    rng = np.random.default_rng(9)
+    K = 4 * H
+    state = O.bf16_from_f32(rng.standard_normal((T, 4, H)).astype(np.float32))
+    fn = O.bf16_from_f32((rng.standard_normal((24, K)) / np.sqrt(K)).astype(np.float32))
+    scale = np.array([1.0, 0.8, 1.5], np.float32)
+    base = (rng.standard_normal(24) * 0.5).astype(np.float32)
+    norm_w = O.bf16_from_f32((1 + 0.1 * rng.standard_normal(H)).astype(np.float32))
+    moe = O.bf16_from_f32(rng.standard_normal((T, H)).astype(np.float32))
+    threads = O.default_threads()
+    O.hc_collapse_norm(state[:1], fn, scale, base, norm_w, threads=threads)  # warm
+    reps, t0 = 3, time.perf_counter()
+    for _ in range(reps):
+        _, _, post, comb, _ = O.hc_collapse_norm(state, fn, scale, base, norm_w, threads=threads)
+    c_s = (time.perf_counter() - t0) / reps
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        O.hc_expand(moe, state, post, comb)
+    e_s = (time.perf_counter() - t0) / reps
+    return {"collapse_norm_us": round(c_s * 1e6, 1), "expand_us": round(e_s * 1e6, 1), "cores": threads,
+            "expand_cores": 1, "kind": "port",
+            "sample": f"T = {T}: collapse + norm on {threads} host threads (double-precision dot products), "
+                      f"expand single-threaded, mean of {reps}"}
 
 
 def bench_dsa_output(dev, stream, peaks):
