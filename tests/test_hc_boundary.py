@@ -262,3 +262,38 @@ def test_hc_rejects_bad_geometry():
     big = G.HyperConnection(16384, device=dev)
     with pytest.raises(ValueError, match="not supported"):
         big(torch.zeros((1, 4, 16384), dtype=torch.bfloat16, device=dev))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("T", [1, 2048])
+def test_hc_calls_replay_bitwise_in_a_cuda_graph(T):
+    """The collapse (mix kernel + its programmatic-dependent finish kernel) and
+    the expand captured in one CUDA graph give the eager results bit for bit,
+    on fresh inputs copied into the captured buffers."""
+    import glm53_flash_mlx_b200 as G
+
+    dev = torch.device("cuda:0")
+    state, fn, scale, base, norm_w = _inputs(T, H_CFG, 300 + T)
+    hc = _module(G, fn, scale, base, H_CFG, dev)
+    norm = G.RMSNorm(H_CFG, device=dev)
+    norm.weight.copy_(from_bits(norm_w, dev))
+    st = from_bits(state, dev)
+    moe = torch.randn((T, H_CFG), device=dev).to(torch.bfloat16)
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        hc.collapse_norm(st, norm)  # eager call first: workspace allocation
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        _, g_nor, g_post, g_comb = hc.collapse_norm(st, norm)
+        g_out = G.hc_expand(moe, st, g_post, g_comb)
+    st2, _, _, _, _ = _inputs(T, H_CFG, 400 + T)
+    st.copy_(from_bits(st2, dev))
+    graph.replay()
+    torch.cuda.synchronize()
+    _, nor, post, comb = hc.collapse_norm(st, norm)
+    out = G.hc_expand(moe, st, post, comb)
+    torch.cuda.synchronize()
+    assert torch.equal(g_nor, nor) and torch.equal(g_post, post) and torch.equal(g_comb, comb)
+    assert torch.equal(g_out, out)
+    del graph
