@@ -10,15 +10,27 @@ seeded layers (8 x 5.44 GB of experts, far above the 126 MB L2) and a pool of
 64 activation vectors, so every step streams its weights from HBM; no L2 flush
 is needed.  Steps are CUDA-graph captured; `value` = steps / device time.
 
-`e2e` runs the same steps through the public module API
-(`PackedFP8MoE(bank, config, Float32Gate, shared)(x)`), copying each token from
-pinned host memory and the result back inside the timed region.
+`e2e` runs the same steps through `PackedFP8MoE.capture_decode()`: one
+`PackedDecodeStep` call per token (one library call: a kernel reads the pinned
+host input row, the Float32Gate router, the packed decode writing the pinned
+host output row), with both host copies inside the timed region.
+`e2e_module` times the plain module call the reference's decode makes
+(`layer.mlp(x)` -> `PackedFP8MoE.__call__`, glm53_flash_mlx/packed.py:896),
+with the input copied from pinned host memory and the result copied back.
+
+Before the warm-up every captured graph is replayed once, and the same step
+graph is replayed for about half a second so that the clock sampler sees the
+GPU under this load; `clocks` covers that settle phase, the warm-up and the
+timed region (`timed_samples` counts the samples inside the timed region).
 
 `--impl reference` times the CPU restatement of the reference kernels (the
 reference's MLX/Metal path cannot run off Apple hardware) on all host cores.
 
-Multi-GPU (torchrun, N>1): replicas only -- every rank runs its own layers,
-no collective on the data path; value = total tokens / max-over-ranks time.
+Multi-GPU (torchrun, N>1): expert-parallel decode -- rank r holds experts
+[r*288/N, (r+1)*288/N) of every layer, each step routes `--ep-batch` tokens
+per rank, dispatches them to the experts' owners over NVLink peer memory (or
+NCCL all-to-all with --ep-transport nccl), decodes and combines at home;
+value = total tokens / max-over-ranks device time.
 """
 
 from __future__ import annotations
@@ -171,6 +183,37 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
                 "reasons": sorted(reasons), "samples": len(sm)}
 
+    def window(self, t_settle: float, t0: float, t1: float) -> dict:
+        """Clocks over the settle phase, the warm-up and the timed region
+        (t_settle..t1), with the count of samples inside the timed region."""
+        d = self.summary(t_settle, t1)
+        d["timed_samples"] = self.summary(t0, t1)["samples"]
+        d["window"] = "settle (~0.5 s of the timed step graph) + warm-up + timed region"
+        return d
+
+
+def settle_clocks(graph, world: int, seconds: float = 0.5) -> float:
+    """Replay `graph` (the timed step graph) for about `seconds` before the
+    warm-up so that the 200 ms clock sampler sees the GPU under this load
+    even when the timed region is a millisecond; returns the host time the
+    settle phase started."""
+    import math
+
+    import torch
+
+    barrier(world)
+    t0 = time.monotonic()
+    graph.replay()
+    torch.cuda.synchronize()
+    one = max(time.monotonic() - t0, 1e-5)
+    # every rank replays the same number of times (the graphs may hold
+    # collectives or peer handshakes)
+    n = int(max_over_ranks(float(math.ceil(seconds / one)), world))
+    for _ in range(min(n, 100000)):
+        graph.replay()
+    torch.cuda.synchronize()
+    return t0
+
 
 def measured_peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
@@ -302,6 +345,10 @@ def bench_b200(args, world, rank, local):
     rem_w, rem_t = args.warmup % GRAPH_STEPS, args.steps % GRAPH_STEPS
     rem = {n: capture(n) for n in {rem_w, rem_t} if n}
     torch.cuda.synchronize()
+    # every graph's first launch (its upload) happens here, outside the timing
+    for g in (full, *rem.values()):
+        g.replay()
+    torch.cuda.synchronize()
 
     def run(k):
         for _ in range(k // GRAPH_STEPS):
@@ -311,6 +358,7 @@ def bench_b200(args, world, rank, local):
 
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(torch.cuda.current_device()) as clocks:
+        hs = settle_clocks(full, world)
         run(args.warmup)
         torch.cuda.synchronize()
         barrier(world)
@@ -324,7 +372,7 @@ def bench_b200(args, world, rank, local):
     t_ms = max_over_ranks(start.elapsed_time(stop), world)
     if int(status.item()) != 0:
         raise RuntimeError(f"device status 0x{int(status.item()):x} during the timed region")
-    clk = clocks.summary(h0, h1)
+    clk = clocks.window(hs, h0, h1)
     tokens = args.steps * world
     value = tokens / (t_ms / 1e3)
 
@@ -360,7 +408,7 @@ def bench_b200(args, world, rank, local):
                 "step_frac": round(STEP_BYTES / (t_ms / args.steps / 1e3) / 1e9 / peaks["hbm_gbs"], 4)}
 
     # ---- e2e through the public module API -------------------------------
-    e2e = None
+    e2e = e2e_module = None
     if not args.no_e2e:
         mods = []
         for L in layers:
@@ -389,12 +437,39 @@ def bench_b200(args, world, rank, local):
                "api": "PackedFP8MoE.capture_decode() step per token: one glm53_decode_step_host call (a kernel "
                       "reads the pinned host input row, Float32Gate router, packed decode writing the pinned host "
                       "output row)"}
+        for c in caps:
+            c.check()
         del caps
+        # the plain module call (layer.mlp(x) -> PackedFP8MoE.__call__), with
+        # the row copied in from pinned host memory and the result copied back
+        n_mod = args.steps
+        for i in range(min(args.warmup, 200)):
+            y = mods[i % args.layers](x_host[i % POOL].to(dev, non_blocking=True))
+            y_host[i % POOL].copy_(y, non_blocking=True)
+        torch.cuda.synchronize()
+        barrier(world)
+        m_start, m_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        m_start.record()
+        for i in range(n_mod):
+            y = mods[i % args.layers](x_host[i % POOL].to(dev, non_blocking=True))
+            y_host[i % POOL].copy_(y, non_blocking=True)
+        m_stop.record()
+        torch.cuda.synchronize()
+        barrier(world)
+        for m in mods:
+            m.check_status()
+        m_ms = max_over_ranks(m_start.elapsed_time(m_stop), world)
+        e2e_module = {"value": round(n_mod * world / (m_ms / 1e3), 2), "unit": "tokens/s",
+                      "h2d_bytes_per_step": H * 2, "d2h_bytes_per_step": H * 2,
+                      "api": "PackedFP8MoE(bank, config, Float32Gate, shared)(x) per token (the reference's "
+                             "layer.mlp(x)), x copied from pinned host memory, result copied back"}
 
     step_us = t_ms / args.steps * 1e3
     extra = {"stages_us": {"router": round(router_ms * 1e3, 2), "gate_up": round(k_ms * 1e3, 2),
                            "down_and_boundaries": round(step_us - (router_ms + k_ms) * 1e3, 2),
                            "note": "router and gate/up each timed alone (64 calls per CUDA graph)"}}
+    if e2e_module is not None:
+        extra["e2e_module"] = e2e_module
     if not args.no_prefill:
         extra["prefill_2048"] = bench_prefill(layers, dev, args)
         extra["linear_config1_5"] = bench_linear(dev, args)
@@ -596,8 +671,14 @@ def bench_ep(args, world, rank, local):
 
     torch.cuda.synchronize()
     barrier(world)
+    if full is not None:  # every graph's first launch happens here, outside the timing
+        for g in (full, *rem.values()):
+            g.replay()
+    torch.cuda.synchronize()
+    barrier(world)
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(torch.cuda.current_device()) as clocks:
+        hs = settle_clocks(full, world) if full is not None else time.monotonic()
         run(args.warmup)
         torch.cuda.synchronize()
         barrier(world)
@@ -612,7 +693,7 @@ def bench_ep(args, world, rank, local):
     bad = max_over_ranks(float(max(int(p.status.item()) for p in plans)), world)
     if bad:
         raise RuntimeError(f"device status 0x{int(bad):x} during the timed region")
-    clk = clocks.summary(h0, h1)
+    clk = clocks.window(hs, h0, h1)
     tokens = args.steps * world
     value = tokens / (t_ms / 1e3)
     peaks = measured_peaks()
@@ -999,16 +1080,10 @@ def main():
         "e2e": res["e2e"],
         "gpu_launches": res["gpu_launches"],
     }
-    if "stages_us" in res:
-        line["stages_us"] = res["stages_us"]
-    if "prefill_2048" in res:
-        line["prefill_2048"] = res["prefill_2048"]
-    if "linear_config1_5" in res:
-        line["linear_config1_5"] = res["linear_config1_5"]
-    if "batched_decode" in res:
-        line["batched_decode"] = res["batched_decode"]
-    if "ffn_boundary" in res:
-        line["ffn_boundary"] = res["ffn_boundary"]
+    base = {"value", "t_ms", "clocks", "roofline", "e2e", "gpu_launches", "graph"}
+    for k, v in res.items():  # secondary measurements (stages, prefill, sweeps, batched, boundary)
+        if k not in base:
+            line[k] = v
     if rank == 0 and world == 1 and not args.no_cpu:
         import torch
 

@@ -128,6 +128,10 @@ SIGNATURES: dict[str, tuple] = {
     ),
     "glm53_sigmoid_bf16": (_int, [_vp, _i64, _vp, _vp]),
     "glm53_decode_step_host": (_int, [_vp, _vp, _vp, _vp]),
+    "glm53_status_mirror": (_int, [_vp, _vp, _vp]),
+    "glm53_packed_decode_workspace_layout": (_int, [_int, _i64, _i64, _i64, _vp]),
+    "glm53_grouped_moe_workspace_layout": (_int, [_i64, _int, _i64, _i64, _i64, _i64, _vp]),
+    "glm53_set_wait_limit_ns": (_int, [ctypes.c_ulonglong]),
     "glm53_hc_collapse_workspace_bytes": (_sz, [_i64, _i64]),
     "glm53_hc_collapse_norm": (
         _int,
@@ -153,7 +157,7 @@ class DecodeStepDesc(ctypes.Structure):
         ("x", _vp), ("expert_ids", _vp), ("scores", _vp), ("out", _vp),
         ("router_workspace", _vp), ("router_workspace_bytes", _sz),
         ("decode_workspace", _vp), ("decode_workspace_bytes", _sz),
-        ("status", _vp),
+        ("status", _vp), ("status_host", _vp),
     ]
 
 _lock = threading.Lock()

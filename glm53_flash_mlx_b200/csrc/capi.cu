@@ -1,5 +1,6 @@
 // Error plumbing, identity and small diagnostic entry points of the C ABI.
 #include <algorithm>
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
@@ -10,6 +11,11 @@
 namespace glm53 {
 
 static thread_local char g_last_error[512] = "";
+
+constexpr unsigned long long kDefaultWaitNs = 2000000000ull;
+static std::atomic<unsigned long long> g_wait_limit_ns{kDefaultWaitNs};
+
+unsigned long long ep_wait_limit_ns() { return g_wait_limit_ns.load(std::memory_order_relaxed); }
 
 void set_last_error(const char* fmt, ...) {
   va_list ap;
@@ -88,11 +94,20 @@ namespace glm53 {
 // 16-byte copy between device memory and pinned (device-mapped) host memory.
 // A programmatic dependent (the router of a host decode step) may launch at
 // once; it waits for this grid before it reads the copy.
+// With `status` and `mirror` set, thread 0 of block 0 also copies the device
+// status word into the mapped host word `mirror` (the work before this grid
+// on the stream has finished, so the word holds every earlier call's bits).
 __global__ void __launch_bounds__(256) copy16_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst,
-                                                     size_t n16) {
+                                                     size_t n16, const uint32_t* __restrict__ status,
+                                                     volatile uint32_t* mirror) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (mirror && blockIdx.x == 0 && threadIdx.x == 0) *mirror = *(const volatile uint32_t*)status;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (size_t)gridDim.x * blockDim.x)
     dst[i] = src[i];
+}
+
+__global__ void status_mirror_kernel(const uint32_t* __restrict__ status, volatile uint32_t* mirror) {
+  *mirror = *(const volatile uint32_t*)status;
 }
 
 void* mapped_host(const void* p) {
@@ -107,7 +122,8 @@ void* mapped_host(const void* p) {
 // Small host <-> device copy: a kernel over the pinned buffer's device
 // mapping (a copy-engine transfer of a few KB costs 7-10 us of stream time
 // on B200, the kernel about 2), else cudaMemcpyAsync.
-cudaError_t small_copy(void* dst, const void* src, size_t bytes, bool to_device, cudaStream_t st, bool* by_kernel) {
+cudaError_t small_copy(void* dst, const void* src, size_t bytes, bool to_device, cudaStream_t st, bool* by_kernel,
+                       const uint32_t* status, uint32_t* status_mirror) {
   const void* host = to_device ? src : dst;
   void* mapped = (bytes % 16 == 0 && ((uintptr_t)src | (uintptr_t)dst) % 16 == 0) ? mapped_host(host) : nullptr;
   if (by_kernel) *by_kernel = mapped != nullptr;
@@ -116,8 +132,19 @@ cudaError_t small_copy(void* dst, const void* src, size_t bytes, bool to_device,
   const size_t n16 = bytes / 16;
   const unsigned blocks = (unsigned)std::min<size_t>((n16 + 255) / 256, 64);
   copy16_kernel<<<blocks, 256, 0, st>>>((const uint4*)(to_device ? mapped : src),
-                                        (uint4*)(to_device ? dst : mapped), n16);
+                                        (uint4*)(to_device ? dst : mapped), n16, status,
+                                        status ? status_mirror : nullptr);
   return cudaGetLastError();
+}
+
+int mirror_status(const uint32_t* status, uint32_t* host_word, cudaStream_t st, const char* fn) {
+  void* mapped = (status && host_word && ((uintptr_t)host_word & 3) == 0) ? mapped_host(host_word) : nullptr;
+  if (!mapped) {
+    set_last_error("%s: the status mirror must be a 4-byte aligned word of pinned (device-mapped) host memory", fn);
+    return GLM53_ERR_INVALID;
+  }
+  status_mirror_kernel<<<1, 1, 0, st>>>(status, (volatile uint32_t*)mapped);
+  return check_launch(fn);
 }
 
 }  // namespace glm53
@@ -137,6 +164,19 @@ extern "C" int glm53_graph_step(void* graph_exec, const void* x_host, void* x_de
     return GLM53_ERR_CUDA;
   }
   return GLM53_OK;
+}
+
+extern "C" int glm53_set_wait_limit_ns(unsigned long long ns) {
+  if (ns != 0 && (ns < 1000000ull || ns > 60000000000ull)) {
+    set_last_error("glm53_set_wait_limit_ns: %llu ns is outside [1 ms, 60 s] (0 restores the default)", ns);
+    return GLM53_ERR_INVALID;
+  }
+  g_wait_limit_ns.store(ns ? ns : kDefaultWaitNs, std::memory_order_relaxed);
+  return GLM53_OK;
+}
+
+extern "C" int glm53_status_mirror(const uint32_t* status, uint32_t* host_word, void* stream) {
+  return mirror_status(status, host_word, (cudaStream_t)stream, "glm53_status_mirror");
 }
 
 extern "C" int glm53_sigmoid_bf16(const void* gate, int64_t n, void* out, void* stream) {

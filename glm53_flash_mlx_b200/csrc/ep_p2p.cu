@@ -21,7 +21,8 @@
 // Buffers are single: a rank only writes step n + 1 into a peer after its own
 // combine of step n, which waited for that peer's down stage of step n, which
 // ran after the peer's gate/up finished reading its slots.  Every wait is
-// bounded (about two seconds) and reports GLM53_STATUS_WAIT_TIMEOUT.
+// bounded (two seconds unless glm53_set_wait_limit_ns says otherwise) and
+// reports GLM53_STATUS_WAIT_TIMEOUT.
 #include <algorithm>
 #include <cstring>
 
@@ -116,7 +117,8 @@ __global__ void p2p_dispatch_kernel(const uint16_t* __restrict__ x, int H, int t
 __global__ void p2p_combine_kernel(const char* __restrict__ buf, EpLayout lay, const float* __restrict__ slot_scores,
                                    const uint32_t* __restrict__ route_pos, int64_t T, int top_k, int64_t H,
                                    const uint16_t* __restrict__ shared, uint16_t* __restrict__ out,
-                                   unsigned long long cta_per_row, uint32_t* status) {
+                                   unsigned long long cta_per_row, uint32_t* status,
+                                   unsigned long long wait_ns) {
   __shared__ unsigned long long s_step;
   // launched as a programmatic dependent of the owner's down stage: the home
   // tokens' shared rows come from that grid
@@ -126,7 +128,8 @@ __global__ void p2p_combine_kernel(const char* __restrict__ buf, EpLayout lay, c
     for (int64_t r = 0; r < T * top_k; ++r) sent += route_pos[r] != kP2pEmpty ? 1ull : 0ull;
     s_step = sent * cta_per_row;
     const unsigned long long before = *reinterpret_cast<const unsigned long long*>(buf + lay.expected);
-    wait_counter_geq(reinterpret_cast<const unsigned long long*>(buf + lay.cnt_back), before + s_step, status);
+    wait_counter_geq(reinterpret_cast<const unsigned long long*>(buf + lay.cnt_back), before + s_step, status,
+                     wait_ns);
   }
   __syncthreads();
   const uint16_t* rows = reinterpret_cast<const uint16_t*>(buf + lay.back);
@@ -301,6 +304,6 @@ extern "C" int glm53_ep_combine_p2p(void* buffer, const uint32_t* route_pos, con
   const int64_t n = std::max<int64_t>(T * (H / 8), 1);
   const int blocks = (int)std::min<int64_t>((n + 255) / 256, 1024);
   launch_pdl(p2p_combine_kernel, dim3((unsigned)blocks), st, (const char*)buffer, lay, slot_scores, route_pos, T,
-             top_k, H, (const uint16_t*)shared, (uint16_t*)out, cta_per_row, status);
+             top_k, H, (const uint16_t*)shared, (uint16_t*)out, cta_per_row, status, ep_wait_limit_ns());
   return check_launch("p2p_combine_kernel");
 }

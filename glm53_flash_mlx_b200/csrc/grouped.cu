@@ -468,6 +468,62 @@ extern "C" int glm53_grouped_fp8_linear(const void* x, int64_t R, int64_t K, con
   return grouped_gemm(a, (cudaStream_t)stream);
 }
 
+extern "C" size_t glm53_grouped_fp8_linear_workspace_bytes(int64_t R, int64_t K) {
+  if (R <= 0 || K <= 0) return 0;
+  return align_up((size_t)R * K * sizeof(__half), 256) + align_up((size_t)R * sizeof(float), 256);
+}
+
+extern "C" int glm53_grouped_fp8_linear_ws(const void* x, int64_t R, int64_t K, const uint32_t* tile_experts,
+                                           const uint32_t* tile_starts, const uint32_t* tile_lengths,
+                                           int64_t descriptor_capacity, int64_t tile_rows, const uint8_t* w,
+                                           int64_t E, int64_t N, const float* scale_inv, void* out,
+                                           void* workspace, size_t workspace_bytes, uint32_t* status,
+                                           uint32_t flags, void* stream) {
+  const char* fn = "glm53_grouped_fp8_linear_ws";
+  if (R < 0 || K <= 0 || N <= 0 || E <= 0 || descriptor_capacity < 0 || tile_rows <= 0 ||
+      (R > 0 && (!x || !tile_experts || !tile_starts || !tile_lengths || !w || !scale_inv || !out || !status))) {
+    set_last_error("%s: invalid arguments", fn);
+    return GLM53_ERR_INVALID;
+  }
+  if (K % 128 != 0 || N % 128 != 0 || (((uintptr_t)w | (uintptr_t)x) & 15) != 0) {
+    set_last_error("%s: block-aligned dimensions required (K=%lld N=%lld)", fn, (long long)K, (long long)N);
+    return GLM53_ERR_INVALID;
+  }
+  if (R == 0 || descriptor_capacity == 0) return GLM53_OK;
+  if (!workspace || workspace_bytes < glm53_grouped_fp8_linear_workspace_bytes(R, K) ||
+      (((uintptr_t)workspace) & 15) != 0 || R > INT32_MAX / 2 || !grouped_tc_supported(K, N, 0.0f, false)) {
+    set_last_error("%s: workspace missing or too small, or geometry outside the tensor-core path", fn);
+    return GLM53_ERR_INVALID;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  __half* x16 = (__half*)workspace;
+  float* xscale = (float*)((char*)workspace + align_up((size_t)R * K * sizeof(__half), 256));
+  int rc = rows_to_f16((const uint16_t*)x, K, nullptr, 1, R, x16, xscale, st);
+  if (rc) return rc;
+  TcGemm g{};
+  g.x16 = x16;
+  g.xscale = xscale;
+  g.R = R;
+  g.K = K;
+  g.tile_experts = tile_experts;
+  g.tile_starts = tile_starts;
+  g.tile_lengths = tile_lengths;
+  g.capacity = descriptor_capacity;
+  g.max_rows = tile_rows;
+  g.dense = false;
+  g.w = w;
+  g.w_rows = N;
+  g.s_gate = scale_inv;
+  g.s_expert = (N / 128) * (K / 128);
+  g.E = E;
+  g.N = N;
+  g.swiglu = false;
+  g.finite = (flags & GLM53_FLAG_E4M3_FINITE) != 0;
+  g.out = (uint16_t*)out;
+  g.status = status;
+  return grouped_tc(g, st);
+}
+
 extern "C" int glm53_activate_gate_up(const void* gate_up, int64_t R, int64_t I, float limit, void* hidden,
                                       void* stream) {
   if (R < 0 || I <= 0 || (R > 0 && (!gate_up || !hidden))) {
@@ -661,6 +717,21 @@ static int grouped_moe_tc(const MoeWorkspace& w, const void* x, int64_t T, int64
 extern "C" size_t glm53_grouped_moe_workspace_bytes(int64_t T, int top_k, int64_t E, int64_t H, int64_t I,
                                                     int64_t I_shared) {
   return carve(nullptr, T, top_k, E, H, I, I_shared).bytes;
+}
+
+extern "C" int glm53_grouped_moe_workspace_layout(int64_t T, int top_k, int64_t E, int64_t H, int64_t I,
+                                                  int64_t I_shared, size_t* offsets) {
+  if (!offsets || T < 0 || top_k <= 0 || E <= 0 || H <= 0 || I <= 0 || I_shared < 0) {
+    set_last_error("glm53_grouped_moe_workspace_layout: invalid arguments");
+    return GLM53_ERR_INVALID;
+  }
+  // offsets from a base of 256 (any aligned base gives the same offsets)
+  char* const base = reinterpret_cast<char*>(256);
+  const MoeWorkspace w = carve(base, T, top_k, E, H, I, I_shared);
+  const void* parts[8] = {w.order, w.inverse, w.sorted_experts, w.sorted_scores,
+                          w.hidden, w.down, w.shared_hidden, w.shared_out};
+  for (int i = 0; i < 8; ++i) offsets[i] = (size_t)(reinterpret_cast<const char*>(parts[i]) - base);
+  return GLM53_OK;
 }
 
 extern "C" int glm53_grouped_moe(const void* x, int64_t T, int64_t H, const uint32_t* indices, const float* scores,

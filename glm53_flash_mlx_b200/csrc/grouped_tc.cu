@@ -400,6 +400,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int d = t / (mtiles * zsub);
           if ((t % (mtiles * zsub)) == 0 && __ldg(a.tile_lengths + d) && __ldg(a.tile_experts + d) >= (uint32_t)a.E)
             atomicOr(a.status, kStatusBadExpert);
+          // a descriptor longer than the launch's sub-tiles cover is not computed past them
+          if ((t % (mtiles * zsub)) == 0 && __ldg(a.tile_lengths + d) > (uint32_t)(zsub * kN))
+            atomicOr(a.status, kStatusBadGeometry);
         }
       }
       Cursor cr{0, 0, 0u, Tile{}}, ca{0, 0, 0u, Tile{}};

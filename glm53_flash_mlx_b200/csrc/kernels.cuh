@@ -103,8 +103,14 @@ int router_topk(const void* x, int64_t T, int64_t H, const float* w, int64_t E, 
 void* mapped_host(const void* p);
 // Small host <-> device copy: a kernel over the pinned buffer's mapping when
 // both addresses and the size are 16-byte multiples (*by_kernel = true), else
-// cudaMemcpyAsync (capi.cu).
-cudaError_t small_copy(void* dst, const void* src, size_t bytes, bool to_device, cudaStream_t st, bool* by_kernel);
+// cudaMemcpyAsync (capi.cu).  When the copy runs as a kernel and `status` and
+// `status_mirror` (pinned host) are given, the kernel also copies the device
+// status word into the host word.
+cudaError_t small_copy(void* dst, const void* src, size_t bytes, bool to_device, cudaStream_t st, bool* by_kernel,
+                       const uint32_t* status = nullptr, uint32_t* status_mirror = nullptr);
+// One-thread kernel copying the device status word into a pinned host word
+// (GLM53_ERR_INVALID when host_word is not device-mapped).
+int mirror_status(const uint32_t* status, uint32_t* host_word, cudaStream_t st, const char* fn);
 
 // Peer-memory expert parallelism: every rank allocates one buffer of this
 // layout and maps every peer's (CUDA IPC).  Slot (src, s) of recv_x/recv_e is
@@ -129,10 +135,14 @@ inline EpLayout ep_layout(int world, int cap, int64_t H) {
   return l;
 }
 
+// Longest wait of the expert-parallel peer handshakes, in ns (default two
+// seconds; glm53_set_wait_limit_ns changes it for later launches).
+unsigned long long ep_wait_limit_ns();
+
 // Bounded wait of one thread until *counter >= target (system-scope acquire);
-// false (and GLM53_STATUS_WAIT_TIMEOUT) after about two seconds.
+// false (and GLM53_STATUS_WAIT_TIMEOUT) after limit_ns of globaltimer time.
 __device__ __forceinline__ bool wait_counter_geq(const unsigned long long* counter, unsigned long long target,
-                                                 uint32_t* status) {
+                                                 uint32_t* status, unsigned long long limit_ns) {
   unsigned long long t0 = 0;
   for (uint32_t it = 0;; ++it) {
     unsigned long long v;
@@ -143,7 +153,7 @@ __device__ __forceinline__ bool wait_counter_geq(const unsigned long long* count
       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
       if (t0 == 0) {
         t0 = now;
-      } else if (now - t0 > 2000000000ull) {
+      } else if (now - t0 > limit_ns) {
         atomicOr(status, kStatusWaitTimeout);
         return false;
       }

@@ -75,6 +75,7 @@ struct DecodeArgs {
   const unsigned long long* arrivals;
   const unsigned long long* epoch;
   unsigned long long arrivals_per_step;
+  unsigned long long wait_ns;  // bound of the arrival wait
   const unsigned long long* peer_base;  // [world] buffer bases (device pointers)
   int64_t back_off, back_cnt_off;
   int rank, cap;
@@ -228,7 +229,7 @@ __global__ void __launch_bounds__(32 * W) decode_gate_up_v4(DecodeArgs a) {
     pdl_wait();  // the router's results
   }
   if (a.arrivals && jb < a.top_k) {  // peer-memory dispatch: wait for every rank's slots
-    if (threadIdx.x == 0) wait_counter_geq(a.arrivals, (*a.epoch + 1ull) * a.arrivals_per_step, a.status);
+    if (threadIdx.x == 0) wait_counter_geq(a.arrivals, (*a.epoch + 1ull) * a.arrivals_per_step, a.status, a.wait_ns);
     __syncthreads();
   }
   // the down stage may launch now: its prologue only streams weights.  After
@@ -304,7 +305,7 @@ __device__ __forceinline__ void decode_down_peer(const DecodeArgs& a, int jb, in
   char* hb = reinterpret_cast<char*>(routed ? a.peer_base[home] : 0ull);
   uint32_t e = 0;
   if (routed) {
-    if (threadIdx.x == 0) wait_counter_geq(a.arrivals, (*a.epoch + 1ull) * a.arrivals_per_step, a.status);
+    if (threadIdx.x == 0) wait_counter_geq(a.arrivals, (*a.epoch + 1ull) * a.arrivals_per_step, a.status, a.wait_ns);
     __syncthreads();
     e = a.ids[jb];
   }
@@ -785,6 +786,18 @@ extern "C" size_t glm53_packed_decode_workspace_bytes(int top_k, int64_t H, int6
   return decode_workspace(top_k, H, I, I_shared).bytes;
 }
 
+extern "C" int glm53_packed_decode_workspace_layout(int top_k, int64_t H, int64_t I, int64_t I_shared,
+                                                    size_t* offsets) {
+  if (!offsets || top_k <= 0 || H <= 0 || I <= 0 || I_shared < 0) {
+    set_last_error("glm53_packed_decode_workspace_layout: invalid arguments");
+    return GLM53_ERR_INVALID;
+  }
+  const DecodeWorkspace w = decode_workspace(top_k, H, I, I_shared);
+  offsets[0] = w.hidden;
+  offsets[1] = w.partial;
+  return GLM53_OK;
+}
+
 extern "C" int glm53_packed_decode_moe(const void* x, int64_t H, const uint32_t* expert_ids, const float* scores,
                                        int top_k, const uint8_t* gate_up_w, const float* gate_up_s,
                                        const uint8_t* down_w, const float* down_s, int64_t E, int64_t I,
@@ -867,11 +880,16 @@ extern "C" int glm53_decode_step_host(const glm53_decode_step_desc* d, const voi
   const size_t row = (size_t)d->H * 2;
   bool copy_kernel = false;
   if (x_host) {
-    cudaError_t e = small_copy(d->x, x_host, row, true, st, &copy_kernel);
+    cudaError_t e = small_copy(d->x, x_host, row, true, st, &copy_kernel, d->status, d->status_host);
     if (e != cudaSuccess) {
       set_last_error("%s: input copy: %s", fn, cudaGetErrorString(e));
       return GLM53_ERR_CUDA;
     }
+  }
+  if (d->status_host && !copy_kernel) {
+    // the copy kernel did not mirror the status word: a one-thread kernel does
+    const int mrc = mirror_status(d->status, d->status_host, st, fn);
+    if (mrc) return mrc;
   }
   int rc = router_topk(d->x, 1, d->H, d->router_w, d->E, d->router_bias, d->top_k, d->n_group, d->topk_group,
                        d->norm_topk_prob, d->routed_scaling_factor, d->expert_ids, d->scores, nullptr,
@@ -1016,6 +1034,7 @@ extern "C" int glm53_ep_owner_decode_p2p(void* buffer, int64_t H, int world, int
   a.arrivals = (const unsigned long long*)(b + lay.cnt_dispatch);
   a.epoch = (const unsigned long long*)(b + lay.epoch);
   a.arrivals_per_step = (unsigned long long)R;
+  a.wait_ns = ep_wait_limit_ns();
   a.peer_base = peer_base;
   a.back_off = (int64_t)lay.back;
   a.back_cnt_off = (int64_t)lay.cnt_back;
@@ -1094,6 +1113,13 @@ extern "C" int glm53_packed_decode_moe_static_scratch(
       (has_shared && (!shared_gate_w || !shared_gate_s || !shared_up_w || !shared_up_s || !shared_down_w ||
                       !shared_down_s))) {
     set_last_error("%s: missing pointer or E <= 0", fn);
+    return GLM53_ERR_INVALID;
+  }
+  if (flags & GLM53_FLAG_AFTER_ROUTER) {
+    // the counter clear below is a stream operation between the router and the
+    // decode, so the decode cannot be the router's programmatic dependent
+    set_last_error("%s: GLM53_FLAG_AFTER_ROUTER is not supported (the scratch counters are cleared on the stream "
+                   "before the decode); call without it", fn);
     return GLM53_ERR_INVALID;
   }
   const DecodeWorkspace wl = decode_workspace(top_k, H, I, I_shared);

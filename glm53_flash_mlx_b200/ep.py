@@ -161,7 +161,12 @@ class ExpertParallelDecode:
         self.zero_ids = torch.zeros(self.max_tokens, dtype=torch.int32, device=dev)
         self.shared_rows = torch.zeros((self.max_tokens, self.H), dtype=torch.bfloat16, device=dev)
         self.workspace = N.Workspace()
-        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        from .packed import StatusWord
+
+        # fail-closed bits (bad expert id, a peer wait that gave up): published
+        # into a pinned host word after every call, raised at the next one
+        self.status_word = StatusWord(dev)
+        self.status = self.status_word.word
         self.flags = N.decode_flags(self.bank[0], self.bank[2])
         self.shared_flags = N.decode_flags(self.shared_bank[0], self.shared_bank[2]) if self.shared_bank else 0
         if transport not in ("p2p", "nccl"):
@@ -236,6 +241,7 @@ class ExpertParallelDecode:
         if indices.shape[-1] != self.top_k:
             raise ValueError(f"expected top-{self.top_k} routes, got {indices.shape[-1]}")
         lib = N.lib()
+        self.status_word.raise_pending()
         st = N.stream(self.device)
         ids = indices.reshape(-1).to(torch.int32).contiguous()
         sc = scores.reshape(-1).to(torch.float32).contiguous()
@@ -243,7 +249,9 @@ class ExpertParallelDecode:
         if out is None:
             out = torch.empty((T, self.H), dtype=torch.bfloat16, device=self.device)
         if self.transport == "p2p":
-            return self._call_p2p(lib, st, flat, T, ids, sc, out).reshape(x.shape)
+            self._call_p2p(lib, st, flat, T, ids, sc, out)
+            self.status_word.publish()
+            return out.reshape(x.shape)
         N.check(lib.glm53_ep_dispatch_pack(flat.data_ptr(), T, self.H, ids.data_ptr(), sc.data_ptr(), self.top_k,
                                            self.experts, self.world, self.capacity, self.send_x.data_ptr(),
                                            self.send_e.data_ptr(), self.slot_scores.data_ptr(),
@@ -262,6 +270,7 @@ class ExpertParallelDecode:
         N.check(lib.glm53_ep_combine(self.back.data_ptr(), self.route_pos.data_ptr(), self.slot_scores.data_ptr(), T,
                                      self.top_k, self.H, shared_ptr, out.data_ptr(), st),
                 "glm53_ep_combine")
+        self.status_word.publish()
         return out.reshape(x.shape)
 
 
@@ -322,6 +331,10 @@ class ExpertParallelMoE(torch.nn.Module):
     def forward(self, x):
         indices, scores = self.gate(x)
         return self.plan(x, indices, scores)
+
+    def status_word(self, device=None):
+        """The plan's StatusWord (fail-closed bits of its kernels)."""
+        return self.plan.status_word
 
     def capture_decode(self):
         """One-token expert-parallel decode as a replayable CUDA graph (every

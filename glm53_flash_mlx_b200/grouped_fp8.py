@@ -221,10 +221,13 @@ class SortedGroupedFP8MoE(PackedFP8MoE):
 
     def grouped_from_routes(self, x, indices, scores):
         shared = shared_fp8_tensors(self.shared_experts)
+        sw = self.status_word(x.device)
+        sw.raise_pending()
         result = grouped_moe(x, indices, scores, self.bank, shared, limit=self.config.swiglu_limit,
-                             workspace=self._workspace)
+                             workspace=self._workspace, status=sw.word)
         if shared is None and self.shared_experts is not None:
             result = result + self.shared_experts(x)
+        sw.publish()
         return result
 
     def forward(self, x):

@@ -325,18 +325,69 @@ def batched_decode_moe(x: torch.Tensor, indices: torch.Tensor, scores: torch.Ten
     return out
 
 
-def check_status(status: torch.Tensor, *, clear: bool = True) -> None:
-    """Raise for device-side fail-closed signals (one device->host read);
-    the word is cleared first so the next call starts clean."""
-    word = int(status.view(torch.int32)[0].item()) & 0xFFFFFFFF
-    if clear and word:
-        status.view(torch.int32)[:1].zero_()
+def _raise_status(word: int) -> None:
     if word & N.STATUS_BAD_EXPERT:
         raise IndexError("expert id out of range in routed MoE")
     if word & N.STATUS_WAIT_TIMEOUT:
         raise RuntimeError("a bounded device wait gave up")
     if word:
         raise RuntimeError(f"device status 0x{word:x}")
+
+
+def check_status(status: torch.Tensor, *, clear: bool = True) -> None:
+    """Raise for device-side fail-closed signals (one device->host read);
+    the word is cleared first so the next call starts clean."""
+    word = int(status.view(torch.int32)[0].item()) & 0xFFFFFFFF
+    if clear and word:
+        status.view(torch.int32)[:1].zero_()
+    _raise_status(word)
+
+
+class StatusWord:
+    """A layer's device status word and its pinned host mirror.
+
+    The kernels OR fail-closed bits into ``word`` (an out-of-range expert id,
+    a bounded wait that gave up) instead of trapping, as the reference's
+    device-side invalid-route counter does (native_indexer_plan.metal:1880-1900).
+    ``publish()`` enqueues a one-thread kernel that copies the word into the
+    pinned host mirror; ``raise_pending()`` reads the mirror with a plain host
+    read -- no device synchronisation on the success path -- and raises the
+    reference's exception (``IndexError`` for a bad expert id, packed.py:868-876;
+    ``RuntimeError`` otherwise).  A module publishes after its kernels and checks
+    at the start of its next call, so an error surfaces one call late at the
+    latest; ``check()`` synchronises and raises at once."""
+
+    def __init__(self, device: torch.device):
+        self.device = torch.device(device)
+        # one int32 word (in a 256-byte allocation of its own)
+        self.word = torch.zeros(64, dtype=torch.int32, device=self.device)[:1]
+        self.host = torch.zeros(4, dtype=torch.int32).pin_memory()
+
+    def publish(self) -> None:
+        N.check(N.lib().glm53_status_mirror(self.word.data_ptr(), self.host.data_ptr(), N.stream(self.device)),
+                "glm53_status_mirror")
+
+    def _fail(self, word: int) -> None:
+        # let every enqueued mirror copy land before clearing, so no stale
+        # copy re-raises at the next call
+        torch.cuda.synchronize(self.device)
+        word |= int(self.word[0].item()) | int(self.host[0])
+        self.word.zero_()
+        torch.cuda.synchronize(self.device)
+        self.host.zero_()
+        _raise_status(word & 0xFFFFFFFF)
+
+    def raise_pending(self) -> None:
+        word = int(self.host[0])
+        if word:
+            self._fail(word)
+
+    def check(self) -> None:
+        """Synchronise the device and raise for any bit set so far."""
+        torch.cuda.synchronize(self.device)
+        word = int(self.word[0].item()) | int(self.host[0])
+        if word:
+            self._fail(word)
 
 
 class CapturedDecode:
@@ -354,6 +405,10 @@ class CapturedDecode:
 
     def __init__(self, module: nn.Module, hidden: int, device):
         device = torch.device(device)
+        # the module's status word (its captured calls publish into the
+        # mirror): raise at the next step, as the module call itself would
+        words = getattr(module, "status_word", None)
+        self._status = words(device) if callable(words) else None
         self.x = torch.zeros((1, 1, hidden), dtype=torch.bfloat16, device=device)
         side = torch.cuda.Stream(device=device)
         side.wait_stream(torch.cuda.current_stream(device))
@@ -370,7 +425,14 @@ class CapturedDecode:
         if not self._exec:
             raise RuntimeError("CapturedDecode: the captured graph has no executable instance")
 
+    def check(self) -> None:
+        """Synchronise and raise for any fail-closed bit the captured kernels set."""
+        if self._status is not None:
+            self._status.check()
+
     def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        if self._status is not None:
+            self._status.raise_pending()
         nbytes = self.x.numel() * self.x.element_size()
         host_in = x.device.type == "cpu" and x.dtype == self.x.dtype and x.is_contiguous() and x.numel() == self.x.numel()
         host_out = out is not None and out.device.type == "cpu" and out.dtype == self.out.dtype and \
@@ -416,11 +478,18 @@ class PackedDecodeStep:
         ws = module._workspace
         rws = ws.get(dev, "step_router", lib.glm53_router_workspace_bytes(1, E))
         dws = ws.get(dev, "step_decode", lib.glm53_packed_decode_workspace_bytes(DECODE_TOP_K, H, I, Is))
-        status = module.status
+        self._status = module.status_word(dev)
+        status = self._status.word
         weights = (bank.gate_up_weight, bank.down_weight, *(() if shared is None else shared[0::2]))
         router_w = gate.weight.contiguous()
         router_b = gate.e_score_correction_bias.contiguous()
         sh = shared if shared is not None else (None,) * 6
+        # the step binds raw device addresses: hold every bound tensor and
+        # remember its identity, so a replaced or rewritten weight is refused
+        # (the reference plan's check, native_packed_moe_plan.cpp:270-272)
+        self._bound = self._bound_tensors(module)
+        self._identity = self._identities(self._bound)
+        self._slots = self._binding_slots(module)
         self._keep = (router_w, router_b, rws, dws, status, sh)
         self._desc = N.DecodeStepDesc(
             H=H, E=E, I=I, I_shared=Is, top_k=DECODE_TOP_K, n_group=gate.n_group, topk_group=gate.topk_group,
@@ -433,8 +502,59 @@ class PackedDecodeStep:
             shared_up_s=N.ptr(sh[3]), shared_down_w=N.ptr(sh[4]), shared_down_s=N.ptr(sh[5]),
             x=self.x.data_ptr(), expert_ids=self._ids.data_ptr(), scores=self._scores.data_ptr(),
             out=self.out.data_ptr(), router_workspace=rws.data_ptr(), router_workspace_bytes=rws.numel(),
-            decode_workspace=dws.data_ptr(), decode_workspace_bytes=dws.numel(), status=status.data_ptr())
+            decode_workspace=dws.data_ptr(), decode_workspace_bytes=dws.numel(), status=status.data_ptr(),
+            status_host=self._status.host.data_ptr())
         self._pdesc = ctypes.pointer(self._desc)
+
+    @staticmethod
+    def _bound_tensors(module) -> tuple:
+        bank, gate = module.bank, module.gate
+        shared = shared_fp8_tensors(module.shared_experts)
+        return (bank.gate_up_weight, bank.gate_up_scale_inv, bank.down_weight, bank.down_scale_inv,
+                gate.weight, gate.e_score_correction_bias, *(() if shared is None else shared))
+
+    @staticmethod
+    def _identities(tensors) -> tuple:
+        return tuple((t.data_ptr(), t._version) for t in tensors)
+
+    @staticmethod
+    def _binding_slots(module) -> tuple:
+        """(dict, name, object) for every attribute the step read its tensors
+        through: the layer's bank / gate / shared expert, the bank's four
+        buffers, the gate's weight and bias, the shared projections' tensors."""
+        def slot(owner, name):
+            for d in (owner._parameters, owner._buffers, owner._modules, owner.__dict__):
+                if name in d:
+                    return (d, name, d[name])
+            raise AttributeError(name)
+
+        slots = [slot(module, "bank"), slot(module, "gate"), slot(module, "shared_experts")]
+        slots += [slot(module.bank, n) for n in ("gate_up_weight", "gate_up_scale_inv", "down_weight",
+                                                 "down_scale_inv")]
+        slots += [slot(module.gate, "weight"), slot(module.gate, "e_score_correction_bias")]
+        if shared_fp8_tensors(module.shared_experts) is not None:
+            for proj in ("gate_proj", "up_proj", "down_proj"):
+                p = getattr(module.shared_experts, proj)
+                slots += [slot(module.shared_experts, proj), slot(p, "weight"), slot(p, "weight_scale_inv")]
+        return tuple(slots)
+
+    def _check_bound(self) -> None:
+        for (d, name, obj) in self._slots:
+            if d.get(name) is not obj:
+                break
+        else:
+            for t, (ptr, version) in zip(self._bound, self._identity):
+                if t._version != version or t.data_ptr() != ptr:
+                    break
+            else:
+                return
+        raise RuntimeError("packed MoE decode step: a bound weight's identity changed (replaced, reallocated or "
+                           "written in place); capture a new step with capture_decode()")
+
+    def check(self) -> None:
+        """Synchronise and raise for any fail-closed bit the step's kernels set
+        (the per-call check sees the bits of earlier calls only)."""
+        self._status.check()
 
     @staticmethod
     def supported(module) -> bool:
@@ -452,6 +572,10 @@ class PackedDecodeStep:
         H = self.x.numel()
         if x.numel() != H:
             raise ValueError(f"decode step input has {x.numel()} values, layer width {H}")
+        self._check_bound()
+        # bits of earlier steps, mirrored into pinned host memory by this
+        # step's predecessors on the stream: a host read, no synchronisation
+        self._status.raise_pending()
         if x.device.type == "cpu":
             x = x.to(torch.bfloat16).contiguous()
             x_host = x.data_ptr()
@@ -467,7 +591,7 @@ class PackedDecodeStep:
         N.check(N.lib().glm53_decode_step_host(self._pdesc, x_host, out_host, N.stream(self.x.device)),
                 "glm53_decode_step_host")
         if _SYNC_STATUS:
-            check_status(self._keep[4])
+            self._status.check()
         if out is None:
             return self.out
         if out_host is None:
@@ -488,13 +612,28 @@ class PackedFP8MoE(DirectFP8MoE):
             bank.expert(expert_id, limit=config.swiglu_limit) for expert_id in range(bank.expert_count)
         )
         self._workspace = N.Workspace()
+        self._status_words: dict = {}
 
     def _expert(self, expert_id: int):
         return self._expert_views[expert_id]
 
+    def status_word(self, device=None) -> StatusWord:
+        """This layer's StatusWord on `device` (default: the bank's device)."""
+        dev = torch.device(device) if device is not None else self.bank.gate_up_weight.device
+        sw = self._status_words.get(dev)
+        if sw is None:
+            sw = self._status_words[dev] = StatusWord(dev)
+        return sw
+
     @property
     def status(self) -> torch.Tensor:
-        return self._workspace.get(self.bank.gate_up_weight.device, "status", 4)
+        """The device status word the layer's kernels write (int32, word 0)."""
+        return self.status_word().word
+
+    def check_status(self) -> None:
+        """Synchronise and raise for any fail-closed bit the layer's kernels set."""
+        for sw in self._status_words.values():
+            sw.check()
 
     def capture_decode(self) -> PackedDecodeStep | CapturedDecode:
         """This layer's one-token decode on static buffers, called once per
@@ -508,16 +647,22 @@ class PackedFP8MoE(DirectFP8MoE):
     def forward(self, x):
         flat_x = x.reshape(-1, x.shape[-1])
         if flat_x.shape[0] != 1:
-            if not 2 <= flat_x.shape[0] <= BATCHED_DECODE_MAX_ROWS:
+            if not 2 <= flat_x.shape[0] <= BATCHED_DECODE_MAX_ROWS or not flat_x.is_cuda:
                 return super().forward(x)
+            sw = self.status_word(flat_x.device)
+            sw.raise_pending()
             indices, scores = self.gate(x)
             limit = self.config.swiglu_limit
             if (indices.shape[-1] != DECODE_TOP_K or float(limit) != int(limit) or
                     self.bank.hidden_size % BLOCK_SIZE or self.bank.intermediate_size % BLOCK_SIZE):
                 return self._forward_routes(x, indices, scores)
-            return batched_decode_moe(flat_x, indices.reshape(flat_x.shape[0], -1),
-                                      scores.reshape(flat_x.shape[0], -1), self.bank, self.shared_experts,
-                                      limit=limit, workspace=self._workspace).reshape(x.shape)
+            out = batched_decode_moe(flat_x, indices.reshape(flat_x.shape[0], -1),
+                                     scores.reshape(flat_x.shape[0], -1), self.bank, self.shared_experts,
+                                     limit=limit, workspace=self._workspace, status=sw.word).reshape(x.shape)
+            sw.publish()
+            return out
+        if flat_x.is_cuda:
+            self.status_word(flat_x.device).raise_pending()
         indices, scores = self.gate(x)
         if indices.shape[-1] != DECODE_TOP_K:
             return super().forward(x)
@@ -525,9 +670,11 @@ class PackedFP8MoE(DirectFP8MoE):
         if float(limit) != int(limit):
             raise ValueError("exact fused packed decode requires an integral clamp limit")
         shared = shared_fp8_tensors(self.shared_experts)
+        sw = self.status_word(flat_x.device)
         result = packed_decode_moe(flat_x[0], indices.reshape(-1), scores.reshape(-1), self.bank, shared,
-                                   limit=limit, workspace=self._workspace,
+                                   limit=limit, workspace=self._workspace, status=sw.word,
                                    after_router=isinstance(self.gate, Float32Gate)).reshape(x.shape)
         if shared is None and self.shared_experts is not None:
             result = result + self.shared_experts(x)
+        sw.publish()
         return result

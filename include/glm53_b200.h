@@ -139,6 +139,14 @@ int glm53_router_topk(const void* x, int64_t T, int64_t H, const float* w,
  * its completion counters at zero again. */
 size_t glm53_packed_decode_workspace_bytes(int top_k, int64_t H, int64_t I, int64_t I_shared);
 
+/* Byte offsets, inside that workspace, of the intermediates a call leaves
+ * there: offsets[0] = the SwiGLU hidden rows (BF16 [top_k * I + I_shared],
+ * slot-major, the shared expert last), offsets[1] = the down projections
+ * before rounding (FP32 [(top_k + 1) * H], slot-major, the shared expert
+ * last).  For inspection (the parity tests certify every rounding site from
+ * them); no reference counterpart. */
+int glm53_packed_decode_workspace_layout(int top_k, int64_t H, int64_t I, int64_t I_shared, size_t* offsets);
+
 /* One-token packed decode MoE over a packed expert bank:
  *   bank: gate_up_w [E,2I,H] (gate rows [0,I), up rows [I,2I)),
  *         gate_up_s [E, 2*ceil(I/128), ceil(H/128)],
@@ -195,9 +203,11 @@ int glm53_selected_decode_moe(const void* x, int64_t H, const float* scores, int
  * current device must own `stream` and the pointers; the first call on each
  * device looks up the array's address (cudaGetSymbolAddress), so make that
  * first call before any stream capture.  Each call clears the array's
- * completion counters on `stream` before its kernels run.  All calls on one
- * device share the array, so calls whose GPU work overlaps (other streams,
- * other host threads) race and must be serialised by the caller. */
+ * completion counters on `stream` before its kernels run; because that clear
+ * sits between a router and this decode on the stream, GLM53_FLAG_AFTER_ROUTER
+ * is rejected with GLM53_ERR_INVALID (the other flags are honoured).  All
+ * calls on one device share the array, so calls whose GPU work overlaps (other
+ * streams, other host threads) race and must be serialised by the caller. */
 int glm53_packed_decode_moe_static_scratch(const void* x, int64_t H, const uint32_t* expert_ids,
                                            const float* scores, int top_k,
                                            const uint8_t* gate_up_w, const float* gate_up_s,
@@ -253,9 +263,31 @@ typedef struct glm53_decode_step_desc {
   void* decode_workspace;
   size_t decode_workspace_bytes;
   uint32_t* status;
+  uint32_t* status_host;        /* pinned host word or NULL: before its own kernels
+                                   run, each call copies *status (the bits of every
+                                   earlier call on the stream) into it */
 } glm53_decode_step_desc;
 
 int glm53_decode_step_host(const glm53_decode_step_desc* d, const void* x_host, void* out_host, void* stream);
+
+/* Copies the device status word into `host_word`, a 4-byte word of pinned
+ * (page-locked, device-mapped) host memory, in stream order: once the work
+ * enqueued before this call has run, the host reads the fail-closed bits
+ * (GLM53_STATUS_*) with a plain memory read, without synchronising the
+ * device.  This is how the Python modules raise the reference's IndexError /
+ * RuntimeError (glm53_flash_mlx/packed.py:868-876; the device-side
+ * invalid-route counter of native_indexer_plan.metal:1880-1900) at their next
+ * call rather than never.  GLM53_ERR_INVALID when host_word is not mapped. */
+int glm53_status_mirror(const uint32_t* status, uint32_t* host_word, void* stream);
+
+/* Bound, in nanoseconds of device time, of the expert-parallel peer waits
+ * (glm53_ep_owner_decode_p2p's arrival wait, glm53_ep_combine_p2p's row
+ * wait) for kernels launched after this call, process-wide; 0 restores the
+ * default of two seconds; values outside [1 ms, 60 s] are GLM53_ERR_INVALID.
+ * A wait that reaches the bound sets GLM53_STATUS_WAIT_TIMEOUT and its kernel
+ * returns.  No reference counterpart (the reference runs on one device); it
+ * lets a test make a wait run out in milliseconds. */
+int glm53_set_wait_limit_ns(unsigned long long ns);
 
 /* Workspace bytes needed by glm53_routes_decode for R route slots. */
 size_t glm53_routes_decode_workspace_bytes(int64_t R, int64_t H, int64_t I);
@@ -470,6 +502,16 @@ int glm53_restore_and_reduce(const void* sorted_out, const float* sorted_scores,
 /* Workspace bytes needed by glm53_grouped_moe. */
 size_t glm53_grouped_moe_workspace_bytes(int64_t T, int top_k, int64_t E,
                                          int64_t H, int64_t I, int64_t I_shared);
+
+/* Byte offsets, inside glm53_grouped_moe's workspace (tensor-core path), of
+ * the intermediates a call leaves there: offsets[0..7] = route order (u32
+ * [R], sorted position -> route t * top_k + j), inverse (u32 [R]), sorted
+ * expert ids (u32 [R]), sorted scores (f32 [R]), hidden rows (FP16 [R, I],
+ * sorted order), down rows (BF16 [R, H], sorted order), the shared expert's
+ * hidden rows (FP16 [T, I_shared]) and output rows (BF16 [T, H]); R = T *
+ * top_k.  For inspection (the parity tests); no reference counterpart. */
+int glm53_grouped_moe_workspace_layout(int64_t T, int top_k, int64_t E, int64_t H, int64_t I,
+                                       int64_t I_shared, size_t* offsets);
 
 /* Whole grouped prefill MoE layer given routes: route plan, grouped gate/up
  * with fused SwiGLU, grouped down, slot-ordered FP32 combine, shared expert

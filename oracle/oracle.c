@@ -819,3 +819,300 @@ void orc_hc_expand(const uint16_t* moe, const uint16_t* residual, const float* p
         out[(t * n + b) * H + d] = bf16_from_f32(branch + mixed);
       }
 }
+
+/* ------------------------------------------------------------------------ */
+/* Rounding envelopes (tolerance certificates for the parity tests)         */
+/* ------------------------------------------------------------------------ */
+
+/* A routed expert's BF16 down rows computed by ANY FP32 evaluation order of
+ * its dot products lie inside the envelope computed here; the parity tests
+ * accept a layer output beyond max-abs 2e-2 only when it lies inside the
+ * envelope propagated through the final combine (a proven rounding flip).
+ *
+ * Error model.  A dot product z = sum_k t_k (t_k = x_k * lut(w_k) * s_k) is
+ * computed exactly here in double (every product is exact in double: 8 + 4 +
+ * 24 significant bits, and the double sum's own error is below K * 2^-53 *
+ * sum|t_k|).  A kernel that evaluates it with FP32 additions (and FP32 block
+ * scale products), at most `depth` roundings of relative size u = 2^-24 on
+ * the path from any term to the result, returns a value within
+ * gamma(depth) * sum|t_k| of z (gamma(n) = n u / (1 - n u), the standard
+ * bound for recursive summation).  The tensor-core kernels sum 16 exact
+ * products per MMA into the FP32 accumulator; each MMA is taken to round at
+ * most twice (its product sum and the add into the accumulator), so a 128-K
+ * block of 8 MMAs adds 16 to the depth, the block-scale product 1 and the
+ * FP32 sum over blocks one per block: depth <= 16 + 1 + K/128 (65 at K =
+ * 4096), rounded up to the `depth` the caller states.  The CUDA kernels
+ * stage activations as FP16 times 2^-e (e = 0 unless the row's largest
+ * magnitude reaches 2^14); a BF16 value is then exact unless it falls below
+ * FP16's normal range (|x| 2^-e < 2^-14), where it is off by at most 2^-25
+ * 2^e: those terms add 2^-25 2^e |lut(w) s| each to the bound.
+ *
+ * The value rounded to BF16 is then one of the BF16 values between the
+ * roundings of the envelope's ends (rounding is monotone).  The SwiGLU of the
+ * reference (BF16 per-op rounding) is evaluated on every candidate pair of
+ * gate / up BF16 values; the down projection is linear in the hidden row, so
+ * its envelope is the exact sum over the hidden intervals plus the same
+ * FP32 evaluation bound. */
+
+/* The CUDA kernels' FP16 staging of a row with largest magnitude mx:
+ * values below *tiny (FP16 subnormal after the 2^-e scale) may be off by
+ * *err. */
+static void env_f16_staging(double mx, double* tiny, double* err) {
+  int e = 0;
+  if (mx >= 16384.0) {
+    int ex;
+    frexp(mx, &ex);
+    e = ex - 14;
+  }
+  *tiny = ldexp(1.0, -14 + e);
+  *err = ldexp(1.0, -25 + e);
+}
+
+static double env_gamma(int depth) {
+  const double u = ldexp(1.0, -24);
+  return depth * u / (1.0 - depth * u) + ldexp(1.0, -45);
+}
+
+/* bit pattern order of BF16 values as integers: +0 < ... , -0 just below +0 */
+static inline int32_t bf16_ord(uint16_t b) { return (b & 0x8000u) ? -(int32_t)(b & 0x7FFFu) - 1 : (int32_t)b; }
+static inline uint16_t bf16_from_ord(int32_t o) { return o < 0 ? (uint16_t)(0x8000u | (uint32_t)(-(o + 1))) : (uint16_t)o; }
+
+/* BF16 value interval reachable by rounding any FP32 value in [lo, hi]
+ * (conservative: the double ends are rounded to the nearest FP32 first). */
+static void bf16_range(double lo, double hi, uint16_t* rlo, uint16_t* rhi) {
+  *rlo = bf16_from_f32((float)lo);
+  *rhi = bf16_from_f32((float)hi);
+}
+
+typedef struct {
+  const uint16_t* x;      /* [R, H] route rows */
+  const uint32_t* order;  /* routes sorted by expert */
+  const int64_t* start;   /* [E + 1] offsets into order */
+  int64_t H, I, E, R;
+  const uint8_t* gu_w;
+  const float* gu_s;
+  const uint8_t* d_w;
+  const float* d_s;
+  float limit;
+  double g_gu, g_d;       /* gamma(depth) of the two projections */
+  float* h_lo;            /* [R, I] hidden envelope */
+  float* h_hi;
+  float* d_lo;            /* [R, H] down envelope (BF16 values as floats) */
+  float* d_hi;
+  int64_t wide;           /* candidate sets that were cut off (should be 0) */
+  pthread_mutex_t mu;
+} env_ctx;
+
+#define ENV_MAX_CAND 16384
+
+/* one (expert, hidden row): gate and up envelopes of every route of the
+ * expert, then the hidden envelope over all candidate pairs */
+static void env_gate_up_item(void* p, int64_t item) {
+  env_ctx* c = (env_ctx*)p;
+  const int64_t e = item / c->I, row = item % c->I;
+  const int64_t H = c->H, I = c->I;
+  const int64_t scale_cols = (H + ORC_BLOCK - 1) / ORC_BLOCK;
+  const int64_t half = (I + ORC_BLOCK - 1) / ORC_BLOCK;
+  const uint8_t* gw = c->gu_w + (e * 2 * I + row) * H;
+  const uint8_t* uw = c->gu_w + (e * 2 * I + I + row) * H;
+  const float* gs = c->gu_s + (e * 2 * half + row / ORC_BLOCK) * scale_cols;
+  const float* us = c->gu_s + (e * 2 * half + half + row / ORC_BLOCK) * scale_cols;
+  int64_t wide = 0;
+  for (int64_t q = c->start[e]; q < c->start[e + 1]; ++q) {
+    const int64_t r = c->order[q];
+    const uint16_t* xr = c->x + r * H;
+    double mx = 0;
+    for (int64_t k = 0; k < H; ++k) mx = fmax(mx, fabs((double)f32_from_bf16(xr[k])));
+    double tiny, serr;
+    env_f16_staging(mx, &tiny, &serr);
+    double gz = 0, ga = 0, uz = 0, ua = 0, gs16 = 0, us16 = 0;
+    for (int64_t k = 0; k < H; ++k) {
+      const double xv = (double)f32_from_bf16(xr[k]);
+      const double wg = (double)g_lut[gw[k]] * (double)gs[k / ORC_BLOCK];
+      const double wu = (double)g_lut[uw[k]] * (double)us[k / ORC_BLOCK];
+      const double tg = xv * wg, tu = xv * wu;
+      gz += tg; ga += fabs(tg);
+      uz += tu; ua += fabs(tu);
+      if (xv != 0 && fabs(xv) < tiny) { gs16 += serr * fabs(wg); us16 += serr * fabs(wu); }
+    }
+    uint16_t g0, g1, u0, u1;
+    bf16_range(gz - c->g_gu * ga - gs16, gz + c->g_gu * ga + gs16, &g0, &g1);
+    bf16_range(uz - c->g_gu * ua - us16, uz + c->g_gu * ua + us16, &u0, &u1);
+    /* The result is monotone in the up value for a fixed gate (the clip and
+     * the final product are), so the up envelope's two ends suffice.  Gate
+     * candidates are enumerated, except inside |g| < 2^-9, where the BF16
+     * sigmoid is exactly 0.5 and silu = g / 2, so the result is monotone in
+     * g there and that band's two ends suffice. */
+    const float uend[2] = {f32_from_bf16(u0), f32_from_bf16(u1)};
+    const int32_t go0 = bf16_ord(g0), go1 = bf16_ord(g1);
+    const int32_t tneg = bf16_ord(0xBB00u), tpos = bf16_ord(0x3B00u);  /* -2^-9, +2^-9 */
+    float lo = INFINITY, hi = -INFINITY;
+    int32_t n = 0;
+    for (int32_t go = go0; go <= go1; ++go) {
+      if (go > tneg && go < tpos) {  /* tiny band: its ends only */
+        const int32_t band_hi = go1 < tpos - 1 ? go1 : tpos - 1;
+        if (go != band_hi) {
+          for (int t = 0; t < 2; ++t) {
+            const float h = f32_from_bf16(orc_swiglu_bf16(f32_from_bf16(bf16_from_ord(go)), uend[t], c->limit));
+            lo = fminf(lo, h);
+            hi = fmaxf(hi, h);
+          }
+          go = band_hi;
+        }
+      }
+      if (++n > ENV_MAX_CAND) { ++wide; break; }
+      for (int t = 0; t < 2; ++t) {
+        const float h = f32_from_bf16(orc_swiglu_bf16(f32_from_bf16(bf16_from_ord(go)), uend[t], c->limit));
+        lo = fminf(lo, h);
+        hi = fmaxf(hi, h);
+      }
+    }
+    c->h_lo[r * I + row] = lo;
+    c->h_hi[r * I + row] = hi;
+  }
+  if (wide) {
+    pthread_mutex_lock(&c->mu);
+    c->wide += wide;
+    pthread_mutex_unlock(&c->mu);
+  }
+}
+
+/* one (expert, output row): the down envelope of every route of the expert */
+static void env_down_item(void* p, int64_t item) {
+  env_ctx* c = (env_ctx*)p;
+  const int64_t e = item / c->H, h = item % c->H;
+  const int64_t H = c->H, I = c->I;
+  const int64_t scale_rows = (H + ORC_BLOCK - 1) / ORC_BLOCK;
+  const int64_t scale_cols = (I + ORC_BLOCK - 1) / ORC_BLOCK;
+  const uint8_t* wr = c->d_w + (e * H + h) * I;
+  const float* srow = c->d_s + (e * scale_rows + h / ORC_BLOCK) * scale_cols;
+  for (int64_t q = c->start[e]; q < c->start[e + 1]; ++q) {
+    const int64_t r = c->order[q];
+    const float* hl = c->h_lo + r * I;
+    const float* hh = c->h_hi + r * I;
+    double mx = 0;
+    for (int64_t k = 0; k < I; ++k) mx = fmax(mx, fmax(fabs((double)hl[k]), fabs((double)hh[k])));
+    double tiny, serr;
+    env_f16_staging(mx, &tiny, &serr);
+    double lo = 0, hi = 0, a = 0, s16 = 0;
+    for (int64_t k = 0; k < I; ++k) {
+      const double ws = (double)g_lut[wr[k]] * (double)srow[k / ORC_BLOCK];
+      const double p0 = (double)hl[k] * ws, p1 = (double)hh[k] * ws;
+      lo += p0 < p1 ? p0 : p1;
+      hi += p0 < p1 ? p1 : p0;
+      a += fabs(p0) > fabs(p1) ? fabs(p0) : fabs(p1);
+      if (fmin(fabs((double)hl[k]), fabs((double)hh[k])) < tiny && (hl[k] != 0 || hh[k] != 0)) s16 += serr * fabs(ws);
+    }
+    uint16_t d0, d1;
+    bf16_range(lo - c->g_d * a - s16, hi + c->g_d * a + s16, &d0, &d1);
+    c->d_lo[r * H + h] = f32_from_bf16(d0);
+    c->d_hi[r * H + h] = f32_from_bf16(d1);
+  }
+}
+
+/* Envelopes of the BF16 down rows of R routes (row r = expert ids[r] applied
+ * to x[r]) through a packed bank (layout of orc_packed_decode_moe), with the
+ * gate/up and down projections evaluated at FP32 depth depth_gu / depth_d.
+ * d_lo / d_hi [R, H] (and optionally h_lo / h_hi [R, I]) receive the
+ * envelope ends.  Returns the number of candidate sets that had to be cut
+ * (0 means the envelope is complete), or -1 for a bad expert id. */
+int64_t orc_rows_envelope(const uint16_t* x, int64_t R, int64_t H, const uint32_t* ids,
+                          const uint8_t* gu_w, const float* gu_s, const uint8_t* d_w, const float* d_s,
+                          int64_t E, int64_t I, float limit, int depth_gu, int depth_d,
+                          float* d_lo, float* d_hi, float* h_lo_out, float* h_hi_out, int nthreads) {
+  lut_init();
+  for (int64_t r = 0; r < R; ++r)
+    if ((int64_t)ids[r] >= E) return -1;
+  int64_t* start = (int64_t*)calloc((size_t)E + 1, sizeof(int64_t));
+  uint32_t* order = (uint32_t*)malloc(sizeof(uint32_t) * (size_t)(R > 0 ? R : 1));
+  for (int64_t r = 0; r < R; ++r) start[ids[r] + 1]++;
+  for (int64_t e = 0; e < E; ++e) start[e + 1] += start[e];
+  int64_t* fill = (int64_t*)malloc(sizeof(int64_t) * (size_t)E);
+  for (int64_t e = 0; e < E; ++e) fill[e] = start[e];
+  for (int64_t r = 0; r < R; ++r) order[fill[ids[r]]++] = (uint32_t)r;
+  free(fill);
+  env_ctx c;
+  memset(&c, 0, sizeof(c));
+  c.x = x; c.order = order; c.start = start; c.H = H; c.I = I; c.E = E; c.R = R;
+  c.gu_w = gu_w; c.gu_s = gu_s; c.d_w = d_w; c.d_s = d_s; c.limit = limit;
+  c.g_gu = env_gamma(depth_gu);
+  c.g_d = env_gamma(depth_d);
+  c.h_lo = h_lo_out ? h_lo_out : (float*)malloc(sizeof(float) * (size_t)(R * I > 0 ? R * I : 1));
+  c.h_hi = h_hi_out ? h_hi_out : (float*)malloc(sizeof(float) * (size_t)(R * I > 0 ? R * I : 1));
+  c.d_lo = d_lo; c.d_hi = d_hi;
+  pthread_mutex_init(&c.mu, NULL);
+  parallel_for(E * I, nthreads, env_gate_up_item, &c);
+  if (d_lo && d_hi) parallel_for(E * H, nthreads, env_down_item, &c);
+  pthread_mutex_destroy(&c.mu);
+  if (!h_lo_out) free(c.h_lo);
+  if (!h_hi_out) free(c.h_hi);
+  free(start);
+  free(order);
+  return c.wide;
+}
+
+typedef struct {
+  const float* h;          /* [R, I] the kernel's hidden rows */
+  const uint32_t* order;
+  const int64_t* start;
+  int64_t H, I;
+  const uint8_t* d_w;
+  const float* d_s;
+  double g;
+  double* lo;              /* [R, H] */
+  double* hi;
+} down_ctx;
+
+static void down_interval_item(void* p, int64_t item) {
+  down_ctx* c = (down_ctx*)p;
+  const int64_t e = item / c->H, h = item % c->H;
+  const int64_t H = c->H, I = c->I;
+  const int64_t scale_rows = (H + ORC_BLOCK - 1) / ORC_BLOCK;
+  const int64_t scale_cols = (I + ORC_BLOCK - 1) / ORC_BLOCK;
+  const uint8_t* wr = c->d_w + (e * H + h) * I;
+  const float* srow = c->d_s + (e * scale_rows + h / ORC_BLOCK) * scale_cols;
+  for (int64_t q = c->start[e]; q < c->start[e + 1]; ++q) {
+    const int64_t r = c->order[q];
+    const float* hr = c->h + r * I;
+    double mx = 0;
+    for (int64_t k = 0; k < I; ++k) mx = fmax(mx, fabs((double)hr[k]));
+    double tiny, serr;
+    env_f16_staging(mx, &tiny, &serr);
+    double z = 0, a = 0, s16 = 0;
+    for (int64_t k = 0; k < I; ++k) {
+      const double ws = (double)g_lut[wr[k]] * (double)srow[k / ORC_BLOCK];
+      const double t = (double)hr[k] * ws;
+      z += t;
+      a += fabs(t);
+      if (hr[k] != 0 && fabs((double)hr[k]) < tiny) s16 += serr * fabs(ws);
+    }
+    c->lo[r * H + h] = z - c->g * a - s16;
+    c->hi[r * H + h] = z + c->g * a + s16;
+  }
+}
+
+/* Real interval [lo, hi] that contains every FP32 evaluation (at most `depth`
+ * roundings on a term's path) of the down projection of route r's hidden row
+ * h[r] (given values, e.g. the kernel's own) through expert ids[r]: the exact
+ * dot product plus / minus gamma(depth) * sum |terms| (plus the FP16 staging
+ * allowance of orc_rows_envelope for hidden values below FP16's normal range).  The parity tests
+ * check the kernel's FP32 or BF16 down values against it. */
+int orc_down_interval(const float* h, int64_t R, int64_t I, const uint32_t* ids, const uint8_t* d_w,
+                      const float* d_s, int64_t E, int64_t H, int depth, double* lo, double* hi, int nthreads) {
+  lut_init();
+  for (int64_t r = 0; r < R; ++r)
+    if ((int64_t)ids[r] >= E) return 3;
+  int64_t* start = (int64_t*)calloc((size_t)E + 1, sizeof(int64_t));
+  uint32_t* order = (uint32_t*)malloc(sizeof(uint32_t) * (size_t)(R > 0 ? R : 1));
+  for (int64_t r = 0; r < R; ++r) start[ids[r] + 1]++;
+  for (int64_t e = 0; e < E; ++e) start[e + 1] += start[e];
+  int64_t* fill = (int64_t*)malloc(sizeof(int64_t) * (size_t)E);
+  for (int64_t e = 0; e < E; ++e) fill[e] = start[e];
+  for (int64_t r = 0; r < R; ++r) order[fill[ids[r]]++] = (uint32_t)r;
+  free(fill);
+  down_ctx c = {h, order, start, H, I, d_w, d_s, env_gamma(depth), lo, hi};
+  parallel_for(E * H, nthreads, down_interval_item, &c);
+  free(start);
+  free(order);
+  return 0;
+}

@@ -40,6 +40,13 @@ __all__ = [
     "rms_norm",
     "hc_expand",
     "head_major_to_rows",
+    "envelope_depth",
+    "rows_envelope",
+    "packed_decode_envelope",
+    "grouped_envelope",
+    "direct_envelope",
+    "hidden_envelope",
+    "down_interval",
 ]
 
 _HERE = Path(__file__).resolve().parent
@@ -102,6 +109,15 @@ def oracle_lib():
                 ),
                 "orc_rms_norm_bf16": (None, [_u16, _i64, _i64, _u16, ctypes.c_float, _u16]),
                 "orc_hc_expand": (None, [_u16, _u16, _f32, _f32, _i64, _i64, _u16]),
+                "orc_down_interval": (
+                    ctypes.c_int,
+                    [_f32, _i64, _i64, _u32, _u8, _f32, _i64, _i64, ctypes.c_int, _f64, _f64, ctypes.c_int],
+                ),
+                "orc_rows_envelope": (
+                    ctypes.c_int64,
+                    [_u16, _i64, _i64, _u32, _u8, _f32, _u8, _f32, _i64, _i64, ctypes.c_float, ctypes.c_int,
+                     ctypes.c_int, _f32, _f32, _f32, _f32, ctypes.c_int],
+                ),
             }
             for name, (res, args) in sig.items():
                 fn = getattr(lib, name)
@@ -495,3 +511,201 @@ def head_major_to_rows(head_major_bits) -> np.ndarray:
             start = (row * heads + head) * dim
             out[start:start + dim] = hm[head, row]
     return out.reshape(rows, heads * dim)
+
+
+# ----------------------------------------------------------------------------
+# Rounding envelopes: the tolerance certificates of the parity tests
+# ----------------------------------------------------------------------------
+
+# FP32 roundings on any term's path through one projection of length K in
+# the CUDA kernels (orc_rows_envelope states the model): two per MMA and
+# eight MMAs per 128-K block (16), the block-scale product (1), one per block
+# of the FP32 sum over blocks (ceil(K / 128)) and up to eight for a
+# cross-warp or split-K reduction tree.
+def envelope_depth(K: int) -> int:
+    return 25 + (int(K) + 127) // 128
+
+
+ENVELOPE_DEPTH = None  # per projection: envelope_depth(K)
+
+
+def _bf16_round_f32(a) -> np.ndarray:
+    """f32 values -> nearest BF16 values (as f32)."""
+    return f32_from_bf16(bf16_from_f32(np.asarray(a, dtype=np.float32)))
+
+
+def rows_envelope(x_rows_bits, ids, bank, limit: float, *, depth: int | None = None,
+                  threads: int | None = None):
+    """Envelope [lo, hi] (f32 arrays [R, H] of BF16 values) of the BF16 down
+    row of expert ids[r] applied to x_rows[r], over every FP32 evaluation
+    order of its dot products (orc_rows_envelope)."""
+    x = _c(x_rows_bits, np.uint16)
+    ids = _c(ids, np.uint32).reshape(-1)
+    gu_w, gu_s, d_w, d_s = (_c(bank[0], np.uint8), _c(bank[1], np.float32),
+                            _c(bank[2], np.uint8), _c(bank[3], np.float32))
+    E, two_i, H = gu_w.shape
+    R = ids.size
+    x = x.reshape(R, H)
+    lo = np.empty((R, H), dtype=np.float32)
+    hi = np.empty((R, H), dtype=np.float32)
+    if R:
+        cut = oracle_lib().orc_rows_envelope(
+            _p(x, _u16), R, H, _p(ids, _u32), _p(gu_w, _u8), _p(gu_s, _f32), _p(d_w, _u8), _p(d_s, _f32), E,
+            two_i // 2, float(limit), depth or envelope_depth(H), depth or envelope_depth(two_i // 2),
+            _p(lo, _f32), _p(hi, _f32), _p(None, _f32), _p(None, _f32), threads or default_threads())
+        if cut < 0:
+            raise IndexError("expert id out of range")
+        assert cut == 0, f"{cut} candidate sets were cut: the envelope is incomplete"
+    return lo, hi
+
+
+def _shared_as_bank(shared):
+    gw, gs, uw, us, dw, ds = (np.asarray(t) for t in shared)
+    return (np.concatenate([gw, uw])[None], np.concatenate([gs, us])[None], dw[None], ds[None])
+
+
+def _shared_envelope(x_rows_bits, shared, limit, threads):
+    if shared is None:
+        return None
+    R = x_rows_bits.shape[0]
+    return rows_envelope(x_rows_bits, np.zeros(R, np.uint32), _shared_as_bank(shared), limit, threads=threads)
+
+
+def _slot_sum_envelope(d_lo, d_hi, scores):
+    """FP32 slot-ordered weighted sum (packed.py:168-179 / grouped_fp8.py:273-276)
+    at both envelope ends; every step is monotone in each term."""
+    lo = np.zeros(d_lo.shape[1:], dtype=np.float32)
+    hi = np.zeros(d_lo.shape[1:], dtype=np.float32)
+    for j in range(d_lo.shape[0]):
+        s = np.float32(scores[j])
+        a, b = d_lo[j] * s, d_hi[j] * s
+        lo = lo + np.minimum(a, b)
+        hi = hi + np.maximum(a, b)
+    return lo, hi
+
+
+def packed_decode_envelope(x_bits, ids, scores, bank, shared, limit: float, *, threads: int | None = None):
+    """Envelope of PackedFP8MoE's one-token decode output: K8's FP32
+    slot-ordered sum -> BF16, then the BF16 shared add, applied to the ends
+    of the routed and shared rows' envelopes.  Returns (lo, hi, pre_lo,
+    pre_hi): the output ends and the FP32 range of the final rounding's
+    argument."""
+    x = _c(x_bits, np.uint16).reshape(1, -1)
+    ids = _c(ids, np.uint32).reshape(-1)
+    sc = _c(scores, np.float32).reshape(-1)
+    d_lo, d_hi = rows_envelope(np.repeat(x, ids.size, 0), ids, bank, limit, threads=threads)
+    t_lo, t_hi = _slot_sum_envelope(d_lo, d_hi, sc)
+    r_lo, r_hi = _bf16_round_f32(t_lo), _bf16_round_f32(t_hi)
+    sh = _shared_envelope(x, shared, limit, threads)
+    if sh is None:
+        return r_lo, r_hi, t_lo, t_hi
+    p_lo, p_hi = r_lo + sh[0][0], r_hi + sh[1][0]
+    return _bf16_round_f32(p_lo), _bf16_round_f32(p_hi), p_lo, p_hi
+
+
+def grouped_envelope(x_bits, indices, scores, bank, shared, limit: float, *, tokens=None,
+                     threads: int | None = None):
+    """Envelope of SortedGroupedFP8MoE's output rows (restore_and_reduce's FP32
+    slot sum -> BF16, + BF16 shared) for the listed tokens (default all).
+    Returns (lo, hi) [len(tokens), H]."""
+    x = _c(x_bits, np.uint16)
+    H = x.shape[-1]
+    flat = x.reshape(-1, H)
+    idx = _c(indices, np.uint32).reshape(flat.shape[0], -1)
+    sc = _c(scores, np.float32).reshape(flat.shape[0], -1)
+    tok = np.arange(flat.shape[0]) if tokens is None else np.asarray(tokens)
+    k = idx.shape[1]
+    rows = np.repeat(flat[tok], k, 0)
+    d_lo, d_hi = rows_envelope(rows, idx[tok].reshape(-1), bank, limit, threads=threads)
+    d_lo = d_lo.reshape(tok.size, k, H)
+    d_hi = d_hi.reshape(tok.size, k, H)
+    lo = np.zeros((tok.size, H), dtype=np.float32)
+    hi = np.zeros((tok.size, H), dtype=np.float32)
+    for j in range(k):
+        s = sc[tok, j][:, None]
+        a, b = d_lo[:, j] * s, d_hi[:, j] * s
+        lo = lo + np.minimum(a, b)
+        hi = hi + np.maximum(a, b)
+    lo, hi = _bf16_round_f32(lo), _bf16_round_f32(hi)
+    sh = _shared_envelope(flat[tok], shared, limit, threads)
+    if sh is not None:
+        lo, hi = _bf16_round_f32(lo + sh[0]), _bf16_round_f32(hi + sh[1])
+    return lo, hi
+
+
+def direct_envelope(x_bits, indices, scores, bank, shared, limit: float, *, threads: int | None = None):
+    """Envelope of DirectFP8MoE's multi-row output (fp8.py:384-397): per token,
+    BF16(row * score) added in BF16 in ascending expert id, then the BF16
+    shared output added.  Returns (lo, hi) [T, H]."""
+    x = _c(x_bits, np.uint16)
+    H = x.shape[-1]
+    flat = x.reshape(-1, H)
+    T = flat.shape[0]
+    idx = _c(indices, np.int64).reshape(T, -1)
+    sc = _c(scores, np.float32).reshape(T, -1)
+    k = idx.shape[1]
+    d_lo, d_hi = rows_envelope(np.repeat(flat, k, 0), idx.reshape(-1), bank, limit, threads=threads)
+    d_lo = d_lo.reshape(T, k, H)
+    d_hi = d_hi.reshape(T, k, H)
+    lo = np.zeros((T, H), dtype=np.float32)
+    hi = np.zeros((T, H), dtype=np.float32)
+    order = np.argsort(idx, axis=1, kind="stable")
+    tt = np.arange(T)
+    for q in range(k):
+        j = order[:, q]
+        s = sc[tt, j][:, None]
+        a = _bf16_round_f32(d_lo[tt, j] * s)
+        b = _bf16_round_f32(d_hi[tt, j] * s)
+        lo = _bf16_round_f32(lo + np.minimum(a, b))
+        hi = _bf16_round_f32(hi + np.maximum(a, b))
+    sh = _shared_envelope(flat, shared, limit, threads)
+    if sh is not None:
+        lo, hi = _bf16_round_f32(lo + sh[0]), _bf16_round_f32(hi + sh[1])
+    return lo, hi
+
+
+def hidden_envelope(x_rows_bits, ids, bank, limit: float, *, depth: int | None = None,
+                    threads: int | None = None):
+    """Envelope [lo, hi] (f32 [R, I], BF16 values) of the SwiGLU hidden row of
+    expert ids[r] applied to x_rows[r]: the BF16 values that any FP32
+    evaluation order of the gate / up dot products can lead to."""
+    x = _c(x_rows_bits, np.uint16)
+    ids = _c(ids, np.uint32).reshape(-1)
+    gu_w, gu_s = _c(bank[0], np.uint8), _c(bank[1], np.float32)
+    E, two_i, H = gu_w.shape
+    I = two_i // 2
+    R = ids.size
+    x = x.reshape(R, H)
+    lo = np.empty((R, I), dtype=np.float32)
+    hi = np.empty((R, I), dtype=np.float32)
+    if R:
+        dummy_w = np.zeros((1, 1, 1), np.uint8)
+        cut = oracle_lib().orc_rows_envelope(
+            _p(x, _u16), R, H, _p(ids, _u32), _p(gu_w, _u8), _p(gu_s, _f32), _p(dummy_w, _u8),
+            _p(np.zeros(1, np.float32), _f32), E, I, float(limit), depth or envelope_depth(H), 1, _p(None, _f32),
+            _p(None, _f32), _p(lo, _f32), _p(hi, _f32), threads or default_threads())
+        if cut < 0:
+            raise IndexError("expert id out of range")
+        assert cut == 0, f"{cut} candidate sets were cut: the envelope is incomplete"
+    return lo, hi
+
+
+def down_interval(hidden_f32, ids, down_w, down_s, *, depth: int | None = None, threads: int | None = None):
+    """Real interval (f64 [R, H] lo, hi) containing every FP32 evaluation of
+    the down projection of the given hidden rows (orc_down_interval)."""
+    h = _c(hidden_f32, np.float32)
+    ids = _c(ids, np.uint32).reshape(-1)
+    d_w, d_s = _c(down_w, np.uint8), _c(down_s, np.float32)
+    E, H, I = d_w.shape
+    R = ids.size
+    h = h.reshape(R, I)
+    lo = np.empty((R, H), dtype=np.float64)
+    hi = np.empty((R, H), dtype=np.float64)
+    if R:
+        rc = oracle_lib().orc_down_interval(_p(h, _f32), R, I, _p(ids, _u32), _p(d_w, _u8), _p(d_s, _f32), E, H,
+                                            depth or envelope_depth(I), _p(lo, _f64), _p(hi, _f64),
+                                            threads or default_threads())
+        if rc == 3:
+            raise IndexError("expert id out of range")
+        assert rc == 0
+    return lo, hi

@@ -2,6 +2,8 @@
 
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
 import torch
 
@@ -40,23 +42,137 @@ def bf16_ulp(v: np.ndarray) -> np.ndarray:
 
 
 def assert_layer_close(gpu_bits: np.ndarray, ref_bits: np.ndarray, *, max_abs: float = MAX_ABS,
-                       min_cos: float = MIN_COSINE, ulps: int = 1) -> dict:
-    """BF16 layer tolerance: every element within max(max_abs, one BF16 ulp of
-    the reference value) -- above |y| = 4 one ulp is 0.03125, so a single
-    rounding flip of a non-bit-identical FP32 sum exceeds 2e-2 -- and
-    cosine >= min_cos over the tensor."""
+                       min_cos: float = MIN_COSINE, certificate: dict | None = None) -> dict:
+    """North-star layer tolerance: every element within max-abs 2e-2 of the
+    oracle and cosine >= 0.9999 over the tensor.  An element beyond 2e-2 is
+    accepted only when ``certificate`` (from ``certify_*``) proves the whole
+    output: every intermediate BF16 / FP16 / FP32 value of the kernels lies in
+    the oracle's rounding envelope of its exact value (a flip at a BF16
+    rounding midpoint within the stated FP32 evaluation bound) and the final
+    combine reproduces the output bit for bit from them.  Such elements are
+    counted, with their size in BF16 ulps of the oracle value."""
     g, r = f32(gpu_bits), f32(ref_bits)
     assert np.isfinite(g).all(), "non-finite GPU output"
     diff = np.abs(g - r)
     err = float(diff.max()) if g.size else 0.0
-    bound = np.maximum(np.float32(max_abs), np.float32(ulps) * bf16_ulp(r))
-    worst = float((diff / bound).max()) if g.size else 0.0
     cos = cosine(g, r)
     same = float((np.asarray(gpu_bits) == np.asarray(ref_bits)).mean()) if g.size else 1.0
-    over = int((diff > max_abs).sum())
-    assert worst <= 1.0, f"max-abs {err} exceeds max({max_abs}, {ulps} BF16 ulp) (worst ratio {worst:.3f})"
+    over = diff > max_abs
+    n_over = int(over.sum())
+    ulps_over = sorted(set((diff[over] / bf16_ulp(r[over])).round(3).tolist())) if n_over else []
+    if n_over:
+        assert certificate is not None and certificate.get("certified"), (
+            f"{n_over} elements beyond max-abs {max_abs} (largest {err}) and no rounding certificate")
     assert cos >= min_cos, f"cosine {cos} < {min_cos}"
-    return {"max_abs": err, "cosine": cos, "bit_identical": same, "over_max_abs_within_ulp": over}
+    out = {"max_abs": err, "cosine": cos, "bit_identical": same, "beyond_max_abs_certified": n_over,
+           "beyond_ulps": ulps_over}
+    if n_over:
+        print(f"[parity] {n_over} element(s) beyond {max_abs}: certified rounding flips of {ulps_over} BF16 ulp")
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Rounding certificates: every intermediate of the kernels against the
+# oracle's envelope of its exact value, and the final combine bit for bit
+# ---------------------------------------------------------------------------
+
+
+def _f32_down(a: np.ndarray) -> np.ndarray:
+    """Largest FP32 <= each float64 value."""
+    f = a.astype(np.float32)
+    return np.where(f.astype(np.float64) > a, np.nextafter(f, np.float32(-np.inf)), f)
+
+
+def _f32_up(a: np.ndarray) -> np.ndarray:
+    f = a.astype(np.float32)
+    return np.where(f.astype(np.float64) < a, np.nextafter(f, np.float32(np.inf)), f)
+
+
+def bf16_round(a) -> np.ndarray:
+    """FP32 values -> nearest-even BF16 values, as FP32."""
+    import oracle as O
+
+    return O.f32_from_bf16(O.bf16_from_f32(np.asarray(a, dtype=np.float32)))
+
+
+def certify_expert_rows(x_rows_bits, ids, bank, limit, hidden, down, *, down_kind: str,
+                        hidden_fp16: bool = False) -> dict:
+    """Certificate of per-route expert rows computed by the GPU.
+
+    hidden: the kernel's SwiGLU hidden rows [R, I] as FP32 values (stored as
+    BF16, or as FP16 when ``hidden_fp16``); down: the kernel's down
+    projections [R, H] -- FP32 values before rounding (``down_kind="f32"``)
+    or BF16 bits (``"bf16"``).
+      1. every hidden value is one of the BF16 values reachable from the exact
+         gate / up dot products by an FP32 evaluation within the stated bound
+         (``oracle.hidden_envelope``; for FP16 storage, the FP16 roundings of
+         the envelope's ends);
+      2. every down value lies in the interval of every FP32 evaluation of the
+         down projection of the kernel's own hidden row
+         (``oracle.down_interval``), or, for BF16 rows, between the BF16
+         roundings of its ends.
+    Returns counts of the values that sit on a rounding flip."""
+    import oracle as O
+
+    h_lo, h_hi = O.hidden_envelope(x_rows_bits, ids, bank, limit)
+    if hidden_fp16:
+        h_lo = h_lo.astype(np.float16).astype(np.float32)
+        h_hi = h_hi.astype(np.float16).astype(np.float32)
+    hidden = np.asarray(hidden, dtype=np.float32)
+    bad = (hidden < h_lo) | (hidden > h_hi)
+    assert not bad.any(), (f"{int(bad.sum())} hidden values outside their rounding envelope, e.g. "
+                           f"{hidden[bad][:4]} vs [{h_lo[bad][:4]}, {h_hi[bad][:4]}]")
+    lo, hi = O.down_interval(hidden, ids, bank[2], bank[3])
+    if down_kind == "f32":
+        d = np.asarray(down, dtype=np.float32)
+        ok = (d >= _f32_down(lo)) & (d <= _f32_up(hi))
+        straddle = bf16_round(_f32_down(lo)) != bf16_round(_f32_up(hi))
+    else:
+        d = f32(down)
+        d_lo, d_hi = bf16_round(_f32_down(lo)), bf16_round(_f32_up(hi))
+        ok = (d >= d_lo) & (d <= d_hi)
+        straddle = d_lo != d_hi
+    assert ok.all(), (f"{int((~ok).sum())} down values outside the FP32 evaluation interval of the kernel's "
+                      f"own hidden rows")
+    return {"hidden_values": int(hidden.size), "hidden_envelope_two_or_more": int((h_hi > h_lo).sum()),
+            "down_values": int(d.size), "down_on_bf16_midpoint_band": int(straddle.sum())}
+
+
+def slot_combine(down_f32_rows, scores, shared=None) -> np.ndarray:
+    """The packed decode / grouped combine (packed.py:168-179,
+    grouped_fp8.py:273-276): FP32 slot-ordered sum of BF16 rows times FP32
+    scores -> BF16, then the BF16 shared add.  down_f32_rows [k, ..., H] BF16
+    values as FP32; returns BF16 bits."""
+    import oracle as O
+
+    total = np.zeros(down_f32_rows.shape[1:], dtype=np.float32)
+    for j in range(down_f32_rows.shape[0]):
+        s = np.asarray(scores[j], dtype=np.float32)
+        s = s[..., None] if s.ndim else s
+        total = total + down_f32_rows[j] * s
+    res = bf16_round(total)
+    if shared is not None:
+        res = res + np.asarray(shared, dtype=np.float32)
+    return O.bf16_from_f32(res)
+
+
+def direct_combine(rows_f32, ids, scores, shared=None) -> np.ndarray:
+    """DirectFP8MoE's multi-row combine (fp8.py:384-397): per token,
+    BF16(row * score) added in BF16 in ascending expert id, then + shared.
+    rows_f32 [T, k, H]; returns BF16 bits [T, H]."""
+    import oracle as O
+
+    T, k, H = rows_f32.shape
+    order = np.argsort(np.asarray(ids).reshape(T, k), axis=1, kind="stable")
+    acc = np.zeros((T, H), dtype=np.float32)
+    tt = np.arange(T)
+    for q in range(k):
+        j = order[:, q]
+        w = bf16_round(rows_f32[tt, j] * np.asarray(scores, dtype=np.float32).reshape(T, k)[tt, j][:, None])
+        acc = bf16_round(acc + w)
+    if shared is not None:
+        acc = bf16_round(acc + np.asarray(shared, dtype=np.float32))
+    return O.bf16_from_f32(acc)
 
 
 def bank_host(bank, ids=None):
@@ -71,3 +187,125 @@ def bank_host(bank, ids=None):
 
 def shared_host(shared_tensors):
     return None if shared_tensors is None else tuple(t.cpu().numpy() for t in shared_tensors)
+
+
+def _shared_bank(shared_host_tuple):
+    gw, gs, uw, us, dw, ds = shared_host_tuple
+    return (np.concatenate([gw, uw])[None], np.concatenate([gs, us])[None], dw[None], ds[None])
+
+
+def workspace_view(buf: torch.Tensor, offset: int, dtype, count: int) -> np.ndarray:
+    """count values of dtype at byte offset of a device workspace (host copy)."""
+    nbytes = np.dtype(dtype).itemsize * count
+    return buf[offset:offset + nbytes].cpu().numpy().view(dtype)
+
+
+def certify_packed_decode(x_bits, ids, scores, bank, shared, limit, out_bits, workspace: torch.Tensor) -> dict:
+    """Certificate of one glm53_packed_decode_moe call from the intermediates
+    it leaves in its workspace (glm53_packed_decode_workspace_layout): the
+    routed and shared hidden rows and FP32 down projections are certified by
+    ``certify_expert_rows``, and the output is K8's slot-ordered combine of the
+    rounded down rows plus the rounded shared row, bit for bit.  bank / shared
+    are host tuples (bank_host / shared_host)."""
+    from glm53_flash_mlx_b200 import _native as N
+
+    ids = np.asarray(ids, dtype=np.uint32).reshape(-1)
+    top_k = ids.size
+    H = bank[0].shape[2]
+    I = bank[0].shape[1] // 2
+    Is = 0 if shared is None else shared[0].shape[0]
+    offs = (ctypes.c_size_t * 2)()
+    N.check(N.lib().glm53_packed_decode_workspace_layout(top_k, H, I, Is, offs), "layout")
+    hidden = f32(workspace_view(workspace, offs[0], np.uint16, top_k * I + Is))
+    partial = workspace_view(workspace, offs[1], np.float32, (top_k + 1) * H).reshape(top_k + 1, H)
+    x = np.asarray(x_bits, dtype=np.uint16).reshape(1, H)
+    cert = certify_expert_rows(np.repeat(x, top_k, 0), ids, bank, limit, hidden[:top_k * I].reshape(top_k, I),
+                               partial[:top_k], down_kind="f32")
+    shared_row = None
+    if shared is not None:
+        cs = certify_expert_rows(x, np.zeros(1, np.uint32), _shared_bank(shared), limit,
+                                 hidden[top_k * I:].reshape(1, Is), partial[top_k:top_k + 1], down_kind="f32")
+        cert = {k: cert[k] + cs[k] for k in cert}
+        shared_row = bf16_round(partial[top_k])
+    expect = slot_combine(bf16_round(partial[:top_k]), np.asarray(scores, dtype=np.float32).reshape(-1),
+                          shared=shared_row)
+    same = np.asarray(out_bits).reshape(-1) == expect
+    assert same.all(), f"{int((~same).sum())} outputs differ from the combine of the certified intermediates"
+    cert["certified"] = True
+    return cert
+
+
+def certify_linear(x_bits, weight, scale_inv, y_bits) -> dict:
+    """Certificate of a block-FP8 linear: each output is one of the BF16
+    roundings of an FP32 evaluation of its dot product within the stated
+    bound (one rounding site)."""
+    import oracle as O
+
+    x = f32(np.asarray(x_bits, dtype=np.uint16))
+    M, K = x.shape
+    N_ = weight.shape[0]
+    lo, hi = O.down_interval(x, np.zeros(M, np.uint32), np.asarray(weight)[None], np.asarray(scale_inv)[None])
+    y = f32(np.asarray(y_bits, dtype=np.uint16)).reshape(M, N_)
+    d_lo, d_hi = bf16_round(_f32_down(lo)), bf16_round(_f32_up(hi))
+    ok = (y >= d_lo) & (y <= d_hi)
+    assert ok.all(), f"{int((~ok).sum())} linear outputs outside the FP32 evaluation interval"
+    return {"certified": True, "outputs_on_bf16_midpoint_band": int((d_lo != d_hi).sum())}
+
+
+def certify_grouped(x_bits, indices, scores, bank, shared, limit, out_bits, workspace: torch.Tensor,
+                    tokens=None) -> dict:
+    """Certificate of one glm53_grouped_moe call (tensor-core path) for the
+    listed tokens, from the intermediates it leaves in its workspace
+    (glm53_grouped_moe_workspace_layout): each route's FP16 hidden row and
+    BF16 down row, and the shared expert's, are certified by
+    ``certify_expert_rows``; each token's output is restore_and_reduce's
+    slot-ordered combine of its down rows plus its shared row, bit for bit.
+    x_bits / indices / scores / out_bits cover all T tokens; bank / shared are
+    host tuples."""
+    from glm53_flash_mlx_b200 import _native as N
+
+    x = np.asarray(x_bits, dtype=np.uint16)
+    T, H = x.shape
+    idx = np.asarray(indices).reshape(T, -1).astype(np.uint32)
+    sc = np.asarray(scores, dtype=np.float32).reshape(T, -1)
+    k = idx.shape[1]
+    E = bank[0].shape[0]
+    I = bank[0].shape[1] // 2
+    Is = 0 if shared is None else shared[0].shape[0]
+    R = T * k
+    offs = (ctypes.c_size_t * 8)()
+    N.check(N.lib().glm53_grouped_moe_workspace_layout(T, k, E, H, I, Is, offs), "layout")
+    inverse = workspace_view(workspace, offs[1], np.uint32, R)
+    sorted_scores = workspace_view(workspace, offs[3], np.float32, R)
+    tok = np.arange(T) if tokens is None else np.asarray(tokens)
+    pos = inverse.reshape(T, k)[tok].reshape(-1).astype(np.int64)
+    assert np.array_equal(sorted_scores[pos], sc[tok].reshape(-1)), "sorted scores do not match the routes"
+    hid_all = workspace[offs[4]:offs[4] + R * I * 2].view(torch.float16).reshape(R, I)
+    dn_all = workspace[offs[5]:offs[5] + R * H * 2].view(torch.int16).reshape(R, H)
+    pos_t = torch.from_numpy(pos).to(workspace.device)
+    hidden = hid_all.index_select(0, pos_t).float().cpu().numpy()
+    down = dn_all.index_select(0, pos_t).cpu().numpy().view(np.uint16)
+    # bank restricted to the touched experts (the certificate reads only those)
+    ids = idx[tok].reshape(-1)
+    touched, local = np.unique(ids, return_inverse=True)
+    sub = tuple(b[touched] for b in bank)
+    cert = certify_expert_rows(np.repeat(x[tok], k, 0), local.astype(np.uint32), sub, limit, hidden, down,
+                               down_kind="bf16", hidden_fp16=True)
+    shared_rows = None
+    if shared is not None:
+        sh_h = workspace[offs[6]:offs[6] + T * Is * 2].view(torch.float16).reshape(T, Is)
+        sh_o = workspace[offs[7]:offs[7] + T * H * 2].view(torch.int16).reshape(T, H)
+        t_t = torch.from_numpy(tok.astype(np.int64)).to(workspace.device)
+        sh_hidden = sh_h.index_select(0, t_t).float().cpu().numpy()
+        sh_out = sh_o.index_select(0, t_t).cpu().numpy().view(np.uint16)
+        cs = certify_expert_rows(x[tok], np.zeros(tok.size, np.uint32), _shared_bank(shared), limit, sh_hidden,
+                                 sh_out, down_kind="bf16", hidden_fp16=True)
+        cert = {key: cert[key] + cs[key] for key in cert}
+        shared_rows = f32(sh_out)
+    rows = f32(down).reshape(tok.size, k, H).transpose(1, 0, 2)
+    expect = slot_combine(rows, sc[tok].T, shared=shared_rows)
+    got = np.asarray(out_bits, dtype=np.uint16).reshape(T, H)[tok]
+    same = got == expect
+    assert same.all(), f"{int((~same).sum())} outputs differ from the combine of the certified intermediates"
+    cert["certified"] = True
+    return cert

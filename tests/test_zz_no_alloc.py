@@ -114,3 +114,20 @@ def test_static_scratch_rejects_sizes_beyond_the_fixed_maximum():
     assert rc == N.GLM53_ERR_INVALID
     msg = lib.glm53_last_error().decode()
     assert "fixed maximum" in msg and str(need) in msg
+
+
+def test_static_scratch_rejects_the_after_router_flag():
+    """The scratch counters are cleared by a stream operation before the decode,
+    so the decode cannot be launched as the router's programmatic dependent:
+    GLM53_FLAG_AFTER_ROUTER is refused (before any CUDA call) instead of being
+    dropped silently."""
+    from glm53_flash_mlx_b200 import _native as N
+
+    lib = N.load_library()
+    H, I, top_k = 4096, 1536, 8
+    fake = ctypes.c_void_p(256)  # never dereferenced: the call is rejected first
+    rc = lib.glm53_packed_decode_moe_static_scratch(
+        fake, H, fake, fake, top_k, fake, fake, fake, fake, 16, I, fake, fake, fake, fake, fake, fake, I, 10.0,
+        fake, fake, N.FLAG_AFTER_ROUTER | N.FLAG_E4M3_FINITE, None)
+    assert rc == N.GLM53_ERR_INVALID
+    assert "GLM53_FLAG_AFTER_ROUTER" in lib.glm53_last_error().decode()
