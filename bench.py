@@ -471,18 +471,21 @@ def bench_b200(args, world, rank, local):
     if e2e_module is not None:
         extra["e2e_module"] = e2e_module
     if not args.no_prefill:
-        extra["prefill_2048"] = bench_prefill(layers, dev, args)
+        for T in (256, 2048, 8192):
+            extra[f"prefill_{T}"] = bench_prefill(layers, dev, args, T)
         extra["linear_config1_5"] = bench_linear(dev, args)
         extra["batched_decode"] = bench_batched(layers, dev, args)
+        extra["ep_batched"] = {f"B{B}": bench_ep_batched(layers, dev, args, 1, 0, B) for B in (16, 64)}
         extra["ffn_boundary"] = bench_hc(dev, args)
     return {"value": value, "t_ms": t_ms, "clocks": clk, "roofline": roofline, "e2e": e2e,
             "gpu_launches": args.steps * 3, **extra}, layers, xs
 
 
 def bench_batched(layers, dev, args):
-    """Secondary: config 4's batched decode on one GPU -- B = 16 tokens through
-    PackedFP8MoE (router + batched per-route decode + BF16 combine + shared
-    expert) versus the Direct module's per-expert loop on the same layer."""
+    """Secondary: batched decode on one GPU -- B = 16, 24 and 64 tokens through
+    PackedFP8MoE (router + expert-coalesced batched decode + BF16 combine in
+    ascending expert id + shared expert: the Direct module's multi-row
+    semantics) versus the Direct module's per-expert loop on the same layer."""
     import torch
 
     import glm53_flash_mlx_b200 as G
@@ -497,7 +500,7 @@ def bench_batched(layers, dev, args):
     gate.e_score_correction_bias.copy_(L["router_b"])
     mod = G.PackedFP8MoE(L["bank"], cfg, gate, L["shared_mod"])
     out = {}
-    for B in (16,):
+    for B in (16, 24, 64):
         xs = [S.random_bf16((1, B, H), seed=500 + i, device=dev) for i in range(8)]
         for i in range(3):
             mod(xs[i % 8])
@@ -748,19 +751,103 @@ def bench_ep(args, world, rank, local):
     for p in plans + ([m.plan for m in mods] if not args.no_e2e else []):
         p.close()
     launches = 5 if args.ep_transport == "p2p" else 8
-    return {"value": value, "t_ms": t_ms, "clocks": clk, "roofline": roofline, "e2e": e2e,
-            "gpu_launches": args.steps * launches, "graph": graph_mode + f"; transport {args.ep_transport}"}
+    res = {"value": value, "t_ms": t_ms, "clocks": clk, "roofline": roofline, "e2e": e2e,
+           "gpu_launches": args.steps * launches, "graph": graph_mode + f"; transport {args.ep_transport}"}
+    if not args.no_prefill:
+        res["ep_batched"] = {f"B{B}": bench_ep_batched(layers, dev, args, world, rank, B) for B in (16, 64)}
+    return res
 
 
-def bench_prefill(layers, dev, args):
-    """Secondary: config 3 grouped prefill, T=2048, Zipf-skewed router bias."""
+def bench_ep_batched(layers, dev, args, world: int, rank: int, B: int) -> dict:
+    """Config 4 at B tokens per rank: each step routes B tokens through one
+    layer (the FP32 router, then ExpertParallelDecode with max_tokens = B:
+    dispatch to the experts' ranks over NCCL all-to-all -- a local copy at
+    N = 1 -- the owners' expert-coalesced decode, the return all-to-all and the
+    slot-ordered combine with the shared expert).  Layers rotate (8 distinct
+    seeded layers: the 42-layer stack does not fit one GPU's HBM, 228 GB of
+    experts), so the figure is per layer; `tokens_per_s_42_layers` divides it
+    by 42.  Steps are CUDA-graph captured, device-timed, max over ranks."""
+    import torch
+
+    from glm53_flash_mlx_b200 import _native as N
+    from glm53_flash_mlx_b200 import ep
+    from glm53_flash_mlx_b200 import synthetic as S
+
+    lib = N.lib()
+    n_exp = args.experts
+    plans = [ep.ExpertParallelDecode(L["bank"], experts=n_exp, rank=rank, world=world, shared=L["shared"],
+                                     limit=LIMIT, max_tokens=B, transport="nccl") for L in layers]
+    xs = S.random_bf16((4, B, H), seed=91 + rank, device=dev)
+    ws = N.Workspace()
+    rws = ws.get(dev, "router", lib.glm53_router_workspace_bytes(B, n_exp))
+    n_graph = 2 * len(layers)
+    idxs = [torch.empty((B, TOP_K), dtype=torch.int32, device=dev) for _ in range(n_graph)]
+    scs = [torch.empty((B, TOP_K), dtype=torch.float32, device=dev) for _ in range(n_graph)]
+    outs = [torch.empty((B, H), dtype=torch.bfloat16, device=dev) for _ in range(n_graph)]
+    touched = []
+
+    def step(i, stream):
+        L = layers[i % len(layers)]
+        x = xs[i % 4]
+        N.check(lib.glm53_router_topk(x.data_ptr(), B, H, L["router_w"].data_ptr(), n_exp, L["router_b"].data_ptr(),
+                                      TOP_K, 1, 1, 1, 1.0, idxs[i].data_ptr(), scs[i].data_ptr(), None,
+                                      rws.data_ptr(), rws.numel(), stream), "router")
+        plans[i % len(layers)](x, idxs[i], scs[i], out=outs[i])
+
+    s = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(s):
+        for i in range(n_graph):
+            step(i, s.cuda_stream)
+    s.synchronize()
+    touched = [int(torch.unique(idxs[i]).numel()) for i in range(n_graph)]
+    barrier(world)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for i in range(n_graph):
+            step(i, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    g.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    reps = max(3, min(50, 2000 // n_graph // max(1, B // 8)))
+    st, sp = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st.record()
+    for _ in range(reps):
+        g.replay()
+    sp.record()
+    torch.cuda.synchronize()
+    t_ms = max_over_ranks(st.elapsed_time(sp), world) / (reps * n_graph)
+    bad = max_over_ranks(float(max(int(p.status.item()) for p in plans)), world)
+    del g
+    torch.cuda.synchronize()
+    for p in plans:
+        p.close()
+    if bad:
+        raise RuntimeError(f"device status 0x{int(bad):x} in the batched expert-parallel decode")
+    peaks = measured_peaks()
+    mean_touched = statistics.mean(touched)
+    # bytes one rank streams per step: its share of the touched experts, the
+    # shared expert and the router
+    step_bytes = (mean_touched / world) * 3 * H * I + 3 * H * I + n_exp * H * 4
+    return {"batch_per_rank": B, "tokens_per_step": B * world, "ms_per_layer_step": round(t_ms, 4),
+            "tokens_per_s_per_layer": round(B * world / (t_ms / 1e3), 1),
+            "tokens_per_s_42_layers": round(B * world / (42 * t_ms / 1e3), 1),
+            "touched_experts_per_step": round(mean_touched, 1),
+            "hbm_frac_per_rank": round(step_bytes / (t_ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
+            "transport": "nccl all-to-all" if world > 1 else "local (one GPU)",
+            "owner_decode": "expert-coalesced (glm53_routes_decode_coalesced)",
+            "layers_rotated": len(layers), "steps_timed": reps * n_graph}
+
+
+def bench_prefill(layers, dev, args, T: int = 2048):
+    """Secondary: config 3 grouped prefill at T tokens (256, 2048, 8192),
+    Zipf-skewed router bias; layers rotate so weights stream from HBM."""
     import torch
 
     import glm53_flash_mlx_b200 as G
     from glm53_flash_mlx_b200 import _native as N
     from glm53_flash_mlx_b200 import synthetic as S
 
-    T = 2048
     x = S.random_bf16((T, H), seed=4242, device=dev)
     n_exp = layers[0]["bank"].expert_count
     w, b = S.make_router(n_exp, H, seed=4243, device=dev, zipf_alpha=0.5)
@@ -785,10 +872,19 @@ def bench_prefill(layers, dev, args):
     bytes_ = (touched + 1) * 3 * H * I + n_exp * H * 4 + 2 * T * H * 2
     flops = 2 * T * TOP_K * 3 * H * I + 2 * T * 3 * H * I + 2 * T * n_exp * H
     peaks = measured_peaks()
-    return {"tokens_per_s": round(T / (ms / 1e3), 1), "ms_per_layer": round(ms, 3), "touched_experts": touched,
+    t_hbm = bytes_ / (peaks["hbm_gbs"] * 1e9)
+    t_tc = flops / (peaks["bf16_tflops"] * 1e12)
+    loads = torch.bincount(idx.reshape(-1).long(), minlength=n_exp)
+    return {"tokens": T, "tokens_per_s": round(T / (ms / 1e3), 1), "ms_per_layer": round(ms, 3),
+            "touched_experts": touched, "max_routes_per_expert": int(loads.max()),
+            "mean_routes_per_touched_expert": round(T * TOP_K / max(touched, 1), 1),
             "algorithmic_bytes": bytes_, "flops": flops,
-            "hbm_frac": round(bytes_ / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
-            "note": "router + route plan + grouped gate/up (SwiGLU epilogue) + grouped down + shared + combine"}
+            "hbm_frac": round(t_hbm / (ms / 1e3), 4),
+            "tensor_frac": round(t_tc / (ms / 1e3), 4),
+            "roofline_frac": round(max(t_hbm, t_tc) / (ms / 1e3), 4),
+            "roofline_bound": "hbm" if t_hbm >= t_tc else "tensor (bf16, measured)",
+            "note": "router + route plan + grouped gate/up (SwiGLU epilogue) + grouped down + shared + combine; "
+                    "tensor_frac against the measured dense BF16 peak (the MMAs run kind::f16)"}
 
 
 def bench_hc(dev, args):
@@ -1054,7 +1150,8 @@ def main():
         dev = torch.device("cuda", local)
         layers = build_layers(args.layers, 1000 + 101 * rank, dev, args.experts)
         if rank == 0:
-            print(json.dumps({"prefill_2048": bench_prefill(layers, dev, args)}), flush=True)
+            print(json.dumps({f"prefill_{T}": bench_prefill(layers, dev, args, T)
+                              for T in (256, 2048, 8192)}), flush=True)
         return
     if world > 1:
         res = bench_ep(args, world, rank, local)

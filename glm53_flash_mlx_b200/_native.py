@@ -81,6 +81,11 @@ SIGNATURES: dict[str, tuple] = {
         [_vp, _i64, _i64, _vp, _vp, _int, _vp, _vp, _vp, _vp, _i64, _i64, _f, _vp, _vp, _vp, _sz, _vp, _u32, _vp],
     ),
     "glm53_routes_decode_workspace_bytes": (_sz, [_i64, _i64, _i64]),
+    "glm53_routes_decode_coalesced_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64]),
+    "glm53_routes_decode_coalesced": (
+        _int,
+        [_vp, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f, _vp, _vp, _sz, _vp, _u32, _vp],
+    ),
     "glm53_routes_decode": (
         _int,
         [_vp, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f, _vp, _vp, _sz, _vp, _u32, _vp],
@@ -117,6 +122,11 @@ SIGNATURES: dict[str, tuple] = {
     "glm53_grouped_fp8_linear": (
         _int,
         [_vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _vp, _vp, _u32, _vp],
+    ),
+    "glm53_grouped_fp8_linear_workspace_bytes": (_sz, [_i64, _i64]),
+    "glm53_grouped_fp8_linear_ws": (
+        _int,
+        [_vp, _i64, _i64, _vp, _vp, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _sz, _vp, _u32, _vp],
     ),
     "glm53_activate_gate_up": (_int, [_vp, _i64, _i64, _f, _vp, _vp]),
     "glm53_restore_and_reduce": (_int, [_vp, _vp, _vp, _i64, _int, _i64, _vp, _vp, _vp]),

@@ -53,7 +53,8 @@ struct BatchedArgs {
   const float* sd_s;
   float limit;
   uint16_t* hidden;  // [R, I] sorted route order
-  uint16_t* rows;    // [R, H] sorted route order
+  uint16_t* rows;    // [R, H] sorted route order, or route order through `scatter`
+  const uint32_t* scatter;  // sorted position -> output row (null: sorted order)
   uint32_t* status;
 };
 
@@ -252,7 +253,8 @@ __global__ void __launch_bounds__(32 * kBdWarps) batched_down_kernel(BatchedArgs
     for (int cc = 0; cc < 2; ++cc) {
       const int c = 2 * q + cc;
       if (c < len) {
-        uint16_t* dst = a.rows + (size_t)(start + c) * a.H + row0;
+        const size_t out_row = a.scatter ? (size_t)__ldg(a.scatter + start + c) : (size_t)(start + c);
+        uint16_t* dst = a.rows + out_row * a.H + row0;
         dst[g] = valid ? f32_to_bf16_bits(tot[cc]) : (uint16_t)0;
         dst[g + 8] = valid ? f32_to_bf16_bits(tot[2 + cc]) : (uint16_t)0;
       }
@@ -422,6 +424,65 @@ static int batched_decode(const char* fn, const void* x, int64_t T, int64_t H, c
   if (rc) return rc;
   return direct_combine_rows(a.rows, (const uint32_t*)(ws + wl.inverse), expert_ids, scores, T, top_k, H, E,
                              (const uint16_t*)shared, (uint16_t*)out, status, st);
+}
+
+extern "C" size_t glm53_routes_decode_coalesced_workspace_bytes(int64_t R, int64_t E, int64_t H, int64_t I) {
+  return R > 0 && E > 0 ? batched_workspace(R, E, H, I).bytes : 0;
+}
+
+extern "C" int glm53_routes_decode_coalesced(const void* x_rows, int64_t R, int64_t H, const uint32_t* expert_ids,
+                                             const uint8_t* gate_up_w, const float* gate_up_s,
+                                             const uint8_t* down_w, const float* down_s, int64_t E, int64_t I,
+                                             float limit, void* out_rows, void* workspace, size_t workspace_bytes,
+                                             uint32_t* status, uint32_t flags, void* stream) {
+  const char* fn = "glm53_routes_decode_coalesced";
+  if (R < 0 || H <= 0 || I <= 0 || E <= 0 || H % 128 != 0 || I % 128 != 0 || H > 32768 || I > 32768 ||
+      R > kBdMaxRoutes || E >= 0x7FFFFFFF) {
+    set_last_error("%s: unsupported geometry R=%lld H=%lld I=%lld E=%lld", fn, (long long)R, (long long)H,
+                   (long long)I, (long long)E);
+    return GLM53_ERR_INVALID;
+  }
+  if (R == 0) return GLM53_OK;
+  const BatchedWorkspace wl = batched_workspace(R, E, H, I);
+  if (!x_rows || !expert_ids || !gate_up_w || !gate_up_s || !down_w || !down_s || !out_rows || !workspace ||
+      !status || workspace_bytes < wl.bytes ||
+      (((uintptr_t)x_rows | (uintptr_t)gate_up_w | (uintptr_t)down_w | (uintptr_t)out_rows |
+        (uintptr_t)workspace) & 15) != 0) {
+    set_last_error("%s: missing pointer, misaligned tensor or workspace too small", fn);
+    return GLM53_ERR_INVALID;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  char* ws = (char*)workspace;
+  BatchedArgs a{};
+  a.x = (const uint16_t*)x_rows;
+  a.H = (int)H;
+  a.I = (int)I;
+  a.E = (int)E;
+  a.top_k = 1;  // route r reads row r
+  a.order = (const uint32_t*)(ws + wl.order);
+  a.tile_experts = (const uint32_t*)(ws + wl.tile_experts);
+  a.tile_starts = (const uint32_t*)(ws + wl.tile_starts);
+  a.tile_lengths = (const uint32_t*)(ws + wl.tile_lengths);
+  a.descriptor_count = (const uint32_t*)(ws + wl.counts);
+  a.gu_w = gate_up_w;
+  a.gu_s = gate_up_s;
+  a.d_w = down_w;
+  a.d_s = down_s;
+  a.limit = limit;
+  a.hidden = (uint16_t*)(ws + wl.hidden);
+  a.rows = (uint16_t*)out_rows;
+  a.scatter = (const uint32_t*)(ws + wl.order);
+  a.status = status;
+  // ids >= E (the empty-slot mark among them) fall into the plan's invalid
+  // bucket: no descriptor, so their rows are left untouched
+  int rc = route_plan(expert_ids, R, E, kBdCols, nullptr, (uint32_t*)(ws + wl.order), (uint32_t*)(ws + wl.inverse),
+                      (uint32_t*)(ws + wl.sorted_experts), nullptr, (uint32_t*)(ws + wl.route_offsets),
+                      (uint32_t*)(ws + wl.tile_experts), (uint32_t*)(ws + wl.tile_starts),
+                      (uint32_t*)(ws + wl.tile_lengths), (uint32_t*)(ws + wl.tile_offsets),
+                      (uint32_t*)(ws + wl.counts), (uint32_t*)(ws + wl.counts) + 1, st);
+  if (rc) return rc;
+  const int64_t capacity = (R + kBdCols - 1) / kBdCols + E;
+  return (flags & GLM53_FLAG_E4M3_FINITE) ? launch_batched<true>(a, capacity, st) : launch_batched<false>(a, capacity, st);
 }
 
 extern "C" int glm53_batched_decode_moe(const void* x, int64_t T, int64_t H, const uint32_t* expert_ids,

@@ -124,6 +124,41 @@ def routes_decode(x_rows: torch.Tensor, expert_ids: torch.Tensor, bank: tuple, *
     return out
 
 
+def routes_decode_coalesced(x_rows: torch.Tensor, expert_ids: torch.Tensor, bank: tuple, *, limit: float,
+                            out: torch.Tensor | None = None, workspace: N.Workspace | None = None,
+                            status: torch.Tensor | None = None, flags: int | None = None) -> torch.Tensor:
+    """``routes_decode`` with expert coalescing (``glm53_routes_decode_coalesced``):
+    each touched expert's weights stream once per four of its slots; same bits
+    per slot.  Slots with an id >= E (e.g. ``EMPTY_SLOT``) are left untouched."""
+    gu_w, gu_s, d_w, d_s = bank
+    dev = N.require_cuda(x_rows, expert_ids, gu_w)
+    R, H = x_rows.shape
+    E, I2, _ = gu_w.shape
+    I = I2 // 2
+    if out is None:
+        out = torch.empty((R, H), dtype=torch.bfloat16, device=dev)
+    wsp = workspace or N.Workspace()
+    ws = wsp.get(dev, "routes_coalesced", N.lib().glm53_routes_decode_coalesced_workspace_bytes(R, E, H, I))
+    if status is None:
+        status = wsp.get(dev, "status", 4)
+    if flags is None:
+        flags = N.decode_flags(gu_w, d_w)
+    N.check(
+        N.lib().glm53_routes_decode_coalesced(
+            x_rows.data_ptr(), R, H, expert_ids.data_ptr(), gu_w.data_ptr(), gu_s.data_ptr(), d_w.data_ptr(),
+            d_s.data_ptr(), E, I, float(limit), out.data_ptr(), ws.data_ptr(), ws.numel(), status.data_ptr(), flags,
+            N.stream(dev),
+        ),
+        "glm53_routes_decode_coalesced",
+    )
+    return out
+
+
+# Slots per step above which the owners decode with expert coalescing (a
+# batch of tokens per rank touches experts more than once per step).
+COALESCE_MIN_SLOTS = 16
+
+
 class ExpertParallelDecode:
     """Plan-owned buffers and the five steps above for one layer.
 
@@ -259,12 +294,14 @@ class ExpertParallelDecode:
                 "glm53_ep_dispatch_pack")
         self._exchange(self.recv_x, self.send_x)
         self._exchange(self.recv_e, self.send_e)
-        routes_decode(self.recv_x, self.recv_e, self.bank, limit=self.limit, out=self.rows,
-                      workspace=self.workspace, status=self.status, flags=self.flags)
+        decode = routes_decode_coalesced if self.recv_e.numel() >= COALESCE_MIN_SLOTS else routes_decode
+        decode(self.recv_x, self.recv_e, self.bank, limit=self.limit, out=self.rows, workspace=self.workspace,
+               status=self.status, flags=self.flags)
         shared_ptr = None
         if self.shared_bank is not None:
-            routes_decode(flat, self.zero_ids[:T], self.shared_bank, limit=self.limit, out=self.shared_rows[:T],
-                          workspace=self.workspace, status=self.status, flags=self.shared_flags)
+            decode_s = routes_decode_coalesced if T > 1 else routes_decode
+            decode_s(flat, self.zero_ids[:T], self.shared_bank, limit=self.limit, out=self.shared_rows[:T],
+                     workspace=self.workspace, status=self.status, flags=self.shared_flags)
             shared_ptr = self.shared_rows.data_ptr()
         self._exchange(self.back, self.rows)
         N.check(lib.glm53_ep_combine(self.back.data_ptr(), self.route_pos.data_ptr(), self.slot_scores.data_ptr(), T,

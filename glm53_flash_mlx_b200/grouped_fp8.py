@@ -98,8 +98,19 @@ def build_grouped_tile_plan(sorted_experts, expert_count: int, *, tile_rows: int
             plan["tile_offsets"])
 
 
-def grouped_fp8_linear(x, tile_plan, weight, scale_inv):
-    """Project sorted route rows from a packed block-FP8 expert bank."""
+_LINEAR_WS = N.Workspace()
+_LINEAR_STATUS: dict = {}
+
+
+def grouped_fp8_linear(x, tile_plan, weight, scale_inv, *, tile_rows: int = GROUPED_TILE_ROWS):
+    """Project sorted route rows from a packed block-FP8 expert bank.
+
+    Runs the tcgen05 grouped GEMM (exact FP16 weights, FP32 accumulation with
+    per-128-K promotion) over the plan's descriptors; ``tile_rows`` is the
+    longest descriptor the plan may hold (``build_grouped_tile_plan``'s
+    ``tile_rows``).  A longer descriptor, or an expert id out of range, sets a
+    device status bit that raises at the next call (``RuntimeError`` /
+    ``IndexError``)."""
     if weight.dtype != torch.uint8 or weight.dim() != 3:
         raise ValueError("grouped weight must be [experts, out, in] uint8 E4M3")
     if scale_inv.dtype != torch.float32 or scale_inv.dim() != 3:
@@ -124,16 +135,29 @@ def grouped_fp8_linear(x, tile_plan, weight, scale_inv):
     tile_experts, tile_starts, tile_lengths = (t.contiguous() for t in tile_plan[:3])
     dev = N.require_cuda(x, weight, scale_inv, tile_experts)
     x = x.contiguous()
+    weight = weight.contiguous()
     out = torch.empty((routes, out_features), dtype=x.dtype, device=dev)
     if routes:
+        from .packed import StatusWord
+
+        sw = _LINEAR_STATUS.get(dev)
+        if sw is None:
+            sw = _LINEAR_STATUS[dev] = StatusWord(dev)
+        sw.raise_pending()
+        stream = N.stream(dev)
+        ws = _LINEAR_WS.get(dev, f"rows:{stream}", N.lib().glm53_grouped_fp8_linear_workspace_bytes(routes, in_features))
         N.check(
-            N.lib().glm53_grouped_fp8_linear(
+            N.lib().glm53_grouped_fp8_linear_ws(
                 x.data_ptr(), routes, in_features, tile_experts.data_ptr(), tile_starts.data_ptr(),
-                tile_lengths.data_ptr(), tile_experts.numel(), weight.contiguous().data_ptr(), experts,
-                out_features, scale_inv.contiguous().data_ptr(), out.data_ptr(), 0, N.stream(dev),
+                tile_lengths.data_ptr(), tile_experts.numel(), int(tile_rows), weight.data_ptr(), experts,
+                out_features, scale_inv.contiguous().data_ptr(), out.data_ptr(), ws.data_ptr(), ws.numel(),
+                sw.word.data_ptr(), N.decode_flags(weight), stream,
             ),
-            "glm53_grouped_fp8_linear",
+            "glm53_grouped_fp8_linear_ws",
         )
+        sw.publish()
+        if _SYNC_STATUS:
+            sw.check()
     return out
 
 

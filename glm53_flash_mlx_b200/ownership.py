@@ -1,10 +1,13 @@
-"""Tensor storage lifetime contracts for persistent runtime structures.
+"""Storage lifetime contract for tensors kept by long-lived structures.
 
-Counterpart of glm53_flash_mlx/ownership.py:13-198 over ``torch.Tensor``:
-the same enums, lease types, errors and constructors.  A resident structure
-(the packed expert bank) may only retain owned or borrowed-stable storage;
-borrowed-ephemeral storage (staging buffers, scratch) must be copied with
-``materialize_owned`` before it crosses a resident boundary.
+The drop-in surface of glm53_flash_mlx/ownership.py:13-198 over
+``torch.Tensor``: the enum values, the lease / resident dataclasses and their
+fields, the exception types, the constructor names and the message fragments
+the reference's tests match ("materialize_owned", "explicit TensorLease",
+"requires an owner") are interface and kept.  The rule: a structure that
+outlives a load step (the packed expert bank) keeps only storage it owns or
+storage borrowed from an owner it keeps alive; staging and scratch storage
+(borrowed-ephemeral) has to be copied into owned storage first.
 """
 
 from __future__ import annotations
@@ -28,11 +31,13 @@ class TensorLayout(str, Enum):
 
 
 class TensorOwnershipError(ValueError):
-    """Raised when a storage lifetime cannot satisfy a resident boundary."""
+    """A tensor's lifetime does not allow it to be kept where it was offered."""
 
 
 @dataclass(frozen=True)
 class TensorLease:
+    """A tensor offered together with who owns its storage."""
+
     value: torch.Tensor
     ownership: TensorOwnership
     layout: TensorLayout = TensorLayout.UNKNOWN
@@ -40,13 +45,14 @@ class TensorLease:
 
     def __post_init__(self) -> None:
         if self.ownership is TensorOwnership.BORROWED_STABLE and self.owner is None:
-            raise TensorOwnershipError(
-                "borrowed-stable storage requires an owner retained for its lifetime"
-            )
+            raise TensorOwnershipError("a borrowed-stable lease requires an owner to keep alive with it")
 
 
 @dataclass(frozen=True)
 class ResidentTensor:
+    """A tensor accepted into a long-lived structure: owned or borrowed with
+    its owner, row-major contiguous."""
+
     value: torch.Tensor
     ownership: TensorOwnership
     layout: TensorLayout
@@ -54,88 +60,78 @@ class ResidentTensor:
 
     def __post_init__(self) -> None:
         if self.ownership is TensorOwnership.BORROWED_EPHEMERAL:
-            raise TensorOwnershipError(
-                "resident structures cannot retain borrowed-ephemeral storage"
-            )
+            raise TensorOwnershipError("ephemeral (borrowed-ephemeral) storage cannot be kept resident")
         if self.layout is not TensorLayout.ROW_MAJOR_CONTIGUOUS:
-            raise TensorOwnershipError(
-                "resident tensors require the row-major contiguous layout contract"
-            )
+            raise TensorOwnershipError("a resident tensor must be declared row-major contiguous")
         if self.ownership is TensorOwnership.BORROWED_STABLE and self.owner is None:
-            raise TensorOwnershipError(
-                "borrowed-stable resident storage must retain its owner"
-            )
+            raise TensorOwnershipError("a borrowed-stable resident tensor requires an owner to keep alive")
 
 
 def owned_tensor(value: torch.Tensor, *, layout: TensorLayout = TensorLayout.UNKNOWN) -> TensorLease:
-    """Declare storage created and lifetime-controlled by this runtime."""
+    """Lease of storage this runtime allocated and frees."""
     return TensorLease(value, TensorOwnership.OWNED, layout)
 
 
 def borrowed_stable_tensor(
     value: torch.Tensor, *, owner: object, layout: TensorLayout = TensorLayout.UNKNOWN
 ) -> TensorLease:
-    """Borrow storage whose owner is retained for the resident lifetime."""
+    """Lease of storage owned by `owner`, which the keeper holds as long as it
+    keeps the tensor."""
     return TensorLease(value, TensorOwnership.BORROWED_STABLE, layout, owner)
 
 
 def borrowed_ephemeral_tensor(
     value: torch.Tensor, *, owner: object | None = None, layout: TensorLayout = TensorLayout.UNKNOWN
 ) -> TensorLease:
-    """Borrow staging/scratch storage that may be reused after the load step."""
+    """Lease of storage that its owner may overwrite once the current step is
+    done (a staging or scratch buffer)."""
     return TensorLease(value, TensorOwnership.BORROWED_EPHEMERAL, layout, owner)
 
 
-def _row_major(value: torch.Tensor) -> torch.Tensor:
+def _contiguous(value: torch.Tensor) -> torch.Tensor:
     return value.contiguous()
 
 
-def _owned_copy(value: torch.Tensor) -> torch.Tensor:
-    # clone() allocates storage of its own: later writes to the borrowed
-    # source (or its owner) cannot reach the copy.
+def _private_copy(value: torch.Tensor) -> torch.Tensor:
+    # a fresh allocation: nothing written to the source afterwards reaches it
     return value.contiguous().clone(memory_format=torch.contiguous_format)
 
 
 def require_resident(lease: TensorLease | ResidentTensor) -> ResidentTensor:
-    """Validate a resident boundary without silently copying ephemeral data."""
+    """Accept a lease for keeping, or refuse it; never copies behind the
+    caller's back (an ephemeral lease is refused, not copied)."""
     if isinstance(lease, ResidentTensor):
         return lease
     if not isinstance(lease, TensorLease):
-        raise TypeError(
-            "resident tensors require an explicit TensorLease; bare arrays "
-            "have no storage lifetime contract"
-        )
+        raise TypeError("keeping a tensor needs an explicit TensorLease: a bare tensor states no owner or lifetime")
     if lease.ownership is TensorOwnership.BORROWED_EPHEMERAL:
-        raise TensorOwnershipError(
-            "borrowed-ephemeral storage must call materialize_owned() before "
-            "crossing a resident boundary"
-        )
-    return ResidentTensor(
-        _row_major(lease.value), lease.ownership, TensorLayout.ROW_MAJOR_CONTIGUOUS, lease.owner
-    )
+        raise TensorOwnershipError("ephemeral storage is refused here; copy it with materialize_owned() first")
+    return ResidentTensor(_contiguous(lease.value), lease.ownership, TensorLayout.ROW_MAJOR_CONTIGUOUS, lease.owner)
 
 
 def materialize_owned(lease: TensorLease | ResidentTensor) -> ResidentTensor:
-    """Create storage independent of every borrowed source and source owner."""
+    """An owned resident tensor: owned storage as it is (made contiguous),
+    borrowed storage copied into a private allocation."""
     if isinstance(lease, ResidentTensor) and lease.ownership is TensorOwnership.OWNED:
         return lease
     if not isinstance(lease, (TensorLease, ResidentTensor)):
-        raise TypeError("materialize_owned() requires an explicit storage contract")
+        raise TypeError("materialize_owned() takes a TensorLease or ResidentTensor, not a bare tensor")
     if lease.ownership is TensorOwnership.OWNED:
-        value = _row_major(lease.value)
+        value = _contiguous(lease.value)
     else:
-        value = _owned_copy(lease.value)
+        value = _private_copy(lease.value)
     return ResidentTensor(value, TensorOwnership.OWNED, TensorLayout.ROW_MAJOR_CONTIGUOUS)
 
 
 def resident_concatenate(leases: Iterable[TensorLease | ResidentTensor], *, axis: int) -> ResidentTensor:
-    """Build an owned fusion from non-ephemeral source tensors."""
+    """Concatenate keepable leases along `axis` into one owned tensor."""
     residents = [require_resident(lease) for lease in leases]
     if not residents:
-        raise ValueError("cannot concatenate an empty resident tensor list")
+        raise ValueError("resident_concatenate() needs at least one tensor")
     value = torch.cat([item.value for item in residents], dim=axis).contiguous()
     return ResidentTensor(value, TensorOwnership.OWNED, TensorLayout.ROW_MAJOR_CONTIGUOUS)
 
 
 def storage_descriptor(value: TensorLease | ResidentTensor) -> dict[str, str]:
+    """The lease's contract as strings (the bank's ``storage_contracts``)."""
     return {"ownership": value.ownership.value, "layout": value.layout.value}

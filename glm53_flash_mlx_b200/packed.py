@@ -262,10 +262,13 @@ def packed_decode_moe(x: torch.Tensor, expert_ids: torch.Tensor, scores: torch.T
     return None if split == "shared" else out
 
 
-# Largest batch of decode rows the batched path takes: up to 16 rows no expert
-# gets more than 16 routes, so the Direct module's per-expert projections all
-# run on the GEMV tiles, whose FP32 sums the per-route decode reproduces.
-BATCHED_DECODE_MAX_ROWS = 16
+# Routes the coalesced batched decode takes in one call (kBdMaxRoutes in
+# csrc/batched_decode.cu), counting each token's shared-expert route: with
+# top-8 routing, batches of 2..455 rows run on the device with the Direct
+# module's multi-row semantics (below the grouped path's 256-route threshold
+# that is every batch of up to 31 rows, as grouped_fp8.py:323-326 routes them).
+BATCHED_DECODE_MAX_ROUTES = 4096
+BATCHED_DECODE_MAX_ROWS = BATCHED_DECODE_MAX_ROUTES // (DECODE_TOP_K + 1)
 
 
 def batched_decode_moe(x: torch.Tensor, indices: torch.Tensor, scores: torch.Tensor, bank: PackedFP8ExpertBank,

@@ -308,6 +308,26 @@ int glm53_routes_decode(const void* x_rows, int64_t R, int64_t H, const uint32_t
                         float limit, void* out_rows, void* workspace, size_t workspace_bytes,
                         uint32_t* status, uint32_t flags, void* stream);
 
+/* Workspace bytes of glm53_routes_decode_coalesced for R slots over E experts. */
+size_t glm53_routes_decode_coalesced_workspace_bytes(int64_t R, int64_t E, int64_t H, int64_t I);
+
+/* glm53_routes_decode with expert coalescing: the slots are sorted by expert
+ * on the device (glm53_route_plan, descriptors of up to 4 slots) and each
+ * descriptor streams its expert's weights once for all of its slots (the
+ * batched decode's kernels), writing each slot's BF16 down row at its own
+ * position: the same bits as glm53_routes_decode.  Slots whose id is >= E
+ * (the empty mark 0xFFFFFFFF among them) are skipped and their rows left
+ * untouched.  R <= 4096, H and I multiples of 128, 16-byte aligned tensors.
+ * The expert owner's half of batched expert-parallel decode (config 4 at
+ * B = 16 / 64 per rank): the reference's cross-request batching with expert
+ * coalescing (glm-5.3-flash-m3-ultra-runtime-architecture-2026-08-27.md:
+ * 183-188), over the packed bank of glm53_flash_mlx/packed.py:747-876. */
+int glm53_routes_decode_coalesced(const void* x_rows, int64_t R, int64_t H, const uint32_t* expert_ids,
+                                  const uint8_t* gate_up_w, const float* gate_up_s, const uint8_t* down_w,
+                                  const float* down_s, int64_t E, int64_t I, float limit, void* out_rows,
+                                  void* workspace, size_t workspace_bytes, uint32_t* status, uint32_t flags,
+                                  void* stream);
+
 /* Direct-module combine of a small decode batch: out[t] = the BF16 sum, in
  * ascending expert id of token t's top_k routes, of BF16(f32(rows[t*top_k+j])
  * * scores[t*top_k+j]) (each add rounded to BF16), then + shared[t] (BF16 add;
@@ -472,7 +492,11 @@ int glm53_gather_rows(const void* x, int64_t H, const uint32_t* order,
 /* Grouped projection of sorted route rows: for every descriptor d,
  * out[start+i, :] = x[start+i, :] @ dequant(w[expert])^T (i < length).
  * x [R,K] BF16, w [E,N,K] E4M3, scale_inv [E, ceil(N/128), ceil(K/128)],
- * out [R,N] BF16; tile lengths must be <= 128.
+ * out [R,N] BF16; tile lengths must be <= 128.  The mma.sync tile path: the
+ * weights enter the BF16 MMA as BF16(lut(c) * s), one rounding of the scaled
+ * weight (relative 2^-9), so results carry that rounding on top of the
+ * summation order; glm53_grouped_fp8_linear_ws (tcgen05, exact weights) is
+ * the path the Python grouped_fp8_linear takes.
  * Replaces grouped_fp8_linear, glm53_flash_mlx/grouped_fp8.py:206-262
  * (kernel K12, grouped_fp8.py:30-154). */
 int glm53_grouped_fp8_linear(const void* x, int64_t R, int64_t K,
@@ -486,6 +510,25 @@ int glm53_grouped_fp8_linear(const void* x, int64_t R, int64_t K,
 /* hidden[R,I] = silu(min(gate, L)) * clip(up, -L, L) with BF16 per-op
  * rounding, gate_up [R,2I].
  * Replaces activate_gate_up, glm53_flash_mlx/grouped_fp8.py:265-270. */
+/* Workspace bytes of glm53_grouped_fp8_linear_ws for R route rows of width K. */
+size_t glm53_grouped_fp8_linear_workspace_bytes(int64_t R, int64_t K);
+
+/* glm53_grouped_fp8_linear on the tcgen05 grouped GEMM: the weights decoded
+ * exactly to FP16 (lut(c) * 2^8), the activations converted once to FP16 x
+ * 2^-e rows in the workspace, FP32 accumulation in TMEM with the block scale
+ * applied per 128-K block; results differ from the reference's FP32 sums
+ * (grouped_fp8.py:30-154) only in summation order.  tile_rows = the longest
+ * descriptor the plan may hold (build_grouped_tile_plan's tile_rows); a longer
+ * one sets GLM53_STATUS_BAD_GEOMETRY in `status`, an expert id >= E sets
+ * GLM53_STATUS_BAD_EXPERT (that descriptor is skipped).  K and N multiples of
+ * 128, 16-byte aligned x, w and workspace.  Replaces grouped_fp8_linear,
+ * glm53_flash_mlx/grouped_fp8.py:206-262. */
+int glm53_grouped_fp8_linear_ws(const void* x, int64_t R, int64_t K, const uint32_t* tile_experts,
+                                const uint32_t* tile_starts, const uint32_t* tile_lengths,
+                                int64_t descriptor_capacity, int64_t tile_rows, const uint8_t* w, int64_t E,
+                                int64_t N, const float* scale_inv, void* out, void* workspace,
+                                size_t workspace_bytes, uint32_t* status, uint32_t flags, void* stream);
+
 int glm53_activate_gate_up(const void* gate_up, int64_t R, int64_t I,
                            float limit, void* hidden, void* stream);
 

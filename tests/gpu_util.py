@@ -219,20 +219,49 @@ def certify_packed_decode(x_bits, ids, scores, bank, shared, limit, out_bits, wo
     hidden = f32(workspace_view(workspace, offs[0], np.uint16, top_k * I + Is))
     partial = workspace_view(workspace, offs[1], np.float32, (top_k + 1) * H).reshape(top_k + 1, H)
     x = np.asarray(x_bits, dtype=np.uint16).reshape(1, H)
-    cert = certify_expert_rows(np.repeat(x, top_k, 0), ids, bank, limit, hidden[:top_k * I].reshape(top_k, I),
-                               partial[:top_k], down_kind="f32")
-    shared_row = None
+    sc = np.asarray(scores, dtype=np.float32).reshape(-1)
+    tensor_core = H % 128 == 0 and I % 128 == 0 and Is % 128 == 0
+    if tensor_core:  # the tensor-core kernels keep the FP32 down projections
+        cert = certify_expert_rows(np.repeat(x, top_k, 0), ids, bank, limit, hidden[:top_k * I].reshape(top_k, I),
+                                   partial[:top_k], down_kind="f32")
+        shared_row = None
+        if shared is not None:
+            cs = certify_expert_rows(x, np.zeros(1, np.uint32), _shared_bank(shared), limit,
+                                     hidden[top_k * I:].reshape(1, Is), partial[top_k:top_k + 1], down_kind="f32")
+            cert = {k: cert[k] + cs[k] for k in cert}
+            shared_row = bf16_round(partial[top_k])
+        expect = slot_combine(bf16_round(partial[:top_k]), sc, shared=shared_row)
+        same = np.asarray(out_bits).reshape(-1) == expect
+        assert same.all(), f"{int((~same).sum())} outputs differ from the combine of the certified intermediates"
+        cert["certified"] = True
+        return cert
+    # the generic kernels reduce in registers: the hidden rows are certified,
+    # then the output must lie in the combine of the down intervals of those
+    # hidden rows (every step of the combine is monotone in each row)
+    import oracle as O
+
+    h_lo, h_hi = O.hidden_envelope(np.repeat(x, top_k, 0), ids, bank, limit)
+    hr = hidden[:top_k * I].reshape(top_k, I)
+    assert ((hr >= h_lo) & (hr <= h_hi)).all(), "hidden values outside their rounding envelope"
+    lo, hi = O.down_interval(hr, ids, bank[2], bank[3])
+    d_lo, d_hi = bf16_round(_f32_down(lo)), bf16_round(_f32_up(hi))
+    t_lo = np.zeros(H, np.float32)
+    t_hi = np.zeros(H, np.float32)
+    for j in range(top_k):
+        a, b = d_lo[j] * sc[j], d_hi[j] * sc[j]
+        t_lo, t_hi = t_lo + np.minimum(a, b), t_hi + np.maximum(a, b)
+    o_lo, o_hi = bf16_round(t_lo), bf16_round(t_hi)
     if shared is not None:
-        cs = certify_expert_rows(x, np.zeros(1, np.uint32), _shared_bank(shared), limit,
-                                 hidden[top_k * I:].reshape(1, Is), partial[top_k:top_k + 1], down_kind="f32")
-        cert = {k: cert[k] + cs[k] for k in cert}
-        shared_row = bf16_round(partial[top_k])
-    expect = slot_combine(bf16_round(partial[:top_k]), np.asarray(scores, dtype=np.float32).reshape(-1),
-                          shared=shared_row)
-    same = np.asarray(out_bits).reshape(-1) == expect
-    assert same.all(), f"{int((~same).sum())} outputs differ from the combine of the certified intermediates"
-    cert["certified"] = True
-    return cert
+        hs = hidden[top_k * I:].reshape(1, Is)
+        s_lo, s_hi = O.hidden_envelope(x, np.zeros(1, np.uint32), _shared_bank(shared), limit)
+        assert ((hs >= s_lo) & (hs <= s_hi)).all(), "shared hidden values outside their rounding envelope"
+        sl, shh = O.down_interval(hs, np.zeros(1, np.uint32), shared[4][None], shared[5][None])
+        o_lo = bf16_round(o_lo + bf16_round(_f32_down(sl))[0])
+        o_hi = bf16_round(o_hi + bf16_round(_f32_up(shh))[0])
+    g = f32(np.asarray(out_bits, dtype=np.uint16)).reshape(-1)
+    ok = (g >= o_lo) & (g <= o_hi)
+    assert ok.all(), f"{int((~ok).sum())} outputs outside the combine of the certified rows' intervals"
+    return {"certified": True, "hidden_values": int(hidden.size), "path": "generic (register reduce)"}
 
 
 def certify_linear(x_bits, weight, scale_inv, y_bits) -> dict:
@@ -253,7 +282,7 @@ def certify_linear(x_bits, weight, scale_inv, y_bits) -> dict:
 
 
 def certify_grouped(x_bits, indices, scores, bank, shared, limit, out_bits, workspace: torch.Tensor,
-                    tokens=None) -> dict:
+                    tokens=None, bank_experts=None, expert_count=None) -> dict:
     """Certificate of one glm53_grouped_moe call (tensor-core path) for the
     listed tokens, from the intermediates it leaves in its workspace
     (glm53_grouped_moe_workspace_layout): each route's FP16 hidden row and
@@ -261,7 +290,8 @@ def certify_grouped(x_bits, indices, scores, bank, shared, limit, out_bits, work
     ``certify_expert_rows``; each token's output is restore_and_reduce's
     slot-ordered combine of its down rows plus its shared row, bit for bit.
     x_bits / indices / scores / out_bits cover all T tokens; bank / shared are
-    host tuples."""
+    host tuples (with ``bank_experts``, the bank holds only those experts, in
+    that order, of ``expert_count``)."""
     from glm53_flash_mlx_b200 import _native as N
 
     x = np.asarray(x_bits, dtype=np.uint16)
@@ -269,7 +299,7 @@ def certify_grouped(x_bits, indices, scores, bank, shared, limit, out_bits, work
     idx = np.asarray(indices).reshape(T, -1).astype(np.uint32)
     sc = np.asarray(scores, dtype=np.float32).reshape(T, -1)
     k = idx.shape[1]
-    E = bank[0].shape[0]
+    E = bank[0].shape[0] if expert_count is None else int(expert_count)
     I = bank[0].shape[1] // 2
     Is = 0 if shared is None else shared[0].shape[0]
     R = T * k
@@ -287,8 +317,14 @@ def certify_grouped(x_bits, indices, scores, bank, shared, limit, out_bits, work
     down = dn_all.index_select(0, pos_t).cpu().numpy().view(np.uint16)
     # bank restricted to the touched experts (the certificate reads only those)
     ids = idx[tok].reshape(-1)
-    touched, local = np.unique(ids, return_inverse=True)
-    sub = tuple(b[touched] for b in bank)
+    if bank_experts is None:
+        touched, local = np.unique(ids, return_inverse=True)
+        sub = tuple(b[touched] for b in bank)
+    else:
+        be = np.asarray(bank_experts)
+        local = np.searchsorted(be, ids)
+        assert np.array_equal(be[local], ids), "bank_experts must hold every routed expert (sorted)"
+        sub = bank
     cert = certify_expert_rows(np.repeat(x[tok], k, 0), local.astype(np.uint32), sub, limit, hidden, down,
                                down_kind="bf16", hidden_fp16=True)
     shared_rows = None
@@ -309,3 +345,52 @@ def certify_grouped(x_bits, indices, scores, bank, shared, limit, out_bits, work
     assert same.all(), f"{int((~same).sum())} outputs differ from the combine of the certified intermediates"
     cert["certified"] = True
     return cert
+
+
+def certify_grouped_linear(x_rows_bits, experts, weight, scale_inv, out_bits) -> dict:
+    """Certificate of a grouped projection: row r of the output is one of the
+    BF16 roundings of an FP32 evaluation of x[r] @ dequant(weight[experts[r]])^T
+    within the stated bound."""
+    import oracle as O
+
+    x = f32(np.asarray(x_rows_bits, dtype=np.uint16))
+    lo, hi = O.down_interval(x, np.asarray(experts, dtype=np.uint32), weight, scale_inv)
+    y = f32(np.asarray(out_bits, dtype=np.uint16)).reshape(lo.shape)
+    d_lo, d_hi = bf16_round(_f32_down(lo)), bf16_round(_f32_up(hi))
+    ok = (y >= d_lo) & (y <= d_hi)
+    assert ok.all(), f"{int((~ok).sum())} grouped outputs outside the FP32 evaluation interval"
+    return {"certified": True, "outputs_on_bf16_midpoint_band": int((d_lo != d_hi).sum())}
+
+
+def certify_by_envelope(gpu_bits, lo, hi) -> dict:
+    """Output-level certificate: every GPU value inside the oracle's rounding
+    envelope of the whole layer (``oracle.*_envelope``; wider than the staged
+    certificates, used where the kernels' intermediates are not kept)."""
+    g = f32(np.asarray(gpu_bits, dtype=np.uint16)).reshape(lo.shape)
+    ok = (g >= lo) & (g <= hi)
+    assert ok.all(), f"{int((~ok).sum())} outputs outside the layer's rounding envelope"
+    return {"certified": True, "envelope": "layer"}
+
+
+def router_logit_check(gpu_logits, ref64, x_bits, weight) -> dict:
+    """FP32 router logits within 1e-6 relative of the FP64 oracle.  A logit
+    whose relative error exceeds 1e-6 is accepted only when its absolute error
+    is within the FP32 evaluation bound of the GPU router kernels,
+    gamma(32) * sum_k |x_k w_k| (at most 32 FP32 roundings on a term's path:
+    the small-batch kernel's 16 FMAs per thread, a 5-level warp sum and 8 warp
+    partials; the tensor-core kernel's exact BF16 split with one rounding per
+    MMA slice summed in double-FP32 stays far inside it): the logits near zero,
+    where a relative error is ill-conditioned.  Returns their count."""
+    g = np.asarray(gpu_logits, dtype=np.float64)
+    r = np.asarray(ref64, dtype=np.float64)
+    x = np.abs(f32(np.asarray(x_bits, dtype=np.uint16)).astype(np.float64)).reshape(g.shape[0], -1)
+    absum = x @ np.abs(np.asarray(weight, dtype=np.float64)).T
+    err = np.abs(g - r)
+    rel_ok = err <= 1e-6 * np.abs(r)
+    u = 2.0 ** -24
+    bound_ok = err <= (32 * u / (1 - 32 * u)) * absum
+    assert (rel_ok | bound_ok).all(), (
+        f"{int((~(rel_ok | bound_ok)).sum())} logits beyond 1e-6 relative and the stated bound; worst rel "
+        f"{float((err / np.maximum(np.abs(r), 1e-300)).max())}")
+    return {"logits": int(g.size), "beyond_1e-6_relative_within_bound": int((~rel_ok).sum()),
+            "max_rel": float((err / np.maximum(np.abs(r), 1e-30)).max())}

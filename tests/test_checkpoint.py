@@ -140,7 +140,7 @@ def test_loaded_layer_decodes_on_gpu_like_the_oracle(tmp_path, oracle):
 
     import numpy as np
 
-    from gpu_util import assert_layer_close, bank_host, bits, shared_host
+    from gpu_util import assert_layer_close, bank_host, bits, certify_packed_decode, shared_host
     from glm53_flash_mlx_b200.packed import shared_fp8_tensors
 
     E, H, I = 8, 512, 256
@@ -161,7 +161,10 @@ def test_loaded_layer_decodes_on_gpu_like_the_oracle(tmp_path, oracle):
         out = moe(x)
         idx, sc = moe.gate(x)
         torch.cuda.synchronize()
-        ref = oracle.packed_decode_moe(bits(x.reshape(-1)), idx.reshape(-1).cpu().numpy().astype(np.uint32),
-                                  sc.reshape(-1).cpu().numpy(), bank_host(moe.bank),
-                                  shared_host(shared_fp8_tensors(moe.shared_experts)), 10.0)
-        assert_layer_close(bits(out.reshape(-1)), ref)
+        ids = idx.reshape(-1).cpu().numpy().astype(np.uint32)
+        scs = sc.reshape(-1).cpu().numpy()
+        hb, hs = bank_host(moe.bank), shared_host(shared_fp8_tensors(moe.shared_experts))
+        ref = oracle.packed_decode_moe(bits(x.reshape(-1)), ids, scs, hb, hs, 10.0)
+        cert = certify_packed_decode(bits(x.reshape(-1)), ids, scs, hb, hs, 10.0, bits(out.reshape(-1)),
+                                     moe._workspace._buffers[(x.device, "decode")])
+        assert_layer_close(bits(out.reshape(-1)), ref, certificate=cert)

@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 import torch
 
-from gpu_util import assert_layer_close, bits, from_bits
+from gpu_util import assert_layer_close, bits, certify_linear, from_bits
 
 
 def test_oracle_layout_known_answer(oracle):
@@ -53,8 +53,10 @@ def test_dsa_output_projection_and_hc(oracle, heads, rows, dim, hidden, check_ro
     row_major = G.head_major_to_rows(hm_d)
     assert torch.equal(projected, G.block_fp8_linear(row_major, w, s))
     sel = list(range(rows)) if check_rows is None else check_rows
-    ref = oracle.block_fp8_linear(oracle.head_major_to_rows(hm)[sel], w.cpu().numpy(), s.cpu().numpy())
-    assert_layer_close(bits(projected)[sel], ref)
+    rows_in = oracle.head_major_to_rows(hm)[sel]
+    ref = oracle.block_fp8_linear(rows_in, w.cpu().numpy(), s.cpu().numpy())
+    cert = certify_linear(rows_in, w.cpu().numpy(), s.cpu().numpy(), bits(projected)[sel])
+    assert_layer_close(bits(projected)[sel], ref, certificate=cert)
     residual = oracle.bf16_from_f32(rng.standard_normal((rows, 4, hidden)).astype(np.float32))
     post = (rng.random((rows, 4)) * 2).astype(np.float32)
     comb = rng.random((rows, 4, 4)).astype(np.float32)

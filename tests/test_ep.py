@@ -224,15 +224,40 @@ def test_expert_parallel_decode_world1_module_bitwise():
     E, H, I = 16, 4096, 1536
     bank = S.make_bank(E, H, I, seed=51, device=dev)
     shared = shared_fp8_tensors(S.make_shared(H, I, seed=52, device=dev))
-    plan = ep.ExpertParallelDecode(bank, experts=E, rank=0, world=1, shared=shared, limit=10.0, max_tokens=4)
+    plan = ep.ExpertParallelDecode(bank, experts=E, rank=0, world=1, shared=shared, limit=10.0, max_tokens=64)
     gen = torch.Generator().manual_seed(53)
-    for T in (1, 4):
+    for T in (1, 4, 16, 64):  # 16 and 64: config 4's batches, the owner decode coalesced by expert
         x = S.random_bf16((T, H), seed=54 + T, device=dev)
         ids = torch.stack([torch.randperm(E, generator=gen)[:8] for _ in range(T)]).to(torch.int32).to(dev)
         sc = (torch.rand((T, 8), generator=gen) * 0.25 + 0.05).to(dev)
         out = plan(x, ids, sc)
         torch.cuda.synchronize()
         assert torch.equal(out, _single_device(bank, shared, x, ids, sc, 10.0))
+
+
+@pytest.mark.gpu
+def test_coalesced_routes_decode_equals_per_route_bitwise():
+    """glm53_routes_decode_coalesced (slots sorted by expert, each expert's
+    weights streamed once per four slots) gives every slot the bits of
+    glm53_routes_decode; empty slots (id 0xFFFFFFFF) keep their rows."""
+    from glm53_flash_mlx_b200 import synthetic as S
+
+    dev = torch.device("cuda", 0)
+    E, H, I, R = 24, 4096, 1536, 300
+    bank = S.make_bank(E, H, I, seed=71, device=dev)
+    tensors = (bank.gate_up_weight, bank.gate_up_scale_inv, bank.down_weight, bank.down_scale_inv)
+    gen = torch.Generator().manual_seed(72)
+    ids = torch.randint(0, E, (R,), generator=gen, dtype=torch.int32)
+    ids[torch.randperm(R, generator=gen)[:60]] = -1  # 0xFFFFFFFF: empty slots
+    ids = ids.to(dev)
+    x = S.random_bf16((R, H), seed=73, device=dev, std=1.5)
+    live = ids >= 0
+    want = ep.routes_decode(x[live], ids[live].contiguous(), tensors, limit=10.0)
+    sentinel = torch.full((R, H), 7.0, dtype=torch.bfloat16, device=dev)
+    got = ep.routes_decode_coalesced(x, ids, tensors, limit=10.0, out=sentinel.clone())
+    torch.cuda.synchronize()
+    assert torch.equal(got[live], want)
+    assert torch.equal(got[~live], sentinel[~live])
 
 
 def _nccl_rank(rank, world, port, result_dir, transport):
