@@ -556,7 +556,7 @@ def bench_linear(dev, args):
         for M in ms_list:
             x = S.random_bf16((M, K), seed=M, device=dev)
             y = torch.empty((M, Nn), dtype=torch.bfloat16, device=dev)
-            wsb = lib.glm53_fp8_linear_workspace_bytes(M, K)
+            wsb = lib.glm53_fp8_linear_splitk_workspace_bytes(M, K, Nn)
             wsp = torch.zeros(max(wsb, 256), dtype=torch.uint8, device=dev)
 
             def call(i, stream):

@@ -51,6 +51,7 @@ SIGNATURES: dict[str, tuple] = {
         [_vp, _i64, _i64, _vp, _i64, _vp, _int, _int, _int, _int, _f, _vp, _vp, _vp, _vp, _sz, _vp],
     ),
     "glm53_fp8_linear_workspace_bytes": (_sz, [_i64, _i64]),
+    "glm53_fp8_linear_splitk_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "glm53_fp8_linear_ws": (_int, [_vp, _i64, _i64, _vp, _i64, _vp, _vp, _vp, _sz, _vp, _u32, _vp]),
     "glm53_packed_decode_workspace_bytes": (_sz, [_int, _i64, _i64, _i64]),
     "glm53_packed_decode_moe": (

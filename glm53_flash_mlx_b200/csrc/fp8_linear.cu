@@ -141,7 +141,9 @@ static int launch_gemv_stream(const uint16_t* x, int M, int K, const uint8_t* w,
   if (rc_attr) return rc_attr;
   const int ntiles = (N + 15) / 16;
   const int chunks = (M + chunk - 1) / chunk;
-  const int per_sm = std::max(1, std::min(2, (int)((220 * 1024) / smem)));
+  // up to three blocks per SM: one 16-row tile per block for N up to
+  // 444 * 16 rows, so no block streams two tiles while others idle
+  const int per_sm = std::max(1, std::min(3, (int)((220 * 1024) / smem)));
   const int bx = std::max(1, std::min(ntiles, (sm_count() * per_sm + chunks - 1) / chunks));
   dim3 grid((unsigned)bx, (unsigned)chunks);
   gemv_stream_kernel<KS, FINITE><<<grid, 32 * KS, smem, stream>>>(x, M, K, w, N, s, y, chunk);
@@ -189,6 +191,17 @@ extern "C" size_t glm53_fp8_linear_workspace_bytes(int64_t M, int64_t K) {
   return M > 0 && K > 0 ? linear_ws_bytes(M, K) : 0;
 }
 
+// K-range count of the tcgen05 GEMM for M rows x N outputs (1: no split).
+static int linear_splits(int64_t M, int64_t K, int64_t N) {
+  if (M <= kGemvMaxRows || K % 128 != 0) return 1;
+  return grouped_tc_splits(((M + 127) / 128) * ((N + 127) / 128), K / 128);
+}
+
+extern "C" size_t glm53_fp8_linear_splitk_workspace_bytes(int64_t M, int64_t K, int64_t N) {
+  if (M <= 0 || K <= 0 || N <= 0) return 0;
+  return linear_ws_bytes(M, K) + grouped_tc_splitk_bytes(M, N, linear_splits(M, K, N));
+}
+
 extern "C" int glm53_fp8_linear_ws(const void* x, int64_t M, int64_t K, const uint8_t* w, int64_t N,
                                    const float* scale_inv, void* y, void* workspace, size_t workspace_bytes,
                                    uint32_t* status, uint32_t flags, void* stream) {
@@ -223,6 +236,13 @@ extern "C" int glm53_fp8_linear_ws(const void* x, int64_t M, int64_t K, const ui
     g.finite = (flags & GLM53_FLAG_E4M3_FINITE) != 0;
     g.out = (uint16_t*)y;
     g.status = status;
+    // fewer output tiles than SMs: split K when the caller's workspace holds
+    // the partial sums (glm53_fp8_linear_splitk_workspace_bytes)
+    const int splits = linear_splits(M, K, N);
+    if (splits > 1 && workspace_bytes >= linear_ws_bytes(M, K) + grouped_tc_splitk_bytes(M, N, splits)) {
+      g.splits = splits;
+      g.partial = (float*)((char*)workspace + linear_ws_bytes(M, K));
+    }
     return grouped_tc(g, st);
   }
   return glm53_fp8_linear(x, M, K, w, N, scale_inv, y, flags, stream);

@@ -561,7 +561,8 @@ constexpr int kTcTileRows = 128;
 struct MoeWorkspace {
   uint32_t *order, *inverse, *sorted_experts, *route_offsets, *tile_offsets, *tile_experts, *tile_starts,
       *tile_lengths, *counts;
-  float *sorted_scores, *xscale, *shared_xscale;
+  float *sorted_scores, *xscale, *shared_xscale, *shared_partial;
+  int shared_splits;
   uint16_t *hidden, *down, *shared_hidden, *shared_out;
   __half *x16, *shared_x16;
   int64_t capacity;
@@ -597,6 +598,10 @@ MoeWorkspace carve(void* base, int64_t T, int top_k, int64_t E, int64_t H, int64
   w.xscale = (float*)take((size_t)R * 4);
   w.shared_x16 = (__half*)take((size_t)T * H * 2);
   w.shared_xscale = (float*)take((size_t)T * 4);
+  // split-K partials of the shared expert's down projection (few output
+  // tiles at small T)
+  w.shared_splits = Is > 0 && Is % 128 == 0 ? grouped_tc_splits(((T + 127) / 128) * ((H + 127) / 128), Is / 128) : 1;
+  w.shared_partial = w.shared_splits > 1 ? (float*)take(grouped_tc_splitk_bytes(T, H, w.shared_splits)) : nullptr;
   w.bytes = off;
   return w;
 }
@@ -707,6 +712,8 @@ static int grouped_moe_tc(const MoeWorkspace& w, const void* x, int64_t T, int64
     sd.I = 0;
     sd.swiglu = false;
     sd.out = w.shared_out;
+    sd.splits = w.shared_splits;
+    sd.partial = w.shared_partial;
     rc = grouped_tc(sd, st);
     if (rc) return rc;
     shared_ptr = w.shared_out;

@@ -102,6 +102,8 @@ struct TcArgs {
   int out_cols;          // columns of out (SwiGLU: I, plain: N)
   uint16_t* out;         // SwiGLU: FP16 hidden rows; plain: BF16 rows
   uint32_t* status;
+  int splits;            // k-block ranges per tile (plain dense only)
+  float* partial;        // [splits][R][out_cols] FP32 partial sums when splits > 1
 };
 
 // ---------------------------------------------------------------------------
@@ -286,10 +288,18 @@ constexpr size_t smem_bytes() {
 struct Tile {
   uint32_t e, start, len;
   int mt;
+  int ks, kb0, kb1;  // split index and its k-block range [kb0, kb1)
 };
 
 __device__ __forceinline__ Tile tile_at(const TcArgs& a, int t, int mtiles, int zsub) {
   Tile tl;
+  // the split index is innermost, so the CTAs of one tile's ranges run side
+  // by side and share its activation rows through L2
+  const int nkb = a.K / kKB;
+  tl.ks = t % a.splits;
+  tl.kb0 = (int)((int64_t)tl.ks * nkb / a.splits);
+  tl.kb1 = (int)((int64_t)(tl.ks + 1) * nkb / a.splits);
+  t /= a.splits;
   const int d = t / (mtiles * zsub);
   const int rem = t - d * mtiles * zsub;
   tl.mt = rem / zsub;
@@ -384,18 +394,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto first = [&](Cursor& c, int t) {
         for (c.t = t; c.t < ntiles; c.t += gridDim.x) {
           c.tl = tile_at(a, c.t, mtiles, zsub);
-          if (c.tl.len) return;
+          if (c.tl.len) {
+            c.kb = c.tl.kb0;
+            return;
+          }
         }
       };
       auto advance = [&](Cursor& c) {
         ++c.g;
-        if (++c.kb == nkb) {
-          c.kb = 0;
-          first(c, c.t + gridDim.x);
-        }
+        if (++c.kb == c.tl.kb1) first(c, c.t + gridDim.x);
       };
       // flag used descriptors whose expert is out of range (skipped as empty)
-      if (!a.dense) {
+      if (!a.dense) {  // (splits == 1 here)
         for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
           const int d = t / (mtiles * zsub);
           if ((t % (mtiles * zsub)) == 0 && __ldg(a.tile_lengths + d) && __ldg(a.tile_experts + d) >= (uint32_t)a.E)
@@ -405,7 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             atomicOr(a.status, kStatusBadGeometry);
         }
       }
-      Cursor cr{0, 0, 0u, Tile{}}, ca{0, 0, 0u, Tile{}};
+      Cursor cr{0, 0, 0u, Tile{}}, ca{0, 0, 0u, Tile{}};  // first() sets kb
       first(cr, blockIdx.x);
       first(ca, blockIdx.x);
       uint64_t t_idle = 0;
@@ -471,7 +481,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const Tile tl = tile_at(a, t, mtiles, zsub);
         if (tl.len == 0) continue;
         const uint32_t idesc = tl.len > 64 ? make_idesc(kM, kN) : make_idesc(kM, 64);
-        for (int kb = 0; kb < nkb; ++kb, ++g) {
+        for (int kb = tl.kb0; kb < tl.kb1; ++kb, ++g) {
           if ((g & 1u) != parity) continue;
           const int s = g % kRing;
           const int as = g % kActStages;
@@ -508,8 +518,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t g = 0;
     bool stop = false;
     for (int t = blockIdx.x; t < ntiles && !stop; t += gridDim.x) {
-      if (tile_at(a, t, mtiles, zsub).len == 0) continue;
-      for (int kb = 0; kb < nkb; ++kb, ++g) {
+      const Tile tl = tile_at(a, t, mtiles, zsub);
+      if (tl.len == 0) continue;
+      for (int kb = tl.kb0; kb < tl.kb1; ++kb, ++g) {
         const int s = g % kRawStages;
         const int ab = g % kRing;
         const uint32_t ring_ph = (g / kRing) & 1u;
@@ -568,7 +579,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float tot[64];
 #pragma unroll
       for (int n = 0; n < 64; ++n) tot[n] = 0.f;
-      for (int kb = 0; kb < nkb; ++kb, ++g) {
+      for (int kb = tl.kb0; kb < tl.kb1; ++kb, ++g) {
         const int cb = g & 1;
         if (!__all_sync(0xffffffffu, mbar_wait(bar(&bars->kb_done[g % kRing]), (g / kRing) & 1u, abort_flag))) {
           stop = true;
@@ -595,7 +606,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       // route range multipliers of this half: lane l holds routes n0 + l and n0 + 32 + l
       const float xa = (a.xscale && n0 + lane < tl.len) ? __ldg(a.xscale + tl.start + n0 + lane) : 1.0f;
       const float xb = (a.xscale && n0 + 32 + lane < tl.len) ? __ldg(a.xscale + tl.start + n0 + 32 + lane) : 1.0f;
-      if (!SWIGLU) {
+      if (!SWIGLU && a.splits > 1) {
+        // this range's FP32 partial sums; the reduce kernel adds the ranges in
+        // order and applies the route multiplier
+        const int col = row0 + r;
+        float* dst = a.partial + (size_t)tl.ks * a.R * a.out_cols;
+#pragma unroll
+        for (int n = 0; n < 64; ++n)
+          if (n0 + n < tl.len && col < a.out_cols) dst[(size_t)(tl.start + n0 + n) * a.out_cols + col] = tot[n];
+      } else if (!SWIGLU) {
         const int col = row0 + r;
 #pragma unroll
         for (int n = 0; n < 64; ++n) {
@@ -708,6 +727,39 @@ static int ensure_sigmoid_table(cudaStream_t st) {
 
 }  // namespace tc
 
+// Sum of the split-K ranges' FP32 partials in range order, times the route
+// multiplier, rounded to BF16: out[r][c] = BF16(xscale[r] * sum_ks p[ks][r][c]).
+__global__ void splitk_reduce_kernel(const float* __restrict__ partial, int splits, int64_t R, int64_t N,
+                                     const float* __restrict__ xscale, uint16_t* __restrict__ out) {
+  const int64_t n4 = N >> 2;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= R * n4) return;
+  const int64_t r = i / n4;
+  const size_t plane = (size_t)R * N;
+  float4 t = reinterpret_cast<const float4*>(partial)[i];
+  for (int ks = 1; ks < splits; ++ks) {
+    const float4 v = reinterpret_cast<const float4*>(partial + ks * plane)[i];
+    t.x += v.x;
+    t.y += v.y;
+    t.z += v.z;
+    t.w += v.w;
+  }
+  const float x = xscale ? __ldg(xscale + r) : 1.0f;
+  const uint32_t lo = (uint32_t)f32_to_bf16_bits(t.x * x) | ((uint32_t)f32_to_bf16_bits(t.y * x) << 16);
+  const uint32_t hi = (uint32_t)f32_to_bf16_bits(t.z * x) | ((uint32_t)f32_to_bf16_bits(t.w * x) << 16);
+  reinterpret_cast<uint2*>(out)[i] = make_uint2(lo, hi);
+}
+
+int grouped_tc_splits(int64_t tiles, int64_t nkb) {
+  const int64_t sms = sm_count();
+  if (tiles <= 0 || tiles * 2 > sms) return 1;
+  return (int)std::max<int64_t>(1, std::min<int64_t>(sms / tiles, nkb / 4));
+}
+
+size_t grouped_tc_splitk_bytes(int64_t R, int64_t N, int splits) {
+  return splits > 1 ? align_up((size_t)splits * R * N * sizeof(float), 256) : 0;
+}
+
 bool grouped_tc_supported(int64_t K, int64_t N, float limit, bool swiglu) {
   // SwiGLU tiles are 64 hidden rows inside one 128-row scale block; plain tiles
   // are 128 output rows, the last one cut at N (8-row granularity)
@@ -763,9 +815,16 @@ int grouped_tc(const TcGemm& g, cudaStream_t st) {
   a.out_cols = (int)cols;
   a.out = g.out;
   a.status = g.status;
+  const int splits = (g.splits > 1 && g.dense && !g.swiglu && g.partial && (cols % 4) == 0) ? g.splits : 1;
+  if (splits > g.K / kKB) {
+    set_last_error("grouped_tc: %d K ranges for %lld k-blocks", splits, (long long)(g.K / kKB));
+    return GLM53_ERR_INVALID;
+  }
+  a.splits = splits;
+  a.partial = g.partial;
   const int mtiles = (int)((cols + wbox - 1) / wbox);
   const int zsub = g.dense ? 1 : (int)((g.max_rows + kN - 1) / kN);
-  const int64_t ntiles = g.capacity * mtiles * zsub;
+  const int64_t ntiles = g.capacity * mtiles * zsub * splits;
   if (ntiles > INT32_MAX) {
     set_last_error("grouped_tc: too many tiles");
     return GLM53_ERR_INVALID;
@@ -785,7 +844,12 @@ int grouped_tc(const TcGemm& g, cudaStream_t st) {
   rc = ensure_max_smem((const void*)kern, smem);
   if (rc) return rc;
   kern<<<grid, kThreads, smem, st>>>(wmap, umap, xmap, xmap64, a, (int)ntiles, mtiles, zsub);
-  return check_launch("grouped_tc_kernel");
+  rc = check_launch("grouped_tc_kernel");
+  if (rc || splits == 1) return rc;
+  const int64_t n4 = g.R * (cols / 4);
+  glm53::splitk_reduce_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(g.partial, splits, g.R, cols, g.xscale,
+                                                                             g.out);
+  return check_launch("splitk_reduce_kernel");
 }
 
 // ---------------------------------------------------------------------------

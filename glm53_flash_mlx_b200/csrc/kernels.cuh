@@ -82,7 +82,18 @@ struct TcGemm {
   bool finite;            // no 0x7F/0xFF codes: hardware E4M3 conversion
   uint16_t* out;
   uint32_t* status;
+  // split-K (plain dense GEMMs only): each tile's k-blocks are cut into
+  // `splits` contiguous ranges computed by different CTAs, whose FP32 partial
+  // sums go to `partial` [splits][R][N] and are added in range order by a
+  // second kernel (grouped_tc_splitk_bytes gives the size)
+  int splits;
+  float* partial;
 };
+
+// Split count for a plain dense GEMM of `tiles` output tiles over nkb 128-K
+// blocks: enough CTAs to cover the SMs, at least four k-blocks per range.
+int grouped_tc_splits(int64_t tiles, int64_t nkb);
+size_t grouped_tc_splitk_bytes(int64_t R, int64_t N, int splits);
 
 bool grouped_tc_supported(int64_t K, int64_t N, float limit, bool swiglu);
 int grouped_tc(const TcGemm& g, cudaStream_t stream);

@@ -164,32 +164,14 @@ __device__ void warp_topk_keys(const uint32_t* keys, const float* sigs, const To
   warp_topk_core<PER>(key, sig, p, idx_out, score_out, choice_smem);
 }
 
-// Double-FP32 accumulation (value hi + lo): the exact product of two FP32
-// values is fl(a b) plus the FMA residual, and TwoSum (Knuth) keeps the exact
-// rounding error of each addition, so the sum carries about 48 significant
-// bits before its one final FP32 rounding.
-// (__fadd_rn / __fmul_rn: the compiler may not contract or reorder them.)
-__device__ __forceinline__ void df_add(float& hi, float& lo, float v) {
-  const float s = __fadd_rn(hi, v);
-  const float bv = __fsub_rn(s, hi);
-  const float err = __fadd_rn(__fsub_rn(hi, __fsub_rn(s, bv)), __fsub_rn(v, bv));
-  hi = s;
-  lo = __fadd_rn(lo, err);
-}
-
-__device__ __forceinline__ void df_fma(float& hi, float& lo, float a, float b) {
-  const float p = __fmul_rn(a, b);
-  const float e = fmaf(a, b, -p);
-  df_add(hi, lo, p);
-  lo = __fadd_rn(lo, e);
-}
-
 // FP32 GEMV for T <= kRouterSmallT tokens: one block per expert row, each
-// thread sums float4 slices k = 4*tid + 1024*i in K order in double-FP32,
-// then an ordered warp / block reduction in double-FP32 and one rounding:
-// the logits are within about one FP32 ulp of the exact dot products (the
-// FP32 router of patch.py:131-142 evaluated to full FP32 accuracy, so a
-// logit near zero keeps its relative accuracy).  The last block to finish
+// thread sums float4 slices k = 4*tid + 1024*i in K order, then an ordered
+// warp / block reduction, and one rounding to FP32.  The sums are FP64: every
+// product of a BF16 activation and an FP32 weight is exact in FP64 (32
+// significant bits) and 4096 FP64 additions leave an error near 2^-41 of the
+// terms' magnitude, so each logit is the exact dot product rounded once to
+// FP32 (the FP32 router of patch.py:131-142 evaluated to full FP32 accuracy:
+// a logit near zero keeps its relative accuracy).  The last block to finish
 // runs the top-k.  The
 // group-mask scratch (8 warps x E floats) is dynamic shared memory, present
 // only when n_group > 1, so that the router's blocks leave room on the SMs
@@ -199,7 +181,7 @@ __global__ void __launch_bounds__(256) router_small_kernel(
     const uint16_t* __restrict__ x, int T, int H, const float* __restrict__ w,
     const float* __restrict__ bias, TopkParams p, float* logits, float* sig_buf, uint32_t* key_buf,
     uint32_t* counter, uint32_t* __restrict__ idx, float* __restrict__ scores) {
-  __shared__ float part[8][T_MAX], partl[8][T_MAX];
+  __shared__ double part[8][T_MAX];
   __shared__ bool is_last;
   extern __shared__ float choice_dyn[];  // [8][E] when n_group > 1
   // launched as a programmatic dependent of the kernel that writes x: wait
@@ -212,9 +194,9 @@ __global__ void __launch_bounds__(256) router_small_kernel(
   const int e = blockIdx.x;
   const float* wr = w + (size_t)e * H;
   const float be = threadIdx.x < T ? __ldg(bias + e) : 0.f;
-  float acc[T_MAX], accl[T_MAX];
+  double acc[T_MAX];
 #pragma unroll
-  for (int t = 0; t < T_MAX; ++t) acc[t] = accl[t] = 0.f;
+  for (int t = 0; t < T_MAX; ++t) acc[t] = 0.0;
 #pragma unroll 4
   for (int k = 4 * threadIdx.x; k < H; k += 1024) {
     const float4 wv = __ldcs(reinterpret_cast<const float4*>(wr + k));
@@ -222,36 +204,26 @@ __global__ void __launch_bounds__(256) router_small_kernel(
     for (int t = 0; t < T_MAX; ++t) {
       if (t < T) {
         const uint2 raw = __ldg(reinterpret_cast<const uint2*>(x + (size_t)t * H + k));
-        df_fma(acc[t], accl[t], __uint_as_float(raw.x << 16), wv.x);
-        df_fma(acc[t], accl[t], __uint_as_float(raw.x & 0xFFFF0000u), wv.y);
-        df_fma(acc[t], accl[t], __uint_as_float(raw.y << 16), wv.z);
-        df_fma(acc[t], accl[t], __uint_as_float(raw.y & 0xFFFF0000u), wv.w);
+        acc[t] = fma((double)__uint_as_float(raw.x << 16), (double)wv.x, acc[t]);
+        acc[t] = fma((double)__uint_as_float(raw.x & 0xFFFF0000u), (double)wv.y, acc[t]);
+        acc[t] = fma((double)__uint_as_float(raw.y << 16), (double)wv.z, acc[t]);
+        acc[t] = fma((double)__uint_as_float(raw.y & 0xFFFF0000u), (double)wv.w, acc[t]);
       }
     }
   }
 #pragma unroll
   for (int t = 0; t < T_MAX; ++t) {
-    float hi = acc[t], lo = accl[t];
+    double v = acc[t];
 #pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) {
-      const float oh = __shfl_xor_sync(0xffffffffu, hi, o), ol = __shfl_xor_sync(0xffffffffu, lo, o);
-      df_add(hi, lo, oh);
-      lo = __fadd_rn(lo, ol);
-    }
-    if (lane == 0) {
-      part[warp][t] = hi;
-      partl[warp][t] = lo;
-    }
+    for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) part[warp][t] = v;
   }
   __syncthreads();
   if (threadIdx.x < T_MAX && threadIdx.x < T) {
-    float hi = 0.f, lo = 0.f;
+    double d = 0.0;
 #pragma unroll
-    for (int ww = 0; ww < 8; ++ww) {
-      df_add(hi, lo, part[ww][threadIdx.x]);
-      lo = __fadd_rn(lo, partl[ww][threadIdx.x]);
-    }
-    const float v = __fadd_rn(hi, lo);
+    for (int ww = 0; ww < 8; ++ww) d += part[ww][threadIdx.x];
+    const float v = (float)d;
     const size_t o = (size_t)threadIdx.x * p.E + e;
     logits[o] = v;
     route_key(v, be, sig_buf[o], key_buf[o]);

@@ -67,7 +67,8 @@ def block_fp8_linear(x: torch.Tensor, weight: torch.Tensor, scale_inv: torch.Ten
     if M > _GEMV_MAX_ROWS:
         # tensor-core GEMM: scratch for the FP16 activation rows, one per device and stream
         stream = N.stream(x.device)
-        ws = _LINEAR_WS.get(x.device, f"rows:{stream}", N.lib().glm53_fp8_linear_workspace_bytes(M, in_features))
+        ws = _LINEAR_WS.get(x.device, f"rows:{stream}",
+                            N.lib().glm53_fp8_linear_splitk_workspace_bytes(M, in_features, out_features))
         status = _LINEAR_WS.get(x.device, "status", 4)
         N.check(
             N.lib().glm53_fp8_linear_ws(

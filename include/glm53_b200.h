@@ -87,6 +87,15 @@ int glm53_fp8_linear(const void* x, int64_t M, int64_t K, const uint8_t* w,
 /* Workspace bytes of glm53_fp8_linear_ws for M rows of width K. */
 size_t glm53_fp8_linear_workspace_bytes(int64_t M, int64_t K);
 
+/* Workspace bytes of glm53_fp8_linear_ws for M x K rows and N outputs with
+ * room for split-K partial sums: when the tcgen05 GEMM has fewer output tiles
+ * (128 rows x 128 outputs) than half the SMs, each tile's K is cut into ranges
+ * computed by different CTAs and the FP32 partials are added in range order
+ * by a second kernel (deterministic; a valid FP32 summation order of the same
+ * products).  A workspace of only glm53_fp8_linear_workspace_bytes runs
+ * without the split. */
+size_t glm53_fp8_linear_splitk_workspace_bytes(int64_t M, int64_t K, int64_t N);
+
 /* glm53_fp8_linear with caller scratch: for M > 16 rows, K % 128 == 0, N % 8
  * == 0 and 16-byte aligned x / w / workspace it runs the tcgen05 GEMM (the
  * activations converted once to FP16 x 2^-e rows in the workspace; exact FP16
