@@ -64,6 +64,11 @@ SIGNATURES: dict[str, tuple] = {
         [_vp, _i64, _vp, _vp, _int, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _f,
          _vp, _vp, _u32, _vp],
     ),
+    "glm53_packed_decode_moe_hc": (
+        _int,
+        [_vp, _i64, _vp, _vp, _int, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _f,
+         _vp, _vp, _vp, _vp, _vp, _sz, _vp, _u32, _vp],
+    ),
     "glm53_selected_decode_moe": (
         _int,
         [_vp, _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _f,

@@ -58,6 +58,13 @@ struct DecodeArgs {
   const uint8_t* sd_w;
   const float* sd_s;
   float limit;
+  // mHC post-expand fused into the final reduce (glm53_packed_decode_moe_hc):
+  // instead of out[h], write hc_out[b][h] = BF16(post[b] * moe[h] + FMA chain
+  // over the 4 sources comb[s][b] * residual[s][h]) for the 4 branches b
+  const uint16_t* hc_residual;  // [4, H] BF16
+  const float* hc_post;         // [4]
+  const float* hc_comb;         // [4][4], comb[source][branch]
+  uint16_t* hc_out;             // [4, H] BF16
   uint16_t* hidden;    // [top_k*I + Is]
   float* partial;      // [(top_k + 1) * H] per-slot down dot products
   uint32_t* counters;  // [H / 16] completion counters (zero between calls)
@@ -483,7 +490,23 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_down_v4(DecodeArgs
     }
     float res = bf16_round(total);
     if (a.Is > 0) res = res + bf16_round(__ldcg(a.partial + (size_t)a.top_k * a.H + h));
-    a.out[h] = f32_to_bf16_bits(res);
+    if (a.hc_out) {
+      // hc expand with the arithmetic order of glm53_hc_expand
+      // (native_indexer_plan.metal:2377-2388)
+      const float moe = bf16_bits_to_f32(f32_to_bf16_bits(res));
+      float rv[4];
+#pragma unroll
+      for (int src = 0; src < 4; ++src) rv[src] = bf16_bits_to_f32(a.hc_residual[(size_t)src * a.H + h]);
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        float mixed = 0.0f;
+#pragma unroll
+        for (int src = 0; src < 4; ++src) mixed = __fmaf_rn(__ldg(a.hc_comb + src * 4 + b), rv[src], mixed);
+        a.hc_out[(size_t)b * a.H + h] = f32_to_bf16_bits(__fadd_rn(__fmul_rn(__ldg(a.hc_post + b), moe), mixed));
+      }
+    } else {
+      a.out[h] = f32_to_bf16_bits(res);
+    }
   }
   if (lane == 0) a.counters[tile] = 0u;  // leave the workspace reusable
 }
@@ -826,6 +849,52 @@ extern "C" int glm53_packed_decode_moe(const void* x, int64_t H, const uint32_t*
   a.d_w = down_w;
   a.d_s = down_s;
   a.after_router = (flags & GLM53_FLAG_AFTER_ROUTER) != 0;
+  return packed_decode(a, (cudaStream_t)stream, false, flags);
+}
+
+extern "C" int glm53_packed_decode_moe_hc(const void* x, int64_t H, const uint32_t* expert_ids, const float* scores,
+                                          int top_k, const uint8_t* gate_up_w, const float* gate_up_s,
+                                          const uint8_t* down_w, const float* down_s, int64_t E, int64_t I,
+                                          const uint8_t* shared_gate_w, const float* shared_gate_s,
+                                          const uint8_t* shared_up_w, const float* shared_up_s,
+                                          const uint8_t* shared_down_w, const float* shared_down_s,
+                                          int64_t I_shared, float limit, const void* residual, const float* post,
+                                          const float* comb, void* out_state, void* workspace,
+                                          size_t workspace_bytes, uint32_t* status, uint32_t flags, void* stream) {
+  const char* fn = "glm53_packed_decode_moe_hc";
+  int rc = check_geometry(fn, H, I, top_k, I_shared);
+  if (rc) return rc;
+  const bool has_shared = I_shared > 0;
+  if (E <= 0 || !x || !expert_ids || !scores || !gate_up_w || !gate_up_s || !down_w || !down_s || !residual ||
+      !post || !comb || !out_state || !status || !workspace ||
+      workspace_bytes < glm53_packed_decode_workspace_bytes(top_k, H, I, I_shared) ||
+      (has_shared && (!shared_gate_w || !shared_gate_s || !shared_up_w || !shared_up_s || !shared_down_w ||
+                      !shared_down_s))) {
+    set_last_error("%s: missing pointer, E <= 0 or workspace too small", fn);
+    return GLM53_ERR_INVALID;
+  }
+  if (flags & GLM53_FLAG_SHARED_ONLY) {
+    set_last_error("%s: GLM53_FLAG_SHARED_ONLY computes no output to expand", fn);
+    return GLM53_ERR_INVALID;
+  }
+  DecodeArgs a{};
+  fill_common(a, x, H, scores, top_k, I, shared_gate_w, shared_gate_s, shared_up_w, shared_up_s, shared_down_w,
+              shared_down_s, I_shared, limit, nullptr, workspace, status);
+  a.E = (int)std::min<int64_t>(E, INT32_MAX);
+  a.ids = expert_ids;
+  a.gu_w = gate_up_w;
+  a.gu_s = gate_up_s;
+  a.d_w = down_w;
+  a.d_s = down_s;
+  a.after_router = (flags & GLM53_FLAG_AFTER_ROUTER) != 0;
+  a.hc_residual = (const uint16_t*)residual;
+  a.hc_post = post;
+  a.hc_comb = comb;
+  a.hc_out = (uint16_t*)out_state;
+  if (!tensor_core_shape(a)) {
+    set_last_error("%s: H, I and I_shared must be multiples of 128 with 16-byte aligned tensors", fn);
+    return GLM53_ERR_INVALID;
+  }
   return packed_decode(a, (cudaStream_t)stream, false, flags);
 }
 

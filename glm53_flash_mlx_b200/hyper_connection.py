@@ -178,4 +178,7 @@ class FFNBoundary(nn.Module):
 
     def forward(self, state: torch.Tensor) -> torch.Tensor:
         _, normalized, post, comb = self.ffn_hc.collapse_norm(state, self.post_attention_layernorm)
+        fused = getattr(self.mlp, "forward_expand", None)
+        if fused is not None:  # a packed MoE: one decode token expands inside its final reduce
+            return fused(normalized, state, post, comb)
         return hc_expand(self.mlp(normalized), state, post, comb)

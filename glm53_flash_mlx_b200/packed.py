@@ -199,7 +199,7 @@ def shared_fp8_tensors(shared) -> tuple | None:
 def packed_decode_moe(x: torch.Tensor, expert_ids: torch.Tensor, scores: torch.Tensor, bank: PackedFP8ExpertBank,
                       shared: tuple | None, *, limit: float, workspace: N.Workspace | None = None,
                       status: torch.Tensor | None = None, split: str | None = None,
-                      after_router: bool = False) -> torch.Tensor | None:
+                      after_router: bool = False, hc: tuple | None = None) -> torch.Tensor | None:
     """One-token routed MoE (+ shared expert) over the packed bank.
 
     x: BF16 [H]; expert_ids: int32/uint32 [top_k]; scores: float32 [top_k].
@@ -210,7 +210,11 @@ def packed_decode_moe(x: torch.Tensor, expert_ids: torch.Tensor, scores: torch.T
     ``after_router=True`` states that the last kernel on the current stream
     is the router that produced ``expert_ids``/``scores`` from ``x``: when no
     argument needs a copy here, the shared expert then streams while that
-    router still runs (GLM53_FLAG_AFTER_ROUTER; same result bits)."""
+    router still runs (GLM53_FLAG_AFTER_ROUTER; same result bits).
+    ``hc=(residual [4, H] BF16, post [4] FP32, comb [4, 4] FP32)`` fuses the
+    layer's mHC post-expand into the final reduce and returns the next state
+    BF16 [4, H] (``glm53_packed_decode_moe_hc``; the bits of the decode
+    followed by ``hc_expand``)."""
     dev = N.require_cuda(x, expert_ids, scores, bank.gate_up_weight)
     H = bank.hidden_size
     I = bank.intermediate_size
@@ -221,7 +225,7 @@ def packed_decode_moe(x: torch.Tensor, expert_ids: torch.Tensor, scores: torch.T
     # programmatic overlap: every argument must be usable as it is
     overlap = (after_router and split is None and x.is_contiguous() and expert_ids.is_contiguous() and
                scores.is_contiguous() and expert_ids.dtype == torch.int32 and
-               scores.dtype == torch.float32)
+               scores.dtype == torch.float32 and (hc is None or all(t.is_contiguous() for t in hc)))
     x = x.reshape(H).contiguous()
     ids = expert_ids.reshape(-1).to(torch.int32).contiguous()
     sc = scores.reshape(-1).to(torch.float32).contiguous()
@@ -246,6 +250,29 @@ def packed_decode_moe(x: torch.Tensor, expert_ids: torch.Tensor, scores: torch.T
         status = wsp.get(dev, "status", 4)
     if overlap:  # nothing was launched since the router: no copy, scan or zero-fill above
         flags |= N.FLAG_AFTER_ROUTER
+    if hc is not None:
+        residual, post, comb = hc
+        if split is not None:
+            raise ValueError("the fused hc expand takes the whole decode (no split)")
+        if (residual.dtype != torch.bfloat16 or residual.numel() != 4 * H or post.dtype != torch.float32 or
+                post.numel() != 4 or comb.dtype != torch.float32 or comb.numel() != 16):
+            raise ValueError("hc needs residual BF16 [4, H], post FP32 [4] and comb FP32 [4, 4]")
+        residual, post, comb = residual.contiguous(), post.contiguous(), comb.contiguous()
+        state = torch.empty((4, H), dtype=torch.bfloat16, device=dev)
+        N.check(
+            N.lib().glm53_packed_decode_moe_hc(
+                x.data_ptr(), H, ids.data_ptr(), sc.data_ptr(), top_k,
+                bank.gate_up_weight.data_ptr(), bank.gate_up_scale_inv.data_ptr(),
+                bank.down_weight.data_ptr(), bank.down_scale_inv.data_ptr(), bank.expert_count, I,
+                N.ptr(sg_w), N.ptr(sg_s), N.ptr(su_w), N.ptr(su_s), N.ptr(sd_w), N.ptr(sd_s), Is,
+                float(limit), residual.data_ptr(), post.data_ptr(), comb.data_ptr(), state.data_ptr(),
+                ws.data_ptr(), ws.numel(), status.data_ptr(), flags, N.stream(dev),
+            ),
+            "glm53_packed_decode_moe_hc",
+        )
+        if _SYNC_STATUS:
+            check_status(status)
+        return state
     out = torch.empty(H, dtype=torch.bfloat16, device=dev)
     N.check(
         N.lib().glm53_packed_decode_moe(
@@ -646,6 +673,33 @@ class PackedFP8MoE(DirectFP8MoE):
         if PackedDecodeStep.supported(self):
             return PackedDecodeStep(self)
         return CapturedDecode(self, self.bank.hidden_size, self.bank.gate_up_weight.device)
+
+    def forward_expand(self, x, residual, post, comb):
+        """The layer followed by the mHC post-expand: ``hc_expand(self(x),
+        residual, post, comb)``.  One token with the Float32Gate router and the
+        tensor-core shapes runs the expand inside the decode's final reduce
+        (``glm53_packed_decode_moe_hc``, same bits); anything else calls the
+        two steps.  x [..., H]; residual [..., 4, H]; returns [..., 4, H]."""
+        from .hyper_connection import hc_expand
+
+        flat_x = x.reshape(-1, x.shape[-1])
+        shared = shared_fp8_tensors(self.shared_experts)
+        limit = self.config.swiglu_limit
+        H, I = self.bank.hidden_size, self.bank.intermediate_size
+        fused = (flat_x.shape[0] == 1 and flat_x.is_cuda and isinstance(self.gate, Float32Gate) and
+                 self.gate.top_k == DECODE_TOP_K and float(limit) == int(limit) and H % BLOCK_SIZE == 0 and
+                 I % BLOCK_SIZE == 0 and (self.shared_experts is None or
+                                          (shared is not None and shared[0].shape[0] == I)))
+        if not fused:
+            return hc_expand(self(x), residual, post, comb)
+        sw = self.status_word(flat_x.device)
+        sw.raise_pending()
+        indices, scores = self.gate(x)
+        state = packed_decode_moe(flat_x[0], indices.reshape(-1), scores.reshape(-1), self.bank, shared, limit=limit,
+                                  workspace=self._workspace, status=sw.word, after_router=True,
+                                  hc=(residual, post, comb))
+        sw.publish()
+        return state.reshape(residual.shape)
 
     def forward(self, x):
         flat_x = x.reshape(-1, x.shape[-1])

@@ -195,6 +195,28 @@ int glm53_selected_decode_moe(const void* x, int64_t H, const float* scores, int
                               void* out, void* workspace, size_t workspace_bytes,
                               uint32_t* status, uint32_t flags, void* stream);
 
+/* glm53_packed_decode_moe followed by the layer's mHC post-expand, in the same
+ * two launches: the final reduce writes, instead of the MoE row moe[h], the 4
+ * branches of the next residual state,
+ *   out_state[b][h] = BF16(post[b] * moe[h] + sum_s comb[s][b] * residual[s][h]),
+ * with the FMA chain over the 4 sources and the rounded post product added
+ * last -- bit for bit what glm53_packed_decode_moe then glm53_hc_expand give.
+ * residual / out_state BF16 [4, H] (they may not alias), post FP32 [4], comb
+ * FP32 [4][4] (comb[source][branch]).  The FFN half of a GLM-5.3 decode layer
+ * (mlp, then hc_expand: scripts/trace_grouped_fp8_route_amplification.py:
+ * 178-214; the expand of native_indexer_plan.metal:2362-2389) without a third
+ * launch.  Tensor-core shapes only (H, I, I_shared multiples of 128); flags
+ * as glm53_packed_decode_moe except GLM53_FLAG_SHARED_ONLY (no output). */
+int glm53_packed_decode_moe_hc(const void* x, int64_t H, const uint32_t* expert_ids, const float* scores,
+                               int top_k, const uint8_t* gate_up_w, const float* gate_up_s,
+                               const uint8_t* down_w, const float* down_s, int64_t E, int64_t I,
+                               const uint8_t* shared_gate_w, const float* shared_gate_s,
+                               const uint8_t* shared_up_w, const float* shared_up_s,
+                               const uint8_t* shared_down_w, const float* shared_down_s, int64_t I_shared,
+                               float limit, const void* residual, const float* post, const float* comb,
+                               void* out_state, void* workspace, size_t workspace_bytes, uint32_t* status,
+                               uint32_t flags, void* stream);
+
 /* Size of the fixed scratch area of glm53_packed_decode_moe_static_scratch:
  * 1 MiB of device memory on every device that loads the library, held until
  * the process exits. */

@@ -227,14 +227,16 @@ def test_hc_expand_bit_exact(oracle, T, H):
 
 
 @pytest.mark.gpu
-def test_ffn_boundary_composes_the_three_calls_bitwise(oracle):
+@pytest.mark.parametrize("T,E,H,I", [(1, 16, 256, 128), (1, 32, 4096, 1536), (3, 16, 256, 128)])
+def test_ffn_boundary_composes_the_three_calls_bitwise(oracle, T, E, H, I):
     """FFNBoundary(state) == hc_expand(mlp(norm(collapse(state)))) through a
-    PackedFP8MoE layer, and its collapse and expand agree with the oracle."""
+    PackedFP8MoE layer (one token: the expand runs inside the decode's final
+    reduce, glm53_packed_decode_moe_hc; more tokens: the separate calls), and
+    its collapse and expand agree with the oracle."""
     import glm53_flash_mlx_b200 as G
     from glm53_flash_mlx_b200 import synthetic as S
 
     dev = torch.device("cuda:0")
-    E, H, I = 16, 256, 128
     config = S.moe_config(H=H, I=I, E=E)
     gate = G.Float32Gate(config, device=dev)
     w, b = S.make_router(E, H, seed=21, device=dev)
@@ -242,7 +244,7 @@ def test_ffn_boundary_composes_the_three_calls_bitwise(oracle):
     gate.e_score_correction_bias.copy_(b)
     bank = S.make_bank(E, H, I, seed=21, device=dev)
     mlp = G.PackedFP8MoE(bank, config, gate, S.make_shared(H, I, seed=21, device=dev))
-    state, fn, scale, base, norm_w = _inputs(1, H, 22)
+    state, fn, scale, base, norm_w = _inputs(T, H, 22)
     hc = _module(G, fn, scale, base, H, dev)
     norm = G.RMSNorm(H, device=dev)
     norm.weight.copy_(from_bits(norm_w, dev))
