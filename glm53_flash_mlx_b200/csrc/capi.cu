@@ -97,13 +97,19 @@ namespace glm53 {
 // With `status` and `mirror` set, thread 0 of block 0 also copies the device
 // status word into the mapped host word `mirror` (the work before this grid
 // on the stream has finished, so the word holds every earlier call's bits).
+// Launched as a programmatic dependent (pdl), the copy may run while the
+// previous kernel still does; the status word is read only after
+// griddepcontrol.wait, when that kernel has finished (a no-op otherwise).
 __global__ void __launch_bounds__(256) copy16_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst,
                                                      size_t n16, const uint32_t* __restrict__ status,
                                                      volatile uint32_t* mirror) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  if (mirror && blockIdx.x == 0 && threadIdx.x == 0) *mirror = *(const volatile uint32_t*)status;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (size_t)gridDim.x * blockDim.x)
     dst[i] = src[i];
+  if (mirror && blockIdx.x == 0 && threadIdx.x == 0) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    *mirror = *(const volatile uint32_t*)status;
+  }
 }
 
 __global__ void status_mirror_kernel(const uint32_t* __restrict__ status, volatile uint32_t* mirror) {
@@ -123,17 +129,24 @@ void* mapped_host(const void* p) {
 // mapping (a copy-engine transfer of a few KB costs 7-10 us of stream time
 // on B200, the kernel about 2), else cudaMemcpyAsync.
 cudaError_t small_copy(void* dst, const void* src, size_t bytes, bool to_device, cudaStream_t st, bool* by_kernel,
-                       const uint32_t* status, uint32_t* status_mirror) {
+                       const uint32_t* status, uint32_t* status_mirror, bool pdl) {
   const void* host = to_device ? src : dst;
   void* mapped = (bytes % 16 == 0 && ((uintptr_t)src | (uintptr_t)dst) % 16 == 0) ? mapped_host(host) : nullptr;
   if (by_kernel) *by_kernel = mapped != nullptr;
   if (!mapped)
     return cudaMemcpyAsync(dst, src, bytes, to_device ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToHost, st);
   const size_t n16 = bytes / 16;
-  const unsigned blocks = (unsigned)std::min<size_t>((n16 + 255) / 256, 64);
-  copy16_kernel<<<blocks, 256, 0, st>>>((const uint4*)(to_device ? mapped : src),
-                                        (uint4*)(to_device ? dst : mapped), n16, status,
-                                        status ? status_mirror : nullptr);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)std::min<size_t>((n16 + 255) / 256, 64));
+  cfg.blockDim = dim3(256);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, copy16_kernel, (const uint4*)(to_device ? mapped : src), (uint4*)(to_device ? dst : mapped),
+                     n16, status, status ? status_mirror : (uint32_t*)nullptr);
   return cudaGetLastError();
 }
 

@@ -116,9 +116,12 @@ void* mapped_host(const void* p);
 // both addresses and the size are 16-byte multiples (*by_kernel = true), else
 // cudaMemcpyAsync (capi.cu).  When the copy runs as a kernel and `status` and
 // `status_mirror` (pinned host) are given, the kernel also copies the device
-// status word into the host word.
+// status word into the host word.  pdl: the kernel is launched as a
+// programmatic dependent of the previous kernel (it copies at once and reads
+// the status word after that kernel has finished); only for a destination
+// the previous kernel does not touch.
 cudaError_t small_copy(void* dst, const void* src, size_t bytes, bool to_device, cudaStream_t st, bool* by_kernel,
-                       const uint32_t* status = nullptr, uint32_t* status_mirror = nullptr);
+                       const uint32_t* status = nullptr, uint32_t* status_mirror = nullptr, bool pdl = false);
 // One-thread kernel copying the device status word into a pinned host word
 // (GLM53_ERR_INVALID when host_word is not device-mapped).
 int mirror_status(const uint32_t* status, uint32_t* host_word, cudaStream_t st, const char* fn);

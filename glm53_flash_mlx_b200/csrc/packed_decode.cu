@@ -111,6 +111,10 @@ struct DecodeArgs {
   // the routed ones for their arrivals), and the down stage lets the combine
   // launch early
   bool pdl_owner;
+  // host decode steps: the down stage lets the next step's input copy launch
+  // once the gate/up grid has finished (no kernel of this step reads the
+  // input row after that), so its host read overlaps the down stage
+  bool trigger_after_wait;
 };
 
 // Physical routed slot p of a peer-memory owner grid -> slot (src, s) = src * cap + s.
@@ -441,6 +445,7 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_down_v4(DecodeArgs
   sd.load(srow, cols, ld);
   // weights are streaming; the hidden rows come from the gate/up stage
   pdl_wait();
+  if (a.trigger_after_wait) pdl_trigger();
   const float smul =
       decode_unscale<FINITE>() * stage_f16(xs, K + 8, a.hidden + (size_t)jb * a.I, 0, 1, K, scratch);
   float part[4] = {0.f, 0.f, 0.f, 0.f}, tot[4] = {0.f, 0.f, 0.f, 0.f};
@@ -504,6 +509,15 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) decode_down_v4(DecodeArgs
         for (int src = 0; src < 4; ++src) mixed = __fmaf_rn(__ldg(a.hc_comb + src * 4 + b), rv[src], mixed);
         a.hc_out[(size_t)b * a.H + h] = f32_to_bf16_bits(__fadd_rn(__fmul_rn(__ldg(a.hc_post + b), moe), mixed));
       }
+    } else if ((((uintptr_t)a.out) & 15) == 0) {
+      // two 16-byte stores per 16-row tile (the output may be host memory
+      // mapped over PCIe, where small writes cost)
+      const uint32_t v = f32_to_bf16_bits(res);
+      const uint32_t w = v | (__shfl_down_sync(0x0000FFFFu, v, 1) << 16);  // even lanes: rows h, h + 1
+      const uint32_t w1 = __shfl_down_sync(0x0000FFFFu, w, 2);
+      const uint32_t w2 = __shfl_down_sync(0x0000FFFFu, w, 4);
+      const uint32_t w3 = __shfl_down_sync(0x0000FFFFu, w, 6);
+      if ((lane & 7) == 0) *reinterpret_cast<uint4*>(a.out + h) = make_uint4(w, w1, w2, w3);
     } else {
       a.out[h] = f32_to_bf16_bits(res);
     }
@@ -821,6 +835,14 @@ extern "C" int glm53_packed_decode_workspace_layout(int top_k, int64_t H, int64_
   return GLM53_OK;
 }
 
+static int packed_decode_moe_impl(const void* x, int64_t H, const uint32_t* expert_ids, const float* scores,
+                                  int top_k, const uint8_t* gate_up_w, const float* gate_up_s, const uint8_t* down_w,
+                                  const float* down_s, int64_t E, int64_t I, const uint8_t* shared_gate_w,
+                                  const float* shared_gate_s, const uint8_t* shared_up_w, const float* shared_up_s,
+                                  const uint8_t* shared_down_w, const float* shared_down_s, int64_t I_shared,
+                                  float limit, void* out, void* workspace, size_t workspace_bytes, uint32_t* status,
+                                  uint32_t flags, void* stream, bool trigger_after_wait);
+
 extern "C" int glm53_packed_decode_moe(const void* x, int64_t H, const uint32_t* expert_ids, const float* scores,
                                        int top_k, const uint8_t* gate_up_w, const float* gate_up_s,
                                        const uint8_t* down_w, const float* down_s, int64_t E, int64_t I,
@@ -829,6 +851,18 @@ extern "C" int glm53_packed_decode_moe(const void* x, int64_t H, const uint32_t*
                                        const uint8_t* shared_down_w, const float* shared_down_s, int64_t I_shared,
                                        float limit, void* out, void* workspace, size_t workspace_bytes,
                                        uint32_t* status, uint32_t flags, void* stream) {
+  return packed_decode_moe_impl(x, H, expert_ids, scores, top_k, gate_up_w, gate_up_s, down_w, down_s, E, I,
+                                shared_gate_w, shared_gate_s, shared_up_w, shared_up_s, shared_down_w, shared_down_s,
+                                I_shared, limit, out, workspace, workspace_bytes, status, flags, stream, false);
+}
+
+static int packed_decode_moe_impl(const void* x, int64_t H, const uint32_t* expert_ids, const float* scores,
+                                  int top_k, const uint8_t* gate_up_w, const float* gate_up_s, const uint8_t* down_w,
+                                  const float* down_s, int64_t E, int64_t I, const uint8_t* shared_gate_w,
+                                  const float* shared_gate_s, const uint8_t* shared_up_w, const float* shared_up_s,
+                                  const uint8_t* shared_down_w, const float* shared_down_s, int64_t I_shared,
+                                  float limit, void* out, void* workspace, size_t workspace_bytes, uint32_t* status,
+                                  uint32_t flags, void* stream, bool trigger_after_wait) {
   int rc = check_geometry("glm53_packed_decode_moe", H, I, top_k, I_shared);
   if (rc) return rc;
   const bool has_shared = I_shared > 0;
@@ -849,6 +883,7 @@ extern "C" int glm53_packed_decode_moe(const void* x, int64_t H, const uint32_t*
   a.d_w = down_w;
   a.d_s = down_s;
   a.after_router = (flags & GLM53_FLAG_AFTER_ROUTER) != 0;
+  a.trigger_after_wait = trigger_after_wait;
   return packed_decode(a, (cudaStream_t)stream, false, flags);
 }
 
@@ -949,7 +984,9 @@ extern "C" int glm53_decode_step_host(const glm53_decode_step_desc* d, const voi
   const size_t row = (size_t)d->H * 2;
   bool copy_kernel = false;
   if (x_host) {
-    cudaError_t e = small_copy(d->x, x_host, row, true, st, &copy_kernel, d->status, d->status_host);
+    // a programmatic dependent of the previous step's down stage, which lets
+    // it launch once no kernel of that step reads d->x any more
+    cudaError_t e = small_copy(d->x, x_host, row, true, st, &copy_kernel, d->status, d->status_host, true);
     if (e != cudaSuccess) {
       set_last_error("%s: input copy: %s", fn, cudaGetErrorString(e));
       return GLM53_ERR_CUDA;
@@ -965,11 +1002,11 @@ extern "C" int glm53_decode_step_host(const glm53_decode_step_desc* d, const voi
                        d->router_workspace, d->router_workspace_bytes, st, copy_kernel);
   if (rc) return rc;
   void* mapped_out = out_host && (((uintptr_t)out_host) & 15) == 0 ? mapped_host(out_host) : nullptr;
-  rc = glm53_packed_decode_moe(d->x, d->H, d->expert_ids, d->scores, d->top_k, d->gate_up_w, d->gate_up_s, d->down_w,
-                               d->down_s, d->E, d->I, d->shared_gate_w, d->shared_gate_s, d->shared_up_w,
-                               d->shared_up_s, d->shared_down_w, d->shared_down_s, d->I_shared, d->limit,
-                               mapped_out ? mapped_out : d->out, d->decode_workspace, d->decode_workspace_bytes,
-                               d->status, d->flags | GLM53_FLAG_AFTER_ROUTER, stream);
+  rc = packed_decode_moe_impl(d->x, d->H, d->expert_ids, d->scores, d->top_k, d->gate_up_w, d->gate_up_s, d->down_w,
+                              d->down_s, d->E, d->I, d->shared_gate_w, d->shared_gate_s, d->shared_up_w,
+                              d->shared_up_s, d->shared_down_w, d->shared_down_s, d->I_shared, d->limit,
+                              mapped_out ? mapped_out : d->out, d->decode_workspace, d->decode_workspace_bytes,
+                              d->status, d->flags | GLM53_FLAG_AFTER_ROUTER, stream, true);
   if (rc || !out_host || mapped_out) return rc;
   const cudaError_t e = cudaMemcpyAsync(out_host, d->out, row, cudaMemcpyDeviceToHost, st);
   if (e != cudaSuccess) {

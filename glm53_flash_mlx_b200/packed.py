@@ -535,6 +535,7 @@ class PackedDecodeStep:
             decode_workspace=dws.data_ptr(), decode_workspace_bytes=dws.numel(), status=status.data_ptr(),
             status_host=self._status.host.data_ptr())
         self._pdesc = ctypes.pointer(self._desc)
+        self._lib = lib
 
     @staticmethod
     def _bound_tensors(module) -> tuple:
@@ -618,7 +619,7 @@ class PackedDecodeStep:
                 raise ValueError("decode step output must be a contiguous BF16 row of the layer width")
             if out.device.type == "cpu":
                 out_host = out.data_ptr()
-        N.check(N.lib().glm53_decode_step_host(self._pdesc, x_host, out_host, N.stream(self.x.device)),
+        N.check(self._lib.glm53_decode_step_host(self._pdesc, x_host, out_host, N.stream(self.x.device)),
                 "glm53_decode_step_host")
         if _SYNC_STATUS:
             self._status.check()
