@@ -291,15 +291,22 @@ struct Tile {
   int ks, kb0, kb1;  // split index and its k-block range [kb0, kb1)
 };
 
+template <bool SPLIT>
 __device__ __forceinline__ Tile tile_at(const TcArgs& a, int t, int mtiles, int zsub) {
   Tile tl;
-  // the split index is innermost, so the CTAs of one tile's ranges run side
-  // by side and share its activation rows through L2
   const int nkb = a.K / kKB;
-  tl.ks = t % a.splits;
-  tl.kb0 = (int)((int64_t)tl.ks * nkb / a.splits);
-  tl.kb1 = (int)((int64_t)(tl.ks + 1) * nkb / a.splits);
-  t /= a.splits;
+  if constexpr (SPLIT) {
+    // the split index is innermost, so the CTAs of one tile's ranges run side
+    // by side and share its activation rows through L2
+    tl.ks = t % a.splits;
+    tl.kb0 = (int)((int64_t)tl.ks * nkb / a.splits);
+    tl.kb1 = (int)((int64_t)(tl.ks + 1) * nkb / a.splits);
+    t /= a.splits;
+  } else {
+    tl.ks = 0;
+    tl.kb0 = 0;
+    tl.kb1 = nkb;
+  }
   const int d = t / (mtiles * zsub);
   const int rem = t - d * mtiles * zsub;
   tl.mt = rem / zsub;
@@ -330,7 +337,7 @@ __device__ __forceinline__ int tile_row0(int mt) {
 // Tensor maps: w (and u) boxes of 64 rows (SwiGLU) or 128 rows (plain) x 128
 // K codes; x boxes of 128 routes and, for tiles of <= 64 routes, x64 boxes of
 // 64 routes, each x 64 K.
-template <bool SWIGLU, bool FINITE>
+template <bool SWIGLU, bool FINITE, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap umap,
                       const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap xmap64, TcArgs a,
@@ -393,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       auto first = [&](Cursor& c, int t) {
         for (c.t = t; c.t < ntiles; c.t += gridDim.x) {
-          c.tl = tile_at(a, c.t, mtiles, zsub);
+          c.tl = tile_at<SPLIT>(a, c.t, mtiles, zsub);
           if (c.tl.len) {
             c.kb = c.tl.kb0;
             return;
@@ -478,7 +485,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t g = 0;
       bool stop = false;
       for (int t = blockIdx.x; t < ntiles && !stop; t += gridDim.x) {
-        const Tile tl = tile_at(a, t, mtiles, zsub);
+        const Tile tl = tile_at<SPLIT>(a, t, mtiles, zsub);
         if (tl.len == 0) continue;
         const uint32_t idesc = tl.len > 64 ? make_idesc(kM, kN) : make_idesc(kM, 64);
         for (int kb = tl.kb0; kb < tl.kb1; ++kb, ++g) {
@@ -518,7 +525,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t g = 0;
     bool stop = false;
     for (int t = blockIdx.x; t < ntiles && !stop; t += gridDim.x) {
-      const Tile tl = tile_at(a, t, mtiles, zsub);
+      const Tile tl = tile_at<SPLIT>(a, t, mtiles, zsub);
       if (tl.len == 0) continue;
       for (int kb = tl.kb0; kb < tl.kb1; ++kb, ++g) {
         const int s = g % kRawStages;
@@ -568,7 +575,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t g = 0, tcount = 0;
     bool stop = false;
     for (int t = blockIdx.x; t < ntiles && !stop; t += gridDim.x) {
-      const Tile tl = tile_at(a, t, mtiles, zsub);
+      const Tile tl = tile_at<SPLIT>(a, t, mtiles, zsub);
       if (tl.len == 0) continue;
       const int row0 = tile_row0<SWIGLU>(tl.mt);
       const float* srow = (up_rows ? a.s_up : a.s_gate) + (size_t)tl.e * a.s_expert + (size_t)(row0 >> 7) * nkb;
@@ -606,7 +613,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // route range multipliers of this half: lane l holds routes n0 + l and n0 + 32 + l
       const float xa = (a.xscale && n0 + lane < tl.len) ? __ldg(a.xscale + tl.start + n0 + lane) : 1.0f;
       const float xb = (a.xscale && n0 + 32 + lane < tl.len) ? __ldg(a.xscale + tl.start + n0 + 32 + lane) : 1.0f;
-      if (!SWIGLU && a.splits > 1) {
+      if (!SWIGLU && SPLIT) {
         // this range's FP32 partial sums; the reduce kernel adds the ranges in
         // order and applies the route multiplier
         const int col = row0 + r;
@@ -835,10 +842,13 @@ int grouped_tc(const TcGemm& g, cudaStream_t st) {
   if (g.swiglu) {
     rc = ensure_sigmoid_table(st);
     if (rc) return rc;
-    kern = g.finite ? grouped_tc_kernel<true, true> : grouped_tc_kernel<true, false>;
+    kern = g.finite ? grouped_tc_kernel<true, true, false> : grouped_tc_kernel<true, false, false>;
     smem = smem_bytes<true>();
+  } else if (splits > 1) {
+    kern = g.finite ? grouped_tc_kernel<false, true, true> : grouped_tc_kernel<false, false, true>;
+    smem = smem_bytes<false>();
   } else {
-    kern = g.finite ? grouped_tc_kernel<false, true> : grouped_tc_kernel<false, false>;
+    kern = g.finite ? grouped_tc_kernel<false, true, false> : grouped_tc_kernel<false, false, false>;
     smem = smem_bytes<false>();
   }
   rc = ensure_max_smem((const void*)kern, smem);
