@@ -536,6 +536,10 @@ class PackedDecodeStep:
             status_host=self._status.host.data_ptr())
         self._pdesc = ctypes.pointer(self._desc)
         self._lib = lib
+        # a second descriptor whose input and output point at the caller's
+        # device rows (run_device): no copy into or out of the static buffers
+        self._ddesc = N.DecodeStepDesc.from_buffer_copy(self._desc)
+        self._pddesc = ctypes.pointer(self._ddesc)
 
     @staticmethod
     def _bound_tensors(module) -> tuple:
@@ -569,23 +573,45 @@ class PackedDecodeStep:
                 slots += [slot(module.shared_experts, proj), slot(p, "weight"), slot(p, "weight_scale_inv")]
         return tuple(slots)
 
-    def _check_bound(self) -> None:
+    def bound_ok(self) -> bool:
+        """True while every tensor the step bound is still the layer's, unchanged."""
         for (d, name, obj) in self._slots:
             if d.get(name) is not obj:
-                break
-        else:
-            for t, (ptr, version) in zip(self._bound, self._identity):
-                if t._version != version or t.data_ptr() != ptr:
-                    break
-            else:
-                return
-        raise RuntimeError("packed MoE decode step: a bound weight's identity changed (replaced, reallocated or "
-                           "written in place); capture a new step with capture_decode()")
+                return False
+        for t, (ptr, version) in zip(self._bound, self._identity):
+            if t._version != version or t.data_ptr() != ptr:
+                return False
+        return True
+
+    def _check_bound(self) -> None:
+        if not self.bound_ok():
+            raise RuntimeError("packed MoE decode step: a bound weight's identity changed (replaced, reallocated or "
+                               "written in place); capture a new step with capture_decode()")
 
     def check(self) -> None:
         """Synchronise and raise for any fail-closed bit the step's kernels set
         (the per-call check sees the bits of earlier calls only)."""
         self._status.check()
+
+    def run_device(self, x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """One token from the device row `x` into the device row `out` (both
+        BF16, contiguous, ``hidden`` values, 16-byte aligned): the router reads
+        `x` and the decode writes `out` directly, one library call."""
+        self._check_bound()
+        self._status.raise_pending()
+        d = self._ddesc
+        d.x = x.data_ptr()
+        d.out = out.data_ptr()
+        N.check(self._lib.glm53_decode_step_host(self._pddesc, None, None, N.stream(x.device)),
+                "glm53_decode_step_host")
+        if _SYNC_STATUS:
+            self._status.check()
+        return out
+
+    @staticmethod
+    def device_row_ok(t: torch.Tensor, H: int) -> bool:
+        return (t.is_cuda and t.dtype == torch.bfloat16 and t.is_contiguous() and t.numel() == H and
+                t.data_ptr() % 16 == 0)
 
     @staticmethod
     def supported(module) -> bool:
@@ -721,6 +747,16 @@ class PackedFP8MoE(DirectFP8MoE):
             return out
         if flat_x.is_cuda:
             self.status_word(flat_x.device).raise_pending()
+            step = self.__dict__.get("_device_step")
+            if step is not None and not step.bound_ok():  # the layer's weights were replaced: rebind
+                step = self.__dict__["_device_step"] = None
+            if step is None and PackedDecodeStep.device_row_ok(flat_x, self.bank.hidden_size) and \
+                    PackedDecodeStep.supported(self):
+                step = self.__dict__["_device_step"] = PackedDecodeStep(self)
+            if step is not None and PackedDecodeStep.device_row_ok(flat_x, self.bank.hidden_size):
+                # one token, FP32 router, tensor-core shapes: router + decode in one library call
+                out = torch.empty_like(flat_x)
+                return step.run_device(flat_x, out).reshape(x.shape)
         indices, scores = self.gate(x)
         if indices.shape[-1] != DECODE_TOP_K:
             return super().forward(x)

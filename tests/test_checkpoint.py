@@ -158,7 +158,7 @@ def test_loaded_layer_decodes_on_gpu_like_the_oracle(tmp_path, oracle):
     moe = C.load_packed_moe(tmp_path, 0, cfg, device="cuda")
     for t in range(3):
         x = S.random_bf16((1, 1, H), seed=50 + t, device="cuda")
-        out = moe(x)
+        out = moe(x)  # one token: router + decode in one library call (the step's workspace)
         idx, sc = moe.gate(x)
         torch.cuda.synchronize()
         ids = idx.reshape(-1).cpu().numpy().astype(np.uint32)
@@ -166,5 +166,5 @@ def test_loaded_layer_decodes_on_gpu_like_the_oracle(tmp_path, oracle):
         hb, hs = bank_host(moe.bank), shared_host(shared_fp8_tensors(moe.shared_experts))
         ref = oracle.packed_decode_moe(bits(x.reshape(-1)), ids, scs, hb, hs, 10.0)
         cert = certify_packed_decode(bits(x.reshape(-1)), ids, scs, hb, hs, 10.0, bits(out.reshape(-1)),
-                                     moe._workspace._buffers[(x.device, "decode")])
+                                     moe._workspace._buffers[(x.device, "step_decode")])
         assert_layer_close(bits(out.reshape(-1)), ref, certificate=cert)
