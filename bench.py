@@ -473,6 +473,7 @@ def bench_b200(args, world, rank, local):
     if not args.no_prefill:
         for T in (256, 2048, 8192):
             extra[f"prefill_{T}"] = bench_prefill(layers, dev, args, T)
+            extra[f"prefill_{T}_f8"] = bench_prefill(layers, dev, args, T, "f8")
         extra["linear_config1_5"] = bench_linear(dev, args)
         extra["batched_decode"] = bench_batched(layers, dev, args)
         extra["ep_batched"] = {f"B{B}": bench_ep_batched(layers, dev, args, 1, 0, B) for B in (16, 64)}
@@ -839,9 +840,11 @@ def bench_ep_batched(layers, dev, args, world: int, rank: int, B: int) -> dict:
             "layers_rotated": len(layers), "steps_timed": reps * n_graph}
 
 
-def bench_prefill(layers, dev, args, T: int = 2048):
+def bench_prefill(layers, dev, args, T: int = 2048, mma: str = "f16"):
     """Secondary: config 3 grouped prefill at T tokens (256, 2048, 8192),
-    Zipf-skewed router bias; layers rotate so weights stream from HBM."""
+    Zipf-skewed router bias; layers rotate so weights stream from HBM.
+    mma="f8": the grouped GEMMs on the kind::f8f6f4 kernel (GLM53_FLAG_F8_MMA),
+    with the output's agreement with the kind::f16 kernel's on the same layer."""
     import torch
 
     import glm53_flash_mlx_b200 as G
@@ -857,7 +860,7 @@ def bench_prefill(layers, dev, args, T: int = 2048):
     for i in range(3):
         L = layers[i % len(layers)]
         G.router_topk(x, w, b, top_k=TOP_K, workspace=ws)
-        G.grouped_moe(x, idx, sc, L["bank"], L["shared"], limit=LIMIT, workspace=ws)
+        G.grouped_moe(x, idx, sc, L["bank"], L["shared"], limit=LIMIT, workspace=ws, mma=mma)
     torch.cuda.synchronize()
     reps = args.prefill_reps
     st, sp = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -865,7 +868,7 @@ def bench_prefill(layers, dev, args, T: int = 2048):
     for i in range(reps):
         L = layers[i % len(layers)]
         G.router_topk(x, w, b, top_k=TOP_K, workspace=ws)
-        G.grouped_moe(x, idx, sc, L["bank"], L["shared"], limit=LIMIT, workspace=ws)
+        G.grouped_moe(x, idx, sc, L["bank"], L["shared"], limit=LIMIT, workspace=ws, mma=mma)
     sp.record()
     torch.cuda.synchronize()
     ms = st.elapsed_time(sp) / reps
@@ -875,7 +878,16 @@ def bench_prefill(layers, dev, args, T: int = 2048):
     t_hbm = bytes_ / (peaks["hbm_gbs"] * 1e9)
     t_tc = flops / (peaks["bf16_tflops"] * 1e12)
     loads = torch.bincount(idx.reshape(-1).long(), minlength=n_exp)
-    return {"tokens": T, "tokens_per_s": round(T / (ms / 1e3), 1), "ms_per_layer": round(ms, 3),
+    agree = None
+    if mma == "f8":
+        L = layers[0]
+        o8 = G.grouped_moe(x, idx, sc, L["bank"], L["shared"], limit=LIMIT, workspace=ws, mma="f8").float()
+        o16 = G.grouped_moe(x, idx, sc, L["bank"], L["shared"], limit=LIMIT, workspace=ws, mma="f16").float()
+        d = (o8 - o16).abs()
+        agree = {"max_abs": float(d.max()), "cosine": float(torch.nn.functional.cosine_similarity(
+                     o8.reshape(1, -1).double(), o16.reshape(1, -1).double()).item()),
+                 "bit_identical": float((o8 == o16).float().mean())}
+    res = {"tokens": T, "tokens_per_s": round(T / (ms / 1e3), 1), "ms_per_layer": round(ms, 3),
             "touched_experts": touched, "max_routes_per_expert": int(loads.max()),
             "mean_routes_per_touched_expert": round(T * TOP_K / max(touched, 1), 1),
             "algorithmic_bytes": bytes_, "flops": flops,
@@ -883,8 +895,12 @@ def bench_prefill(layers, dev, args, T: int = 2048):
             "tensor_frac": round(t_tc / (ms / 1e3), 4),
             "roofline_frac": round(max(t_hbm, t_tc) / (ms / 1e3), 4),
             "roofline_bound": "hbm" if t_hbm >= t_tc else "tensor (bf16, measured)",
+            "mma": "kind::f8f6f4 (E4M3 weights, hi + lo E4M3 activation terms)" if mma == "f8" else "kind::f16",
             "note": "router + route plan + grouped gate/up (SwiGLU epilogue) + grouped down + shared + combine; "
-                    "tensor_frac against the measured dense BF16 peak (the MMAs run kind::f16)"}
+                    "tensor_frac against the measured dense BF16 peak"}
+    if agree is not None:
+        res["vs_f16_kernel"] = agree
+    return res
 
 
 def bench_hc(dev, args):
@@ -1150,8 +1166,11 @@ def main():
         dev = torch.device("cuda", local)
         layers = build_layers(args.layers, 1000 + 101 * rank, dev, args.experts)
         if rank == 0:
-            print(json.dumps({f"prefill_{T}": bench_prefill(layers, dev, args, T)
-                              for T in (256, 2048, 8192)}), flush=True)
+            res = {}
+            for T in (256, 2048, 8192):
+                res[f"prefill_{T}"] = bench_prefill(layers, dev, args, T)
+                res[f"prefill_{T}_f8"] = bench_prefill(layers, dev, args, T, "f8")
+            print(json.dumps(res), flush=True)
         return
     if world > 1:
         res = bench_ep(args, world, rank, local)

@@ -26,6 +26,7 @@ FLAG_E4M3_FINITE = 1
 FLAG_SHARED_ONLY = 2
 FLAG_SKIP_SHARED = 4
 FLAG_AFTER_ROUTER = 8
+FLAG_F8_MMA = 16
 
 STATUS_BAD_EXPERT = 1
 STATUS_WAIT_TIMEOUT = 2
@@ -147,6 +148,8 @@ SIGNATURES: dict[str, tuple] = {
     "glm53_status_mirror": (_int, [_vp, _vp, _vp]),
     "glm53_packed_decode_workspace_layout": (_int, [_int, _i64, _i64, _i64, _vp]),
     "glm53_grouped_moe_workspace_layout": (_int, [_i64, _int, _i64, _i64, _i64, _i64, _vp]),
+    "glm53_grouped_moe_term_layout": (_int, [_i64, _int, _i64, _i64, _i64, _i64, _vp]),
+    "glm53_e4m3_split_rows": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
     "glm53_set_wait_limit_ns": (_int, [ctypes.c_ulonglong]),
     "glm53_hc_collapse_workspace_bytes": (_sz, [_i64, _i64]),
     "glm53_hc_collapse_norm": (

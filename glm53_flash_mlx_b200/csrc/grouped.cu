@@ -561,7 +561,7 @@ constexpr int kTcTileRows = 128;
 struct MoeWorkspace {
   uint32_t *order, *inverse, *sorted_experts, *route_offsets, *tile_offsets, *tile_experts, *tile_starts,
       *tile_lengths, *counts;
-  float *sorted_scores, *xscale, *shared_xscale, *shared_partial;
+  float *sorted_scores, *xscale, *shared_xscale, *shared_partial, *hscale, *shared_hscale;
   int shared_splits;
   uint16_t *hidden, *down, *shared_hidden, *shared_out;
   __half *x16, *shared_x16;
@@ -602,6 +602,9 @@ MoeWorkspace carve(void* base, int64_t T, int top_k, int64_t E, int64_t H, int64
   // tiles at small T)
   w.shared_splits = Is > 0 && Is % 128 == 0 ? grouped_tc_splits(((T + 127) / 128) * ((H + 127) / 128), Is / 128) : 1;
   w.shared_partial = w.shared_splits > 1 ? (float*)take(grouped_tc_splitk_bytes(T, H, w.shared_splits)) : nullptr;
+  // range multipliers of the hidden rows' E4M3 terms (kind::f8f6f4 path)
+  w.hscale = (float*)take((size_t)R * 4);
+  w.shared_hscale = (float*)take((size_t)T * 4);
   w.bytes = off;
   return w;
 }
@@ -615,18 +618,30 @@ static int grouped_moe_tc(const MoeWorkspace& w, const void* x, int64_t T, int64
                           const uint8_t* down_w, const float* down_s, int64_t E, int64_t I,
                           const uint8_t* shared_gate_w, const float* shared_gate_s, const uint8_t* shared_up_w,
                           const float* shared_up_s, const uint8_t* shared_down_w, const float* shared_down_s,
-                          int64_t Is, float limit, uint16_t* out, uint32_t* status, bool finite, cudaStream_t st) {
+                          int64_t Is, float limit, uint16_t* out, uint32_t* status, bool finite, bool f8,
+                          cudaStream_t st) {
   const int64_t R = T * top_k;
+  // kind::f8f6f4 for a gate/up + down pair: finite banks whose shapes fit the
+  // kernel; the shared pair also needs an unsplit down projection
+  const bool routed_f8 = f8 && finite && grouped_f8_supported(H, I, true) && grouped_f8_supported(I, H, false);
+  const bool shared_f8 = f8 && finite && Is > 0 && grouped_f8_supported(H, Is, true) &&
+                         grouped_f8_supported(Is, H, false) && w.shared_splits == 1;
   int rc = route_plan(indices, R, E, kTcTileRows, scores, w.order, w.inverse, w.sorted_experts, w.sorted_scores,
                       w.route_offsets, w.tile_experts, w.tile_starts, w.tile_lengths, w.tile_offsets, w.counts,
                       w.counts + 1, st);
   if (rc) return rc;
-  rc = rows_to_f16((const uint16_t*)x, H, w.order, top_k, R, w.x16, w.xscale, st);
+  if (routed_f8)
+    rc = rows_to_e4m3_split((const uint16_t*)x, H, w.order, top_k, R, reinterpret_cast<uint8_t*>(w.x16), w.xscale,
+                            st);
+  else
+    rc = rows_to_f16((const uint16_t*)x, H, w.order, top_k, R, w.x16, w.xscale, st);
   if (rc) return rc;
   const int64_t hcols = H / 128, icols = I / 128;
   TcGemm gu{};
   gu.x16 = w.x16;
   gu.xscale = w.xscale;
+  gu.f8 = routed_f8;
+  gu.x8 = reinterpret_cast<const uint8_t*>(w.x16);
   gu.R = R;
   gu.K = H;
   gu.tile_experts = w.tile_experts;
@@ -654,6 +669,13 @@ static int grouped_moe_tc(const MoeWorkspace& w, const void* x, int64_t T, int64
   TcGemm dn = gu;
   dn.x16 = reinterpret_cast<const __half*>(w.hidden);
   dn.xscale = nullptr;
+  if (routed_f8) {
+    // BF16 hidden rows -> their E4M3 terms, in place
+    rc = rows_to_e4m3_split(w.hidden, I, nullptr, 1, R, reinterpret_cast<uint8_t*>(w.hidden), w.hscale, st);
+    if (rc) return rc;
+    dn.x8 = reinterpret_cast<const uint8_t*>(w.hidden);
+    dn.xscale = w.hscale;
+  }
   dn.K = I;
   dn.w = down_w;
   dn.w_up = nullptr;
@@ -671,11 +693,17 @@ static int grouped_moe_tc(const MoeWorkspace& w, const void* x, int64_t T, int64
   if (rc) return rc;
   const uint16_t* shared_ptr = nullptr;
   if (Is > 0) {
-    rc = rows_to_f16((const uint16_t*)x, H, nullptr, 1, T, w.shared_x16, w.shared_xscale, st);
+    if (shared_f8)
+      rc = rows_to_e4m3_split((const uint16_t*)x, H, nullptr, 1, T, reinterpret_cast<uint8_t*>(w.shared_x16),
+                              w.shared_xscale, st);
+    else
+      rc = rows_to_f16((const uint16_t*)x, H, nullptr, 1, T, w.shared_x16, w.shared_xscale, st);
     if (rc) return rc;
     TcGemm sg{};
     sg.x16 = w.shared_x16;
     sg.xscale = w.shared_xscale;
+    sg.f8 = shared_f8;
+    sg.x8 = reinterpret_cast<const uint8_t*>(w.shared_x16);
     sg.R = T;
     sg.K = H;
     sg.capacity = (T + kTcTileRows - 1) / kTcTileRows;
@@ -701,6 +729,13 @@ static int grouped_moe_tc(const MoeWorkspace& w, const void* x, int64_t T, int64
     TcGemm sd = sg;
     sd.x16 = reinterpret_cast<const __half*>(w.shared_hidden);
     sd.xscale = nullptr;
+    if (shared_f8) {
+      rc = rows_to_e4m3_split(w.shared_hidden, Is, nullptr, 1, T, reinterpret_cast<uint8_t*>(w.shared_hidden),
+                              w.shared_hscale, st);
+      if (rc) return rc;
+      sd.x8 = reinterpret_cast<const uint8_t*>(w.shared_hidden);
+      sd.xscale = w.shared_hscale;
+    }
     sd.K = Is;
     sd.w = shared_down_w;
     sd.w_up = nullptr;
@@ -741,6 +776,28 @@ extern "C" int glm53_grouped_moe_workspace_layout(int64_t T, int top_k, int64_t 
   return GLM53_OK;
 }
 
+extern "C" int glm53_grouped_moe_term_layout(int64_t T, int top_k, int64_t E, int64_t H, int64_t I,
+                                             int64_t I_shared, size_t* offsets) {
+  if (!offsets || T < 0 || top_k <= 0 || E <= 0 || H <= 0 || I <= 0 || I_shared < 0) {
+    set_last_error("glm53_grouped_moe_term_layout: invalid arguments");
+    return GLM53_ERR_INVALID;
+  }
+  char* const base = reinterpret_cast<char*>(256);
+  const MoeWorkspace w = carve(base, T, top_k, E, H, I, I_shared);
+  const void* parts[6] = {w.x16, w.xscale, w.hscale, w.shared_x16, w.shared_xscale, w.shared_hscale};
+  for (int i = 0; i < 6; ++i) offsets[i] = (size_t)(reinterpret_cast<const char*>(parts[i]) - base);
+  return GLM53_OK;
+}
+
+extern "C" int glm53_e4m3_split_rows(const void* x, int64_t rows, int64_t K, void* terms, float* scale,
+                                     void* stream) {
+  if (rows < 0 || K <= 0 || (rows > 0 && (!x || !terms || !scale))) {
+    set_last_error("glm53_e4m3_split_rows: invalid arguments");
+    return GLM53_ERR_INVALID;
+  }
+  return rows_to_e4m3_split((const uint16_t*)x, K, nullptr, 1, rows, (uint8_t*)terms, scale, (cudaStream_t)stream);
+}
+
 extern "C" int glm53_grouped_moe(const void* x, int64_t T, int64_t H, const uint32_t* indices, const float* scores,
                                  int top_k, const uint8_t* gate_up_w, const float* gate_up_s, const uint8_t* down_w,
                                  const float* down_s, int64_t E, int64_t I, const uint8_t* shared_gate_w,
@@ -775,7 +832,8 @@ extern "C" int glm53_grouped_moe(const void* x, int64_t T, int64_t H, const uint
       (!has_shared || ((((uintptr_t)shared_gate_w | (uintptr_t)shared_up_w | (uintptr_t)shared_down_w) & 15) == 0)))
     return grouped_moe_tc(w, x, T, H, indices, scores, top_k, gate_up_w, gate_up_s, down_w, down_s, E, I,
                           shared_gate_w, shared_gate_s, shared_up_w, shared_up_s, shared_down_w, shared_down_s,
-                          I_shared, limit, (uint16_t*)out, status, (flags & GLM53_FLAG_E4M3_FINITE) != 0, st);
+                          I_shared, limit, (uint16_t*)out, status, (flags & GLM53_FLAG_E4M3_FINITE) != 0,
+                          (flags & GLM53_FLAG_F8_MMA) != 0, st);
   int rc = route_plan(indices, R, E, BM, scores, w.order, w.inverse, w.sorted_experts, w.sorted_scores,
                       w.route_offsets, w.tile_experts, w.tile_starts, w.tile_lengths, w.tile_offsets, w.counts,
                       w.counts + 1, st);

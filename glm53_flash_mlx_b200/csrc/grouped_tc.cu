@@ -672,6 +672,341 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// FP8 tensor-core variant (tcgen05.mma kind::f8f6f4)
+// ---------------------------------------------------------------------------
+//
+// The E4M3 weight tiles feed the MMA straight from shared memory: no decode
+// warps and no A operand in TMEM.  Each activation row arrives as two E4M3
+// terms of x * 2^-e (hi = E4M3(x 2^-e), lo = E4M3(x 2^-e - hi), written by
+// split_rows_kernel), with the row maximum scaled into [128, 256).  A BF16
+// value has 8 significant bits and hi holds the top 4, so hi + lo = x 2^-e
+// exactly for every element within 2^9 of its row maximum (lo then stays a
+// normal or subnormal E4M3 multiple of 2^-9); a smaller element keeps an
+// absolute error below 2^-10 in the scaled domain.  Products of two E4M3
+// values are exact in FP32, so every 128-K block sum is a sum of exact
+// products, as in the kind::f16 kernel.
+//
+// A CTA tile is two 128-row weight sub-tiles against one activation tile of
+// up to 128 routes: SwiGLU gate rows [128 mt, +128) and the matching up rows
+// (TMEM lane r then holds the gate and the up total of hidden row 128 mt + r,
+// so the epilogue needs no exchange), or plain output rows [256 mt, +128) and
+// [256 mt + 128, +128).  Per 128-K block: 2 sub-tiles x 2 terms x 4 MMAs of
+// M128 x N x K32 into the k-block's accumulator pair; TMEM holds two pairs
+// (512 columns), so the epilogue's per-block promotion overlaps the next
+// block's MMAs.  Each activation tile serves 256 weight rows, half the
+// activation traffic per weight byte of the kind::f16 kernel.
+// Roles: warp 0 TMA producer (weight ring and activation ring, two cursors);
+// warps 1 and 2 issue the even and odd k-blocks; warps 3-18 epilogue (four
+// per TMEM lane quarter, 32 routes each).
+namespace f8 {
+constexpr int kWStages = 4;                     // weight ring: two 128x128 E4M3 sub-tiles per stage
+constexpr int kAStages = 3;                     // activation ring: hi and lo tiles of up to 128 routes
+constexpr int kDone = 4;                        // k-block completion barriers
+constexpr int kSub = kM * kKB;                  // 16 KB: one sub-tile, or one term tile of 128 routes
+constexpr int kWBytes = 2 * kSub;
+constexpr int kABytes = 2 * kSub;
+constexpr int kEpiWarps = 16;
+constexpr int kThreads = (3 + kEpiWarps) * 32;  // 608
+static_assert(kWStages == kDone, "weight stages are released by the completion barrier of the same slot");
+static_assert(kAStages < kDone, "an activation stage is released by an older completion barrier");
+
+struct __align__(8) Bars {
+  uint64_t w_full[kWStages], a_full[kAStages], kb_done[kDone], acc_empty[2], drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+constexpr size_t smem_bytes() {
+  return 1024 /* alignment slack */ + (size_t)kWStages * kWBytes + (size_t)kAStages * kABytes + sizeof(Bars);
+}
+static_assert(smem_bytes() <= 232448, "F8 tile rings exceed the shared memory of one CTA");
+
+// D[tmem] (+)= A[smem] . B[smem]^T, kind::f8f6f4 (E4M3 x E4M3, FP32 accumulation), cta_group::1.
+__device__ __forceinline__ void mma_f8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// First weight row of sub-tile `sub` of tile mt inside one expert's rows.
+template <bool SWIGLU>
+__device__ __forceinline__ int sub_row0(const TcArgs& a, int mt, int sub) {
+  return SWIGLU ? (sub ? a.u_off : 0) + kM * mt : 2 * kM * mt + sub * kM;
+}
+}  // namespace f8
+
+// Tensor maps: w and u boxes of 128 rows x 128 codes; x and x64 boxes of 128
+// and 64 routes x 128 bytes over the [R][hi K | lo K] term rows.
+template <bool SWIGLU>
+__global__ void __launch_bounds__(f8::kThreads, 1)
+    grouped_f8_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap umap,
+                      const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap xmap64, TcArgs a,
+                      int ntiles, int mtiles, int zsub) {
+  using f8::kWStages;
+  using f8::kAStages;
+  using f8::kDone;
+  using f8::kSub;
+  using f8::kWBytes;
+  using f8::kABytes;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint8_t* wring = smem;                                  // [stage][sub 2][128 rows][128 B], swizzled
+  uint8_t* aring = wring + (size_t)kWStages * kWBytes;    // [stage][term 2][routes][128 B], swizzled
+  f8::Bars* bars = reinterpret_cast<f8::Bars*>(aring + (size_t)kAStages * kABytes);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nkb = a.K / kKB;
+
+  auto bar = [&](uint64_t* p) { return smem_addr(p); };
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kWStages; ++s) mbar_init(bar(&bars->w_full[s]), 1);
+    for (int s = 0; s < kAStages; ++s) mbar_init(bar(&bars->a_full[s]), 1);
+    for (int s = 0; s < kDone; ++s) mbar_init(bar(&bars->kb_done[s]), 1);
+    for (int s = 0; s < 2; ++s) mbar_init(bar(&bars->acc_empty[s]), f8::kEpiWarps);
+    mbar_init(bar(&bars->drain), 2);  // one commit per MMA issuer
+    bars->abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&wmap)) : "memory");
+    if (SWIGLU) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&umap)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap64)) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_addr(&bars->tmem_base)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tmem_fence_before();
+  __syncthreads();
+  tmem_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  volatile int* abort_flag = &bars->abort_flag;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    // k-block g uses weight stage g % kWStages and activation stage
+    // g % kAStages; a stage is free again once the k-block that last used it
+    // (g - kWStages, g - kAStages) has completed.  Completion barrier j
+    // serves k-blocks j, j + kDone, ...: k-block p + kDone cannot complete
+    // before both cursors have seen p complete (it needs the stages they
+    // refill after p), so one parity bit identifies p.
+    if (lane == 0) {
+      struct Cursor {
+        int t, kb;
+        uint32_t g;
+        Tile tl;
+      };
+      auto first = [&](Cursor& c, int t) {
+        for (c.t = t; c.t < ntiles; c.t += gridDim.x) {
+          c.tl = tile_at<false>(a, c.t, mtiles, zsub);
+          if (c.tl.len) {
+            c.kb = c.tl.kb0;
+            return;
+          }
+        }
+      };
+      auto advance = [&](Cursor& c) {
+        ++c.g;
+        if (++c.kb == c.tl.kb1) first(c, c.t + gridDim.x);
+      };
+      auto done = [&](uint32_t p) { return mbar_try(bar(&bars->kb_done[p % kDone]), (p / kDone) & 1u); };
+      if (!a.dense) {
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+          const int d = t / (mtiles * zsub);
+          if ((t % (mtiles * zsub)) == 0 && __ldg(a.tile_lengths + d) && __ldg(a.tile_experts + d) >= (uint32_t)a.E)
+            atomicOr(a.status, kStatusBadExpert);
+          if ((t % (mtiles * zsub)) == 0 && __ldg(a.tile_lengths + d) > (uint32_t)(zsub * kN))
+            atomicOr(a.status, kStatusBadGeometry);
+        }
+      }
+      Cursor cw{0, 0, 0u, Tile{}}, ca{0, 0, 0u, Tile{}};
+      first(cw, blockIdx.x);
+      first(ca, blockIdx.x);
+      uint64_t t_idle = 0;
+      while ((cw.t < ntiles || ca.t < ntiles) && !*abort_flag) {
+        bool progress = false;
+        if (cw.t < ntiles && (cw.g < (uint32_t)kWStages || done(cw.g - kWStages))) {
+          const int s = cw.g % kWStages;
+          const uint32_t wf = bar(&bars->w_full[s]);
+          mbar_expect_tx(wf, kWBytes);
+          uint8_t* ws = wring + (size_t)s * kWBytes;
+          tma_load_2d(smem_addr(ws), &wmap, cw.kb * kKB,
+                      (int)cw.tl.e * a.w_rows + f8::sub_row0<SWIGLU>(a, cw.tl.mt, 0), wf);
+          if (SWIGLU)
+            tma_load_2d(smem_addr(ws + kSub), &umap, cw.kb * kKB,
+                        (int)cw.tl.e * a.u_rows + f8::sub_row0<SWIGLU>(a, cw.tl.mt, 1), wf);
+          else
+            tma_load_2d(smem_addr(ws + kSub), &wmap, cw.kb * kKB,
+                        (int)cw.tl.e * a.w_rows + f8::sub_row0<SWIGLU>(a, cw.tl.mt, 1), wf);
+          advance(cw);
+          progress = true;
+        }
+        if (ca.t < ntiles && (ca.g < (uint32_t)kAStages || done(ca.g - kAStages))) {
+          const int s = ca.g % kAStages;
+          const uint32_t af = bar(&bars->a_full[s]);
+          const bool wide = ca.tl.len > 64;
+          mbar_expect_tx(af, wide ? 2 * kSub : kSub);
+          uint8_t* as = aring + (size_t)s * kABytes;
+          const CUtensorMap* xm = wide ? &xmap : &xmap64;
+          tma_load_2d(smem_addr(as), xm, ca.kb * kKB, (int)ca.tl.start, af);               // hi terms
+          tma_load_2d(smem_addr(as + kSub), xm, a.K + ca.kb * kKB, (int)ca.tl.start, af);  // lo terms
+          advance(ca);
+          progress = true;
+        }
+        if (progress) {
+          t_idle = 0;
+        } else {
+          const uint64_t now = global_ns();
+          if (t_idle == 0) {
+            t_idle = now;
+          } else if (now - t_idle > kWaitNs) {
+            *abort_flag = 1;
+          }
+        }
+      }
+      int zero = 0;
+      for (uint32_t k = cw.g > (uint32_t)kWStages ? cw.g - kWStages : 0u; k < cw.g; ++k)
+        mbar_wait(bar(&bars->w_full[k % kWStages]), (k / kWStages) & 1u, &zero);
+      for (uint32_t k = ca.g > (uint32_t)kAStages ? ca.g - kAStages : 0u; k < ca.g; ++k)
+        mbar_wait(bar(&bars->a_full[k % kAStages]), (k / kAStages) & 1u, &zero);
+    }
+  } else if (warp == 1 || warp == 2) {
+    // ---------------- MMA issuers (even / odd k-blocks) ----------------
+    if (lane == 0) {
+      const uint32_t parity = (uint32_t)(warp - 1);
+      uint32_t g = 0;
+      bool stop = false;
+      for (int t = blockIdx.x; t < ntiles && !stop; t += gridDim.x) {
+        const Tile tl = tile_at<false>(a, t, mtiles, zsub);
+        if (tl.len == 0) continue;
+        // E4M3 A and B: format code 0 in both fields, as F16 is for kind::f16
+        const uint32_t idesc = tl.len > 64 ? make_idesc(kM, kN) : make_idesc(kM, 64);
+        for (int kb = tl.kb0; kb < tl.kb1; ++kb, ++g) {
+          if ((g & 1u) != parity) continue;
+          const int ws = g % kWStages, as = g % kAStages, cb = g & 1;
+          if (!mbar_wait(bar(&bars->w_full[ws]), (g / kWStages) & 1u, abort_flag) ||
+              !mbar_wait(bar(&bars->a_full[as]), (g / kAStages) & 1u, abort_flag) ||
+              !mbar_wait(bar(&bars->acc_empty[cb]), ((g >> 1) & 1u) ^ 1u, abort_flag)) {
+            stop = true;
+            break;
+          }
+          tmem_fence_after();
+          const uint32_t w_s = smem_addr(wring + (size_t)ws * kWBytes);
+          const uint32_t a_s = smem_addr(aring + (size_t)as * kABytes);
+#pragma unroll
+          for (int sub = 0; sub < 2; ++sub) {
+            const uint32_t d_t = tmem + cb * (2 * kN) + sub * kN;
+#pragma unroll
+            for (int term = 0; term < 2; ++term) {
+#pragma unroll
+              for (int k32 = 0; k32 < kKB / 32; ++k32) {
+                const uint64_t a_desc = make_sw128_desc(w_s + sub * kSub + k32 * 32);
+                const uint64_t b_desc = make_sw128_desc(a_s + term * kSub + k32 * 32);
+                f8::mma_f8_ss(d_t, a_desc, b_desc, idesc, (term | k32) ? 1u : 0u);
+              }
+            }
+          }
+          mma_commit(bar(&bars->kb_done[g % kDone]));
+        }
+      }
+      int zero = 0;
+      mma_commit(bar(&bars->drain));
+      mbar_wait(bar(&bars->drain), 0, &zero);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue: per-block promotion, then output ----------------
+    const int q = warp & 3;         // TMEM lane quarter
+    const int h = (warp - 3) >> 2;  // routes [32 h, 32 h + 32) of the tile
+    const int r = q * 32 + lane;    // weight row of each sub-tile = TMEM lane
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    uint32_t g = 0;
+    bool stop = false;
+    for (int t = blockIdx.x; t < ntiles && !stop; t += gridDim.x) {
+      const Tile tl = tile_at<false>(a, t, mtiles, zsub);
+      if (tl.len == 0) continue;
+      const size_t sbase = (size_t)tl.e * a.s_expert;
+      const float* srow0 = a.s_gate + sbase + (size_t)(SWIGLU ? tl.mt : 2 * tl.mt) * nkb;
+      const float* srow1 = SWIGLU ? a.s_up + sbase + (size_t)tl.mt * nkb : a.s_gate + sbase + (size_t)(2 * tl.mt + 1) * nkb;
+      WarpScales sc0, sc1;
+      sc0.load(srow0, nkb, true);
+      sc1.load(srow1, nkb, true);
+      const uint32_t n0 = (uint32_t)h * 32;
+      const bool active = n0 < tl.len;
+      float t0[32], t1[32];
+#pragma unroll
+      for (int n = 0; n < 32; ++n) t0[n] = t1[n] = 0.f;
+      for (int kb = tl.kb0; kb < tl.kb1; ++kb, ++g) {
+        const int cb = g & 1;
+        if (!__all_sync(0xffffffffu, mbar_wait(bar(&bars->kb_done[g % kDone]), (g / kDone) & 1u, abort_flag))) {
+          stop = true;
+          break;
+        }
+        tmem_fence_after();
+        const float s0 = sc0.at(kb), s1 = sc1.at(kb);
+        if (active) {
+          const uint32_t acc = tmem + lane_base + cb * (2 * kN) + n0;
+          uint32_t v[16];
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            tmem_ld16(acc + c * 16, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) t0[c * 16 + i] = fmaf(s0, __uint_as_float(v[i]), t0[c * 16 + i]);
+            tmem_ld16(acc + kN + c * 16, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) t1[c * 16 + i] = fmaf(s1, __uint_as_float(v[i]), t1[c * 16 + i]);
+          }
+        }
+        tmem_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(&bars->acc_empty[cb]));
+      }
+      if (stop) break;
+      // lane l holds the range multiplier of route n0 + l
+      const float xl = (a.xscale && n0 + lane < tl.len) ? __ldg(a.xscale + tl.start + n0 + lane) : 1.0f;
+      if (SWIGLU) {
+        const int col = kM * tl.mt + r;
+#pragma unroll
+        for (int n = 0; n < 32; ++n) {
+          const float x = __shfl_sync(0xffffffffu, xl, n);
+          if (n0 + n < tl.len) {
+            // the reference's BF16 up value, then its BF16 SwiGLU; BF16 hidden rows
+            const float up = bf16_bits_to_f32(f32_to_bf16_bits(t1[n] * x));
+            a.out[(size_t)(tl.start + n0 + n) * a.out_cols + col] = swiglu_bf16_tab(t0[n] * x, up, a.limit);
+          }
+        }
+      } else {
+        const int col0 = 2 * kM * tl.mt + r, col1 = col0 + kM;
+#pragma unroll
+        for (int n = 0; n < 32; ++n) {
+          const float x = __shfl_sync(0xffffffffu, xl, n);
+          if (n0 + n < tl.len) {
+            uint16_t* orow = a.out + (size_t)(tl.start + n0 + n) * a.out_cols;
+            if (col0 < a.out_cols) orow[col0] = f32_to_bf16_bits(t0[n] * x);
+            if (col1 < a.out_cols) orow[col1] = f32_to_bf16_bits(t1[n] * x);
+          }
+        }
+      }
+    }
+  }
+
+  __syncthreads();
+  if (threadIdx.x == 0 && bars->abort_flag) atomicOr(a.status, kStatusWaitTimeout);
+  if (warp == 1) {
+    tmem_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host: tensor maps and launch
 // ---------------------------------------------------------------------------
 
@@ -776,8 +1111,83 @@ bool grouped_tc_supported(int64_t K, int64_t N, float limit, bool swiglu) {
   return true;
 }
 
+bool grouped_f8_supported(int64_t K, int64_t N, bool swiglu) {
+  // SwiGLU tiles are 128 hidden rows, plain tiles 256 output rows (no tile
+  // crosses an expert); the activation split holds a row of K <= 4096
+  return K > 0 && K % tc::kKB == 0 && K <= 16 * 256 && N > 0 && N % (swiglu ? 128 : 256) == 0;
+}
+
+static int grouped_f8(const TcGemm& g, cudaStream_t st) {
+  using namespace tc;
+  const int64_t cols = g.swiglu ? g.I : g.N;
+  if (!grouped_f8_supported(g.K, cols, g.swiglu) || !g.finite || g.splits > 1 || g.R <= 0 || g.max_rows <= 0 ||
+      !g.x8 || (((uintptr_t)g.x8 | (uintptr_t)g.w | (uintptr_t)(g.swiglu ? g.w_up : g.w)) & 15) != 0) {
+    set_last_error("grouped_f8: unsupported geometry");
+    return GLM53_ERR_INVALID;
+  }
+  if (g.capacity == 0) return GLM53_OK;
+  CUtensorMap wmap, umap, xmap, xmap64;
+  int rc = make_map(&wmap, g.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)g.K, (uint64_t)(g.E * g.w_rows), kKB, kM);
+  if (rc) return rc;
+  if (g.swiglu) {
+    rc = make_map(&umap, g.w_up, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)g.K, (uint64_t)(g.E * g.u_rows), kKB,
+                  kM);
+    if (rc) return rc;
+  } else {
+    umap = wmap;
+  }
+  // term rows [R][hi K | lo K]: the lo tile of k-block kb starts at column K + 128 kb
+  rc = make_map(&xmap, g.x8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)(2 * g.K), (uint64_t)g.R, kKB, kN);
+  if (rc) return rc;
+  rc = make_map(&xmap64, g.x8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)(2 * g.K), (uint64_t)g.R, kKB, kN / 2);
+  if (rc) return rc;
+  TcArgs a{};
+  a.tile_experts = g.tile_experts;
+  a.tile_starts = g.tile_starts;
+  a.tile_lengths = g.tile_lengths;
+  a.dense = g.dense ? 1 : 0;
+  a.R = (int)g.R;
+  a.K = (int)g.K;
+  a.E = (int)g.E;
+  a.w_rows = (int)g.w_rows;
+  a.u_rows = (int)g.u_rows;
+  a.u_off = (int)g.u_off;
+  a.s_gate = g.s_gate;
+  a.s_up = g.s_up ? g.s_up : g.s_gate;
+  a.s_expert = g.s_expert;
+  a.xscale = g.xscale;
+  a.limit = g.limit;
+  a.out_cols = (int)cols;
+  a.out = g.out;
+  a.status = g.status;
+  a.splits = 1;
+  a.partial = nullptr;
+  const int mtiles = (int)(g.swiglu ? cols / kM : cols / (2 * kM));
+  const int zsub = g.dense ? 1 : (int)((g.max_rows + kN - 1) / kN);
+  const int64_t ntiles = g.capacity * mtiles * zsub;
+  if (ntiles > INT32_MAX) {
+    set_last_error("grouped_f8: too many tiles");
+    return GLM53_ERR_INVALID;
+  }
+  const int grid = (int)std::min<int64_t>(ntiles, sm_count());
+  void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, TcArgs, int, int, int);
+  if (g.swiglu) {
+    rc = ensure_sigmoid_table(st);
+    if (rc) return rc;
+    kern = grouped_f8_kernel<true>;
+  } else {
+    kern = grouped_f8_kernel<false>;
+  }
+  const size_t smem = f8::smem_bytes();
+  rc = ensure_max_smem((const void*)kern, smem);
+  if (rc) return rc;
+  kern<<<grid, f8::kThreads, smem, st>>>(wmap, umap, xmap, xmap64, a, (int)ntiles, mtiles, zsub);
+  return check_launch("grouped_f8_kernel");
+}
+
 int grouped_tc(const TcGemm& g, cudaStream_t st) {
   using namespace tc;
+  if (g.f8) return grouped_f8(g, st);
   const int64_t cols = g.swiglu ? g.I : g.N;
   // a plain tile cut at N needs the rows past N to be out of the map (one expert)
   const bool cut_ok = g.swiglu || g.N % kM == 0 || g.E == 1;
@@ -918,6 +1328,100 @@ int rows_to_f16(const uint16_t* x, int64_t H, const uint32_t* order, int div, in
   }
   to_f16_rows_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(x, H, order, div, rows, y, scale);
   return check_launch("to_f16_rows_kernel");
+}
+
+// ---------------------------------------------------------------------------
+// Activations for the kind::f8f6f4 kernel: BF16 row x (optionally gathered
+// through the route order) -> [hi K | lo K] E4M3 terms of x * 2^-e, the row
+// maximum scaled into [128, 256), scale[r] = 2^e.  One warp per row holds the
+// whole row in registers before it writes, so y may alias x (the two term
+// rows take the bytes of the BF16 row).  A row whose maximum is infinite gets
+// scale NaN (its outputs become NaN); NaN elements stay NaN in both terms.
+// ---------------------------------------------------------------------------
+
+constexpr int kSplitChunks = 16;  // 16 x 256 elements per row at most
+
+// E4M3 pair, round to nearest even, saturating: e0 in the low byte.
+__device__ __forceinline__ uint32_t e4m3x2_rn(float e0, float e1) {
+  uint16_t d;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(d) : "f"(e1), "f"(e0));
+  return d;
+}
+
+__device__ __forceinline__ float2 e4m3x2_value(uint32_t p) {
+  uint32_t h;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"((uint16_t)p));
+  const __half2 v = *reinterpret_cast<const __half2*>(&h);
+  return __half22float2(v);
+}
+
+__global__ void split_rows_kernel(const uint16_t* x, int64_t K, const uint32_t* __restrict__ order, int div,
+                                  int64_t rows, uint8_t* y, float* __restrict__ scale) {
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int64_t src = order ? (int64_t)(__ldg(order + row) / (uint32_t)div) : row;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + src * K);
+  const int n8 = (int)(K >> 3);
+  uint4 v[kSplitChunks];
+  float m = 0.f;
+#pragma unroll
+  for (int j = 0; j < kSplitChunks; ++j) {
+    const int i = lane + 32 * j;
+    if (i < n8) {
+      v[j] = xr[i];
+      const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        m = fmaxf(m, fabsf(__uint_as_float(w[t] << 16)));
+        m = fmaxf(m, fabsf(__uint_as_float(w[t] & 0xFFFF0000u)));
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  int e = 0;
+  if (m > 0.f && m <= 3.402823466e38f) {
+    int ex;
+    frexpf(m, &ex);  // m in [2^(ex-1), 2^ex)
+    e = max(ex - 8, -126);
+  }
+  const float mul = ldexpf(1.0f, -e);
+  __syncwarp();  // every lane's row chunks are in registers before any term is written
+  uint8_t* yr = y + row * 2 * K;
+#pragma unroll
+  for (int j = 0; j < kSplitChunks; ++j) {
+    const int i = lane + 32 * j;
+    if (i < n8) {
+      const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+      uint32_t hi[2] = {0u, 0u}, lo[2] = {0u, 0u};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float f0 = __uint_as_float(w[t] << 16) * mul;
+        const float f1 = __uint_as_float(w[t] & 0xFFFF0000u) * mul;
+        const uint32_t ph = e4m3x2_rn(f0, f1);
+        const float2 hv = e4m3x2_value(ph);
+        const uint32_t pl = e4m3x2_rn(f0 - hv.x, f1 - hv.y);
+        hi[t >> 1] |= ph << (16 * (t & 1));
+        lo[t >> 1] |= pl << (16 * (t & 1));
+      }
+      *reinterpret_cast<uint2*>(yr + 8 * i) = make_uint2(hi[0], hi[1]);
+      *reinterpret_cast<uint2*>(yr + K + 8 * i) = make_uint2(lo[0], lo[1]);
+    }
+  }
+  if (lane == 0) scale[row] = m > 3.402823466e38f ? __int_as_float(0x7fc00000) : ldexpf(1.0f, e);
+}
+
+int rows_to_e4m3_split(const uint16_t* x, int64_t K, const uint32_t* order, int div, int64_t rows, uint8_t* y,
+                       float* scale, cudaStream_t st) {
+  if (rows <= 0) return GLM53_OK;
+  if (K % 8 != 0 || K > 32 * 8 * kSplitChunks || (((uintptr_t)x | (uintptr_t)y) & 15) != 0 ||
+      (order && (const void*)x == (const void*)y)) {
+    set_last_error("rows_to_e4m3_split: 16-byte aligned rows of K <= %d required", 32 * 8 * kSplitChunks);
+    return GLM53_ERR_INVALID;
+  }
+  split_rows_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(x, K, order, div, rows, y, scale);
+  return check_launch("split_rows_kernel");
 }
 
 }  // namespace glm53

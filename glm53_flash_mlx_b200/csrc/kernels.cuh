@@ -88,6 +88,11 @@ struct TcGemm {
   // second kernel (grouped_tc_splitk_bytes gives the size)
   int splits;
   float* partial;
+  // kind::f8f6f4 kernel (finite banks): x8 holds the activation rows as
+  // [R][hi K | lo K] E4M3 terms (rows_to_e4m3_split), xscale their 2^e; the
+  // SwiGLU form writes BF16 hidden rows
+  bool f8;
+  const uint8_t* x8;
 };
 
 // Split count for a plain dense GEMM of `tiles` output tiles over nkb 128-K
@@ -96,6 +101,11 @@ int grouped_tc_splits(int64_t tiles, int64_t nkb);
 size_t grouped_tc_splitk_bytes(int64_t R, int64_t N, int splits);
 
 bool grouped_tc_supported(int64_t K, int64_t N, float limit, bool swiglu);
+bool grouped_f8_supported(int64_t K, int64_t N, bool swiglu);
+// y[r] = [hi K | lo K] E4M3 terms of x[order ? order[r] / div : r] * 2^-e_r
+// (K <= 4096; y may alias x when order is null), scale[r] = 2^e_r.
+int rows_to_e4m3_split(const uint16_t* x, int64_t K, const uint32_t* order, int div, int64_t rows, uint8_t* y,
+                       float* scale, cudaStream_t st);
 int grouped_tc(const TcGemm& g, cudaStream_t stream);
 // y[r] = FP16(x[order ? order[r] / div : r] * 2^-e_r), scale[r] = 2^e_r.
 int rows_to_f16(const uint16_t* x, int64_t H, const uint32_t* order, int div, int64_t rows, __half* y, float* scale,

@@ -195,8 +195,16 @@ def restore_and_reduce(sorted_output, sorted_scores, inverse_order, shape, top_k
 
 
 def grouped_moe(x, indices, scores, bank, shared, *, limit: float, workspace: N.Workspace | None = None,
-                status: torch.Tensor | None = None):
-    """Whole grouped prefill layer from given routes (one C-ABI call)."""
+                status: torch.Tensor | None = None, mma: str = "f16"):
+    """Whole grouped prefill layer from given routes (one C-ABI call).
+
+    mma="f8" runs the grouped GEMMs on the FP8 tensor-core kernel
+    (GLM53_FLAG_F8_MMA: E4M3 weights straight into tcgen05 kind::f8f6f4,
+    activations as hi + lo E4M3 terms, exact within 2^9 of each row's
+    maximum) when the bank has no 0x7F/0xFF codes; otherwise, and with "f16",
+    the kind::f16 kernel."""
+    if mma not in ("f16", "f8"):
+        raise ValueError(f"mma must be 'f16' or 'f8', got {mma!r}")
     dev = N.require_cuda(x, indices, scores, bank.gate_up_weight)
     H = bank.hidden_size
     I = bank.intermediate_size
@@ -214,6 +222,8 @@ def grouped_moe(x, indices, scores, bank, shared, *, limit: float, workspace: N.
         sg_w = sg_s = su_w = su_s = sd_w = sd_s = None
         Is = 0
     flags = N.decode_flags(bank.gate_up_weight, bank.down_weight, *(() if shared is None else (sg_w, su_w, sd_w)))
+    if mma == "f8":
+        flags |= N.FLAG_F8_MMA
     wsp = workspace or N.Workspace()
     nbytes = N.lib().glm53_grouped_moe_workspace_bytes(T, top_k, bank.expert_count, H, I, Is)
     ws = wsp.get(dev, "grouped", nbytes)

@@ -69,6 +69,16 @@ extern "C" {
  * without the flag; ignored together with the split flags. */
 #define GLM53_FLAG_AFTER_ROUTER 8u
 
+/* `flags` bit of glm53_grouped_moe (with GLM53_FLAG_E4M3_FINITE): run the
+ * grouped GEMMs on the FP8 tensor-core kernel (tcgen05 kind::f8f6f4).  The
+ * E4M3 weights feed the MMA directly; each activation row is held as two E4M3
+ * terms hi + lo of x * 2^-e (row maximum scaled into [128, 256)), exact for
+ * every element within 2^9 of its row maximum, and the hidden rows between
+ * gate/up and down stay BF16.  Ignored without GLM53_FLAG_E4M3_FINITE or when
+ * a projection's shape does not fit the kernel (K % 128, K <= 4096; SwiGLU
+ * hidden % 128; plain outputs % 256), which then runs the kind::f16 kernel. */
+#define GLM53_FLAG_F8_MMA 16u
+
 /* Kernel ABI identity string (replaces glm53_flash_mlx/abi.py:3-15 for the
  * CUDA kernels; part of any cache identity that depends on kernel numerics). */
 const char* glm53_kernel_abi(void);
@@ -586,6 +596,28 @@ size_t glm53_grouped_moe_workspace_bytes(int64_t T, int top_k, int64_t E,
  * top_k.  For inspection (the parity tests); no reference counterpart. */
 int glm53_grouped_moe_workspace_layout(int64_t T, int top_k, int64_t E, int64_t H, int64_t I,
                                        int64_t I_shared, size_t* offsets);
+
+/* Byte offsets of the E4M3 activation terms a GLM53_FLAG_F8_MMA call of
+ * glm53_grouped_moe leaves in its workspace: offsets[0..5] = routed input
+ * terms (u8 [R][hi H | lo H], sorted order), their scales (f32 [R]), the
+ * routed hidden rows' scales (f32 [R]; the hidden terms [R][hi I | lo I]
+ * replace the hidden rows in place), the shared expert's input terms (u8
+ * [T][hi H | lo H]), their scales (f32 [T]) and its hidden rows' scales
+ * (f32 [T]; terms in place of its hidden rows).  A row's activation is
+ * (hi + lo) * scale.  For inspection (the parity tests). */
+int glm53_grouped_moe_term_layout(int64_t T, int top_k, int64_t E, int64_t H, int64_t I,
+                                  int64_t I_shared, size_t* offsets);
+
+/* The activation split of the FP8 tensor-core path (GLM53_FLAG_F8_MMA):
+ * each BF16 row x[r] ([rows, K], K % 8 == 0, K <= 4096) becomes E4M3 terms
+ * terms[r] = [hi K | lo K] of x[r] * 2^-e (e = exponent of the row maximum
+ * minus 8, at least -126; 0 for a zero row), hi = E4M3(x 2^-e),
+ * lo = E4M3(x 2^-e - hi), both round-to-nearest-even and saturating, and
+ * scale[r] = 2^e (NaN for a row with an infinite element).  terms may alias
+ * x (16-byte aligned).  No reference counterpart: the reference multiplies
+ * BF16 activations; this is the representation its FP8 tensor-core option
+ * multiplies instead. */
+int glm53_e4m3_split_rows(const void* x, int64_t rows, int64_t K, void* terms, float* scale, void* stream);
 
 /* Whole grouped prefill MoE layer given routes: route plan, grouped gate/up
  * with fused SwiGLU, grouped down, slot-ordered FP32 combine, shared expert

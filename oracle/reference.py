@@ -47,6 +47,8 @@ __all__ = [
     "direct_envelope",
     "hidden_envelope",
     "down_interval",
+    "e4m3_round",
+    "split_e4m3_rows",
 ]
 
 _HERE = Path(__file__).resolve().parent
@@ -709,3 +711,36 @@ def down_interval(hidden_f32, ids, down_w, down_s, *, depth: int | None = None, 
             raise IndexError("expert id out of range")
         assert rc == 0
     return lo, hi
+
+
+def e4m3_round(a) -> np.ndarray:
+    """Nearest E4M3 value of each FP32 value (ties to even, saturating at
+    +-448, NaN kept): the conversion the kind::f8f6f4 activation split uses
+    (PTX cvt.rn.satfinite.e4m3x2.f32).  E4M3 has 3 fraction bits, normals
+    from 2^-6, subnormals spaced 2^-9."""
+    a = np.asarray(a, dtype=np.float64)
+    m = np.abs(a)
+    e = np.floor(np.log2(np.maximum(m, 2.0 ** -6)))
+    q = np.exp2(e - 3)
+    r = np.minimum(np.rint(m / q) * q, 448.0)
+    return np.copysign(r, a).astype(np.float32)
+
+
+def split_e4m3_rows(x_bits):
+    """hi, lo (FP32 values of E4M3 codes, [R, K]) and scale ([R]) of the
+    activation split of the kind::f8f6f4 path: e = frexp(max |x|) - 8
+    (at least -126; 0 for an all-zero row) puts the row maximum in
+    [128, 256); hi = E4M3(x 2^-e), lo = E4M3(x 2^-e - hi), scale = 2^e.
+    (hi + lo) * scale is the activation the tensor cores multiply; it equals
+    x for every element within 2^9 of the row maximum."""
+    x = f32_from_bf16(np.asarray(x_bits, dtype=np.uint16)).astype(np.float32)
+    x = x.reshape(-1, x.shape[-1]) if x.ndim > 1 else x.reshape(1, -1)
+    m = np.abs(x).max(axis=1) if x.size else np.zeros(x.shape[0], np.float32)
+    ex = np.frexp(m)[1].astype(np.int64)
+    e = np.where((m > 0) & np.isfinite(m), np.maximum(ex - 8, -126), 0)
+    xs = (x * np.ldexp(np.float32(1.0), -e)[:, None].astype(np.float32)).astype(np.float32)
+    hi = e4m3_round(xs)
+    lo = e4m3_round((xs - hi).astype(np.float32))
+    scale = np.ldexp(np.float32(1.0), e).astype(np.float32)
+    scale = np.where(np.isinf(m), np.float32(np.nan), scale).astype(np.float32)
+    return hi, lo, scale

@@ -394,3 +394,174 @@ def router_logit_check(gpu_logits, ref64, x_bits, weight) -> dict:
         f"{float((err / np.maximum(np.abs(r), 1e-300)).max())}")
     return {"logits": int(g.size), "beyond_1e-6_relative_within_bound": int((~rel_ok).sum()),
             "max_rel": float((err / np.maximum(np.abs(r), 1e-30)).max())}
+
+
+# ---------------------------------------------------------------------------
+# FP8 tensor-core path (GLM53_FLAG_F8_MMA): activations as E4M3 term pairs
+# ---------------------------------------------------------------------------
+
+
+def term_rows(workspace: torch.Tensor, offset: int, rows, K: int):
+    """hi, lo (FP32 values) of the E4M3 term rows [.., 2K bytes] at a byte
+    offset of a device workspace, rows selected by index."""
+    import oracle as O
+
+    rows = np.asarray(rows, dtype=np.int64)
+    n = int(rows.max()) + 1 if rows.size else 0
+    buf = workspace[offset:offset + n * 2 * K].view(torch.uint8).reshape(n, 2 * K)
+    t = buf.index_select(0, torch.from_numpy(rows).to(workspace.device)).cpu().numpy()
+    tab = O.e4m3_table()
+    return tab[t[:, :K]].astype(np.float32), tab[t[:, K:]].astype(np.float32)
+
+
+def split_value(v, scale) -> np.ndarray:
+    """The activation the FP8 kernel multiplies for value v of a row whose
+    split scale is `scale`: (E4M3(v/s) + E4M3(v/s - E4M3(v/s))) * s.  Monotone
+    in v, so it maps an envelope [lo, hi] onto [split(lo), split(hi)]."""
+    import oracle as O
+
+    s = np.asarray(scale, dtype=np.float32)
+    vs = (np.asarray(v, dtype=np.float32) / s).astype(np.float32)
+    hi = O.e4m3_round(vs)
+    lo = O.e4m3_round((vs - hi).astype(np.float32))
+    return ((hi.astype(np.float64) + lo) * s).astype(np.float32)
+
+
+def _check_terms(hi, lo, scale, x_rows_bits, what: str) -> np.ndarray:
+    """Kernel term rows against the oracle's split of the same BF16 rows,
+    value for value; returns the represented rows as BF16 bits."""
+    import oracle as O
+
+    ohi, olo, osc = O.split_e4m3_rows(x_rows_bits)
+    assert np.array_equal(scale, osc), f"{what}: split scales differ from the oracle's"
+    assert np.array_equal(hi, ohi) and np.array_equal(lo, olo), f"{what}: E4M3 terms differ from the oracle's split"
+    rep = ((hi.astype(np.float64) + lo) * scale[:, None]).astype(np.float32)
+    rep_bits = O.bf16_from_f32(rep)
+    assert np.array_equal(f32(rep_bits), rep), f"{what}: a represented activation is not a BF16 value"
+    return rep_bits
+
+
+def _certify_f8_rows(x_rep_bits, ids, bank, limit, h_hi, h_lo, h_scale, down_bits) -> dict:
+    """Hidden terms and BF16 down rows of one F8 gate/up + down pair.
+
+    The kernel's BF16 hidden value h (replaced in place by its terms) must lie
+    in the hidden envelope of the represented input; its terms are the split
+    of h at the row's scale, so (hi + lo) * scale lies in
+    [split(env lo), split(env hi)].  The row scale must be the split scale of
+    the row's largest term value (the maximum itself is exact).  The down row
+    must be a BF16 rounding of an FP32 evaluation of the down projection of the
+    represented hidden row."""
+    import oracle as O
+
+    e_lo, e_hi = O.hidden_envelope(x_rep_bits, ids, bank, limit)
+    rep = ((h_hi.astype(np.float64) + h_lo) * h_scale[:, None]).astype(np.float32)
+    m = np.abs(rep).max(axis=1)
+    ex = np.frexp(m)[1]
+    want = np.where(m > 0, np.ldexp(np.float32(1.0), np.maximum(ex - 8, -126)), np.float32(1.0))
+    assert np.array_equal(h_scale, want.astype(np.float32)), "hidden split scales do not match the rows' maxima"
+    q_lo, q_hi = split_value(e_lo, h_scale[:, None]), split_value(e_hi, h_scale[:, None])
+    bad = (rep < q_lo) | (rep > q_hi)
+    assert not bad.any(), (f"{int(bad.sum())} hidden terms outside the split of their rounding envelope, e.g. "
+                           f"{rep[bad][:4]} vs [{q_lo[bad][:4]}, {q_hi[bad][:4]}]")
+    lo, hi = O.down_interval(rep, ids, bank[2], bank[3])
+    d = f32(down_bits)
+    d_lo, d_hi = bf16_round(_f32_down(lo)), bf16_round(_f32_up(hi))
+    ok = (d >= d_lo) & (d <= d_hi)
+    assert ok.all(), f"{int((~ok).sum())} down values outside the FP32 evaluation interval of the represented rows"
+    return {"hidden_values": int(rep.size), "hidden_envelope_two_or_more": int((e_hi > e_lo).sum()),
+            "down_values": int(d.size), "down_on_bf16_midpoint_band": int((d_lo != d_hi).sum())}
+
+
+def shared_down_splits(T: int, H: int, Is: int) -> int:
+    """Split count the grouped composition gives the shared down projection
+    (grouped_tc_splits over 128x128 output tiles); the FP8 shared pair runs
+    only unsplit."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    tiles = ((T + 127) // 128) * ((H + 127) // 128)
+    if Is <= 0 or Is % 128 or tiles * 2 > sms:
+        return 1
+    return max(1, min(sms // tiles, (Is // 128) // 4))
+
+
+def certify_grouped_f8(x_bits, indices, scores, bank, shared, limit, out_bits, workspace: torch.Tensor,
+                       tokens=None, bank_experts=None, expert_count=None) -> dict:
+    """Certificate of one GLM53_FLAG_F8_MMA glm53_grouped_moe call for the
+    listed tokens, from the intermediates it leaves in its workspace
+    (glm53_grouped_moe_workspace_layout, glm53_grouped_moe_term_layout):
+
+      1. every route's input terms and scale equal the oracle's split of its
+         token row (``oracle.split_e4m3_rows``), value for value;
+      2. hidden terms and down rows of the routed and the shared pair are
+         certified against the represented input (``_certify_f8_rows``);
+      3. each token's output is restore_and_reduce's slot-ordered combine of
+         its down rows plus its shared row, bit for bit.
+
+    The certificate proves the kernels' arithmetic on the represented
+    activations; the representation itself (exact within 2^9 of each row's
+    maximum) is counted in ``inexact_inputs`` / ``inexact_hidden``."""
+    from glm53_flash_mlx_b200 import _native as N
+
+    x = np.asarray(x_bits, dtype=np.uint16)
+    T, H = x.shape
+    idx = np.asarray(indices).reshape(T, -1).astype(np.uint32)
+    sc = np.asarray(scores, dtype=np.float32).reshape(T, -1)
+    k = idx.shape[1]
+    E = bank[0].shape[0] if expert_count is None else int(expert_count)
+    I = bank[0].shape[1] // 2
+    Is = 0 if shared is None else shared[0].shape[0]
+    R = T * k
+    offs = (ctypes.c_size_t * 8)()
+    N.check(N.lib().glm53_grouped_moe_workspace_layout(T, k, E, H, I, Is, offs), "layout")
+    toffs = (ctypes.c_size_t * 6)()
+    N.check(N.lib().glm53_grouped_moe_term_layout(T, k, E, H, I, Is, toffs), "term layout")
+    inverse = workspace_view(workspace, offs[1], np.uint32, R)
+    sorted_scores = workspace_view(workspace, offs[3], np.float32, R)
+    tok = np.arange(T) if tokens is None else np.asarray(tokens)
+    pos = inverse.reshape(T, k)[tok].reshape(-1).astype(np.int64)
+    assert np.array_equal(sorted_scores[pos], sc[tok].reshape(-1)), "sorted scores do not match the routes"
+    ids = idx[tok].reshape(-1)
+    if bank_experts is None:
+        touched, local = np.unique(ids, return_inverse=True)
+        sub = tuple(b[touched] for b in bank)
+    else:
+        be = np.asarray(bank_experts)
+        local = np.searchsorted(be, ids)
+        assert np.array_equal(be[local], ids), "bank_experts must hold every routed expert (sorted)"
+        sub = bank
+    x_rows = np.repeat(x[tok], k, 0)
+    hi, lo = term_rows(workspace, toffs[0], pos, H)
+    xs = workspace_view(workspace, toffs[1], np.float32, R)[pos]
+    x_rep = _check_terms(hi, lo, xs, x_rows, "routed input")
+    hh, hl = term_rows(workspace, offs[4], pos, I)
+    hs = workspace_view(workspace, toffs[2], np.float32, R)[pos]
+    dn_all = workspace[offs[5]:offs[5] + R * H * 2].view(torch.int16).reshape(R, H)
+    down = dn_all.index_select(0, torch.from_numpy(pos).to(workspace.device)).cpu().numpy().view(np.uint16)
+    cert = _certify_f8_rows(x_rep, local.astype(np.uint32), sub, limit, hh, hl, hs, down)
+    cert["inexact_inputs"] = int((x_rep != x_rows).sum())
+    shared_rows = None
+    if shared is not None:
+        t_t = torch.from_numpy(tok.astype(np.int64)).to(workspace.device)
+        sh_o = workspace[offs[7]:offs[7] + T * H * 2].view(torch.int16).reshape(T, H)
+        sh_out = sh_o.index_select(0, t_t).cpu().numpy().view(np.uint16)
+        if shared_down_splits(T, H, Is) == 1:
+            shi, slo = term_rows(workspace, toffs[3], tok, H)
+            ssc = workspace_view(workspace, toffs[4], np.float32, T)[tok]
+            s_rep = _check_terms(shi, slo, ssc, x[tok], "shared input")
+            sh, sl = term_rows(workspace, offs[6], tok, Is)
+            shs = workspace_view(workspace, toffs[5], np.float32, T)[tok]
+            cs = _certify_f8_rows(s_rep, np.zeros(tok.size, np.uint32), _shared_bank(shared), limit, sh, sl, shs,
+                                  sh_out)
+        else:  # a split shared down projection runs the shared pair on the kind::f16 kernels
+            sh_h = workspace[offs[6]:offs[6] + T * Is * 2].view(torch.float16).reshape(T, Is)
+            cs = certify_expert_rows(x[tok], np.zeros(tok.size, np.uint32), _shared_bank(shared), limit,
+                                     sh_h.index_select(0, t_t).float().cpu().numpy(), sh_out, down_kind="bf16",
+                                     hidden_fp16=True)
+        cert = {key: cert[key] + cs[key] if key in cs else cert[key] for key in cert}
+        shared_rows = f32(sh_out)
+    rows = f32(down).reshape(tok.size, k, H).transpose(1, 0, 2)
+    expect = slot_combine(rows, sc[tok].T, shared=shared_rows)
+    got = np.asarray(out_bits, dtype=np.uint16).reshape(T, H)[tok]
+    same = got == expect
+    assert same.all(), f"{int((~same).sum())} outputs differ from the combine of the certified intermediates"
+    cert["certified"] = True
+    return cert

@@ -10,8 +10,8 @@ import pytest
 import torch
 
 from gpu_util import (MAX_ABS, assert_layer_close, bank_host, bits, certify_by_envelope, certify_expert_rows,
-                      certify_grouped, certify_grouped_linear, certify_linear, certify_packed_decode, direct_combine,
-                      f32, from_bits, router_logit_check, shared_host)
+                      certify_grouped, certify_grouped_f8, certify_grouped_linear, certify_linear,
+                      certify_packed_decode, direct_combine, f32, from_bits, router_logit_check, shared_host)
 
 pytestmark = pytest.mark.gpu
 KATS = json.loads((Path(__file__).resolve().parent / "golden" / "reference_kats.json").read_text())
@@ -509,6 +509,98 @@ def test_grouped_moe_config3_full_size_token_subset(G, S, oracle):
     loads = np.bincount(idx_all.reshape(-1), minlength=E)
     print(f"[config3 T=2048, 256 tokens, {touched.size} experts, loads {loads[touched].min()}..{loads.max()}] "
           f"{stats} {cert}")
+
+
+@pytest.mark.parametrize("T,E,H,I,Is", [(32, 8, 256, 128, 128), (200, 64, 1024, 384, 256)])
+def test_grouped_moe_f8_matches_oracle(G, S, oracle, T, E, H, I, Is):
+    """GLM53_FLAG_F8_MMA (tcgen05 kind::f8f6f4, hi + lo E4M3 activations):
+    within the north-star bound of the oracle on the real BF16 input, with the
+    F8 certificate (terms bit-exact against the oracle's split, every
+    intermediate inside the rounding envelope of the represented problem, the
+    combine bit for bit)."""
+    from glm53_flash_mlx_b200 import _native as N
+    from glm53_flash_mlx_b200.packed import shared_fp8_tensors
+
+    bank = S.make_bank(E, H, I, seed=T, device="cuda")
+    shared = shared_fp8_tensors(S.make_shared(H, Is, seed=T + 1, device="cuda"))
+    w, b = S.make_router(E, H, seed=T + 2, device="cuda", zipf_alpha=0.5)
+    x = S.random_bf16((T, H), seed=T + 3, device="cuda")
+    idx, sc = G.router_topk(x, w, b, top_k=8)
+    ws = N.Workspace()
+    out = G.grouped_moe(x, idx, sc, bank, shared, limit=10.0, workspace=ws, mma="f8")
+    torch.cuda.synchronize()
+    assert int(ws.get(x.device, "status", 4).view(torch.int32)[0].item()) == 0
+    hb, hs = bank_host(bank), shared_host(shared)
+    ref = oracle.grouped_moe(bits(x), idx.cpu().numpy(), sc.cpu().numpy(), hb, hs, 10.0)
+    cert = certify_grouped_f8(bits(x), idx.cpu().numpy(), sc.cpu().numpy(), hb, hs, 10.0, bits(out),
+                              ws._buffers[(x.device, "grouped")])
+    stats = assert_layer_close(bits(out), ref, certificate=cert)
+    print(f"[f8 T={T} H={H} I={I}] {stats} {cert}")
+
+
+def test_grouped_moe_f8_config3_full_size_token_subset(G, S, oracle):
+    """Config 3 at T=2048 on the FP8 tensor-core kernels, checked like the
+    kind::f16 run: 256 tokens covering the most and the least loaded experts,
+    the F8 certificate and the north-star bound against the oracle."""
+    from glm53_flash_mlx_b200 import _native as N
+    from glm53_flash_mlx_b200.packed import shared_fp8_tensors
+
+    E, H, I, T = 288, 4096, 1536, 2048
+    bank = S.make_bank(E, H, I, seed=2, device="cuda")
+    shared = shared_fp8_tensors(S.make_shared(H, I, seed=3, device="cuda"))
+    w, b = S.make_router(E, H, seed=4, device="cuda", zipf_alpha=0.5)
+    x = S.random_bf16((T, H), seed=5, device="cuda")
+    idx, sc = G.router_topk(x, w, b, top_k=8)
+    ws = N.Workspace()
+    out = G.grouped_moe(x, idx, sc, bank, shared, limit=10.0, workspace=ws, mma="f8")
+    torch.cuda.synchronize()
+    assert int(ws.get(x.device, "status", 4).view(torch.int32)[0].item()) == 0
+    idx_all = idx.cpu().numpy()
+    sel = _spread_tokens(idx_all, E, 256)
+    idx_np = idx_all[sel]
+    touched = np.unique(idx_np)
+    remap = np.searchsorted(touched, idx_np).astype(np.uint32)
+    hb, hs = bank_host(bank, touched), shared_host(shared)
+    ref = oracle.grouped_moe(bits(x)[sel], remap, sc.cpu().numpy()[sel], hb, hs, 10.0)
+    cert = certify_grouped_f8(bits(x), idx_all, sc.cpu().numpy(), hb, hs, 10.0, bits(out),
+                              ws._buffers[(x.device, "grouped")], tokens=sel, bank_experts=touched, expert_count=E)
+    stats = assert_layer_close(bits(out)[sel], ref, certificate=cert)
+    print(f"[f8 config3 T=2048, 256 tokens, {touched.size} experts] {stats} {cert}")
+
+
+def test_e4m3_split_rows_matches_oracle(oracle):
+    """glm53_e4m3_split_rows: terms and scales equal the oracle's split value
+    for value (rows with tiny, zero, large and denormal-scale entries), and the
+    in-place form writes the same bytes."""
+    from glm53_flash_mlx_b200 import _native as N
+
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((64, 4096)).astype(np.float32)
+    x[0, :100] *= 1e-5
+    x[1] = 0
+    x[2, 5] = 3e4
+    x[3] *= 1e-30
+    xb = oracle.bf16_from_f32(x)
+    xt = from_bits(xb)
+    terms = torch.empty((64, 2 * 4096), dtype=torch.uint8, device="cuda")
+    scale = torch.empty(64, dtype=torch.float32, device="cuda")
+    dev = xt.device
+    N.check(N.lib().glm53_e4m3_split_rows(xt.data_ptr(), 64, 4096, terms.data_ptr(), scale.data_ptr(),
+                                          N.stream(dev)), "glm53_e4m3_split_rows")
+    torch.cuda.synchronize()
+    tab = oracle.e4m3_table()
+    t = terms.cpu().numpy()
+    hi, lo, s = oracle.split_e4m3_rows(xb)
+    assert np.array_equal(tab[t[:, :4096]], hi) and np.array_equal(tab[t[:, 4096:]], lo)
+    assert np.array_equal(scale.cpu().numpy(), s)
+    rep = (hi.astype(np.float64) + lo) * s[:, None]
+    exact = np.abs(f32(xb)) >= np.abs(f32(xb)).max(axis=1, keepdims=True) * 2.0 ** -9
+    assert np.array_equal(rep[exact], f32(xb)[exact])
+    xt2 = xt.clone()
+    N.check(N.lib().glm53_e4m3_split_rows(xt2.data_ptr(), 64, 4096, xt2.data_ptr(), scale.data_ptr(),
+                                          N.stream(dev)), "glm53_e4m3_split_rows")
+    torch.cuda.synchronize()
+    assert torch.equal(xt2.view(torch.uint8).reshape(64, -1), terms)
 
 
 def test_sorted_grouped_module_vs_direct_and_decode_fallback(G, S):

@@ -180,3 +180,39 @@ def test_swiglu_clamps(oracle, limit):
     assert abs(h[0] - expected) <= expected * 2 ** -6
     assert abs(h[1]) < 1e-3
     assert h[2] == 0.0
+
+
+def test_e4m3_round_matches_ml_dtypes_and_the_table(oracle):
+    """oracle.e4m3_round (the FP8 path's activation conversion) is the
+    round-to-nearest-even E4M3 conversion: identity on every finite table
+    value, equal to ml_dtypes' float8_e4m3fn cast inside the finite range,
+    saturating at +-448 above it."""
+    lut = oracle.e4m3_table()
+    fin = np.abs(lut) <= 448
+    assert np.array_equal(oracle.e4m3_round(lut[fin]), lut[fin])
+    rng = np.random.default_rng(7)
+    a = (rng.standard_normal(200_000) * np.exp2(rng.integers(-14, 9, 200_000))).astype(np.float32)
+    a = a[np.abs(a) < 464]
+    want = a.astype(ml_dtypes.float8_e4m3fn).astype(np.float32)
+    assert np.array_equal(oracle.e4m3_round(a), want)
+    assert oracle.e4m3_round(np.float32([500.0, -1e9]))[0] == 448.0
+    assert oracle.e4m3_round(np.float32([-1e9]))[0] == -448.0
+
+
+def test_split_e4m3_rows_is_exact_within_2e9_of_the_row_maximum(oracle):
+    """(hi + lo) * scale reproduces every BF16 element within 2^9 of its row
+    maximum, and misses a smaller one by at most 2^-10 * scale."""
+    rng = np.random.default_rng(8)
+    x = (rng.standard_normal((32, 1024)) * np.exp2(rng.integers(-20, 20, (32, 1)))).astype(np.float32)
+    x[3, :50] *= 1e-6
+    x[5] = 0
+    xb = oracle.bf16_from_f32(x)
+    xv = oracle.f32_from_bf16(xb).astype(np.float64)
+    hi, lo, s = oracle.split_e4m3_rows(xb)
+    rep = (hi.astype(np.float64) + lo) * s[:, None]
+    m = np.abs(xv).max(axis=1, keepdims=True)
+    exact = np.abs(xv) >= m * 2.0 ** -9
+    assert np.array_equal(rep[exact], xv[exact])
+    assert (np.abs(rep - xv) <= 2.0 ** -10 * s[:, None]).all()
+    assert (np.abs(hi) <= 448).all() and (np.abs(hi).max(axis=1)[m[:, 0] > 0] >= 128).all()
+    assert s[5] == 1.0 and not rep[5].any()
