@@ -73,6 +73,9 @@ def parse_args():
     p.add_argument("--prefill-only", action="store_true",
                    help="profiling aid: only the T=2048 grouped prefill measurement (prints its JSON and exits)")
     p.add_argument("--prefill-reps", type=int, default=8, help="timed grouped prefill layers")
+    p.add_argument("--prefill-tokens", default="256,2048,8192", help="--prefill-only: token counts")
+    p.add_argument("--prefill-mma", choices=["f16", "f8", "both"], default="both",
+                   help="--prefill-only: grouped GEMM kernel(s) to time")
     p.add_argument("--hc-only", action="store_true",
                    help="run only the FFN-boundary (mHC collapse + RMSNorm, hc expand) measurement")
     p.add_argument("--hc-tokens", default="1,256,2048", help="token counts of the FFN-boundary measurement")
@@ -1167,9 +1170,11 @@ def main():
         layers = build_layers(args.layers, 1000 + 101 * rank, dev, args.experts)
         if rank == 0:
             res = {}
-            for T in (256, 2048, 8192):
-                res[f"prefill_{T}"] = bench_prefill(layers, dev, args, T)
-                res[f"prefill_{T}_f8"] = bench_prefill(layers, dev, args, T, "f8")
+            for T in (int(t) for t in args.prefill_tokens.split(",")):
+                if args.prefill_mma in ("f16", "both"):
+                    res[f"prefill_{T}"] = bench_prefill(layers, dev, args, T)
+                if args.prefill_mma in ("f8", "both"):
+                    res[f"prefill_{T}_f8"] = bench_prefill(layers, dev, args, T, "f8")
             print(json.dumps(res), flush=True)
         return
     if world > 1:

@@ -591,9 +591,11 @@ MoeWorkspace carve(void* base, int64_t T, int top_k, int64_t E, int64_t H, int64
   w.tile_lengths = (uint32_t*)take(w.capacity * 4);
   w.counts = (uint32_t*)take(2 * 4);
   w.hidden = (uint16_t*)take((size_t)R * I * 2);
-  w.down = (uint16_t*)take((size_t)R * H * 2);
+  // down rows [R, H]; before the down projection the same bytes hold the
+  // gate/up rows [R][gate I | up I] (likewise for the shared expert)
+  w.down = (uint16_t*)take((size_t)R * std::max(H, 2 * I) * 2);
   w.shared_hidden = (uint16_t*)take((size_t)T * (Is > 0 ? Is : 1) * 2);
-  w.shared_out = (uint16_t*)take((size_t)T * H * 2);
+  w.shared_out = (uint16_t*)take((size_t)T * std::max(H, 2 * Is) * 2);
   w.x16 = (__half*)take((size_t)R * H * 2);
   w.xscale = (float*)take((size_t)R * 4);
   w.shared_x16 = (__half*)take((size_t)T * H * 2);
@@ -662,7 +664,7 @@ static int grouped_moe_tc(const MoeWorkspace& w, const void* x, int64_t T, int64
   gu.swiglu = true;
   gu.limit = limit;
   gu.finite = finite;
-  gu.out = w.hidden;
+  gu.out = w.down;  // [R][gate I | up I]
   gu.status = status;
   rc = grouped_tc(gu, st);
   if (rc) return rc;
@@ -670,11 +672,14 @@ static int grouped_moe_tc(const MoeWorkspace& w, const void* x, int64_t T, int64
   dn.x16 = reinterpret_cast<const __half*>(w.hidden);
   dn.xscale = nullptr;
   if (routed_f8) {
-    // BF16 hidden rows -> their E4M3 terms, in place
-    rc = rows_to_e4m3_split(w.hidden, I, nullptr, 1, R, reinterpret_cast<uint8_t*>(w.hidden), w.hscale, st);
+    // SwiGLU -> the E4M3 terms of the BF16 hidden rows
+    rc = swiglu_split(w.down, R, I, limit, reinterpret_cast<uint8_t*>(w.hidden), w.hscale, st);
     if (rc) return rc;
     dn.x8 = reinterpret_cast<const uint8_t*>(w.hidden);
     dn.xscale = w.hscale;
+  } else {
+    rc = swiglu_rows(w.down, R, I, limit, reinterpret_cast<__half*>(w.hidden), st);
+    if (rc) return rc;
   }
   dn.K = I;
   dn.w = down_w;
@@ -722,7 +727,7 @@ static int grouped_moe_tc(const MoeWorkspace& w, const void* x, int64_t T, int64
     sg.swiglu = true;
     sg.limit = limit;
     sg.finite = finite;
-    sg.out = w.shared_hidden;
+    sg.out = w.shared_out;  // [T][gate Is | up Is]
     sg.status = status;
     rc = grouped_tc(sg, st);
     if (rc) return rc;
@@ -730,11 +735,14 @@ static int grouped_moe_tc(const MoeWorkspace& w, const void* x, int64_t T, int64
     sd.x16 = reinterpret_cast<const __half*>(w.shared_hidden);
     sd.xscale = nullptr;
     if (shared_f8) {
-      rc = rows_to_e4m3_split(w.shared_hidden, Is, nullptr, 1, T, reinterpret_cast<uint8_t*>(w.shared_hidden),
-                              w.shared_hscale, st);
+      rc = swiglu_split(w.shared_out, T, Is, limit, reinterpret_cast<uint8_t*>(w.shared_hidden), w.shared_hscale,
+                        st);
       if (rc) return rc;
       sd.x8 = reinterpret_cast<const uint8_t*>(w.shared_hidden);
       sd.xscale = w.shared_hscale;
+    } else {
+      rc = swiglu_rows(w.shared_out, T, Is, limit, reinterpret_cast<__half*>(w.shared_hidden), st);
+      if (rc) return rc;
     }
     sd.K = Is;
     sd.w = shared_down_w;

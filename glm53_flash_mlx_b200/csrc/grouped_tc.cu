@@ -5,7 +5,7 @@
 //
 // One CTA computes D = W . X^T for one tile of 128 weight rows x up to 128
 // routes over the whole K, for one route descriptor (expert, first route,
-// routes <= 128).  With the SwiGLU epilogue the 128 rows are 64 gate rows
+// routes <= 128).  For the gate/up projection the 128 rows are 64 gate rows
 // stacked on the matching 64 up rows, so one M=128 MMA produces both halves
 // of 64 hidden rows.  Roles (persistent CTA, one per SM):
 //   warp 0      TMA producer: raw E4M3 weight tiles [128 rows x 128 K] and
@@ -28,16 +28,19 @@
 //               after every 128-K block, read the block's partial product
 //               from TMEM and promote it in FP32 with the 128x128 block scale
 //               (tot += s_kb * P_kb), then apply the route's activation range
-//               scale and either store BF16 rows, or hand the up rows to the
-//               gate rows' warps through shared memory and apply the
-//               reference's BF16 SwiGLU there.
+//               scale and store BF16 rows (gate/up tiles: the reference's BF16
+//               gate and up values, [R][gate I | up I]; swiglu_rows applies
+//               its BF16 SwiGLU).  The output phase is kept short: the
+//               accumulator of the next tile's third k-block waits for it
+//               (a trace put the SwiGLU epilogue formerly done here at ~17,000
+//               cycles per tile, a third of the kernel).
 // Products of FP16 weights (4 significant bits) and FP16 activations are
 // exact in FP32, so each 128-K block sum differs from the reference's FP32
 // sum only in summation order.  Activations are the BF16 inputs converted to
 // FP16 after multiplication by a power of two 2^-e per route (e chosen so the
 // row's largest magnitude stays below 2^15); the epilogue multiplies by 2^e.
-// The SwiGLU's BF16 sigmoid comes from a 64K-entry table built on the device
-// by sigmoid_bf16 itself (bit-identical, without the FP64 exponential).
+// swiglu_rows takes the BF16 sigmoid from a 64K-entry table built on the
+// device by sigmoid_bf16 itself (bit-identical, without the FP64 exponential).
 //
 // Measured tcgen05 cost on B200 (one thread issuing back-to-back M128 K16
 // kind::f16 MMAs, A from TMEM or shared memory alike): 47 cycles at N=64, 64 at
@@ -76,7 +79,6 @@ constexpr int kEpiWarps = 8;    // two per TMEM lane quarter, 64 routes each
 constexpr int kRawBytes = kM * kKB;      // 16 KB of E4M3 per stage
 constexpr int kActBox = kN * 64 * 2;     // one 64-K box of up to 128 routes (FP16)
 constexpr int kActBytes = 2 * kActBox;   // 32 KB per stage
-constexpr int kXchBytes = kN * 64 * 2;   // SwiGLU up rows handed to the gate rows: BF16 [route][64 rows]
 constexpr int kTmemCols = 512;
 // TMEM columns: accumulators [2][kN] at 0, A operands [kRing][64] at 256
 constexpr int kAccCol = 0;
@@ -270,7 +272,7 @@ __device__ __forceinline__ uint16_t swiglu_bf16_tab(float gate_total, float up_t
 // accumulator holds the block's partial product.
 struct __align__(8) Bars {
   uint64_t raw_full[kRawStages], raw_empty[kRawStages], act_full[kActStages], a_full[kRing], kb_done[kRing];
-  uint64_t acc_empty[2], xch_full, xch_empty, drain;
+  uint64_t acc_empty[2], drain;
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -278,7 +280,7 @@ struct __align__(8) Bars {
 template <bool SWIGLU>
 constexpr size_t smem_bytes() {
   return 1024 /* alignment slack */ + (size_t)kRawStages * kRawBytes + (size_t)kActStages * kActBytes +
-         (SWIGLU ? kXchBytes : 0) + sizeof(Bars);
+         sizeof(Bars);
 }
 
 // Tile t of the persistent schedule: descriptor d = t / (mtiles * zsub), then
@@ -346,8 +348,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint8_t* raw = smem;                                      // [stage][128][128] E4M3, swizzled
   uint8_t* act = raw + (size_t)kRawStages * kRawBytes;      // [stage][box 2][routes][128 B] FP16, swizzled
-  uint16_t* xch = reinterpret_cast<uint16_t*>(act + (size_t)kActStages * kActBytes);  // [route][64] BF16
-  Bars* bars = reinterpret_cast<Bars*>(reinterpret_cast<uint8_t*>(xch) + (SWIGLU ? kXchBytes : 0));
+  Bars* bars = reinterpret_cast<Bars*>(act + (size_t)kActStages * kActBytes);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nkb = a.K / kKB;
@@ -364,8 +365,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(&bars->kb_done[s]), 1);
     }
     for (int s = 0; s < 2; ++s) mbar_init(bar(&bars->acc_empty[s]), kEpiWarps);
-    mbar_init(bar(&bars->xch_full), 4);   // the four up-row warps
-    mbar_init(bar(&bars->xch_empty), 4);  // the four gate-row warps
     mbar_init(bar(&bars->drain), 2);      // one commit per MMA issuer
     bars->abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -572,7 +571,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = q * 32 + lane;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     const bool up_rows = SWIGLU && q >= 2;  // TMEM lanes 64-127 hold the up rows
-    uint32_t g = 0, tcount = 0;
+    uint32_t g = 0;
     bool stop = false;
     for (int t = blockIdx.x; t < ntiles && !stop; t += gridDim.x) {
       const Tile tl = tile_at<SPLIT>(a, t, mtiles, zsub);
@@ -583,6 +582,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       sc.load(srow, nkb, true);
       const uint32_t n0 = (uint32_t)h * 64;
       const bool active = n0 < tl.len;  // this half has routes
+      // route range multipliers of this half: lane l holds routes n0 + l and
+      // n0 + 32 + l (loaded ahead of the output phase)
+      const float xa = (a.xscale && n0 + lane < tl.len) ? __ldg(a.xscale + tl.start + n0 + lane) : 1.0f;
+      const float xb = (a.xscale && n0 + 32 + lane < tl.len) ? __ldg(a.xscale + tl.start + n0 + 32 + lane) : 1.0f;
       float tot[64];
 #pragma unroll
       for (int n = 0; n < 64; ++n) tot[n] = 0.f;
@@ -610,9 +613,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(bar(&bars->acc_empty[cb]));
       }
       if (stop) break;
-      // route range multipliers of this half: lane l holds routes n0 + l and n0 + 32 + l
-      const float xa = (a.xscale && n0 + lane < tl.len) ? __ldg(a.xscale + tl.start + n0 + lane) : 1.0f;
-      const float xb = (a.xscale && n0 + 32 + lane < tl.len) ? __ldg(a.xscale + tl.start + n0 + 32 + lane) : 1.0f;
       if (!SWIGLU && SPLIT) {
         // this range's FP32 partial sums; the reduce kernel adds the ranges in
         // order and applies the route multiplier
@@ -621,44 +621,38 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int n = 0; n < 64; ++n)
           if (n0 + n < tl.len && col < a.out_cols) dst[(size_t)(tl.start + n0 + n) * a.out_cols + col] = tot[n];
-      } else if (!SWIGLU) {
-        const int col = row0 + r;
-#pragma unroll
-        for (int n = 0; n < 64; ++n) {
-          const float x = __shfl_sync(0xffffffffu, n < 32 ? xa : xb, n & 31);
-          // the last weight tile of a plain GEMM may extend past N (TMA zero-fills those rows)
-          if (n0 + n < tl.len && col < a.out_cols)
-            a.out[(size_t)(tl.start + n0 + n) * a.out_cols + col] = f32_to_bf16_bits(tot[n] * x);
-        }
       } else {
-        const uint32_t xph = tcount & 1u;
-        if (up_rows) {
-          // up row r - 64: the reference's BF16 up value per route, [route][row]
-          if (!__all_sync(0xffffffffu, mbar_wait(bar(&bars->xch_empty), xph ^ 1u, abort_flag))) break;
-          const int u = r - 64;
+        // BF16 output rows.  Plain tiles: column row0 + r.  SwiGLU tiles write
+        // the [R, 2I] gate/up rows that swiglu_rows applies the activation to:
+        // TMEM lanes 0-63 are gate rows (columns row0 + r), lanes 64-127 the
+        // matching up rows (columns I + row0 + r - 64).
+        const int col = SWIGLU ? (r < 64 ? row0 + r : (a.out_cols >> 1) + row0 + r - 64) : row0 + r;
+        if ((reinterpret_cast<uintptr_t>(a.out) & 3u) == 0) {
+          // lane pairs exchange values so that each store writes two adjacent
+          // columns (out_cols is a multiple of 8): half the store instructions
+          // of the output phase, which the next tile's accumulators wait for
+          const uint32_t odd = lane & 1u;
+          const int colw = col - (int)odd;
 #pragma unroll
-          for (int n = 0; n < 64; ++n) {
-            const float x = __shfl_sync(0xffffffffu, n < 32 ? xa : xb, n & 31);
-            xch[(n0 + n) * 64 + u] = f32_to_bf16_bits(tot[n] * x);
+          for (int n = 0; n < 64; n += 2) {
+            const float x0 = __shfl_sync(0xffffffffu, n < 32 ? xa : xb, n & 31);
+            const float x1 = __shfl_sync(0xffffffffu, n < 32 ? xa : xb, (n + 1) & 31);
+            const uint32_t b0 = f32_to_bf16_bits(tot[n] * x0), b1 = f32_to_bf16_bits(tot[n + 1] * x1);
+            const uint32_t got = __shfl_xor_sync(0xffffffffu, odd ? b0 : b1, 1);
+            const uint32_t word = odd ? (got | (b1 << 16)) : (b0 | (got << 16));
+            const uint32_t rn = n + odd;
+            // the last weight tile of a plain GEMM may extend past N (TMA zero-fills those rows)
+            if (n0 + rn < tl.len && colw < a.out_cols)
+              *reinterpret_cast<uint32_t*>(a.out + (size_t)(tl.start + n0 + rn) * a.out_cols + colw) = word;
           }
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar(&bars->xch_full));
         } else {
-          if (!__all_sync(0xffffffffu, mbar_wait(bar(&bars->xch_full), xph, abort_flag))) break;
-          const int col = row0 + r;
 #pragma unroll
           for (int n = 0; n < 64; ++n) {
             const float x = __shfl_sync(0xffffffffu, n < 32 ? xa : xb, n & 31);
-            if (n0 + n < tl.len) {
-              const uint16_t hv = swiglu_bf16_tab(tot[n] * x, bf16_bits_to_f32(xch[(n0 + n) * 64 + r]), a.limit);
-              const __half hh = __float2half_rn(bf16_bits_to_f32(hv));
-              a.out[(size_t)(tl.start + n0 + n) * a.out_cols + col] = *reinterpret_cast<const uint16_t*>(&hh);
-            }
+            if (n0 + n < tl.len && col < a.out_cols)
+              a.out[(size_t)(tl.start + n0 + n) * a.out_cols + col] = f32_to_bf16_bits(tot[n] * x);
           }
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar(&bars->xch_empty));
         }
-        ++tcount;
       }
     }
   }
@@ -939,6 +933,8 @@ __global__ void __launch_bounds__(f8::kThreads, 1)
       sc1.load(srow1, nkb, true);
       const uint32_t n0 = (uint32_t)h * 32;
       const bool active = n0 < tl.len;
+      // lane l holds the range multiplier of route n0 + l (loaded ahead of the output phase)
+      const float xl = (a.xscale && n0 + lane < tl.len) ? __ldg(a.xscale + tl.start + n0 + lane) : 1.0f;
       float t0[32], t1[32];
 #pragma unroll
       for (int n = 0; n < 32; ++n) t0[n] = t1[n] = 0.f;
@@ -970,28 +966,29 @@ __global__ void __launch_bounds__(f8::kThreads, 1)
         if (lane == 0) mbar_arrive(bar(&bars->acc_empty[cb]));
       }
       if (stop) break;
-      // lane l holds the range multiplier of route n0 + l
-      const float xl = (a.xscale && n0 + lane < tl.len) ? __ldg(a.xscale + tl.start + n0 + lane) : 1.0f;
-      if (SWIGLU) {
-        const int col = kM * tl.mt + r;
+      // Output: BF16 rows.  The accumulator pair of the next tile's third
+      // k-block waits for this phase, so it is kept short: no activation here
+      // (gate/up tiles write the reference's BF16 gate and up values to the
+      // [R][gate I | up I] rows that swiglu_split applies the SwiGLU to), and
+      // lane pairs exchange values so that each store writes two adjacent
+      // columns.  Sub-tile 0 goes to column col0, sub-tile 1 to col0 + c1.
+      const uint32_t odd = lane & 1u;
+      {
+        const int col0 = (SWIGLU ? kM * tl.mt : 2 * kM * tl.mt) + r - (int)odd;
+        const int c1 = SWIGLU ? (a.out_cols >> 1) : kM;
 #pragma unroll
-        for (int n = 0; n < 32; ++n) {
-          const float x = __shfl_sync(0xffffffffu, xl, n);
-          if (n0 + n < tl.len) {
-            // the reference's BF16 up value, then its BF16 SwiGLU; BF16 hidden rows
-            const float up = bf16_bits_to_f32(f32_to_bf16_bits(t1[n] * x));
-            a.out[(size_t)(tl.start + n0 + n) * a.out_cols + col] = swiglu_bf16_tab(t0[n] * x, up, a.limit);
-          }
-        }
-      } else {
-        const int col0 = 2 * kM * tl.mt + r, col1 = col0 + kM;
+        for (int n = 0; n < 32; n += 2) {
+          const float x0 = __shfl_sync(0xffffffffu, xl, n), x1 = __shfl_sync(0xffffffffu, xl, n + 1);
 #pragma unroll
-        for (int n = 0; n < 32; ++n) {
-          const float x = __shfl_sync(0xffffffffu, xl, n);
-          if (n0 + n < tl.len) {
-            uint16_t* orow = a.out + (size_t)(tl.start + n0 + n) * a.out_cols;
-            if (col0 < a.out_cols) orow[col0] = f32_to_bf16_bits(t0[n] * x);
-            if (col1 < a.out_cols) orow[col1] = f32_to_bf16_bits(t1[n] * x);
+          for (int sub = 0; sub < 2; ++sub) {
+            const float* tt = sub ? t1 : t0;
+            const uint32_t b0 = f32_to_bf16_bits(tt[n] * x0), b1 = f32_to_bf16_bits(tt[n + 1] * x1);
+            const uint32_t got = __shfl_xor_sync(0xffffffffu, odd ? b0 : b1, 1);
+            const uint32_t word = odd ? (got | (b1 << 16)) : (b0 | (got << 16));
+            const uint32_t rn = n + odd;
+            const int col = col0 + sub * c1;
+            if (n0 + rn < tl.len && col < a.out_cols)
+              *reinterpret_cast<uint32_t*>(a.out + (size_t)(tl.start + n0 + rn) * a.out_cols + col) = word;
           }
         }
       }
@@ -1157,7 +1154,7 @@ static int grouped_f8(const TcGemm& g, cudaStream_t st) {
   a.s_expert = g.s_expert;
   a.xscale = g.xscale;
   a.limit = g.limit;
-  a.out_cols = (int)cols;
+  a.out_cols = (int)(g.swiglu ? 2 * cols : cols);  // gate/up tiles write [R][gate I | up I]
   a.out = g.out;
   a.status = g.status;
   a.splits = 1;
@@ -1171,13 +1168,7 @@ static int grouped_f8(const TcGemm& g, cudaStream_t st) {
   }
   const int grid = (int)std::min<int64_t>(ntiles, sm_count());
   void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, TcArgs, int, int, int);
-  if (g.swiglu) {
-    rc = ensure_sigmoid_table(st);
-    if (rc) return rc;
-    kern = grouped_f8_kernel<true>;
-  } else {
-    kern = grouped_f8_kernel<false>;
-  }
+  kern = g.swiglu ? grouped_f8_kernel<true> : grouped_f8_kernel<false>;
   const size_t smem = f8::smem_bytes();
   rc = ensure_max_smem((const void*)kern, smem);
   if (rc) return rc;
@@ -1229,7 +1220,7 @@ int grouped_tc(const TcGemm& g, cudaStream_t st) {
   a.s_expert = g.s_expert;
   a.xscale = g.xscale;
   a.limit = g.limit;
-  a.out_cols = (int)cols;
+  a.out_cols = (int)(g.swiglu ? 2 * cols : cols);  // gate/up tiles write [R][gate I | up I]
   a.out = g.out;
   a.status = g.status;
   const int splits = (g.splits > 1 && g.dense && !g.swiglu && g.partial && (cols % 4) == 0) ? g.splits : 1;
@@ -1250,8 +1241,6 @@ int grouped_tc(const TcGemm& g, cudaStream_t st) {
   void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, TcArgs, int, int, int);
   size_t smem;
   if (g.swiglu) {
-    rc = ensure_sigmoid_table(st);
-    if (rc) return rc;
     kern = g.finite ? grouped_tc_kernel<true, true, false> : grouped_tc_kernel<true, false, false>;
     smem = smem_bytes<true>();
   } else if (splits > 1) {
@@ -1355,6 +1344,42 @@ __device__ __forceinline__ float2 e4m3x2_value(uint32_t p) {
   return __half22float2(v);
 }
 
+// One warp writes the [hi K | lo K] terms of a BF16 row held as 8-element
+// chunks v[j] (lane + 32 j) with row maximum m (already reduced over the
+// warp), and the row's scale.
+__device__ __forceinline__ void write_terms(const uint4 (&v)[kSplitChunks], int n8, float m, int64_t K, uint8_t* yr,
+                                            float* scale) {
+  const int lane = threadIdx.x & 31;
+  int e = 0;
+  if (m > 0.f && m <= 3.402823466e38f) {
+    int ex;
+    frexpf(m, &ex);  // m in [2^(ex-1), 2^ex)
+    e = max(ex - 8, -126);
+  }
+  const float mul = ldexpf(1.0f, -e);
+#pragma unroll
+  for (int j = 0; j < kSplitChunks; ++j) {
+    const int i = lane + 32 * j;
+    if (i < n8) {
+      const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+      uint32_t hi[2] = {0u, 0u}, lo[2] = {0u, 0u};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float f0 = __uint_as_float(w[t] << 16) * mul;
+        const float f1 = __uint_as_float(w[t] & 0xFFFF0000u) * mul;
+        const uint32_t ph = e4m3x2_rn(f0, f1);
+        const float2 hv = e4m3x2_value(ph);
+        const uint32_t pl = e4m3x2_rn(f0 - hv.x, f1 - hv.y);
+        hi[t >> 1] |= ph << (16 * (t & 1));
+        lo[t >> 1] |= pl << (16 * (t & 1));
+      }
+      *reinterpret_cast<uint2*>(yr + 8 * i) = make_uint2(hi[0], hi[1]);
+      *reinterpret_cast<uint2*>(yr + K + 8 * i) = make_uint2(lo[0], lo[1]);
+    }
+  }
+  if (lane == 0) *scale = m > 3.402823466e38f ? __int_as_float(0x7fc00000) : ldexpf(1.0f, e);
+}
+
 __global__ void split_rows_kernel(const uint16_t* x, int64_t K, const uint32_t* __restrict__ order, int div,
                                   int64_t rows, uint8_t* y, float* __restrict__ scale) {
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -1380,36 +1405,8 @@ __global__ void split_rows_kernel(const uint16_t* x, int64_t K, const uint32_t* 
   }
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  int e = 0;
-  if (m > 0.f && m <= 3.402823466e38f) {
-    int ex;
-    frexpf(m, &ex);  // m in [2^(ex-1), 2^ex)
-    e = max(ex - 8, -126);
-  }
-  const float mul = ldexpf(1.0f, -e);
   __syncwarp();  // every lane's row chunks are in registers before any term is written
-  uint8_t* yr = y + row * 2 * K;
-#pragma unroll
-  for (int j = 0; j < kSplitChunks; ++j) {
-    const int i = lane + 32 * j;
-    if (i < n8) {
-      const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-      uint32_t hi[2] = {0u, 0u}, lo[2] = {0u, 0u};
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const float f0 = __uint_as_float(w[t] << 16) * mul;
-        const float f1 = __uint_as_float(w[t] & 0xFFFF0000u) * mul;
-        const uint32_t ph = e4m3x2_rn(f0, f1);
-        const float2 hv = e4m3x2_value(ph);
-        const uint32_t pl = e4m3x2_rn(f0 - hv.x, f1 - hv.y);
-        hi[t >> 1] |= ph << (16 * (t & 1));
-        lo[t >> 1] |= pl << (16 * (t & 1));
-      }
-      *reinterpret_cast<uint2*>(yr + 8 * i) = make_uint2(hi[0], hi[1]);
-      *reinterpret_cast<uint2*>(yr + K + 8 * i) = make_uint2(lo[0], lo[1]);
-    }
-  }
-  if (lane == 0) scale[row] = m > 3.402823466e38f ? __int_as_float(0x7fc00000) : ldexpf(1.0f, e);
+  write_terms(v, n8, m, K, y + row * 2 * K, scale + row);
 }
 
 int rows_to_e4m3_split(const uint16_t* x, int64_t K, const uint32_t* order, int div, int64_t rows, uint8_t* y,
@@ -1422,6 +1419,102 @@ int rows_to_e4m3_split(const uint16_t* x, int64_t K, const uint32_t* order, int 
   }
   split_rows_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(x, K, order, div, rows, y, scale);
   return check_launch("split_rows_kernel");
+}
+
+
+// ---------------------------------------------------------------------------
+// SwiGLU of the grouped gate/up rows [R][gate I | up I] (BF16, the reference's
+// gate and up values): the reference's BF16 SwiGLU (swiglu_bf16, sigmoid from
+// the table), as FP16 hidden rows for the kind::f16 down projection
+// (swiglu_rows) or as the E4M3 terms of the BF16 hidden rows for the
+// kind::f8f6f4 one (swiglu_split).
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ uint4 swiglu8(uint4 g, uint4 u, float limit) {
+  const uint32_t gw[4] = {g.x, g.y, g.z, g.w}, uw[4] = {u.x, u.y, u.z, u.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    const uint32_t h0 = tc::swiglu_bf16_tab(__uint_as_float(gw[t] << 16), __uint_as_float(uw[t] << 16), limit);
+    const uint32_t h1 =
+        tc::swiglu_bf16_tab(__uint_as_float(gw[t] & 0xFFFF0000u), __uint_as_float(uw[t] & 0xFFFF0000u), limit);
+    o[t] = h0 | (h1 << 16);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+__global__ void swiglu_rows_kernel(const uint16_t* __restrict__ gu, int64_t R, int64_t I, float limit,
+                                   __half* __restrict__ hidden) {
+  const int64_t n8 = I >> 3;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < R * n8; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / n8, c = i - r * n8;
+    const uint4 g = *reinterpret_cast<const uint4*>(gu + r * 2 * I + 8 * c);
+    const uint4 u = *reinterpret_cast<const uint4*>(gu + r * 2 * I + I + 8 * c);
+    const uint4 h = swiglu8(g, u, limit);
+    const uint32_t hw[4] = {h.x, h.y, h.z, h.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const __half2 hh = __floats2half2_rn(__uint_as_float(hw[t] << 16), __uint_as_float(hw[t] & 0xFFFF0000u));
+      o[t] = *reinterpret_cast<const uint32_t*>(&hh);
+    }
+    *reinterpret_cast<uint4*>(hidden + r * I + 8 * c) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+__global__ void swiglu_split_kernel(const uint16_t* __restrict__ gu, int64_t R, int64_t I, float limit,
+                                    uint8_t* __restrict__ terms, float* __restrict__ scale) {
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= R) return;
+  const uint16_t* gr = gu + row * 2 * I;
+  const int n8 = (int)(I >> 3);
+  uint4 v[kSplitChunks];
+  float m = 0.f;
+#pragma unroll
+  for (int j = 0; j < kSplitChunks; ++j) {
+    const int i = lane + 32 * j;
+    if (i < n8) {
+      v[j] = swiglu8(*reinterpret_cast<const uint4*>(gr + 8 * i), *reinterpret_cast<const uint4*>(gr + I + 8 * i),
+                     limit);
+      const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        m = fmaxf(m, fabsf(__uint_as_float(w[t] << 16)));
+        m = fmaxf(m, fabsf(__uint_as_float(w[t] & 0xFFFF0000u)));
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  write_terms(v, n8, m, I, terms + row * 2 * I, scale + row);
+}
+
+int swiglu_rows(const uint16_t* gu, int64_t R, int64_t I, float limit, __half* hidden, cudaStream_t st) {
+  if (R <= 0) return GLM53_OK;
+  if (I % 8 != 0 || (((uintptr_t)gu | (uintptr_t)hidden) & 15) != 0) {
+    set_last_error("swiglu_rows: 16-byte aligned rows required");
+    return GLM53_ERR_INVALID;
+  }
+  int rc = tc::ensure_sigmoid_table(st);
+  if (rc) return rc;
+  const int64_t n = R * (I / 8);
+  const unsigned blocks = (unsigned)std::min<int64_t>((n + 255) / 256, (int64_t)sm_count() * 16);
+  swiglu_rows_kernel<<<blocks, 256, 0, st>>>(gu, R, I, limit, hidden);
+  return check_launch("swiglu_rows_kernel");
+}
+
+int swiglu_split(const uint16_t* gu, int64_t R, int64_t I, float limit, uint8_t* terms, float* scale,
+                 cudaStream_t st) {
+  if (R <= 0) return GLM53_OK;
+  if (I % 8 != 0 || I > 32 * 8 * kSplitChunks || (((uintptr_t)gu | (uintptr_t)terms) & 15) != 0) {
+    set_last_error("swiglu_split: 16-byte aligned rows of I <= %d required", 32 * 8 * kSplitChunks);
+    return GLM53_ERR_INVALID;
+  }
+  int rc = tc::ensure_sigmoid_table(st);
+  if (rc) return rc;
+  swiglu_split_kernel<<<(unsigned)((R + 7) / 8), 256, 0, st>>>(gu, R, I, limit, terms, scale);
+  return check_launch("swiglu_split_kernel");
 }
 
 }  // namespace glm53

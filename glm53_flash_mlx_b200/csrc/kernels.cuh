@@ -77,7 +77,8 @@ struct TcGemm {
   int64_t E;
   int64_t N;              // plain output columns
   int64_t I;              // SwiGLU hidden columns
-  bool swiglu;
+  bool swiglu;            // gate/up form: out holds [R][gate I | up I] BF16 rows (the reference's
+                          // gate and up values; swiglu_rows / swiglu_split apply the activation)
   float limit;
   bool finite;            // no 0x7F/0xFF codes: hardware E4M3 conversion
   uint16_t* out;
@@ -106,6 +107,12 @@ bool grouped_f8_supported(int64_t K, int64_t N, bool swiglu);
 // (K <= 4096; y may alias x when order is null), scale[r] = 2^e_r.
 int rows_to_e4m3_split(const uint16_t* x, int64_t K, const uint32_t* order, int div, int64_t rows, uint8_t* y,
                        float* scale, cudaStream_t st);
+// The reference's BF16 SwiGLU of [R][gate I | up I] BF16 rows (a SwiGLU-form
+// grouped_tc output): FP16 hidden rows [R, I], or the E4M3 terms
+// [R][hi I | lo I] of the BF16 hidden rows and their scales (I <= 4096).
+int swiglu_rows(const uint16_t* gu, int64_t R, int64_t I, float limit, __half* hidden, cudaStream_t st);
+int swiglu_split(const uint16_t* gu, int64_t R, int64_t I, float limit, uint8_t* terms, float* scale,
+                 cudaStream_t st);
 int grouped_tc(const TcGemm& g, cudaStream_t stream);
 // y[r] = FP16(x[order ? order[r] / div : r] * 2^-e_r), scale[r] = 2^e_r.
 int rows_to_f16(const uint16_t* x, int64_t H, const uint32_t* order, int div, int64_t rows, __half* y, float* scale,

@@ -216,3 +216,4 @@ def test_split_e4m3_rows_is_exact_within_2e9_of_the_row_maximum(oracle):
     assert (np.abs(rep - xv) <= 2.0 ** -10 * s[:, None]).all()
     assert (np.abs(hi) <= 448).all() and (np.abs(hi).max(axis=1)[m[:, 0] > 0] >= 128).all()
     assert s[5] == 1.0 and not rep[5].any()
+
