@@ -560,7 +560,7 @@ constexpr int kTcTileRows = 128;
 
 struct MoeWorkspace {
   uint32_t *order, *inverse, *sorted_experts, *route_offsets, *tile_offsets, *tile_experts, *tile_starts,
-      *tile_lengths, *counts;
+      *tile_lengths, *counts, *plan_scratch;
   float *sorted_scores, *xscale, *shared_xscale, *shared_partial, *hscale, *shared_hscale;
   int shared_splits;
   uint16_t *hidden, *down, *shared_hidden, *shared_out;
@@ -607,6 +607,7 @@ MoeWorkspace carve(void* base, int64_t T, int top_k, int64_t E, int64_t H, int64
   // range multipliers of the hidden rows' E4M3 terms (kind::f8f6f4 path)
   w.hscale = (float*)take((size_t)R * 4);
   w.shared_hscale = (float*)take((size_t)T * 4);
+  w.plan_scratch = (uint32_t*)take(route_plan_scratch_bytes(R, E));
   w.bytes = off;
   return w;
 }
@@ -628,9 +629,9 @@ static int grouped_moe_tc(const MoeWorkspace& w, const void* x, int64_t T, int64
   const bool routed_f8 = f8 && finite && grouped_f8_supported(H, I, true) && grouped_f8_supported(I, H, false);
   const bool shared_f8 = f8 && finite && Is > 0 && grouped_f8_supported(H, Is, true) &&
                          grouped_f8_supported(Is, H, false) && w.shared_splits == 1;
-  int rc = route_plan(indices, R, E, kTcTileRows, scores, w.order, w.inverse, w.sorted_experts, w.sorted_scores,
-                      w.route_offsets, w.tile_experts, w.tile_starts, w.tile_lengths, w.tile_offsets, w.counts,
-                      w.counts + 1, st);
+  int rc = route_plan_chunked(indices, R, E, kTcTileRows, scores, w.order, w.inverse, w.sorted_experts,
+                              w.sorted_scores, w.route_offsets, w.tile_experts, w.tile_starts, w.tile_lengths,
+                              w.tile_offsets, w.counts, w.counts + 1, w.plan_scratch, st);
   if (rc) return rc;
   if (routed_f8)
     rc = rows_to_e4m3_split((const uint16_t*)x, H, w.order, top_k, R, reinterpret_cast<uint8_t*>(w.x16), w.xscale,

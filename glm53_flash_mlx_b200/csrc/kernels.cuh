@@ -52,6 +52,15 @@ int route_plan(const uint32_t* ids, int64_t R, int64_t E, int64_t tile_rows, con
                uint32_t* route_offsets, uint32_t* tile_experts, uint32_t* tile_starts,
                uint32_t* tile_lengths, uint32_t* tile_offsets, uint32_t* descriptor_count,
                uint32_t* invalid_count, cudaStream_t stream);
+// route_plan for long route lists, on several blocks (the same outputs):
+// scratch of route_plan_scratch_bytes(R, E); at most 4,096 routes, or without
+// scratch, it runs route_plan.
+size_t route_plan_scratch_bytes(int64_t R, int64_t E);
+int route_plan_chunked(const uint32_t* ids, int64_t R, int64_t E, int64_t tile_rows, const float* scores,
+                       uint32_t* order, uint32_t* inverse, uint32_t* sorted_experts, float* sorted_scores,
+                       uint32_t* route_offsets, uint32_t* tile_experts, uint32_t* tile_starts, uint32_t* tile_lengths,
+                       uint32_t* tile_offsets, uint32_t* descriptor_count, uint32_t* invalid_count, uint32_t* scratch,
+                       cudaStream_t stream);
 
 // tcgen05 grouped GEMM (grouped_tc.cu).  Rows of x16 (FP16, row multiplier
 // xscale) are routes; descriptors as for GroupedGemmArgs, each at most

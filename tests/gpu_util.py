@@ -565,3 +565,22 @@ def certify_grouped_f8(x_bits, indices, scores, bank, shared, limit, out_bits, w
     assert same.all(), f"{int((~same).sum())} outputs differ from the combine of the certified intermediates"
     cert["certified"] = True
     return cert
+
+
+def check_grouped_route_plan(workspace: torch.Tensor, indices, scores, E: int, H: int, I: int, Is: int) -> None:
+    """The route plan a glm53_grouped_moe call leaves in its workspace (order,
+    inverse, sorted expert ids and scores) equals the oracle's stable expert
+    sort of the same routes, element for element."""
+    import oracle as O
+    from glm53_flash_mlx_b200 import _native as N
+
+    idx = np.asarray(indices)
+    T, k = idx.shape
+    R = T * k
+    offs = (ctypes.c_size_t * 8)()
+    N.check(N.lib().glm53_grouped_moe_workspace_layout(T, k, E, H, I, Is, offs), "layout")
+    rp = O.route_plan(idx.reshape(-1).astype(np.uint32), E, np.asarray(scores, dtype=np.float32).reshape(-1))
+    for name, off, dt in (("order", 0, np.uint32), ("inverse", 1, np.uint32), ("sorted_experts", 2, np.uint32),
+                          ("sorted_scores", 3, np.float32)):
+        got = workspace_view(workspace, offs[off], dt, R)
+        assert np.array_equal(got, rp[name]), f"route plan {name} differs from the oracle's stable sort"

@@ -11,7 +11,8 @@ import torch
 
 from gpu_util import (MAX_ABS, assert_layer_close, bank_host, bits, certify_by_envelope, certify_expert_rows,
                       certify_grouped, certify_grouped_f8, certify_grouped_linear, certify_linear,
-                      certify_packed_decode, direct_combine, f32, from_bits, router_logit_check, shared_host)
+                      certify_packed_decode, check_grouped_route_plan, direct_combine, f32, from_bits,
+                      router_logit_check, shared_host)
 
 pytestmark = pytest.mark.gpu
 KATS = json.loads((Path(__file__).resolve().parent / "golden" / "reference_kats.json").read_text())
@@ -506,6 +507,8 @@ def test_grouped_moe_config3_full_size_token_subset(G, S, oracle):
     cert = certify_grouped(bits(x), idx_all, sc.cpu().numpy(), hb, hs, 10.0, bits(out),
                            ws._buffers[(x.device, "grouped")], tokens=sel, bank_experts=touched, expert_count=E)
     stats = assert_layer_close(bits(out)[sel], ref, certificate=cert)
+    # 16,384 routes: the chunked (multi-block) route plan
+    check_grouped_route_plan(ws._buffers[(x.device, "grouped")], idx_all, sc.cpu().numpy(), E, H, I, I)
     loads = np.bincount(idx_all.reshape(-1), minlength=E)
     print(f"[config3 T=2048, 256 tokens, {touched.size} experts, loads {loads[touched].min()}..{loads.max()}] "
           f"{stats} {cert}")
