@@ -18,14 +18,16 @@ namespace glm53 {
 // to 8 activation rows (blockIdx.y); K split across ksplit_for(K) warps, each
 // streaming its K range through a cp.async ring; ordered cross-warp sum.
 // Requires K % 128 == 0 and 16-byte aligned x / w rows.
-constexpr int kGemvRing = 8;
-
-template <int KS, bool FINITE>
+// Ring depth P (64-wide K slices in flight per warp): 8, or 5 when that is
+// what lets every 16-row tile run in one wave (three blocks per SM instead of
+// two): config 1 (6144 x 4096, 384 tiles) measured 8.30 -> 6.86 us per call,
+// while shapes that fit one wave at depth 8 are fastest there (4096 x 12288:
+// 12.7 us at 8, 17.0 at 5).
+template <int KS, bool FINITE, int P>
 __global__ void __launch_bounds__(32 * KS) gemv_stream_kernel(const uint16_t* __restrict__ x, int M, int K,
                                                               const uint8_t* __restrict__ w, int N,
                                                               const float* __restrict__ s, uint16_t* __restrict__ y,
                                                               int chunk) {
-  constexpr int P = kGemvRing;
   extern __shared__ __align__(16) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
   const int m0 = blockIdx.y * chunk;
@@ -60,6 +62,12 @@ __global__ void __launch_bounds__(32 * KS) gemv_stream_kernel(const uint16_t* __
   };
 #pragma unroll 1
   for (int p = 0; p < P - 1; ++p) issue();
+  // Launched as a programmatic dependent of the previous kernel on the stream:
+  // the weight slices above never depend on it, so they stream while it
+  // finishes; x is read and y written only after it has completed.  The next
+  // kernel may launch now (its CTAs take SMs as this grid's CTAs exit).
+  pdl_trigger();
+  pdl_wait();
   const float smul = decode_unscale<FINITE>() * stage_f16(xs, stride, x + (size_t)m0 * K, K, ncols, K, scratch);
   float part[4] = {0.f, 0.f, 0.f, 0.f}, tot[4] = {0.f, 0.f, 0.f, 0.f};
   // this warp's block scales of the current tile, the next tile's prefetched
@@ -126,28 +134,50 @@ __global__ void __launch_bounds__(256) fp8_linear_scalar_kernel(const uint16_t* 
   if (lane == 0) y[m * N + n] = f32_to_bf16_bits(acc);
 }
 
-static size_t gemv_smem(int KS, int chunk, int64_t K) {
-  return (size_t)KS * kGemvRing * 64 * 16 + (size_t)chunk * ((xs_stride(K) + 7) & ~7) * 2 +
+static size_t gemv_smem(int KS, int P, int chunk, int64_t K) {
+  return (size_t)KS * P * 64 * 16 + (size_t)chunk * ((xs_stride(K) + 7) & ~7) * 2 +
          (size_t)(2 * KS * 128 + 32) * sizeof(float);
+}
+
+// Blocks per SM the launch counts on: up to three (one 16-row tile per block
+// for N up to 444 * 16 rows, so no block streams two tiles while others idle).
+static int gemv_per_sm(size_t smem) { return std::max(1, std::min(3, (int)((220 * 1024) / smem))); }
+
+template <int KS, bool FINITE, int P>
+static int launch_gemv_ring(const uint16_t* x, int M, int K, const uint8_t* w, int N, const float* s, uint16_t* y,
+                            int chunk, cudaStream_t stream) {
+  const size_t smem = gemv_smem(KS, P, chunk, K);
+  int rc_attr = ensure_max_smem((const void*)gemv_stream_kernel<KS, FINITE, P>, smem);
+  if (rc_attr) return rc_attr;
+  const int ntiles = (N + 15) / 16;
+  const int chunks = (M + chunk - 1) / chunk;
+  const int per_sm = gemv_per_sm(smem);
+  const int bx = std::max(1, std::min(ntiles, (sm_count() * per_sm + chunks - 1) / chunks));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)bx, (unsigned)chunks);
+  cfg.blockDim = dim3(32 * KS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, gemv_stream_kernel<KS, FINITE, P>, x, M, K, w, N, s, y, chunk);
+  return check_launch("gemv_stream_kernel");
 }
 
 template <int KS, bool FINITE>
 static int launch_gemv_stream(const uint16_t* x, int M, int K, const uint8_t* w, int N, const float* s,
                               uint16_t* y, cudaStream_t stream) {
   int chunk = std::min(8, M);
-  while (chunk > 1 && gemv_smem(KS, chunk, K) > 200 * 1024) chunk = (chunk + 1) / 2;
-  const size_t smem = gemv_smem(KS, chunk, K);
-  int rc_attr = ensure_max_smem((const void*)gemv_stream_kernel<KS, FINITE>, smem);
-  if (rc_attr) return rc_attr;
-  const int ntiles = (N + 15) / 16;
-  const int chunks = (M + chunk - 1) / chunk;
-  // up to three blocks per SM: one 16-row tile per block for N up to
-  // 444 * 16 rows, so no block streams two tiles while others idle
-  const int per_sm = std::max(1, std::min(3, (int)((220 * 1024) / smem)));
-  const int bx = std::max(1, std::min(ntiles, (sm_count() * per_sm + chunks - 1) / chunks));
-  dim3 grid((unsigned)bx, (unsigned)chunks);
-  gemv_stream_kernel<KS, FINITE><<<grid, 32 * KS, smem, stream>>>(x, M, K, w, N, s, y, chunk);
-  return check_launch("gemv_stream_kernel");
+  while (chunk > 1 && gemv_smem(KS, 8, chunk, K) > 200 * 1024) chunk = (chunk + 1) / 2;
+  const int64_t units = (int64_t)((N + 15) / 16) * ((M + chunk - 1) / chunk);
+  const int64_t wave8 = (int64_t)sm_count() * gemv_per_sm(gemv_smem(KS, 8, chunk, K));
+  const int64_t wave5 = (int64_t)sm_count() * gemv_per_sm(gemv_smem(KS, 5, chunk, K));
+  if (units > wave8 && units <= wave5)
+    return launch_gemv_ring<KS, FINITE, 5>(x, M, K, w, N, s, y, chunk, stream);
+  return launch_gemv_ring<KS, FINITE, 8>(x, M, K, w, N, s, y, chunk, stream);
 }
 
 template <bool FINITE>
@@ -166,7 +196,7 @@ static int dispatch_gemv(const uint16_t* x, int M, int K, const uint8_t* w, int 
 int fp8_linear_small_m(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w, int64_t N,
                        const float* s, uint16_t* y, uint32_t flags, cudaStream_t stream) {
   const bool tc = (K % 128 == 0) && (((uintptr_t)w & 15) == 0) && (((uintptr_t)x & 15) == 0) &&
-                  gemv_smem(ksplit_for(K), 1, K) <= 200 * 1024 && N <= INT32_MAX - 16;
+                  gemv_smem(ksplit_for(K), 8, 1, K) <= 200 * 1024 && N <= INT32_MAX - 16;
   if (!tc) {
     int64_t warps = M * N;
     int64_t blocks = (warps + 7) / 8;
