@@ -184,22 +184,33 @@ __global__ void __launch_bounds__(256) router_small_kernel(
   __shared__ double part[8][T_MAX];
   __shared__ bool is_last;
   extern __shared__ float choice_dyn[];  // [8][E] when n_group > 1
-  // launched as a programmatic dependent of the kernel that writes x: wait
-  // for it (a no-op otherwise).  Then a dependent launched with programmatic
-  // serialisation may start; it waits (griddepcontrol.wait) before it reads
-  // this kernel's results, and may read x right away.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e = blockIdx.x;
   const float* wr = w + (size_t)e * H;
+  // The weights and the bias never depend on the previous kernel: the first
+  // kRouterPre float4 of this thread's slice of the row (all of it for
+  // H <= 4096) are in flight before the wait below.
+  constexpr int kRouterPre = 4;
+  float4 pre[kRouterPre];
+#pragma unroll
+  for (int i = 0; i < kRouterPre; ++i) {
+    const int k = 4 * threadIdx.x + 1024 * i;
+    pre[i] = k < H ? __ldcs(reinterpret_cast<const float4*>(wr + k)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   const float be = threadIdx.x < T ? __ldg(bias + e) : 0.f;
+  // launched as a programmatic dependent of the kernel that writes x: wait
+  // for it (a no-op otherwise) before reading x or writing any result.  Then
+  // a dependent launched with programmatic serialisation may start; it waits
+  // (griddepcontrol.wait) before it reads this kernel's results, and may read
+  // x right away.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   double acc[T_MAX];
 #pragma unroll
   for (int t = 0; t < T_MAX; ++t) acc[t] = 0.0;
-#pragma unroll 4
-  for (int k = 4 * threadIdx.x; k < H; k += 1024) {
-    const float4 wv = __ldcs(reinterpret_cast<const float4*>(wr + k));
+  // the products in K order: the prefetched float4 first, then the rest of
+  // the row (H > 4096)
+  auto accumulate = [&](int k, const float4 wv) {
 #pragma unroll
     for (int t = 0; t < T_MAX; ++t) {
       if (t < T) {
@@ -210,7 +221,15 @@ __global__ void __launch_bounds__(256) router_small_kernel(
         acc[t] = fma((double)__uint_as_float(raw.y & 0xFFFF0000u), (double)wv.w, acc[t]);
       }
     }
+  };
+#pragma unroll
+  for (int i = 0; i < kRouterPre; ++i) {
+    const int k = 4 * threadIdx.x + 1024 * i;
+    if (k < H) accumulate(k, pre[i]);
   }
+#pragma unroll 4
+  for (int k = 4 * threadIdx.x + 1024 * kRouterPre; k < H; k += 1024)
+    accumulate(k, __ldcs(reinterpret_cast<const float4*>(wr + k)));
 #pragma unroll
   for (int t = 0; t < T_MAX; ++t) {
     double v = acc[t];
@@ -572,6 +591,10 @@ extern "C" int glm53_router_topk(const void* x, int64_t T, int64_t H, const floa
                                  int norm_topk_prob, float routed_scaling_factor, uint32_t* indices,
                                  float* scores, float* logits, void* workspace, size_t workspace_bytes,
                                  void* stream) {
+  // the small-T kernel is always a programmatic dependent of the previous
+  // kernel: it writes nothing and reads only its weights before
+  // griddepcontrol.wait, and a previous kernel that never lets dependents
+  // launch early simply delays it to that kernel's end
   return router_topk(x, T, H, w, E, bias, top_k, n_group, topk_group, norm_topk_prob, routed_scaling_factor,
-                     indices, scores, logits, workspace, workspace_bytes, (cudaStream_t)stream, false);
+                     indices, scores, logits, workspace, workspace_bytes, (cudaStream_t)stream, true);
 }
