@@ -216,6 +216,17 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uin
       : "memory");
 }
 
+// D[tmem] (+)= A[smem] . B[smem]^T, kind::f16, cta_group::1.
+__device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
@@ -1003,6 +1014,193 @@ __global__ void __launch_bounds__(f8::kThreads, 1)
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// FP32 router logits on the tensor cores (T > 32 tokens)
+// ---------------------------------------------------------------------------
+//
+// logits[t][e] = x[t] . w[e] with x BF16 [T, H] and w FP32 [E, H].  Every FP32
+// weight is the exact sum of three BF16 numbers (planes [3][E][H], split once
+// per call), and BF16 x BF16 products are exact in FP32, so the logit is a sum
+// of exact products.  A CTA tile is 128 expert rows x 64 tokens over one
+// range of K: per 128-K block, 3 planes x 8 tcgen05.mma kind::f16 (BF16,
+// M128 x N64 x K16) accumulate into one TMEM accumulator, and the epilogue
+// adds the block's sum into a double-FP32 total (TwoSum: ~48 significant
+// bits).  A product's path thus holds at most 24 FP32 additions inside the
+// block and the exact-to-2^-48 block total; each range stores its total as
+// FP64 and router_logits_reduce adds the ranges in range order.  (The
+// mma.sync kernel it replaces for T > 32 sums 16-wide slices the same way, at
+// ~130 TFLOP/s on B200.)
+// Roles: warp 0 TMA producer (4-stage ring of 64-K stages: the three planes'
+// 128-row tiles and the token tile); warp 1 MMA issuer (and TMEM owner);
+// warps 2-17 epilogue (four per TMEM lane quarter, 16 tokens each: the
+// double-FP32 totals of 32 tokens per thread did not fit the registers).
+namespace rt {
+constexpr int kStages = 4;
+constexpr int kStageK = 64;                     // 128-byte swizzle rows of BF16
+constexpr int kTokens = 64;                     // tokens per tile (MMA N)
+constexpr int kTile = 128 * kStageK * 2;        // 16 KB: 128 expert rows x 64 K
+constexpr int kXTile = kTokens * kStageK * 2;   // 8 KB: 64 tokens x 64 K
+constexpr int kStageBytes = 3 * kTile + kXTile;
+constexpr int kEpiWarps = 16;
+constexpr int kThreads = (2 + kEpiWarps) * 32;  // 576
+constexpr int kCols = 128;                      // two accumulators of 64 tokens
+
+struct __align__(8) Bars {
+  uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2];
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+constexpr size_t smem_bytes() { return 1024 + (size_t)kStages * kStageBytes + sizeof(Bars); }
+static_assert(smem_bytes() <= 232448, "router stages exceed the shared memory of one CTA");
+}  // namespace rt
+
+// Tensor maps: wmap over the planes as [3E, H] rows (box 64 K x 128 rows;
+// rows past a plane's E belong to the next plane or are zero-filled and only
+// reach logits of experts >= E, which are not stored), xmap over [T, H].
+__global__ void __launch_bounds__(rt::kThreads, 1)
+    router_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap, int T, int H,
+                     int E, int nkb, int splits, double* __restrict__ partial, uint32_t* abort_out) {
+  using namespace rt;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  rt::Bars* bars = reinterpret_cast<rt::Bars*>(smem + (size_t)kStages * kStageBytes);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // tile: expert block ey, token block tx, K range z
+  const int z = blockIdx.x % splits;
+  const int tile = blockIdx.x / splits;
+  const int ey = tile % ((E + 127) / 128), tx = tile / ((E + 127) / 128);
+  const int e0 = ey * 128, t0 = tx * rt::kTokens;
+  // this range's 128-K blocks [kb0, kb1) and 64-K stages
+  const int kb0 = (int)((int64_t)z * nkb / splits), kb1 = (int)((int64_t)(z + 1) * nkb / splits);
+  const int nstage = 2 * (kb1 - kb0);
+  auto bar = [&](uint64_t* p) { return smem_addr(p); };
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(bar(&bars->full[s]), 1);
+      mbar_init(bar(&bars->empty[s]), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar(&bars->acc_full[s]), 1);
+      mbar_init(bar(&bars->acc_empty[s]), rt::kEpiWarps);
+    }
+    bars->abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&wmap)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_addr(&bars->tmem_base)),
+                 "r"(kCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tmem_fence_before();
+  __syncthreads();
+  tmem_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  volatile int* abort_flag = &bars->abort_flag;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int zero = 0;
+      for (int i = 0; i < nstage && !*abort_flag; ++i) {
+        const int s = i % kStages;
+        if (i >= kStages && !mbar_wait(bar(&bars->empty[s]), ((i / kStages) - 1) & 1u, abort_flag)) break;
+        const uint32_t f = bar(&bars->full[s]);
+        mbar_expect_tx(f, kStageBytes);
+        uint8_t* st = smem + (size_t)s * kStageBytes;
+        const int k = (2 * kb0 + i) * kStageK;
+#pragma unroll
+        for (int p = 0; p < 3; ++p) tma_load_2d(smem_addr(st + p * kTile), &wmap, k, p * E + e0, f);
+        tma_load_2d(smem_addr(st + 3 * kTile), &xmap, k, t0, f);  // tokens past T: zero-filled
+      }
+      // let every issued copy land before the CTA can exit
+      for (int i = nstage > kStages ? nstage - kStages : 0; i < nstage; ++i)
+        mbar_wait(bar(&bars->full[i % kStages]), (i / kStages) & 1u, &zero);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // BF16 A and B (format code 1 in both fields), FP32 accumulation
+      const uint32_t idesc = make_idesc(128, kTokens) | (1u << 7) | (1u << 10);
+      bool stop = false;
+      for (int b = 0; b < kb1 - kb0 && !stop; ++b) {
+        const int cb = b & 1;
+        if (!mbar_wait(bar(&bars->acc_empty[cb]), ((b >> 1) & 1u) ^ 1u, abort_flag)) break;
+        tmem_fence_after();
+        const uint32_t d_t = tmem + cb * kTokens;
+        for (int h = 0; h < 2; ++h) {
+          const int i = 2 * b + h, s = i % kStages;
+          if (!mbar_wait(bar(&bars->full[s]), (i / kStages) & 1u, abort_flag)) {
+            stop = true;
+            break;
+          }
+          tmem_fence_after();
+          const uint32_t st = smem_addr(smem + (size_t)s * kStageBytes);
+#pragma unroll
+          for (int p = 0; p < 3; ++p)
+#pragma unroll
+            for (int k16 = 0; k16 < kStageK / 16; ++k16)
+              mma_f16_ss(d_t, make_sw128_desc(st + p * kTile + k16 * 32),
+                             make_sw128_desc(st + 3 * kTile + k16 * 32), idesc, (h | p | k16) ? 1u : 0u);
+          mma_commit(bar(&bars->empty[s]));
+        }
+        if (!stop) mma_commit(bar(&bars->acc_full[cb]));
+      }
+    }
+    __syncwarp();
+  } else {
+    // epilogue: TMEM lane = expert row e0 + r; tokens [16 h, 16 h + 16)
+    const int q = warp & 3;
+    const int h = (warp - 2) >> 2;
+    const int r = q * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    float s_[16], c_[16];
+#pragma unroll
+    for (int n = 0; n < 16; ++n) s_[n] = c_[n] = 0.f;
+    bool ok = true;
+    for (int b = 0; b < kb1 - kb0; ++b) {
+      const int cb = b & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(bar(&bars->acc_full[cb]), (b >> 1) & 1u, abort_flag))) {
+        ok = false;
+        break;
+      }
+      tmem_fence_after();
+      uint32_t v[16];
+      tmem_ld16(tmem + lane_base + cb * kTokens + 16 * h, v);
+      tmem_wait_ld();
+#pragma unroll
+      for (int n = 0; n < 16; ++n) {  // TwoSum(s, v): s + v = t + (error, added to c)
+        const float vv = __uint_as_float(v[n]);
+        const float t = __fadd_rn(s_[n], vv);
+        const float bp = __fsub_rn(t, s_[n]);
+        const float e = __fadd_rn(__fsub_rn(s_[n], __fsub_rn(t, bp)), __fsub_rn(vv, bp));
+        c_[n] = __fadd_rn(c_[n], e);
+        s_[n] = t;
+      }
+      tmem_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(&bars->acc_empty[cb]));
+    }
+    if (ok) {
+      const int e = e0 + r;
+#pragma unroll
+      for (int n = 0; n < 16; ++n) {
+        const int t = t0 + 16 * h + n;
+        if (e < E && t < T) partial[((size_t)z * T + t) * E + e] = (double)s_[n] + (double)c_[n];
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && bars->abort_flag) atomicExch(abort_out, 1u);
+  if (warp == 1) {
+    tmem_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Host: tensor maps and launch
 // ---------------------------------------------------------------------------
@@ -1065,6 +1263,39 @@ static int ensure_sigmoid_table(cudaStream_t st) {
 }
 
 }  // namespace tc
+
+bool router_tc_supported(int64_t T, int64_t H, int64_t E) {
+  return T > 0 && T <= INT32_MAX / 2 && H > 0 && H % 128 == 0 && H <= 8192 && E > 0 && E <= 1024;
+}
+
+// K ranges per tile: about two CTAs per SM (one is resident at a time; the
+// second wave covers the first's uneven finish), at most 8.
+int router_tc_splits(int64_t T, int64_t E) {
+  const int64_t tiles = ((E + 127) / 128) * ((T + tc::rt::kTokens - 1) / tc::rt::kTokens);
+  return (int)std::max<int64_t>(1, std::min<int64_t>(8, (2 * sm_count() + tiles / 2) / tiles));
+}
+
+int router_logits_tc(const uint16_t* x, int64_t T, int64_t H, const uint16_t* planes, int64_t E, double* partial,
+                     int splits, uint32_t* abort_out, cudaStream_t st) {
+  using namespace tc;
+  if (!router_tc_supported(T, H, E) || splits < 1 || splits > (int)(H / 128) ||
+      (((uintptr_t)x | (uintptr_t)planes) & 15) != 0) {
+    set_last_error("router_logits_tc: unsupported geometry");
+    return GLM53_ERR_INVALID;
+  }
+  CUtensorMap wmap, xmap;
+  int rc = make_map(&wmap, planes, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)H, (uint64_t)(3 * E), 64, 128);
+  if (rc) return rc;
+  rc = make_map(&xmap, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)H, (uint64_t)T, 64, rt::kTokens);
+  if (rc) return rc;
+  const int64_t tiles = ((E + 127) / 128) * ((T + rt::kTokens - 1) / rt::kTokens);
+  const size_t smem = rt::smem_bytes();
+  rc = ensure_max_smem((const void*)router_tc_kernel, smem);
+  if (rc) return rc;
+  router_tc_kernel<<<(unsigned)(tiles * splits), rt::kThreads, smem, st>>>(wmap, xmap, (int)T, (int)H, (int)E,
+                                                                         (int)(H / 128), splits, partial, abort_out);
+  return check_launch("router_tc_kernel");
+}
 
 // Sum of the split-K ranges' FP32 partials in range order, times the route
 // multiplier, rounded to BF16: out[r][c] = BF16(xscale[r] * sum_ks p[ks][r][c]).

@@ -112,6 +112,13 @@ size_t grouped_tc_splitk_bytes(int64_t R, int64_t N, int splits);
 
 bool grouped_tc_supported(int64_t K, int64_t N, float limit, bool swiglu);
 bool grouped_f8_supported(int64_t K, int64_t N, bool swiglu);
+// FP32 router logits on the tensor cores: partial[z][t][e] (FP64) of x BF16
+// [T, H] against the weights' three BF16 planes [3][E][H], K split into
+// `splits` ranges; abort_out is set when a bounded wait gave up.
+bool router_tc_supported(int64_t T, int64_t H, int64_t E);
+int router_tc_splits(int64_t T, int64_t E);
+int router_logits_tc(const uint16_t* x, int64_t T, int64_t H, const uint16_t* planes, int64_t E, double* partial,
+                     int splits, uint32_t* abort_out, cudaStream_t st);
 // y[r] = [hi K | lo K] E4M3 terms of x[order ? order[r] / div : r] * 2^-e_r
 // (K <= 4096; y may alias x when order is null), scale[r] = 2^e_r.
 int rows_to_e4m3_split(const uint16_t* x, int64_t K, const uint32_t* order, int div, int64_t rows, uint8_t* y,

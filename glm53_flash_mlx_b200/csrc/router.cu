@@ -454,24 +454,49 @@ static int router_splits(int64_t T, int64_t E) {
   return s;
 }
 
+// With `aborted` set (the tensor-core logits kernel gave up on a bounded
+// wait), every slot gets the expert id E, which the MoE kernels reject.
 template <int PER>
 __global__ void __launch_bounds__(256) router_topk_kernel(const float* logits, int T,
                                                           const float* __restrict__ bias, TopkParams p,
                                                           uint32_t* __restrict__ idx,
-                                                          float* __restrict__ scores) {
+                                                          float* __restrict__ scores,
+                                                          const uint32_t* __restrict__ aborted) {
   __shared__ float choice_smem[8][kRouterMaxE];
-  const int warp = threadIdx.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + warp;
   if (t >= T) return;
+  if (aborted && *aborted) {
+    for (int j = lane; j < p.top_k; j += 32) {
+      idx[(size_t)t * p.top_k + j] = (uint32_t)p.E;
+      scores[(size_t)t * p.top_k + j] = 0.f;
+    }
+    return;
+  }
   warp_topk<PER>(logits + (size_t)t * p.E, bias, p, idx + (size_t)t * p.top_k,
                  scores + (size_t)t * p.top_k, choice_smem[warp]);
 }
 
 template <int PER>
 static int launch_topk(const float* logits, int T, const float* bias, TopkParams p, uint32_t* idx,
-                       float* scores, cudaStream_t st) {
-  router_topk_kernel<PER><<<(T + 7) / 8, 256, 0, st>>>(logits, T, bias, p, idx, scores);
+                       float* scores, cudaStream_t st, const uint32_t* aborted = nullptr) {
+  router_topk_kernel<PER><<<(T + 7) / 8, 256, 0, st>>>(logits, T, bias, p, idx, scores, aborted);
   return check_launch("router_topk_kernel");
+}
+
+// The weights' exact three-way BF16 split w = hi + mid + lo, as three planes
+// [3][E][H] for the tensor-core logits kernel.
+__global__ void __launch_bounds__(256) router_split_kernel(const float* __restrict__ w, int64_t n4,
+                                                           uint16_t* __restrict__ planes, int64_t plane) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 v = reinterpret_cast<const float4*>(w)[i];
+    uint32_t h0, m0, l0, h1, m1, l1;
+    split3_bf16x2(v.x, v.y, h0, m0, l0);
+    split3_bf16x2(v.z, v.w, h1, m1, l1);
+    reinterpret_cast<uint2*>(planes)[i] = make_uint2(h0, h1);
+    reinterpret_cast<uint2*>(planes + plane)[i] = make_uint2(m0, m1);
+    reinterpret_cast<uint2*>(planes + 2 * plane)[i] = make_uint2(l0, l1);
+  }
 }
 
 struct RouterScratch {
@@ -516,10 +541,22 @@ using namespace glm53;
 
 // Workspace: logits | sigmoids | keys (T x E each) | completion counter |
 // FP64 partial logits of the K ranges (tensor-core path, T > 32).
+// For T > 32 also: the tensor-core path's FP64 range partials (or the
+// mma.sync path's, whichever is larger), the weights' three BF16 planes (for
+// H <= 8192) and its abort word.
+static size_t router_partial_bytes(int64_t T, int64_t E) {
+  if (T <= kRouterSmallT) return 0;
+  const int s = std::max(router_splits(T, E), router_tc_splits(T, E));
+  return align_up((size_t)s * (size_t)T * (size_t)E * sizeof(double), 256);
+}
+
+static size_t router_planes_bytes(int64_t T, int64_t E) {
+  return T > kRouterSmallT ? align_up((size_t)3 * E * 8192 * 2, 256) + 256 : 0;
+}
+
 extern "C" size_t glm53_router_workspace_bytes(int64_t T, int64_t E) {
   const size_t base = 3 * align_up((size_t)std::max<int64_t>(T, 1) * (size_t)E * sizeof(float), 256) + 256;
-  const int s = T > kRouterSmallT ? router_splits(T, E) : 1;
-  return base + (s > 1 ? align_up((size_t)s * (size_t)T * (size_t)E * sizeof(double), 256) : 0);
+  return base + router_partial_bytes(T, E) + router_planes_bytes(T, E);
 }
 
 namespace glm53 {
@@ -560,10 +597,36 @@ int router_topk(const void* x, int64_t T, int64_t H, const float* w, int64_t E, 
   }
   dim3 grid((unsigned)((T + 63) / 64), (unsigned)((E + 63) / 64));
   int rc;
+  double* partial_buf = (double*)(ws + 3 * plane + 256);
+  if (router_tc_supported(T, H, E) && (((uintptr_t)x | (uintptr_t)w) & 15) == 0) {
+    // tensor cores: the weights' BF16 planes, the logits' K-range partials,
+    // their sum in range order, the top-k
+    uint16_t* planes = (uint16_t*)((char*)partial_buf + router_partial_bytes(T, E));
+    uint32_t* aborted = (uint32_t*)((char*)planes + router_planes_bytes(T, E) - 256);
+    const int64_t n4 = E * H / 4;
+    if (cudaMemsetAsync(aborted, 0, sizeof(uint32_t), st) != cudaSuccess) {
+      set_last_error("glm53_router_topk: memset failed");
+      return GLM53_ERR_CUDA;
+    }
+    router_split_kernel<<<(unsigned)std::min<int64_t>((n4 + 255) / 256, 1184), 256, 0, st>>>(w, n4, planes, E * H);
+    rc = check_launch("router_split_kernel");
+    if (rc) return rc;
+    const int splits = router_tc_splits(T, E);
+    rc = router_logits_tc((const uint16_t*)x, T, H, planes, E, partial_buf, splits, aborted, st);
+    if (rc) return rc;
+    const int64_t n = T * E;
+    router_logits_reduce<<<(unsigned)std::min<int64_t>((n + 255) / 256, 1184), 256, 0, st>>>(partial_buf, splits, n,
+                                                                                             lbuf);
+    rc = check_launch("router_logits_reduce");
+    if (rc) return rc;
+    if (per <= 4) return launch_topk<4>(lbuf, (int)T, bias, p, indices, scores, st, aborted);
+    if (per <= 10) return launch_topk<10>(lbuf, (int)T, bias, p, indices, scores, st, aborted);
+    return launch_topk<32>(lbuf, (int)T, bias, p, indices, scores, st, aborted);
+  }
   if (H % kRmBK == 0 && (((uintptr_t)x | (uintptr_t)w) & 15) == 0) {
     int splits = router_splits(T, E);
     while (splits > 1 && (H / kRmBK) % splits != 0) splits /= 2;
-    double* partial = splits > 1 ? (double*)(ws + 3 * plane + 256) : nullptr;
+    double* partial = splits > 1 ? partial_buf : nullptr;
     grid.z = (unsigned)splits;
     router_mma_kernel<<<grid, 128, 0, st>>>((const uint16_t*)x, (int)T, (int)H, w, (int)E, lbuf,
                                             (int)(H / splits), partial);
