@@ -46,14 +46,28 @@ __global__ void p2p_dispatch_kernel(const uint16_t* __restrict__ x, int H, int t
                                     EpLayout lay, float* __restrict__ slot_scores, uint32_t* __restrict__ route_pos,
                                     uint32_t* __restrict__ status) {
   __shared__ uint32_t s_route;
+  const int k = blockIdx.x, d = k / cap, s = k - d * cap;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int per_rank = E / world;
+  char* base = reinterpret_cast<char*>(peer_base[d]);
+  const size_t slot = (size_t)rank * cap + s;
+  // One token (T = 1): every slot carries row 0 whatever the routes, so it
+  // is stored before the routes are known, while the router still runs (an
+  // empty slot's row is never read).  x is final here: this grid launches
+  // only once the router has passed its own wait for the kernel that wrote
+  // x; and the owner finished reading this slot in the previous step, which
+  // this rank's previous combine waited for.
+  const bool row_first = R == top_k;
+  if (row_first) {
+    const uint4* src = reinterpret_cast<const uint4*>(x);
+    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(base + lay.recv_x) + slot * H);
+    for (int i = threadIdx.x; i < (H >> 3); i += blockDim.x) dst[i] = src[i];
+  }
   // launched as a programmatic dependent of the router: the owner decode may
   // launch at once (its routed CTAs wait for the arrivals, its shared-expert
   // CTAs for this grid), and the routes are read after the router finished
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int k = blockIdx.x, d = k / cap, s = k - d * cap;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int per_rank = E / world;
   if (warp == 0) {
     uint32_t found = kP2pEmpty, seen = 0;
     for (int c0 = 0; c0 < R && found == kP2pEmpty; c0 += 32) {
@@ -94,20 +108,23 @@ __global__ void p2p_dispatch_kernel(const uint16_t* __restrict__ x, int H, int t
   }
   __syncthreads();
   const uint32_t r = s_route;
-  char* base = reinterpret_cast<char*>(peer_base[d]);
-  const size_t slot = (size_t)rank * cap + s;
   if (threadIdx.x == 0) {
     slot_scores[k] = r == kP2pEmpty ? 0.f : scores[r];
     reinterpret_cast<uint32_t*>(base + lay.recv_e)[slot] = r == kP2pEmpty ? kP2pEmpty : ids[r] - (uint32_t)(d * per_rank);
   }
-  if (r != kP2pEmpty) {
+  if (r != kP2pEmpty && !row_first) {
     const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)(r / top_k) * H);
     uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(base + lay.recv_x) + slot * H);
     for (int i = threadIdx.x; i < (H >> 3); i += blockDim.x) dst[i] = src[i];
   }
-  __threadfence_system();
+  // release: the block barrier orders every thread's stores before thread 0's
+  // system-scope fence (cumulative), which orders them before the arrival
+  // (one fence per CTA; a fence in every thread cost more)
   __syncthreads();
-  if (threadIdx.x == 0) atomicAdd(reinterpret_cast<unsigned long long*>(base + lay.cnt_dispatch), 1ull);
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    atomicAdd(reinterpret_cast<unsigned long long*>(base + lay.cnt_dispatch), 1ull);
+  }
 }
 
 // Combine after waiting for every owner's rows of this step: each routed

@@ -367,9 +367,13 @@ __device__ __forceinline__ void decode_down_peer(const DecodeArgs& a, int jb, in
     if (!valid && lane == 0) atomicOr(a.status, kStatusBadExpert);
   }
   if (routed && e != kEmptySlot) {  // empty slots send nothing home and count nothing
-    __threadfence_system();
+    // release: the block barrier, then one cumulative system-scope fence
+    // before the arrival
     __syncthreads();
-    if (threadIdx.x == 0) atomicAdd(reinterpret_cast<unsigned long long*>(hb + a.back_cnt_off), 1ull);
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      atomicAdd(reinterpret_cast<unsigned long long*>(hb + a.back_cnt_off), 1ull);
+    }
   }
 }
 
