@@ -69,7 +69,7 @@ def parse_args():
     p.add_argument("--no-e2e", action="store_true", help="skip the module-API end-to-end pass")
     p.add_argument("--quick-linear", action="store_true", help="config-5 sweep at M in {1, 64, 512} only")
     p.add_argument("--linear-only", action="store_true", help="run only the config-1/5 block-linear sweep")
-    p.add_argument("--batched-only", action="store_true", help="run only the batched (B=16) decode measurement")
+    p.add_argument("--batched-only", action="store_true", help="run only the batched decode measurements (B = 16, 24, 64; config 4 at N = 1)")
     p.add_argument("--prefill-only", action="store_true",
                    help="profiling aid: only the T=2048 grouped prefill measurement (prints its JSON and exits)")
     p.add_argument("--prefill-reps", type=int, default=8, help="timed grouped prefill layers")
@@ -528,7 +528,12 @@ def bench_batched(layers, dev, args):
         torch.cuda.synchronize()
         loop_us = st.elapsed_time(sp) * 1e3 / 3
         touched = int(torch.unique(idx).numel())
+        mean_touched = statistics.mean(int(torch.unique(mod.gate(x)[0]).numel()) for x in xs)
+        # bytes one call streams: the touched experts, the shared expert and the router
+        call_bytes = (mean_touched + 1) * 3 * H * I + n_exp * H * 4
         out[f"B{B}"] = {"us": round(us, 1), "tokens_per_s": round(B / (us / 1e6), 1), "touched_experts": touched,
+                        "mean_touched_experts": round(mean_touched, 1),
+                        "hbm_frac": round(call_bytes / (us / 1e6) / 1e9 / measured_peaks()["hbm_gbs"], 4),
                         "direct_loop_us": round(loop_us, 1)}
     return out
 
@@ -1153,9 +1158,11 @@ def main():
         import torch
 
         dev = torch.device("cuda", local)
-        layers = build_layers(1, 1000 + 101 * rank, dev, args.experts)
+        layers = build_layers(args.layers, 1000 + 101 * rank, dev, args.experts)
         if rank == 0:
-            print(json.dumps({"batched_decode": bench_batched(layers, dev, args)}), flush=True)
+            res = {"batched_decode": bench_batched(layers, dev, args),
+                   "ep_batched": {f"B{B}": bench_ep_batched(layers, dev, args, 1, 0, B) for B in (16, 64)}}
+            print(json.dumps(res), flush=True)
         return
     if args.hc_only:
         import torch

@@ -3,19 +3,25 @@
 //
 // The expert side of the Direct module's multi-row path
 // (glm53_flash_mlx/fp8.py:384-399: per touched expert, gate/up, SwiGLU and
-// down over the rows routed to it), for up to a few dozen routes.  The routes
-// are sorted by expert (route_plan, descriptors of up to kBdCols routes); a
-// descriptor's routes ride in the N columns of the m16n8k16 GEMV tiles of
-// gemv_tile.cuh (the single-token decode uses column 0 only), so each weight
-// tile is loaded once per descriptor instead of once per route.  Every output
-// column of an MMA is its own dot product, so a route's values are those of
-// the per-route decode (glm53_routes_decode).
-//   batched_gate_up_kernel: work item = (descriptor, 32 hidden rows); four
-//     warps of 8 gate + 8 up rows over the whole K; BF16 SwiGLU per column;
+// down over the rows routed to it), for up to a few hundred routes.  The
+// routes are sorted by expert (route_plan, descriptors of up to kBdCols = 8
+// routes, every N column of the MMA); a descriptor's routes ride in the N
+// columns of the m16n8k16 GEMV tiles of gemv_tile.cuh (the single-token decode
+// uses column 0 only), so each weight tile is loaded once per descriptor
+// instead of once per route.  Every output column of an MMA is its own dot
+// product, so a route's values are those of the per-route decode
+// (glm53_routes_decode).
+//   batched_gate_up_kernel: work item = (descriptor, 8 x WARPS hidden rows);
+//     each warp 8 gate + 8 up rows over the whole K; BF16 SwiGLU per column;
 //     hidden rows in sorted route order.
-//   batched_down_kernel: work item = (descriptor, 64 output rows); four warps
-//     of 16 rows over the whole K = I; BF16 down rows in sorted route order.
-// Both are persistent over the device-side descriptor count (no host sync).
+//   batched_down_kernel: work item = (descriptor, 16 x WARPS output rows);
+//     each warp 16 rows over the whole K = I; BF16 down rows in sorted route
+//     order.
+// Both are persistent over the device-side descriptor count (no host sync),
+// one 16-warp CTA per SM where the staged rows fit: the descriptor's route
+// rows are staged once per SM and the warps run through the items of one
+// descriptor without a barrier (only a new descriptor's staging waits for
+// every warp).
 #include <algorithm>
 
 #include "common.cuh"
@@ -24,11 +30,12 @@
 
 namespace glm53 {
 
-constexpr int kBdWarps = 4;
-constexpr int kBdCols = 4;        // routes per descriptor (MMA N columns used)
+constexpr int kBdCols = 8;        // routes per descriptor (the MMA's N columns)
 constexpr int kBdRing = 8;        // gate/up: K slices in flight per warp
 constexpr int kBdRingDown = 12;   // down: its K streams are short
 constexpr int kBdMaxRoutes = 4096;
+constexpr size_t kBdSmemCta = 232448;  // opt-in shared memory of one CTA (sm_100)
+constexpr size_t kBdSmemSm = 233472;   // shared memory of one SM
 
 __host__ __device__ __forceinline__ int bd_align16(int v) { return (v + 15) & ~15; }
 
@@ -111,16 +118,16 @@ __device__ __forceinline__ float stage_routes_f16(__half* xs, int stride, const 
   return ldexpf(1.0f, e);
 }
 
-template <bool FINITE>
-__global__ void __launch_bounds__(32 * kBdWarps) batched_gate_up_kernel(BatchedArgs a) {
+template <int WARPS, bool FINITE>
+__global__ void __launch_bounds__(32 * WARPS) batched_gate_up_kernel(BatchedArgs a) {
   constexpr int P = kBdRing;
   extern __shared__ __align__(16) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
   uint4* ring = reinterpret_cast<uint4*>(smem) + (size_t)warp * P * 64;
-  __half* xs = reinterpret_cast<__half*>(reinterpret_cast<uint4*>(smem) + (size_t)kBdWarps * P * 64);
+  __half* xs = reinterpret_cast<__half*>(reinterpret_cast<uint4*>(smem) + (size_t)WARPS * P * 64);
   const int stride = bd_align16(a.H + 8);
   float* red = reinterpret_cast<float*>(xs + (size_t)kBdCols * stride);
-  const int groups = a.I / (8 * kBdWarps);
+  const int groups = a.I / (8 * WARPS);
   const int nwork = (int)__ldg(a.descriptor_count) * groups;
   const int cols = a.H >> 7, half = a.I >> 7;
   const int nslice = a.H >> 6;
@@ -137,7 +144,7 @@ __global__ void __launch_bounds__(32 * kBdWarps) batched_gate_up_kernel(BatchedA
     const bool shared = a.sg_w && e == (uint32_t)a.E;
     const bool valid = e < (uint32_t)a.E || shared;
     const uint32_t es = e < (uint32_t)a.E ? e : 0u;
-    const int r0 = grp * 8 * kBdWarps + warp * 8;
+    const int r0 = grp * 8 * WARPS + warp * 8;
     const uint8_t* gw = shared ? a.sg_w + (size_t)r0 * a.H : a.gu_w + ((size_t)es * 2 * a.I + r0) * a.H;
     const uint8_t* uw = shared ? a.su_w + (size_t)r0 * a.H : gw + (size_t)a.I * a.H;
     const float* gs = shared ? a.sg_s + (size_t)(r0 >> 7) * cols : a.gu_s + ((size_t)es * 2 * half + (r0 >> 7)) * cols;
@@ -158,6 +165,7 @@ __global__ void __launch_bounds__(32 * kBdWarps) batched_gate_up_kernel(BatchedA
     ssg.load(gs, cols, valid);
     ssu.load(us, cols, valid);
     if (d != staged) {
+      if (staged >= 0) __syncthreads();  // every warp is done with the previous descriptor's rows
       staged_mul = stage_routes_f16(xs, stride, a.x, a.order + start, a.top_k, len, a.H, red);
       staged = d;
     }
@@ -183,21 +191,20 @@ __global__ void __launch_bounds__(32 * kBdWarps) batched_gate_up_kernel(BatchedA
                                                                          : (uint16_t)0;
     }
     if (!valid && threadIdx.x == 0) atomicOr(a.status, kStatusBadExpert);
-    __syncthreads();  // every warp is done with xs before the next item stages
   }
 }
 
-template <bool FINITE>
-__global__ void __launch_bounds__(32 * kBdWarps) batched_down_kernel(BatchedArgs a) {
+template <int WARPS, bool FINITE>
+__global__ void __launch_bounds__(32 * WARPS) batched_down_kernel(BatchedArgs a) {
   constexpr int P = kBdRingDown;
   extern __shared__ __align__(16) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
   const int K = a.I;
   uint4* ring = reinterpret_cast<uint4*>(smem) + (size_t)warp * P * 64;
-  __half* hs = reinterpret_cast<__half*>(reinterpret_cast<uint4*>(smem) + (size_t)kBdWarps * P * 64);
+  __half* hs = reinterpret_cast<__half*>(reinterpret_cast<uint4*>(smem) + (size_t)WARPS * P * 64);
   const int stride = bd_align16(K + 8);
   float* red = reinterpret_cast<float*>(hs + (size_t)kBdCols * stride);
-  const int groups = a.H / (16 * kBdWarps);
+  const int groups = a.H / (16 * WARPS);
   const int nwork = (int)__ldg(a.descriptor_count) * groups;
   const int cols = K >> 7;
   const int nslice = K >> 6;
@@ -212,7 +219,7 @@ __global__ void __launch_bounds__(32 * kBdWarps) batched_down_kernel(BatchedArgs
     const bool shared = a.sd_w && e == (uint32_t)a.E;
     const bool valid = e < (uint32_t)a.E || shared;
     const uint32_t es = e < (uint32_t)a.E ? e : 0u;
-    const int row0 = grp * 16 * kBdWarps + warp * 16;
+    const int row0 = grp * 16 * WARPS + warp * 16;
     const uint8_t* w0 = shared ? a.sd_w + (size_t)row0 * K : a.d_w + ((size_t)es * a.H + row0) * K;
     const float* srow = shared ? a.sd_s + (size_t)(row0 >> 7) * cols
                                : a.d_s + ((size_t)es * (a.H >> 7) + (row0 >> 7)) * cols;
@@ -231,6 +238,7 @@ __global__ void __launch_bounds__(32 * kBdWarps) batched_down_kernel(BatchedArgs
     WarpScales sd;
     sd.load(srow, cols, valid);
     if (d != staged) {
+      if (staged >= 0) __syncthreads();  // every warp is done with the previous descriptor's rows
       staged_mul = stage_f16(hs, stride, a.hidden + (size_t)start * K, K, len, K, red);
       staged = d;
     }
@@ -260,7 +268,6 @@ __global__ void __launch_bounds__(32 * kBdWarps) batched_down_kernel(BatchedArgs
       }
     }
     if (!valid && threadIdx.x == 0) atomicOr(a.status, kStatusBadExpert);
-    __syncthreads();
   }
 }
 
@@ -296,23 +303,57 @@ static BatchedWorkspace batched_workspace(int64_t R, int64_t E, int64_t H, int64
   return w;
 }
 
+static size_t bd_smem(int warps, int ring, int K) {
+  return (size_t)warps * ring * 64 * 16 + (size_t)kBdCols * bd_align16(K + 8) * 2 + 32 * sizeof(float);
+}
+
+// Warps per CTA: 16 where the rings and the staged rows fit one CTA and the
+// rows split evenly (rows_per_warp x 16 divides `rows`), else 8, else 4;
+// 0 when even 4 do not fit.
+static int bd_warps(int ring, int K, int rows_per_warp, int rows) {
+  for (int w : {16, 8, 4})
+    if (bd_smem(w, ring, K) <= kBdSmemCta && rows % (rows_per_warp * w) == 0) return w;
+  return 0;
+}
+
+template <int WARPS, bool FINITE>
+static int launch_gate_up(const BatchedArgs& a, int64_t capacity, cudaStream_t st) {
+  const size_t smem = bd_smem(WARPS, kBdRing, a.H);
+  int rc = ensure_max_smem((const void*)batched_gate_up_kernel<WARPS, FINITE>, smem);
+  if (rc) return rc;
+  const int per_sm = std::max(1, std::min(64 / WARPS, (int)(kBdSmemSm / (smem + 1024))));
+  const int64_t items = capacity * (a.I / (8 * WARPS));
+  batched_gate_up_kernel<WARPS, FINITE>
+      <<<(unsigned)std::min<int64_t>(items, (int64_t)per_sm * sm_count()), 32 * WARPS, smem, st>>>(a);
+  return check_launch("batched_gate_up_kernel");
+}
+
+template <int WARPS, bool FINITE>
+static int launch_down(const BatchedArgs& a, int64_t capacity, cudaStream_t st) {
+  const size_t smem = bd_smem(WARPS, kBdRingDown, a.I);
+  int rc = ensure_max_smem((const void*)batched_down_kernel<WARPS, FINITE>, smem);
+  if (rc) return rc;
+  const int per_sm = std::max(1, std::min(64 / WARPS, (int)(kBdSmemSm / (smem + 1024))));
+  const int64_t items = capacity * (a.H / (16 * WARPS));
+  batched_down_kernel<WARPS, FINITE>
+      <<<(unsigned)std::min<int64_t>(items, (int64_t)per_sm * sm_count()), 32 * WARPS, smem, st>>>(a);
+  return check_launch("batched_down_kernel");
+}
+
 template <bool FINITE>
 static int launch_batched(const BatchedArgs& a, int64_t capacity, cudaStream_t st) {
-  const size_t smem_gu = (size_t)kBdWarps * kBdRing * 64 * 16 + (size_t)kBdCols * bd_align16(a.H + 8) * 2 +
-                         32 * sizeof(float);
-  const size_t smem_dn = (size_t)kBdWarps * kBdRingDown * 64 * 16 + (size_t)kBdCols * bd_align16(a.I + 8) * 2 +
-                         32 * sizeof(float);
-  int rc = ensure_max_smem((const void*)batched_gate_up_kernel<FINITE>, smem_gu);
+  const int wg = bd_warps(kBdRing, a.H, 8, a.I), wd = bd_warps(kBdRingDown, a.I, 16, a.H);
+  if (!wg || !wd) {
+    set_last_error("batched decode: H=%d / I=%d rows do not fit one CTA's shared memory", a.H, a.I);
+    return GLM53_ERR_INVALID;
+  }
+  int rc = wg == 16 ? launch_gate_up<16, FINITE>(a, capacity, st)
+           : wg == 8 ? launch_gate_up<8, FINITE>(a, capacity, st)
+                     : launch_gate_up<4, FINITE>(a, capacity, st);
   if (rc) return rc;
-  rc = ensure_max_smem((const void*)batched_down_kernel<FINITE>, smem_dn);
-  if (rc) return rc;
-  const int resident = 4 * sm_count();
-  const int64_t gu_items = capacity * (a.I / (8 * kBdWarps)), dn_items = capacity * (a.H / (16 * kBdWarps));
-  batched_gate_up_kernel<FINITE><<<(unsigned)std::min<int64_t>(gu_items, resident), 32 * kBdWarps, smem_gu, st>>>(a);
-  rc = check_launch("batched_gate_up_kernel");
-  if (rc) return rc;
-  batched_down_kernel<FINITE><<<(unsigned)std::min<int64_t>(dn_items, resident), 32 * kBdWarps, smem_dn, st>>>(a);
-  return check_launch("batched_down_kernel");
+  return wd == 16 ? launch_down<16, FINITE>(a, capacity, st)
+         : wd == 8 ? launch_down<8, FINITE>(a, capacity, st)
+                   : launch_down<4, FINITE>(a, capacity, st);
 }
 
 // Every token's routes plus one route to the shared expert (id E, weight
