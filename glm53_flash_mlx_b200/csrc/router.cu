@@ -176,7 +176,7 @@ __device__ void warp_topk_keys(const uint32_t* keys, const float* sigs, const To
 // group-mask scratch (8 warps x E floats) is dynamic shared memory, present
 // only when n_group > 1, so that the router's blocks leave room on the SMs
 // for a decode stage launched as their programmatic dependent.
-template <int T_MAX, int PER>
+template <int TG, int T_MAX, int PER>
 __global__ void __launch_bounds__(256) router_small_kernel(
     const uint16_t* __restrict__ x, int T, int H, const float* __restrict__ w,
     const float* __restrict__ bias, TopkParams p, float* logits, float* sig_buf, uint32_t* key_buf,
@@ -205,37 +205,44 @@ __global__ void __launch_bounds__(256) router_small_kernel(
   // x right away.
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  double acc[T_MAX];
+  // Tokens in groups of TG (the unrolled body stays TG tokens wide): every
+  // token's products are summed in the same K order by the same thread,
+  // whatever T and the group, so a token's logit does not depend on the
+  // batch it rides in.
+  const int t_end = T_MAX == TG ? 1 : T;  // one group (a fixed trip count) when T_MAX == TG
+  for (int t0 = 0; t0 < t_end; t0 += TG) {
+    double acc[TG];
 #pragma unroll
-  for (int t = 0; t < T_MAX; ++t) acc[t] = 0.0;
-  // the products in K order: the prefetched float4 first, then the rest of
-  // the row (H > 4096)
-  auto accumulate = [&](int k, const float4 wv) {
+    for (int t = 0; t < TG; ++t) acc[t] = 0.0;
+    // the products in K order: the prefetched float4 first, then the rest of
+    // the row (H > 4096)
+    auto accumulate = [&](int k, const float4 wv) {
 #pragma unroll
-    for (int t = 0; t < T_MAX; ++t) {
-      if (t < T) {
-        const uint2 raw = __ldg(reinterpret_cast<const uint2*>(x + (size_t)t * H + k));
-        acc[t] = fma((double)__uint_as_float(raw.x << 16), (double)wv.x, acc[t]);
-        acc[t] = fma((double)__uint_as_float(raw.x & 0xFFFF0000u), (double)wv.y, acc[t]);
-        acc[t] = fma((double)__uint_as_float(raw.y << 16), (double)wv.z, acc[t]);
-        acc[t] = fma((double)__uint_as_float(raw.y & 0xFFFF0000u), (double)wv.w, acc[t]);
+      for (int t = 0; t < TG; ++t) {
+        if (t0 + t < T) {
+          const uint2 raw = __ldg(reinterpret_cast<const uint2*>(x + (size_t)(t0 + t) * H + k));
+          acc[t] = fma((double)__uint_as_float(raw.x << 16), (double)wv.x, acc[t]);
+          acc[t] = fma((double)__uint_as_float(raw.x & 0xFFFF0000u), (double)wv.y, acc[t]);
+          acc[t] = fma((double)__uint_as_float(raw.y << 16), (double)wv.z, acc[t]);
+          acc[t] = fma((double)__uint_as_float(raw.y & 0xFFFF0000u), (double)wv.w, acc[t]);
+        }
       }
+    };
+#pragma unroll
+    for (int i = 0; i < kRouterPre; ++i) {
+      const int k = 4 * threadIdx.x + 1024 * i;
+      if (k < H) accumulate(k, pre[i]);
     }
-  };
-#pragma unroll
-  for (int i = 0; i < kRouterPre; ++i) {
-    const int k = 4 * threadIdx.x + 1024 * i;
-    if (k < H) accumulate(k, pre[i]);
-  }
 #pragma unroll 4
-  for (int k = 4 * threadIdx.x + 1024 * kRouterPre; k < H; k += 1024)
-    accumulate(k, __ldcs(reinterpret_cast<const float4*>(wr + k)));
+    for (int k = 4 * threadIdx.x + 1024 * kRouterPre; k < H; k += 1024)
+      accumulate(k, __ldcs(reinterpret_cast<const float4*>(wr + k)));
 #pragma unroll
-  for (int t = 0; t < T_MAX; ++t) {
-    double v = acc[t];
+    for (int t = 0; t < TG; ++t) {
+      double v = acc[t];
 #pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (lane == 0) part[warp][t] = v;
+      for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0 && t0 + t < T_MAX) part[warp][t0 + t] = v;
+    }
   }
   __syncthreads();
   if (threadIdx.x < T_MAX && threadIdx.x < T) {
@@ -506,7 +513,7 @@ struct RouterScratch {
   uint32_t* counter;
 };
 
-template <int T_MAX, int PER>
+template <int TG, int T_MAX, int PER>
 static void launch_small_t(const uint16_t* x, int T, int H, const float* w, const float* bias, TopkParams p,
                            const RouterScratch& r, uint32_t* idx, float* scores, cudaStream_t st, bool pdl) {
   cudaLaunchConfig_t cfg = {};
@@ -519,19 +526,19 @@ static void launch_small_t(const uint16_t* x, int T, int H, const float* w, cons
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  cudaLaunchKernelEx(&cfg, router_small_kernel<T_MAX, PER>, x, T, H, w, bias, p, r.logits, r.sig, r.key, r.counter,
-                     idx, scores);
+  cudaLaunchKernelEx(&cfg, router_small_kernel<TG, T_MAX, PER>, x, T, H, w, bias, p, r.logits, r.sig, r.key,
+                     r.counter, idx, scores);
 }
 
 template <int PER>
 static int launch_small(const uint16_t* x, int T, int H, const float* w, const float* bias, TopkParams p,
                         const RouterScratch& r, uint32_t* idx, float* scores, cudaStream_t st, bool pdl) {
   if (T <= 1)
-    launch_small_t<1, PER>(x, T, H, w, bias, p, r, idx, scores, st, pdl);
+    launch_small_t<1, 1, PER>(x, T, H, w, bias, p, r, idx, scores, st, pdl);
   else if (T <= 8)
-    launch_small_t<8, PER>(x, T, H, w, bias, p, r, idx, scores, st, pdl);
+    launch_small_t<8, 8, PER>(x, T, H, w, bias, p, r, idx, scores, st, pdl);
   else
-    launch_small_t<kRouterSmallT, PER>(x, T, H, w, bias, p, r, idx, scores, st, pdl);
+    launch_small_t<8, kRouterSmallT, PER>(x, T, H, w, bias, p, r, idx, scores, st, pdl);
   return check_launch("router_small_kernel");
 }
 
