@@ -119,7 +119,7 @@ __device__ __forceinline__ float stage_routes_f16(__half* xs, int stride, const 
 }
 
 template <int WARPS, bool FINITE>
-__global__ void __launch_bounds__(32 * WARPS) batched_gate_up_kernel(BatchedArgs a) {
+__global__ void __launch_bounds__(32 * WARPS, 1) batched_gate_up_kernel(BatchedArgs a) {
   constexpr int P = kBdRing;
   extern __shared__ __align__(16) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
@@ -128,16 +128,21 @@ __global__ void __launch_bounds__(32 * WARPS) batched_gate_up_kernel(BatchedArgs
   const int stride = bd_align16(a.H + 8);
   float* red = reinterpret_cast<float*>(xs + (size_t)kBdCols * stride);
   const int groups = a.I / (8 * WARPS);
+  // launched as a programmatic dependent of the route plan: wait for it, then
+  // let the down stage launch (it reads only the plan before its own wait)
+  pdl_wait();
+  pdl_trigger();
   const int nwork = (int)__ldg(a.descriptor_count) * groups;
   const int cols = a.H >> 7, half = a.I >> 7;
   const int nslice = a.H >> 6;
-  // a contiguous run of work items per CTA: consecutive items share their
-  // descriptor, whose route rows are staged once
-  const int per = (nwork + (int)gridDim.x - 1) / (int)gridDim.x;
-  const int w_end = min(nwork, ((int)blockIdx.x + 1) * per);
+  // a contiguous run of work items per CTA (consecutive items share their
+  // descriptor, whose route rows are staged once), the runs balanced to
+  // within one item
+  const int w_begin = (int)((int64_t)blockIdx.x * nwork / gridDim.x);
+  const int w_end = (int)((int64_t)(blockIdx.x + 1) * nwork / gridDim.x);
   int staged = -1;
   float staged_mul = 0.f;
-  for (int w = blockIdx.x * per; w < w_end; ++w) {
+  for (int w = w_begin; w < w_end; ++w) {
     const int d = w / groups, grp = w - d * groups;
     const uint32_t e = __ldg(a.tile_experts + d), start = __ldg(a.tile_starts + d);
     const int len = (int)min(__ldg(a.tile_lengths + d), (uint32_t)kBdCols);
@@ -205,14 +210,17 @@ __global__ void __launch_bounds__(32 * WARPS) batched_down_kernel(BatchedArgs a)
   const int stride = bd_align16(K + 8);
   float* red = reinterpret_cast<float*>(hs + (size_t)kBdCols * stride);
   const int groups = a.H / (16 * WARPS);
+  // Launched as a programmatic dependent of the gate/up stage, which starts
+  // it only after the route plan completed: the plan and the weights are read
+  // before griddepcontrol.wait, the hidden rows after it.
   const int nwork = (int)__ldg(a.descriptor_count) * groups;
   const int cols = K >> 7;
   const int nslice = K >> 6;
-  const int per = (nwork + (int)gridDim.x - 1) / (int)gridDim.x;  // contiguous items, as in gate/up
-  const int w_end = min(nwork, ((int)blockIdx.x + 1) * per);
+  const int w_begin = (int)((int64_t)blockIdx.x * nwork / gridDim.x);  // balanced runs, as in gate/up
+  const int w_end = (int)((int64_t)(blockIdx.x + 1) * nwork / gridDim.x);
   int staged = -1;
   float staged_mul = 0.f;
-  for (int w = blockIdx.x * per; w < w_end; ++w) {
+  for (int w = w_begin; w < w_end; ++w) {
     const int d = w / groups, grp = w - d * groups;
     const uint32_t e = __ldg(a.tile_experts + d), start = __ldg(a.tile_starts + d);
     const int len = (int)min(__ldg(a.tile_lengths + d), (uint32_t)kBdCols);
@@ -238,7 +246,12 @@ __global__ void __launch_bounds__(32 * WARPS) batched_down_kernel(BatchedArgs a)
     WarpScales sd;
     sd.load(srow, cols, valid);
     if (d != staged) {
-      if (staged >= 0) __syncthreads();  // every warp is done with the previous descriptor's rows
+      if (staged >= 0) {
+        __syncthreads();  // every warp is done with the previous descriptor's rows
+      } else {
+        pdl_wait();  // the gate/up stage's hidden rows
+        pdl_trigger();
+      }
       staged_mul = stage_f16(hs, stride, a.hidden + (size_t)start * K, K, len, K, red);
       staged = d;
     }
@@ -323,8 +336,9 @@ static int launch_gate_up(const BatchedArgs& a, int64_t capacity, cudaStream_t s
   if (rc) return rc;
   const int per_sm = std::max(1, std::min(64 / WARPS, (int)(kBdSmemSm / (smem + 1024))));
   const int64_t items = capacity * (a.I / (8 * WARPS));
-  batched_gate_up_kernel<WARPS, FINITE>
-      <<<(unsigned)std::min<int64_t>(items, (int64_t)per_sm * sm_count()), 32 * WARPS, smem, st>>>(a);
+  launch_programmatic(batched_gate_up_kernel<WARPS, FINITE>,
+                      dim3((unsigned)std::min<int64_t>(items, (int64_t)per_sm * sm_count())), dim3(32 * WARPS), smem,
+                      st, a);
   return check_launch("batched_gate_up_kernel");
 }
 
@@ -335,8 +349,9 @@ static int launch_down(const BatchedArgs& a, int64_t capacity, cudaStream_t st) 
   if (rc) return rc;
   const int per_sm = std::max(1, std::min(64 / WARPS, (int)(kBdSmemSm / (smem + 1024))));
   const int64_t items = capacity * (a.H / (16 * WARPS));
-  batched_down_kernel<WARPS, FINITE>
-      <<<(unsigned)std::min<int64_t>(items, (int64_t)per_sm * sm_count()), 32 * WARPS, smem, st>>>(a);
+  launch_programmatic(batched_down_kernel<WARPS, FINITE>,
+                      dim3((unsigned)std::min<int64_t>(items, (int64_t)per_sm * sm_count())), dim3(32 * WARPS), smem,
+                      st, a);
   return check_launch("batched_down_kernel");
 }
 

@@ -140,4 +140,23 @@ void set_last_error(const char* fmt, ...);
 int check_launch(const char* what);
 int sm_count();
 int ensure_max_smem(const void* func, size_t bytes);
+
+// Launch with programmatic stream serialisation: the kernel may start before
+// the previous kernel on the stream has finished (once that kernel's blocks
+// have all triggered or exited) and orders itself with griddepcontrol.wait.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_programmatic(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
 }  // namespace glm53

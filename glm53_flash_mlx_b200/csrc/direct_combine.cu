@@ -33,6 +33,8 @@ __global__ void __launch_bounds__(kCombineThreads) direct_combine_kernel(
   __shared__ uint32_t srow[kCombineMaxK];  // in expert order; 0xFFFFFFFF = skipped slot
   __shared__ float ssc[kCombineMaxK];
   const int t = blockIdx.x, j = threadIdx.x;
+  // launched as a programmatic dependent of the stage that writes `rows`
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   if (j < top_k) sid[j] = __ldg(ids + (size_t)t * top_k + j);
   __syncthreads();
   if (j < top_k) {
@@ -99,8 +101,8 @@ static dim3 combine_grid(int64_t T, int64_t H) {
 int direct_combine_rows(const uint16_t* rows, const uint32_t* row_of_slot, const uint32_t* expert_ids,
                         const float* scores, int64_t T, int top_k, int64_t H, int64_t E, const uint16_t* shared,
                         uint16_t* out, uint32_t* status, cudaStream_t st) {
-  direct_combine_kernel<<<combine_grid(T, H), kCombineThreads, 0, st>>>(rows, row_of_slot, expert_ids, scores, top_k,
-                                                                        (int)H, (uint32_t)E, status, shared, out);
+  launch_programmatic(direct_combine_kernel, combine_grid(T, H), dim3(kCombineThreads), 0, st, rows, row_of_slot,
+                      expert_ids, scores, top_k, (int)H, (uint32_t)E, status, shared, out);
   return check_launch("direct_combine_kernel");
 }
 
