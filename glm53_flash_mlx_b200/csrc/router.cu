@@ -484,6 +484,160 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* logits, i
                  scores + (size_t)t * p.top_k, choice_smem[warp]);
 }
 
+// ---------------------------------------------------------------------------
+// FP32 router logits on the FP64 tensor cores, for 9 <= T <= 64 tokens.
+//
+// D[e][t] = sum_k W[e][k] * X[t][k] with mma.sync m8n8k4 .f64: every product
+// of a BF16 activation and an FP32 weight is exact in FP64 and the sums are
+// FP64, so each logit is the dot product to within ~2^-40 of its terms'
+// magnitude before its one rounding to FP32 (the accuracy of the one-token
+// kernel above; the two may differ in the last FP32 bit, as any two FP64
+// summation orders may).  One 8-expert x 8-token tile per warp and MMA.  On
+// B200 the FP64 tensor MMAs and the FP64 FMAs ran at about the same rate
+// (~5 TFLOP/s measured), which bounds both kernels; the tiles here cost the
+// same per product but replace the per-expert CTAs' register-held token
+// groups and their last-CTA top-k (one warp per token in parallel instead).
+// Grid (E/8 expert tiles, H/1024 K ranges), 8 warps per CTA, 128 K per warp:
+// lane (g, q) holds the A element W[e0+g][k] and the B element X[8n+g][k]
+// of k = kb + 4q + j in MMA j (j = 0..3) of each 16-wide K chunk kb, so its
+// loads are one float4 of weights and one 8-byte activation vector per chunk.
+// The 8 warps' tiles are added in warp order, the CTA's sums stored as FP64
+// partials [K range][T][E]; router_partial_topk_kernel adds the K ranges in
+// order, rounds to FP32 and selects the top-k.
+// ---------------------------------------------------------------------------
+constexpr int kRdK = 1024;   // K per CTA (8 warps x 128)
+constexpr int kRdMaxT = 64;  // tokens per launch (8 token tiles)
+
+__device__ __forceinline__ void dmma_884(double (&d)[2], double a, double b) {
+  asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};\n"
+               : "+d"(d[0]), "+d"(d[1])
+               : "d"(a), "d"(b));
+}
+
+template <int NT>
+__global__ void __launch_bounds__(256) router_dmma_kernel(const uint16_t* __restrict__ x, int T, int H,
+                                                          const float* __restrict__ w, int E,
+                                                          double* __restrict__ partial) {
+  __shared__ double red[8][8][8 * NT];  // [warp][expert of the tile][token]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+  const int e0 = blockIdx.x * 8, s = blockIdx.y;
+  const int kb0 = s * kRdK + warp * 128;
+  const bool erow = e0 + g < E;
+  const float* wp = w + (size_t)(erow ? e0 + g : 0) * H + kb0 + 4 * q;
+  // this warp's weights (never written by the previous kernel) are in flight
+  // before the wait for the activations
+  float4 wv[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    wv[c] = erow ? __ldcs(reinterpret_cast<const float4*>(wp + 16 * c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  double acc[NT][2];
+#pragma unroll
+  for (int n = 0; n < NT; ++n) acc[n][0] = acc[n][1] = 0.0;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const int k = kb0 + 16 * c + 4 * q;
+    const double a0 = wv[c].x, a1 = wv[c].y, a2 = wv[c].z, a3 = wv[c].w;
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      const int t = 8 * n + g;
+      const uint2 raw = t < T ? __ldg(reinterpret_cast<const uint2*>(x + (size_t)t * H + k)) : make_uint2(0u, 0u);
+      dmma_884(acc[n], a0, (double)__uint_as_float(raw.x << 16));
+      dmma_884(acc[n], a1, (double)__uint_as_float(raw.x & 0xFFFF0000u));
+      dmma_884(acc[n], a2, (double)__uint_as_float(raw.y << 16));
+      dmma_884(acc[n], a3, (double)__uint_as_float(raw.y & 0xFFFF0000u));
+    }
+  }
+  // lane (g, q) holds D[e0 + g][8n + 2q + {0, 1}]
+#pragma unroll
+  for (int n = 0; n < NT; ++n) {
+    red[warp][g][8 * n + 2 * q] = acc[n][0];
+    red[warp][g][8 * n + 2 * q + 1] = acc[n][1];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 8 * T; i += 256) {
+    const int t = i >> 3, ge = i & 7;
+    if (e0 + ge < E) {
+      double v = red[0][ge][t];
+#pragma unroll
+      for (int ww = 1; ww < 8; ++ww) v += red[ww][ge][t];
+      partial[((size_t)s * T + t) * E + e0 + ge] = v;
+    }
+  }
+}
+
+// One warp per token: the logit of expert e is the FP32 rounding of the K
+// ranges' FP64 partials added in range order; then the top-k of
+// router_topk_kernel.  Launched as a programmatic dependent of
+// router_dmma_kernel.
+template <int PER>
+__global__ void __launch_bounds__(256) router_partial_topk_kernel(const double* __restrict__ partial, int splits,
+                                                                  int T, const float* __restrict__ bias,
+                                                                  TopkParams p, float* __restrict__ logits,
+                                                                  uint32_t* __restrict__ idx,
+                                                                  float* __restrict__ scores) {
+  __shared__ float choice_smem[8][kRouterMaxE];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + warp;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (t >= T) return;
+  uint32_t key[PER];
+  float sig[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int e = lane + 32 * i;
+    key[i] = 0u;
+    sig[i] = 0.f;
+    if (e < p.E) {
+      double v = __ldcg(partial + (size_t)t * p.E + e);
+      for (int z = 1; z < splits; ++z) v += __ldcg(partial + ((size_t)z * T + t) * p.E + e);
+      const float l = (float)v;
+      if (logits) logits[(size_t)t * p.E + e] = l;
+      route_key(l, __ldg(bias + e), sig[i], key[i]);
+    }
+  }
+  warp_topk_core<PER>(key, sig, p, idx + (size_t)t * p.top_k, scores + (size_t)t * p.top_k, choice_smem[warp]);
+}
+
+// 9..64 tokens (up to 8 the one-CTA-per-expert kernel, sized to T, is faster:
+// both are bound by the FP64 pipe, which the tiles here fill in steps of 8
+// tokens).
+static bool router_dmma_supported(int64_t T, int64_t H) {
+  return T > 8 && T <= kRdMaxT && H % kRdK == 0 && H <= 8 * kRdK;
+}
+
+template <int NT>
+static void launch_dmma_t(const uint16_t* x, int T, int H, const float* w, int E, double* partial, cudaStream_t st,
+                          bool pdl) {
+  const dim3 grid((unsigned)((E + 7) / 8), (unsigned)(H / kRdK));
+  if (pdl)
+    launch_programmatic(router_dmma_kernel<NT>, grid, dim3(256), 0, st, x, T, H, w, E, partial);
+  else
+    router_dmma_kernel<NT><<<grid, 256, 0, st>>>(x, T, H, w, E, partial);
+}
+
+template <int PER>
+static int launch_dmma(const uint16_t* x, int T, int H, const float* w, const float* bias, TopkParams p,
+                       double* partial, float* logits, uint32_t* idx, float* scores, cudaStream_t st, bool pdl) {
+  // token tiles sized to T: every tile's MMAs run whether its tokens exist or not
+  if (T <= 16)
+    launch_dmma_t<2>(x, T, H, w, p.E, partial, st, pdl);
+  else if (T <= 24)
+    launch_dmma_t<3>(x, T, H, w, p.E, partial, st, pdl);
+  else if (T <= 32)
+    launch_dmma_t<4>(x, T, H, w, p.E, partial, st, pdl);
+  else if (T <= 48)
+    launch_dmma_t<6>(x, T, H, w, p.E, partial, st, pdl);
+  else
+    launch_dmma_t<8>(x, T, H, w, p.E, partial, st, pdl);
+  int rc = check_launch("router_dmma_kernel");
+  if (rc) return rc;
+  launch_programmatic(router_partial_topk_kernel<PER>, dim3((unsigned)((T + 7) / 8)), dim3(256), 0, st,
+                      (const double*)partial, H / kRdK, T, bias, p, logits, idx, scores);
+  return check_launch("router_partial_topk_kernel");
+}
+
 template <int PER>
 static int launch_topk(const float* logits, int T, const float* bias, TopkParams p, uint32_t* idx,
                        float* scores, cudaStream_t st, const uint32_t* aborted = nullptr) {
@@ -533,8 +687,14 @@ static void launch_small_t(const uint16_t* x, int T, int H, const float* w, cons
 template <int PER>
 static int launch_small(const uint16_t* x, int T, int H, const float* w, const float* bias, TopkParams p,
                         const RouterScratch& r, uint32_t* idx, float* scores, cudaStream_t st, bool pdl) {
+  // the FP64 FMAs of absent tokens in a group still occupy the FP64 pipe
+  // (predicated off), so the group is sized to T up to 8 tokens
   if (T <= 1)
     launch_small_t<1, 1, PER>(x, T, H, w, bias, p, r, idx, scores, st, pdl);
+  else if (T <= 2)
+    launch_small_t<2, 2, PER>(x, T, H, w, bias, p, r, idx, scores, st, pdl);
+  else if (T <= 4)
+    launch_small_t<4, 4, PER>(x, T, H, w, bias, p, r, idx, scores, st, pdl);
   else if (T <= 8)
     launch_small_t<8, 8, PER>(x, T, H, w, bias, p, r, idx, scores, st, pdl);
   else
@@ -552,9 +712,13 @@ using namespace glm53;
 // mma.sync path's, whichever is larger), the weights' three BF16 planes (for
 // H <= 8192) and its abort word.
 static size_t router_partial_bytes(int64_t T, int64_t E) {
-  if (T <= kRouterSmallT) return 0;
-  const int s = std::max(router_splits(T, E), router_tc_splits(T, E));
-  return align_up((size_t)s * (size_t)T * (size_t)E * sizeof(double), 256);
+  size_t b = 0;
+  if (T > 8 && T <= kRdMaxT) b = (size_t)8 * T * E * sizeof(double);  // up to 8 K ranges (H <= 8192)
+  if (T > kRouterSmallT) {
+    const int s = std::max(router_splits(T, E), router_tc_splits(T, E));
+    b = std::max(b, (size_t)s * (size_t)T * (size_t)E * sizeof(double));
+  }
+  return align_up(b, 256);
 }
 
 static size_t router_planes_bytes(int64_t T, int64_t E) {
@@ -595,6 +759,15 @@ int router_topk(const void* x, int64_t T, int64_t H, const float* w, int64_t E, 
   TopkParams p{(int)E, top_k, n_group < 1 ? 1 : n_group, topk_group, norm_topk_prob, routed_scaling_factor};
   const bool vec = (H % 4 == 0) && (((uintptr_t)w & 15) == 0) && (((uintptr_t)x & 7) == 0);
   const int per = (int)((E + 31) / 32);
+  if (router_dmma_supported(T, H) && vec) {
+    double* partial = (double*)(ws + 3 * plane + 256);
+    if (per <= 4)
+      return launch_dmma<4>((const uint16_t*)x, (int)T, (int)H, w, bias, p, partial, logits, indices, scores, st, pdl);
+    if (per <= 10)
+      return launch_dmma<10>((const uint16_t*)x, (int)T, (int)H, w, bias, p, partial, logits, indices, scores, st,
+                             pdl);
+    return launch_dmma<32>((const uint16_t*)x, (int)T, (int)H, w, bias, p, partial, logits, indices, scores, st, pdl);
+  }
   if (T <= kRouterSmallT && vec) {
     if (per <= 4)
       return launch_small<4>((const uint16_t*)x, (int)T, (int)H, w, bias, p, rs, indices, scores, st, pdl);

@@ -120,7 +120,7 @@ def test_block_linear_fail_closed_checks(G):
 # ---------------------------------------------------------------------------
 
 
-@pytest.mark.parametrize("T", [1, 5, 8, 16, 32, 64, 300])
+@pytest.mark.parametrize("T", [1, 2, 5, 8, 9, 16, 24, 32, 40, 64, 300])
 def test_router_matches_oracle(G, S, oracle, T):
     E, H = 288, 4096
     w, b = S.make_router(E, H, seed=1, device="cuda", zipf_alpha=0.5 if T > 8 else 0.0)
@@ -130,7 +130,8 @@ def test_router_matches_oracle(G, S, oracle, T):
     r_idx, r_sc, r_l64, margin = oracle.router(bits(x), w.cpu().numpy(), b.cpu().numpy(), top_k=8)
     stats = router_logit_check(logits.cpu().numpy(), r_l64, bits(x), w.cpu().numpy())
     print(f"[router T={T}] {stats}")
-    if T <= 32:  # double-FP32 accumulation: every logit within 1e-6 relative, none excepted
+    if T <= 64:  # FP64 sums (per-expert CTAs up to 8 tokens, FP64 tensor-core tiles to 64): every logit
+        # within 1e-6 relative of the FP64 oracle, none excepted
         assert stats["beyond_1e-6_relative_within_bound"] == 0, stats
     clear = margin > 1e-5
     assert clear.mean() > 0.9
