@@ -375,6 +375,7 @@ static int launch_batched(const BatchedArgs& a, int64_t capacity, cudaStream_t s
 // 1.0, last in the token's slots); ids >= E become 0xFFFFFFFF (still bad).
 __global__ void extend_routes_kernel(const uint32_t* __restrict__ ids, const float* __restrict__ scores, int64_t T,
                                      int top_k, uint32_t E, uint32_t* __restrict__ ids2, float* __restrict__ scores2) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the router's ids and scores
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= T * (top_k + 1)) return;
   const int64_t t = i / (top_k + 1);
@@ -575,8 +576,8 @@ extern "C" int glm53_batched_decode_moe_shared(const void* x, int64_t T, int64_t
   const size_t plan = batched_workspace(R, E + 1, H, I).bytes;
   uint32_t* ids2 = (uint32_t*)((char*)workspace + plan);
   float* scores2 = (float*)((char*)workspace + plan + align_up((size_t)R * 4, 256));
-  extend_routes_kernel<<<(unsigned)((R + 255) / 256), 256, 0, st>>>(expert_ids, scores, T, top_k, (uint32_t)E, ids2,
-                                                                   scores2);
+  launch_programmatic(extend_routes_kernel, dim3((unsigned)((R + 255) / 256)), dim3(256), 0, st, expert_ids, scores,
+                      T, top_k, (uint32_t)E, ids2, scores2);
   int rc = check_launch("extend_routes_kernel");
   if (rc) return rc;
   const SharedWeights sw{shared_gate_w, shared_gate_s, shared_up_w, shared_up_s, shared_down_w, shared_down_s};

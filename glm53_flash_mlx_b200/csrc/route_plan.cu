@@ -33,6 +33,9 @@ __global__ void __launch_bounds__(kPlanThreads) route_plan_kernel(
   const int B = E + 1;
   for (int i = tid; i < B; i += kPlanThreads) cursor[i] = 0;
   for (int i = tid; i < kPlanWarps * B; i += kPlanThreads) wcount[i] = 0;
+  // launched as a programmatic dependent of the kernel that writes the ids:
+  // nothing global is read or written before this
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   __syncthreads();
   // 1. histogram (eight loads in flight per thread: the ids come from L2/HBM)
   for (int r0 = tid; r0 < R; r0 += 8 * kPlanThreads) {
@@ -158,10 +161,10 @@ int route_plan(const uint32_t* ids, int64_t R, int64_t E, int64_t tile_rows, con
     int rc_attr = ensure_max_smem((const void*)route_plan_kernel, smem);
     if (rc_attr) return rc_attr;
   }
-  route_plan_kernel<<<1, kPlanThreads, smem, stream>>>(
-      ids, (int)R, (int)E, (int)tile_rows, scores, order, inverse, sorted_experts, sorted_scores,
-      route_offsets, tile_experts, tile_starts, tile_lengths, tile_offsets, descriptor_count, invalid_count,
-      (int)capacity);
+  launch_programmatic(route_plan_kernel, dim3(1), dim3(kPlanThreads), smem, stream, ids, (int)R, (int)E,
+                      (int)tile_rows, scores, order, inverse, sorted_experts, sorted_scores, route_offsets,
+                      tile_experts, tile_starts, tile_lengths, tile_offsets, descriptor_count, invalid_count,
+                      (int)capacity);
   return check_launch("route_plan_kernel");
 }
 
