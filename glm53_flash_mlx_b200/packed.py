@@ -392,6 +392,8 @@ class StatusWord:
         # one int32 word (in a 256-byte allocation of its own)
         self.word = torch.zeros(64, dtype=torch.int32, device=self.device)[:1]
         self.host = torch.zeros(4, dtype=torch.int32).pin_memory()
+        # a plain host read of the mirror (indexing the tensor costs ~3 us a call)
+        self._host_word = ctypes.c_int32.from_address(self.host.data_ptr())
 
     def publish(self) -> None:
         N.check(N.lib().glm53_status_mirror(self.word.data_ptr(), self.host.data_ptr(), N.stream(self.device)),
@@ -408,7 +410,7 @@ class StatusWord:
         _raise_status(word & 0xFFFFFFFF)
 
     def raise_pending(self) -> None:
-        word = int(self.host[0])
+        word = self._host_word.value
         if word:
             self._fail(word)
 
@@ -536,6 +538,7 @@ class PackedDecodeStep:
             status_host=self._status.host.data_ptr())
         self._pdesc = ctypes.pointer(self._desc)
         self._lib = lib
+        self._device = self.x.device
         # a second descriptor whose input and output point at the caller's
         # device rows (run_device): no copy into or out of the static buffers
         self._ddesc = N.DecodeStepDesc.from_buffer_copy(self._desc)
@@ -578,10 +581,7 @@ class PackedDecodeStep:
         for (d, name, obj) in self._slots:
             if d.get(name) is not obj:
                 return False
-        for t, (ptr, version) in zip(self._bound, self._identity):
-            if t._version != version or t.data_ptr() != ptr:
-                return False
-        return True
+        return tuple([(t.data_ptr(), t._version) for t in self._bound]) == self._identity
 
     def _check_bound(self) -> None:
         if not self.bound_ok():
@@ -602,7 +602,7 @@ class PackedDecodeStep:
         d = self._ddesc
         d.x = x.data_ptr()
         d.out = out.data_ptr()
-        N.check(self._lib.glm53_decode_step_host(self._pddesc, None, None, N.stream(x.device)),
+        N.check(self._lib.glm53_decode_step_host(self._pddesc, None, None, N.stream(self._device)),
                 "glm53_decode_step_host")
         if _SYNC_STATUS:
             self._status.check()
@@ -626,15 +626,16 @@ class PackedDecodeStep:
                 (module.shared_experts is None or (shared is not None and shared[0].shape[0] % BLOCK_SIZE == 0)))
 
     def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-        H = self.x.numel()
+        H = self._desc.H
         if x.numel() != H:
             raise ValueError(f"decode step input has {x.numel()} values, layer width {H}")
         self._check_bound()
         # bits of earlier steps, mirrored into pinned host memory by this
         # step's predecessors on the stream: a host read, no synchronisation
         self._status.raise_pending()
-        if x.device.type == "cpu":
-            x = x.to(torch.bfloat16).contiguous()
+        if not x.is_cuda:
+            if x.dtype != torch.bfloat16 or not x.is_contiguous():
+                x = x.to(torch.bfloat16).contiguous()
             x_host = x.data_ptr()
         else:
             self.x.copy_(x.reshape(self.x.shape))
@@ -643,9 +644,9 @@ class PackedDecodeStep:
         if out is not None:
             if out.numel() != H or out.dtype != torch.bfloat16 or not out.is_contiguous():
                 raise ValueError("decode step output must be a contiguous BF16 row of the layer width")
-            if out.device.type == "cpu":
+            if not out.is_cuda:
                 out_host = out.data_ptr()
-        N.check(self._lib.glm53_decode_step_host(self._pdesc, x_host, out_host, N.stream(self.x.device)),
+        N.check(self._lib.glm53_decode_step_host(self._pdesc, x_host, out_host, N.stream(self._device)),
                 "glm53_decode_step_host")
         if _SYNC_STATUS:
             self._status.check()
