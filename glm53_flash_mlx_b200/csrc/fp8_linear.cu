@@ -23,31 +23,40 @@ namespace glm53 {
 // two): config 1 (6144 x 4096, 384 tiles) measured 8.30 -> 6.86 us per call,
 // while shapes that fit one wave at depth 8 are fastest there (4096 x 12288:
 // 12.7 us at 8, 17.0 at 5).
-template <int KS, bool FINITE, int P>
-__global__ void __launch_bounds__(32 * KS) gemv_stream_kernel(const uint16_t* __restrict__ x, int M, int K,
-                                                              const uint8_t* __restrict__ w, int N,
-                                                              const float* __restrict__ s, uint16_t* __restrict__ y,
-                                                              int chunk) {
+// TG groups of KS warps per block stream TG tiles at once over one staged copy
+// of the activation rows (group g takes the block's tiles g, g + TG, ...): with
+// eight rows staged (64 KB at K = 4096) only one block fits an SM, and two
+// groups keep as many bytes in flight as the one-row launch's blocks do.
+// Every output is the same ordered sum of the same per-warp K ranges whatever
+// TG, P and the grid.
+template <int KS, int TG, bool FINITE, int P>
+__global__ void __launch_bounds__(32 * KS * TG) gemv_stream_kernel(const uint16_t* __restrict__ x, int M, int K,
+                                                                   const uint8_t* __restrict__ w, int N,
+                                                                   const float* __restrict__ s,
+                                                                   uint16_t* __restrict__ y, int chunk) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+  const int grp = warp / KS, kwarp = warp - grp * KS;
   const int m0 = blockIdx.y * chunk;
   const int ncols = min(chunk, M - m0);
   const int stride = (xs_stride(K) + 7) & ~7;
   uint4* ring = reinterpret_cast<uint4*>(smem) + (size_t)warp * P * 64;
-  __half* xs = reinterpret_cast<__half*>(reinterpret_cast<uint4*>(smem) + (size_t)KS * P * 64);
-  float* red = reinterpret_cast<float*>(xs + (size_t)chunk * stride);  // [2][KS][128]
-  float* scratch = red + 2 * KS * 128;
+  __half* xs = reinterpret_cast<__half*>(reinterpret_cast<uint4*>(smem) + (size_t)KS * TG * P * 64);
+  float* red = reinterpret_cast<float*>(xs + (size_t)chunk * stride);  // [TG][2][KS][128]
+  float* scratch = red + TG * 2 * KS * 128;
   const int ntiles = (N + 15) >> 4;
-  const int my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int cta_tiles = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int my_tiles = cta_tiles > grp ? (cta_tiles - 1 - grp) / TG + 1 : 0;
+  auto row_of = [&](int it) { return (blockIdx.x + (grp + it * TG) * gridDim.x) << 4; };
   const int kper = K / KS;
   const int nslice = kper >> 6;
-  const int kw = warp * kper + 16 * q;
+  const int kw = kwarp * kper + 16 * q;
   const int scols = K >> 7;
   // issue cursor (tile, slice) runs P - 1 slices ahead of the consume cursor
   int i_it = 0, i_sl = 0;
   auto issue = [&]() {
     if (i_it < my_tiles) {
-      const int row0 = (blockIdx.x + i_it * gridDim.x) << 4;
+      const int row0 = row_of(i_it);
       const int k = kw + 64 * i_sl;
       uint4* dst = ring + ((i_it * nslice + i_sl) % P) * 64 + lane;
       const bool v0 = row0 + g < N, v8 = row0 + g + 8 < N;
@@ -72,14 +81,12 @@ __global__ void __launch_bounds__(32 * KS) gemv_stream_kernel(const uint16_t* __
   float part[4] = {0.f, 0.f, 0.f, 0.f}, tot[4] = {0.f, 0.f, 0.f, 0.f};
   // this warp's block scales of the current tile, the next tile's prefetched
   const int nb = kper >> 7;
-  auto srow_of = [&](int it) {
-    return s + (size_t)(((blockIdx.x + it * gridDim.x) << 4) >> 7) * scols + ((warp * kper) >> 7);
-  };
+  auto srow_of = [&](int it) { return s + (size_t)(row_of(it) >> 7) * scols + ((kwarp * kper) >> 7); };
   WarpScales cur, nxt;
   cur.load(srow_of(0), nb, my_tiles > 0);
   int u = 0;
   for (int it = 0; it < my_tiles; ++it) {
-    const int row0 = (blockIdx.x + it * gridDim.x) << 4;
+    const int row0 = row_of(it);
     nxt.load(srow_of(it + 1), nb, it + 1 < my_tiles);
     for (int sl = 0; sl < nslice; ++sl, ++u) {
       issue();
@@ -92,16 +99,17 @@ __global__ void __launch_bounds__(32 * KS) gemv_stream_kernel(const uint16_t* __
       if (sl & 1) promote(tot, part, cur.at(sl >> 1) * smul);
     }
     cur = nxt;
-    float* r = red + (it & 1) * KS * 128 + warp * 128;
+    float* r = red + ((grp * 2 + (it & 1)) * KS + kwarp) * 128;
     r[g * 8 + 2 * q] = tot[0];
     r[g * 8 + 2 * q + 1] = tot[1];
     r[(g + 8) * 8 + 2 * q] = tot[2];
     r[(g + 8) * 8 + 2 * q + 1] = tot[3];
 #pragma unroll
     for (int c = 0; c < 4; ++c) tot[c] = 0.f;
-    __syncthreads();
-    const float* rb = red + (it & 1) * KS * 128;
-    for (int i = threadIdx.x; i < 128; i += blockDim.x) {
+    // the group's KS warps only (barrier 1 + group; stage_f16 used barrier 0)
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + grp), "r"(32 * KS) : "memory");
+    const float* rb = red + (grp * 2 + (it & 1)) * KS * 128;
+    for (int i = threadIdx.x - grp * 32 * KS; i < 128; i += 32 * KS) {
       const int rr = i >> 3, c = i & 7;
       if (c < ncols && row0 + rr < N) {
         float v = 0.f;
@@ -134,28 +142,28 @@ __global__ void __launch_bounds__(256) fp8_linear_scalar_kernel(const uint16_t* 
   if (lane == 0) y[m * N + n] = f32_to_bf16_bits(acc);
 }
 
-static size_t gemv_smem(int KS, int P, int chunk, int64_t K) {
-  return (size_t)KS * P * 64 * 16 + (size_t)chunk * ((xs_stride(K) + 7) & ~7) * 2 +
-         (size_t)(2 * KS * 128 + 32) * sizeof(float);
+static size_t gemv_smem(int KS, int P, int chunk, int64_t K, int TG = 1) {
+  return (size_t)KS * TG * P * 64 * 16 + (size_t)chunk * ((xs_stride(K) + 7) & ~7) * 2 +
+         (size_t)(TG * 2 * KS * 128 + 32) * sizeof(float);
 }
 
 // Blocks per SM the launch counts on: up to three (one 16-row tile per block
 // for N up to 444 * 16 rows, so no block streams two tiles while others idle).
 static int gemv_per_sm(size_t smem) { return std::max(1, std::min(3, (int)((220 * 1024) / smem))); }
 
-template <int KS, bool FINITE, int P>
+template <int KS, int TG, bool FINITE, int P>
 static int launch_gemv_ring(const uint16_t* x, int M, int K, const uint8_t* w, int N, const float* s, uint16_t* y,
                             int chunk, cudaStream_t stream) {
-  const size_t smem = gemv_smem(KS, P, chunk, K);
-  int rc_attr = ensure_max_smem((const void*)gemv_stream_kernel<KS, FINITE, P>, smem);
+  const size_t smem = gemv_smem(KS, P, chunk, K, TG);
+  int rc_attr = ensure_max_smem((const void*)gemv_stream_kernel<KS, TG, FINITE, P>, smem);
   if (rc_attr) return rc_attr;
   const int ntiles = (N + 15) / 16;
   const int chunks = (M + chunk - 1) / chunk;
   const int per_sm = gemv_per_sm(smem);
-  const int bx = std::max(1, std::min(ntiles, (sm_count() * per_sm + chunks - 1) / chunks));
+  const int bx = std::max(1, std::min((ntiles + TG - 1) / TG, (sm_count() * per_sm + chunks - 1) / chunks));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)bx, (unsigned)chunks);
-  cfg.blockDim = dim3(32 * KS);
+  cfg.blockDim = dim3(32 * KS * TG);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -163,7 +171,7 @@ static int launch_gemv_ring(const uint16_t* x, int M, int K, const uint8_t* w, i
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaLaunchKernelEx(&cfg, gemv_stream_kernel<KS, FINITE, P>, x, M, K, w, N, s, y, chunk);
+  cudaLaunchKernelEx(&cfg, gemv_stream_kernel<KS, TG, FINITE, P>, x, M, K, w, N, s, y, chunk);
   return check_launch("gemv_stream_kernel");
 }
 
@@ -172,12 +180,17 @@ static int launch_gemv_stream(const uint16_t* x, int M, int K, const uint8_t* w,
                               uint16_t* y, cudaStream_t stream) {
   int chunk = std::min(8, M);
   while (chunk > 1 && gemv_smem(KS, 8, chunk, K) > 200 * 1024) chunk = (chunk + 1) / 2;
+  // two tile groups per block when the staged rows leave room for only one
+  // single-group block per SM and two groups' rings fit beside them
+  if (KS * 2 <= 16 && gemv_per_sm(gemv_smem(KS, 8, chunk, K)) == 1 &&
+      gemv_smem(KS, 8, chunk, K, 2) <= 220 * 1024)
+    return launch_gemv_ring<KS, 2, FINITE, 8>(x, M, K, w, N, s, y, chunk, stream);
   const int64_t units = (int64_t)((N + 15) / 16) * ((M + chunk - 1) / chunk);
   const int64_t wave8 = (int64_t)sm_count() * gemv_per_sm(gemv_smem(KS, 8, chunk, K));
   const int64_t wave5 = (int64_t)sm_count() * gemv_per_sm(gemv_smem(KS, 5, chunk, K));
   if (units > wave8 && units <= wave5)
-    return launch_gemv_ring<KS, FINITE, 5>(x, M, K, w, N, s, y, chunk, stream);
-  return launch_gemv_ring<KS, FINITE, 8>(x, M, K, w, N, s, y, chunk, stream);
+    return launch_gemv_ring<KS, 1, FINITE, 5>(x, M, K, w, N, s, y, chunk, stream);
+  return launch_gemv_ring<KS, 1, FINITE, 8>(x, M, K, w, N, s, y, chunk, stream);
 }
 
 template <bool FINITE>

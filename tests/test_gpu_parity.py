@@ -71,7 +71,9 @@ def test_sigmoid_sweep_bit_exact_on_gpu(N, oracle):
 @pytest.mark.parametrize(
     "M,N_,K",
     [(1, 129, 257), (2, 129, 257), (1, 256, 4096), (3, 384, 1024), (8, 512, 2048), (16, 256, 256),
-     (17, 256, 512), (64, 256, 512), (200, 384, 1024), (1, 6144, 4096)],
+     (17, 256, 512), (64, 256, 512), (200, 384, 1024), (1, 6144, 4096),
+     # two tile groups per block (eight / five staged rows at K = 4096), an odd tile count
+     (8, 6144, 4096), (5, 1040, 4096), (16, 4096, 4096)],
 )
 def test_block_linear_matches_oracle(G, S, oracle, M, N_, K):
     w, s = S.random_block_fp8(N_, K, seed=M * 1000 + N_, device="cuda")
