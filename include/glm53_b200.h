@@ -144,6 +144,12 @@ size_t glm53_router_workspace_bytes(int64_t T, int64_t E);
  * choice (slot order: descending choice, ties to the lower expert id);
  * scores = s[idx], normalised over the top_k when norm_topk_prob, times
  * routed_scaling_factor.  logits may be NULL.
+ * Up to 64 tokens every logit is summed in FP64 (the products of BF16
+ * activations and FP32 weights are exact there) and rounded once to FP32:
+ * one CTA per expert row up to 8 tokens, FP64 tensor-core tiles of 8 experts
+ * x 8 tokens for 9..64 (H a multiple of 1024, up to 8192), so a token routed
+ * alone and in such a batch may differ in a logit's last FP32 bit.  Larger
+ * batches use BF16-split tensor-core tiles with FP64 sums of the K ranges.
  * Replaces Float32Gate.__call__, glm53_flash_mlx/patch.py:131-142, and the
  * mlx-vlm group_expert_select it calls. */
 int glm53_router_topk(const void* x, int64_t T, int64_t H, const float* w,
