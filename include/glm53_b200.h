@@ -390,7 +390,7 @@ size_t glm53_batched_decode_workspace_bytes(int64_t T, int top_k, int64_t E, int
 
 /* A small decode batch (T tokens, T * top_k <= 4096 routes) through the packed
  * bank with the Direct module's multi-row semantics: the routes are sorted by
- * expert on the device (glm53_route_plan, descriptors of up to 4 routes), each
+ * expert on the device (glm53_route_plan, descriptors of up to 8 routes), each
  * descriptor streams its expert's weights once for all its routes (per-route
  * values identical to glm53_routes_decode), and glm53_direct_combine's BF16
  * scatter-add in ascending expert id adds them per token, then `shared`
