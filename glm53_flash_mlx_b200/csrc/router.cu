@@ -791,7 +791,8 @@ int router_topk(const void* x, int64_t T, int64_t H, const float* w, int64_t E, 
     router_split_kernel<<<(unsigned)std::min<int64_t>((n4 + 255) / 256, 1184), 256, 0, st>>>(w, n4, planes, E * H);
     rc = check_launch("router_split_kernel");
     if (rc) return rc;
-    const int splits = router_tc_splits(T, E);
+    // at most one K range per 128-wide K block (small H with few tiles)
+    const int splits = std::min(router_tc_splits(T, E), (int)(H / 128));
     rc = router_logits_tc((const uint16_t*)x, T, H, planes, E, partial_buf, splits, aborted, st);
     if (rc) return rc;
     const int64_t n = T * E;

@@ -141,6 +141,23 @@ def test_router_matches_oracle(G, S, oracle, T):
     np.testing.assert_allclose(sc.cpu().numpy()[clear], r_sc[clear], rtol=1e-6, atol=1e-6)
 
 
+@pytest.mark.parametrize("T,E,H", [(40, 16, 512), (100, 16, 256), (12, 16, 512), (70, 64, 1024)])
+def test_router_small_width_matches_oracle(G, S, oracle, T, E, H):
+    """Widths below the FP64 tensor-core tiles' 1024 and few expert tiles: the
+    per-expert kernel up to 32 tokens, the BF16-split tcgen05 kernel above
+    (its K ranges capped at one per 128-wide K block)."""
+    w, b = S.make_router(E, H, seed=T + H, device="cuda")
+    x = S.random_bf16((T, H), seed=T, device="cuda")
+    idx, sc, logits = G.router_topk(x, w, b, top_k=8, return_logits=True)
+    torch.cuda.synchronize()
+    r_idx, r_sc, r_l64, margin = oracle.router(bits(x), w.cpu().numpy(), b.cpu().numpy(), top_k=8)
+    stats = router_logit_check(logits.cpu().numpy(), r_l64, bits(x), w.cpu().numpy())
+    assert stats["beyond_1e-6_relative_within_bound"] == 0 or T > 32, stats
+    clear = margin > 1e-5
+    assert np.array_equal(idx.cpu().numpy()[clear].astype(np.uint32), r_idx[clear])
+    np.testing.assert_allclose(sc.cpu().numpy()[clear], r_sc[clear], rtol=1e-6, atol=1e-6)
+
+
 def test_router_group_selection_matches_oracle(G, S, oracle):
     E, H, T = 64, 512, 16
     w, b = S.make_router(E, H, seed=3, device="cuda")
