@@ -43,6 +43,25 @@ def test_workspace_queries_are_pure_host_functions():
     assert ws >= 16384 * (4096 + 1536) * 2
 
 
+def test_router_workspace_covers_each_batch_path():
+    """glm53_router_workspace_bytes(T, E): logits, sigmoids and keys (T x E each)
+    for every T; from 9 to 64 tokens also the FP64 tensor-core tiles' partials
+    (up to 8 K ranges x T x E doubles); above 32 the BF16 weight planes
+    (3 x E x 8192) of the tcgen05 router as well."""
+    from glm53_flash_mlx_b200 import _native as N
+
+    lib = N.load_library()
+    E = 288
+    for T in (1, 2, 8):
+        assert lib.glm53_router_workspace_bytes(T, E) >= 3 * T * E * 4
+    for T in (9, 16, 32, 64):
+        assert lib.glm53_router_workspace_bytes(T, E) >= 3 * T * E * 4 + 8 * T * E * 8
+    for T in (33, 64, 300, 2048):
+        assert lib.glm53_router_workspace_bytes(T, E) >= 3 * T * E * 4 + 3 * E * 8192 * 2
+    sizes = [lib.glm53_router_workspace_bytes(T, E) for T in range(1, 80)]
+    assert sizes == sorted(sizes)  # a workspace sized for T serves every smaller batch
+
+
 def test_operators_fail_closed_without_cuda():
     import pytest
     import torch
