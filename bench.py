@@ -70,6 +70,7 @@ def parse_args():
     p.add_argument("--quick-linear", action="store_true", help="config-5 sweep at M in {1, 64, 512} only")
     p.add_argument("--linear-only", action="store_true", help="run only the config-1/5 block-linear sweep")
     p.add_argument("--batched-only", action="store_true", help="run only the batched decode measurements (B = 16, 24, 64; config 4 at N = 1)")
+    p.add_argument("--batched-tokens", default="16,24,64", help="batch sizes of the batched decode measurement")
     p.add_argument("--prefill-only", action="store_true",
                    help="profiling aid: only the T=2048 grouped prefill measurement (prints its JSON and exits)")
     p.add_argument("--prefill-reps", type=int, default=8, help="timed grouped prefill layers")
@@ -504,7 +505,7 @@ def bench_batched(layers, dev, args):
     gate.e_score_correction_bias.copy_(L["router_b"])
     mod = G.PackedFP8MoE(L["bank"], cfg, gate, L["shared_mod"])
     out = {}
-    for B in (16, 24, 64):
+    for B in (int(b) for b in args.batched_tokens.split(",")):
         xs = [S.random_bf16((1, B, H), seed=500 + i, device=dev) for i in range(8)]
         for i in range(3):
             mod(xs[i % 8])
@@ -1161,7 +1162,8 @@ def main():
         layers = build_layers(args.layers, 1000 + 101 * rank, dev, args.experts)
         if rank == 0:
             res = {"batched_decode": bench_batched(layers, dev, args),
-                   "ep_batched": {f"B{B}": bench_ep_batched(layers, dev, args, 1, 0, B) for B in (16, 64)}}
+                   "ep_batched": {f"B{B}": bench_ep_batched(layers, dev, args, 1, 0, int(B))
+                                  for B in args.batched_tokens.split(",") if int(B) in (16, 64)}}
             print(json.dumps(res), flush=True)
         return
     if args.hc_only:
