@@ -492,11 +492,12 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* logits, i
 // FP64, so each logit is the dot product to within ~2^-40 of its terms'
 // magnitude before its one rounding to FP32 (the accuracy of the one-token
 // kernel above; the two may differ in the last FP32 bit, as any two FP64
-// summation orders may).  One 8-expert x 8-token tile per warp and MMA.  On
-// B200 the FP64 tensor MMAs and the FP64 FMAs ran at about the same rate
-// (~5 TFLOP/s measured), which bounds both kernels; the tiles here cost the
-// same per product but replace the per-expert CTAs' register-held token
-// groups and their last-CTA top-k (one warp per token in parallel instead).
+// summation orders may).  One 8-expert x 8-token tile per warp and MMA.
+// Beyond 8 tokens this beats the per-expert CTAs, whose register-held token
+// groups run one after another and whose last CTA selects every token's
+// top-k in turn (here one warp per token, in parallel).  Both kernels run few
+// warps per SM and are bound by latency rather than by an FP64 pipe (ncu at
+// T = 16: the DMMA subpipe busy 29% of active cycles).
 // Grid (E/8 expert tiles, H/1024 K ranges), 8 warps per CTA, 128 K per warp:
 // lane (g, q) holds the A element W[e0+g][k] and the B element X[8n+g][k]
 // of k = kb + 4q + j in MMA j (j = 0..3) of each 16-wide K chunk kb, so its
@@ -600,9 +601,8 @@ __global__ void __launch_bounds__(256) router_partial_topk_kernel(const double* 
   warp_topk_core<PER>(key, sig, p, idx + (size_t)t * p.top_k, scores + (size_t)t * p.top_k, choice_smem[warp]);
 }
 
-// 9..64 tokens (up to 8 the one-CTA-per-expert kernel, sized to T, is faster:
-// both are bound by the FP64 pipe, which the tiles here fill in steps of 8
-// tokens).
+// 9..64 tokens (up to 8 the one-CTA-per-expert kernel, its token group sized
+// to T, measured faster: 9.4 against 13.6 us at T = 8 / 9).
 static bool router_dmma_supported(int64_t T, int64_t H) {
   return T > 8 && T <= kRdMaxT && H % kRdK == 0 && H <= 8 * kRdK;
 }
@@ -687,8 +687,9 @@ static void launch_small_t(const uint16_t* x, int T, int H, const float* w, cons
 template <int PER>
 static int launch_small(const uint16_t* x, int T, int H, const float* w, const float* bias, TopkParams p,
                         const RouterScratch& r, uint32_t* idx, float* scores, cudaStream_t st, bool pdl) {
-  // the FP64 FMAs of absent tokens in a group still occupy the FP64 pipe
-  // (predicated off), so the group is sized to T up to 8 tokens
+  // the token group is sized to T up to 8 tokens (T = 2: 5.7 us with a
+  // 2-token group, 8.1 us with the 8-token one, whose absent tokens' work is
+  // issued predicated off)
   if (T <= 1)
     launch_small_t<1, 1, PER>(x, T, H, w, bias, p, r, idx, scores, st, pdl);
   else if (T <= 2)
