@@ -911,6 +911,29 @@ def test_coalesced_batched_decode_equals_per_route_decode_bitwise(G, S, T, E, H,
     assert torch.equal(got, want)
 
 
+@pytest.mark.parametrize("top_k,H", [(8, 4096), (9, 520), (32, 1024)])
+def test_direct_combine_orders_slots_by_expert_then_slot(top_k, H):
+    """glm53_direct_combine: per token, BF16(row * score) added in BF16 in
+    ascending expert id -- repeated ids in slot order (a stable sort, as
+    np.argsort(kind="stable") and the module's index_add order) -- then the
+    shared row; widths that are not multiples of the CTA's 512 columns."""
+    from glm53_flash_mlx_b200 import _native as N
+
+    T = 5
+    gen = torch.Generator().manual_seed(top_k * 7 + H)
+    ids = torch.randint(0, 6, (T, top_k), generator=gen, dtype=torch.int32)  # repeats within a token
+    sc = torch.rand((T, top_k), generator=gen) * 0.5 + 0.05
+    rows = (torch.randn((T * top_k, H), generator=gen) * 3).to(torch.bfloat16)
+    shared = (torch.randn((T, H), generator=gen)).to(torch.bfloat16)
+    out = torch.empty((T, H), dtype=torch.bfloat16, device="cuda")
+    rd, idd, sd, shd = rows.cuda(), ids.cuda(), sc.cuda(), shared.cuda()
+    N.check(N.lib().glm53_direct_combine(rd.data_ptr(), idd.data_ptr(), sd.data_ptr(), T, top_k, H, shd.data_ptr(),
+                                         out.data_ptr(), N.stream()), "combine")
+    torch.cuda.synchronize()
+    expect = direct_combine(f32(bits(rows)).reshape(T, top_k, H), ids.numpy(), sc.numpy(), shared=f32(bits(shared)))
+    assert np.array_equal(bits(out), expect)
+
+
 def test_batched_decode_flags_bad_expert_without_trapping(G, S):
     from glm53_flash_mlx_b200 import _native as N
     from glm53_flash_mlx_b200.packed import batched_decode_moe
